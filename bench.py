@@ -1,0 +1,341 @@
+"""Benchmark: Q4 MoE decode through the Qwen3-30B-A3B-shaped MoE stack on B200.
+
+    python bench.py [--gpus N] [--steps K] [--warmup W] [--impl ours|reference] [--batch B]
+
+Workload (one "step" = one decode step of B tokens through the hot path of every layer):
+48 MoE layers of Qwen3-30B-A3B shape — per layer x = rmsnorm(h, ffn_norm), router [128 x 2048]
+f32, softmax top-8 renormalised, 8 Q4 experts (gate/up 2048->768, down 768->2048, SwiGLU), the
+rank-order expert sum and h += sum. Attention and the LM head are not on this path (they are the
+reference's dense backbone, outside the MoE hot path), so tok/s counts the MoE stack only.
+Weights are synthetic (seeded, N(0, 0.02)-like Q4 statistics), generated in HBM; every expert is
+resident (14.7 GB). N > 1 (torchrun): each rank runs its own replica on its own GPU (weak scaling).
+
+value  : tokens/s with inputs resident in HBM (CUDA events on the launching stream, max over ranks)
+e2e    : tokens/s through the public C ABI with host buffers (hxb_moe_forward: pinned-host copies
+         of h in and out every step, inside the timed region)
+--impl reference: the reference's own AVX-512 kernels + thread pool (oracle/_ref, built from the
+         reference sources) on all host cores, same workload and byte-identical weights.
+"""
+from __future__ import annotations
+
+import argparse
+import json
+import os
+import subprocess
+import sys
+import threading
+import time
+
+import numpy as np
+
+REPO = os.path.dirname(os.path.abspath(__file__))
+sys.path.insert(0, REPO)
+
+METRIC = "Q4 MoE decode tok/s (Qwen3-30B-A3B shape); expert-GEMV HBM GB/s vs peak"
+L_, D_, F_, E_, K_ = 48, 2048, 768, 128, 8
+SEED, SIGMA = 2, 0.02
+
+
+def algorithmic_bytes():
+    """Bytes the path must read per token and layer (B = 1), FORMAT §6 row sizes."""
+    q4_row_d = 34 * D_ // 64            # gate/up row: 1088 B
+    q4_row_f = 34 * F_ // 64            # down row: 408 B
+    expert = 2 * F_ * q4_row_d + D_ * q4_row_f
+    router = E_ * D_ * 4
+    return dict(gateup=K_ * 2 * F_ * q4_row_d, down=K_ * D_ * q4_row_f, router=router, norm=D_ * 4,
+                layer=K_ * expert + router + D_ * 4, expert=expert)
+
+
+def peaks():
+    p = os.path.join(REPO, "MEASURED_PEAKS.json")
+    if os.path.exists(p):
+        with open(p) as f:
+            j = json.load(f)
+        return float(j["hbm_gbs"]), "measured"
+    return 6650.0, "fallback"
+
+
+class Clocks:
+    """nvidia-smi sampling during the timed region (SM clock, throttle reasons)."""
+
+    Q = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,clocks_event_reasons.hw_slowdown,"
+         "clocks_event_reasons.hw_thermal_slowdown,clocks_event_reasons.sw_thermal_slowdown,"
+         "clocks_event_reasons.sw_power_cap")
+
+    def __init__(self, index: int):
+        self.index = index
+        self.proc = None
+        self.lines = []
+
+    def start(self):
+        try:
+            self.proc = subprocess.Popen(["nvidia-smi", "-i", str(self.index), f"--query-gpu={self.Q}",
+                                          "--format=csv,noheader,nounits", "-lms", "200"],
+                                         stdout=subprocess.PIPE, stderr=subprocess.DEVNULL, text=True)
+            self.t = threading.Thread(target=self._read, daemon=True)
+            self.t.start()
+        except Exception:
+            self.proc = None
+
+    def _read(self):
+        for line in self.proc.stdout:
+            self.lines.append(line.strip())
+
+    def stop(self):
+        if not self.proc:
+            return {"sm_mhz": None, "sm_max_mhz": None, "reasons": ["nvidia-smi unavailable"]}
+        self.proc.terminate()
+        try:
+            self.proc.wait(timeout=5)
+        except Exception:
+            self.proc.kill()
+        sm, mx, reasons = [], None, set()
+        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
+        for ln in self.lines:
+            f = [x.strip() for x in ln.split(",")]
+            if len(f) < 9:
+                continue
+            try:
+                sm.append(float(f[1]))
+                mx = float(f[2])
+            except ValueError:
+                continue
+            for n, v in zip(names, f[5:9]):
+                if v.lower() == "active":
+                    reasons.add(n)
+        return {"sm_mhz": float(np.median(sm)) if sm else None, "sm_max_mhz": mx, "reasons": sorted(reasons),
+                "samples": len(sm)}
+
+
+def dist_env():
+    return int(os.environ.get("RANK", 0)), int(os.environ.get("WORLD_SIZE", 1)), int(os.environ.get("LOCAL_RANK", 0))
+
+
+def max_over_ranks(v: float, world: int, device=None) -> float:
+    if world <= 1:
+        return v
+    import torch
+    import torch.distributed as dist
+    t = torch.tensor([v], dtype=torch.float64, device=device)
+    dist.all_reduce(t, op=dist.ReduceOp.MAX)
+    return float(t.item())
+
+
+def cpu_model(ref, n_layers):
+    """The benchmark's model on the host, byte-identical to hxb_moe_synthesize(SEED)."""
+    from oracle import oracle as O
+    up, down, nb = O.slab_layout(O.Q4, D_, F_)
+    slabs = ref.synth_q4(n_layers * E_, nb, D_, F_, SEED, SIGMA)
+    model = O.MoeModel(D_, F_, E_, K_, score_fn=0, norm_topk_prob=1, eps=1e-6, residual_scale=1.0)
+    for l in range(n_layers):
+        router = ref.synth_f32(E_ * D_, SEED * 1000003 + l, SIGMA).reshape(E_, D_)
+        model.add_layer(router, [slabs[l * E_ + e] for e in range(E_)], [O.Q4] * E_)
+    return model, slabs
+
+
+def time_cpu(ref, model, arr, B, tokens_budget_s: float, max_tokens: int, rng):
+    """Times decode steps of B tokens on the host; returns (tokens/s, tokens timed, outputs, inputs)."""
+    h0 = rng.standard_normal((B, D_)).astype(np.float32)
+    ref.forward(model, h0.copy(), arr)                       # warm pass
+    ins, outs = [], []
+    t0 = time.perf_counter()
+    n = 0
+    while n < max_tokens:
+        h = rng.standard_normal((B, D_)).astype(np.float32)
+        ins.append(h.copy())
+        ref.forward(model, h, arr)
+        outs.append(h)
+        n += 1
+        if time.perf_counter() - t0 > tokens_budget_s:
+            break
+    dt = time.perf_counter() - t0
+    return n * B / dt, n, ins, outs
+
+
+def run_reference(args, rank, world):
+    """The reference's own CPU implementation of the path (rank 0 only)."""
+    if rank != 0:
+        return
+    from oracle import oracle as O
+    if O.moe_ref_lib() is None:
+        print(json.dumps({"impl": "reference", "unavailable": "oracle/_ref was not built (reference sources absent)"}))
+        return
+    ref = O.MoeRef(n_threads=0)
+    model, _ = cpu_model(ref, L_)
+    arr = model.c_layers()
+    rng = np.random.default_rng(123)
+    for _ in range(max(1, min(args.warmup, 3))):
+        ref.forward(model, rng.standard_normal((args.batch, D_)).astype(np.float32), arr)
+    # bounded sample: at most ~60 s of timed work whatever --steps says
+    tps, n, _, _ = time_cpu(ref, model, arr, args.batch, 60.0, args.steps, rng)
+    line = {"metric": METRIC, "value": round(tps, 3), "unit": "tok/s", "n_gpus": args.gpus, "steps": n,
+            "warmup": args.warmup, "ms_per_step": round(1000.0 * args.batch / tps, 3), "higher_is_better": True,
+            "scaling": "weak", "vs_baseline": None, "dtype": "q4xq8-int32+f32", "data": "synthetic",
+            "impl": "reference",
+            "config": {"workload": f"qwen3-30b-a3b MoE stack decode, {L_} layers, batch {args.batch}",
+                       "layers": L_, "d_model": D_, "expert_ffn_dim": F_, "n_experts": E_, "top_k": K_,
+                       "batch": args.batch},
+            "cpu_baseline": {"value": round(tps, 3), "unit": "tok/s", "cores": ref.threads, "kind": "reference",
+                             "sample": f"{n} decode steps of batch {args.batch} (60 s cap), reference AVX-512 "
+                                       f"kernels (isa {ref.isa}) + hx_pool on {ref.threads} threads"},
+            "e2e": {"value": round(tps, 3), "unit": "tok/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0}}
+    print(json.dumps(line), flush=True)
+    ref.close()
+
+
+def run_ours(args, rank, world, local_rank):
+    import torch
+    import hearth_b200 as hb
+    torch.cuda.set_device(local_rank)
+    dev = torch.device("cuda", local_rank)
+    B = args.batch
+    be = hb.MoeBackend(n_layers=L_, d_model=D_, expert_ffn_dim=F_, n_experts=E_, top_k=K_, score_fn=0,
+                       norm_topk_prob=1, max_tokens=B, device=local_rank)
+    be.synthesize(SEED, SIGMA, SIGMA)
+    # token pool resident in HBM; each step evaluates a fresh slot in place
+    P = 64
+    g = torch.Generator(device=dev).manual_seed(1000 + rank)
+    pool = torch.randn((P, B, D_), generator=g, device=dev, dtype=torch.float32)
+    stream = torch.cuda.current_stream(dev)
+    sp = stream.cuda_stream
+    for i in range(max(args.warmup, 3)):
+        be.forward_dev(pool[i % P], B, stream=sp)
+    for i in range(P):                                   # every pool slot's graph exists before timing
+        be.forward_dev(pool[i], B, stream=sp)
+    be.sync(sp)
+    torch.cuda.synchronize(dev)
+    if world > 1:
+        import torch.distributed as dist
+        dist.barrier()
+    clocks = Clocks(local_rank)
+    clocks.start()
+    time.sleep(0.3)
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    torch.cuda.synchronize(dev)
+    if world > 1:
+        dist.barrier()
+    e0.record(stream)
+    for i in range(args.steps):
+        be.forward_dev(pool[i % P], B, stream=sp)
+    e1.record(stream)
+    torch.cuda.synchronize(dev)
+    be.sync(sp)
+    ms = e0.elapsed_time(e1)
+    if world > 1:
+        dist.barrier()
+    clk = clocks.stop()
+    ms = max_over_ranks(ms, world, dev)
+    value = world * args.steps * B / (ms / 1000.0)
+    assert torch.isfinite(pool).all().item()
+
+    # ---- end to end through the public C ABI with host buffers
+    rng = np.random.default_rng(7 + rank)
+    host = [np.ascontiguousarray(rng.standard_normal((B, D_)).astype(np.float32)) for _ in range(P)]
+    for i in range(3):
+        be.forward_into(host[i])
+    e2e_steps = min(args.steps, 2000)
+    torch.cuda.synchronize(dev)
+    if world > 1:
+        dist.barrier()
+    t0 = time.perf_counter()
+    for i in range(e2e_steps):
+        be.forward_into(host[i % P])
+    t_e2e = time.perf_counter() - t0
+    t_e2e = max_over_ranks(t_e2e, world, dev)
+    e2e = world * e2e_steps * B / t_e2e
+
+    # ---- live per-kernel timing for the roofline (CUDA events on the handle's stream)
+    us = be.profile(B, 2)
+    ab = algorithmic_bytes()
+    hbm, peak_kind = peaks()
+    gateup_gbs = ab["gateup"] / (us[2] * 1e-6) / 1e9
+    step_gbs = L_ * ab["layer"] / (ms / args.steps * 1e-3) / 1e9
+
+    # ---- CPU baseline (rank 0, N = 1): reference kernels on the host, same weights; and a full-size
+    # bit-exact spot check of the GPU against it on the sampled tokens
+    cpu = None
+    parity = None
+    if rank == 0 and world == 1 and not args.no_cpu:
+        from oracle import oracle as O
+        if O.moe_ref_lib() is not None:
+            ref = O.MoeRef(n_threads=0)
+            model, _ = cpu_model(ref, L_)
+            arr = model.c_layers()
+            tps, n, ins, outs = time_cpu(ref, model, arr, B, 20.0, 400, np.random.default_rng(99))
+            cpu = {"value": round(tps, 3), "unit": "tok/s", "cores": ref.threads, "kind": "reference",
+                   "sample": f"{n} decode steps of batch {B} (~20 s) of the same 48-layer workload, reference "
+                             f"AVX-512 kernels + hx_pool on {ref.threads} threads"}
+            bad = 0
+            for hin, hout in zip(ins[:16], outs[:16]):
+                g_ = be.forward(hin)
+                bad += int(not np.array_equal(g_.view(np.uint32), hout.view(np.uint32)))
+            parity = f"{min(16, len(ins)) - bad}/{min(16, len(ins))} decode steps bit-identical to the CPU reference"
+            ref.close()
+        else:
+            cpu = {"value": None, "unit": "tok/s", "cores": 0, "kind": "reference",
+                   "sample": "oracle/_ref not built"}
+
+    launches_per_step = L_ * 4 if B * K_ <= 64 else L_ * 6
+    line = {"metric": METRIC, "value": round(value, 3), "unit": "tok/s", "n_gpus": world, "steps": args.steps,
+            "warmup": args.warmup, "ms_per_step": round(ms / args.steps, 5), "higher_is_better": True,
+            "scaling": "weak", "vs_baseline": None, "dtype": "q4xq8-int32+f32", "data": "synthetic",
+            "config": {"workload": f"qwen3-30b-a3b MoE stack decode, {L_} layers, batch {B}",
+                       "layers": L_, "d_model": D_, "expert_ffn_dim": F_, "n_experts": E_, "top_k": K_,
+                       "batch": B, "parallelism": f"replica x{world}",
+                       "l2": "no flush: each step reads ~1.01 GB of expert/router weights (> 126 MB L2)"},
+            "roofline": {"bound": "hbm", "achieved": round(gateup_gbs, 1), "peak": hbm, "unit": "GB/s",
+                         "frac": round(gateup_gbs / hbm, 4), "traffic": None,
+                         "kernel": "k_moe_gateup (Q4 gate+up GEMV, SwiGLU, mid act-quant)",
+                         "peak_kind": peak_kind,
+                         "stage_us": {"norm_act": round(us[0], 3), "router": round(us[1], 3),
+                                      "gateup": round(us[2], 3), "down": round(us[3], 3)},
+                         "bytes_per_launch": ab["gateup"],
+                         "step_bytes": L_ * ab["layer"], "step_gbs": round(step_gbs, 1),
+                         "step_frac": round(step_gbs / hbm, 4)},
+            "cpu_baseline": cpu,
+            "e2e": {"value": round(e2e, 3), "unit": "tok/s", "h2d_bytes_per_step": B * D_ * 4,
+                    "d2h_bytes_per_step": B * D_ * 4 + 4, "timing": "host clock around synchronous hxb_moe_forward"},
+            "gpu_launches": launches_per_step * args.steps,
+            "clocks": clk}
+    if parity:
+        line["parity"] = parity
+    if rank == 0:
+        print(json.dumps(line), flush=True)
+    be.close()
+
+
+def main():
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--steps", type=int, default=5000)
+    ap.add_argument("--warmup", type=int, default=20)
+    ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
+    ap.add_argument("--batch", type=int, default=1)
+    ap.add_argument("--layers", type=int, default=L_, help="MoE layers (48 = the Qwen3-30B-A3B stack); fewer only "
+                                                            "for small profiling captures")
+    ap.add_argument("--no-cpu", action="store_true", help="skip the CPU baseline leg")
+    args = ap.parse_args()
+    global L_
+    L_ = args.layers
+    rank, world, local_rank = dist_env()
+    if world > 1:
+        import datetime
+        import torch
+        import torch.distributed as dist
+        torch.cuda.set_device(local_rank)
+        dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=300),
+                                device_id=torch.device("cuda", local_rank))
+    try:
+        if args.impl == "reference":
+            run_reference(args, rank, world)
+        else:
+            run_ours(args, rank, world, local_rank)
+    finally:
+        if world > 1:
+            import torch.distributed as dist
+            dist.barrier()
+            dist.destroy_process_group()
+
+
+if __name__ == "__main__":
+    main()

@@ -1,0 +1,16 @@
+"""hearth_b200 — B200-native (sm_100a) backend for Hearth's quantized MoE expert path.
+
+* ``native``  — the reference's ``hearth._native`` kernel entry points (``matmul``, ``dequantize``,
+  ``row_bytes``) on the GPU, same names, argument meaning and errors.
+* ``MoeBackend`` — the MoE half of the engine (router, Q4/Q8 experts, rank-order sum) behind one
+  handle with an HBM-resident expert store.
+
+Everything runs through the C ABI of include/hearth_b200.h in ``libhearth_b200.so``; there is no
+CPU fallback.
+"""
+from ._lib import (BF16, F16, F32, POLICY_LFU, POLICY_LRU, Q4, Q8, SCORE_SIGMOID, SCORE_SOFTMAX,  # noqa: F401
+                   lib, last_error)
+from . import native  # noqa: F401
+from .moe import MoeBackend  # noqa: F401
+
+__all__ = ["lib", "last_error", "native", "MoeBackend", "F32", "F16", "BF16", "Q8", "Q4"]

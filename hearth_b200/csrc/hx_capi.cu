@@ -1,0 +1,844 @@
+// hx_capi.cu — the C ABI (include/hearth_b200.h): kernel-level entry points and the MoE backend
+// handle (device weights, HBM expert store, per-call scratch, CUDA-graph replay).
+#include "../../include/hearth_b200.h"
+#include "hx_common.cuh"
+#include "hx_kernels.h"
+#include "hx_store.h"
+
+#include <chrono>
+#include <cstdarg>
+#include <cstdio>
+#include <cstring>
+#include <map>
+#include <memory>
+#include <string>
+#include <tuple>
+#include <vector>
+
+using namespace hx;
+
+namespace {
+
+thread_local std::string g_err;
+
+int fail(int code, const char *fmt, ...) {
+    char buf[512];
+    va_list ap;
+    va_start(ap, fmt);
+    vsnprintf(buf, sizeof buf, fmt, ap);
+    va_end(ap);
+    g_err = buf;
+    return code;
+}
+
+bool cuda_ok(cudaError_t e, const char *what) {
+    if (e == cudaSuccess) return true;
+    g_err = std::string(what) + ": " + cudaGetErrorString(e);
+    cudaGetLastError();
+    return false;
+}
+
+double now_s() {
+    return std::chrono::duration<double>(std::chrono::steady_clock::now().time_since_epoch()).count();
+}
+
+// A device buffer owned by the handle.
+struct DevBuf {
+    void *p = nullptr;
+    size_t n = 0;
+    DevBuf() = default;
+    DevBuf(const DevBuf &) = delete;
+    DevBuf &operator=(const DevBuf &) = delete;
+    ~DevBuf() { release(); }
+    bool alloc(size_t bytes) {
+        release();
+        if (bytes == 0) bytes = 16;
+        if (cudaMalloc(&p, bytes) != cudaSuccess) {
+            cudaGetLastError();
+            p = nullptr;
+            return false;
+        }
+        n = bytes;
+        cudaMemset(p, 0, bytes);
+        return true;
+    }
+    void release() {
+        if (p) cudaFree(p);
+        p = nullptr;
+        n = 0;
+    }
+    template <class T>
+    T *as() const {
+        return static_cast<T *>(p);
+    }
+};
+
+// Host scratch for the kernel-level entry points, grown on demand (device).
+struct Scratch1 {
+    DevBuf w, x, act, y;
+};
+
+}  // namespace
+
+// =============================================================================================
+// Kernel-level boundary
+// =============================================================================================
+
+extern "C" HXB_API const char *hxb_version(void) { return "hearth-b200 0.1.0 (sm_100a)"; }
+extern "C" HXB_API const char *hxb_last_error(void) { return g_err.c_str(); }
+
+extern "C" HXB_API int hxb_device_count(void) {
+    int n = 0;
+    if (cudaGetDeviceCount(&n) != cudaSuccess) {
+        cudaGetLastError();
+        return 0;
+    }
+    return n;
+}
+
+extern "C" HXB_API size_t hxb_row_bytes(int dtype, int64_t n_cols) {
+    if (dtype < F32 || dtype > Q4) return 0;
+    return (size_t)row_bytes(dtype, n_cols);
+}
+
+extern "C" HXB_API int hxb_act_quantize_dev(const float *x, int64_t n, int T, void *act, void *stream) {
+    if (!x || !act || n <= 0 || n % QK || T < 0) return fail(HXB_E_ARG, "act_quantize: bad arguments");
+    if (!cuda_ok(launch_act_quantize(x, n, (act_q8 *)act, n, T, (cudaStream_t)stream), "act_quantize"))
+        return HXB_E_DEVICE;
+    return HXB_OK;
+}
+
+extern "C" HXB_API int hxb_matmul_dev(int dtype, const void *W, int64_t n_cols, const void *act, int T, float *Y,
+                                      int64_t ldy, int64_t r0, int64_t r1, void *stream) {
+    if (dtype < F32 || dtype > Q4 || row_bytes(dtype, n_cols) == 0 || T < 0 || r0 < 0 || r1 < r0)
+        return fail(HXB_E_ARG, "matmul_dev: bad arguments");
+    if (T == 0 || r1 == r0) return HXB_OK;
+    if (!W || !act || !Y) return fail(HXB_E_ARG, "matmul_dev: null pointer");
+    if (!cuda_ok(launch_matmul(dtype, W, n_cols, act, T, Y, ldy, r0, r1, (cudaStream_t)stream), "matmul"))
+        return HXB_E_DEVICE;
+    return HXB_OK;
+}
+
+extern "C" HXB_API int hxb_dequantize_dev(int dtype, const void *W, int64_t n_rows, int64_t n_cols, float *out,
+                                          void *stream) {
+    if (dtype < F32 || dtype > Q4 || row_bytes(dtype, n_cols) == 0 || n_rows < 0)
+        return fail(HXB_E_ARG, "dequantize_dev: bad arguments");
+    if (n_rows == 0) return HXB_OK;
+    if (!W || !out) return fail(HXB_E_ARG, "dequantize_dev: null pointer");
+    if (!cuda_ok(launch_dequantize(dtype, W, n_rows, n_cols, out, (cudaStream_t)stream), "dequantize"))
+        return HXB_E_DEVICE;
+    return HXB_OK;
+}
+
+extern "C" HXB_API int hxb_expf_dev(uint32_t x0, int64_t n, float *out, void *stream) {
+    if (n < 0 || (n && !out)) return fail(HXB_E_ARG, "expf_dev: bad arguments");
+    if (!cuda_ok(launch_expf_bits(x0, n, out, (cudaStream_t)stream), "expf")) return HXB_E_DEVICE;
+    return HXB_OK;
+}
+
+// hearth_matmul with host buffers (engine/src/quant.c:574-600): same argument checks and codes.
+extern "C" HXB_API int hxb_matmul(int dtype, const void *W, int64_t n_rows, int64_t n_cols, const float *X, int T,
+                                  float *Y) {
+    if (dtype < F32 || dtype > Q4 || n_rows < 0 || T < 0 || row_bytes(dtype, n_cols) == 0) {
+        fail(HXB_MM_E_ARG, "hxb_matmul: bad arguments");
+        return HXB_MM_E_ARG;
+    }
+    if (T == 0 || n_rows == 0) return HXB_MM_OK;
+    if (!W || !X || !Y) {
+        fail(HXB_MM_E_ARG, "hxb_matmul: null pointer");
+        return HXB_MM_E_ARG;
+    }
+    if (hxb_device_count() <= 0) {
+        fail(HXB_MM_E_NODEV, "hxb_matmul: no CUDA device");
+        return HXB_MM_E_NODEV;
+    }
+    const size_t wb = (size_t)row_bytes(dtype, n_cols) * (size_t)n_rows;
+    const size_t xb = sizeof(float) * (size_t)n_cols * (size_t)T;
+    const size_t ab = is_quant(dtype) ? (size_t)(n_cols / QK) * ACT_BLOCK * (size_t)T : 0;
+    const size_t yb = sizeof(float) * (size_t)n_rows * (size_t)T;
+    Scratch1 s;
+    if (!s.w.alloc(wb) || !s.x.alloc(xb) || !s.act.alloc(ab) || !s.y.alloc(yb)) {
+        fail(HXB_MM_E_ALLOC, "hxb_matmul: device allocation failed");
+        return HXB_MM_E_ALLOC;
+    }
+    cudaStream_t st = nullptr;
+    bool ok = cuda_ok(cudaMemcpy(s.w.p, W, wb, cudaMemcpyHostToDevice), "copy W") &&
+              cuda_ok(cudaMemcpy(s.x.p, X, xb, cudaMemcpyHostToDevice), "copy X");
+    const void *act = s.x.p;
+    if (ok && is_quant(dtype)) {
+        ok = cuda_ok(launch_act_quantize(s.x.as<float>(), n_cols, s.act.as<act_q8>(), n_cols, T, st), "act");
+        act = s.act.p;
+    }
+    ok = ok && cuda_ok(launch_matmul(dtype, s.w.p, n_cols, act, T, s.y.as<float>(), n_rows, 0, n_rows, st), "mm");
+    ok = ok && cuda_ok(cudaMemcpy(Y, s.y.p, yb, cudaMemcpyDeviceToHost), "copy Y");
+    if (!ok) return HXB_MM_E_NODEV;
+    return HXB_MM_OK;
+}
+
+extern "C" HXB_API int hxb_dequantize(int dtype, const void *src, int64_t n_rows, int64_t n_cols, float *dst) {
+    if (dtype < F32 || dtype > Q4 || row_bytes(dtype, n_cols) == 0 || n_rows < 0)
+        return fail(HXB_E_ARG, "hxb_dequantize: bad arguments");
+    if (n_rows == 0) return HXB_OK;
+    if (!src || !dst) return fail(HXB_E_ARG, "hxb_dequantize: null pointer");
+    const size_t wb = (size_t)row_bytes(dtype, n_cols) * (size_t)n_rows;
+    const size_t ob = sizeof(float) * (size_t)n_rows * (size_t)n_cols;
+    DevBuf w, o;
+    if (!w.alloc(wb) || !o.alloc(ob)) return fail(HXB_E_NOMEM, "hxb_dequantize: device allocation failed");
+    bool ok = cuda_ok(cudaMemcpy(w.p, src, wb, cudaMemcpyHostToDevice), "copy") &&
+              cuda_ok(launch_dequantize(dtype, w.p, n_rows, n_cols, o.as<float>(), nullptr), "dequantize") &&
+              cuda_ok(cudaMemcpy(dst, o.p, ob, cudaMemcpyDeviceToHost), "copy back");
+    return ok ? HXB_OK : HXB_E_DEVICE;
+}
+
+// =============================================================================================
+// MoE backend handle
+// =============================================================================================
+
+struct LayerBufs {
+    DevBuf router, bias, norm, sh_gate, sh_up, sh_down, sh_gate_inp;
+    bool set = false;
+};
+
+struct GraphKey {
+    int T, l0, nl;
+    const void *h;
+    cudaStream_t s;
+    bool operator<(const GraphKey &o) const {
+        return std::tie(T, l0, nl, h, s) < std::tie(o.T, o.l0, o.nl, o.h, o.s);
+    }
+};
+
+struct hxb_moe {
+    hxb_moe_config cfg{};
+    int device = 0;
+    size_t slab_bytes = 0;
+    slab_layout lay{};
+    cudaStream_t stream = nullptr;
+    HbmStore store;
+    bool resident_mode = false;          // every expert has a slot: no host round trip per layer
+    std::unique_ptr<LayerBufs[]> layers;
+    DevBuf table;                        // [L*E] device slab pointers
+    const uint8_t **host_table = nullptr;  // pinned mirror
+    // scratch
+    DevBuf x, xact, logits, sh_logit, ids, wts, nu, ulist, u_p0, u_n, pair_tok, pair_of, act_mid, Y, S, ticket, err;
+    DevBuf hbuf, obuf;                   // device copies of host inputs/outputs
+    float *hpin = nullptr;               // pinned staging [max_tokens, D]
+    int *epin = nullptr;                 // pinned: error word, nu, ulist
+    std::map<GraphKey, cudaGraphExec_t> graphs;
+    hxb_moe_stats st{};
+    int last_T = 0;
+
+    MoeScratch scratch() const {
+        MoeScratch s;
+        s.x = x.as<float>();
+        s.xact = xact.as<act_q8>();
+        s.logits = logits.as<float>();
+        s.sh_logit = sh_logit.as<float>();
+        s.ids = ids.as<int>();
+        s.wts = wts.as<float>();
+        s.nu = nu.as<int>();
+        s.ulist = ulist.as<int>();
+        s.u_p0 = u_p0.as<int>();
+        s.u_n = u_n.as<int>();
+        s.pair_tok = pair_tok.as<int>();
+        s.pair_of = pair_of.as<int>();
+        s.act_mid = act_mid.as<act_q8>();
+        s.Y = Y.as<float>();
+        s.S = S.as<float>();
+        s.ticket = ticket.as<unsigned>();
+        s.err = err.as<int>();
+        return s;
+    }
+
+    MoeShape shape(int T) const {
+        MoeShape sh;
+        sh.D = cfg.d_model;
+        sh.F = cfg.expert_ffn_dim;
+        sh.E = cfg.n_experts;
+        sh.K = cfg.top_k;
+        sh.T = T;
+        sh.eps = cfg.norm_eps;
+        sh.residual_scale = cfg.residual_scale;
+        sh.route.E = cfg.n_experts;
+        sh.route.K = cfg.top_k;
+        sh.route.score_fn = cfg.score_fn;
+        sh.route.score_bias = cfg.score_bias;
+        sh.route.n_group = cfg.n_group;
+        sh.route.topk_group = cfg.topk_group;
+        sh.route.norm_topk_prob = cfg.norm_topk_prob;
+        sh.route.routed_scale = cfg.routed_scale;
+        return sh;
+    }
+
+    MoeLayerDev layer_dev(int l, bool with_norm) const {
+        const LayerBufs &b = layers[(size_t)l];
+        MoeLayerDev d;
+        d.router = b.router.as<float>();
+        d.router_bias = cfg.score_bias ? b.bias.as<float>() : nullptr;
+        d.ffn_norm = with_norm ? b.norm.as<float>() : nullptr;
+        d.slab = table.as<const uint8_t *>() + (size_t)l * cfg.n_experts;
+        d.expert_dtype = cfg.expert_dtype;
+        d.off_up = lay.off_up;
+        d.off_down = lay.off_down;
+        d.Fs = cfg.shared_ffn_dim;
+        d.sh_dtype = cfg.shared_dtype;
+        d.sh_gate = b.sh_gate.as<uint8_t>();
+        d.sh_up = b.sh_up.as<uint8_t>();
+        d.sh_down = b.sh_down.as<uint8_t>();
+        d.sh_gate_inp = cfg.shared_gate ? b.sh_gate_inp.as<float>() : nullptr;
+        return d;
+    }
+
+    ~hxb_moe() {
+        if (stream) cudaStreamSynchronize(stream);
+        for (auto &g : graphs) cudaGraphExecDestroy(g.second);
+        graphs.clear();
+        if (hpin) cudaFreeHost(hpin);
+        if (epin) cudaFreeHost(epin);
+        if (host_table) cudaFreeHost(host_table);
+        store.close();
+        if (stream) cudaStreamDestroy(stream);
+    }
+};
+
+extern "C" HXB_API void hxb_moe_default_config(hxb_moe_config *c) {
+    if (!c) return;
+    std::memset(c, 0, sizeof *c);
+    c->n_layers = 1;
+    c->top_k = 1;
+    c->n_group = 1;
+    c->topk_group = 1;
+    c->norm_topk_prob = 1;
+    c->routed_scale = 1.0f;
+    c->residual_scale = 1.0f;
+    c->norm_eps = 1e-6f;
+    c->expert_dtype = Q4;
+    c->shared_dtype = Q8;
+    c->max_tokens = 1;
+    c->cache_gb = 0.0;
+    c->policy = POLICY_LFU;
+    c->heat_decay = 0.995f;
+}
+
+static void set_errbuf(char *err, size_t errlen, const std::string &msg) {
+    g_err = msg;
+    if (err && errlen) {
+        std::snprintf(err, errlen, "%s", msg.c_str());
+    }
+}
+
+extern "C" HXB_API hxb_moe *hxb_moe_open(const hxb_moe_config *c, char *err, size_t errlen) {
+    if (!c) {
+        set_errbuf(err, errlen, "hxb_moe_open: null config");
+        return nullptr;
+    }
+    const hxb_moe_config &k = *c;
+    std::string why;
+    if (k.n_layers <= 0) why = "n_layers must be positive";
+    else if (k.d_model <= 0 || k.d_model % QK != 0 || k.d_model > 8192) why = "d_model must be a multiple of 64 up to 8192";
+    else if (k.expert_ffn_dim <= 0 || k.expert_ffn_dim % QK) why = "expert_ffn_dim must be a positive multiple of 64";
+    else if (k.n_experts <= 0 || k.n_experts > 384) why = "n_experts must be 1..384";
+    else if (k.top_k <= 0 || k.top_k > 32 || k.top_k > k.n_experts) why = "top_k must be 1..min(32, n_experts)";
+    else if (k.expert_dtype != Q4 && k.expert_dtype != Q8) why = "expert_dtype must be Q4 or Q8";
+    else if (k.shared_ffn_dim < 0 || k.shared_ffn_dim % QK) why = "shared_ffn_dim must be a multiple of 64";
+    else if (k.shared_ffn_dim && k.shared_dtype != Q4 && k.shared_dtype != Q8) why = "shared_dtype must be Q4 or Q8";
+    else if (k.n_group > 1 && (k.n_experts % k.n_group || k.n_group > 32 || k.topk_group < 1 || k.topk_group > k.n_group))
+        why = "bad expert grouping";
+    else if (k.max_tokens <= 0 || k.max_tokens > 8192) why = "max_tokens must be 1..8192";
+    if (!why.empty()) {
+        set_errbuf(err, errlen, "hxb_moe_open: " + why);
+        return nullptr;
+    }
+    if (hxb_device_count() <= k.device) {
+        set_errbuf(err, errlen, "hxb_moe_open: CUDA device " + std::to_string(k.device) + " not available");
+        return nullptr;
+    }
+    std::unique_ptr<hxb_moe> m(new hxb_moe());
+    m->cfg = k;
+    m->device = k.device;
+    cudaSetDevice(k.device);
+    m->lay = make_slab_layout(k.expert_dtype, k.d_model, k.expert_ffn_dim);
+    m->slab_bytes = (size_t)m->lay.nbytes;
+    const int L = k.n_layers, E = k.n_experts, D = k.d_model, T = k.max_tokens, K = k.top_k;
+    const int64_t nkeys = (int64_t)L * E;
+    int64_t n_slots = nkeys;
+    if (k.cache_gb > 0.0) {
+        const int64_t by_budget = (int64_t)(k.cache_gb * 1073741824.0 / (double)m->slab_bytes);
+        n_slots = std::min<int64_t>(nkeys, std::max<int64_t>(by_budget, (int64_t)E + 2));
+    }
+    m->resident_mode = n_slots >= nkeys;
+    if (cudaStreamCreateWithFlags(&m->stream, cudaStreamNonBlocking) != cudaSuccess) {
+        set_errbuf(err, errlen, "hxb_moe_open: cannot create a stream");
+        return nullptr;
+    }
+    if (!m->store.open(L, E, m->slab_bytes, (int)n_slots, k.policy, k.heat_decay, why)) {
+        set_errbuf(err, errlen, "hxb_moe_open: " + why);
+        return nullptr;
+    }
+    m->layers.reset(new LayerBufs[(size_t)L]);
+    const int Fmax = std::max(k.expert_ffn_dim, k.shared_ffn_dim);
+    const size_t P = (size_t)T * K;
+    bool ok = m->table.alloc(sizeof(void *) * (size_t)nkeys) && m->x.alloc(sizeof(float) * (size_t)T * D) &&
+              m->xact.alloc((size_t)T * (D / QK) * ACT_BLOCK) && m->logits.alloc(sizeof(float) * (size_t)T * E) &&
+              m->sh_logit.alloc(sizeof(float) * (size_t)T) && m->ids.alloc(sizeof(int) * P) &&
+              m->wts.alloc(sizeof(float) * P) && m->nu.alloc(sizeof(int) * 4) && m->ulist.alloc(sizeof(int) * E) &&
+              m->u_p0.alloc(sizeof(int) * E) && m->u_n.alloc(sizeof(int) * E) &&
+              m->pair_tok.alloc(sizeof(int) * P) && m->pair_of.alloc(sizeof(int) * P) &&
+              m->act_mid.alloc((P + (size_t)T) * (size_t)(Fmax / QK) * ACT_BLOCK) &&
+              m->Y.alloc(P * kFusedMaxPairs > 0 && (int)P > kFusedMaxPairs ? sizeof(float) * P * D : 16) &&
+              m->S.alloc(k.shared_ffn_dim && (int)P > kFusedMaxPairs ? sizeof(float) * (size_t)T * D : 16) &&
+              m->ticket.alloc(64) && m->err.alloc(64) && m->hbuf.alloc(sizeof(float) * (size_t)T * D) &&
+              m->obuf.alloc(sizeof(float) * (size_t)T * D);
+    ok = ok && cudaHostAlloc((void **)&m->hpin, sizeof(float) * (size_t)T * D, cudaHostAllocDefault) == cudaSuccess;
+    ok = ok && cudaHostAlloc((void **)&m->epin, sizeof(int) * (size_t)(8 + 2 * E), cudaHostAllocDefault) == cudaSuccess;
+    ok = ok && cudaHostAlloc((void **)&m->host_table, sizeof(void *) * (size_t)nkeys, cudaHostAllocDefault) ==
+                   cudaSuccess;
+    if (!ok) {
+        cudaGetLastError();
+        set_errbuf(err, errlen, "hxb_moe_open: out of device or pinned memory");
+        return nullptr;
+    }
+    std::memset(m->host_table, 0, sizeof(void *) * (size_t)nkeys);
+    if (!cuda_ok(init_kernel_attributes(), "kernel attributes")) {
+        set_errbuf(err, errlen, "hxb_moe_open: " + g_err);
+        return nullptr;
+    }
+    cudaDeviceSynchronize();
+    m->st.n_slots = m->store.n_slots();
+    m->st.slot_bytes = m->slab_bytes;
+    return m.release();
+}
+
+extern "C" HXB_API void hxb_moe_close(hxb_moe *m) { delete m; }
+
+extern "C" HXB_API size_t hxb_moe_slab_bytes(const hxb_moe *m) { return m ? m->slab_bytes : 0; }
+
+static bool upload(DevBuf &b, const void *src, size_t bytes) {
+    if (!src) {
+        b.release();
+        return true;
+    }
+    if (!b.alloc(bytes)) return false;
+    return cudaMemcpy(b.p, src, bytes, cudaMemcpyHostToDevice) == cudaSuccess;
+}
+
+static void drop_graphs(hxb_moe *m) {
+    if (m->stream) cudaStreamSynchronize(m->stream);
+    for (auto &g : m->graphs) cudaGraphExecDestroy(g.second);
+    m->graphs.clear();
+}
+
+extern "C" HXB_API int hxb_moe_set_layer(hxb_moe *m, int layer, const float *router, const float *router_bias,
+                                         const float *ffn_norm, const void *sh_gate, const void *sh_up,
+                                         const void *sh_down, const float *sh_gate_inp) {
+    if (!m || layer < 0 || layer >= m->cfg.n_layers || !router) return fail(HXB_E_ARG, "set_layer: bad arguments");
+    const hxb_moe_config &k = m->cfg;
+    if (k.score_bias && !router_bias) return fail(HXB_E_ARG, "set_layer: score_bias needs router_bias");
+    if (k.shared_ffn_dim && (!sh_gate || !sh_up || !sh_down)) return fail(HXB_E_ARG, "set_layer: shared expert missing");
+    if (k.shared_gate && !sh_gate_inp) return fail(HXB_E_ARG, "set_layer: shared gate input missing");
+    cudaSetDevice(m->device);
+    LayerBufs &b = m->layers[(size_t)layer];
+    const size_t D = (size_t)k.d_model, E = (size_t)k.n_experts, Fs = (size_t)k.shared_ffn_dim;
+    const size_t shb = Fs ? (size_t)row_bytes(k.shared_dtype, (int64_t)D) * Fs : 0;
+    const size_t shd = Fs ? (size_t)row_bytes(k.shared_dtype, (int64_t)Fs) * D : 0;
+    bool ok = upload(b.router, router, sizeof(float) * E * D) && upload(b.bias, router_bias, sizeof(float) * E) &&
+              upload(b.sh_gate, Fs ? sh_gate : nullptr, shb) && upload(b.sh_up, Fs ? sh_up : nullptr, shb) &&
+              upload(b.sh_down, Fs ? sh_down : nullptr, shd) &&
+              upload(b.sh_gate_inp, k.shared_gate ? sh_gate_inp : nullptr, sizeof(float) * D);
+    if (ok) {
+        if (ffn_norm) ok = upload(b.norm, ffn_norm, sizeof(float) * D);
+        else {
+            std::vector<float> ones(D, 1.0f);
+            ok = upload(b.norm, ones.data(), sizeof(float) * D);
+        }
+    }
+    if (!ok) {
+        cudaGetLastError();
+        return fail(HXB_E_NOMEM, "set_layer: device allocation or copy failed");
+    }
+    b.set = true;
+    drop_graphs(m);
+    return HXB_OK;
+}
+
+extern "C" HXB_API int hxb_moe_set_expert(hxb_moe *m, int layer, int expert, const void *slab, size_t nbytes) {
+    if (!m || layer < 0 || layer >= m->cfg.n_layers || expert < 0 || expert >= m->cfg.n_experts || !slab ||
+        nbytes < (size_t)m->lay.end || nbytes > m->slab_bytes)
+        return fail(HXB_E_ARG, "set_expert: bad arguments (slab must be %zu bytes)", m ? m->slab_bytes : (size_t)0);
+    cudaSetDevice(m->device);
+    std::string why;
+    if (!m->store.set_source(layer, expert, slab, nbytes, why)) return fail(HXB_E_NOMEM, "set_expert: %s", why.c_str());
+    if (m->resident_mode) {   // every expert keeps a slot: copy it in now
+        cudaEvent_t ev = nullptr;
+        const uint8_t *p = m->store.acquire_async(layer, expert, &ev);
+        if (!p) return fail(HXB_E_IO, "set_expert: could not place the expert in HBM");
+        m->store.release(layer, expert, m->store.copy_stream());
+        cudaStreamSynchronize(m->store.copy_stream());
+        m->host_table[(size_t)layer * m->cfg.n_experts + expert] = p;
+        if (!cuda_ok(cudaMemcpy(m->table.as<const uint8_t *>() + (size_t)layer * m->cfg.n_experts + expert, &p,
+                                sizeof p, cudaMemcpyHostToDevice),
+                     "set_expert table"))
+            return HXB_E_DEVICE;
+        m->store.reset_stats();
+    }
+    drop_graphs(m);
+    return HXB_OK;
+}
+
+extern "C" HXB_API int hxb_moe_synthesize(hxb_moe *m, uint64_t seed, float sigma_router, float sigma_expert) {
+    if (!m) return fail(HXB_E_ARG, "synthesize: null handle");
+    if (!m->resident_mode) return fail(HXB_E_ARG, "synthesize: needs every expert resident (cache_gb = 0)");
+    if (m->cfg.expert_dtype != Q4) return fail(HXB_E_UNSUPPORTED, "synthesize: Q4 experts only");
+    if (m->cfg.shared_ffn_dim) return fail(HXB_E_UNSUPPORTED, "synthesize: no shared expert");
+    cudaSetDevice(m->device);
+    const hxb_moe_config &k = m->cfg;
+    const int L = k.n_layers, E = k.n_experts, D = k.d_model;
+    for (int l = 0; l < L; l++) {
+        LayerBufs &b = m->layers[(size_t)l];
+        bool ok = b.router.alloc(sizeof(float) * (size_t)E * D) && b.norm.alloc(sizeof(float) * (size_t)D) &&
+                  (!k.score_bias || b.bias.alloc(sizeof(float) * (size_t)E));
+        if (!ok) return fail(HXB_E_NOMEM, "synthesize: out of device memory");
+        if (!cuda_ok(launch_synth_f32(b.router.as<float>(), (int64_t)E * D, seed * 1000003ull + (uint64_t)l,
+                                      sigma_router, m->stream),
+                     "synth router"))
+            return HXB_E_DEVICE;
+        std::vector<float> ones((size_t)D, 1.0f);
+        cudaMemcpy(b.norm.p, ones.data(), sizeof(float) * D, cudaMemcpyHostToDevice);
+        b.set = true;
+        for (int e = 0; e < E; e++) {
+            uint8_t *p = m->store.place_resident(l, e);
+            if (!p) return fail(HXB_E_NOMEM, "synthesize: no slot");
+            m->host_table[(size_t)l * E + e] = p;
+        }
+    }
+    // slots were handed out in order, so the L*E slabs are contiguous: one launch fills them all
+    const uint8_t *base = m->host_table[0];
+    for (int64_t i = 0; i < (int64_t)L * E; i++)
+        if (m->host_table[i] != base + (size_t)i * m->slab_bytes)
+            return fail(HXB_E_ARG, "synthesize: expert slots are not contiguous (experts were set before)");
+    if (!cuda_ok(launch_synth_q4(const_cast<uint8_t *>(base), (int64_t)L * E, (int64_t)m->slab_bytes, D,
+                                 k.expert_ffn_dim, seed, sigma_expert, m->stream),
+                 "synth experts"))
+        return HXB_E_DEVICE;
+    if (!cuda_ok(cudaMemcpyAsync(m->table.p, m->host_table, sizeof(void *) * (size_t)L * E, cudaMemcpyHostToDevice,
+                                 m->stream),
+                 "table"))
+        return HXB_E_DEVICE;
+    if (!cuda_ok(cudaStreamSynchronize(m->stream), "synthesize")) return HXB_E_DEVICE;
+    drop_graphs(m);
+    return HXB_OK;
+}
+
+// ---------------------------------------------------------------------------------------------
+// Evaluation
+// ---------------------------------------------------------------------------------------------
+
+// Reads and clears the device error word (after the stream was synchronised).
+static int take_device_error(hxb_moe *m, int word) {
+    if (!word) return HXB_OK;
+    cudaMemset(m->err.p, 0, sizeof(int));
+    if (word == 2) return fail(HXB_E_IO, "an expert was not resident in HBM");
+    if (word == 3) return fail(HXB_E_UNSUPPORTED, "expert dtype not handled by the kernels");
+    return fail(HXB_E_DEVICE, "device error word %d (a bounded wait gave up)", word);
+}
+
+// Every expert resident: the whole range is device work only (capturable).
+static int enqueue_resident(hxb_moe *m, float *h, float *out, int T, int l0, int nl, bool with_norm, bool resid,
+                            cudaStream_t s) {
+    const MoeScratch sc = m->scratch();
+    const MoeShape sh = m->shape(T);
+    for (int l = l0; l < l0 + nl; l++) {
+        const MoeLayerDev L = m->layer_dev(l, with_norm);
+        if (!cuda_ok(launch_moe_layer(sh, L, sc, h, out, resid, s), "moe layer")) return HXB_E_DEVICE;
+    }
+    return HXB_OK;
+}
+
+// Experts may be missing from HBM: route on the device, read the bucket list back, acquire the
+// experts from the store (copies on its copy stream, waited for on the device), then run them.
+static int run_streaming(hxb_moe *m, float *h, float *out, int T, int l0, int nl, bool with_norm, bool resid,
+                         cudaStream_t s) {
+    const MoeScratch sc = m->scratch();
+    const MoeShape sh = m->shape(T);
+    const int E = m->cfg.n_experts;
+    for (int l = l0; l < l0 + nl; l++) {
+        const MoeLayerDev L = m->layer_dev(l, with_norm);
+        if (!cuda_ok(launch_moe_route(sh, L, sc, h, s), "route")) return HXB_E_DEVICE;
+        int *nu_h = m->epin + 1, *ul_h = m->epin + 8, *un_h = m->epin + 8 + E;
+        bool ok = cuda_ok(cudaMemcpyAsync(nu_h, sc.nu, sizeof(int), cudaMemcpyDeviceToHost, s), "nu") &&
+                  cuda_ok(cudaMemcpyAsync(ul_h, sc.ulist, sizeof(int) * (size_t)E, cudaMemcpyDeviceToHost, s), "ulist") &&
+                  cuda_ok(cudaMemcpyAsync(un_h, sc.u_n, sizeof(int) * (size_t)E, cudaMemcpyDeviceToHost, s), "u_n") &&
+                  cuda_ok(cudaMemcpyAsync(m->epin, sc.err, sizeof(int), cudaMemcpyDeviceToHost, s), "err");
+        const double t0 = now_s();
+        ok = ok && cuda_ok(cudaStreamSynchronize(s), "route sync");
+        m->st.stall_s += now_s() - t0;
+        if (!ok) return HXB_E_DEVICE;
+        if (m->epin[0]) return take_device_error(m, m->epin[0]);
+        const int nu = *nu_h;
+        std::vector<int> got;
+        int rc = HXB_OK;
+        for (int u = 0; u < nu; u++) {
+            const int e = ul_h[u];
+            cudaEvent_t ev = nullptr;
+            const uint8_t *p = m->store.acquire_async(l, e, &ev);
+            if (!p) {
+                rc = fail(HXB_E_IO, "layer %d expert %d could not be brought into HBM", l, e);
+                break;
+            }
+            got.push_back(e);
+            // one use per (token, rank) routed here, as sequential evaluation counts them
+            if (un_h[u] > 1) m->store.count_uses(l, e, (uint32_t)(un_h[u] - 1));
+            if (ev && !cuda_ok(cudaStreamWaitEvent(s, ev, 0), "wait copy")) {
+                rc = HXB_E_DEVICE;
+                break;
+            }
+            m->host_table[(size_t)l * E + e] = p;
+        }
+        if (rc == HXB_OK &&
+            !cuda_ok(cudaMemcpyAsync(m->table.as<const uint8_t *>() + (size_t)l * E, m->host_table + (size_t)l * E,
+                                     sizeof(void *) * (size_t)E, cudaMemcpyHostToDevice, s),
+                     "table"))
+            rc = HXB_E_DEVICE;
+        if (rc == HXB_OK && !cuda_ok(launch_moe_experts(sh, L, sc, h, out, resid, s), "experts")) rc = HXB_E_DEVICE;
+        for (int e : got) m->store.release(l, e, s);
+        if (rc != HXB_OK) {
+            cudaStreamSynchronize(s);   // nothing of this call may still run when it returns
+            return rc;
+        }
+    }
+    return HXB_OK;
+}
+
+static int run_range(hxb_moe *m, float *h, float *out, int T, int l0, int nl, bool with_norm, bool resid,
+                     cudaStream_t user, bool host_io, const float *hin, float *hout) {
+    cudaStream_t s = user ? user : m->stream;
+    const size_t bytes = sizeof(float) * (size_t)T * m->cfg.d_model;
+    const double t0 = now_s();
+    int rc = HXB_OK;
+    if (m->resident_mode) {
+        // one CUDA graph per (T, range, buffers): the host copies (host variants) are part of it
+        GraphKey key{T, l0 * 2 + (with_norm ? 1 : 0), nl * 2 + (resid ? 1 : 0), host_io ? nullptr : (const void *)h,
+                     (cudaStream_t)(uintptr_t)(out ? 1 : 0)};
+        if (!host_io) key.s = (cudaStream_t)(uintptr_t)((uintptr_t)out ^ 0x5);
+        auto it = m->graphs.find(key);
+        if (it == m->graphs.end() && m->graphs.size() >= 256) drop_graphs(m);   // bound the cache
+        if (it == m->graphs.end()) {
+            cudaGraph_t g = nullptr;
+            cudaGraphExec_t ex = nullptr;
+            if (!cuda_ok(cudaStreamBeginCapture(m->stream, cudaStreamCaptureModeThreadLocal), "capture")) return HXB_E_DEVICE;
+            float *dh = host_io ? m->hbuf.as<float>() : h;
+            float *dout = host_io ? (out ? m->obuf.as<float>() : nullptr) : out;
+            if (host_io) cudaMemcpyAsync(dh, m->hpin, bytes, cudaMemcpyHostToDevice, m->stream);
+            rc = enqueue_resident(m, dh, dout, T, l0, nl, with_norm, resid, m->stream);
+            if (host_io) cudaMemcpyAsync(m->hpin, out ? dout : dh, bytes, cudaMemcpyDeviceToHost, m->stream);
+            cudaMemcpyAsync(m->epin, m->err.p, sizeof(int), cudaMemcpyDeviceToHost, m->stream);
+            const cudaError_t ce = cudaStreamEndCapture(m->stream, &g);
+            if (rc != HXB_OK || !cuda_ok(ce, "end capture")) {
+                if (g) cudaGraphDestroy(g);
+                return rc != HXB_OK ? rc : HXB_E_DEVICE;
+            }
+            const bool iok = cuda_ok(cudaGraphInstantiate(&ex, g, 0), "instantiate");
+            cudaGraphDestroy(g);
+            if (!iok) return HXB_E_DEVICE;
+            it = m->graphs.emplace(key, ex).first;
+        }
+        if (host_io) std::memcpy(m->hpin, hin, bytes);
+        if (!cuda_ok(cudaGraphLaunch(it->second, s), "graph launch")) return HXB_E_DEVICE;
+        if (host_io) {   // device variants stay asynchronous: hxb_moe_sync reports their errors
+            if (!cuda_ok(cudaStreamSynchronize(s), "sync")) return HXB_E_DEVICE;
+            rc = take_device_error(m, m->epin[0]);
+            if (rc == HXB_OK) std::memcpy(hout, m->hpin, bytes);
+        }
+    } else {
+        float *dh = h, *dout = out;
+        if (host_io) {
+            dh = m->hbuf.as<float>();
+            dout = out ? m->obuf.as<float>() : nullptr;
+            std::memcpy(m->hpin, hin, bytes);
+            if (!cuda_ok(cudaMemcpyAsync(dh, m->hpin, bytes, cudaMemcpyHostToDevice, s), "h in")) return HXB_E_DEVICE;
+        }
+        rc = run_streaming(m, dh, dout, T, l0, nl, with_norm, resid, s);
+        if (rc == HXB_OK && host_io) {
+            if (!cuda_ok(cudaMemcpyAsync(m->hpin, out ? dout : dh, bytes, cudaMemcpyDeviceToHost, s), "h out") ||
+                !cuda_ok(cudaStreamSynchronize(s), "sync"))
+                return HXB_E_DEVICE;
+            std::memcpy(hout, m->hpin, bytes);
+        } else if (rc == HXB_OK && !user) {
+            if (!cuda_ok(cudaStreamSynchronize(s), "sync")) return HXB_E_DEVICE;
+        }
+    }
+    if (rc != HXB_OK) return rc;
+    m->st.tokens += (uint64_t)T;
+    m->st.forward_calls++;
+    m->st.expert_uses += (uint64_t)T * (uint64_t)m->cfg.top_k * (uint64_t)nl;
+    m->st.wall_s += now_s() - t0;
+    m->last_T = T;
+    return HXB_OK;
+}
+
+static int check_eval(hxb_moe *m, int T, int l0, int nl) {
+    if (!m) return fail(HXB_E_ARG, "null handle");
+    if (T <= 0 || l0 < 0 || nl <= 0 || l0 + nl > m->cfg.n_layers) return fail(HXB_E_ARG, "bad token count or layer range");
+    if (T > m->cfg.max_tokens) return fail(HXB_E_CAPACITY, "T=%d exceeds max_tokens=%d", T, m->cfg.max_tokens);
+    for (int l = l0; l < l0 + nl; l++)
+        if (!m->layers[(size_t)l].set) return fail(HXB_E_ARG, "layer %d has no weights", l);
+    cudaSetDevice(m->device);
+    return HXB_OK;
+}
+
+extern "C" HXB_API int hxb_moe_forward(hxb_moe *m, float *h, int T, int layer0, int n_layers) {
+    int rc = check_eval(m, T, layer0, n_layers);
+    if (rc) return rc;
+    if (!h) return fail(HXB_E_ARG, "null h");
+    return run_range(m, nullptr, nullptr, T, layer0, n_layers, true, true, nullptr, true, h, h);
+}
+
+extern "C" HXB_API int hxb_moe_forward_dev(hxb_moe *m, float *h, int T, int layer0, int n_layers, void *stream) {
+    int rc = check_eval(m, T, layer0, n_layers);
+    if (rc) return rc;
+    if (!h) return fail(HXB_E_ARG, "null h");
+    return run_range(m, h, nullptr, T, layer0, n_layers, true, true, (cudaStream_t)stream, false, nullptr, nullptr);
+}
+
+extern "C" HXB_API int hxb_moe_layer(hxb_moe *m, int layer, const float *x, int T, float *out) {
+    int rc = check_eval(m, T, layer, 1);
+    if (rc) return rc;
+    if (!x || !out) return fail(HXB_E_ARG, "null buffer");
+    return run_range(m, nullptr, m->obuf.as<float>(), T, layer, 1, false, false, nullptr, true, x, out);
+}
+
+extern "C" HXB_API int hxb_moe_layer_dev(hxb_moe *m, int layer, const float *x, int T, float *out, void *stream) {
+    int rc = check_eval(m, T, layer, 1);
+    if (rc) return rc;
+    if (!x || !out) return fail(HXB_E_ARG, "null buffer");
+    return run_range(m, const_cast<float *>(x), out, T, layer, 1, false, false, (cudaStream_t)stream, false, nullptr,
+                     nullptr);
+}
+
+extern "C" HXB_API int hxb_moe_last_routing(hxb_moe *m, int *ids, float *weights, int T) {
+    if (!m || T <= 0 || T > m->last_T) return fail(HXB_E_ARG, "last_routing: bad arguments");
+    const size_t n = (size_t)T * m->cfg.top_k;
+    cudaSetDevice(m->device);
+    if (ids && !cuda_ok(cudaMemcpy(ids, m->ids.p, sizeof(int) * n, cudaMemcpyDeviceToHost), "ids")) return HXB_E_DEVICE;
+    if (weights && !cuda_ok(cudaMemcpy(weights, m->wts.p, sizeof(float) * n, cudaMemcpyDeviceToHost), "wts"))
+        return HXB_E_DEVICE;
+    return HXB_OK;
+}
+
+extern "C" HXB_API int hxb_moe_get_stats(hxb_moe *m, hxb_moe_stats *out) {
+    if (!m || !out) return fail(HXB_E_ARG, "get_stats: bad arguments");
+    *out = m->st;
+    const StoreStats ss = m->store.stats();
+    if (m->resident_mode) {
+        out->hits = out->expert_uses;
+        out->misses = 0;
+    } else {
+        out->hits = ss.hits;
+        out->misses = ss.misses;
+    }
+    out->evictions = ss.evictions;
+    out->prefetch_issued = ss.prefetch_issued;
+    out->prefetch_used = ss.prefetch_used;
+    out->prefetch_wasted = ss.prefetch_wasted;
+    out->bytes_copied = ss.bytes_copied;
+    out->copies = ss.copies;
+    out->copy_errors = ss.copy_errors;
+    out->n_slots = m->store.n_slots();
+    out->resident = m->store.n_ready();
+    out->pinned = m->store.n_pinned();
+    out->slot_bytes = m->slab_bytes;
+    return HXB_OK;
+}
+
+extern "C" HXB_API void hxb_moe_reset_stats(hxb_moe *m) {
+    if (!m) return;
+    const int ns = m->st.n_slots;
+    m->st = hxb_moe_stats();
+    m->st.n_slots = ns;
+    m->store.reset_stats();
+}
+
+extern "C" HXB_API int hxb_moe_is_resident(hxb_moe *m, int layer, int expert) {
+    if (!m || layer < 0 || layer >= m->cfg.n_layers || expert < 0 || expert >= m->cfg.n_experts) return 0;
+    return m->store.is_resident(layer, expert) ? 1 : 0;
+}
+
+extern "C" HXB_API void hxb_moe_tick(hxb_moe *m) {
+    if (m) m->store.tick();
+}
+
+extern "C" HXB_API int hxb_moe_prefetch(hxb_moe *m, int layer, const int *experts, int n) {
+    if (!m || layer < 0 || layer >= m->cfg.n_layers || n < 0 || (n && !experts)) return fail(HXB_E_ARG, "prefetch: bad arguments");
+    cudaSetDevice(m->device);
+    m->store.prefetch(layer, experts, n);
+    return HXB_OK;
+}
+
+extern "C" HXB_API int hxb_moe_seed_heat(hxb_moe *m, const float *counts, int n_keys, float pin_fraction,
+                                         int warm_start) {
+    if (!m || !counts || n_keys != m->cfg.n_layers * m->cfg.n_experts) return fail(HXB_E_ARG, "seed_heat: bad arguments");
+    cudaSetDevice(m->device);
+    m->store.seed_heat(counts, n_keys, pin_fraction, warm_start != 0);
+    cudaStreamSynchronize(m->store.copy_stream());
+    return HXB_OK;
+}
+
+extern "C" HXB_API void hxb_moe_set_copy_hook(hxb_moe *m, hxb_copy_hook fn, void *ctx) {
+    if (!m) return;
+    if (!fn) m->store.set_copy_hook(nullptr);
+    else m->store.set_copy_hook([fn, ctx](int layer, int expert) { return fn(ctx, layer, expert); });
+}
+
+extern "C" HXB_API int hxb_moe_sync(hxb_moe *m, void *stream) {
+    if (!m) return fail(HXB_E_ARG, "sync: null handle");
+    cudaSetDevice(m->device);
+    cudaStream_t s = stream ? (cudaStream_t)stream : m->stream;
+    if (!cuda_ok(cudaStreamSynchronize(s), "sync")) return HXB_E_DEVICE;
+    int word = 0;
+    if (!cuda_ok(cudaMemcpy(&word, m->err.p, sizeof word, cudaMemcpyDeviceToHost), "error word")) return HXB_E_DEVICE;
+    return take_device_error(m, word);
+}
+
+// Per-kernel device times of one resident layer evaluation (eager launches bracketed by CUDA
+// events on the handle's stream, averaged over iters x layers): us[0] norm+activation,
+// us[1] router+routing, us[2] gate/up+SwiGLU, us[3] down+rank-order sum. For roofline accounting;
+// the graph path runs the same kernels back to back.
+extern "C" HXB_API int hxb_moe_profile(hxb_moe *m, int T, int iters, double *us) {
+    int rc = check_eval(m, T, 0, m ? m->cfg.n_layers : 1);
+    if (rc) return rc;
+    if (!m->resident_mode || iters <= 0 || !us) return fail(HXB_E_ARG, "profile: needs every expert resident");
+    const MoeScratch sc = m->scratch();
+    const MoeShape sh = m->shape(T);
+    cudaEvent_t ev[5];
+    for (auto &e : ev) cudaEventCreate(&e);
+    double acc[4] = {0, 0, 0, 0};
+    float *h = m->hbuf.as<float>();
+    cudaMemsetAsync(h, 0, sizeof(float) * (size_t)T * m->cfg.d_model, m->stream);
+    launch_synth_f32(h, (int64_t)T * m->cfg.d_model, 77, 1.0f, m->stream);
+    int n = 0;
+    for (int it = 0; it < iters; it++)
+        for (int l = 0; l < m->cfg.n_layers; l++) {
+            const MoeLayerDev L = m->layer_dev(l, true);
+            cudaEventRecord(ev[0], m->stream);
+            launch_moe_stage(0, sh, L, sc, h, nullptr, true, m->stream);
+            cudaEventRecord(ev[1], m->stream);
+            launch_moe_stage(1, sh, L, sc, h, nullptr, true, m->stream);
+            cudaEventRecord(ev[2], m->stream);
+            launch_moe_stage(2, sh, L, sc, h, nullptr, true, m->stream);
+            cudaEventRecord(ev[3], m->stream);
+            launch_moe_stage(3, sh, L, sc, h, nullptr, true, m->stream);
+            cudaEventRecord(ev[4], m->stream);
+            if (!cuda_ok(cudaEventSynchronize(ev[4]), "profile")) return HXB_E_DEVICE;
+            for (int k = 0; k < 4; k++) {
+                float ms = 0;
+                cudaEventElapsedTime(&ms, ev[k], ev[k + 1]);
+                acc[k] += ms * 1000.0;
+            }
+            n++;
+        }
+    for (auto &e : ev) cudaEventDestroy(e);
+    for (int k = 0; k < 4; k++) us[k] = acc[k] / n;
+    int word = 0;
+    cudaMemcpy(&word, m->err.p, sizeof word, cudaMemcpyDeviceToHost);
+    return take_device_error(m, word);
+}

@@ -1,0 +1,137 @@
+// hx_device.cuh — sm_100a plumbing shared by the kernels: shared-memory addresses, mbarriers with
+// bounded waits, 1-D bulk copies (cp.async.bulk, no cluster multicast), the device error word,
+// and the canonical row-chain machinery of the quantized GEMV tiles.
+#pragma once
+
+#include "hx_common.cuh"
+
+namespace hx {
+
+// Error codes a kernel leaves in the device error word (first one wins).
+enum : int {
+    DEV_OK = 0,
+    DEV_E_WAIT_TIMEOUT = 1,   // a bulk copy did not complete within the spin limit
+    DEV_E_NOT_RESIDENT = 2,   // a routed expert had no slab in HBM
+    DEV_E_BAD_DTYPE = 3,      // an expert dtype the kernels do not handle
+};
+
+constexpr uint32_t kSpinLimit = 1u << 24;   // try_wait rounds before a wait is declared lost
+
+__device__ __forceinline__ uint32_t smem_u32(const void *p) {
+    return static_cast<uint32_t>(__cvta_generic_to_shared(p));
+}
+
+__device__ __forceinline__ void set_error(int *err, int code) {
+    if (err) atomicCAS(err, 0, code);
+}
+
+__device__ __forceinline__ void mbar_init(uint64_t *bar, uint32_t count) {
+    asm volatile("mbarrier.init.shared::cta.b64 [%0], %1;" ::"r"(smem_u32(bar)), "r"(count) : "memory");
+}
+
+__device__ __forceinline__ void fence_mbar_init() {
+    asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
+}
+
+__device__ __forceinline__ void fence_proxy_async() {
+    asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
+}
+
+__device__ __forceinline__ void mbar_expect_tx(uint64_t *bar, uint32_t bytes) {
+    asm volatile("mbarrier.arrive.expect_tx.shared::cta.b64 _, [%0], %1;" ::"r"(smem_u32(bar)), "r"(bytes)
+                 : "memory");
+}
+
+// 1-D bulk copy global -> this CTA's shared memory, completion counted on bar.
+// dst, src 16-byte aligned; bytes a multiple of 16.
+__device__ __forceinline__ void bulk_g2s(void *dst, const void *src, uint32_t bytes, uint64_t *bar) {
+    asm volatile(
+        "cp.async.bulk.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1], %2, [%3];" ::"r"(
+            smem_u32(dst)),
+        "l"(src), "r"(bytes), "r"(smem_u32(bar))
+        : "memory");
+}
+
+__device__ __forceinline__ bool mbar_try_wait(uint64_t *bar, uint32_t parity) {
+    uint32_t ok;
+    asm volatile(
+        "{\n\t.reg .pred p;\n\t"
+        "mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2;\n\t"
+        "selp.u32 %0, 1, 0, p;\n\t}"
+        : "=r"(ok)
+        : "r"(smem_u32(bar)), "r"(parity)
+        : "memory");
+    return ok != 0;
+}
+
+// Bounded wait on an mbarrier phase: returns false (and records the error) when the limit is hit.
+__device__ __forceinline__ bool mbar_wait(uint64_t *bar, uint32_t parity, int *err) {
+    for (uint32_t i = 0; i < kSpinLimit; i++)
+        if (mbar_try_wait(bar, parity)) return true;
+    set_error(err, DEV_E_WAIT_TIMEOUT);
+    return false;
+}
+
+// ---------------------------------------------------------------------------------------------
+// Quantized row tiles. A tile is `rows` consecutive rows of a Q4/Q8 matrix with nb blocks per
+// row, resident in shared memory (row stride rb bytes). For each (row, token) the canonical
+// NUMERICS §3 value is acc = ((0 + t_0) + t_1) + ... with t_g = (float)isum_g * (dw_g * dx_g).
+//
+// Work split inside one warp: the (row, block) items of the warp's rows are spread over the 32
+// lanes; each lane writes its block terms into the warp's term buffer P[chain][g], one chain per
+// (row, token); then one lane per chain adds its terms in block order. The integer dots and the
+// products are independent, only the adds form a chain, and that chain runs in exactly the
+// reference's order.
+// ---------------------------------------------------------------------------------------------
+
+// Warp-level: rows rlist[0..nr) of the tile (local row indices) against tokens 0..nt whose
+// activation rows (nb blocks each) start at act + tok_off[i]. Writes the canonical value of
+// (rlist[k], token i) to out[k * ok + i * oi]. Blocks are taken 32 at a time; the chain lane keeps
+// its running sum across those chunks, so P holds nr * nt * 33 floats whatever nb is. nr * nt <= 32.
+template <int DT>
+__device__ __forceinline__ void warp_rows(const uint8_t *tile, int64_t rb, int nb, const int *rlist, int nr,
+                                          const act_q8 *act, const int *tok_off, int nt, float *P, float *out,
+                                          int ok, int oi) {
+    const int lane = threadIdx.x & 31;
+    const int nch = nr * nt;
+    constexpr int BS = DT == Q4 ? Q4_BLOCK : Q8_BLOCK;
+    float acc = 0.0f;
+    for (int g0 = 0; g0 < nb; g0 += 32) {
+        const int gn = min(32, nb - g0);
+        const int items = nr * gn;
+        for (int it = lane; it < items; it += 32) {
+            const int k = it / gn, g = it - k * gn;
+            const uint8_t *blk = tile + (int64_t)rlist[k] * rb + (int64_t)(g0 + g) * BS;
+            float *pk = P + (k * nt) * 33 + g;
+            if constexpr (DT == Q4) {
+                uint32_t nib[8];
+                const float dw = f16_to_f32(load_q4_block(blk, nib));
+                for (int i = 0; i < nt; i++) {
+                    act_regs ar;
+                    load_act(act + tok_off[i] + g0 + g, ar);
+                    pk[i * 33] = __fmul_rn(__int2float_rn(q4_isum(nib, ar.q, ar.sum)), __fmul_rn(dw, ar.d));
+                }
+            } else {
+                uint32_t q[16];
+                const float dw = f16_to_f32(load_q8_block(blk, q));
+                for (int i = 0; i < nt; i++) {
+                    act_regs ar;
+                    load_act(act + tok_off[i] + g0 + g, ar);
+                    pk[i * 33] = __fmul_rn(__int2float_rn(q8_isum(q, ar.q)), __fmul_rn(dw, ar.d));
+                }
+            }
+        }
+        __syncwarp();
+        if (lane < nch) {
+            const float *p = P + lane * 33;
+            for (int g = 0; g < gn; g++) acc = __fadd_rn(acc, p[g]);
+        }
+        __syncwarp();
+    }
+    if (lane < nch) {
+        const int k = lane / nt, i = lane - k * nt;
+        out[k * ok + i * oi] = canon(acc);
+    }
+}
+
+}  // namespace hx

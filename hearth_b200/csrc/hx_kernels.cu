@@ -1,0 +1,955 @@
+// hx_kernels.cu — hand-written sm_100a kernels of the quantized MoE expert path.
+//
+// Every float result follows the canonical operation order of the reference
+// (pierce-lonergan/hearth docs/NUMERICS.md): integer block dots are exact and may be computed in
+// any order; every float sum runs in the reference's order with one rounding per operation.
+#include "hx_device.cuh"
+#include "hx_kernels.h"
+
+#include <algorithm>
+
+namespace hx {
+
+// =============================================================================================
+// Activation quantization (NUMERICS §2, engine/src/quant.c:325-348): one warp per 64-block.
+// =============================================================================================
+
+__device__ __forceinline__ void act_quant_warp(float x0, float x1, act_q8 *o, int lane) {
+    float amax = fmaxf(fabsf(x0), fabsf(x1));   // fmaxf drops NaN, like `a > amax` in C
+#pragma unroll
+    for (int s = 16; s >= 1; s >>= 1) amax = fmaxf(amax, __shfl_xor_sync(0xffffffffu, amax, s));
+    amax = fmaxf(amax, 0.0f);
+    const float d = __fdiv_rn(amax, 127.0f);
+    const float id = d != 0.0f ? __fdiv_rn(1.0f, d) : 0.0f;
+    float v0 = __fmul_rn(x0, id), v1 = __fmul_rn(x1, id);
+    if (v0 != v0) v0 = 0.0f;
+    if (v1 != v1) v1 = 0.0f;
+    v0 = v0 > 127.0f ? 127.0f : (v0 < -127.0f ? -127.0f : v0);
+    v1 = v1 > 127.0f ? 127.0f : (v1 < -127.0f ? -127.0f : v1);
+    const int q0 = __float2int_rn(v0), q1 = __float2int_rn(v1);   // round half to even
+    int sum = q0 + q1;
+#pragma unroll
+    for (int s = 16; s >= 1; s >>= 1) sum += __shfl_xor_sync(0xffffffffu, sum, s);
+    o->q[lane] = (int8_t)q0;
+    o->q[lane + 32] = (int8_t)q1;
+    if (lane == 0) {
+        o->d = d;
+        o->sum = sum;
+    }
+}
+
+__global__ void k_act_quantize(const float *__restrict__ x, int64_t ldx, act_q8 *__restrict__ out, int nb,
+                               int T) {
+    const int64_t w = ((int64_t)blockIdx.x * blockDim.x + threadIdx.x) >> 5;
+    const int lane = threadIdx.x & 31;
+    if (w >= (int64_t)T * nb) return;
+    const int64_t t = w / nb, b = w - t * nb;
+    const float *xb = x + t * ldx + b * QK;
+    act_quant_warp(xb[lane], xb[lane + 32], out + w, lane);
+}
+
+cudaError_t launch_act_quantize(const float *x, int64_t ldx, act_q8 *out, int64_t n, int T, cudaStream_t s) {
+    const int nb = (int)(n / QK);
+    const int64_t warps = (int64_t)nb * T;
+    if (warps == 0) return cudaSuccess;
+    k_act_quantize<<<(unsigned)((warps + 7) / 8), 256, 0, s>>>(x, ldx, out, nb, T);
+    return cudaGetLastError();
+}
+
+// =============================================================================================
+// Generic row-range matmul (the hearth_matmul boundary, engine/src/quant.c:352-427, 574-600).
+// =============================================================================================
+
+// Quantized weights: one warp per row, up to 16 tokens per pass, block terms chained per
+// (row, token) in block order.
+template <int DT>
+__global__ void __launch_bounds__(256) k_matmul_q(const uint8_t *__restrict__ W, int nb, int64_t rb,
+                                                  const act_q8 *__restrict__ act, int T, float *__restrict__ Y,
+                                                  int64_t ldy, int64_t r0, int64_t r1) {
+    __shared__ float Pbuf[8][16 * 33];
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    const int64_t r = r0 + (int64_t)blockIdx.x * 8 + warp;
+    if (r >= r1) return;
+    float *P = Pbuf[warp];
+    constexpr int BS = DT == Q4 ? Q4_BLOCK : Q8_BLOCK;
+    const uint8_t *row = W + r * rb;
+    for (int t0 = blockIdx.y * 16; t0 < T; t0 += gridDim.y * 16) {
+        const int nt = min(16, T - t0);
+        float acc = 0.0f;
+        for (int g0 = 0; g0 < nb; g0 += 32) {
+            const int gn = min(32, nb - g0);
+            if (lane < gn) {
+                const int g = g0 + lane;
+                const uint8_t *blk = row + (int64_t)g * BS;
+                uint32_t wq[16];
+                float dw;
+                if constexpr (DT == Q4) dw = f16_to_f32(load_q4_block(blk, wq));
+                else dw = f16_to_f32(load_q8_block(blk, wq));
+                for (int i = 0; i < nt; i++) {
+                    act_regs ar;
+                    load_act(act + (int64_t)(t0 + i) * nb + g, ar);
+                    int isum;
+                    if constexpr (DT == Q4) isum = q4_isum(wq, ar.q, ar.sum);
+                    else isum = q8_isum(wq, ar.q);
+                    P[i * 33 + lane] = __fmul_rn(__int2float_rn(isum), __fmul_rn(dw, ar.d));
+                }
+            }
+            __syncwarp();
+            if (lane < nt)
+                for (int g = 0; g < gn; g++) acc = __fadd_rn(acc, P[lane * 33 + g]);
+            __syncwarp();
+        }
+        if (lane < nt) Y[(int64_t)(t0 + lane) * ldy + r] = canon(acc);
+    }
+}
+
+// Float weights: NUMERICS §1 dot16, one 16-lane group per (row, token).
+template <int DT>
+__device__ __forceinline__ float load_wf(const uint8_t *row, int64_t i) {
+    if constexpr (DT == F32) return reinterpret_cast<const float *>(row)[i];
+    else if constexpr (DT == F16) return f16_to_f32(reinterpret_cast<const uint16_t *>(row)[i]);
+    else return bf16_to_f32(reinterpret_cast<const uint16_t *>(row)[i]);
+}
+
+template <int DT>
+__device__ __forceinline__ float dot16_group(const uint8_t *row, const float *x, int64_t n, int j) {
+    float L = 0.0f;
+    for (int64_t i = j; i < n; i += 16) L = __fadd_rn(L, __fmul_rn(load_wf<DT>(row, i), x[i]));
+    return L;
+}
+
+template <int DT>
+__global__ void __launch_bounds__(256) k_matmul_f(const uint8_t *__restrict__ W, int64_t n, int64_t rb,
+                                                  const float *__restrict__ X, int T, float *__restrict__ Y,
+                                                  int64_t ldy, int64_t r0, int64_t r1) {
+    const int grp = threadIdx.x >> 4, j = threadIdx.x & 15;
+    const int64_t item = (int64_t)blockIdx.x * 16 + grp;   // (row, token) item
+    const int64_t rows = r1 - r0;
+    const bool valid = item < rows * T;
+    const int64_t r = valid ? r0 + item % rows : r0;
+    const int64_t t = valid ? item / rows : 0;
+    float L = valid ? dot16_group<DT>(W + r * rb, X + t * n, n, j) : 0.0f;
+    const unsigned mask = 0xffffffffu;
+    L = tree16(L, mask);
+    if (valid && j == 0) Y[t * ldy + r] = canon(L);
+}
+
+cudaError_t launch_matmul(int dtype, const void *W, int64_t n_cols, const void *act, int T, float *Y,
+                          int64_t ldy, int64_t r0, int64_t r1, cudaStream_t s) {
+    const int64_t rows = r1 - r0;
+    if (rows <= 0 || T <= 0) return cudaSuccess;
+    const int64_t rb = row_bytes(dtype, n_cols);
+    const uint8_t *w = static_cast<const uint8_t *>(W);
+    if (is_quant(dtype)) {
+        const int nb = (int)(n_cols / QK);
+        dim3 grid((unsigned)((rows + 7) / 8), (unsigned)std::min<int64_t>((T + 15) / 16, 65535));
+        if (dtype == Q4)
+            k_matmul_q<Q4><<<grid, 256, 0, s>>>(w, nb, rb, (const act_q8 *)act, T, Y, ldy, r0, r1);
+        else
+            k_matmul_q<Q8><<<grid, 256, 0, s>>>(w, nb, rb, (const act_q8 *)act, T, Y, ldy, r0, r1);
+    } else {
+        const int64_t items = rows * T;
+        const unsigned grid = (unsigned)((items + 15) / 16);
+        const float *x = static_cast<const float *>(act);
+        if (dtype == F32) k_matmul_f<F32><<<grid, 256, 0, s>>>(w, n_cols, rb, x, T, Y, ldy, r0, r1);
+        else if (dtype == F16) k_matmul_f<F16><<<grid, 256, 0, s>>>(w, n_cols, rb, x, T, Y, ldy, r0, r1);
+        else k_matmul_f<BF16><<<grid, 256, 0, s>>>(w, n_cols, rb, x, T, Y, ldy, r0, r1);
+    }
+    return cudaGetLastError();
+}
+
+// hearth_dequantize (engine/src/quant.c:257-307): w = f16(d) * q, one element per thread.
+__global__ void k_dequantize(int dtype, const uint8_t *__restrict__ W, int64_t n_rows, int64_t n_cols, int64_t rb,
+                             float *__restrict__ out) {
+    const int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
+    if (i >= n_rows * n_cols) return;
+    const int64_t r = i / n_cols, c = i - r * n_cols;
+    const uint8_t *row = W + r * rb;
+    float v;
+    switch (dtype) {
+    case F32: v = reinterpret_cast<const float *>(row)[c]; break;
+    case F16: v = f16_to_f32(reinterpret_cast<const uint16_t *>(row)[c]); break;
+    case BF16: v = bf16_to_f32(reinterpret_cast<const uint16_t *>(row)[c]); break;
+    case Q8: {
+        const uint8_t *blk = row + (c / QK) * Q8_BLOCK;
+        v = __fmul_rn(f16_to_f32((uint32_t)blk[0] | ((uint32_t)blk[1] << 8)), (float)(int8_t)blk[2 + c % QK]);
+        break;
+    }
+    default: {
+        const uint8_t *blk = row + (c / QK) * Q4_BLOCK;
+        const int j = (int)(c % QK);
+        const int nib = j < 32 ? (blk[2 + j] & 15) : (blk[2 + j - 32] >> 4);
+        v = __fmul_rn(f16_to_f32((uint32_t)blk[0] | ((uint32_t)blk[1] << 8)), (float)(nib - 8));
+        break;
+    }
+    }
+    out[i] = v;
+}
+
+cudaError_t launch_dequantize(int dtype, const void *W, int64_t n_rows, int64_t n_cols, float *out,
+                              cudaStream_t s) {
+    const int64_t n = n_rows * n_cols;
+    if (n <= 0) return cudaSuccess;
+    k_dequantize<<<(unsigned)((n + 255) / 256), 256, 0, s>>>(dtype, (const uint8_t *)W, n_rows, n_cols,
+                                                             row_bytes(dtype, n_cols), out);
+    return cudaGetLastError();
+}
+
+// =============================================================================================
+// MoE: normalisation + activation, router, routing.
+// =============================================================================================
+
+// One CTA per token: x = rmsnorm(h, w) (NUMERICS §4) or x = h, then x's activation blocks.
+__global__ void __launch_bounds__(256) k_moe_norm_act(const float *__restrict__ h, const float *__restrict__ w,
+                                                      float eps, int D, float *__restrict__ x,
+                                                      act_q8 *__restrict__ xact) {
+    __shared__ float xs[8192];
+    __shared__ float rsh;
+    const int t = blockIdx.x, tid = threadIdx.x;
+    const float *ht = h + (int64_t)t * D;
+    for (int i = tid; i < D; i += blockDim.x) xs[i] = ht[i];
+    __syncthreads();
+    if (w) {
+        if (tid < 16) {   // ms = dot16(h, h) / n ; r = 1 / sqrtf(ms + eps)
+            float L = 0.0f;
+            for (int i = tid; i < D; i += 16) L = __fadd_rn(L, __fmul_rn(xs[i], xs[i]));
+            L = tree16(L, 0xffffu);
+            if (tid == 0) {
+                const float ms = __fdiv_rn(L, (float)D);
+                rsh = __fdiv_rn(1.0f, __fsqrt_rn(__fadd_rn(ms, eps)));
+            }
+        }
+        __syncthreads();
+        const float r = rsh;
+        for (int i = tid; i < D; i += blockDim.x) xs[i] = __fmul_rn(__fmul_rn(xs[i], r), w[i]);
+        __syncthreads();
+    }
+    float *xt = x + (int64_t)t * D;
+    for (int i = tid; i < D; i += blockDim.x) xt[i] = xs[i];
+    const int warp = tid >> 5, lane = tid & 31, nb = D / QK;
+    for (int b = warp; b < nb; b += blockDim.x >> 5)
+        act_quant_warp(xs[b * QK + lane], xs[b * QK + lane + 32], xact + (int64_t)t * nb + b, lane);
+}
+
+// Top-k routing of one token by one warp (engine/src/model.c:793-843, NUMERICS §5.3).
+// logit: [E] (global, written by other CTAs: read through L2), score/sel: [E] shared scratch.
+__device__ void route_token_warp(const RouteCfg &R, const float *logit, const float *bias, float *score,
+                                 float *sel, int *ids_out, float *w_out) {
+    const int lane = threadIdx.x & 31, E = R.E, K = R.K;
+    if (R.score_fn == SCORE_SOFTMAX) {
+        float m = -__uint_as_float(0x7f800000u);
+        for (int i = lane; i < E; i += 32) m = fmaxf(m, __ldcg(logit + i));
+#pragma unroll
+        for (int s = 16; s >= 1; s >>= 1) m = fmaxf(m, __shfl_xor_sync(0xffffffffu, m, s));
+        const float x0 = __ldcg(logit);
+        if (x0 != x0) m = x0;   // `m = x[0]; m = x[i] > m ? x[i] : m` keeps a leading NaN
+        for (int i = lane; i < E; i += 32) score[i] = host_expf(__fsub_rn(__ldcg(logit + i), m));
+        __syncwarp();
+        float L = 0.0f;
+        if (lane < 16)
+            for (int i = lane; i < E; i += 16) L = __fadd_rn(L, score[i]);
+        L = tree16(L, 0xffffffffu);
+        const float ssum = __shfl_sync(0xffffffffu, L, 0);
+        for (int i = lane; i < E; i += 32) score[i] = __fdiv_rn(score[i], ssum);
+    } else {
+        for (int i = lane; i < E; i += 32) score[i] = sigmoid_c(__ldcg(logit + i));
+    }
+    __syncwarp();
+    for (int i = lane; i < E; i += 32) sel[i] = (R.score_bias && bias) ? __fadd_rn(score[i], bias[i]) : score[i];
+    __syncwarp();
+    if (R.n_group > 1) {
+        const int ng = R.n_group, gs = E / ng;
+        // group score: sum of the group's top-2 selection values (model.c:801-812)
+        float gsc = 0.0f;
+        if (lane < ng) {
+            const float *v = sel + lane * gs;
+            int i1 = 0, i2 = -1;
+            for (int i = 1; i < gs; i++) {
+                if (ranks_before(v[i], i, v[i1], i1)) {
+                    i2 = i1;
+                    i1 = i;
+                } else if (i2 < 0 || ranks_before(v[i], i, v[i2], i2)) {
+                    i2 = i;
+                }
+            }
+            gsc = i2 >= 0 ? __fadd_rn(v[i1], v[i2]) : v[i1];
+        }
+        unsigned keep = 0;
+        for (int r = 0; r < R.topk_group; r++) {
+            float bv = gsc;
+            int bi = (lane < ng && !((keep >> lane) & 1u)) ? lane : -1;
+#pragma unroll
+            for (int s = 16; s >= 1; s >>= 1) {
+                const float ov = __shfl_xor_sync(0xffffffffu, bv, s);
+                const int oi = __shfl_xor_sync(0xffffffffu, bi, s);
+                if (oi >= 0 && (bi < 0 || ranks_before(ov, oi, bv, bi))) {
+                    bv = ov;
+                    bi = oi;
+                }
+            }
+            keep |= 1u << bi;
+        }
+        for (int i = lane; i < E; i += 32)
+            if (!((keep >> (i / gs)) & 1u)) sel[i] = 0.0f;
+        __syncwarp();
+    }
+    // top-K by selection value, descending, ties to the lower index, NaN last
+    unsigned taken[12] = {0};   // E <= 384: lane owns i = lane + 32 m
+    int myid = -1;
+    for (int j = 0; j < K; j++) {
+        float bv = 0.0f;
+        int bi = -1;
+        for (int m = 0, i = lane; i < E; m++, i += 32) {
+            if (taken[m]) continue;
+            const float v = sel[i];
+            if (bi < 0 || ranks_before(v, i, bv, bi)) {
+                bv = v;
+                bi = i;
+            }
+        }
+#pragma unroll
+        for (int s = 16; s >= 1; s >>= 1) {
+            const float ov = __shfl_xor_sync(0xffffffffu, bv, s);
+            const int oi = __shfl_xor_sync(0xffffffffu, bi, s);
+            if (oi >= 0 && (bi < 0 || ranks_before(ov, oi, bv, bi))) {
+                bv = ov;
+                bi = oi;
+            }
+        }
+        if ((bi & 31) == lane) taken[bi >> 5] = 1u;
+        if (lane == j) myid = bi;
+    }
+    // weights (route_weights, model.c:833-843): score of the chosen expert, optional
+    // renormalisation by the rank-order sum + 1e-20f, then routed_scale
+    // gather the K ids to every lane
+    int idj = -1;
+    float wj = 0.0f;
+    if (lane < K) {
+        idj = myid;
+        wj = score[myid];
+    }
+    // sequential renormalisation sum in rank order (lane 0), then divide and scale
+    float den = 1.0f;
+    if (R.norm_topk_prob) {
+        float s = 0.0f;
+        for (int j = 0; j < K; j++) s = __fadd_rn(s, __shfl_sync(0xffffffffu, wj, j));
+        den = __fadd_rn(s, 1e-20f);
+    }
+    if (lane < K) {
+        float v = wj;
+        if (R.norm_topk_prob) v = __fdiv_rn(v, den);
+        v = __fmul_rn(v, R.routed_scale);
+        ids_out[lane] = idj;
+        w_out[lane] = v;
+    }
+}
+
+// Expert buckets of the batch (engine/src/model.c:1020-1037), by one CTA: experts ascending,
+// tokens ascending within an expert; pair_of[t*K + j] is the pair of token t's rank j.
+__device__ void route_union_cta(int T, int K, int E, const int *ids, int *cnt, int *start, int *nu_out,
+                                int *ulist, int *u_p0, int *u_n, int *pair_tok, int *pair_of) {
+    const int tid = threadIdx.x, nt = blockDim.x;
+    for (int e = tid; e < E; e += nt) cnt[e] = 0;
+    __syncthreads();
+    for (int i = tid; i < T * K; i += nt) atomicAdd(&cnt[__ldcg(ids + i)], 1);
+    __syncthreads();
+    if (tid == 0) {
+        int nu = 0, p = 0;
+        for (int e = 0; e < E; e++) {
+            start[e] = p;
+            if (!cnt[e]) continue;
+            ulist[nu] = e;
+            u_p0[nu] = p;
+            u_n[nu] = cnt[e];
+            p += cnt[e];
+            nu++;
+        }
+        *nu_out = nu;
+    }
+    __syncthreads();
+    for (int e = tid; e < E; e += nt) {
+        if (!cnt[e]) continue;
+        int p = start[e];
+        for (int t = 0; t < T; t++)
+            for (int j = 0; j < K; j++)
+                if (__ldcg(ids + t * K + j) == e) {
+                    pair_tok[p] = t;
+                    pair_of[t * K + j] = p;
+                    p++;
+                }
+    }
+}
+
+// Router logits (F32 dot16 rows, canonical NaN) and the shared-expert gate logit, one 16-lane
+// group per (row, token). With fuse_route the last CTA to finish routes every token and builds
+// the buckets.
+__global__ void __launch_bounds__(256) k_moe_router(MoeShape sh, const float *__restrict__ router,
+                                                    const float *__restrict__ gate_inp,
+                                                    const float *__restrict__ bias, MoeScratch sc, int fuse_route) {
+    extern __shared__ float rsm[];
+    __shared__ int last;
+    const int D = sh.D, E = sh.route.E, T = sh.T;
+    const int rows = E + (gate_inp ? 1 : 0);
+    const int grp = threadIdx.x >> 4, j = threadIdx.x & 15;
+    const int64_t item = (int64_t)blockIdx.x * (blockDim.x >> 4) + grp;
+    const bool valid = item < (int64_t)rows * T;
+    const int r = valid ? (int)(item % rows) : 0;
+    const int t = valid ? (int)(item / rows) : 0;
+    const float *x = sc.x + (int64_t)t * D;
+    const float *w = r < E ? router + (int64_t)r * D : gate_inp;
+    float L = 0.0f;
+    if (valid) {
+#pragma unroll 8
+        for (int i = j; i < D; i += 16) L = __fadd_rn(L, __fmul_rn(__ldg(w + i), x[i]));
+    }
+    L = tree16(L, 0xffffffffu);
+    if (valid && j == 0) {
+        if (r < E) sc.logits[(int64_t)t * E + r] = canon(L);
+        else sc.sh_logit[t] = L;
+    }
+    if (!fuse_route) return;
+    __syncthreads();
+    if (threadIdx.x == 0) {
+        __threadfence();
+        const unsigned ticket = atomicAdd(sc.ticket, 1u);
+        last = ticket == gridDim.x - 1;
+    }
+    __syncthreads();
+    if (!last) return;
+    __threadfence();
+    // this CTA saw every other CTA's logits: route each token (one warp per token)
+    const int warp = threadIdx.x >> 5, nwarps = blockDim.x >> 5;
+    float *score = rsm + warp * 2 * E, *sel = score + E;
+    for (int tt = warp; tt < T; tt += nwarps)
+        route_token_warp(sh.route, sc.logits + (int64_t)tt * E, bias, score, sel, sc.ids + tt * sh.route.K,
+                         sc.wts + tt * sh.route.K);
+    __syncthreads();
+    __threadfence_block();
+    int *cnt = reinterpret_cast<int *>(rsm), *start = cnt + E;
+    route_union_cta(T, sh.route.K, E, sc.ids, cnt, start, sc.nu, sc.ulist, sc.u_p0, sc.u_n, sc.pair_tok,
+                    sc.pair_of);
+    if (threadIdx.x == 0) *sc.ticket = 0u;   // ready for the next launch
+}
+
+__global__ void __launch_bounds__(256) k_route_select(MoeShape sh, const float *__restrict__ bias, MoeScratch sc) {
+    extern __shared__ float rsm[];
+    const int warp = threadIdx.x >> 5, E = sh.route.E;
+    const int t = blockIdx.x * 8 + warp;
+    if (t >= sh.T) return;
+    float *score = rsm + warp * 2 * E, *sel = score + E;
+    route_token_warp(sh.route, sc.logits + (int64_t)t * E, bias, score, sel, sc.ids + t * sh.route.K,
+                     sc.wts + t * sh.route.K);
+}
+
+__global__ void __launch_bounds__(512) k_route_union(MoeShape sh, MoeScratch sc) {
+    extern __shared__ int usm[];
+    route_union_cta(sh.T, sh.route.K, sh.route.E, sc.ids, usm, usm + sh.route.E, sc.nu, sc.ulist, sc.u_p0,
+                    sc.u_n, sc.pair_tok, sc.pair_of);
+}
+
+// =============================================================================================
+// MoE experts. A "job" is one routed expert bucket (jobs 0..nu-1, experts ascending) or the
+// shared expert over all tokens (job nu). Activation rows of job pairs: routed pair p -> p,
+// shared token t -> T*K + t.
+// =============================================================================================
+
+struct Job {
+    const uint8_t *gate, *up, *down;
+    int dtype, F, nbF, n, p0;   // rows of gate/up, down's blocks per row, tokens, first pair
+    bool shared;
+};
+
+__device__ __forceinline__ bool get_job(const MoeShape &sh, const MoeLayerDev &L, const MoeScratch &sc, int u,
+                                        int nu, Job &j) {
+    if (u < nu) {
+        const int e = sc.ulist[u];
+        const uint8_t *slab = L.slab[e];
+        if (!slab) {
+            set_error(sc.err, DEV_E_NOT_RESIDENT);
+            return false;
+        }
+        j.gate = slab;
+        j.up = slab + L.off_up;
+        j.down = slab + L.off_down;
+        j.dtype = L.expert_dtype;
+        j.F = sh.F;
+        j.n = sc.u_n[u];
+        j.p0 = sc.u_p0[u];
+        j.shared = false;
+    } else {
+        j.gate = L.sh_gate;
+        j.up = L.sh_up;
+        j.down = L.sh_down;
+        j.dtype = L.sh_dtype;
+        j.F = L.Fs;
+        j.n = sh.T;
+        j.p0 = sh.T * sh.route.K;
+        j.shared = true;
+    }
+    j.nbF = j.F / QK;
+    if (j.dtype != Q4 && j.dtype != Q8) {
+        set_error(sc.err, DEV_E_BAD_DTYPE);
+        return false;
+    }
+    return true;
+}
+
+__device__ __forceinline__ int job_token(const MoeScratch &sc, const Job &j, int i) {
+    return j.shared ? i : sc.pair_tok[j.p0 + i];
+}
+
+constexpr int GU_ROWS = 64;    // gate/up rows per CTA: one activation block of the mid vector
+constexpr int GU_CH = 8;       // rows of gate (and of up) per pipeline stage
+constexpr int GU_NCH = GU_ROWS / GU_CH;
+constexpr int DN_ROWS = 16;    // down rows per CTA
+
+struct GateUpCfg {
+    int nst;        // pipeline stages
+    int ntok;       // tokens per pass
+    int64_t stage;  // bytes per stage (max over the jobs' dtypes)
+    int nbD;
+    int fmax_nb;    // activation blocks per mid row (max of F, Fs over 64)
+};
+
+template <int DT>
+__device__ void gateup_body(const MoeShape &sh, const MoeScratch &sc, const Job &job, const GateUpCfg &c,
+                            uint8_t *smem, int rb) {
+    const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+    const int nbD = c.nbD;
+    const int64_t rbD = row_bytes(DT, sh.D);
+    const int64_t chunk = (int64_t)GU_CH * rbD;   // bytes of one matrix's stage rows
+    uint64_t *bars = reinterpret_cast<uint64_t *>(smem);
+    uint8_t *ring = smem + 128;
+    act_q8 *acts = reinterpret_cast<act_q8 *>(ring + (int64_t)c.nst * c.stage);
+    float *P = reinterpret_cast<float *>(acts + (int64_t)c.ntok * nbD) + warp * (32 * 33);
+    float *GU = reinterpret_cast<float *>(acts + (int64_t)c.ntok * nbD) + 8 * 32 * 33;   // [2][ntok][64]
+    int *tok_off = reinterpret_cast<int *>(GU + 2 * c.ntok * GU_ROWS);                  // [ntok]
+
+    const int npass = (job.n + c.ntok - 1) / c.ntok;
+    const int total = npass * GU_NCH;
+    const uint8_t *g0 = job.gate + (int64_t)rb * GU_ROWS * rbD, *u0 = job.up + (int64_t)rb * GU_ROWS * rbD;
+    if (tid == 0) {
+        for (int s = 0; s < c.nst; s++) mbar_init(&bars[s], 1);
+        fence_mbar_init();
+    }
+    __syncthreads();
+    auto issue = [&](int q) {   // thread 0: chunk q (pass q / GU_NCH, chunk q % GU_NCH)
+        const int s = q % c.nst, ch = q % GU_NCH;
+        uint8_t *dst = ring + (int64_t)s * c.stage;
+        mbar_expect_tx(&bars[s], (uint32_t)(2 * chunk));
+        bulk_g2s(dst, g0 + ch * chunk, (uint32_t)chunk, &bars[s]);
+        bulk_g2s(dst + chunk, u0 + ch * chunk, (uint32_t)chunk, &bars[s]);
+    };
+    if (tid == 0)
+        for (int q = 0; q < min(c.nst, total); q++) issue(q);
+    bool ok = true;
+    for (int pass = 0; pass < npass; pass++) {
+        const int i0 = pass * c.ntok, nt = min(c.ntok, job.n - i0);
+        // stage this pass's token activations (nbD blocks each) and their offsets
+        for (int i = 0; i < nt; i++) {
+            const int t = job_token(sc, job, i0 + i);
+            const uint32_t *src = reinterpret_cast<const uint32_t *>(sc.xact + (int64_t)t * nbD);
+            uint32_t *dst = reinterpret_cast<uint32_t *>(acts + (int64_t)i * nbD);
+            for (int k = tid; k < nbD * (ACT_BLOCK / 4); k += blockDim.x) dst[k] = src[k];
+        }
+        if (tid < nt) tok_off[tid] = tid * nbD;
+        __syncthreads();
+        for (int ch = 0; ch < GU_NCH; ch++) {
+            const int q = pass * GU_NCH + ch, s = q % c.nst;
+            ok = ok && mbar_wait(&bars[s], (uint32_t)((q / c.nst) & 1), sc.err);
+            if (ok) {
+                const uint8_t *st = ring + (int64_t)s * c.stage;
+                // warp w: gate row w and up row w of this stage (rows 0..7 gate, 8..15 up)
+                const int rl[2] = {warp, GU_CH + warp};
+                const int row = ch * GU_CH + warp;   // row within the CTA's 64
+                for (int tg = 0; tg < nt; tg += 16) {
+                    const int ntg = min(16, nt - tg);
+                    warp_rows<DT>(st, rbD, nbD, rl, 2, acts, tok_off + tg, ntg, P,
+                                  GU + (int64_t)tg * GU_ROWS + row, c.ntok * GU_ROWS, GU_ROWS);
+                }
+            }
+            __syncthreads();
+            if (tid == 0 && q + c.nst < total) {
+                fence_proxy_async();
+                issue(q + c.nst);
+            }
+        }
+        if (!ok) break;
+        // SwiGLU and the mid activation block of each token (warp per token)
+        for (int i = warp; i < nt; i += 8) {
+            const float *G = GU + i * GU_ROWS, *U = GU + c.ntok * GU_ROWS + i * GU_ROWS;
+            const float m0 = swiglu_c(G[lane], U[lane]), m1 = swiglu_c(G[lane + 32], U[lane + 32]);
+            act_q8 *dst = sc.act_mid + (int64_t)(job.p0 + i0 + i) * c.fmax_nb + rb;
+            act_quant_warp(m0, m1, dst, lane);
+        }
+        __syncthreads();
+    }
+}
+
+__global__ void __launch_bounds__(256) k_moe_gateup(MoeShape sh, MoeLayerDev L, MoeScratch sc, GateUpCfg c) {
+    extern __shared__ __align__(128) uint8_t smem[];
+    const int u = blockIdx.y, rb = blockIdx.x;
+    const int nu = *sc.nu;
+    const int njobs = nu + (L.Fs > 0 ? 1 : 0);
+    if (u >= njobs) return;
+    Job job;
+    if (!get_job(sh, L, sc, u, nu, job)) return;
+    if (rb * GU_ROWS >= job.F) return;
+    if (job.dtype == Q4) gateup_body<Q4>(sh, sc, job, c, smem, rb);
+    else gateup_body<Q8>(sh, sc, job, c, smem, rb);
+}
+
+struct DownCfg {
+    int nst;          // pipeline stages
+    int64_t stage;    // bytes per stage (DN_ROWS rows of the widest down matrix)
+    int fmax_nb;      // activation blocks per mid row
+    int fused;        // keep Y in shared memory and finish the rank-order sum here
+    int max_pairs;    // fused: T*K (Y rows held in shared memory)
+};
+
+// One down tile (DN_ROWS rows of a job's down matrix) against the job's mid activations.
+template <int DT>
+__device__ void down_tile(const MoeShape &sh, const MoeScratch &sc, const Job &job, const DownCfg &c,
+                          const uint8_t *tile, float *P, int *tok_off, float *Ys, float *Ss, int r0) {
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    const int64_t rbF = row_bytes(DT, job.F);
+    const int rl[2] = {2 * warp, 2 * warp + 1};
+    for (int i0 = 0; i0 < job.n; i0 += 16) {
+        const int nt = min(16, job.n - i0);
+        if (lane < nt) tok_off[lane] = (job.p0 + i0 + lane) * c.fmax_nb;
+        __syncwarp();
+        float *out;
+        int oi;
+        if (c.fused) {
+            out = job.shared ? Ss + (int64_t)i0 * DN_ROWS + 2 * warp : Ys + (int64_t)(job.p0 + i0) * DN_ROWS + 2 * warp;
+            oi = DN_ROWS;
+        } else {
+            out = job.shared ? sc.S + (int64_t)i0 * sh.D + r0 + 2 * warp
+                             : sc.Y + (int64_t)(job.p0 + i0) * sh.D + r0 + 2 * warp;
+            oi = sh.D;
+        }
+        warp_rows<DT>(tile, rbF, job.nbF, rl, 2, sc.act_mid, tok_off, nt, P, out, 1, oi);
+        __syncwarp();
+    }
+}
+
+// Per (token, row): out = sum_j w_j * y_j in rank order from +0.0f, + shared (times its sigmoid
+// gate), then h += rs * out and/or out written (engine/src/model.c:904-923, 925-934).
+__device__ __forceinline__ void finish_row(const MoeShape &sh, const MoeScratch &sc, int t, int r, const float *Yrow,
+                                           int ystride, float sval, bool has_shared, const float *sh_logit,
+                                           float *h, float *out, bool resid) {
+    const int K = sh.route.K;
+    float o = 0.0f;
+    for (int j = 0; j < K; j++) {
+        const float wj = sc.wts[t * K + j];
+        const float y = Yrow[(int64_t)sc.pair_of[t * K + j] * ystride];
+        o = __fadd_rn(o, __fmul_rn(wj, y));
+    }
+    if (has_shared) {
+        float s = sval;
+        if (sh_logit) s = __fmul_rn(s, sigmoid_c(sh_logit[t]));
+        o = __fadd_rn(o, s);
+    }
+    const int64_t idx = (int64_t)t * sh.D + r;
+    if (out) out[idx] = o;
+    if (resid) h[idx] = __fadd_rn(h[idx], __fmul_rn(sh.residual_scale, o));
+}
+
+__global__ void __launch_bounds__(256) k_moe_down(MoeShape sh, MoeLayerDev L, MoeScratch sc, DownCfg c, float *h,
+                                                  float *out, int resid) {
+    extern __shared__ __align__(128) uint8_t smem[];
+    const int tid = threadIdx.x, warp = tid >> 5;
+    const int r0 = blockIdx.x * DN_ROWS;
+    const int nu = *sc.nu;
+    const int njobs = nu + (L.Fs > 0 ? 1 : 0);
+    uint64_t *bars = reinterpret_cast<uint64_t *>(smem);
+    uint8_t *ring = smem + 128;
+    float *P = reinterpret_cast<float *>(ring + (int64_t)c.nst * c.stage) + warp * (32 * 33);
+    int *tok_off = reinterpret_cast<int *>(reinterpret_cast<float *>(ring + (int64_t)c.nst * c.stage) + 8 * 32 * 33) +
+                   warp * 16;
+    float *Ys = reinterpret_cast<float *>(reinterpret_cast<int *>(reinterpret_cast<float *>(
+                                               ring + (int64_t)c.nst * c.stage) + 8 * 32 * 33) + 8 * 16);
+    float *Ss = Ys + (int64_t)(c.fused ? c.max_pairs : 0) * DN_ROWS;
+    if (tid == 0) {
+        for (int s = 0; s < c.nst; s++) mbar_init(&bars[s], 1);
+        fence_mbar_init();
+    }
+    __syncthreads();
+    auto issue = [&](int u) {
+        Job j;
+        if (!get_job(sh, L, sc, u, nu, j)) return false;
+        const int64_t rbF = row_bytes(j.dtype, j.F);
+        const int s = u % c.nst;
+        mbar_expect_tx(&bars[s], (uint32_t)(DN_ROWS * rbF));
+        bulk_g2s(ring + (int64_t)s * c.stage, j.down + (int64_t)r0 * rbF, (uint32_t)(DN_ROWS * rbF), &bars[s]);
+        return true;
+    };
+    __shared__ int issued_ok;
+    if (tid == 0) {
+        int ok = 1;
+        for (int u = 0; u < min(c.nst, njobs); u++) ok &= issue(u) ? 1 : 0;
+        issued_ok = ok;
+    }
+    __syncthreads();
+    bool ok = issued_ok != 0;
+    for (int u = 0; u < njobs && ok; u++) {
+        Job job;
+        get_job(sh, L, sc, u, nu, job);
+        const int s = u % c.nst;
+        ok = mbar_wait(&bars[s], (uint32_t)((u / c.nst) & 1), sc.err);
+        if (ok) {
+            const uint8_t *tile = ring + (int64_t)s * c.stage;
+            if (job.dtype == Q4) down_tile<Q4>(sh, sc, job, c, tile, P, tok_off, Ys, Ss, r0);
+            else down_tile<Q8>(sh, sc, job, c, tile, P, tok_off, Ys, Ss, r0);
+        }
+        __syncthreads();
+        if (tid == 0 && u + c.nst < njobs) {
+            fence_proxy_async();
+            if (!issue(u + c.nst)) issued_ok = 0;
+        }
+        __syncthreads();
+        ok = ok && issued_ok != 0;
+    }
+    if (!ok) {
+        // drain copies that may still be landing in this CTA's shared memory before exiting
+        if (tid == 0)
+            for (int u = 0; u < njobs && u < c.nst; u++) mbar_wait(&bars[u % c.nst], 0, nullptr);
+        return;
+    }
+    if (!c.fused) return;
+    const int T = sh.T;
+    const bool has_shared = L.Fs > 0;
+    for (int it = tid; it < T * DN_ROWS; it += blockDim.x) {
+        const int t = it / DN_ROWS, rr = it - t * DN_ROWS;
+        finish_row(sh, sc, t, r0 + rr, Ys + rr, DN_ROWS, has_shared ? Ss[t * DN_ROWS + rr] : 0.0f, has_shared,
+                   L.sh_gate_inp ? sc.sh_logit : nullptr, h, out, resid != 0);
+    }
+}
+
+__global__ void k_moe_sum(MoeShape sh, MoeLayerDev L, MoeScratch sc, float *h, float *out, int resid) {
+    const int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
+    if (i >= (int64_t)sh.T * sh.D) return;
+    const int t = (int)(i / sh.D), r = (int)(i - (int64_t)t * sh.D);
+    const bool has_shared = L.Fs > 0;
+    finish_row(sh, sc, t, r, sc.Y + r, sh.D, has_shared ? sc.S[i] : 0.0f, has_shared,
+               L.sh_gate_inp ? sc.sh_logit : nullptr, h, out, resid != 0);
+}
+
+// =============================================================================================
+// Launch sequences.
+// =============================================================================================
+
+static int fmax_nb_of(const MoeShape &sh, const MoeLayerDev &L) { return std::max(sh.F, L.Fs) / QK; }
+
+// Stage 0: x = rmsnorm(h) and its activations; stage 1: router logits and routing.
+static void launch_route_stages(int which, const MoeShape &sh, const MoeLayerDev &L, const MoeScratch &sc,
+                                const float *h, cudaStream_t s) {
+    const int T = sh.T, E = sh.route.E, K = sh.route.K;
+    const bool fused = T * K <= kFusedMaxPairs;
+    if (which & 1) k_moe_norm_act<<<T, 256, 0, s>>>(h, L.ffn_norm, sh.eps, sh.D, sc.x, sc.xact);
+    if (which & 2) {
+        const int rows = E + (L.sh_gate_inp ? 1 : 0);
+        const int64_t items = (int64_t)rows * T;
+        constexpr int RT = 64;   // 4 (row, token) items per CTA: E=128 rows -> 32 CTAs at T=1
+        const unsigned grid = (unsigned)((items + RT / 16 - 1) / (RT / 16));
+        const size_t route_smem = (size_t)8 * 2 * E * sizeof(float);
+        k_moe_router<<<grid, RT, fused ? route_smem : 0, s>>>(sh, L.router, L.sh_gate_inp, L.router_bias, sc,
+                                                               fused ? 1 : 0);
+        if (!fused) {
+            k_route_select<<<(T + 7) / 8, 256, route_smem, s>>>(sh, L.router_bias, sc);
+            k_route_union<<<1, 512, (size_t)2 * E * sizeof(int), s>>>(sh, sc);
+        }
+    }
+}
+
+cudaError_t launch_moe_route(const MoeShape &sh, const MoeLayerDev &L, const MoeScratch &sc, const float *h,
+                             cudaStream_t s) {
+    launch_route_stages(3, sh, L, sc, h, s);
+    return cudaGetLastError();
+}
+
+static size_t smem_limit() {
+    static size_t lim = 0;
+    if (!lim) {
+        int dev = 0, v = 0;
+        cudaGetDevice(&dev);
+        cudaDeviceGetAttribute(&v, cudaDevAttrMaxSharedMemoryPerBlockOptin, dev);
+        lim = (size_t)v;
+    }
+    return lim;
+}
+
+cudaError_t init_kernel_attributes() {
+    const int lim = (int)smem_limit();
+    cudaError_t e = cudaFuncSetAttribute(k_moe_gateup, cudaFuncAttributeMaxDynamicSharedMemorySize, lim);
+    if (e == cudaSuccess) e = cudaFuncSetAttribute(k_moe_down, cudaFuncAttributeMaxDynamicSharedMemorySize, lim);
+    // load every MoE kernel now, so no module loading happens inside a stream capture later
+    cudaFuncAttributes fa;
+    const void *kernels[] = {(const void *)k_moe_norm_act, (const void *)k_moe_router, (const void *)k_route_select,
+                             (const void *)k_route_union, (const void *)k_moe_sum};
+    for (const void *k : kernels)
+        if (e == cudaSuccess) e = cudaFuncGetAttributes(&fa, k);
+    return e;
+}
+
+// Stage 2 (which & 1): gate/up + SwiGLU + mid activations; stage 3 (which & 2): down (+ sum).
+static cudaError_t launch_expert_stages(int which, const MoeShape &sh, const MoeLayerDev &L, const MoeScratch &sc,
+                                        float *h, float *out, bool resid, cudaStream_t s) {
+    const int T = sh.T, K = sh.route.K, E = sh.route.E;
+    const bool fused = T * K <= kFusedMaxPairs;
+    const size_t lim = smem_limit() - 1024;
+    const int fmax_nb = fmax_nb_of(sh, L);
+    // ---- gate/up + SwiGLU + mid activations
+    if (which & 1) {
+        GateUpCfg c;
+        c.nbD = sh.D / QK;
+        c.fmax_nb = fmax_nb;
+        int64_t rb = row_bytes(sh.F > 0 ? L.expert_dtype : Q4, sh.D);
+        if (L.Fs > 0) rb = std::max<int64_t>(rb, row_bytes(L.sh_dtype, sh.D));
+        c.stage = 2 * GU_CH * rb;
+        c.ntok = std::min(8, std::max(1, T));
+        auto fixed = [&](int ntok) {
+            return (size_t)128 + (size_t)ntok * c.nbD * ACT_BLOCK + (size_t)8 * 32 * 33 * 4 +
+                   (size_t)2 * ntok * GU_ROWS * 4 + (size_t)ntok * 4 + 64;
+        };
+        while (c.ntok > 1 && fixed(c.ntok) + (size_t)c.stage > lim) c.ntok /= 2;
+        c.nst = (int)std::min<int64_t>(GU_NCH, (int64_t)((lim - fixed(c.ntok)) / (size_t)c.stage));
+        if (c.nst < 1) return cudaErrorInvalidConfiguration;
+        const size_t smem = fixed(c.ntok) + (size_t)c.nst * c.stage;
+        const int maxjobs = std::min(E, T * K) + (L.Fs > 0 ? 1 : 0);
+        dim3 grid((unsigned)(std::max(sh.F, L.Fs) / GU_ROWS), (unsigned)maxjobs);
+        k_moe_gateup<<<grid, 256, smem, s>>>(sh, L, sc, c);
+    }
+    // ---- down (+ rank-order sum for small batches)
+    if (which & 2) {
+        DownCfg c;
+        c.fmax_nb = fmax_nb;
+        c.fused = fused ? 1 : 0;
+        c.max_pairs = T * K;
+        int64_t rbF = row_bytes(L.expert_dtype, sh.F);
+        if (L.Fs > 0) rbF = std::max<int64_t>(rbF, row_bytes(L.sh_dtype, L.Fs));
+        c.stage = ((int64_t)DN_ROWS * rbF + 127) / 128 * 128;
+        const size_t fixed = 128 + (size_t)8 * 32 * 33 * 4 + (size_t)8 * 16 * 4 +
+                             (fused ? (size_t)(T * K + T) * DN_ROWS * 4 : 0) + 64;
+        const int maxjobs = std::min(E, T * K) + (L.Fs > 0 ? 1 : 0);
+        c.nst = (int)std::min<int64_t>(std::min(maxjobs, 16), (int64_t)((lim - fixed) / (size_t)c.stage));
+        if (c.nst < 1) return cudaErrorInvalidConfiguration;
+        const size_t smem = fixed + (size_t)c.nst * c.stage;
+        k_moe_down<<<(unsigned)(sh.D / DN_ROWS), 256, smem, s>>>(sh, L, sc, c, h, out, resid ? 1 : 0);
+        if (!fused) {
+            const int64_t n = (int64_t)T * sh.D;
+            k_moe_sum<<<(unsigned)((n + 255) / 256), 256, 0, s>>>(sh, L, sc, h, out, resid ? 1 : 0);
+        }
+    }
+    return cudaGetLastError();
+}
+
+cudaError_t launch_moe_experts(const MoeShape &sh, const MoeLayerDev &L, const MoeScratch &sc, float *h,
+                               float *out, bool resid, cudaStream_t s) {
+    return launch_expert_stages(3, sh, L, sc, h, out, resid, s);
+}
+
+cudaError_t launch_moe_stage(int stage, const MoeShape &sh, const MoeLayerDev &L, const MoeScratch &sc, float *h,
+                             float *out, bool resid, cudaStream_t s) {
+    if (stage < 2) {
+        launch_route_stages(stage == 0 ? 1 : 2, sh, L, sc, h, s);
+        return cudaGetLastError();
+    }
+    return launch_expert_stages(stage == 2 ? 1 : 2, sh, L, sc, h, out, resid, s);
+}
+
+cudaError_t launch_moe_layer(const MoeShape &sh, const MoeLayerDev &L, const MoeScratch &sc, float *h, float *out,
+                             bool resid, cudaStream_t s) {
+    cudaError_t e = launch_moe_route(sh, L, sc, h, s);
+    if (e != cudaSuccess) return e;
+    return launch_moe_experts(sh, L, sc, h, out, resid, s);
+}
+
+// =============================================================================================
+// Synthetic weights (benchmarks without a container) and the expf self-check.
+// =============================================================================================
+
+__host__ __device__ inline uint64_t splitmix64(uint64_t z) {
+    z += 0x9e3779b97f4a7c15ull;
+    z = (z ^ (z >> 30)) * 0xbf58476d1ce4e5b9ull;
+    z = (z ^ (z >> 27)) * 0x94d049bb133111ebull;
+    return z ^ (z >> 31);
+}
+
+// Q4 blocks with the statistics of N(0, sigma) weights packed by the reference quantizer:
+// nibbles follow a discretised Irwin-Hall(4) bell around 8, scales jitter around sigma/2.
+// One thread per 34-byte block; padding bytes of the slab stay zero.
+__global__ void k_synth_q4(uint8_t *dev, int64_t n_slabs, int64_t slab_bytes, int D, int F, uint64_t seed,
+                           uint32_t scale_bits) {
+    const slab_layout lay = make_slab_layout(Q4, D, F);
+    const int64_t nb_gate = (int64_t)F * (D / QK);      // blocks in gate (and in up)
+    const int64_t nb_down = (int64_t)D * (F / QK);
+    const int64_t per_slab = 2 * nb_gate + nb_down;
+    const int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
+    if (i >= n_slabs * per_slab) return;
+    const int64_t slab = i / per_slab, b = i - slab * per_slab;
+    int64_t off;
+    if (b < nb_gate) off = b * Q4_BLOCK;
+    else if (b < 2 * nb_gate) off = lay.off_up + (b - nb_gate) * Q4_BLOCK;
+    else off = lay.off_down + (b - 2 * nb_gate) * Q4_BLOCK;
+    uint8_t *blk = dev + slab * slab_bytes + off;
+    uint64_t h = splitmix64(seed ^ splitmix64((uint64_t)i));
+    const uint32_t sc = scale_bits + (uint32_t)(h & 0x3f) - 32u;
+    blk[0] = (uint8_t)(sc & 0xff);
+    blk[1] = (uint8_t)(sc >> 8);
+    for (int j = 0; j < 32; j++) {
+        uint8_t v = 0;
+        for (int half = 0; half < 2; half++) {
+            h = splitmix64(h);
+            const int s4 = (int)(h & 0xff) + (int)((h >> 8) & 0xff) + (int)((h >> 16) & 0xff) + (int)((h >> 24) & 0xff);
+            int q = 8 + (s4 - 510 + 37 + 740) / 74 - 10;   // ~ round((s4-510)/74): sd ~2
+            q = q < 0 ? 0 : (q > 15 ? 15 : q);
+            v |= (uint8_t)(q << (4 * half));
+        }
+        blk[2 + j] = v;
+    }
+}
+
+cudaError_t launch_synth_q4(uint8_t *dev, int64_t n_slabs, int64_t slab_bytes, int D, int F, uint64_t seed,
+                            float sigma, cudaStream_t s) {
+    // the f16 bits of sigma/2 (finite, normal for any sensible sigma)
+    const float v = sigma * 0.5f;
+    uint32_t fb;
+    std::memcpy(&fb, &v, 4);
+    const int e = (int)((fb >> 23) & 0xff) - 127 + 15;
+    const uint32_t scale_bits = (uint32_t)(e << 10) | ((fb >> 13) & 0x3ffu);
+    const int64_t per_slab = 2 * (int64_t)F * (D / QK) + (int64_t)D * (F / QK);
+    const int64_t n = n_slabs * per_slab;
+    cudaMemsetAsync(dev, 0, (size_t)(n_slabs * slab_bytes), s);
+    k_synth_q4<<<(unsigned)((n + 255) / 256), 256, 0, s>>>(dev, n_slabs, slab_bytes, D, F, seed, scale_bits);
+    return cudaGetLastError();
+}
+
+// f32 ~ N(0, sigma) approximated by Irwin-Hall(4) over bytes, one rounding: (s4 - 510) * (sigma/147.8).
+__global__ void k_synth_f32(float *dev, int64_t n, uint64_t seed, float k) {
+    const int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
+    if (i >= n) return;
+    const uint64_t h = splitmix64(seed ^ splitmix64((uint64_t)i));
+    const int s4 = (int)(h & 0xff) + (int)((h >> 8) & 0xff) + (int)((h >> 16) & 0xff) + (int)((h >> 24) & 0xff);
+    dev[i] = __fmul_rn(__int2float_rn(s4 - 510), k);
+}
+
+cudaError_t launch_synth_f32(float *dev, int64_t n, uint64_t seed, float sigma, cudaStream_t s) {
+    if (n <= 0) return cudaSuccess;
+    k_synth_f32<<<(unsigned)((n + 255) / 256), 256, 0, s>>>(dev, n, seed, sigma / 147.8f);
+    return cudaGetLastError();
+}
+
+__global__ void k_expf_bits(uint32_t x0, int64_t n, float *out) {
+    const int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
+    if (i >= n) return;
+    out[i] = host_expf(__uint_as_float(x0 + (uint32_t)i));
+}
+
+cudaError_t launch_expf_bits(uint32_t x0, int64_t n, float *out, cudaStream_t s) {
+    if (n <= 0) return cudaSuccess;
+    k_expf_bits<<<(unsigned)((n + 255) / 256), 256, 0, s>>>(x0, n, out);
+    return cudaGetLastError();
+}
+
+}  // namespace hx

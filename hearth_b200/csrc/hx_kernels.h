@@ -1,0 +1,112 @@
+// hx_kernels.h — launch interface of the sm_100a kernels (host side, C++).
+//
+// Kernel inventory (all in hx_kernels.cu):
+//   act_quantize      NUMERICS §2 activation blocks           (engine/src/quant.c:325-348)
+//   matmul            hearth_matmul rows for F32/F16/BF16/Q8/Q4 (quant.c:352-427, 574-600)
+//   dequantize        hearth_dequantize                         (quant.c:257-307)
+//   moe_norm_act      x = rmsnorm(h, ffn_norm), its Q8 activations (model.c:1209-1210, 1050)
+//   moe_router        F32 router + shared-gate logits; the last CTA routes small batches
+//                     (route_select/route_weights model.c:793-843, union model.c:1020-1037)
+//   route_select      one warp per token (large batches)
+//   route_union       expert buckets (large batches)
+//   moe_gateup        Q4/Q8 gate+up rows, SwiGLU, mid activation blocks (model.c:847-897, 419-439)
+//   moe_down          Q4/Q8 down rows; for small batches also the rank-order sum + shared expert +
+//                     residual (model.c:904-923)
+//   moe_sum           rank-order sum for large batches
+#pragma once
+
+#include <cstddef>
+#include <cstdint>
+#include <cuda_runtime.h>
+
+namespace hx {
+
+struct act_q8;
+
+// Routing configuration of one MoE layer (hx_config fields, engine/src/hx_modelfile.h:39-40).
+struct RouteCfg {
+    int E, K;
+    int score_fn, score_bias, n_group, topk_group, norm_topk_prob;
+    float routed_scale;
+};
+
+// Device scratch of one MoE evaluation (sized for max_tokens by the engine).
+struct MoeScratch {
+    float *x;            // [T, D] normed input
+    act_q8 *xact;        // [T, D/64]
+    float *logits;       // [T, E]
+    float *sh_logit;     // [T] shared-expert gate logit
+    int *ids;            // [T, K]
+    float *wts;          // [T, K]
+    int *nu;             // [1] unique experts
+    int *ulist, *u_p0, *u_n;   // [E]
+    int *pair_tok, *pair_of;   // [T*K]
+    act_q8 *act_mid;     // [T*K + T, Fmax/64]
+    float *Y;            // [T*K, D] per (token, rank) outputs (large batches)
+    float *S;            // [T, D] shared expert output (large batches)
+    unsigned *ticket;    // [1] last-CTA counter of moe_router (returns to 0 after every launch)
+    int *err;            // [1] device error word
+};
+
+// One MoE layer's weights on the device.
+struct MoeLayerDev {
+    const float *router;        // [E, D] f32
+    const float *router_bias;   // [E] or null
+    const float *ffn_norm;      // [D] or null (then x = h as given)
+    const uint8_t *const *slab; // [E] device pointers of the resident slabs (null = not resident)
+    int expert_dtype;           // Q4 or Q8 (uniform per layer)
+    int64_t off_up, off_down;   // FORMAT §5 slab layout
+    // shared expert (Fs = 0: none)
+    int Fs, sh_dtype;
+    const uint8_t *sh_gate, *sh_up, *sh_down;
+    const float *sh_gate_inp;   // [D] or null
+};
+
+struct MoeShape {
+    int D, F, E, K, T;
+    float eps, residual_scale;
+    RouteCfg route;
+};
+
+// Chooses the fused small-batch path (routing in moe_router's last CTA, sum in moe_down) when
+// T * K is at most this many pairs.
+constexpr int kFusedMaxPairs = 64;
+
+// Raises the dynamic shared-memory limit of the staged kernels to the device maximum (once per
+// device, before any launch or stream capture).
+cudaError_t init_kernel_attributes();
+
+// Launchers return cudaGetLastError() of their launches.
+cudaError_t launch_act_quantize(const float *x, int64_t ldx, act_q8 *out, int64_t n, int T, cudaStream_t s);
+cudaError_t launch_matmul(int dtype, const void *W, int64_t n_cols, const void *act, int T, float *Y,
+                          int64_t ldy, int64_t r0, int64_t r1, cudaStream_t s);
+cudaError_t launch_dequantize(int dtype, const void *W, int64_t n_rows, int64_t n_cols, float *out,
+                              cudaStream_t s);
+
+// One MoE FFN. Input: h [T, D] (when L.ffn_norm is set, x = rmsnorm(h); otherwise x = h).
+// Output: if out != null, out [T, D] = rank-order expert sum (+ shared); if resid, h += rs * sum.
+cudaError_t launch_moe_layer(const MoeShape &sh, const MoeLayerDev &L, const MoeScratch &sc, float *h,
+                             float *out, bool resid, cudaStream_t s);
+
+// Pieces of launch_moe_layer, for hosts that must look at the routing before the experts run
+// (the streaming expert store): routing only, then the experts.
+cudaError_t launch_moe_route(const MoeShape &sh, const MoeLayerDev &L, const MoeScratch &sc, const float *h,
+                             cudaStream_t s);
+cudaError_t launch_moe_experts(const MoeShape &sh, const MoeLayerDev &L, const MoeScratch &sc, float *h,
+                               float *out, bool resid, cudaStream_t s);
+
+// One stage of launch_moe_layer (0 norm+activations, 1 router+routing, 2 gate/up, 3 down+sum),
+// for per-kernel timing.
+cudaError_t launch_moe_stage(int stage, const MoeShape &sh, const MoeLayerDev &L, const MoeScratch &sc, float *h,
+                             float *out, bool resid, cudaStream_t s);
+
+// Fills every expert slab of `n` slabs at dev with deterministic synthetic Q4 blocks (the
+// statistics of N(0, sigma) weights packed to Q4), for benchmarks without a container.
+cudaError_t launch_synth_q4(uint8_t *dev, int64_t n_slabs, int64_t slab_bytes, int D, int F, uint64_t seed,
+                            float sigma, cudaStream_t s);
+cudaError_t launch_synth_f32(float *dev, int64_t n, uint64_t seed, float sigma, cudaStream_t s);
+
+// Device expf restatement over [x0, x0 + n) bit patterns (self-check support).
+cudaError_t launch_expf_bits(uint32_t x0, int64_t n, float *out, cudaStream_t s);
+
+}  // namespace hx

@@ -1,0 +1,162 @@
+/*
+ * hearth_b200.h — C ABI of the B200 (sm_100a) backend for Hearth's quantized MoE expert path.
+ *
+ * Plain C types only (pointers, sizes, ints); no CUDA or torch types. Device pointers are
+ * passed as void* / float*, CUDA streams as void* (NULL = the library's own stream).
+ *
+ * The entry points replace these reference interfaces (pierce-lonergan/hearth):
+ *   hxb_matmul          hearth_matmul       engine/include/hearth.h:157-158, engine/src/quant.c:574-600
+ *   hxb_dequantize      hearth_dequantize   engine/include/hearth.h:153,     engine/src/quant.c:563-571
+ *   hxb_row_bytes       hearth_row_bytes    engine/include/hearth.h:150,     engine/src/quant.c:507
+ *   hxb_matmul_dev      hx_matmul_fn        engine/src/hx_quant.h:49-57 (row-range kernel contract)
+ *   hxb_act_quantize_dev  act_quantize_q8   engine/src/hx_quant.h:62,        engine/src/quant.c:325-348
+ *   hxb_moe_*           the MoE half of hx_model (engine/src/model.c:986-1131 moe_layer and the
+ *                       FFN half of forward, model.c:1209-1214) plus the expert store it acquires
+ *                       experts from (engine/src/hx_store.h:51-89), as a backend handle
+ *   hxb_moe_stats       hx_store_stats      engine/src/hx_store.h:78-87 (+ hearth_stats timers)
+ *
+ * Return codes follow hx_model.h:60-68 (HX_E_*) where one exists.
+ * Threading: a handle is used by one host thread at a time (engine/include/hearth.h:10-12).
+ */
+#ifndef HEARTH_B200_H
+#define HEARTH_B200_H
+
+#include <stddef.h>
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+#define HXB_API __attribute__((visibility("default")))
+
+enum {
+    HXB_OK = 0,
+    HXB_E_ARG = -1,          /* HX_E_ARG */
+    HXB_E_CAPACITY = -3,     /* HX_E_CAPACITY: more tokens than the handle was opened for */
+    HXB_E_IO = -4,           /* HX_E_IO: an expert could not be brought into HBM */
+    HXB_E_NOMEM = -5,        /* HX_E_NOMEM */
+    HXB_E_FORMAT = -6,       /* HX_E_FORMAT */
+    HXB_E_DEVICE = -7,       /* CUDA error or a kernel's device error word */
+    HXB_E_UNSUPPORTED = -8   /* a dtype / shape the kernels do not handle */
+};
+
+/* hearth_matmul's own codes (engine/src/quant.c:573): 0 ok, -1 bad args, -2 no device, -3 alloc. */
+enum { HXB_MM_OK = 0, HXB_MM_E_ARG = -1, HXB_MM_E_NODEV = -2, HXB_MM_E_ALLOC = -3 };
+
+/* ---- kernel-level boundary ------------------------------------------------------------------ */
+HXB_API const char *hxb_version(void);
+HXB_API const char *hxb_last_error(void);   /* message of the calling thread's last failure */
+HXB_API int hxb_device_count(void);
+HXB_API size_t hxb_row_bytes(int dtype, int64_t n_cols);
+
+/* Y[T, n_rows] = W[n_rows, n_cols] . X[T, n_cols] with host buffers, NUMERICS §3 (bit-identical
+ * to hearth_matmul on every dtype F32/F16/BF16/Q8/Q4). */
+HXB_API int hxb_matmul(int dtype, const void *W, int64_t n_rows, int64_t n_cols, const float *X, int T,
+                       float *Y);
+HXB_API int hxb_dequantize(int dtype, const void *src, int64_t n_rows, int64_t n_cols, float *dst);
+
+/* Device-pointer variants. act: T activations of n_cols (72-byte blocks for Q8/Q4 weights,
+ * f32 vectors for float weights); Y[t * ldy + r] for rows [r0, r1). */
+HXB_API int hxb_act_quantize_dev(const float *x, int64_t n, int T, void *act, void *stream);
+HXB_API int hxb_matmul_dev(int dtype, const void *W, int64_t n_cols, const void *act, int T, float *Y,
+                           int64_t ldy, int64_t r0, int64_t r1, void *stream);
+HXB_API int hxb_dequantize_dev(int dtype, const void *W, int64_t n_rows, int64_t n_cols, float *out,
+                               void *stream);
+/* The device expf (the host libm's results) on the bit patterns [x0, x0 + n): self-check support. */
+HXB_API int hxb_expf_dev(uint32_t x0, int64_t n, float *out, void *stream);
+
+/* ---- MoE backend handle ---------------------------------------------------------------------- */
+typedef struct hxb_moe hxb_moe;
+
+typedef struct hxb_moe_config {
+    int n_layers;          /* MoE layers held by this handle */
+    int d_model;           /* D */
+    int expert_ffn_dim;    /* F */
+    int n_experts;         /* E (<= 384) */
+    int top_k;             /* K (<= 32) */
+    int score_fn;          /* 0 softmax, 1 sigmoid (HX_SCORE_*) */
+    int score_bias;        /* 1: selection adds the router bias */
+    int n_group, topk_group;
+    int norm_topk_prob;
+    float routed_scale, residual_scale, norm_eps;
+    int expert_dtype;      /* HEARTH_Q4 or HEARTH_Q8 */
+    int shared_ffn_dim;    /* 0 = no shared expert */
+    int shared_dtype;      /* HEARTH_Q8 or HEARTH_Q4 */
+    int shared_gate;       /* 1: shared output scaled by sigmoid(dot16(gate_inp, x)) */
+    int max_tokens;        /* largest T per call */
+    double cache_gb;       /* HBM budget for expert slots in GiB; 0 = every expert resident */
+    int policy;            /* HEARTH_POLICY_LRU (0) / HEARTH_POLICY_LFU (1) */
+    float heat_decay;      /* LFU per-token decay (default 0.995) */
+    int device;            /* CUDA device ordinal */
+} hxb_moe_config;
+
+typedef struct hxb_moe_stats {
+    uint64_t tokens, forward_calls;
+    uint64_t expert_uses, expert_loads_unique;
+    uint64_t hits, misses, evictions;
+    uint64_t prefetch_issued, prefetch_used, prefetch_wasted;
+    uint64_t bytes_copied, copies, copy_errors;
+    int n_slots, resident, pinned;
+    uint64_t slot_bytes;
+    double wall_s, stall_s;
+} hxb_moe_stats;
+
+HXB_API void hxb_moe_default_config(hxb_moe_config *c);
+HXB_API hxb_moe *hxb_moe_open(const hxb_moe_config *c, char *err, size_t errlen);
+HXB_API void hxb_moe_close(hxb_moe *m);
+
+/* Dense per-layer weights (host buffers, copied to HBM): router [E, D] f32, router_bias [E] or
+ * NULL, ffn_norm [D] or NULL (then the input is used as given), shared expert gate/up [Fs, D],
+ * down [D, Fs] in shared_dtype and gate_inp [D] (all NULL without a shared expert). */
+HXB_API int hxb_moe_set_layer(hxb_moe *m, int layer, const float *router, const float *router_bias,
+                              const float *ffn_norm, const void *sh_gate, const void *sh_up, const void *sh_down,
+                              const float *sh_gate_inp);
+/* One routed expert's slab (docs/FORMAT.md §5 layout, nbytes = the slab size) from host memory.
+ * The store keeps a pinned host copy (the host tier) and moves it into HBM when needed. */
+HXB_API int hxb_moe_set_expert(hxb_moe *m, int layer, int expert, const void *slab, size_t nbytes);
+/* Benchmarks without a container: deterministic synthetic router (N(0, sigma_router)), unit
+ * norms and Q4/Q8 expert slabs for every layer, generated in HBM (every expert resident). */
+HXB_API int hxb_moe_synthesize(hxb_moe *m, uint64_t seed, float sigma_router, float sigma_expert);
+HXB_API size_t hxb_moe_slab_bytes(const hxb_moe *m);
+
+/* h[T, D] (host, in place): for l in [layer0, layer0 + n_layers): x = rmsnorm(h, ffn_norm_l);
+ * h = h + residual_scale * moe_l(x)   (docs/NUMERICS.md §5, the FFN half of each layer). */
+HXB_API int hxb_moe_forward(hxb_moe *m, float *h, int T, int layer0, int n_layers);
+HXB_API int hxb_moe_forward_dev(hxb_moe *m, float *h, int T, int layer0, int n_layers, void *stream);
+/* One MoE FFN on x[T, D] as given (no norm, no residual): out[T, D] = rank-order expert sum
+ * (+ shared expert). Host and device variants. */
+HXB_API int hxb_moe_layer(hxb_moe *m, int layer, const float *x, int T, float *out);
+HXB_API int hxb_moe_layer_dev(hxb_moe *m, int layer, const float *x, int T, float *out, void *stream);
+/* The *_dev calls are asynchronous on their stream; this waits for the stream and returns the
+ * status of the device work since the last check (HXB_E_IO if an expert was not resident,
+ * HXB_E_DEVICE if a bounded device wait gave up). */
+HXB_API int hxb_moe_sync(hxb_moe *m, void *stream);
+/* Average device time in microseconds of each kernel stage of one layer at T tokens (every
+ * expert resident; eager launches between CUDA events): us[0] rmsnorm + activations, us[1]
+ * router + routing, us[2] gate/up + SwiGLU + mid activations, us[3] down + rank-order sum. */
+HXB_API int hxb_moe_profile(hxb_moe *m, int T, int iters, double *us);
+/* Routing of the last evaluated layer: ids / weights [T, K] (host). */
+HXB_API int hxb_moe_last_routing(hxb_moe *m, int *ids, float *weights, int T);
+
+HXB_API int hxb_moe_get_stats(hxb_moe *m, hxb_moe_stats *out);
+HXB_API void hxb_moe_reset_stats(hxb_moe *m);
+HXB_API int hxb_moe_is_resident(hxb_moe *m, int layer, int expert);
+/* Token boundary for the store (heat clock, prefetch protection): hx_store_tick
+ * (engine/src/hx_store.h:70). */
+HXB_API void hxb_moe_tick(hxb_moe *m);
+/* Low-priority hints (hx_store_prefetch, engine/src/hx_store.h:67-69): copies start at once into
+ * free or cold unprotected slots, and are dropped otherwise. */
+HXB_API int hxb_moe_prefetch(hxb_moe *m, int layer, const int *experts, int n);
+/* Heat profile (FORMAT.md §8 counts, n_keys = n_layers * n_experts): pins the hottest
+ * pin_fraction of the slots and, with warm_start, fills the rest (engine/src/store.c:815-860). */
+HXB_API int hxb_moe_seed_heat(hxb_moe *m, const float *counts, int n_keys, float pin_fraction, int warm_start);
+/* Test seam (the counterpart of hx_store_set_read_hook, engine/src/store.c:614-622): called
+ * before every host->HBM expert copy; a nonzero return fails that copy. NULL removes it. */
+typedef int (*hxb_copy_hook)(void *ctx, int layer, int expert);
+HXB_API void hxb_moe_set_copy_hook(hxb_moe *m, hxb_copy_hook fn, void *ctx);
+
+#ifdef __cplusplus
+}
+#endif
+#endif /* HEARTH_B200_H */

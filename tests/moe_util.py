@@ -1,0 +1,79 @@
+"""Shared helpers of the MoE tests: random layers with reference-quantized experts, loaded into
+both the oracle model and the GPU backend."""
+import numpy as np
+
+import hearth_b200 as hb
+from oracle import oracle as O
+
+
+def q_matrix(rng, rows, cols, dt, sigma=0.02):
+    W = (rng.standard_normal((rows, cols)) * sigma).astype(np.float32)
+    if O.ref_lib() is not None:
+        return O.ref_quantize(dt, W)
+    # reference not built on this machine: synthetic valid blocks with realistic statistics
+    bs = 34 if dt == O.Q4 else 66
+    rb = O.row_bytes(dt, cols)
+    q = np.zeros((rows, rb), np.uint8)
+    nb = cols // 64
+    for b in range(nb):
+        blk = W[:, b * 64:(b + 1) * 64]
+        amax = np.abs(blk).max(axis=1)
+        if dt == O.Q4:
+            d = (amax / 7.0).astype(np.float16)
+            df = d.astype(np.float32)
+            qi = np.clip(np.rint(blk / np.where(df == 0, 1, df)[:, None]), -8, 7).astype(np.int32) + 8
+            q[:, b * bs:b * bs + 2] = d.view(np.uint8).reshape(rows, 2)
+            q[:, b * bs + 2:b * bs + 34] = (qi[:, :32] | (qi[:, 32:] << 4)).astype(np.uint8)
+        else:
+            d = (amax / 127.0).astype(np.float16)
+            df = d.astype(np.float32)
+            qi = np.clip(np.rint(blk / np.where(df == 0, 1, df)[:, None]), -127, 127).astype(np.int8)
+            q[:, b * bs:b * bs + 2] = d.view(np.uint8).reshape(rows, 2)
+            q[:, b * bs + 2:b * bs + 66] = qi.view(np.uint8)
+    return q
+
+
+def make_slab(rng, D, F, dt=O.Q4):
+    up, down, nb = O.slab_layout(dt, D, F)
+    s = np.zeros(nb, np.uint8)
+    g, u, d = q_matrix(rng, F, D, dt), q_matrix(rng, F, D, dt), q_matrix(rng, D, F, dt)
+    s[:g.size] = g.reshape(-1)
+    s[up:up + u.size] = u.reshape(-1)
+    s[down:down + d.size] = d.reshape(-1)
+    return s
+
+
+def build_pair(seed, *, L=1, D=256, F=128, E=16, K=4, score_fn=0, score_bias=0, n_group=1, topk_group=1,
+               norm=1, routed_scale=1.0, Fs=0, shared_gate=False, max_tokens=64, cache_gb=0.0, policy=1,
+               router_sigma=0.15, residual_scale=1.0):
+    """An oracle model and a GPU backend holding the same random weights."""
+    rng = np.random.default_rng(seed)
+    model = O.MoeModel(D, F, E, K, score_fn=score_fn, score_bias=score_bias, n_group=n_group,
+                       topk_group=topk_group, norm_topk_prob=norm, routed_scale=routed_scale,
+                       residual_scale=residual_scale)
+    be = hb.MoeBackend(n_layers=L, d_model=D, expert_ffn_dim=F, n_experts=E, top_k=K, score_fn=score_fn,
+                       score_bias=score_bias, n_group=n_group, topk_group=topk_group, norm_topk_prob=norm,
+                       routed_scale=routed_scale, residual_scale=residual_scale, shared_ffn_dim=Fs,
+                       shared_dtype=O.Q8, shared_gate=int(shared_gate), max_tokens=max_tokens, cache_gb=cache_gb,
+                       policy=policy)
+    for l in range(L):
+        router = (rng.standard_normal((E, D)) * router_sigma).astype(np.float32)
+        bias = (rng.standard_normal(E) * 0.05).astype(np.float32) if score_bias else None
+        norm_w = (1.0 + 0.1 * rng.standard_normal(D)).astype(np.float32)
+        slabs = [make_slab(rng, D, F) for _ in range(E)]
+        shared = None
+        if Fs:
+            shared = dict(Fs=Fs, dtype=O.Q8, gate=q_matrix(rng, Fs, D, O.Q8), up=q_matrix(rng, Fs, D, O.Q8),
+                          down=q_matrix(rng, D, Fs, O.Q8),
+                          gate_inp=(rng.standard_normal(D) * 0.1).astype(np.float32) if shared_gate else None)
+        model.add_layer(router, slabs, [O.Q4] * E, ffn_norm=norm_w, bias=bias, shared=shared)
+        be.set_layer(l, router, bias, norm_w,
+                     shared["gate"] if shared else None, shared["up"] if shared else None,
+                     shared["down"] if shared else None, shared["gate_inp"] if shared else None)
+        for e in range(E):
+            be.set_expert(l, e, slabs[e])
+    return model, be
+
+
+def bits(a):
+    return np.ascontiguousarray(a, np.float32).view(np.uint32)

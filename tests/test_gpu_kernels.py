@@ -1,0 +1,151 @@
+"""GPU parity of the kernel-level boundary (hxb_matmul / hxb_dequantize / act quantization / expf)
+against the oracle and the reference's pinned hashes. Bit-exact: integer work and the canonical
+float order leave no tolerance."""
+import ctypes as C
+
+import numpy as np
+import pytest
+
+import hearth_b200 as hb
+from hearth_b200 import native
+from oracle import oracle as O
+
+pytestmark = pytest.mark.gpu
+
+PIN_Y = {0: 0x78ee7e5c72e238a0, 1: 0xacbfba9fb13b1207, 2: 0xaa0b6460cbd8ad23, 3: 0x532a2d32570c08dc,
+         4: 0xa8a0369ab6f0ed22}
+
+
+def bits(a):
+    return np.ascontiguousarray(a, np.float32).view(np.uint32)
+
+
+@pytest.mark.parametrize("dt", [0, 1, 2, 3, 4])
+def test_matmul_reproduces_pinned_hashes(gpu, golden, dt):
+    g = golden("pinned_matmul.npz")
+    Y = native.matmul(dt, g[f"W{dt}"], 24, 512, g["X"])
+    assert O.fnv1a(Y) == PIN_Y[dt]
+
+
+# the input kinds of engine/tests/test_quant.c:179-221
+def fill(rng, n, kind, quant_target=False):
+    x = rng.standard_normal(n).astype(np.float32)
+    if kind == "zero-blocks":
+        x[(np.arange(n) // 64) % 2 == 0] = 0.0
+    elif kind == "outlier":
+        x[rng.integers(n)] = 3.0e4 if rng.integers(2) else -3.0e4
+    elif kind == "max":
+        m = 60000.0 if quant_target else 1.0e18
+        r = rng.integers(0, 4, n)
+        x = np.where(r == 0, m, np.where(r == 1, -m, x * m * 0.5)).astype(np.float32)
+    elif kind == "ties":
+        k = rng.integers(-126, 127, n).astype(np.float32)
+        x = np.clip(k + np.where(rng.integers(0, 2, n) == 1, 0.5, -0.5), -127, 127).astype(np.float32)
+        x[::64] = np.where(rng.integers(0, 2, x[::64].size) == 1, 127.0, -127.0)
+    elif kind == "tiny":
+        r = rng.integers(0, 3, n)
+        x = np.where(r == 0, x * 1e-30, np.where(r == 1, x * 1e-41, 0.0)).astype(np.float32)
+    elif kind == "cancel":
+        x[1::2] = -x[0::2][: x[1::2].size]
+    return x
+
+
+KINDS = ["gauss", "zero-blocks", "outlier", "max", "ties", "tiny", "cancel"]
+
+
+def quantize(dt, W):
+    if dt == 0:
+        return np.ascontiguousarray(W, np.float32).view(np.uint8).reshape(W.shape[0], -1)
+    if dt in (1, 2):
+        import torch
+        t = torch.from_numpy(W).to(torch.float16 if dt == 1 else torch.bfloat16)
+        return t.view(torch.int16).numpy().view(np.uint8).reshape(W.shape[0], -1)
+    if O.ref_lib() is not None:
+        return O.ref_quantize(dt, W)
+    # no reference build: random valid blocks
+    rng = np.random.default_rng(0)
+    rows, cols = W.shape
+    rb = O.row_bytes(dt, cols)
+    q = rng.integers(0, 256, (rows, rb), dtype=np.uint8)
+    bs = 34 if dt == 4 else 66
+    for b in range(cols // 64):
+        q[:, b * bs:b * bs + 2] = np.frombuffer(np.full(rows, 0.01, np.float16).tobytes(), np.uint8).reshape(rows, 2)
+    return q
+
+
+@pytest.mark.parametrize("dt", [0, 1, 2, 3, 4])
+@pytest.mark.parametrize("kind", KINDS)
+def test_matmul_equals_oracle(gpu, dt, kind):
+    rng = np.random.default_rng(hash((dt, kind)) % 2**32)
+    for rows, cols, T in ((37, 128, 1), (16, 2048, 3), (70, 768, 17), (5, 7168, 2)):
+        W = fill(rng, rows * cols, kind, quant_target=True).reshape(rows, cols)
+        X = fill(rng, T * cols, kind).reshape(T, cols)
+        q = quantize(dt, W)
+        Yg = native.matmul(dt, q, rows, cols, X)
+        Yo = O.matmul(dt, q, rows, cols, X)
+        assert np.array_equal(bits(Yg), bits(Yo)), (dt, kind, rows, cols, T)
+
+
+@pytest.mark.parametrize("dt", [3, 4])
+def test_matmul_nonfinite_weights_and_scales(gpu, dt):
+    rng = np.random.default_rng(7)
+    rows, cols, T = 24, 256, 3
+    rb = O.row_bytes(dt, cols)
+    q = rng.integers(0, 256, (rows, rb), dtype=np.uint8)
+    bs = 34 if dt == 4 else 66
+    specials = np.array([0x7c00, 0xfc00, 0x7e00, 0x7d01, 0x0001, 0x03ff, 0x8000, 0x3c00], np.uint16)
+    for r in range(rows):
+        for b in range(cols // 64):
+            h = specials[(r + b) % len(specials)] if (r * 7 + b) % 3 == 0 else np.float16(0.01).view(np.uint16)
+            q[r, b * bs:b * bs + 2] = np.frombuffer(np.uint16(h).tobytes(), np.uint8)
+    X = rng.standard_normal((T, cols)).astype(np.float32)
+    X[1, 5] = np.inf
+    X[2, 70] = np.nan
+    X[2, 200] = -np.inf
+    Yg = native.matmul(dt, q, rows, cols, X)
+    Yo = O.matmul(dt, q, rows, cols, X)
+    assert np.array_equal(bits(Yg), bits(Yo))
+    nan = np.isnan(Yg)
+    assert nan.any() and (bits(Yg)[nan] == 0x7FC00000).all()
+
+
+@pytest.mark.parametrize("dt", [0, 1, 2, 3, 4])
+def test_dequantize_equals_oracle(gpu, dt):
+    rng = np.random.default_rng(11 + dt)
+    rows, cols = 9, 320
+    q = rng.integers(0, 256, (rows, O.row_bytes(dt, cols)), dtype=np.uint8)
+    assert np.array_equal(bits(native.dequantize(dt, q, rows, cols)), bits(O.dequantize(dt, q, rows, cols)))
+
+
+def test_act_quantize_equals_oracle(gpu):
+    import torch
+    rng = np.random.default_rng(2)
+    for kind in KINDS + ["nonfinite"]:
+        n, T = 7168, 3
+        x = fill(rng, n * T, "gauss" if kind == "nonfinite" else kind).reshape(T, n)
+        if kind == "nonfinite":
+            x[0, 1], x[0, 70], x[1, 200], x[2, 201] = np.nan, np.inf, -np.inf, np.nan
+            x[1, 128:192] = np.where(np.arange(64) % 2, 1e-39, -3e-40)
+            x[2, ::7] = np.where(np.arange(x[2, ::7].size) % 2, np.finfo(np.float32).max, -np.finfo(np.float32).max)
+        xd = torch.from_numpy(x).cuda()
+        ad = torch.zeros((T, n // 64 * 72), dtype=torch.uint8, device="cuda")
+        rc = hb.lib().hxb_act_quantize_dev(C.c_void_p(xd.data_ptr()), n, T, C.c_void_p(ad.data_ptr()), None)
+        assert rc == 0
+        torch.cuda.synchronize()
+        assert np.array_equal(ad.cpu().numpy(), O.act_quantize(x)), kind
+
+
+def test_device_expf_equals_host_libm_on_all_inputs(gpu):
+    """Every float32 input: the device expf restatement vs the host C library (via the oracle)."""
+    import torch
+    chunk = 1 << 27
+    out = torch.empty(chunk, dtype=torch.float32, device="cuda")
+    for c in range((1 << 32) // chunk):
+        x0 = c * chunk
+        assert hb.lib().hxb_expf_dev(x0, chunk, C.c_void_p(out.data_ptr()), None) == 0
+        dev = out.cpu().numpy()
+        xs = (np.arange(chunk, dtype=np.uint64) + x0).astype(np.uint32).view(np.float32)
+        host = O.host_expf(xs)
+        same = dev.view(np.uint32) == host.view(np.uint32)
+        same |= np.isnan(dev) & np.isnan(host)
+        assert same.all(), f"chunk {c}: {np.count_nonzero(~same)} mismatches, e.g. x={xs[~same][:4]}"
