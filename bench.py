@@ -305,17 +305,17 @@ def run_ours(args, rank, world, local_rank):
 
 
 def main():
+    global L_
     ap = argparse.ArgumentParser()
     ap.add_argument("--gpus", type=int, default=1)
     ap.add_argument("--steps", type=int, default=5000)
     ap.add_argument("--warmup", type=int, default=20)
     ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
     ap.add_argument("--batch", type=int, default=1)
-    ap.add_argument("--layers", type=int, default=L_, help="MoE layers (48 = the Qwen3-30B-A3B stack); fewer only "
+    ap.add_argument("--layers", type=int, default=48, help="MoE layers (48 = the Qwen3-30B-A3B stack); fewer only "
                                                             "for small profiling captures")
     ap.add_argument("--no-cpu", action="store_true", help="skip the CPU baseline leg")
     args = ap.parse_args()
-    global L_
     L_ = args.layers
     rank, world, local_rank = dist_env()
     if world > 1:

@@ -158,6 +158,15 @@ cudaError_t launch_matmul(int dtype, const void *W, int64_t n_cols, const void *
     return cudaGetLastError();
 }
 
+// d * (float)q with the NaN results of the host's SSE multiply, which the reference's dequantize
+// stores unmodified: a NaN scale comes back as itself (already quiet after the f16 decode) and
+// inf * 0 gives the x86 default NaN 0xffc00000. GPU arithmetic would return its own canonical NaN.
+__device__ __forceinline__ float x86_mul_scale(float d, int q) {
+    if (d != d) return d;
+    if (q == 0 && fabsf(d) == __uint_as_float(0x7f800000u)) return __uint_as_float(0xffc00000u);
+    return __fmul_rn(d, (float)q);
+}
+
 // hearth_dequantize (engine/src/quant.c:257-307): w = f16(d) * q, one element per thread.
 __global__ void k_dequantize(int dtype, const uint8_t *__restrict__ W, int64_t n_rows, int64_t n_cols, int64_t rb,
                              float *__restrict__ out) {
@@ -172,14 +181,14 @@ __global__ void k_dequantize(int dtype, const uint8_t *__restrict__ W, int64_t n
     case BF16: v = bf16_to_f32(reinterpret_cast<const uint16_t *>(row)[c]); break;
     case Q8: {
         const uint8_t *blk = row + (c / QK) * Q8_BLOCK;
-        v = __fmul_rn(f16_to_f32((uint32_t)blk[0] | ((uint32_t)blk[1] << 8)), (float)(int8_t)blk[2 + c % QK]);
+        v = x86_mul_scale(f16_to_f32((uint32_t)blk[0] | ((uint32_t)blk[1] << 8)), (int)(int8_t)blk[2 + c % QK]);
         break;
     }
     default: {
         const uint8_t *blk = row + (c / QK) * Q4_BLOCK;
         const int j = (int)(c % QK);
         const int nib = j < 32 ? (blk[2 + j] & 15) : (blk[2 + j - 32] >> 4);
-        v = __fmul_rn(f16_to_f32((uint32_t)blk[0] | ((uint32_t)blk[1] << 8)), (float)(nib - 8));
+        v = x86_mul_scale(f16_to_f32((uint32_t)blk[0] | ((uint32_t)blk[1] << 8)), nib - 8);
         break;
     }
     }
@@ -781,10 +790,15 @@ static size_t smem_limit() {
 
 cudaError_t init_kernel_attributes() {
     const int lim = (int)smem_limit();
-    cudaError_t e = cudaFuncSetAttribute(k_moe_gateup, cudaFuncAttributeMaxDynamicSharedMemorySize, lim);
-    if (e == cudaSuccess) e = cudaFuncSetAttribute(k_moe_down, cudaFuncAttributeMaxDynamicSharedMemorySize, lim);
-    // load every MoE kernel now, so no module loading happens inside a stream capture later
     cudaFuncAttributes fa;
+    // the dynamic limit is the opt-in maximum minus the kernel's static shared memory
+    cudaError_t e = cudaFuncGetAttributes(&fa, (const void *)k_moe_gateup);
+    if (e == cudaSuccess)
+        e = cudaFuncSetAttribute(k_moe_gateup, cudaFuncAttributeMaxDynamicSharedMemorySize, lim - (int)fa.sharedSizeBytes);
+    if (e == cudaSuccess) e = cudaFuncGetAttributes(&fa, (const void *)k_moe_down);
+    if (e == cudaSuccess)
+        e = cudaFuncSetAttribute(k_moe_down, cudaFuncAttributeMaxDynamicSharedMemorySize, lim - (int)fa.sharedSizeBytes);
+    // load every MoE kernel now, so no module loading happens inside a stream capture later
     const void *kernels[] = {(const void *)k_moe_norm_act, (const void *)k_moe_router, (const void *)k_route_select,
                              (const void *)k_route_union, (const void *)k_moe_sum};
     for (const void *k : kernels)
