@@ -80,6 +80,10 @@ struct Scratch1 {
 
 }  // namespace
 
+namespace hx {
+void set_last_error(const char *msg) { g_err = msg; }
+}  // namespace hx
+
 // =============================================================================================
 // Kernel-level boundary
 // =============================================================================================

@@ -66,6 +66,21 @@ HXB_API int hxb_dequantize_dev(int dtype, const void *W, int64_t n_rows, int64_t
 /* The device expf (the host libm's results) on the bit patterns [x0, x0 + n): self-check support. */
 HXB_API int hxb_expf_dev(uint32_t x0, int64_t n, float *out, void *stream);
 
+/* ---- allocation-free matmul ------------------------------------------------------------------
+ * No counterpart in the reference (its hearth_matmul allocates a buffer on every call).
+ * For callers that must not allocate device memory when they run a matmul: a serving engine
+ * that reserved all of HBM for its own pool up front, code running while a CUDA graph is being
+ * captured (cudaMalloc cannot be recorded into a graph), or an application that budgets device
+ * memory once at start. W (n_rows rows of dtype), X [T, n_cols] f32 and Y [T, n_rows] f32 are
+ * the caller's device buffers; the Q8/Q4 activation scratch is a 4 MiB static device array
+ * (T * n_cols / 64 * 72 bytes at most, else HXB_E_CAPACITY with a message), held by every GPU
+ * that loads the library until exit. The first call on a device looks up that array's address,
+ * so make it before any stream capture. All calls share the array: calls that overlap on the
+ * GPU race and must be serialised by the caller. Results equal hxb_matmul's bit for bit. */
+#define HXB_NOALLOC_SCRATCH_BYTES ((size_t)4 << 20)
+HXB_API int hxb_matmul_noalloc(int dtype, const void *W, int64_t n_rows, int64_t n_cols, const float *X, int T,
+                               float *Y, void *stream);
+
 /* ---- MoE backend handle ---------------------------------------------------------------------- */
 typedef struct hxb_moe hxb_moe;
 
