@@ -6,6 +6,7 @@
 #include "hx_store.h"
 
 #include <chrono>
+#include <cstdlib>
 #include <cstdarg>
 #include <cstdio>
 #include <cstring>
@@ -231,6 +232,10 @@ struct hxb_moe {
     std::map<GraphKey, cudaGraphExec_t> graphs;
     hxb_moe_stats st{};
     int last_T = 0;
+    // persistent single-token decode kernel (every expert resident)
+    bool use_decode = false, dec_dirty = true;
+    DevBuf dec_router, dec_norm, dec_bias, dec_mbuf, dec_cnt, dec_bar;
+    DevBuf dec_trace;                    // phase timeline of the last launch (HXB_TRACE=1)
 
     MoeScratch scratch() const {
         MoeScratch s;
@@ -403,6 +408,29 @@ extern "C" HXB_API hxb_moe *hxb_moe_open(const hxb_moe_config *c, char *err, siz
         return nullptr;
     }
     std::memset(m->host_table, 0, sizeof(void *) * (size_t)nkeys);
+    if (m->resident_mode) {
+        const char *env = std::getenv("HXB_PERSISTENT");
+        std::string why_not;
+        m->use_decode = !(env && env[0] == '0') &&
+                        decode_supported(D, k.expert_ffn_dim, E, K, k.expert_dtype, k.shared_ffn_dim > 0, &why_not);
+        if (m->use_decode) {
+            const size_t nb = (size_t)L * K * (k.expert_ffn_dim / QK);
+            if (!m->dec_router.alloc(sizeof(void *) * (size_t)L) || !m->dec_norm.alloc(sizeof(void *) * (size_t)L) ||
+                !m->dec_bias.alloc(sizeof(void *) * (size_t)L) ||
+                !m->dec_mbuf.alloc(sizeof(float) * (size_t)K * k.expert_ffn_dim) ||
+                !m->dec_cnt.alloc(sizeof(unsigned) * nb) || !m->dec_bar.alloc(64) ||
+                !cuda_ok(init_decode_attributes(), "decode attributes")) {
+                set_errbuf(err, errlen, "hxb_moe_open: persistent decode setup failed: " + g_err);
+                return nullptr;
+            }
+            const char *tr = std::getenv("HXB_TRACE");
+            if (tr && tr[0] == '1' &&
+                !m->dec_trace.alloc(sizeof(unsigned long long) * (size_t)L * decode_grid() * decode_stamps())) {
+                set_errbuf(err, errlen, "hxb_moe_open: trace buffer");
+                return nullptr;
+            }
+        }
+    }
     if (!cuda_ok(init_kernel_attributes(), "kernel attributes")) {
         set_errbuf(err, errlen, "hxb_moe_open: " + g_err);
         return nullptr;
@@ -461,6 +489,7 @@ extern "C" HXB_API int hxb_moe_set_layer(hxb_moe *m, int layer, const float *rou
         return fail(HXB_E_NOMEM, "set_layer: device allocation or copy failed");
     }
     b.set = true;
+    m->dec_dirty = true;
     drop_graphs(m);
     return HXB_OK;
 }
@@ -529,6 +558,7 @@ extern "C" HXB_API int hxb_moe_synthesize(hxb_moe *m, uint64_t seed, float sigma
                  "table"))
         return HXB_E_DEVICE;
     if (!cuda_ok(cudaStreamSynchronize(m->stream), "synthesize")) return HXB_E_DEVICE;
+    m->dec_dirty = true;
     drop_graphs(m);
     return HXB_OK;
 }
@@ -613,13 +643,89 @@ static int run_streaming(hxb_moe *m, float *h, float *out, int T, int l0, int nl
     return HXB_OK;
 }
 
+// Device pointer tables of the per-layer dense weights for the persistent kernel.
+static bool refresh_decode_tables(hxb_moe *m) {
+    if (!m->dec_dirty) return true;
+    const int L = m->cfg.n_layers;
+    std::vector<const void *> r((size_t)L), n((size_t)L), b((size_t)L);
+    for (int l = 0; l < L; l++) {
+        r[(size_t)l] = m->layers[(size_t)l].router.p;
+        n[(size_t)l] = m->layers[(size_t)l].norm.p;
+        b[(size_t)l] = m->cfg.score_bias ? m->layers[(size_t)l].bias.p : nullptr;
+    }
+    if (!cuda_ok(cudaMemcpy(m->dec_router.p, r.data(), sizeof(void *) * (size_t)L, cudaMemcpyHostToDevice), "tables") ||
+        !cuda_ok(cudaMemcpy(m->dec_norm.p, n.data(), sizeof(void *) * (size_t)L, cudaMemcpyHostToDevice), "tables") ||
+        !cuda_ok(cudaMemcpy(m->dec_bias.p, b.data(), sizeof(void *) * (size_t)L, cudaMemcpyHostToDevice), "tables"))
+        return false;
+    m->dec_dirty = false;
+    return true;
+}
+
+static cudaError_t enqueue_decode(hxb_moe *m, float *h, int l0, int nl, cudaStream_t s) {
+    const hxb_moe_config &k = m->cfg;
+    DecodeParams p;
+    p.n_layers = nl;
+    p.D = k.d_model;
+    p.F = k.expert_ffn_dim;
+    p.E = k.n_experts;
+    p.K = k.top_k;
+    p.dtype = k.expert_dtype;
+    p.route = m->shape(1).route;
+    p.eps = k.norm_eps;
+    p.rs = k.residual_scale;
+    p.off_up = m->lay.off_up;
+    p.off_down = m->lay.off_down;
+    p.router = m->dec_router.as<const float *>() + l0;
+    p.norm = m->dec_norm.as<const float *>() + l0;
+    p.bias = m->dec_bias.as<const float *>() + l0;
+    p.slab = m->table.as<const uint8_t *>() + (size_t)l0 * k.n_experts;
+    p.h = h;
+    p.logits = m->logits.as<float>();
+    p.mbuf = m->dec_mbuf.as<float>();
+    p.act_mid = m->act_mid.as<act_q8>();
+    p.bar = m->dec_bar.as<unsigned>();
+    p.blk_cnt = m->dec_cnt.as<unsigned>();
+    p.err = m->err.as<int>();
+    p.ids_out = m->ids.as<int>();
+    p.w_out = m->wts.as<float>();
+    p.trace = m->dec_trace.as<unsigned long long>();
+    return launch_moe_decode(p, s);
+}
+
+// After a device error the persistent kernel's barrier word and arrival counters may be mid-way.
+static void reset_decode_state(hxb_moe *m) {
+    if (!m->use_decode) return;
+    cudaMemset(m->dec_bar.p, 0, m->dec_bar.n);
+    cudaMemset(m->dec_cnt.p, 0, m->dec_cnt.n);
+}
+
 static int run_range(hxb_moe *m, float *h, float *out, int T, int l0, int nl, bool with_norm, bool resid,
                      cudaStream_t user, bool host_io, const float *hin, float *hout) {
     cudaStream_t s = user ? user : m->stream;
     const size_t bytes = sizeof(float) * (size_t)T * m->cfg.d_model;
     const double t0 = now_s();
     int rc = HXB_OK;
-    if (m->resident_mode) {
+    if (m->resident_mode && m->use_decode && T == 1 && with_norm && resid && !out) {
+        if (!refresh_decode_tables(m)) return HXB_E_DEVICE;
+        float *dh = host_io ? m->hbuf.as<float>() : h;
+        if (host_io) {
+            std::memcpy(m->hpin, hin, bytes);
+            if (!cuda_ok(cudaMemcpyAsync(dh, m->hpin, bytes, cudaMemcpyHostToDevice, s), "h in")) return HXB_E_DEVICE;
+        }
+        if (!cuda_ok(enqueue_decode(m, dh, l0, nl, s), "decode launch")) return HXB_E_DEVICE;
+        if (host_io) {
+            if (!cuda_ok(cudaMemcpyAsync(m->hpin, dh, bytes, cudaMemcpyDeviceToHost, s), "h out") ||
+                !cuda_ok(cudaMemcpyAsync(m->epin, m->err.p, sizeof(int), cudaMemcpyDeviceToHost, s), "err") ||
+                !cuda_ok(cudaStreamSynchronize(s), "sync"))
+                return HXB_E_DEVICE;
+            rc = take_device_error(m, m->epin[0]);
+            if (rc != HXB_OK) {
+                reset_decode_state(m);
+                return rc;
+            }
+            std::memcpy(hout, m->hpin, bytes);
+        }
+    } else if (m->resident_mode) {
         // one CUDA graph per (T, range, buffers): the host copies (host variants) are part of it
         GraphKey key{T, l0 * 2 + (with_norm ? 1 : 0), nl * 2 + (resid ? 1 : 0), host_io ? nullptr : (const void *)h,
                      (cudaStream_t)(uintptr_t)(out ? 1 : 0)};
@@ -800,6 +906,7 @@ extern "C" HXB_API int hxb_moe_sync(hxb_moe *m, void *stream) {
     if (!cuda_ok(cudaStreamSynchronize(s), "sync")) return HXB_E_DEVICE;
     int word = 0;
     if (!cuda_ok(cudaMemcpy(&word, m->err.p, sizeof word, cudaMemcpyDeviceToHost), "error word")) return HXB_E_DEVICE;
+    if (word) reset_decode_state(m);
     return take_device_error(m, word);
 }
 
@@ -845,4 +952,15 @@ extern "C" HXB_API int hxb_moe_profile(hxb_moe *m, int T, int iters, double *us)
     int word = 0;
     cudaMemcpy(&word, m->err.p, sizeof word, cudaMemcpyDeviceToHost);
     return take_device_error(m, word);
+}
+
+// Phase timeline of the last persistent decode launch (handles opened with HXB_TRACE=1):
+// out[layer][cta][stamp] SM clock cycles; returns the number of values (0 without a trace).
+extern "C" HXB_API int64_t hxb_moe_phase_trace(hxb_moe *m, uint64_t *out, int64_t max_values) {
+    if (!m || !m->dec_trace.p) return 0;
+    const int64_t n = (int64_t)(m->dec_trace.n / sizeof(unsigned long long));
+    if (!out || max_values < n) return n;
+    cudaSetDevice(m->device);
+    if (cudaMemcpy(out, m->dec_trace.p, sizeof(uint64_t) * (size_t)n, cudaMemcpyDeviceToHost) != cudaSuccess) return -1;
+    return n;
 }

@@ -186,20 +186,25 @@ __device__ __forceinline__ float tree16(float v, unsigned mask) {
 // One 64-block integer dot: Q4 nibbles (stored q+8) against activation q, exact:
 // sum (nib-8)*xq = sum nib*xq - 8*sum(xq) (NUMERICS §3 note).
 __device__ __forceinline__ int q4_isum(const uint32_t nib[8], const int32_t aq[16], int32_t asum) {
-    int acc = 0;
+    int a0 = 0, a1 = 0;   // two independent chains (integer sums: any order is exact)
 #pragma unroll
     for (int k = 0; k < 8; k++) {
-        acc = __dp4a((int)(nib[k] & 0x0f0f0f0fu), aq[k], acc);
-        acc = __dp4a((int)((nib[k] >> 4) & 0x0f0f0f0fu), aq[8 + k], acc);
+        a0 = __dp4a((int)(nib[k] & 0x0f0f0f0fu), aq[k], a0);
+        a1 = __dp4a((int)((nib[k] >> 4) & 0x0f0f0f0fu), aq[8 + k], a1);
     }
-    return acc - 8 * asum;
+    return a0 + a1 - 8 * asum;
 }
 
 __device__ __forceinline__ int q8_isum(const uint32_t w[16], const int32_t aq[16]) {
-    int acc = 0;
+    int a0 = 0, a1 = 0, a2 = 0, a3 = 0;
 #pragma unroll
-    for (int k = 0; k < 16; k++) acc = __dp4a((int)w[k], aq[k], acc);
-    return acc;
+    for (int k = 0; k < 16; k += 4) {
+        a0 = __dp4a((int)w[k], aq[k], a0);
+        a1 = __dp4a((int)w[k + 1], aq[k + 1], a1);
+        a2 = __dp4a((int)w[k + 2], aq[k + 2], a2);
+        a3 = __dp4a((int)w[k + 3], aq[k + 3], a3);
+    }
+    return (a0 + a1) + (a2 + a3);
 }
 
 // Loads a Q4 block that starts at a 2-byte aligned byte address with aligned loads that stay

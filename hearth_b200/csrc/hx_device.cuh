@@ -15,7 +15,7 @@ enum : int {
     DEV_E_BAD_DTYPE = 3,      // an expert dtype the kernels do not handle
 };
 
-constexpr uint32_t kSpinLimit = 1u << 24;   // try_wait rounds before a wait is declared lost
+constexpr uint32_t kSpinLimit = 1u << 20;   // try_wait rounds before a wait is declared lost
 
 __device__ __forceinline__ uint32_t smem_u32(const void *p) {
     return static_cast<uint32_t>(__cvta_generic_to_shared(p));

@@ -17,6 +17,7 @@
 
 #include <cstddef>
 #include <cstdint>
+#include <string>
 #include <cuda_runtime.h>
 
 namespace hx {
@@ -99,6 +100,34 @@ cudaError_t launch_moe_experts(const MoeShape &sh, const MoeLayerDev &L, const M
 // for per-kernel timing.
 cudaError_t launch_moe_stage(int stage, const MoeShape &sh, const MoeLayerDev &L, const MoeScratch &sc, float *h,
                              float *out, bool resid, cudaStream_t s);
+
+// The persistent single-token decode kernel (hx_decode.cu): every layer of [0, n_layers) in one
+// cooperative launch with one CTA per SM (every expert resident, no shared expert).
+struct DecodeParams {
+    int n_layers, D, F, E, K, dtype;
+    RouteCfg route;
+    float eps, rs;
+    int64_t off_up, off_down;
+    const float *const *router;   // [n_layers] device pointers
+    const float *const *norm;
+    const float *const *bias;
+    const uint8_t *const *slab;   // [n_layers * E]
+    float *h;                     // [D]
+    float *logits;                // [E]
+    float *mbuf;                  // [K * F]
+    act_q8 *act_mid;              // [K * F / 64]
+    unsigned *bar;                // grid barrier word (zero at allocation)
+    unsigned *blk_cnt;            // [n_layers * K * F / 64] (zero at allocation)
+    int *err;
+    int *ids_out;
+    float *w_out;
+    unsigned long long *trace;    // null, or [n_layers][grid][decode_stamps()] phase timestamps
+};
+int decode_grid();
+int decode_stamps();
+bool decode_supported(int D, int F, int E, int K, int dtype, bool shared, std::string *why);
+cudaError_t init_decode_attributes();
+cudaError_t launch_moe_decode(const DecodeParams &p, cudaStream_t s);
 
 // Fills every expert slab of `n` slabs at dev with deterministic synthetic Q4 blocks (the
 // statistics of N(0, sigma) weights packed to Q4), for benchmarks without a container.

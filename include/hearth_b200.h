@@ -151,6 +151,12 @@ HXB_API int hxb_moe_sync(hxb_moe *m, void *stream);
  * expert resident; eager launches between CUDA events): us[0] rmsnorm + activations, us[1]
  * router + routing, us[2] gate/up + SwiGLU + mid activations, us[3] down + rank-order sum. */
 HXB_API int hxb_moe_profile(hxb_moe *m, int T, int iters, double *us);
+/* Phase timeline of the last single-token persistent launch, for handles opened with the
+ * environment variable HXB_TRACE=1: out[layer][cta][stamp] SM clock cycles (per-SM counter: compare
+ * stamps of one CTA only; stamps: start, norm,
+ * router, barrier 1, routing, gate/up, mid blocks, barrier 2, down, sum, barrier 3). Returns the
+ * number of values (call with out = NULL to size the buffer), 0 when not tracing. */
+HXB_API int64_t hxb_moe_phase_trace(hxb_moe *m, uint64_t *out, int64_t max_values);
 /* Routing of the last evaluated layer: ids / weights [T, K] (host). */
 HXB_API int hxb_moe_last_routing(hxb_moe *m, int *ids, float *weights, int T);
 
