@@ -245,16 +245,18 @@ def run_ours(args, rank, world, local_rank):
     e2e = world * e2e_steps * B / t_e2e
 
     # ---- roofline of the dominant kernel, timed live with CUDA events on its launching stream.
-    # Batch 1 runs the persistent kernel k_moe_decode: one launch per step covers every layer, so
+    # Batch 1 runs a persistent decode kernel: one launch per step covers every layer, so
     # its average launch duration is the timed region / steps. Other batches run the per-stage
     # kernels; their dominant one is k_moe_gateup, timed by hxb_moe_profile.
     us = be.profile(B, 2)
     ab = algorithmic_bytes()
     hbm, peak_kind = peaks()
     step_gbs = L_ * ab["layer"] / (ms / args.steps * 1e-3) / 1e9
-    persistent = B == 1 and os.environ.get("HXB_PERSISTENT", "1") != "0"
+    path = be.decode_path()
+    persistent = B == 1 and path != "layers"
     if persistent:
-        kernel, kbytes, kgbs = "k_moe_decode (persistent, one launch per token, all layers)", L_ * ab["layer"], step_gbs
+        kernel = "k_moe_decode (persistent, one launch per token, all layers)"
+        kbytes, kgbs = L_ * ab["layer"], step_gbs
     else:
         kernel, kbytes = "k_moe_gateup (Q4 gate+up GEMV, SwiGLU, mid act-quant)", ab["gateup"]
         kgbs = ab["gateup"] / (us[2] * 1e-6) / 1e9

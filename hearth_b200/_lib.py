@@ -26,7 +26,7 @@ EXPORTS = [
     "hxb_moe_synthesize", "hxb_moe_slab_bytes", "hxb_moe_forward", "hxb_moe_forward_dev", "hxb_moe_layer",
     "hxb_moe_layer_dev", "hxb_moe_last_routing", "hxb_moe_get_stats", "hxb_moe_reset_stats",
     "hxb_moe_is_resident", "hxb_moe_tick", "hxb_moe_prefetch", "hxb_moe_seed_heat", "hxb_moe_set_copy_hook",
-    "hxb_moe_sync", "hxb_moe_profile", "hxb_matmul_noalloc", "hxb_moe_phase_trace",
+    "hxb_moe_sync", "hxb_moe_profile", "hxb_matmul_noalloc", "hxb_moe_phase_trace", "hxb_moe_decode_path",
 ]
 
 
@@ -96,6 +96,7 @@ def lib() -> C.CDLL:
         "hxb_moe_profile": (i, [vp, i, i, C.POINTER(C.c_double)]),
         "hxb_matmul_noalloc": (i, [i, vp, i64, i64, vp, i, vp, vp]),
         "hxb_moe_phase_trace": (i64, [vp, vp, i64]),
+        "hxb_moe_decode_path": (C.c_int, [vp]),
     }
     for name, (res, args) in sig.items():
         fn = getattr(L, name)

@@ -235,6 +235,7 @@ struct hxb_moe {
     // persistent single-token decode kernel (every expert resident)
     bool use_decode = false, dec_dirty = true;
     DevBuf dec_router, dec_norm, dec_bias, dec_mbuf, dec_cnt, dec_bar;
+    unsigned dec_bars = 0;               // barriers completed by earlier persistent launches
     DevBuf dec_trace;                    // phase timeline of the last launch (HXB_TRACE=1)
 
     MoeScratch scratch() const {
@@ -409,16 +410,18 @@ extern "C" HXB_API hxb_moe *hxb_moe_open(const hxb_moe_config *c, char *err, siz
     }
     std::memset(m->host_table, 0, sizeof(void *) * (size_t)nkeys);
     if (m->resident_mode) {
+        // HXB_PERSISTENT=0: per-phase kernels only
         const char *env = std::getenv("HXB_PERSISTENT");
         std::string why_not;
-        m->use_decode = !(env && env[0] == '0') &&
+        const bool off = env && env[0] == '0';
+        m->use_decode = !off &&
                         decode_supported(D, k.expert_ffn_dim, E, K, k.expert_dtype, k.shared_ffn_dim > 0, &why_not);
         if (m->use_decode) {
             const size_t nb = (size_t)L * K * (k.expert_ffn_dim / QK);
             if (!m->dec_router.alloc(sizeof(void *) * (size_t)L) || !m->dec_norm.alloc(sizeof(void *) * (size_t)L) ||
                 !m->dec_bias.alloc(sizeof(void *) * (size_t)L) ||
                 !m->dec_mbuf.alloc(sizeof(float) * (size_t)K * k.expert_ffn_dim) ||
-                !m->dec_cnt.alloc(sizeof(unsigned) * nb) || !m->dec_bar.alloc(64) ||
+                !m->dec_cnt.alloc(sizeof(unsigned) * nb) || !m->dec_bar.alloc(16 * 128) ||
                 !cuda_ok(init_decode_attributes(), "decode attributes")) {
                 set_errbuf(err, errlen, "hxb_moe_open: persistent decode setup failed: " + g_err);
                 return nullptr;
@@ -684,6 +687,8 @@ static cudaError_t enqueue_decode(hxb_moe *m, float *h, int l0, int nl, cudaStre
     p.mbuf = m->dec_mbuf.as<float>();
     p.act_mid = m->act_mid.as<act_q8>();
     p.bar = m->dec_bar.as<unsigned>();
+    p.bar_base = m->dec_bars;
+    m->dec_bars += 3u * (unsigned)nl;
     p.blk_cnt = m->dec_cnt.as<unsigned>();
     p.err = m->err.as<int>();
     p.ids_out = m->ids.as<int>();
@@ -695,8 +700,10 @@ static cudaError_t enqueue_decode(hxb_moe *m, float *h, int l0, int nl, cudaStre
 // After a device error the persistent kernel's barrier word and arrival counters may be mid-way.
 static void reset_decode_state(hxb_moe *m) {
     if (!m->use_decode) return;
+    cudaDeviceSynchronize();
     cudaMemset(m->dec_bar.p, 0, m->dec_bar.n);
     cudaMemset(m->dec_cnt.p, 0, m->dec_cnt.n);
+    m->dec_bars = 0;
 }
 
 static int run_range(hxb_moe *m, float *h, float *out, int T, int l0, int nl, bool with_norm, bool resid,
@@ -705,7 +712,7 @@ static int run_range(hxb_moe *m, float *h, float *out, int T, int l0, int nl, bo
     const size_t bytes = sizeof(float) * (size_t)T * m->cfg.d_model;
     const double t0 = now_s();
     int rc = HXB_OK;
-    if (m->resident_mode && m->use_decode && T == 1 && with_norm && resid && !out) {
+    if (m->resident_mode && m->use_decode && T == 1 && with_norm && resid && !out && nl <= decode_max_layers()) {
         if (!refresh_decode_tables(m)) return HXB_E_DEVICE;
         float *dh = host_io ? m->hbuf.as<float>() : h;
         if (host_io) {
@@ -952,6 +959,11 @@ extern "C" HXB_API int hxb_moe_profile(hxb_moe *m, int T, int iters, double *us)
     int word = 0;
     cudaMemcpy(&word, m->err.p, sizeof word, cudaMemcpyDeviceToHost);
     return take_device_error(m, word);
+}
+
+extern "C" HXB_API int hxb_moe_decode_path(const hxb_moe *m) {
+    if (!m) return HXB_E_ARG;
+    return m->use_decode ? 1 : 0;
 }
 
 // Phase timeline of the last persistent decode launch (handles opened with HXB_TRACE=1):

@@ -99,7 +99,9 @@ __device__ __forceinline__ float canon(float v) { return v != v ? __uint_as_floa
      0x3fef5818dcfba487ull, 0x3fef7c97337b9b5full, 0x3fefa4afa2a490daull, 0x3fefd0765b6e4540ull}
 
 #ifdef __CUDACC__
-static __constant__ uint64_t kExp2TabDev[32] = HX_EXP2_TAB;
+// global memory, read through the L1 / read-only path: the 32 lanes of a warp index the table
+// independently, which the constant cache would serialise
+static __device__ const uint64_t kExp2TabDev[32] = HX_EXP2_TAB;
 #endif
 static const uint64_t kExp2TabHost[32] = HX_EXP2_TAB;
 
@@ -108,7 +110,7 @@ static const uint64_t kExp2TabHost[32] = HX_EXP2_TAB;
 #define HX_DMUL(a, b) __dmul_rn((a), (b))
 #define HX_DSUB(a, b) __dsub_rn((a), (b))
 #define HX_D2F(a) __double2float_rn(a)
-#define HX_EXP2(i) kExp2TabDev[i]
+#define HX_EXP2(i) __ldg(&kExp2TabDev[i])
 #define HX_F2U(f) __float_as_uint(f)
 #define HX_U2F(u) __uint_as_float(u)
 #define HX_D2U(d) ((uint64_t)__double_as_longlong(d))

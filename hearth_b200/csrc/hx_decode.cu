@@ -32,19 +32,21 @@ constexpr int DEC_THREADS = 512;
 constexpr int DEC_WARPS = DEC_THREADS / 32;
 constexpr int DEC_CH = 4;          // gate/up row pairs per chunk (one bulk-copy group)
 constexpr int DEC_PROWS = 8;       // rows per warp_rows_1tok call (P buffer rows)
-constexpr int DEC_MAXQ = 24;       // chunks per CTA
+constexpr int DEC_MAXL = 128;      // layers per launch (router / norm / bias pointer tables in smem)
 constexpr int BAR_DOWN = 28, BAR_ROUTER = 29;
 // Phase stamps of the optional timeline (thread 0 of every CTA, per layer).
 enum : int { ST_START, ST_NORM, ST_ROUTER, ST_BAR1, ST_ROUTE, ST_GATEUP, ST_MID, ST_BAR2, ST_DOWN, ST_SUM, ST_BAR3,
              DEC_STAMPS };
 
-// Shared-memory carve-up of one CTA (identical on host and device).
+// Shared-memory carve-up of one CTA (identical on host and device). The router rows and ffn_norm
+// of a layer share the gate/up region: they are read in phase A and copied in after the previous
+// layer's gate/up rows were consumed.
 struct DecodeLayout {
-    int G, R, rpc, ppc;                // CTAs, down rows / CTA, router rows / CTA, gate/up pairs / CTA
+    int G, R, rpc, units;              // CTAs, down rows / CTA, router rows / CTA, gate/up units (64-row blocks)
     int nbD, nbF;
     int64_t rbD, rbF;
-    size_t off_hs, off_xs, off_norm, off_rrow, off_stab, off_xact, off_gu, off_dn, off_amid, off_y, off_p, off_gout,
-        off_score, off_ids, off_w, off_done, total;
+    size_t off_hs, off_stab, off_xact, off_gu, off_rrow, off_norm, off_dn, off_amid, off_y, off_p, off_gout,
+        off_mloc, off_lg, off_score, off_sel, off_key, off_gsc, off_keep, off_ids, off_w, off_ptrs, total;
 };
 
 HX_HD inline size_t align16(size_t v) { return (v + 15) & ~size_t(15); }
@@ -62,24 +64,31 @@ HX_HD inline DecodeLayout decode_layout(int G, int D, int F, int E, int K, int d
     L.R = (D + G - 1) / G;
     L.R = (L.R + ra - 1) / ra * ra;
     L.rpc = (E + G - 1) / G;
-    L.ppc = (K * F + G - 1) / G;
+    L.units = K * L.nbF;
     size_t o = 512;   // mbarriers
     L.off_hs = o; o = align16(o + (size_t)D * 4);
-    L.off_xs = o; o = align16(o + (size_t)D * 4);
-    L.off_norm = o; o = align16(o + (size_t)D * 4);
-    L.off_rrow = o; o = align16(o + (size_t)L.rpc * D * 4);
     L.off_stab = o; o = align16(o + (size_t)E * 8);
     L.off_xact = o; o = align16(o + (size_t)L.nbD * ACT_BLOCK);
-    L.off_gu = o; o = align16(o + (size_t)(L.ppc + 1) * 2 * L.rbD);
+    L.off_gu = o;
+    const size_t gu_bytes = (size_t)QK * 2 * L.rbD, rr_bytes = (size_t)(L.rpc + 1) * D * 4;
+    L.off_rrow = o;
+    L.off_norm = o + (size_t)L.rpc * D * 4;
+    o = align16(o + (gu_bytes > rr_bytes ? gu_bytes : rr_bytes));
     L.off_dn = o; o = align16(o + (size_t)K * L.R * L.rbF);
     L.off_amid = o; o = align16(o + (size_t)K * L.nbF * ACT_BLOCK);
     L.off_y = o; o = align16(o + (size_t)K * L.R * 4);
     L.off_p = o; o = align16(o + (size_t)DEC_WARPS * DEC_PROWS * 33 * 4);
     L.off_gout = o; o = align16(o + (size_t)DEC_WARPS * DEC_PROWS * 4);
-    L.off_score = o; o = align16(o + (size_t)3 * E * 4 + 16 + (size_t)E * 8 + 64 * 4 + 16 + 64 * 4);
+    L.off_mloc = o; o = align16(o + (size_t)QK * 4);
+    L.off_lg = o; o = align16(o + (size_t)E * 4);
+    L.off_score = o; o = align16(o + (size_t)E * 4);
+    L.off_sel = o; o = align16(o + (size_t)E * 4);
+    L.off_key = o; o = align16(o + (size_t)((E + 3) / 4 * 4) * 8);
+    L.off_gsc = o; o = align16(o + 64 * 4);
+    L.off_keep = o; o = align16(o + 64 * 4);
     L.off_ids = o; o = align16(o + (size_t)K * 4);
     L.off_w = o; o = align16(o + (size_t)K * 4);
-    L.off_done = o; o = align16(o + (size_t)(2 * 32 + 1) * 4);
+    L.off_ptrs = o; o = align16(o + (size_t)3 * DEC_MAXL * 8);
     L.total = o;
     return L;
 }
@@ -97,7 +106,8 @@ struct DecodeArgs {
     float *logits;                // [E]
     float *mbuf;                  // [K, F] SwiGLU outputs
     act_q8 *act_mid;              // [K, F/64]
-    unsigned *bar;                // grid barrier word
+    unsigned *bar;                // [DEC_BAR_LINES * 32] barrier counters (zero at allocation)
+    unsigned bar_base;            // barriers completed by earlier launches (3 * layers per launch)
     unsigned *blk_cnt;            // [Lyr, K, F/64] arrival counters (zero between launches)
     int *err;
     int *ids_out;                 // [K] routing of the last layer
@@ -124,19 +134,30 @@ __device__ __forceinline__ unsigned ld_acquire(const unsigned *p) {
     return v;
 }
 
-// Sense-reversing grid barrier: CTA 0 adds 2^31 - (G - 1), every other CTA adds 1, so the top bit
-// of the word flips exactly when all G CTAs have arrived and the low bits return to their value.
-__device__ __forceinline__ void grid_sync(unsigned *bar, int *err) {
+// Grid barrier on one counter: after the block barrier, thread 0 adds 1 with a release reduction
+// (the block barrier orders the other threads' writes before it, so no separate fence), and lane 0..
+// of warp 0 poll with acquire loads until the counter reaches the target. The target grows by the
+// grid size with every barrier and across launches (the host passes each launch's first barrier
+// number), so nothing is ever reset; the 32-bit counts are compared wrap-safely. Counters spread
+// over several 128-byte lines measured slower than one on B200 (2482 vs 2290 cycles a barrier), so
+// DEC_BAR_LINES is 1; the code keeps the general form.
+constexpr int DEC_BAR_LINES = 1;
+
+__device__ __forceinline__ void red_release_add(unsigned *p, unsigned v) {
+    asm volatile("red.release.gpu.global.add.u32 [%0], %1;" ::"l"(p), "r"(v) : "memory");
+}
+
+__device__ __forceinline__ void grid_sync(unsigned *ctr, unsigned target, int *err) {
     __syncthreads();
-    if (threadIdx.x == 0) {
-        const unsigned inc = blockIdx.x == 0 ? 0x80000000u - (gridDim.x - 1) : 1u;
-        __threadfence();
-        const unsigned old = atom_add_release(bar, inc);
-        uint32_t spins = 0;
-        while (((ld_acquire(bar) ^ old) & 0x80000000u) == 0) {
-            // give up on the limit, or at once when another wait of this launch already gave up
-            if (++spins > kBarrierSpinLimit || ((spins & 1023u) == 0 && *(volatile int *)err)) {
-                set_error(err, DEV_E_BARRIER);
+    if (threadIdx.x < 32) {
+        const int lane = threadIdx.x;
+        if (lane == 0) red_release_add(ctr + (blockIdx.x % DEC_BAR_LINES) * 32, 1u);
+        for (uint32_t spins = 0;; spins++) {
+            const unsigned v = lane < DEC_BAR_LINES ? ld_acquire(ctr + lane * 32) : 0u;
+            const unsigned sum = __reduce_add_sync(0xffffffffu, v);
+            if ((int)(sum - target) >= 0) break;
+            if (spins > kBarrierSpinLimit || ((spins & 1023u) == 0 && *(volatile int *)err)) {
+                if (lane == 0) set_error(err, DEV_E_BARRIER);
                 break;
             }
         }
@@ -205,62 +226,48 @@ __device__ __forceinline__ void warp_rows_1tok(const uint8_t *tile, int64_t rb, 
     __syncwarp();
 }
 
-// The CTA's gate/up pairs: pair p in [0, K*F) is (rank j = p / F, row r = p % F); CTA c owns
-// [c * K*F / G, (c+1) * K*F / G), cut into chunks of at most DEC_CH pairs that stay in one expert.
-struct Chunk {
-    int j, r0, n, pbase;   // expert rank, first row, pairs, index of its first pair within the CTA
-};
-
-__device__ __forceinline__ int cta_chunks(int c, int G, int K, int F, Chunk *out) {
-    const int64_t P = (int64_t)K * F;
-    const int p0 = (int)(P * c / G), p1 = (int)(P * (c + 1) / G);
-    int n = 0;
-    for (int p = p0; p < p1 && n < DEC_MAXQ;) {
-        const int j = p / F, r = p - j * F;
-        const int len = min(min(DEC_CH, F - r), p1 - p);
-        out[n].j = j;
-        out[n].r0 = r;
-        out[n].n = len;
-        out[n].pbase = p - p0;
-        n++;
-        p += len;
-    }
-    return n;
-}
-
 template <int DT>
 __device__ void decode_body(const DecodeArgs &a, uint8_t *smem) {
     const DecodeLayout &ly = a.lay;
     const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
     const int c = blockIdx.x, G = gridDim.x;
-    const int D = a.D, F = a.F, E = a.E, K = a.K;
+    const int D = a.D, E = a.E, K = a.K;
     uint64_t *bars = reinterpret_cast<uint64_t *>(smem);
-    float *hs = reinterpret_cast<float *>(smem + ly.off_hs);
-    float *xs = reinterpret_cast<float *>(smem + ly.off_xs);
-    float *normv = reinterpret_cast<float *>(smem + ly.off_norm);
-    float *rrow = reinterpret_cast<float *>(smem + ly.off_rrow);
+    float *hs = reinterpret_cast<float *>(smem + ly.off_hs);   // h, then x in place
     const uint8_t **stab = reinterpret_cast<const uint8_t **>(smem + ly.off_stab);   // this layer's slabs
     act_q8 *xact = reinterpret_cast<act_q8 *>(smem + ly.off_xact);
     uint8_t *gu = smem + ly.off_gu;
+    float *rrow = reinterpret_cast<float *>(smem + ly.off_rrow);
+    float *normv = reinterpret_cast<float *>(smem + ly.off_norm);
     uint8_t *dn = smem + ly.off_dn;
     act_q8 *amid = reinterpret_cast<act_q8 *>(smem + ly.off_amid);
     float *Y = reinterpret_cast<float *>(smem + ly.off_y);
     float *P = reinterpret_cast<float *>(smem + ly.off_p) + warp * DEC_PROWS * 33;
     float *gout = reinterpret_cast<float *>(smem + ly.off_gout) + warp * DEC_PROWS;
-    float *score = reinterpret_cast<float *>(smem + ly.off_score), *sel = score + E, *lgs = sel + E;
-    unsigned long long *rkey = reinterpret_cast<unsigned long long *>(
-        smem + align16(ly.off_score + (size_t)3 * E * 4));
-    float *gscr = reinterpret_cast<float *>(rkey + E), *red = gscr + 64;
-    int *gkeep = reinterpret_cast<int *>(red + 4);
+    float *mloc = reinterpret_cast<float *>(smem + ly.off_mloc);
+    float *lgs = reinterpret_cast<float *>(smem + ly.off_lg);
+    float *score = reinterpret_cast<float *>(smem + ly.off_score);
+    float *sel = reinterpret_cast<float *>(smem + ly.off_sel);
+    unsigned long long *rkey = reinterpret_cast<unsigned long long *>(smem + ly.off_key);
+    float *gscr = reinterpret_cast<float *>(smem + ly.off_gsc);
+    int *gkeep = reinterpret_cast<int *>(smem + ly.off_keep);
     int *ids = reinterpret_cast<int *>(smem + ly.off_ids);
     float *wts = reinterpret_cast<float *>(smem + ly.off_w);
-    int *done = reinterpret_cast<int *>(smem + ly.off_done);   // [0] count, then (j, b) pairs
+    const float **p_router = reinterpret_cast<const float **>(smem + ly.off_ptrs);
+    const float **p_norm = p_router + DEC_MAXL, **p_bias = p_norm + DEC_MAXL;
     __shared__ float rms_r;
+    for (int i = tid; i < a.Lyr; i += DEC_THREADS) {
+        p_router[i] = a.router[i];
+        p_norm[i] = a.norm[i];
+        p_bias[i] = a.bias[i];
+    }
 
-    Chunk ch[DEC_MAXQ];
-    const int nq = cta_chunks(c, G, K, F, ch);
+    // this CTA's gate/up unit: the 64-row block b of the rank-j expert (one mid activation block)
+    const bool has_unit = c < ly.units;
+    const int uj = has_unit ? c / ly.nbF : 0, ub = has_unit ? c - uj * ly.nbF : 0;
     const int d0 = c * ly.R, d1 = min(D, d0 + ly.R), nrow = max(0, d1 - d0);
-    const int pfirst = (int)((int64_t)K * F * c / G), plast = (int)((int64_t)K * F * (c + 1) / G);
+    const uint32_t chunk_bytes = (uint32_t)(DEC_CH * ly.rbD);
+    const bool small_route = E <= 128 && a.route.n_group <= 1;
 
     if (tid == 0) {
         for (int i = 0; i < 32; i++) mbar_init(&bars[i], 1);
@@ -272,16 +279,18 @@ __device__ void decode_body(const DecodeArgs &a, uint8_t *smem) {
         for (int t = 0; t < ly.rpc; t++)
             if (c + t * G < E) bytes += (uint32_t)D * 4;
         mbar_expect_tx(&bars[BAR_ROUTER], bytes);
-        bulk_g2s(normv, a.norm[l], (uint32_t)D * 4, &bars[BAR_ROUTER]);
+        bulk_g2s(normv, p_norm[l], (uint32_t)D * 4, &bars[BAR_ROUTER]);
         bulk_g2s(stab, a.slab + (size_t)l * E, (uint32_t)E * 8, &bars[BAR_ROUTER]);
         for (int t = 0; t < ly.rpc; t++)
             if (c + t * G < E)
-                bulk_g2s(rrow + (size_t)t * D, a.router[l] + (size_t)(c + t * G) * D, (uint32_t)D * 4,
+                bulk_g2s(rrow + (size_t)t * D, p_router[l] + (size_t)(c + t * G) * D, (uint32_t)D * 4,
                          &bars[BAR_ROUTER]);
     };
     if (tid == 0) issue_router(0);
 
     unsigned long long *stamp = nullptr;
+    unsigned nbar = a.bar_base;   // barriers passed so far
+    auto barrier = [&]() { grid_sync(a.bar, (++nbar) * (unsigned)G, a.err); };
     for (int l = 0; l < a.Lyr; l++) {
         const uint32_t par = (uint32_t)(l & 1);
         if (a.trace) stamp = a.trace + ((size_t)l * G + c) * DEC_STAMPS;
@@ -305,10 +314,10 @@ __device__ void decode_body(const DecodeArgs &a, uint8_t *smem) {
         HX_STAMP(ST_NORM);
         {
             const float r = rms_r;
-            for (int i = tid; i < D; i += DEC_THREADS) xs[i] = __fmul_rn(__fmul_rn(hs[i], r), normv[i]);
+            for (int i = tid; i < D; i += DEC_THREADS) hs[i] = __fmul_rn(__fmul_rn(hs[i], r), normv[i]);
         }
         __syncthreads();
-        for (int b = warp; b < ly.nbD; b += DEC_WARPS) act_quant_warp(xs[b * QK + lane], xs[b * QK + lane + 32], xact + b, lane);
+        for (int b = warp; b < ly.nbD; b += DEC_WARPS) act_quant_warp(hs[b * QK + lane], hs[b * QK + lane + 32], xact + b, lane);
         {   // router rows: one 16-lane group each (warp-uniform tree; idle groups add zeros)
             const int t = tid >> 4, j = tid & 15;
             const bool active = t < ly.rpc && c + t * G < E;
@@ -316,7 +325,7 @@ __device__ void decode_body(const DecodeArgs &a, uint8_t *smem) {
             if (active) {
                 const float *w = rrow + (size_t)t * D;
 #pragma unroll 8
-                for (int i = j; i < D; i += 16) L = __fadd_rn(L, __fmul_rn(w[i], xs[i]));
+                for (int i = j; i < D; i += 16) L = __fadd_rn(L, __fmul_rn(w[i], hs[i]));
             }
             if (warp < (ly.rpc + 1) / 2) {
                 L = tree16(L, 0xffffffffu);
@@ -324,87 +333,63 @@ __device__ void decode_body(const DecodeArgs &a, uint8_t *smem) {
             }
         }
         HX_STAMP(ST_ROUTER);
-        grid_sync(a.bar, a.err);
+        barrier();
         HX_STAMP(ST_BAR1);
 
-        // ---------------- phase B: routing, expert rows in flight, gate/up + SwiGLU + mid blocks
-        route_token_cta(a.route, a.logits, a.bias[l], lgs, rkey, score, sel, gscr, gkeep, red, ids, wts);
-        HX_STAMP(ST_ROUTE);
-        if (warp == 0) {   // issue every copy of this layer from the 32 lanes (slab pointers in smem)
+        // ---------------- phase B: routing (warp 0), copies in flight, gate/up + SwiGLU, mid block
+        if (small_route) route_token_cta_small(a.route, a.logits, p_bias[l], score, rkey, ids, wts);
+        if (warp == 0) {
+            if (!small_route)
+                route_token_warp1(a.route, a.logits, p_bias[l], lgs, rkey, score, sel, gscr, gkeep, ids, wts);
+            if (lane == 0) HX_STAMP(ST_ROUTE);
             fence_proxy_async();
-            for (int q = lane; q < nq; q += 32) {   // gate/up chunks, one barrier each
-                const uint8_t *slab = stab[ids[ch[q].j]];
-                const uint32_t bytes = (uint32_t)(ch[q].n * ly.rbD);
-                uint8_t *dst = gu + (size_t)ch[q].pbase * 2 * ly.rbD;
-                if (!slab) {
-                    set_error(a.err, DEV_E_NOT_RESIDENT);
-                    mbar_expect_tx(&bars[q], 0);
-                    continue;
+            if (has_unit) {   // gate/up rows of the unit: chunk q = rows 4q..4q+3 of gate and of up
+                const uint8_t *slab = stab[ids[uj]];
+                if (lane < QK / DEC_CH) {
+                    if (!slab) {
+                        if (lane == 0) set_error(a.err, DEV_E_NOT_RESIDENT);
+                        mbar_expect_tx(&bars[lane], 0);
+                    } else {
+                        const int64_t r0 = (int64_t)ub * QK + lane * DEC_CH;
+                        uint8_t *dst = gu + (size_t)lane * 2 * chunk_bytes;
+                        mbar_expect_tx(&bars[lane], 2 * chunk_bytes);
+                        bulk_g2s(dst, slab + r0 * ly.rbD, chunk_bytes, &bars[lane]);
+                        bulk_g2s(dst + chunk_bytes, slab + a.off_up + r0 * ly.rbD, chunk_bytes, &bars[lane]);
+                    }
                 }
-                mbar_expect_tx(&bars[q], 2 * bytes);
-                bulk_g2s(dst, slab + (int64_t)ch[q].r0 * ly.rbD, bytes, &bars[q]);
-                bulk_g2s(dst + bytes, slab + a.off_up + (int64_t)ch[q].r0 * ly.rbD, bytes, &bars[q]);
             }
             if (nrow > 0) {   // down rows [d0, d1) of the K experts on one barrier
-                const bool have = lane < K && stab[ids[lane]] != nullptr;
+                const uint8_t *slab = lane < K ? stab[ids[lane]] : nullptr;
+                const bool have = slab != nullptr;
                 if (lane < K && !have) set_error(a.err, DEV_E_NOT_RESIDENT);
                 const unsigned nhave = __popc(__ballot_sync(0xffffffffu, have));
                 if (lane == 0) mbar_expect_tx(&bars[BAR_DOWN], nhave * (uint32_t)(nrow * ly.rbF));
                 __syncwarp();
                 if (have)
-                    bulk_g2s(dn + (size_t)lane * ly.R * ly.rbF, stab[ids[lane]] + a.off_down + (int64_t)d0 * ly.rbF,
+                    bulk_g2s(dn + (size_t)lane * ly.R * ly.rbF, slab + a.off_down + (int64_t)d0 * ly.rbF,
                              (uint32_t)(nrow * ly.rbF), &bars[BAR_DOWN]);
             }
             __syncwarp();
         }
-        __syncthreads();   // every lane has read stab: the next layer's pointers may land there
-        if (tid == 0) {
+        if (has_unit) {   // warp q: chunk q (4 gate rows then 4 up rows) -> 4 SwiGLU values
+            const int q = warp;
+            if (q < QK / DEC_CH && mbar_wait(&bars[q], par, a.err)) {
+                warp_rows_1tok<DT>(gu + (size_t)q * 2 * chunk_bytes, ly.rbD, ly.nbD, 2 * DEC_CH, xact, P, gout);
+                if (lane < DEC_CH) mloc[q * DEC_CH + lane] = swiglu_c(gout[lane], gout[DEC_CH + lane]);
+            }
+        }
+        __syncthreads();
+        HX_STAMP(ST_GATEUP);
+        if (has_unit && warp == 0) {   // the unit's mid activation block (NUMERICS §2)
+            act_quant_warp(mloc[lane], mloc[lane + 32], a.act_mid + (size_t)uj * ly.nbF + ub, lane);
+            __threadfence();
+        }
+        if (tid == 0) {   // gate/up rows are consumed: the next layer's router rows may land there
             fence_proxy_async();
             if (l + 1 < a.Lyr) issue_router(l + 1);
         }
-        for (int q = warp; q < nq; q += DEC_WARPS) {
-            if (!mbar_wait(&bars[q], par, a.err)) continue;
-            const Chunk &k = ch[q];
-            warp_rows_1tok<DT>(gu + (size_t)k.pbase * 2 * ly.rbD, ly.rbD, ly.nbD, 2 * k.n, xact, P, gout);
-            if (lane < k.n) {
-                const float m = swiglu_c(gout[lane], gout[k.n + lane]);
-                __stcg(a.mbuf + (size_t)k.j * F + k.r0 + lane, m);
-            }
-            __syncwarp();
-        }
-        __threadfence();
-        __syncthreads();
-        HX_STAMP(ST_GATEUP);
-        if (warp == 0) {   // arrivals per 64-row mid block; the CTA that completes a block quantizes it
-            // the CTA's pair range [pfirst, plast) touches at most 32 blocks: lane i takes the i-th
-            const int j0 = pfirst / F, b0 = (pfirst - j0 * F) / QK;
-            const int gb = j0 * ly.nbF + b0 + lane;   // global block index = j * nbF + b
-            const int j = gb / ly.nbF, b = gb - j * ly.nbF;
-            const int bs = j * F + b * QK, be = bs + QK;
-            const int lo = max(bs, pfirst), hi = min(be, plast);
-            bool fin = false;
-            if (lo < hi) {
-                const unsigned cnt = (unsigned)(hi - lo);
-                unsigned *ctr = a.blk_cnt + ((size_t)l * K + j) * ly.nbF + b;
-                fin = atomicAdd(ctr, cnt) + cnt == (unsigned)QK;
-            }
-            const unsigned m = __ballot_sync(0xffffffffu, fin);
-            if (fin) {
-                const int slot = __popc(m & ((1u << lane) - 1u));
-                done[1 + 2 * slot] = j;
-                done[2 + 2 * slot] = b;
-            }
-            if (lane == 0) done[0] = __popc(m);
-            __threadfence();
-        }
-        __syncthreads();
-        for (int i = warp; i < done[0]; i += DEC_WARPS) {
-            const int j = done[1 + 2 * i], b = done[2 + 2 * i];
-            const float *m = a.mbuf + (size_t)j * F + (size_t)b * QK;
-            act_quant_warp(__ldcg(m + lane), __ldcg(m + lane + 32), a.act_mid + (size_t)j * ly.nbF + b, lane);
-        }
         HX_STAMP(ST_MID);
-        grid_sync(a.bar, a.err);
+        barrier();
         HX_STAMP(ST_BAR2);
 
         // ---------------- phase C: down rows, rank-order sum, residual
@@ -436,21 +421,19 @@ __device__ void decode_body(const DecodeArgs &a, uint8_t *smem) {
             a.w_out[tid] = wts[tid];
         }
         HX_STAMP(ST_SUM);
-        grid_sync(a.bar, a.err);
+        barrier();
         HX_STAMP(ST_BAR3);
 #undef HX_STAMP
     }
     // every bulk copy this CTA issued has landed before it exits (already true unless a wait gave up)
     if (tid == 0 && a.Lyr > 0) {
         const uint32_t last = (uint32_t)((a.Lyr - 1) & 1);
-        for (int q = 0; q < nq; q++) mbar_wait(&bars[q], last, nullptr);
+        if (has_unit)
+            for (int q = 0; q < QK / DEC_CH; q++) mbar_wait(&bars[q], last, nullptr);
         if (nrow > 0) mbar_wait(&bars[BAR_DOWN], last, nullptr);
         mbar_wait(&bars[BAR_ROUTER], last, nullptr);
     }
     __syncthreads();
-    // leave the arrival counters at zero for the next launch
-    const int ncnt = a.Lyr * K * ly.nbF;
-    for (int i = c * DEC_THREADS + tid; i < ncnt; i += G * DEC_THREADS) a.blk_cnt[i] = 0u;
 }
 
 __global__ void __launch_bounds__(DEC_THREADS, 1) k_moe_decode(DecodeArgs a) {
@@ -462,6 +445,7 @@ __global__ void __launch_bounds__(DEC_THREADS, 1) k_moe_decode(DecodeArgs a) {
 // ------------------------------------------------------------------------------------- host side
 
 int decode_stamps() { return DEC_STAMPS; }
+int decode_max_layers() { return DEC_MAXL; }
 
 int decode_grid() {
     static int cached[64] = {};
@@ -490,8 +474,10 @@ bool decode_supported(int D, int F, int E, int K, int dtype, bool shared, std::s
     const int G = decode_grid();
     const DecodeLayout ly = decode_layout(G, D, F, E, K, dtype);
     if (ly.rpc > 2 * DEC_WARPS) return no("router rows per CTA");
-    if (ly.R > 16) return no("down rows per CTA > 16");
-    if (((int64_t)K * F + G - 1) / G > DEC_CH * (DEC_MAXQ - 2)) return no("gate/up pairs per CTA");
+    if (ly.R > DEC_PROWS * DEC_WARPS) return no("down rows per CTA");
+    if (ly.units > G) return no("more gate/up blocks (top_k * F / 64) than SMs");
+    (void)0;
+    if (QK / DEC_CH > DEC_WARPS || QK / DEC_CH > BAR_DOWN) return no("chunking");
     int lim = 0, dev = 0;
     cudaGetDevice(&dev);
     cudaDeviceGetAttribute(&lim, cudaDevAttrMaxSharedMemoryPerBlockOptin, dev);
@@ -534,6 +520,7 @@ cudaError_t launch_moe_decode(const DecodeParams &p, cudaStream_t s) {
     a.mbuf = p.mbuf;
     a.act_mid = p.act_mid;
     a.bar = p.bar;
+    a.bar_base = p.bar_base;
     a.blk_cnt = p.blk_cnt;
     a.err = p.err;
     a.ids_out = p.ids_out;

@@ -116,7 +116,8 @@ struct DecodeParams {
     float *logits;                // [E]
     float *mbuf;                  // [K * F]
     act_q8 *act_mid;              // [K * F / 64]
-    unsigned *bar;                // grid barrier word (zero at allocation)
+    unsigned *bar;                // barrier counters: 16 lines of 128 bytes, zero at allocation
+    unsigned bar_base;            // barriers of earlier launches (3 * n_layers each)
     unsigned *blk_cnt;            // [n_layers * K * F / 64] (zero at allocation)
     int *err;
     int *ids_out;
@@ -125,6 +126,7 @@ struct DecodeParams {
 };
 int decode_grid();
 int decode_stamps();
+int decode_max_layers();
 bool decode_supported(int D, int F, int E, int K, int dtype, bool shared, std::string *why);
 cudaError_t init_decode_attributes();
 cudaError_t launch_moe_decode(const DecodeParams &p, cudaStream_t s);

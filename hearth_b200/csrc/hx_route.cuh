@@ -195,54 +195,46 @@ __device__ __forceinline__ unsigned long long rank_key(float v, int i) {
     return ((unsigned long long)u << 32) | (unsigned long long)(0xffffffffu - (uint32_t)i);
 }
 
-// Top-k routing of one token by a whole CTA (engine/src/model.c:793-843), for the decode path:
-// logits -> score (softmax or sigmoid) -> selection value (+ bias) -> group mask -> top-K by rank.
-// Each thread ranks its experts against all E: rank(i) = #{k : k ranks before i}; the order is
-// total (ties to the lower index, NaN last), so the K experts with rank < K are exactly
-// route_select's ids in descending order. lg, score, sel: [E] shared, key: [E] shared (8-byte
-// aligned); gsc/keep: [n_group] shared; red: 4 floats.
-// Results land in ids/w (shared, K each). Every thread of the CTA must call it.
-__device__ __forceinline__ void route_token_cta(const RouteCfg &R, const float *logit_g, const float *bias,
-                                                float *lg, unsigned long long *key, float *score, float *sel,
-                                                float *gsc, int *keep, float *red, int *ids, float *w) {
-    const int tid = threadIdx.x, nt = blockDim.x, lane = tid & 31, warp = tid >> 5;
+// Top-k routing of one token by ONE warp, warp-synchronous (no CTA barrier), for the decode path:
+// logits -> score (softmax or sigmoid) -> selection value (+ bias) -> group mask -> top-K.
+// The top-K comes from ranks: rank(i) = #{o : key(o) > key(i)} with rank_key's order, which is
+// route_select's (engine/src/model.c:793-831), so the experts with rank < K are its ids in order.
+// lg/score/sel [E], key [E] (8-byte aligned), gsc/keep [n_group]: this warp's shared scratch.
+// Results: ids[K], w[K] in shared memory, valid after the call for this warp (and for the CTA
+// after its next barrier).
+__device__ __forceinline__ void route_token_warp1(const RouteCfg &R, const float *logit_g, const float *bias,
+                                                  float *lg, unsigned long long *key, float *score, float *sel,
+                                                  float *gsc, int *keep, int *ids, float *w) {
+    const int lane = threadIdx.x & 31;
     const int E = R.E, K = R.K;
-    for (int i = tid; i < E; i += nt) lg[i] = __ldcg(logit_g + i);
-    __syncthreads();
+    for (int i = lane; i < E; i += 32) lg[i] = __ldcg(logit_g + i);
+    __syncwarp();
     if (R.score_fn == SCORE_SOFTMAX) {
-        if (warp == 0) {   // m = x[0]; m = x[i] > m ? x[i] : m  (a leading NaN stays)
-            float m = -__uint_as_float(0x7f800000u);
-            for (int i = lane; i < E; i += 32) m = fmaxf(m, lg[i]);
+        float m = -__uint_as_float(0x7f800000u);   // m = x[0]; m = x[i] > m ? x[i] : m
+        for (int i = lane; i < E; i += 32) m = fmaxf(m, lg[i]);
 #pragma unroll
-            for (int s = 16; s >= 1; s >>= 1) m = fmaxf(m, __shfl_xor_sync(0xffffffffu, m, s));
-            if (lane == 0) red[0] = lg[0] != lg[0] ? lg[0] : m;
-        }
-        __syncthreads();
-        const float m = red[0];
-        for (int i = tid; i < E; i += nt) score[i] = host_expf(__fsub_rn(lg[i], m));
-        __syncthreads();
-        if (warp == 0) {   // sum16 over E, then every score divided by it
-            float L = 0.0f;
-            if (lane < 16) {
+        for (int s = 16; s >= 1; s >>= 1) m = fmaxf(m, __shfl_xor_sync(0xffffffffu, m, s));
+        if (lg[0] != lg[0]) m = lg[0];
+        for (int i = lane; i < E; i += 32) score[i] = host_expf(__fsub_rn(lg[i], m));
+        __syncwarp();
+        float L = 0.0f;   // sum16 (NUMERICS §1)
+        if (lane < 16) {
 #pragma unroll 8
-                for (int i = lane; i < E; i += 16) L = __fadd_rn(L, score[i]);
-            }
-            L = tree16(L, 0xffffffffu);
-            if (lane == 0) red[1] = L;
+            for (int i = lane; i < E; i += 16) L = __fadd_rn(L, score[i]);
         }
-        __syncthreads();
-        const float ssum = red[1];
-        for (int i = tid; i < E; i += nt) score[i] = __fdiv_rn(score[i], ssum);
+        L = tree16(L, 0xffffffffu);
+        const float ssum = __shfl_sync(0xffffffffu, L, 0);
+        for (int i = lane; i < E; i += 32) score[i] = __fdiv_rn(score[i], ssum);
     } else {
-        for (int i = tid; i < E; i += nt) score[i] = sigmoid_c(lg[i]);
+        for (int i = lane; i < E; i += 32) score[i] = sigmoid_c(lg[i]);
     }
-    __syncthreads();
-    for (int i = tid; i < E; i += nt) sel[i] = (R.score_bias && bias) ? __fadd_rn(score[i], bias[i]) : score[i];
-    __syncthreads();
+    __syncwarp();
+    for (int i = lane; i < E; i += 32) sel[i] = (R.score_bias && bias) ? __fadd_rn(score[i], __ldg(bias + i)) : score[i];
+    __syncwarp();
     if (R.n_group > 1) {
         const int ng = R.n_group, gs = E / ng;
-        for (int g = tid; g < ng; g += nt) {   // group score: sum of the group's top-2 (model.c:801-812)
-            const float *v = sel + g * gs;
+        if (lane < ng) {   // group score: sum of the group's top-2 (model.c:801-812)
+            const float *v = sel + lane * gs;
             int i1 = 0, i2 = -1;
             for (int i = 1; i < gs; i++) {
                 if (ranks_before(v[i], i, v[i1], i1)) {
@@ -252,56 +244,142 @@ __device__ __forceinline__ void route_token_cta(const RouteCfg &R, const float *
                     i2 = i;
                 }
             }
-            gsc[g] = i2 >= 0 ? __fadd_rn(v[i1], v[i2]) : v[i1];
+            gsc[lane] = i2 >= 0 ? __fadd_rn(v[i1], v[i2]) : v[i1];
         }
-        __syncthreads();
-        for (int g = tid; g < ng; g += nt) {   // keep the topk_group best groups
+        __syncwarp();
+        if (lane < ng) {   // keep the topk_group best groups
             int rk = 0;
-            for (int o = 0; o < ng; o++) rk += ranks_before(gsc[o], o, gsc[g], g) ? 1 : 0;
-            keep[g] = rk < R.topk_group;
+            for (int o = 0; o < ng; o++) rk += ranks_before(gsc[o], o, gsc[lane], lane) ? 1 : 0;
+            keep[lane] = rk < R.topk_group;
         }
-        __syncthreads();
-        for (int i = tid; i < E; i += nt)
+        __syncwarp();
+        for (int i = lane; i < E; i += 32)
             if (!keep[i / gs]) sel[i] = 0.0f;
-        __syncthreads();
+        __syncwarp();
     }
-    // rank of each expert by a 64-bit key with the order of ranks_before: order-preserving bits of
-    // the value (NaN lowest, -0 counted as +0), then the lower index first
-    for (int i = tid; i < E; i += nt) key[i] = rank_key(sel[i], i);
-    __syncthreads();
-    {
-        int P = 1;   // lanes per expert (a power of two <= 32 with E * P <= threads)
-        while (P < 32 && E * (P * 2) <= nt) P *= 2;
-        const int per = (E + P - 1) / P;
-        for (int base = 0; base < E * P; base += nt) {
-            const int t = base + tid, i = t / P, part = t - i * P;
-            int rk = 0;
-            unsigned long long ki = 0;
-            if (i < E) {
-                ki = key[i];
-                const int o0 = part * per, o1 = min(E, o0 + per);
-#pragma unroll 8
-                for (int o = o0; o < o1; o++) rk += key[o] > ki ? 1 : 0;
+    for (int i = lane; i < E; i += 32) key[i] = rank_key(sel[i], i);
+    __syncwarp();
+    for (int i0 = 0; i0 < E; i0 += 128) {   // up to 4 of this lane's experts ranked per sweep
+        unsigned long long k4[4];
+        int r4[4] = {0, 0, 0, 0};
+#pragma unroll
+        for (int t = 0; t < 4; t++) {
+            const int i = i0 + t * 32 + lane;
+            k4[t] = i < E ? key[i] : ~0ull;
+        }
+#pragma unroll 4
+        for (int o = 0; o < E; o++) {
+            const unsigned long long ko = key[o];
+#pragma unroll
+            for (int t = 0; t < 4; t++) r4[t] += ko > k4[t] ? 1 : 0;
+        }
+#pragma unroll
+        for (int t = 0; t < 4; t++) {
+            const int i = i0 + t * 32 + lane;
+            if (i < E && r4[t] < K) ids[r4[t]] = i;
+        }
+    }
+    __syncwarp();
+    // route_weights (model.c:833-843): rank-order renormalisation sum, division, routed_scale
+    float wj = lane < K ? score[ids[lane]] : 0.0f;
+    float sacc = 0.0f;
+    for (int j = 0; j < K; j++) sacc = __fadd_rn(sacc, __shfl_sync(0xffffffffu, wj, j));
+    const float den = __fadd_rn(sacc, 1e-20f);
+    if (lane < K) {
+        if (R.norm_topk_prob) wj = __fdiv_rn(wj, den);
+        w[lane] = __fmul_rn(wj, R.routed_scale);
+    }
+    __syncwarp();
+}
+
+// Top-k routing of one token by a whole CTA, for E <= 128 without expert groups. Warp 0 computes
+// the scores (lane l holds experts l, l+32, l+64, l+96) and writes them with their sort keys to
+// shared memory; after one block barrier every thread takes one (expert i, quarter q) pair and counts
+// the keys of quarter q above key(i), four lanes add their counts (rank(i) = #{o : key(o) > key(i)}),
+// and the experts of rank < K are route_select's ids in order; after a second barrier warp 0 forms
+// the weights. One warp for the scores keeps the double-precision exp work off the other warps.
+// score_s [E] and key_s [4 * ceil(E/4)] are shared scratch; key(o) for o = q * ceil(E/4) + k lives at
+// key_s[4k + q] so that the four quarters read by a warp fall in different banks. Results ids / w
+// (shared); every thread of the CTA must call it.
+// kSharedLogits: the logits are in shared memory (plain loads) rather than global (L2 loads).
+template <bool kSharedLogits = false>
+__device__ __forceinline__ void route_token_cta_small(const RouteCfg &R, const float *logit_g, const float *bias,
+                                                      float *score_s, unsigned long long *key_s, int *ids,
+                                                      float *w) {
+    const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+    const int E = R.E, K = R.K, Q = (E + 3) >> 2;
+    if (warp == 0) {
+        float x[4], sc[4];
+#pragma unroll
+        for (int t = 0; t < 4; t++)
+            x[t] = (t * 32 + lane < E) ? (kSharedLogits ? logit_g[t * 32 + lane] : __ldcg(logit_g + t * 32 + lane))
+                                       : 0.0f;
+        if (R.score_fn == SCORE_SOFTMAX) {
+            float m = -__uint_as_float(0x7f800000u);   // m = x[0]; m = x[i] > m ? x[i] : m
+#pragma unroll
+            for (int t = 0; t < 4; t++)
+                if (t * 32 + lane < E) m = fmaxf(m, x[t]);
+#pragma unroll
+            for (int s = 16; s >= 1; s >>= 1) m = fmaxf(m, __shfl_xor_sync(0xffffffffu, m, s));
+            const float x0 = __shfl_sync(0xffffffffu, x[0], 0);
+            if (x0 != x0) m = x0;
+            float e[4];
+#pragma unroll
+            for (int t = 0; t < 4; t++) e[t] = (t * 32 + lane < E) ? host_expf(__fsub_rn(x[t], m)) : 0.0f;
+            // sum16: lane j < 16 adds e[j], e[j+16], e[j+32], ... in order; e[i] lives in lane i%32,
+            // slot i/32, so the sequence alternates this lane's slot t and lane j+16's slot t (absent
+            // elements are +0.0f, which leaves a sum of non-negative terms unchanged)
+            float L = 0.0f;
+#pragma unroll
+            for (int t = 0; t < 4; t++) {
+                const float other = __shfl_down_sync(0xffffffffu, e[t], 16);
+                L = __fadd_rn(L, e[t]);
+                L = __fadd_rn(L, other);
             }
-            for (int s = 1; s < P; s <<= 1) rk += __shfl_xor_sync(0xffffffffu, rk, s, P);
-            if (i < E && part == 0 && rk < K) ids[rk] = i;
+            L = tree16(L, 0xffffffffu);
+            const float ssum = __shfl_sync(0xffffffffu, L, 0);
+#pragma unroll
+            for (int t = 0; t < 4; t++) sc[t] = __fdiv_rn(e[t], ssum);
+        } else {
+#pragma unroll
+            for (int t = 0; t < 4; t++) sc[t] = sigmoid_c(x[t]);
+        }
+#pragma unroll
+        for (int t = 0; t < 4; t++) {
+            const int i = t * 32 + lane;
+            if (i < 4 * Q) {   // slots past E hold key 0, which ranks after every real expert
+                const float sv = (R.score_bias && bias && i < E) ? __fadd_rn(sc[t], __ldg(bias + i)) : sc[t];
+                const int q = i / Q, k = i - q * Q;
+                key_s[4 * k + q] = i < E ? rank_key(sv, i) : 0ull;
+                if (i < E) score_s[i] = sc[t];
+            }
         }
     }
     __syncthreads();
-    // route_weights (model.c:833-843): the renormalisation sum runs in rank order on one thread,
-    // the divisions and routed_scale on K threads
-    if (tid == 0) {
+    for (int p0 = 0; p0 < 4 * Q; p0 += blockDim.x) {   // warp-uniform trip count (shuffles below)
+        const int p = p0 + (int)threadIdx.x, i = p >> 2, q = p & 3;
+        int cnt = 0;
+        if (i < E) {
+            const int qi = i / Q, ki_ = i - qi * Q;
+            const unsigned long long ki = key_s[4 * ki_ + qi];
+            for (int k = 0; k < Q; k++) cnt += key_s[4 * k + q] > ki ? 1 : 0;
+        }
+        cnt += __shfl_xor_sync(0xffffffffu, cnt, 1);
+        cnt += __shfl_xor_sync(0xffffffffu, cnt, 2);
+        if (i < E && q == 0 && cnt < K) ids[cnt] = i;
+    }
+    __syncthreads();
+    if (warp == 0) {   // route_weights (model.c:833-843)
+        float wj = lane < K ? score_s[ids[lane]] : 0.0f;
         float sacc = 0.0f;
-        for (int j = 0; j < K; j++) sacc = __fadd_rn(sacc, score[ids[j]]);
-        red[2] = __fadd_rn(sacc, 1e-20f);
+        for (int j = 0; j < K; j++) sacc = __fadd_rn(sacc, __shfl_sync(0xffffffffu, wj, j));
+        const float den = __fadd_rn(sacc, 1e-20f);
+        if (lane < K) {
+            if (R.norm_topk_prob) wj = __fdiv_rn(wj, den);
+            w[lane] = __fmul_rn(wj, R.routed_scale);
+        }
+        __syncwarp();
     }
-    __syncthreads();
-    if (tid < K) {
-        float v = score[ids[tid]];
-        if (R.norm_topk_prob) v = __fdiv_rn(v, red[2]);
-        w[tid] = __fmul_rn(v, R.routed_scale);
-    }
-    __syncthreads();
 }
 
 }  // namespace hx

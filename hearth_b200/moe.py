@@ -104,6 +104,11 @@ class MoeBackend:
         """Waits for the stream of the *_dev calls and raises on a device-side error."""
         check(lib().hxb_moe_sync(self.h, C.c_void_p(stream or 0)), "hxb_moe_sync")
 
+    def decode_path(self) -> str:
+        """Kernel of a single-token forward over every layer: "layers" (per-phase kernels) or
+        "persistent" (one launch for all layers)."""
+        return ("layers", "persistent")[lib().hxb_moe_decode_path(self.h)]
+
     def profile(self, T: int = 1, iters: int = 3) -> list:
         """Average device microseconds per stage of one layer: [norm+act, router, gate/up, down]."""
         us = (C.c_double * 4)()

@@ -157,6 +157,11 @@ HXB_API int hxb_moe_profile(hxb_moe *m, int T, int iters, double *us);
  * router, barrier 1, routing, gate/up, mid blocks, barrier 2, down, sum, barrier 3). Returns the
  * number of values (call with out = NULL to size the buffer), 0 when not tracing. */
 HXB_API int64_t hxb_moe_phase_trace(hxb_moe *m, uint64_t *out, int64_t max_values);
+/* Which kernel evaluates a single-token forward over every layer (every expert resident):
+ * 0 per-phase kernels (one launch per phase and layer), 1 the persistent decode kernel (one launch
+ * for all layers). Chosen at open from the shape; the environment variable HXB_PERSISTENT=0 forces
+ * 0. No counterpart in the reference (one CPU path). */
+HXB_API int hxb_moe_decode_path(const hxb_moe *m);
 /* Routing of the last evaluated layer: ids / weights [T, K] (host). */
 HXB_API int hxb_moe_last_routing(hxb_moe *m, int *ids, float *weights, int T);
 

@@ -152,56 +152,67 @@ def test_heat_profile_pins(gpu):
 
 
 def _persistent_pair(seed, **kw):
-    """Shapes the persistent decode kernel takes (gate/up rows a multiple of 16 bytes)."""
+    """Shapes the persistent decode kernels take (gate/up rows a multiple of 16 bytes)."""
     return build_pair(seed, **kw)
 
 
-@pytest.mark.parametrize("case", ["softmax", "sigmoid_group", "nonorm"])
+@pytest.mark.parametrize("case", ["softmax", "sigmoid_group", "nonorm", "sigmoid_bias"])
 def test_persistent_decode_equals_oracle(gpu, case):
     kw = dict(L=3, D=512, F=256, E=32, K=4, max_tokens=4, residual_scale=0.7)
     if case == "sigmoid_group":
         kw.update(score_fn=1, score_bias=1, n_group=4, topk_group=2, routed_scale=2.5)
     if case == "nonorm":
         kw.update(norm=0, K=6)
+    if case == "sigmoid_bias":
+        kw.update(score_fn=1, score_bias=1, E=48, K=5, routed_scale=1.5)
     model, be = _persistent_pair(31, **kw)
     with be:
+        assert be.decode_path() == "persistent"
         rng = np.random.default_rng(4)
         for _ in range(3):
             h = rng.standard_normal((1, 512)).astype(np.float32)
             hg = be.forward(h)
             assert np.array_equal(bits(hg), bits(model.forward(h)))
         ids, w = be.last_routing(1)
-    # the routing reported is the last layer's
-    x = np.zeros((1, 512), np.float32)
     assert ids.shape == (1, kw["K"])
 
 
 def test_persistent_decode_qwen3_shape_matches_multi_kernel_path(gpu, monkeypatch):
     """Qwen3-30B-A3B layer shape (D 2048, F 768, 128 experts, top-8), 2 layers: the persistent kernel,
-    the multi-kernel path and the oracle agree bit for bit."""
+    the multi-kernel path and the oracle agree bit for bit, and so does the last layer's routing."""
     model, be = build_pair(41, L=2, D=2048, F=768, E=128, K=8, max_tokens=1, router_sigma=0.02)
     rng = np.random.default_rng(5)
     hs = [rng.standard_normal((1, 2048)).astype(np.float32) for _ in range(3)]
     with be:
-        got = [be.forward(h) for h in hs]
+        assert be.decode_path() == "persistent"
+        got = []
+        for h in hs:
+            got.append(be.forward(h))
+            ids, w = be.last_routing(1)
         stats = be.stats()
     monkeypatch.setenv("HXB_PERSISTENT", "0")
     model2, be2 = build_pair(41, L=2, D=2048, F=768, E=128, K=8, max_tokens=1, router_sigma=0.02)
     with be2:
-        got2 = [be2.forward(h) for h in hs]
+        assert be2.decode_path() == "layers"
+        got2 = []
+        for h in hs:
+            got2.append(be2.forward(h))
+            ids2, w2 = be2.last_routing(1)
     for h, a, b in zip(hs, got, got2):
         want = model.forward(h)
         assert np.array_equal(bits(a), bits(want))
         assert np.array_equal(bits(b), bits(want))
+    assert np.array_equal(ids, ids2) and np.array_equal(bits(w), bits(w2))
     assert stats["expert_uses"] == 3 * 2 * 8
 
 
 def test_persistent_decode_device_api_repeats(gpu):
-    """forward_dev on a device buffer, many launches back to back (barrier word and arrival
-    counters carry over between launches), then one sync."""
+    """forward_dev on a device buffer, many launches back to back (the barrier counter carries
+    over between launches), then one sync."""
     import torch
     model, be = build_pair(43, L=2, D=512, F=256, E=32, K=4, max_tokens=1)
     with be:
+        assert be.decode_path() == "persistent"
         rng = np.random.default_rng(6)
         h0 = rng.standard_normal((1, 512)).astype(np.float32)
         d = torch.from_numpy(h0.copy()).cuda()
