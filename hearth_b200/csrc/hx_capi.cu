@@ -234,8 +234,8 @@ struct hxb_moe {
     int last_T = 0;
     // persistent single-token decode kernel (every expert resident)
     bool use_decode = false, dec_dirty = true;
-    DevBuf dec_router, dec_norm, dec_bias, dec_mbuf, dec_cnt, dec_bar;
-    unsigned dec_bars = 0;               // barriers completed by earlier persistent launches
+    DevBuf dec_router, dec_norm, dec_bias;
+    DevBuf dec_xbuf, dec_epoch;          // exchange buffers (two sets) and the launch counter
     DevBuf dec_trace;                    // phase timeline of the last launch (HXB_TRACE=1)
 
     MoeScratch scratch() const {
@@ -417,11 +417,11 @@ extern "C" HXB_API hxb_moe *hxb_moe_open(const hxb_moe_config *c, char *err, siz
         m->use_decode = !off &&
                         decode_supported(D, k.expert_ffn_dim, E, K, k.expert_dtype, k.shared_ffn_dim > 0, &why_not);
         if (m->use_decode) {
-            const size_t nb = (size_t)L * K * (k.expert_ffn_dim / QK);
+            const size_t xb = sizeof(float) * (size_t)decode_xbuf_floats(L, D, k.expert_ffn_dim, E, K);
             if (!m->dec_router.alloc(sizeof(void *) * (size_t)L) || !m->dec_norm.alloc(sizeof(void *) * (size_t)L) ||
-                !m->dec_bias.alloc(sizeof(void *) * (size_t)L) ||
-                !m->dec_mbuf.alloc(sizeof(float) * (size_t)K * k.expert_ffn_dim) ||
-                !m->dec_cnt.alloc(sizeof(unsigned) * nb) || !m->dec_bar.alloc(16 * 128) ||
+                !m->dec_bias.alloc(sizeof(void *) * (size_t)L) || !m->dec_xbuf.alloc(xb) || !m->dec_epoch.alloc(64) ||
+                !cuda_ok(cudaMemset(m->dec_xbuf.p, 0xff, xb), "decode buffers") ||
+                !cuda_ok(cudaMemset(m->dec_epoch.p, 0, 64), "decode buffers") ||
                 !cuda_ok(init_decode_attributes(), "decode attributes")) {
                 set_errbuf(err, errlen, "hxb_moe_open: persistent decode setup failed: " + g_err);
                 return nullptr;
@@ -683,27 +683,24 @@ static cudaError_t enqueue_decode(hxb_moe *m, float *h, int l0, int nl, cudaStre
     p.bias = m->dec_bias.as<const float *>() + l0;
     p.slab = m->table.as<const uint8_t *>() + (size_t)l0 * k.n_experts;
     p.h = h;
-    p.logits = m->logits.as<float>();
-    p.mbuf = m->dec_mbuf.as<float>();
-    p.act_mid = m->act_mid.as<act_q8>();
-    p.bar = m->dec_bar.as<unsigned>();
-    p.bar_base = m->dec_bars;
-    m->dec_bars += 3u * (unsigned)nl;
-    p.blk_cnt = m->dec_cnt.as<unsigned>();
+    p.xbuf = m->dec_xbuf.as<float>();
+    p.buf_layers = k.n_layers;
+    p.epoch = m->dec_epoch.as<unsigned>();
     p.err = m->err.as<int>();
     p.ids_out = m->ids.as<int>();
     p.w_out = m->wts.as<float>();
     p.trace = m->dec_trace.as<unsigned long long>();
+    p.prefetch = true;
+    p.slab_used = (m->lay.end + 15) / 16 * 16;
     return launch_moe_decode(p, s);
 }
 
-// After a device error the persistent kernel's barrier word and arrival counters may be mid-way.
+// After a device error the persistent kernel's exchange buffers may hold values of the failed launch.
 static void reset_decode_state(hxb_moe *m) {
     if (!m->use_decode) return;
     cudaDeviceSynchronize();
-    cudaMemset(m->dec_bar.p, 0, m->dec_bar.n);
-    cudaMemset(m->dec_cnt.p, 0, m->dec_cnt.n);
-    m->dec_bars = 0;
+    cudaMemset(m->dec_xbuf.p, 0xff, m->dec_xbuf.n);
+    cudaMemset(m->dec_epoch.p, 0, m->dec_epoch.n);
 }
 
 static int run_range(hxb_moe *m, float *h, float *out, int T, int l0, int nl, bool with_norm, bool resid,

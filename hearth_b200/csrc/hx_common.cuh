@@ -256,6 +256,64 @@ __device__ __forceinline__ uint32_t load_q8_block(const uint8_t *blk, uint32_t q
     return scale;
 }
 
+// Shared-memory block loaders: one aligned word per 4 bytes from the word that holds the block's
+// first byte, the block bytes picked out with byte permutes (no branch on the block's 2-byte
+// alignment). When the block starts on a word boundary the last word read extends 2 bytes past the
+// block, so these are only for tiles in shared memory with readable bytes after them.
+__device__ __forceinline__ uint32_t load_q4_block_pad(const uint8_t *blk, uint32_t nib[8]) {
+    const uintptr_t a = reinterpret_cast<uintptr_t>(blk);
+    const uint32_t o = (uint32_t)(a & 2u);
+    const uint32_t sel = o ? 0x7654u : 0x5432u;
+    const uint32_t *w = reinterpret_cast<const uint32_t *>(a & ~uintptr_t(3));
+    uint32_t v[9];
+#pragma unroll
+    for (int i = 0; i < 9; i++) v[i] = w[i];
+#pragma unroll
+    for (int k = 0; k < 8; k++) nib[k] = __byte_perm(v[k], v[k + 1], sel);
+    return (v[0] >> (o * 8u)) & 0xffffu;
+}
+
+__device__ __forceinline__ uint32_t load_q8_block_pad(const uint8_t *blk, uint32_t q[16]) {
+    const uintptr_t a = reinterpret_cast<uintptr_t>(blk);
+    const uint32_t o = (uint32_t)(a & 2u);
+    const uint32_t sel = o ? 0x7654u : 0x5432u;
+    const uint32_t *w = reinterpret_cast<const uint32_t *>(a & ~uintptr_t(3));
+    uint32_t v[17];
+#pragma unroll
+    for (int i = 0; i < 17; i++) v[i] = w[i];
+#pragma unroll
+    for (int k = 0; k < 16; k++) q[k] = __byte_perm(v[k], v[k + 1], sel);
+    return (v[0] >> (o * 8u)) & 0xffffu;
+}
+
+// dp4a with unsigned bytes in a and signed bytes in b.
+__device__ __forceinline__ int dp4a_us(uint32_t a, int b, int c) {
+    int d;
+    asm("dp4a.u32.s32 %0, %1, %2, %3;" : "=r"(d) : "r"(a), "r"(b), "r"(c));
+    return d;
+}
+
+// q4_isum with the high nibbles left in place: (nib & 0xf0f0f0f0) . aq = 16 * sum(hi * aq), an
+// exact multiple of 16, so an arithmetic shift recovers the sum (one fewer operation per word).
+__device__ __forceinline__ int q4_isum_hi(const uint32_t nib[8], const int32_t aq[16], int32_t asum) {
+    int a0 = 0, a1 = 0;
+#pragma unroll
+    for (int k = 0; k < 8; k++) {
+        a0 = __dp4a((int)(nib[k] & 0x0f0f0f0fu), aq[k], a0);
+        a1 = dp4a_us(nib[k] & 0xf0f0f0f0u, aq[8 + k], a1);
+    }
+    return a0 + (a1 >> 4) - 8 * asum;
+}
+
+// Hardware f16 -> f32: exact for every finite value and infinity; a NaN keeps NaN-ness but not
+// necessarily its payload, so this is for products whose sums are canonicalised (canon()) before
+// they are stored, never for dequantized values.
+__device__ __forceinline__ float f16_to_f32_hw(uint32_t h) {
+    float f;
+    asm("cvt.f32.f16 %0, %1;" : "=f"(f) : "h"((unsigned short)h));
+    return f;
+}
+
 // The product term of NUMERICS §3 for one block: (float)isum * (dw * dx), rounded per op.
 __device__ __forceinline__ float block_term(int isum, uint32_t dw_bits, float dx) {
     return __fmul_rn(__int2float_rn(isum), __fmul_rn(f16_to_f32(dw_bits), dx));

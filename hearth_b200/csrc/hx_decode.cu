@@ -1,96 +1,157 @@
-// hx_decode.cu — the persistent single-token decode kernel of the MoE stack.
+// hx_decode.cu — single-token decode of a whole MoE stack in one persistent launch.
 //
-// One cooperative launch evaluates every layer of the stack for one token, with one CTA per SM.
-// Per layer (engine/src/model.c:1209-1214 FFN half of forward, 986-1131 moe_layer):
-//   A  every CTA: x = rmsnorm(h, ffn_norm) (redundantly), the activation blocks of x, and its share
-//      of the F32 router rows (dot16);                                   grid barrier
-//   B  every CTA: softmax/sigmoid top-k routing of the 128 logits (redundantly), then it bulk-copies
-//      its contiguous share of the K experts' gate/up rows AND its share of the down rows into
-//      shared memory at once, computes gate/up, SwiGLU, and the mid activation block of every
-//      64-row block it completes (per-block arrival counters);          grid barrier
-//   C  every CTA: its down rows of all K experts, the rank-order weighted sum and h += rs * sum for
-//      those rows;                                                       grid barrier
-// The router rows and ffn_norm of layer l+1 are copied in while layer l runs.
-// Every float result follows the canonical order of the reference's NUMERICS §1-§5, exactly as the
-// multi-kernel path does (same device routines).
+// One cooperative launch of one 512-thread CTA per SM evaluates every layer of the range for one
+// token: rmsnorm, router, routing, Q4/Q8 gate/up + SwiGLU, mid activation blocks, down, rank-order
+// sum and residual (engine/src/model.c:1203-1214 with moe_layer, model.c:857-930), each float
+// result in the reference's canonical order (NUMERICS §1-§5), bit-identical to the per-phase kernels.
 //
-// Grid barriers are sense-reversing arrival counters in global memory with bounded spins; a wait
-// that runs out records an error in the device error word and lets the CTA continue, so a fault of
-// the protocol ends the launch with an error status instead of a hang.
+// The CTAs hand data to one another through exchange buffers in global memory whose words are their
+// own readiness flags: every slot holds kEmpty (0xffffffff, a NaN bit pattern no canonicalised value
+// has) until its producer stores the value, and a consumer polls exactly the words it needs. There
+// is no grid barrier, no atomic and no fence on the data path. Per layer l:
+//   P1  every CTA: h_l (layer 0: the input; later: polled from xh[l]), rmsnorm, x, activation
+//       blocks; CTA c computes router row c (dot16) -> xlg[l][c], and a predicted logit of the next
+//       layer's router -> xpr[l][c] (steers the L2 prefetch only);
+//   P2  every CTA: polls the E logits, routes the token (identical everywhere), issues the bulk
+//       copies of its gate/up chunks and of its down rows;
+//   P3  CTA c: gate/up chunks [c*NCH/G, (c+1)*NCH/G) of the K x F/4 four-row-pair chunks (warp q
+//       takes chunk q as soon as it lands), SwiGLU -> xmid[l][j][f]; the issuing warp then predicts
+//       the next layer's experts and issues L2 prefetches of this CTA's share of their slabs;
+//   P4  CTA c belongs to the down group of rank j = c*K/G: polls expert j's F mid values, forms its
+//       F/64 activation blocks (NUMERICS §2), computes its slice of expert j's down rows -> xy[l][j][d];
+//   P5  CTA c owns h rows [c*D/G, (c+1)*D/G): polls y of the K experts for them, rank-order sum,
+//       residual -> xh[l+1][d] (the last layer: the output h).
+// Exchange slots are written once per launch. Two sets alternate by a launch counter kept in device
+// memory; each launch resets the set the previous launch used (spread over its layers), so the next
+// launch finds it empty — no end-of-launch barrier, and the launch can be captured in a CUDA graph.
+// Every poll and every mbarrier wait is bounded: on expiry it records an error word and moves on.
 #include "hx_device.cuh"
 #include "hx_kernels.h"
 #include "hx_route.cuh"
 
-#include <algorithm>
 #include <string>
 
 namespace hx {
 
-enum : int { DEV_E_BARRIER = 4 };
-constexpr uint32_t kBarrierSpinLimit = 1u << 21;
 constexpr int DEC_THREADS = 512;
 constexpr int DEC_WARPS = DEC_THREADS / 32;
-constexpr int DEC_CH = 4;          // gate/up row pairs per chunk (one bulk-copy group)
+constexpr int DEC_CH = 4;          // gate/up row pairs per chunk (one mbarrier, two bulk copies)
 constexpr int DEC_PROWS = 8;       // rows per warp_rows_1tok call (P buffer rows)
 constexpr int DEC_MAXL = 128;      // layers per launch (router / norm / bias pointer tables in smem)
+constexpr int DEC_MAXCH = 26;      // gate/up chunks per CTA (mbarriers 0..25)
 constexpr int BAR_DOWN = 28, BAR_ROUTER = 29;
+constexpr int kIssueWarp = DEC_WARPS - 1;   // issues the bulk copies and the prefetch of a layer
+constexpr uint32_t kEmpty = 0xffffffffu;
+constexpr uint32_t kPollLimit = 1u << 18;   // polls of one word before giving up (~30 ms)
+enum : int { DEV_E_POLL = 4 };             // an exchange word never arrived
+
 // Phase stamps of the optional timeline (thread 0 of every CTA, per layer).
-enum : int { ST_START, ST_NORM, ST_ROUTER, ST_BAR1, ST_ROUTE, ST_GATEUP, ST_MID, ST_BAR2, ST_DOWN, ST_SUM, ST_BAR3,
+enum : int { ST_START, ST_H, ST_NORM, ST_ROUTER, ST_LG, ST_ROUTE, ST_GATEUP, ST_MID, ST_DOWN, ST_Y, ST_SUM,
              DEC_STAMPS };
 
-// Shared-memory carve-up of one CTA (identical on host and device). The router rows and ffn_norm
-// of a layer share the gate/up region: they are read in phase A and copied in after the previous
-// layer's gate/up rows were consumed.
+// Next-layer prefetch: each CTA c < E also computes router[l+1][c] . (h_l * rms(h_l) * ffn_norm[l+1])
+// in any summation order (it only steers the prefetch); an idle warp of every CTA takes the K
+// largest of these, and the CTAs issue cp.async.bulk.prefetch.L2 over those experts' slabs in
+// kPrefetchPiece pieces (piece i by CTA i mod G), early in the layer. A prefetch only moves data into
+// L2, so it cannot change any result.
+constexpr int kPredVec = 2;                 // float4 router / norm values per thread: D <= 4096
+constexpr uint32_t kPrefetchPiece = 32768;  // bytes per prefetch instruction
+
+// Work split of one launch (identical on host and device).
+struct DecodePlan {
+    int G, nch, ch_max;           // CTAs, gate/up chunks (K * F / 4), chunks per CTA at most
+    int ra, dr_max, hr_max;       // down-row alignment, down rows / CTA at most, h rows / CTA at most
+    int rpc;                      // router rows per CTA
+};
+
+HX_HD inline void chunk_range(int c, int G, int nch, int *c0, int *c1) {
+    *c0 = (int)((int64_t)nch * c / G);
+    *c1 = (int)((int64_t)nch * (c + 1) / G);
+}
+HX_HD inline int down_group(int c, int G, int K) { return (int)((int64_t)c * K / G); }
+HX_HD inline int group_first(int j, int G, int K) { return (int)(((int64_t)j * G + K - 1) / K); }
+// down rows [*r0, *r1) of CTA c: its group's CTAs split expert j's D rows in multiples of ra
+HX_HD inline void down_rows(int c, int G, int K, int D, int ra, int *r0, int *r1) {
+    const int j = down_group(c, G, K), g0 = group_first(j, G, K), g1 = group_first(j + 1, G, K);
+    const int n = g1 - g0, r = c - g0;
+    *r0 = (int)((int64_t)D * r / n) / ra * ra;
+    *r1 = r + 1 == n ? D : (int)((int64_t)D * (r + 1) / n) / ra * ra;
+}
+HX_HD inline void h_rows(int c, int G, int D, int *r0, int *r1) {
+    *r0 = (int)((int64_t)D * c / G);
+    *r1 = (int)((int64_t)D * (c + 1) / G);
+}
+
+HX_HD inline DecodePlan decode_plan(int G, int D, int F, int E, int K, int dtype) {
+    DecodePlan P{};
+    P.G = G;
+    P.nch = K * F / DEC_CH;
+    P.ch_max = (P.nch + G - 1) / G;
+    const int64_t rbF = row_bytes(dtype, F);
+    P.ra = 1;
+    while ((P.ra * rbF) % 16) P.ra++;
+    const int nmin = G / K;   // smallest down group
+    P.dr_max = (D + nmin - 1) / nmin + P.ra;
+    P.hr_max = (D + G - 1) / G + 1;
+    P.rpc = (E + G - 1) / G;
+    return P;
+}
+
+// Shared-memory carve-up of one CTA (identical on host and device).
 struct DecodeLayout {
-    int G, R, rpc, units;              // CTAs, down rows / CTA, router rows / CTA, gate/up units (64-row blocks)
+    DecodePlan plan;
     int nbD, nbF;
     int64_t rbD, rbF;
-    size_t off_hs, off_stab, off_xact, off_gu, off_rrow, off_norm, off_dn, off_amid, off_y, off_p, off_gout,
-        off_mloc, off_lg, off_score, off_sel, off_key, off_gsc, off_keep, off_ids, off_w, off_ptrs, total;
+    size_t off_hs, off_xs, off_xact, off_stab, off_rrow, off_norm, off_gu, off_dn, off_mid, off_amid, off_y, off_p,
+        off_gout, off_lg, off_pr, off_score, off_sel, off_key, off_gsc, off_keep, off_ids, off_w, off_yv, off_ptrs,
+        total;
 };
 
 HX_HD inline size_t align16(size_t v) { return (v + 15) & ~size_t(15); }
 
 HX_HD inline DecodeLayout decode_layout(int G, int D, int F, int E, int K, int dtype) {
     DecodeLayout L{};
-    L.G = G;
+    L.plan = decode_plan(G, D, F, E, K, dtype);
     L.nbD = D / QK;
     L.nbF = F / QK;
     L.rbD = row_bytes(dtype, D);
     L.rbF = row_bytes(dtype, F);
-    // down rows per CTA: R * rbF must be a multiple of 16 bytes for the bulk copies
-    int ra = 1;
-    while ((ra * L.rbF) % 16) ra++;
-    L.R = (D + G - 1) / G;
-    L.R = (L.R + ra - 1) / ra * ra;
-    L.rpc = (E + G - 1) / G;
-    L.units = K * L.nbF;
+    const DecodePlan &P = L.plan;
+    const int Ek = E > 128 ? E : 128;
     size_t o = 512;   // mbarriers
     L.off_hs = o; o = align16(o + (size_t)D * 4);
-    L.off_stab = o; o = align16(o + (size_t)E * 8);
+    L.off_xs = o; o = align16(o + (size_t)D * 4);
     L.off_xact = o; o = align16(o + (size_t)L.nbD * ACT_BLOCK);
-    L.off_gu = o;
-    const size_t gu_bytes = (size_t)QK * 2 * L.rbD, rr_bytes = (size_t)(L.rpc + 1) * D * 4;
-    L.off_rrow = o;
-    L.off_norm = o + (size_t)L.rpc * D * 4;
-    o = align16(o + (gu_bytes > rr_bytes ? gu_bytes : rr_bytes));
-    L.off_dn = o; o = align16(o + (size_t)K * L.R * L.rbF);
-    L.off_amid = o; o = align16(o + (size_t)K * L.nbF * ACT_BLOCK);
-    L.off_y = o; o = align16(o + (size_t)K * L.R * 4);
+    L.off_stab = o; o = align16(o + (size_t)E * 8);
+    L.off_rrow = o; o = align16(o + (size_t)P.rpc * D * 4);
+    L.off_norm = o; o = align16(o + (size_t)D * 4);
+    // tiles keep 16 readable bytes after them (the padded block loaders read up to 2 past a block)
+    L.off_gu = o; o = align16(o + (size_t)P.ch_max * 2 * DEC_CH * L.rbD + 16);
+    L.off_dn = o; o = align16(o + (size_t)P.dr_max * L.rbF + 16);
+    L.off_mid = o; o = align16(o + (size_t)F * 4);
+    L.off_amid = o; o = align16(o + (size_t)L.nbF * ACT_BLOCK);
+    L.off_y = o; o = align16(o + (size_t)P.dr_max * 4);
     L.off_p = o; o = align16(o + (size_t)DEC_WARPS * DEC_PROWS * 33 * 4);
     L.off_gout = o; o = align16(o + (size_t)DEC_WARPS * DEC_PROWS * 4);
-    L.off_mloc = o; o = align16(o + (size_t)QK * 4);
-    L.off_lg = o; o = align16(o + (size_t)E * 4);
+    L.off_lg = o; o = align16(o + (size_t)Ek * 4);
+    L.off_pr = o; o = align16(o + (size_t)Ek * 4);
     L.off_score = o; o = align16(o + (size_t)E * 4);
     L.off_sel = o; o = align16(o + (size_t)E * 4);
-    L.off_key = o; o = align16(o + (size_t)((E + 3) / 4 * 4) * 8);
+    L.off_key = o; o = align16(o + (size_t)Ek * 8);
     L.off_gsc = o; o = align16(o + 64 * 4);
     L.off_keep = o; o = align16(o + 64 * 4);
-    L.off_ids = o; o = align16(o + (size_t)K * 4);
-    L.off_w = o; o = align16(o + (size_t)K * 4);
+    L.off_ids = o; o = align16(o + 16 * 4);
+    L.off_w = o; o = align16(o + 16 * 4);
+    L.off_yv = o; o = align16(o + (size_t)K * P.hr_max * 4);
     L.off_ptrs = o; o = align16(o + (size_t)3 * DEC_MAXL * 8);
     L.total = o;
     return L;
+}
+
+// Exchange buffers of one set, in floats: xlg [Lb][E], xpr [Lb][E], xmid [Lb][K][F], xy [Lb][K][D],
+// xh [Lb][D] (Lb = buffer layers, at least the layers of any launch).
+HX_HD inline int64_t xset_floats(int Lb, int D, int F, int E, int K) {
+    return (int64_t)Lb * (2 * (int64_t)E + (int64_t)K * F + (int64_t)K * D + D);
 }
 
 struct DecodeArgs {
@@ -103,16 +164,15 @@ struct DecodeArgs {
     const float *const *bias;     // [Lyr] router bias [E] (null entries without score_bias)
     const uint8_t *const *slab;   // [Lyr * E]
     float *h;                     // [D] in / out
-    float *logits;                // [E]
-    float *mbuf;                  // [K, F] SwiGLU outputs
-    act_q8 *act_mid;              // [K, F/64]
-    unsigned *bar;                // [DEC_BAR_LINES * 32] barrier counters (zero at allocation)
-    unsigned bar_base;            // barriers completed by earlier launches (3 * layers per launch)
-    unsigned *blk_cnt;            // [Lyr, K, F/64] arrival counters (zero between launches)
+    float *xbuf;                  // two exchange sets of xset_floats(Lb, ...) floats, kEmpty at rest
+    int Lb;
+    unsigned *epoch;              // [2]: launch counter (set = epoch & 1), CTAs done with this launch
     int *err;
     int *ids_out;                 // [K] routing of the last layer
     float *w_out;
     unsigned long long *trace;    // null, or [Lyr][G][DEC_STAMPS] SM clock stamps of thread 0
+    bool predict;                 // next-layer prediction and prefetch
+    int64_t slab_used;            // bytes of a slab the kernels read (prefetch extent)
     DecodeLayout lay;
 };
 
@@ -122,56 +182,84 @@ __device__ __forceinline__ unsigned long long sm_clock() {
     return t;
 }
 
-__device__ __forceinline__ unsigned atom_add_release(unsigned *p, unsigned v) {
-    unsigned old;
-    asm volatile("atom.add.release.gpu.u32 %0, [%1], %2;" : "=r"(old) : "l"(p), "r"(v) : "memory");
-    return old;
+__device__ __forceinline__ void prefetch_l2(const void *p, uint32_t bytes) {
+    asm volatile("cp.async.bulk.prefetch.L2.global [%0], %1;" ::"l"(p), "r"(bytes) : "memory");
 }
 
-__device__ __forceinline__ unsigned ld_acquire(const unsigned *p) {
-    unsigned v;
-    asm volatile("ld.acquire.gpu.u32 %0, [%1];" : "=r"(v) : "l"(p) : "memory");
+__device__ __forceinline__ float ld_poll(const float *p) {
+    float v;
+    asm volatile("ld.relaxed.gpu.global.f32 %0, [%1];" : "=f"(v) : "l"(p) : "memory");
     return v;
 }
 
-// Grid barrier on one counter: after the block barrier, thread 0 adds 1 with a release reduction
-// (the block barrier orders the other threads' writes before it, so no separate fence), and lane 0..
-// of warp 0 poll with acquire loads until the counter reaches the target. The target grows by the
-// grid size with every barrier and across launches (the host passes each launch's first barrier
-// number), so nothing is ever reset; the 32-bit counts are compared wrap-safely. Counters spread
-// over several 128-byte lines measured slower than one on B200 (2482 vs 2290 cycles a barrier), so
-// DEC_BAR_LINES is 1; the code keeps the general form.
-constexpr int DEC_BAR_LINES = 1;
-
-__device__ __forceinline__ void red_release_add(unsigned *p, unsigned v) {
-    asm volatile("red.release.gpu.global.add.u32 [%0], %1;" ::"l"(p), "r"(v) : "memory");
+__device__ __forceinline__ float4 ld_poll4(const float *p) {
+    float4 v;
+    asm volatile("ld.relaxed.gpu.global.v4.f32 {%0, %1, %2, %3}, [%4];"
+                 : "=f"(v.x), "=f"(v.y), "=f"(v.z), "=f"(v.w)
+                 : "l"(p)
+                 : "memory");
+    return v;
 }
 
-__device__ __forceinline__ void grid_sync(unsigned *ctr, unsigned target, int *err) {
-    __syncthreads();
-    if (threadIdx.x < 32) {
-        const int lane = threadIdx.x;
-        if (lane == 0) red_release_add(ctr + (blockIdx.x % DEC_BAR_LINES) * 32, 1u);
-        for (uint32_t spins = 0;; spins++) {
-            const unsigned v = lane < DEC_BAR_LINES ? ld_acquire(ctr + lane * 32) : 0u;
-            const unsigned sum = __reduce_add_sync(0xffffffffu, v);
-            if ((int)(sum - target) >= 0) break;
-            if (spins > kBarrierSpinLimit || ((spins & 1023u) == 0 && *(volatile int *)err)) {
-                if (lane == 0) set_error(err, DEV_E_BARRIER);
-                break;
-            }
+__device__ __forceinline__ void st_x(float *p, float v) {
+    asm volatile("st.relaxed.gpu.global.f32 [%0], %1;" ::"l"(p), "f"(v) : "memory");
+}
+
+__device__ __forceinline__ bool empty_word(float v) { return __float_as_uint(v) == kEmpty; }
+
+// Polls one exchange word until it is filled (bounded; on expiry records an error and returns 0).
+__device__ __forceinline__ float poll1(const float *p, int *err) {
+    for (uint32_t spins = 0;; spins++) {
+        const float v = ld_poll(p);
+        if (!empty_word(v)) return v;
+        if (spins > kPollLimit || ((spins & 255u) == 255u && *(volatile int *)err)) {
+            set_error(err, DEV_E_POLL);
+            return 0.0f;
         }
+        __nanosleep(64);
     }
-    __syncthreads();
+}
+
+__device__ __forceinline__ float4 poll4(const float *p, int *err) {
+    for (uint32_t spins = 0;; spins++) {
+        const float4 v = ld_poll4(p);
+        if (!empty_word(v.x) && !empty_word(v.y) && !empty_word(v.z) && !empty_word(v.w)) return v;
+        if (spins > kPollLimit || ((spins & 255u) == 255u && *(volatile int *)err)) {
+            set_error(err, DEV_E_POLL);
+            return make_float4(0.0f, 0.0f, 0.0f, 0.0f);
+        }
+        __nanosleep(64);
+    }
+}
+
+// n consecutive exchange floats (n % 4 == 0, 16-byte aligned) -> shared dst, by the whole CTA.
+__device__ __forceinline__ void poll_vec(const float *src, float *dst, int n, int *err) {
+    for (int i = threadIdx.x * 4; i < n; i += DEC_THREADS * 4)
+        *reinterpret_cast<float4 *>(dst + i) = poll4(src + i, err);
 }
 
 // Rows [0, nr) of a tile whose rows are consecutive in shared memory, against one activation row
-// of nb blocks. out[k] = canonical NUMERICS §3 value of row k. nr <= DEC_PROWS.
+// of nb blocks. out[k] = canonical NUMERICS §3 value of row k. nr <= DEC_PROWS. The row loop is
+// unrolled to DEC_PROWS (predicated on nr) so that the rows' loads and dot chains overlap.
 template <int DT>
 __device__ __forceinline__ void warp_rows_1tok(const uint8_t *tile, int64_t rb, int nb, int nr, const act_q8 *act,
                                                float *P, float *out) {
     const int lane = threadIdx.x & 31;
     constexpr int BS = DT == Q4 ? Q4_BLOCK : Q8_BLOCK;
+    auto term = [&](const uint8_t *blk, const act_regs &ar) {
+        int isum;
+        uint32_t sc;
+        if constexpr (DT == Q4) {
+            uint32_t nib[8];
+            sc = load_q4_block_pad(blk, nib);
+            isum = q4_isum_hi(nib, ar.q, ar.sum);
+        } else {
+            uint32_t q[16];
+            sc = load_q8_block_pad(blk, q);
+            isum = q8_isum(q, ar.q);
+        }
+        return __fmul_rn(__int2float_rn(isum), __fmul_rn(f16_to_f32_hw(sc), ar.d));
+    };
     float acc = 0.0f;
     for (int g0 = 0; g0 < nb; g0 += 32) {
         const int gn = min(32, nb - g0);
@@ -179,39 +267,15 @@ __device__ __forceinline__ void warp_rows_1tok(const uint8_t *tile, int64_t rb, 
             act_regs ar;
             load_act(act + g0 + lane, ar);
             const uint8_t *col = tile + (int64_t)(g0 + lane) * BS;
-            for (int k = 0; k < nr; k++) {
-                const uint8_t *blk = col + (int64_t)k * rb;
-                int isum;
-                uint32_t sc;
-                if constexpr (DT == Q4) {
-                    uint32_t nib[8];
-                    sc = load_q4_block(blk, nib);
-                    isum = q4_isum(nib, ar.q, ar.sum);
-                } else {
-                    uint32_t q[16];
-                    sc = load_q8_block(blk, q);
-                    isum = q8_isum(q, ar.q);
-                }
-                P[k * 33 + lane] = __fmul_rn(__int2float_rn(isum), __fmul_rn(f16_to_f32(sc), ar.d));
-            }
+#pragma unroll
+            for (int k = 0; k < DEC_PROWS; k++)
+                if (k < nr) P[k * 33 + lane] = term(col + (int64_t)k * rb, ar);
         } else {
             for (int it = lane; it < nr * gn; it += 32) {
                 const int k = it / gn, g = it - k * gn;
-                const uint8_t *blk = tile + (int64_t)k * rb + (int64_t)(g0 + g) * BS;
                 act_regs ar;
                 load_act(act + g0 + g, ar);
-                int isum;
-                uint32_t sc;
-                if constexpr (DT == Q4) {
-                    uint32_t nib[8];
-                    sc = load_q4_block(blk, nib);
-                    isum = q4_isum(nib, ar.q, ar.sum);
-                } else {
-                    uint32_t q[16];
-                    sc = load_q8_block(blk, q);
-                    isum = q8_isum(q, ar.q);
-                }
-                P[k * 33 + g] = __fmul_rn(__int2float_rn(isum), __fmul_rn(f16_to_f32(sc), ar.d));
+                P[k * 33 + g] = term(tile + (int64_t)k * rb + (int64_t)(g0 + g) * BS, ar);
             }
         }
         __syncwarp();
@@ -226,26 +290,65 @@ __device__ __forceinline__ void warp_rows_1tok(const uint8_t *tile, int64_t rb, 
     __syncwarp();
 }
 
+// The K largest of E <= 128 values (one warp; any order among equal values): ids[0..K) of the
+// predicted experts (-1 when fewer than K are numbers). Each round takes the warp maximum of an
+// order-preserving 32-bit key.
+__device__ __forceinline__ void warp_topk_pred(const float *v, int E, int K, int *ids) {
+    const int lane = threadIdx.x & 31;
+    uint32_t key[4];
+#pragma unroll
+    for (int t = 0; t < 4; t++) {
+        const int i = t * 32 + lane;
+        const uint32_t b = i < E ? __float_as_uint(v[i]) : 0u;
+        const bool nan = (b & 0x7fffffffu) > 0x7f800000u;
+        key[t] = i >= E || nan ? 0u : ((b & 0x80000000u) ? ~b : (b | 0x80000000u));
+    }
+    for (int r = 0; r < K; r++) {
+        uint32_t best = 0;
+        int bt = 0;
+#pragma unroll
+        for (int t = 0; t < 4; t++)
+            if (key[t] > best) {
+                best = key[t];
+                bt = t;
+            }
+        const uint32_t top = __reduce_max_sync(0xffffffffu, best);
+        const unsigned owners = __ballot_sync(0xffffffffu, best == top && top != 0u);
+        if (!owners) {
+            if (lane == 0) ids[r] = -1;
+            continue;
+        }
+        const int src = __ffs(owners) - 1;
+        const int id = __shfl_sync(0xffffffffu, bt * 32 + lane, src);
+        if (lane == src) key[bt] = 0u;
+        if (lane == 0) ids[r] = id;
+    }
+    __syncwarp();
+}
+
 template <int DT>
 __device__ void decode_body(const DecodeArgs &a, uint8_t *smem) {
     const DecodeLayout &ly = a.lay;
+    const DecodePlan &pl = ly.plan;
     const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
     const int c = blockIdx.x, G = gridDim.x;
-    const int D = a.D, E = a.E, K = a.K;
+    const int D = a.D, F = a.F, E = a.E, K = a.K;
     uint64_t *bars = reinterpret_cast<uint64_t *>(smem);
-    float *hs = reinterpret_cast<float *>(smem + ly.off_hs);   // h, then x in place
-    const uint8_t **stab = reinterpret_cast<const uint8_t **>(smem + ly.off_stab);   // this layer's slabs
+    float *hs = reinterpret_cast<float *>(smem + ly.off_hs);
+    float *xs = reinterpret_cast<float *>(smem + ly.off_xs);
     act_q8 *xact = reinterpret_cast<act_q8 *>(smem + ly.off_xact);
-    uint8_t *gu = smem + ly.off_gu;
+    const uint8_t **stab = reinterpret_cast<const uint8_t **>(smem + ly.off_stab);   // this layer's slabs
     float *rrow = reinterpret_cast<float *>(smem + ly.off_rrow);
     float *normv = reinterpret_cast<float *>(smem + ly.off_norm);
+    uint8_t *gu = smem + ly.off_gu;
     uint8_t *dn = smem + ly.off_dn;
+    float *mids = reinterpret_cast<float *>(smem + ly.off_mid);
     act_q8 *amid = reinterpret_cast<act_q8 *>(smem + ly.off_amid);
-    float *Y = reinterpret_cast<float *>(smem + ly.off_y);
+    float *Ys = reinterpret_cast<float *>(smem + ly.off_y);
     float *P = reinterpret_cast<float *>(smem + ly.off_p) + warp * DEC_PROWS * 33;
     float *gout = reinterpret_cast<float *>(smem + ly.off_gout) + warp * DEC_PROWS;
-    float *mloc = reinterpret_cast<float *>(smem + ly.off_mloc);
     float *lgs = reinterpret_cast<float *>(smem + ly.off_lg);
+    float *prs = reinterpret_cast<float *>(smem + ly.off_pr);
     float *score = reinterpret_cast<float *>(smem + ly.off_score);
     float *sel = reinterpret_cast<float *>(smem + ly.off_sel);
     unsigned long long *rkey = reinterpret_cast<unsigned long long *>(smem + ly.off_key);
@@ -253,35 +356,59 @@ __device__ void decode_body(const DecodeArgs &a, uint8_t *smem) {
     int *gkeep = reinterpret_cast<int *>(smem + ly.off_keep);
     int *ids = reinterpret_cast<int *>(smem + ly.off_ids);
     float *wts = reinterpret_cast<float *>(smem + ly.off_w);
+    float *yv = reinterpret_cast<float *>(smem + ly.off_yv);
     const float **p_router = reinterpret_cast<const float **>(smem + ly.off_ptrs);
     const float **p_norm = p_router + DEC_MAXL, **p_bias = p_norm + DEC_MAXL;
     __shared__ float rms_r;
+    __shared__ float pred_part[DEC_WARPS];
+    __shared__ int pred_ids[16];
+    __shared__ unsigned s_epoch;
+
     for (int i = tid; i < a.Lyr; i += DEC_THREADS) {
         p_router[i] = a.router[i];
         p_norm[i] = a.norm[i];
         p_bias[i] = a.bias[i];
     }
-
-    // this CTA's gate/up unit: the 64-row block b of the rank-j expert (one mid activation block)
-    const bool has_unit = c < ly.units;
-    const int uj = has_unit ? c / ly.nbF : 0, ub = has_unit ? c - uj * ly.nbF : 0;
-    const int d0 = c * ly.R, d1 = min(D, d0 + ly.R), nrow = max(0, d1 - d0);
-    const uint32_t chunk_bytes = (uint32_t)(DEC_CH * ly.rbD);
-    const bool small_route = E <= 128 && a.route.n_group <= 1;
-
     if (tid == 0) {
+        s_epoch = *(volatile unsigned *)a.epoch;
         for (int i = 0; i < 32; i++) mbar_init(&bars[i], 1);
         fence_mbar_init();
     }
     __syncthreads();
+
+    // this launch's exchange set and the other one (reset during the launch for the next)
+    const int64_t xset = xset_floats(a.Lb, D, F, E, K);
+    float *X = a.xbuf + (int64_t)(s_epoch & 1u) * xset;
+    float *Xo = a.xbuf + (int64_t)((s_epoch & 1u) ^ 1u) * xset;
+    const int64_t o_lg = 0, o_pr = (int64_t)a.Lb * E, o_mid = o_pr + (int64_t)a.Lb * E,
+                  o_y = o_mid + (int64_t)a.Lb * K * F, o_h = o_y + (int64_t)a.Lb * K * D;
+    auto xlg = [&](int l) { return X + o_lg + (int64_t)l * E; };
+    auto xpr = [&](int l) { return X + o_pr + (int64_t)l * E; };
+    auto xmid = [&](int l, int j) { return X + o_mid + ((int64_t)l * K + j) * F; };
+    auto xy = [&](int l, int j) { return X + o_y + ((int64_t)l * K + j) * D; };
+    auto xh = [&](int l) { return X + o_h + (int64_t)l * D; };
+
+    // this CTA's work
+    int ch0, ch1;
+    chunk_range(c, G, pl.nch, &ch0, &ch1);
+    const int nch_c = ch1 - ch0;
+    const int jd = down_group(c, G, K);
+    int dr0, dr1, hr0, hr1;
+    down_rows(c, G, K, D, pl.ra, &dr0, &dr1);
+    h_rows(c, G, D, &hr0, &hr1);
+    const int ndr = dr1 - dr0, nhr = hr1 - hr0;
+    const int cpe = F / DEC_CH;   // chunks per expert
+    const uint32_t chunk_bytes = (uint32_t)(DEC_CH * ly.rbD);
+    const bool small_route = E <= 128 && a.route.n_group <= 1;
+
     auto issue_router = [&](int l) {   // router rows e = c + t*G, ffn_norm and the slab pointers of layer l
         uint32_t bytes = (uint32_t)D * 4 + (uint32_t)E * 8;
-        for (int t = 0; t < ly.rpc; t++)
+        for (int t = 0; t < pl.rpc; t++)
             if (c + t * G < E) bytes += (uint32_t)D * 4;
         mbar_expect_tx(&bars[BAR_ROUTER], bytes);
         bulk_g2s(normv, p_norm[l], (uint32_t)D * 4, &bars[BAR_ROUTER]);
         bulk_g2s(stab, a.slab + (size_t)l * E, (uint32_t)E * 8, &bars[BAR_ROUTER]);
-        for (int t = 0; t < ly.rpc; t++)
+        for (int t = 0; t < pl.rpc; t++)
             if (c + t * G < E)
                 bulk_g2s(rrow + (size_t)t * D, p_router[l] + (size_t)(c + t * G) * D, (uint32_t)D * 4,
                          &bars[BAR_ROUTER]);
@@ -289,17 +416,34 @@ __device__ void decode_body(const DecodeArgs &a, uint8_t *smem) {
     if (tid == 0) issue_router(0);
 
     unsigned long long *stamp = nullptr;
-    unsigned nbar = a.bar_base;   // barriers passed so far
-    auto barrier = [&]() { grid_sync(a.bar, (++nbar) * (unsigned)G, a.err); };
     for (int l = 0; l < a.Lyr; l++) {
         const uint32_t par = (uint32_t)(l & 1);
         if (a.trace) stamp = a.trace + ((size_t)l * G + c) * DEC_STAMPS;
 #define HX_STAMP(i) \
     if (stamp && tid == 0) stamp[i] = sm_clock()
         HX_STAMP(ST_START);
-        // ---------------- phase A: rmsnorm, activations, router rows
-        for (int i = tid; i < D; i += DEC_THREADS) hs[i] = __ldcg(a.h + i);
+        // ---------------- P1: h, rmsnorm, activations, router rows, predicted logit
+        const bool predict = a.predict && l + 1 < a.Lyr;   // launch-uniform
+        float4 pr[kPredVec], pn[kPredVec];
+        if (predict && c < E) {   // operands of the predicted logit (independent of h)
+            const float4 *rw = reinterpret_cast<const float4 *>(p_router[l + 1] + (size_t)c * D);
+            const float4 *nw = reinterpret_cast<const float4 *>(p_norm[l + 1]);
+#pragma unroll
+            for (int v = 0; v < kPredVec; v++) {
+                const int i4 = tid + v * DEC_THREADS;
+                if (i4 * 4 < D) {
+                    pr[v] = __ldcg(rw + i4);
+                    pn[v] = __ldcg(nw + i4);
+                }
+            }
+        }
+        if (l == 0) {
+            for (int i = tid; i < D; i += DEC_THREADS) hs[i] = __ldcg(a.h + i);
+        } else {
+            poll_vec(xh(l), hs, D, a.err);
+        }
         __syncthreads();
+        HX_STAMP(ST_H);
         if (warp == 0) {
             float L = 0.0f;
             if (lane < 16) {
@@ -314,124 +458,174 @@ __device__ void decode_body(const DecodeArgs &a, uint8_t *smem) {
         HX_STAMP(ST_NORM);
         {
             const float r = rms_r;
-            for (int i = tid; i < D; i += DEC_THREADS) hs[i] = __fmul_rn(__fmul_rn(hs[i], r), normv[i]);
+            for (int i = tid; i < D; i += DEC_THREADS) xs[i] = __fmul_rn(__fmul_rn(hs[i], r), normv[i]);
         }
         __syncthreads();
-        for (int b = warp; b < ly.nbD; b += DEC_WARPS) act_quant_warp(hs[b * QK + lane], hs[b * QK + lane + 32], xact + b, lane);
-        {   // router rows: one 16-lane group each (warp-uniform tree; idle groups add zeros)
+        {   // router rows first (the logits are on every CTA's path): one 16-lane group each
             const int t = tid >> 4, j = tid & 15;
-            const bool active = t < ly.rpc && c + t * G < E;
+            const bool active = t < pl.rpc && c + t * G < E;
             float L = 0.0f;
             if (active) {
                 const float *w = rrow + (size_t)t * D;
 #pragma unroll 8
-                for (int i = j; i < D; i += 16) L = __fadd_rn(L, __fmul_rn(w[i], hs[i]));
+                for (int i = j; i < D; i += 16) L = __fadd_rn(L, __fmul_rn(w[i], xs[i]));
             }
-            if (warp < (ly.rpc + 1) / 2) {
+            if (warp < (pl.rpc + 1) / 2) {
                 L = tree16(L, 0xffffffffu);
-                if (active && j == 0) a.logits[c + t * G] = canon(L);
+                if (active && j == 0) st_x(xlg(l) + c + t * G, canon(L));
             }
         }
-        HX_STAMP(ST_ROUTER);
-        barrier();
-        HX_STAMP(ST_BAR1);
-
-        // ---------------- phase B: routing (warp 0), copies in flight, gate/up + SwiGLU, mid block
-        if (small_route) route_token_cta_small(a.route, a.logits, p_bias[l], score, rkey, ids, wts);
-        if (warp == 0) {
-            if (!small_route)
-                route_token_warp1(a.route, a.logits, p_bias[l], lgs, rkey, score, sel, gscr, gkeep, ids, wts);
-            if (lane == 0) HX_STAMP(ST_ROUTE);
-            fence_proxy_async();
-            if (has_unit) {   // gate/up rows of the unit: chunk q = rows 4q..4q+3 of gate and of up
-                const uint8_t *slab = stab[ids[uj]];
-                if (lane < QK / DEC_CH) {
-                    if (!slab) {
-                        if (lane == 0) set_error(a.err, DEV_E_NOT_RESIDENT);
-                        mbar_expect_tx(&bars[lane], 0);
-                    } else {
-                        const int64_t r0 = (int64_t)ub * QK + lane * DEC_CH;
-                        uint8_t *dst = gu + (size_t)lane * 2 * chunk_bytes;
-                        mbar_expect_tx(&bars[lane], 2 * chunk_bytes);
-                        bulk_g2s(dst, slab + r0 * ly.rbD, chunk_bytes, &bars[lane]);
-                        bulk_g2s(dst + chunk_bytes, slab + a.off_up + r0 * ly.rbD, chunk_bytes, &bars[lane]);
-                    }
+        for (int b = warp; b < ly.nbD; b += DEC_WARPS) act_quant_warp(xs[b * QK + lane], xs[b * QK + lane + 32], xact + b, lane);
+        if (predict && c < E) {   // partial of the predicted logit (every thread, any order)
+            float sum = 0.0f;
+#pragma unroll
+            for (int v = 0; v < kPredVec; v++) {
+                const int i4 = tid + v * DEC_THREADS;
+                if (i4 * 4 < D) {
+                    const float4 hh = reinterpret_cast<const float4 *>(hs)[i4];
+                    sum += pr[v].x * pn[v].x * hh.x + pr[v].y * pn[v].y * hh.y + pr[v].z * pn[v].z * hh.z +
+                           pr[v].w * pn[v].w * hh.w;
                 }
             }
-            if (nrow > 0) {   // down rows [d0, d1) of the K experts on one barrier
-                const uint8_t *slab = lane < K ? stab[ids[lane]] : nullptr;
-                const bool have = slab != nullptr;
-                if (lane < K && !have) set_error(a.err, DEV_E_NOT_RESIDENT);
-                const unsigned nhave = __popc(__ballot_sync(0xffffffffu, have));
-                if (lane == 0) mbar_expect_tx(&bars[BAR_DOWN], nhave * (uint32_t)(nrow * ly.rbF));
-                __syncwarp();
-                if (have)
-                    bulk_g2s(dn + (size_t)lane * ly.R * ly.rbF, slab + a.off_down + (int64_t)d0 * ly.rbF,
-                             (uint32_t)(nrow * ly.rbF), &bars[BAR_DOWN]);
+#pragma unroll
+            for (int o = 16; o >= 1; o >>= 1) sum += __shfl_xor_sync(0xffffffffu, sum, o);
+            if (lane == 0) pred_part[warp] = sum;
+        }
+        HX_STAMP(ST_ROUTER);
+
+        // ---------------- P2: logits, routing, copies in flight
+        poll_vec(xlg(l), lgs, E, a.err);
+        __syncthreads();
+        HX_STAMP(ST_LG);
+        if (predict && c < E && warp == 1) {
+            float v = lane < DEC_WARPS ? pred_part[lane] : 0.0f;
+#pragma unroll
+            for (int o = 16; o >= 1; o >>= 1) v += __shfl_xor_sync(0xffffffffu, v, o);
+            if (lane == 0) st_x(xpr(l) + c, canon(v * rms_r));
+        }
+        if (small_route) {
+            route_token_cta_small<true>(a.route, lgs, p_bias[l], score, rkey, ids, wts);
+        } else if (warp == 0) {
+            route_token_warp1<true>(a.route, lgs, p_bias[l], lgs, rkey, score, sel, gscr, gkeep, ids, wts);
+        }
+        __syncthreads();
+        if (warp == kIssueWarp) {   // a warp without a chunk (when nch_c < 16): the others start at once
+            fence_proxy_async();
+            for (int q = lane; q < nch_c; q += 32) {   // chunk q: rows 4p..4p+3 of gate and of up, expert rank j
+                const int g = ch0 + q, j = g / cpe, p = g - j * cpe;
+                const uint8_t *slab = stab[ids[j]];
+                if (!slab) {
+                    set_error(a.err, DEV_E_NOT_RESIDENT);
+                    mbar_expect_tx(&bars[q], 0);
+                } else {
+                    const int64_t r0 = (int64_t)p * DEC_CH;
+                    uint8_t *dst = gu + (size_t)q * 2 * chunk_bytes;
+                    mbar_expect_tx(&bars[q], 2 * chunk_bytes);
+                    bulk_g2s(dst, slab + r0 * ly.rbD, chunk_bytes, &bars[q]);
+                    bulk_g2s(dst + chunk_bytes, slab + a.off_up + r0 * ly.rbD, chunk_bytes, &bars[q]);
+                }
+            }
+            if (lane == 0) {   // this CTA's slice of the rank-jd expert's down rows
+                const uint8_t *slab = stab[ids[jd]];
+                if (!slab) {
+                    set_error(a.err, DEV_E_NOT_RESIDENT);
+                    mbar_expect_tx(&bars[BAR_DOWN], 0);
+                } else {
+                    mbar_expect_tx(&bars[BAR_DOWN], (uint32_t)(ndr * ly.rbF));
+                    bulk_g2s(dn, slab + a.off_down + (int64_t)dr0 * ly.rbF, (uint32_t)(ndr * ly.rbF), &bars[BAR_DOWN]);
+                }
             }
             __syncwarp();
-        }
-        if (has_unit) {   // warp q: chunk q (4 gate rows then 4 up rows) -> 4 SwiGLU values
-            const int q = warp;
-            if (q < QK / DEC_CH && mbar_wait(&bars[q], par, a.err)) {
-                warp_rows_1tok<DT>(gu + (size_t)q * 2 * chunk_bytes, ly.rbD, ly.nbD, 2 * DEC_CH, xact, P, gout);
-                if (lane < DEC_CH) mloc[q * DEC_CH + lane] = swiglu_c(gout[lane], gout[DEC_CH + lane]);
+            if (lane == 0 && l + 1 < a.Lyr) {   // rrow / normv / stab are consumed
+                fence_proxy_async();
+                issue_router(l + 1);
             }
         }
-        __syncthreads();
-        HX_STAMP(ST_GATEUP);
-        if (has_unit && warp == 0) {   // the unit's mid activation block (NUMERICS §2)
-            act_quant_warp(mloc[lane], mloc[lane + 32], a.act_mid + (size_t)uj * ly.nbF + ub, lane);
-            __threadfence();
-        }
-        if (tid == 0) {   // gate/up rows are consumed: the next layer's router rows may land there
-            fence_proxy_async();
-            if (l + 1 < a.Lyr) issue_router(l + 1);
-        }
-        HX_STAMP(ST_MID);
-        barrier();
-        HX_STAMP(ST_BAR2);
+        HX_STAMP(ST_ROUTE);
 
-        // ---------------- phase C: down rows, rank-order sum, residual
-        {
-            const uint32_t *src = reinterpret_cast<const uint32_t *>(a.act_mid);
-            uint32_t *dst = reinterpret_cast<uint32_t *>(amid);
-            for (int i = tid; i < K * ly.nbF * (ACT_BLOCK / 4); i += DEC_THREADS) dst[i] = __ldcg(src + i);
-        }
-        __syncthreads();
-        if (nrow > 0) {
-            const bool ok = mbar_wait(&bars[BAR_DOWN], par, a.err);
-            const int per = (nrow + DEC_PROWS - 1) / DEC_PROWS;   // row groups per expert
-            for (int u = warp; u < K * per && ok; u += DEC_WARPS) {
-                const int j = u / per, r0 = (u - j * per) * DEC_PROWS, nr = min(DEC_PROWS, nrow - r0);
-                warp_rows_1tok<DT>(dn + ((size_t)j * ly.R + r0) * ly.rbF, ly.rbF, ly.nbF, nr,
-                                   amid + (size_t)j * ly.nbF, P, Y + (size_t)j * ly.R + r0);
+        // ---------------- P3: gate/up chunks -> SwiGLU -> mid exchange; next-layer prefetch
+        for (int q = warp; q < nch_c; q += DEC_WARPS) {
+            const int g = ch0 + q, j = g / cpe, p = g - j * cpe;
+            if (mbar_wait(&bars[q], par, a.err)) {
+                warp_rows_1tok<DT>(gu + (size_t)q * 2 * chunk_bytes, ly.rbD, ly.nbD, 2 * DEC_CH, xact, P, gout);
+                if (lane < DEC_CH)
+                    st_x(xmid(l, j) + p * DEC_CH + lane, canon(swiglu_c(gout[lane], gout[DEC_CH + lane])));
             }
         }
+        if (predict && warp == kIssueWarp && nch_c <= kIssueWarp) {
+            for (int i = lane; i < E; i += 32) prs[i] = poll1(xpr(l) + i, a.err);
+            __syncwarp();
+            warp_topk_pred(prs, E, K, pred_ids);
+            const int per = (int)((a.slab_used + kPrefetchPiece - 1) / kPrefetchPiece);
+            for (int pi = c + lane * G; pi < K * per; pi += 32 * G) {
+                const int j = pi / per, k = pi - j * per;
+                const int e = pred_ids[j];
+                const uint8_t *sl = e >= 0 ? a.slab[(size_t)(l + 1) * E + e] : nullptr;
+                const int64_t off = (int64_t)k * kPrefetchPiece, left = a.slab_used - off;
+                if (sl) prefetch_l2(sl + off, left < (int64_t)kPrefetchPiece ? (uint32_t)left : kPrefetchPiece);
+            }
+        }
+        {   // reset this CTA's share of the other set's slots of buffer layers [b0, b1) for the next launch
+            const int b0 = (int)((int64_t)a.Lb * l / a.Lyr), b1 = (int)((int64_t)a.Lb * (l + 1) / a.Lyr);
+            const int64_t per_layer[5] = {E, E, (int64_t)K * F, (int64_t)K * D, D};
+            const int64_t base[5] = {o_lg, o_pr, o_mid, o_y, o_h};
+            for (int k = 0; k < 5; k++)
+                for (int b = b0; b < b1; b++) {
+                    float *s0 = Xo + base[k] + (int64_t)b * per_layer[k];
+                    for (int64_t i = (int64_t)c * DEC_THREADS + tid; i < per_layer[k]; i += (int64_t)G * DEC_THREADS)
+                        s0[i] = __uint_as_float(kEmpty);
+                }
+        }
+        HX_STAMP(ST_GATEUP);
+
+        // ---------------- P4: expert jd's mid -> activation blocks -> this CTA's down rows -> y exchange
+        poll_vec(xmid(l, jd), mids, F, a.err);
         __syncthreads();
+        for (int b = warp; b < ly.nbF; b += DEC_WARPS) act_quant_warp(mids[b * QK + lane], mids[b * QK + lane + 32], amid + b, lane);
+        __syncthreads();
+        HX_STAMP(ST_MID);
+        {
+            const bool ok = mbar_wait(&bars[BAR_DOWN], par, a.err);
+            for (int r0 = warp * DEC_PROWS; r0 < ndr && ok; r0 += DEC_WARPS * DEC_PROWS)
+                warp_rows_1tok<DT>(dn + (size_t)r0 * ly.rbF, ly.rbF, ly.nbF, min(DEC_PROWS, ndr - r0), amid, P, Ys + r0);
+        }
+        __syncthreads();
+        for (int r = tid; r < ndr; r += DEC_THREADS) st_x(xy(l, jd) + dr0 + r, Ys[r]);
         HX_STAMP(ST_DOWN);
-        if (tid < nrow) {
-            float o = 0.0f;
-            for (int j = 0; j < K; j++) o = __fadd_rn(o, __fmul_rn(wts[j], Y[(size_t)j * ly.R + tid]));
-            float *hp = a.h + d0 + tid;
-            __stcg(hp, __fadd_rn(__ldcg(hp), __fmul_rn(a.rs, o)));
+
+        // ---------------- P5: y of the K experts for this CTA's h rows -> rank-order sum -> residual
+        for (int i = tid; i < K * nhr; i += DEC_THREADS) {
+            const int j = i / nhr, r = i - j * nhr;
+            yv[i] = poll1(xy(l, j) + hr0 + r, a.err);
+        }
+        __syncthreads();
+        HX_STAMP(ST_Y);
+        if (tid < nhr) {
+            float o = 0.0f;   // rank-order sum (engine/src/model.c:904-923)
+            for (int j = 0; j < K; j++) o = __fadd_rn(o, __fmul_rn(wts[j], yv[j * nhr + tid]));
+            const float hn = __fadd_rn(hs[hr0 + tid], __fmul_rn(a.rs, o));
+            if (l + 1 < a.Lyr) st_x(xh(l + 1) + hr0 + tid, canon(hn));
+            else a.h[hr0 + tid] = hn;
         }
         if (l == a.Lyr - 1 && c == 0 && tid < K) {
             a.ids_out[tid] = ids[tid];
             a.w_out[tid] = wts[tid];
         }
         HX_STAMP(ST_SUM);
-        barrier();
-        HX_STAMP(ST_BAR3);
+        __syncthreads();   // hs rows of P5 are read before the next layer's h lands in hs
 #undef HX_STAMP
     }
     // every bulk copy this CTA issued has landed before it exits (already true unless a wait gave up)
     if (tid == 0 && a.Lyr > 0) {
         const uint32_t last = (uint32_t)((a.Lyr - 1) & 1);
-        if (has_unit)
-            for (int q = 0; q < QK / DEC_CH; q++) mbar_wait(&bars[q], last, nullptr);
-        if (nrow > 0) mbar_wait(&bars[BAR_DOWN], last, nullptr);
+        for (int q = 0; q < nch_c; q++) mbar_wait(&bars[q], last, nullptr);
+        mbar_wait(&bars[BAR_DOWN], last, nullptr);
         mbar_wait(&bars[BAR_ROUTER], last, nullptr);
+        // the last CTA to finish advances the launch counter (every CTA read it at its start)
+        if (atomicAdd(a.epoch + 1, 1u) == (unsigned)G - 1) {
+            a.epoch[1] = 0u;
+            a.epoch[0] = s_epoch + 1u;
+        }
     }
     __syncthreads();
 }
@@ -457,9 +651,7 @@ int decode_grid() {
     return sms;
 }
 
-size_t decode_smem_bytes(int D, int F, int E, int K, int dtype) {
-    return decode_layout(decode_grid(), D, F, E, K, dtype).total;
-}
+int64_t decode_xbuf_floats(int Lb, int D, int F, int E, int K) { return 2 * xset_floats(Lb, D, F, E, K); }
 
 bool decode_supported(int D, int F, int E, int K, int dtype, bool shared, std::string *why) {
     auto no = [&](const char *w) {
@@ -470,14 +662,14 @@ bool decode_supported(int D, int F, int E, int K, int dtype, bool shared, std::s
     if (dtype != Q4 && dtype != Q8) return no("dtype");
     if (row_bytes(dtype, D) % 16) return no("gate/up rows not a multiple of 16 bytes");
     if (K > 16) return no("top_k > 16");
-    if (E % 2) return no("odd expert count (slab pointer row not a multiple of 16 bytes)");
+    if (E % 4 || D % 4 || F % 4) return no("exchange vectors (D, F, E multiples of 4)");
     const int G = decode_grid();
     const DecodeLayout ly = decode_layout(G, D, F, E, K, dtype);
-    if (ly.rpc > 2 * DEC_WARPS) return no("router rows per CTA");
-    if (ly.R > DEC_PROWS * DEC_WARPS) return no("down rows per CTA");
-    if (ly.units > G) return no("more gate/up blocks (top_k * F / 64) than SMs");
-    (void)0;
-    if (QK / DEC_CH > DEC_WARPS || QK / DEC_CH > BAR_DOWN) return no("chunking");
+    const DecodePlan &pl = ly.plan;
+    if (pl.rpc > 2 * DEC_WARPS) return no("router rows per CTA");
+    if (pl.ch_max > DEC_MAXCH) return no("gate/up chunks per CTA");
+    if (G < K || D % pl.ra) return no("down groups");
+    if (D / (G / K) < 2 * pl.ra) return no("down rows per CTA");
     int lim = 0, dev = 0;
     cudaGetDevice(&dev);
     cudaDeviceGetAttribute(&lim, cudaDevAttrMaxSharedMemoryPerBlockOptin, dev);
@@ -499,6 +691,7 @@ cudaError_t init_decode_attributes() {
 }
 
 cudaError_t launch_moe_decode(const DecodeParams &p, cudaStream_t s) {
+    if (p.n_layers > p.buf_layers || p.n_layers > DEC_MAXL) return cudaErrorInvalidValue;
     DecodeArgs a;
     a.Lyr = p.n_layers;
     a.D = p.D;
@@ -516,18 +709,18 @@ cudaError_t launch_moe_decode(const DecodeParams &p, cudaStream_t s) {
     a.bias = p.bias;
     a.slab = p.slab;
     a.h = p.h;
-    a.logits = p.logits;
-    a.mbuf = p.mbuf;
-    a.act_mid = p.act_mid;
-    a.bar = p.bar;
-    a.bar_base = p.bar_base;
-    a.blk_cnt = p.blk_cnt;
+    a.xbuf = p.xbuf;
+    a.Lb = p.buf_layers;
+    a.epoch = p.epoch;
     a.err = p.err;
     a.ids_out = p.ids_out;
     a.w_out = p.w_out;
     a.trace = p.trace;
+    a.slab_used = p.slab_used;
     const int G = decode_grid();
     a.lay = decode_layout(G, p.D, p.F, p.E, p.K, p.dtype);
+    a.predict = p.prefetch && p.E <= G && p.E <= 128 && p.route.n_group <= 1 &&
+                p.D <= 4 * kPredVec * DEC_THREADS && a.lay.plan.ch_max < DEC_WARPS && p.slab_used % 16 == 0;
     cudaLaunchConfig_t cfg = {};
     cfg.gridDim = dim3((unsigned)G);
     cfg.blockDim = dim3(DEC_THREADS);

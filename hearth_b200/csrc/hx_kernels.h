@@ -113,20 +113,20 @@ struct DecodeParams {
     const float *const *bias;
     const uint8_t *const *slab;   // [n_layers * E]
     float *h;                     // [D]
-    float *logits;                // [E]
-    float *mbuf;                  // [K * F]
-    act_q8 *act_mid;              // [K * F / 64]
-    unsigned *bar;                // barrier counters: 16 lines of 128 bytes, zero at allocation
-    unsigned bar_base;            // barriers of earlier launches (3 * n_layers each)
-    unsigned *blk_cnt;            // [n_layers * K * F / 64] (zero at allocation)
+    float *xbuf;                  // decode_xbuf_floats(buf_layers, ...) floats, 0xffffffff at allocation
+    int buf_layers;               // layers the exchange buffers hold (>= n_layers)
+    unsigned *epoch;              // [2] launch counter and arrival count, zero at allocation
     int *err;
     int *ids_out;
     float *w_out;
     unsigned long long *trace;    // null, or [n_layers][grid][decode_stamps()] phase timestamps
+    bool prefetch;                // predict the next layer's experts and prefetch them into L2
+    int64_t slab_used;            // bytes of a slab the kernels read (gate, up, down)
 };
 int decode_grid();
 int decode_stamps();
 int decode_max_layers();
+int64_t decode_xbuf_floats(int buf_layers, int D, int F, int E, int K);
 bool decode_supported(int D, int F, int E, int K, int dtype, bool shared, std::string *why);
 cudaError_t init_decode_attributes();
 cudaError_t launch_moe_decode(const DecodeParams &p, cudaStream_t s);

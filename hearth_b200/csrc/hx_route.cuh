@@ -201,13 +201,18 @@ __device__ __forceinline__ unsigned long long rank_key(float v, int i) {
 // route_select's (engine/src/model.c:793-831), so the experts with rank < K are its ids in order.
 // lg/score/sel [E], key [E] (8-byte aligned), gsc/keep [n_group]: this warp's shared scratch.
 // Results: ids[K], w[K] in shared memory, valid after the call for this warp (and for the CTA
-// after its next barrier).
+// after its next barrier). kSharedLogits: logit_g is already this warp's shared copy (lg unused).
+template <bool kSharedLogits = false>
 __device__ __forceinline__ void route_token_warp1(const RouteCfg &R, const float *logit_g, const float *bias,
                                                   float *lg, unsigned long long *key, float *score, float *sel,
                                                   float *gsc, int *keep, int *ids, float *w) {
     const int lane = threadIdx.x & 31;
     const int E = R.E, K = R.K;
-    for (int i = lane; i < E; i += 32) lg[i] = __ldcg(logit_g + i);
+    if constexpr (kSharedLogits) {
+        lg = const_cast<float *>(logit_g);
+    } else {
+        for (int i = lane; i < E; i += 32) lg[i] = __ldcg(logit_g + i);
+    }
     __syncwarp();
     if (R.score_fn == SCORE_SOFTMAX) {
         float m = -__uint_as_float(0x7f800000u);   // m = x[0]; m = x[i] > m ? x[i] : m
@@ -292,87 +297,107 @@ __device__ __forceinline__ void route_token_warp1(const RouteCfg &R, const float
     __syncwarp();
 }
 
-// Top-k routing of one token by a whole CTA, for E <= 128 without expert groups. Warp 0 computes
-// the scores (lane l holds experts l, l+32, l+64, l+96) and writes them with their sort keys to
-// shared memory; after one block barrier every thread takes one (expert i, quarter q) pair and counts
-// the keys of quarter q above key(i), four lanes add their counts (rank(i) = #{o : key(o) > key(i)}),
-// and the experts of rank < K are route_select's ids in order; after a second barrier warp 0 forms
-// the weights. One warp for the scores keeps the double-precision exp work off the other warps.
-// score_s [E] and key_s [4 * ceil(E/4)] are shared scratch; key(o) for o = q * ceil(E/4) + k lives at
-// key_s[4k + q] so that the four quarters read by a warp fall in different banks. Results ids / w
-// (shared); every thread of the CTA must call it.
-// kSharedLogits: the logits are in shared memory (plain loads) rather than global (L2 loads).
+// Profiling hook of route_token_cta_small: HX_ROUTE_STAMP(i) marks the end of step i (empty here;
+// a timing harness defines it before including this header).
+#ifndef HX_ROUTE_STAMP
+#define HX_ROUTE_STAMP(i)
+#endif
+
+// Top-k routing of one token by a whole CTA (at least 128 threads), for E <= 128 and K <= 16
+// without expert groups. Threads 0..E-1 own one expert each: softmax takes the maximum (warp 0), exp
+// per expert, the sum16 of the exps (warp 0, NUMERICS §1 order), then one division per expert;
+// sigmoid scores need none of the shared steps. Selection is exact without comparing all pairs:
+// each of warps 0..3 ranks its 32 keys among themselves (rank_key order; the slots past E get
+// distinct keys below every real key), the keys of within-warp rank < K are the warp's candidates,
+// and a candidate's rank is its within-warp rank plus, for each other warp, the number of that
+// warp's candidates above it. That count is exact whenever it is below K for every warp, and reaches
+// K otherwise, so the experts of rank < K come out exactly, in route_select's order. Warp 0 then
+// forms the weights. score_s [E] and key_s [128] are shared scratch. Results ids / w (shared);
+// every thread of the CTA must call it. kSharedLogits: the logits are in shared memory (plain
+// loads) rather than global (L2 loads).
 template <bool kSharedLogits = false>
 __device__ __forceinline__ void route_token_cta_small(const RouteCfg &R, const float *logit_g, const float *bias,
                                                       float *score_s, unsigned long long *key_s, int *ids,
                                                       float *w) {
-    const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
-    const int E = R.E, K = R.K, Q = (E + 3) >> 2;
-    if (warp == 0) {
-        float x[4], sc[4];
-#pragma unroll
-        for (int t = 0; t < 4; t++)
-            x[t] = (t * 32 + lane < E) ? (kSharedLogits ? logit_g[t * 32 + lane] : __ldcg(logit_g + t * 32 + lane))
-                                       : 0.0f;
-        if (R.score_fn == SCORE_SOFTMAX) {
-            float m = -__uint_as_float(0x7f800000u);   // m = x[0]; m = x[i] > m ? x[i] : m
+    __shared__ float s_red[2];                 // softmax maximum, sum of exps
+    __shared__ unsigned long long s_cand[4][16];   // each warp's K largest keys, by within-warp rank
+    const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
+    const int E = R.E, K = R.K;
+    auto logit = [&](int i) { return kSharedLogits ? logit_g[i] : __ldcg(logit_g + i); };
+    const bool mine = tid < E;   // this thread scores expert tid
+    const float x = mine ? logit(tid) : 0.0f;
+    float sc = 0.0f;
+    if (R.score_fn == SCORE_SOFTMAX) {
+        if (warp == 0) {   // m = x[0]; m = x[i] > m ? x[i] : m (NaN only through x[0])
+            float m = -__uint_as_float(0x7f800000u);
 #pragma unroll
             for (int t = 0; t < 4; t++)
-                if (t * 32 + lane < E) m = fmaxf(m, x[t]);
+                if (t * 32 + lane < E) m = fmaxf(m, logit(t * 32 + lane));
 #pragma unroll
             for (int s = 16; s >= 1; s >>= 1) m = fmaxf(m, __shfl_xor_sync(0xffffffffu, m, s));
-            const float x0 = __shfl_sync(0xffffffffu, x[0], 0);
-            if (x0 != x0) m = x0;
-            float e[4];
-#pragma unroll
-            for (int t = 0; t < 4; t++) e[t] = (t * 32 + lane < E) ? host_expf(__fsub_rn(x[t], m)) : 0.0f;
-            // sum16: lane j < 16 adds e[j], e[j+16], e[j+32], ... in order; e[i] lives in lane i%32,
-            // slot i/32, so the sequence alternates this lane's slot t and lane j+16's slot t (absent
-            // elements are +0.0f, which leaves a sum of non-negative terms unchanged)
+            const float x0 = __shfl_sync(0xffffffffu, x, 0);
+            if (lane == 0) s_red[0] = x0 != x0 ? x0 : m;
+        }
+        HX_ROUTE_STAMP(0);
+        __syncthreads();
+        const float e = mine ? host_expf(__fsub_rn(x, s_red[0])) : 0.0f;
+        if (mine) score_s[tid] = e;
+        HX_ROUTE_STAMP(1);
+        __syncthreads();
+        if (warp == 0) {   // sum16: lane j < 16 adds e[j], e[j+16], ... in order, then the 8/4/2/1 tree
             float L = 0.0f;
+            if (lane < 16)
 #pragma unroll
-            for (int t = 0; t < 4; t++) {
-                const float other = __shfl_down_sync(0xffffffffu, e[t], 16);
-                L = __fadd_rn(L, e[t]);
-                L = __fadd_rn(L, other);
-            }
+                for (int i = lane; i < 128; i += 16)
+                    if (i < E) L = __fadd_rn(L, score_s[i]);
             L = tree16(L, 0xffffffffu);
-            const float ssum = __shfl_sync(0xffffffffu, L, 0);
-#pragma unroll
-            for (int t = 0; t < 4; t++) sc[t] = __fdiv_rn(e[t], ssum);
-        } else {
-#pragma unroll
-            for (int t = 0; t < 4; t++) sc[t] = sigmoid_c(x[t]);
+            if (lane == 0) s_red[1] = L;
         }
+        HX_ROUTE_STAMP(2);
+        __syncthreads();
+        sc = __fdiv_rn(e, s_red[1]);
+    } else {
+        sc = sigmoid_c(x);
+    }
+    unsigned long long ki = 0;
+    if (tid < 128) {   // slot s >= E: key 127 - s, below every real key (whose low word is >= 2^32 - 128)
+        const float sv = (R.score_bias && bias && mine) ? __fadd_rn(sc, __ldg(bias + tid)) : sc;
+        ki = mine ? rank_key(sv, tid) : (unsigned long long)(127 - tid);
+        key_s[tid] = ki;
+        if (mine) score_s[tid] = sc;
+    }
+    HX_ROUTE_STAMP(3);
+    __syncthreads();
+    int r = 0;
+    if (tid < 128) {   // within-warp rank: 32 broadcast loads
+        const unsigned long long *kw = key_s + (tid & ~31);
 #pragma unroll
-        for (int t = 0; t < 4; t++) {
-            const int i = t * 32 + lane;
-            if (i < 4 * Q) {   // slots past E hold key 0, which ranks after every real expert
-                const float sv = (R.score_bias && bias && i < E) ? __fadd_rn(sc[t], __ldg(bias + i)) : sc[t];
-                const int q = i / Q, k = i - q * Q;
-                key_s[4 * k + q] = i < E ? rank_key(sv, i) : 0ull;
-                if (i < E) score_s[i] = sc[t];
+        for (int k = 0; k < 32; k++) r += kw[k] > ki ? 1 : 0;
+        if (r < K) s_cand[warp][r] = ki;
+    }
+    HX_ROUTE_STAMP(4);
+    __syncthreads();
+    if (mine && r < K) {   // own warp's candidates above ki number exactly r
+        int rank = 0;
+#pragma unroll
+        for (int w2 = 0; w2 < 4; w2++)
+#pragma unroll
+            for (int k = 0; k < 16; k++) rank += (k < K && s_cand[w2][k] > ki) ? 1 : 0;
+        if (rank < K) ids[rank] = tid;
+    }
+    HX_ROUTE_STAMP(5);
+    __syncthreads();
+    if (warp == 0) {   // route_weights (model.c:833-843): every lane forms the rank-order sum itself
+        float v[16];
+#pragma unroll
+        for (int j = 0; j < 16; j++) v[j] = j < K ? score_s[ids[j]] : 0.0f;
+        float sacc = 0.0f, wj = 0.0f;
+#pragma unroll
+        for (int j = 0; j < 16; j++)
+            if (j < K) {
+                sacc = __fadd_rn(sacc, v[j]);
+                if (j == lane) wj = v[j];
             }
-        }
-    }
-    __syncthreads();
-    for (int p0 = 0; p0 < 4 * Q; p0 += blockDim.x) {   // warp-uniform trip count (shuffles below)
-        const int p = p0 + (int)threadIdx.x, i = p >> 2, q = p & 3;
-        int cnt = 0;
-        if (i < E) {
-            const int qi = i / Q, ki_ = i - qi * Q;
-            const unsigned long long ki = key_s[4 * ki_ + qi];
-            for (int k = 0; k < Q; k++) cnt += key_s[4 * k + q] > ki ? 1 : 0;
-        }
-        cnt += __shfl_xor_sync(0xffffffffu, cnt, 1);
-        cnt += __shfl_xor_sync(0xffffffffu, cnt, 2);
-        if (i < E && q == 0 && cnt < K) ids[cnt] = i;
-    }
-    __syncthreads();
-    if (warp == 0) {   // route_weights (model.c:833-843)
-        float wj = lane < K ? score_s[ids[lane]] : 0.0f;
-        float sacc = 0.0f;
-        for (int j = 0; j < K; j++) sacc = __fadd_rn(sacc, __shfl_sync(0xffffffffu, wj, j));
         const float den = __fadd_rn(sacc, 1e-20f);
         if (lane < K) {
             if (R.norm_topk_prob) wj = __fdiv_rn(wj, den);
@@ -380,6 +405,7 @@ __device__ __forceinline__ void route_token_cta_small(const RouteCfg &R, const f
         }
         __syncwarp();
     }
+    HX_ROUTE_STAMP(6);
 }
 
 }  // namespace hx

@@ -45,8 +45,9 @@ def make_slab(rng, D, F, dt=O.Q4):
 
 def build_pair(seed, *, L=1, D=256, F=128, E=16, K=4, score_fn=0, score_bias=0, n_group=1, topk_group=1,
                norm=1, routed_scale=1.0, Fs=0, shared_gate=False, max_tokens=64, cache_gb=0.0, policy=1,
-               router_sigma=0.15, residual_scale=1.0):
-    """An oracle model and a GPU backend holding the same random weights."""
+               router_sigma=0.15, residual_scale=1.0, router_fn=None):
+    """An oracle model and a GPU backend holding the same random weights. router_fn(router) may
+    rewrite each layer's router matrix (e.g. duplicate rows to force tied scores)."""
     rng = np.random.default_rng(seed)
     model = O.MoeModel(D, F, E, K, score_fn=score_fn, score_bias=score_bias, n_group=n_group,
                        topk_group=topk_group, norm_topk_prob=norm, routed_scale=routed_scale,
@@ -58,6 +59,8 @@ def build_pair(seed, *, L=1, D=256, F=128, E=16, K=4, score_fn=0, score_bias=0, 
                        policy=policy)
     for l in range(L):
         router = (rng.standard_normal((E, D)) * router_sigma).astype(np.float32)
+        if router_fn is not None:
+            router = np.ascontiguousarray(router_fn(router), np.float32)
         bias = (rng.standard_normal(E) * 0.05).astype(np.float32) if score_bias else None
         norm_w = (1.0 + 0.1 * rng.standard_normal(D)).astype(np.float32)
         slabs = [make_slab(rng, D, F) for _ in range(E)]

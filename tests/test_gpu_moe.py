@@ -177,6 +177,32 @@ def test_persistent_decode_equals_oracle(gpu, case):
     assert ids.shape == (1, kw["K"])
 
 
+@pytest.mark.parametrize("score_fn", [0, 1])
+def test_persistent_decode_tied_scores(gpu, score_fn):
+    """Duplicated router rows give bit-identical scores; the persistent kernel's selection breaks the
+    ties by expert index exactly like the reference (lower index first), across its scoring warps."""
+    E, K = 96, 8
+
+    def tie(router):
+        r = router.copy()
+        for dst in (5, 40, 70, 95):      # a tie group spread over the four scoring warps, pushed up
+            r[dst] = r[3]
+        r[[3, 5, 40, 70, 95]] *= 4.0
+        r[[12, 44]] = r[60]                # a second group, elsewhere in the order
+        return r
+
+    model, be = build_pair(51, L=2, D=512, F=256, E=E, K=K, score_fn=score_fn, max_tokens=1, router_fn=tie)
+    rng = np.random.default_rng(8)
+    with be:
+        assert be.decode_path() == "persistent"
+        for _ in range(4):
+            h = rng.standard_normal((1, 512)).astype(np.float32)
+            assert np.array_equal(bits(be.forward(h)), bits(model.forward(h)))
+            ids, _ = be.last_routing(1)
+            tied = [e for e in ids[0] if e in (3, 5, 40, 70, 95)]
+            assert tied == sorted(tied)
+
+
 def test_persistent_decode_qwen3_shape_matches_multi_kernel_path(gpu, monkeypatch):
     """Qwen3-30B-A3B layer shape (D 2048, F 768, 128 experts, top-8), 2 layers: the persistent kernel,
     the multi-kernel path and the oracle agree bit for bit, and so does the last layer's routing."""
