@@ -196,8 +196,10 @@ def run_ours(args, rank, world, local_rank):
     P = 64
     g = torch.Generator(device=dev).manual_seed(1000 + rank)
     pool = torch.randn((P, B, D_), generator=g, device=dev, dtype=torch.float32)
+    # kernels and events on one stream: the torch stream object (its default stream is passed to the
+    # library as the legacy default stream, not as "the library's own stream")
     stream = torch.cuda.current_stream(dev)
-    sp = stream.cuda_stream
+    sp = stream
     for i in range(max(args.warmup, 3)):
         be.forward_dev(pool[i % P], B, stream=sp)
     for i in range(P):                                   # every pool slot's graph exists before timing

@@ -22,6 +22,20 @@ def _ptr(a):
     return C.c_void_p(a.ctypes.data)
 
 
+_CUDA_STREAM_LEGACY = 1   # cudaStreamLegacy: the legacy default stream, as a stream handle
+
+
+def _stream(s):
+    """Stream argument of the *_dev calls. None or 0: the library's own stream. A torch.cuda.Stream:
+    that stream (torch's default stream maps to the legacy default stream, so the work orders with
+    what torch issues there). Anything else: a raw cudaStream_t handle."""
+    if s is None:
+        return C.c_void_p(0)
+    if hasattr(s, "cuda_stream"):
+        return C.c_void_p(s.cuda_stream or _CUDA_STREAM_LEGACY)
+    return C.c_void_p(int(s))
+
+
 class MoeBackend:
     """One MoE stack (n_layers layers of the same shape) on one CUDA device."""
 
@@ -97,12 +111,12 @@ class MoeBackend:
         """h: device buffer (torch tensor or raw pointer) of [T, D] float32, updated in place."""
         n_layers = self.n_layers - layer0 if n_layers is None else n_layers
         hp = _ptr(h) if hasattr(h, "data_ptr") else C.c_void_p(int(h))
-        check(lib().hxb_moe_forward_dev(self.h, hp, T, layer0, n_layers, C.c_void_p(stream or 0)),
+        check(lib().hxb_moe_forward_dev(self.h, hp, T, layer0, n_layers, _stream(stream)),
               "hxb_moe_forward_dev")
 
     def sync(self, stream=None) -> None:
         """Waits for the stream of the *_dev calls and raises on a device-side error."""
-        check(lib().hxb_moe_sync(self.h, C.c_void_p(stream or 0)), "hxb_moe_sync")
+        check(lib().hxb_moe_sync(self.h, _stream(stream)), "hxb_moe_sync")
 
     def decode_path(self) -> str:
         """Kernel of a single-token forward over every layer: "layers" (per-phase kernels) or
@@ -123,7 +137,7 @@ class MoeBackend:
         return out
 
     def layer_dev(self, layer: int, x, out, T: int, stream=None) -> None:
-        check(lib().hxb_moe_layer_dev(self.h, layer, _ptr(x), T, _ptr(out), C.c_void_p(stream or 0)),
+        check(lib().hxb_moe_layer_dev(self.h, layer, _ptr(x), T, _ptr(out), _stream(stream)),
               "hxb_moe_layer_dev")
 
     def last_routing(self, T: int):

@@ -66,3 +66,20 @@ def test_open_rejects_bad_config():
         args.update(kw)
         with pytest.raises(RuntimeError):
             hb.MoeBackend(**args)
+
+
+def test_stream_argument_mapping():
+    """None / 0 select the library's own stream; a torch stream object is used as given, and torch's
+    default stream (handle 0) becomes the legacy default stream, so events recorded on it bracket
+    the library's kernels."""
+    from hearth_b200.moe import _stream
+
+    class FakeStream:
+        def __init__(self, h):
+            self.cuda_stream = h
+
+    assert _stream(None).value in (None, 0)
+    assert _stream(0).value in (None, 0)
+    assert _stream(FakeStream(0)).value == 1
+    assert _stream(FakeStream(0x1234)).value == 0x1234
+    assert _stream(0x5678).value == 0x5678
