@@ -46,6 +46,12 @@ def algorithmic_bytes():
                 layer=K_ * expert + router + D_ * 4, expert=expert)
 
 
+# DRAM bytes (read + write) per layer of k_moe_decode from one ncu capture of a 4-layer launch of the
+# same shape (bench.py --layers 4: dram__bytes_read.sum 94.62 MB, dram__bytes_write.sum 2.69 MB); a
+# launch's traffic grows with its layers, so the full launch's figure is this times its layers.
+DECODE_DRAM_BYTES_PER_LAYER = (94_621_952 + 2_688_000) / 4
+
+
 def peaks():
     p = os.path.join(REPO, "MEASURED_PEAKS.json")
     if os.path.exists(p):
@@ -183,6 +189,46 @@ def run_reference(args, rank, world):
     ref.close()
 
 
+TRACE_STAMPS = ["start", "h polled", "rmsnorm chain", "router rows in", "x", "logit stored", "activation blocks",
+                "predicted-logit partial", "logits polled", "routed", "routing barrier", "first chunk landed",
+                "its SwiGLU stored", "exchange reset", "mid polled", "mid blocks", "down rows landed",
+                "down rows computed", "y stored", "y polled", "h stored"]
+
+
+def run_trace(args, local_rank):
+    """Per-phase timeline of the persistent decode kernel (one JSON line): for each stamp, the mean and
+    the per-layer maximum over CTAs of the interval from the previous stamp, in us at the SM clock."""
+    os.environ["HXB_TRACE"] = "1"
+    import torch
+    import hearth_b200 as hb
+    torch.cuda.set_device(local_rank)
+    be = hb.MoeBackend(n_layers=L_, d_model=D_, expert_ffn_dim=F_, n_experts=E_, top_k=K_, score_fn=0,
+                       norm_topk_prob=1, max_tokens=1, device=local_rank)
+    be.synthesize(SEED, SIGMA, SIGMA)
+    g = torch.Generator(device="cuda").manual_seed(1000)
+    pool = torch.randn((64, 1, D_), generator=g, device="cuda")
+    s = torch.cuda.current_stream()
+    for i in range(max(args.warmup, 3) + 64):
+        be.forward_dev(pool[i % 64], 1, stream=s)
+    be.sync(s)
+    t = be.phase_trace()
+    S = len(TRACE_STAMPS)
+    t = t.reshape(L_, -1, S).astype(np.int64)
+    mhz = 1965.0
+    try:
+        out = subprocess.run(["nvidia-smi", "-i", str(local_rank), "--query-gpu=clocks.max.sm",
+                              "--format=csv,noheader,nounits"], capture_output=True, text=True, timeout=10)
+        mhz = float(out.stdout.strip().splitlines()[0])
+    except Exception:
+        pass
+    d = np.diff(t, axis=2) / mhz
+    phases = {TRACE_STAMPS[i + 1]: {"mean_us": round(float(d[:, :, i].mean()), 3),
+                                    "max_us": round(float(d[:, :, i].max(axis=1).mean()), 3)} for i in range(S - 1)}
+    layer = (t[:, :, S - 1] - t[:, :, 0]) / mhz
+    print(json.dumps({"trace": "k_moe_decode phases", "layers": L_, "ctas": int(t.shape[1]), "clock_mhz": mhz,
+                      "layer_us_mean": round(float(layer.mean()), 3), "phases": phases}), flush=True)
+
+
 def run_ours(args, rank, world, local_rank):
     import torch
     import hearth_b200 as hb
@@ -296,7 +342,10 @@ def run_ours(args, rank, world, local_rank):
                        "batch": B, "parallelism": f"replica x{world}",
                        "l2": "no flush: each step reads ~1.01 GB of expert/router weights (> 126 MB L2)"},
             "roofline": {"bound": "hbm", "achieved": round(kgbs, 1), "peak": hbm, "unit": "GB/s",
-                         "frac": round(kgbs / hbm, 4), "traffic": None,
+                         "frac": round(kgbs / hbm, 4),
+                         "traffic": round(DECODE_DRAM_BYTES_PER_LAYER * L_) if persistent else None,
+                         "traffic_note": ("ncu dram bytes of a 4-layer capture scaled to the launch's layers"
+                                          if persistent else None),
                          "kernel": kernel, "peak_kind": peak_kind,
                          "multi_kernel_stage_us": {"norm_act": round(us[0], 3), "router": round(us[1], 3),
                                                    "gateup": round(us[2], 3), "down": round(us[3], 3)},
@@ -326,6 +375,9 @@ def main():
     ap.add_argument("--layers", type=int, default=48, help="MoE layers (48 = the Qwen3-30B-A3B stack); fewer only "
                                                             "for small profiling captures")
     ap.add_argument("--no-cpu", action="store_true", help="skip the CPU baseline leg")
+    ap.add_argument("--trace", action="store_true",
+                    help="instead of the bench line: the persistent kernel's per-phase timeline (mean us per "
+                         "layer over CTAs, thread 0's SM clock) as one JSON line")
     args = ap.parse_args()
     L_ = args.layers
     rank, world, local_rank = dist_env()
@@ -337,7 +389,10 @@ def main():
         dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=300),
                                 device_id=torch.device("cuda", local_rank))
     try:
-        if args.impl == "reference":
+        if args.trace:
+            if rank == 0:
+                run_trace(args, local_rank)
+        elif args.impl == "reference":
             run_reference(args, rank, world)
         else:
             run_ours(args, rank, world, local_rank)

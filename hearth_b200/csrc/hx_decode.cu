@@ -46,8 +46,13 @@ constexpr uint32_t kPollLimit = 1u << 18;   // polls of one word before giving u
 enum : int { DEV_E_POLL = 4 };             // an exchange word never arrived
 
 // Phase stamps of the optional timeline (thread 0 of every CTA, per layer).
-enum : int { ST_START, ST_H, ST_NORM, ST_ROUTER, ST_LG, ST_ROUTE, ST_GATEUP, ST_MID, ST_DOWN, ST_Y, ST_SUM,
-             DEC_STAMPS };
+// ST_H h polled; ST_RMS rmsnorm chain done; ST_NORM router rows in, barrier; ST_X x; ST_LOGIT logit
+// stored; ST_ACT activation blocks; ST_PRED predicted-logit partial; ST_LG logits polled; ST_RT
+// routed; ST_ROUTE barrier after routing; ST_CH0 thread 0's chunk landed; ST_CHD its SwiGLU values
+// stored; ST_RESET other set's slots reset; ST_MIDP mid polled; ST_MIDQ mid blocks; ST_DNW down rows
+// landed; ST_DOWN down rows computed; ST_YST y stored; ST_Y y polled; ST_SUM h stored.
+enum : int { ST_START, ST_H, ST_RMS, ST_NORM, ST_X, ST_LOGIT, ST_ACT, ST_PRED, ST_LG, ST_RT, ST_ROUTE, ST_CH0,
+             ST_CHD, ST_RESET, ST_MIDP, ST_MIDQ, ST_DNW, ST_DOWN, ST_YST, ST_Y, ST_SUM, DEC_STAMPS };
 
 // Next-layer prefetch: each CTA c < E also computes router[l+1][c] . (h_l * rms(h_l) * ffn_norm[l+1])
 // in any summation order (it only steers the prefetch); an idle warp of every CTA takes the K
@@ -452,6 +457,7 @@ __device__ void decode_body(const DecodeArgs &a, uint8_t *smem) {
             }
             L = tree16(L, 0xffffffffu);
             if (lane == 0) rms_r = __fdiv_rn(1.0f, __fsqrt_rn(__fadd_rn(__fdiv_rn(L, (float)D), a.eps)));
+            HX_STAMP(ST_RMS);
         }
         mbar_wait(&bars[BAR_ROUTER], par, a.err);
         __syncthreads();
@@ -461,6 +467,7 @@ __device__ void decode_body(const DecodeArgs &a, uint8_t *smem) {
             for (int i = tid; i < D; i += DEC_THREADS) xs[i] = __fmul_rn(__fmul_rn(hs[i], r), normv[i]);
         }
         __syncthreads();
+        HX_STAMP(ST_X);
         {   // router rows first (the logits are on every CTA's path): one 16-lane group each
             const int t = tid >> 4, j = tid & 15;
             const bool active = t < pl.rpc && c + t * G < E;
@@ -475,7 +482,9 @@ __device__ void decode_body(const DecodeArgs &a, uint8_t *smem) {
                 if (active && j == 0) st_x(xlg(l) + c + t * G, canon(L));
             }
         }
+        HX_STAMP(ST_LOGIT);
         for (int b = warp; b < ly.nbD; b += DEC_WARPS) act_quant_warp(xs[b * QK + lane], xs[b * QK + lane + 32], xact + b, lane);
+        HX_STAMP(ST_ACT);
         if (predict && c < E) {   // partial of the predicted logit (every thread, any order)
             float sum = 0.0f;
 #pragma unroll
@@ -491,7 +500,7 @@ __device__ void decode_body(const DecodeArgs &a, uint8_t *smem) {
             for (int o = 16; o >= 1; o >>= 1) sum += __shfl_xor_sync(0xffffffffu, sum, o);
             if (lane == 0) pred_part[warp] = sum;
         }
-        HX_STAMP(ST_ROUTER);
+        HX_STAMP(ST_PRED);
 
         // ---------------- P2: logits, routing, copies in flight
         poll_vec(xlg(l), lgs, E, a.err);
@@ -508,6 +517,7 @@ __device__ void decode_body(const DecodeArgs &a, uint8_t *smem) {
         } else if (warp == 0) {
             route_token_warp1<true>(a.route, lgs, p_bias[l], lgs, rkey, score, sel, gscr, gkeep, ids, wts);
         }
+        HX_STAMP(ST_RT);
         __syncthreads();
         if (warp == kIssueWarp) {   // a warp without a chunk (when nch_c < 16): the others start at once
             fence_proxy_async();
@@ -547,9 +557,11 @@ __device__ void decode_body(const DecodeArgs &a, uint8_t *smem) {
         for (int q = warp; q < nch_c; q += DEC_WARPS) {
             const int g = ch0 + q, j = g / cpe, p = g - j * cpe;
             if (mbar_wait(&bars[q], par, a.err)) {
+                if (q == 0) HX_STAMP(ST_CH0);
                 warp_rows_1tok<DT>(gu + (size_t)q * 2 * chunk_bytes, ly.rbD, ly.nbD, 2 * DEC_CH, xact, P, gout);
                 if (lane < DEC_CH)
                     st_x(xmid(l, j) + p * DEC_CH + lane, canon(swiglu_c(gout[lane], gout[DEC_CH + lane])));
+                if (q == 0) HX_STAMP(ST_CHD);
             }
         }
         if (predict && warp == kIssueWarp && nch_c <= kIssueWarp) {
@@ -576,22 +588,25 @@ __device__ void decode_body(const DecodeArgs &a, uint8_t *smem) {
                         s0[i] = __uint_as_float(kEmpty);
                 }
         }
-        HX_STAMP(ST_GATEUP);
+        HX_STAMP(ST_RESET);
 
         // ---------------- P4: expert jd's mid -> activation blocks -> this CTA's down rows -> y exchange
         poll_vec(xmid(l, jd), mids, F, a.err);
         __syncthreads();
+        HX_STAMP(ST_MIDP);
         for (int b = warp; b < ly.nbF; b += DEC_WARPS) act_quant_warp(mids[b * QK + lane], mids[b * QK + lane + 32], amid + b, lane);
         __syncthreads();
-        HX_STAMP(ST_MID);
+        HX_STAMP(ST_MIDQ);
         {
             const bool ok = mbar_wait(&bars[BAR_DOWN], par, a.err);
+            HX_STAMP(ST_DNW);
             for (int r0 = warp * DEC_PROWS; r0 < ndr && ok; r0 += DEC_WARPS * DEC_PROWS)
                 warp_rows_1tok<DT>(dn + (size_t)r0 * ly.rbF, ly.rbF, ly.nbF, min(DEC_PROWS, ndr - r0), amid, P, Ys + r0);
         }
         __syncthreads();
-        for (int r = tid; r < ndr; r += DEC_THREADS) st_x(xy(l, jd) + dr0 + r, Ys[r]);
         HX_STAMP(ST_DOWN);
+        for (int r = tid; r < ndr; r += DEC_THREADS) st_x(xy(l, jd) + dr0 + r, Ys[r]);
+        HX_STAMP(ST_YST);
 
         // ---------------- P5: y of the K experts for this CTA's h rows -> rank-order sum -> residual
         for (int i = tid; i < K * nhr; i += DEC_THREADS) {

@@ -123,6 +123,18 @@ class MoeBackend:
         "persistent" (one launch for all layers)."""
         return ("layers", "persistent")[lib().hxb_moe_decode_path(self.h)]
 
+    def phase_trace(self):
+        """Phase timeline of the last single-token persistent launch (handle opened with the
+        environment variable HXB_TRACE=1): uint64 array [layers, CTAs, stamps] of SM clock cycles,
+        or None when not tracing."""
+        n = lib().hxb_moe_phase_trace(self.h, None, 0)
+        if n <= 0:
+            return None
+        buf = np.zeros(n, np.uint64)
+        if lib().hxb_moe_phase_trace(self.h, C.c_void_p(buf.ctypes.data), n) != n:
+            raise RuntimeError("hxb_moe_phase_trace failed")
+        return buf
+
     def profile(self, T: int = 1, iters: int = 3) -> list:
         """Average device microseconds per stage of one layer: [norm+act, router, gate/up, down]."""
         us = (C.c_double * 4)()

@@ -152,9 +152,11 @@ HXB_API int hxb_moe_sync(hxb_moe *m, void *stream);
  * router + routing, us[2] gate/up + SwiGLU + mid activations, us[3] down + rank-order sum. */
 HXB_API int hxb_moe_profile(hxb_moe *m, int T, int iters, double *us);
 /* Phase timeline of the last single-token persistent launch, for handles opened with the
- * environment variable HXB_TRACE=1: out[layer][cta][stamp] SM clock cycles (per-SM counter: compare
- * stamps of one CTA only; stamps: start, norm,
- * router, barrier 1, routing, gate/up, mid blocks, barrier 2, down, sum, barrier 3). Returns the
+ * environment variable HXB_TRACE=1: out[layer][cta][stamp] SM clock cycles of thread 0 (per-SM
+ * counter: compare stamps of one CTA only). 21 stamps per layer, in order: start, h polled, rmsnorm
+ * chain, router rows in, x, logit stored, activation blocks, predicted-logit partial, logits polled,
+ * routed, routing barrier, first gate/up chunk landed, its SwiGLU values stored, exchange reset, mid
+ * polled, mid blocks, down rows landed, down rows computed, y stored, y polled, h stored. Returns the
  * number of values (call with out = NULL to size the buffer), 0 when not tracing. */
 HXB_API int64_t hxb_moe_phase_trace(hxb_moe *m, uint64_t *out, int64_t max_values);
 /* Which kernel evaluates a single-token forward over every layer (every expert resident):
