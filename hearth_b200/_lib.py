@@ -27,6 +27,7 @@ EXPORTS = [
     "hxb_moe_layer_dev", "hxb_moe_last_routing", "hxb_moe_get_stats", "hxb_moe_reset_stats",
     "hxb_moe_is_resident", "hxb_moe_tick", "hxb_moe_prefetch", "hxb_moe_seed_heat", "hxb_moe_set_copy_hook",
     "hxb_moe_sync", "hxb_moe_profile", "hxb_matmul_noalloc", "hxb_moe_phase_trace", "hxb_moe_decode_path",
+    "hxb_moe_ep_layer_dev", "hxb_moe_ep_combine_dev",
 ]
 
 
@@ -37,7 +38,7 @@ class MoeConfig(C.Structure):
                 ("residual_scale", C.c_float), ("norm_eps", C.c_float), ("expert_dtype", C.c_int),
                 ("shared_ffn_dim", C.c_int), ("shared_dtype", C.c_int), ("shared_gate", C.c_int),
                 ("max_tokens", C.c_int), ("cache_gb", C.c_double), ("policy", C.c_int), ("heat_decay", C.c_float),
-                ("device", C.c_int)]
+                ("device", C.c_int), ("ep_size", C.c_int), ("ep_rank", C.c_int)]
 
 
 class MoeStats(C.Structure):
@@ -97,6 +98,8 @@ def lib() -> C.CDLL:
         "hxb_matmul_noalloc": (i, [i, vp, i64, i64, vp, i, vp, vp]),
         "hxb_moe_phase_trace": (i64, [vp, vp, i64]),
         "hxb_moe_decode_path": (C.c_int, [vp]),
+        "hxb_moe_ep_layer_dev": (i, [vp, i, vp, i, vp, vp]),
+        "hxb_moe_ep_combine_dev": (i, [vp, i, vp, i, vp, vp]),
     }
     for name, (res, args) in sig.items():
         fn = getattr(L, name)

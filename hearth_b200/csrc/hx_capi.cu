@@ -233,6 +233,7 @@ struct hxb_moe {
     hxb_moe_stats st{};
     int last_T = 0;
     // persistent single-token decode kernel (every expert resident)
+    DevBuf ujob, nu_job;                 // expert parallelism: this rank's buckets
     bool use_decode = false, dec_dirty = true;
     DevBuf dec_router, dec_norm, dec_bias;
     DevBuf dec_xbuf, dec_epoch;          // exchange buffers (two sets) and the launch counter
@@ -255,6 +256,8 @@ struct hxb_moe {
         s.act_mid = act_mid.as<act_q8>();
         s.Y = Y.as<float>();
         s.S = S.as<float>();
+        s.ujob = ujob.as<int>();
+        s.nu_job = nu_job.as<int>();
         s.ticket = ticket.as<unsigned>();
         s.err = err.as<int>();
         return s;
@@ -277,7 +280,16 @@ struct hxb_moe {
         sh.route.topk_group = cfg.topk_group;
         sh.route.norm_topk_prob = cfg.norm_topk_prob;
         sh.route.routed_scale = cfg.routed_scale;
+        sh.ep_size = cfg.ep_size;
+        sh.ep_rank = cfg.ep_rank;
         return sh;
+    }
+
+    bool owns(int e) const { return e % cfg.ep_size == cfg.ep_rank; }
+    int owned_experts() const {
+        int n = 0;
+        for (int e = 0; e < cfg.n_experts; e++) n += owns(e) ? 1 : 0;
+        return n;
     }
 
     MoeLayerDev layer_dev(int l, bool with_norm) const {
@@ -328,6 +340,8 @@ extern "C" HXB_API void hxb_moe_default_config(hxb_moe_config *c) {
     c->cache_gb = 0.0;
     c->policy = POLICY_LFU;
     c->heat_decay = 0.995f;
+    c->ep_size = 1;
+    c->ep_rank = 0;
 }
 
 static void set_errbuf(char *err, size_t errlen, const std::string &msg) {
@@ -355,6 +369,8 @@ extern "C" HXB_API hxb_moe *hxb_moe_open(const hxb_moe_config *c, char *err, siz
     else if (k.n_group > 1 && (k.n_experts % k.n_group || k.n_group > 32 || k.topk_group < 1 || k.topk_group > k.n_group))
         why = "bad expert grouping";
     else if (k.max_tokens <= 0 || k.max_tokens > 8192) why = "max_tokens must be 1..8192";
+    else if (k.ep_size < 1 || k.ep_size > 64 || k.ep_rank < 0 || k.ep_rank >= k.ep_size || k.ep_size > k.n_experts)
+        why = "expert parallelism: need 1 <= ep_size <= min(64, n_experts) and 0 <= ep_rank < ep_size";
     if (!why.empty()) {
         set_errbuf(err, errlen, "hxb_moe_open: " + why);
         return nullptr;
@@ -371,12 +387,13 @@ extern "C" HXB_API hxb_moe *hxb_moe_open(const hxb_moe_config *c, char *err, siz
     m->slab_bytes = (size_t)m->lay.nbytes;
     const int L = k.n_layers, E = k.n_experts, D = k.d_model, T = k.max_tokens, K = k.top_k;
     const int64_t nkeys = (int64_t)L * E;
-    int64_t n_slots = nkeys;
+    const int64_t owned_keys = (int64_t)L * m->owned_experts();   // all keys without expert parallelism
+    int64_t n_slots = owned_keys;
     if (k.cache_gb > 0.0) {
         const int64_t by_budget = (int64_t)(k.cache_gb * 1073741824.0 / (double)m->slab_bytes);
-        n_slots = std::min<int64_t>(nkeys, std::max<int64_t>(by_budget, (int64_t)E + 2));
+        n_slots = std::min<int64_t>(owned_keys, std::max<int64_t>(by_budget, (int64_t)E + 2));
     }
-    m->resident_mode = n_slots >= nkeys;
+    m->resident_mode = n_slots >= owned_keys;
     if (cudaStreamCreateWithFlags(&m->stream, cudaStreamNonBlocking) != cudaSuccess) {
         set_errbuf(err, errlen, "hxb_moe_open: cannot create a stream");
         return nullptr;
@@ -396,7 +413,9 @@ extern "C" HXB_API hxb_moe *hxb_moe_open(const hxb_moe_config *c, char *err, siz
               m->pair_tok.alloc(sizeof(int) * P) && m->pair_of.alloc(sizeof(int) * P) &&
               m->act_mid.alloc((P + (size_t)T) * (size_t)(Fmax / QK) * ACT_BLOCK) &&
               m->Y.alloc(P * kFusedMaxPairs > 0 && (int)P > kFusedMaxPairs ? sizeof(float) * P * D : 16) &&
-              m->S.alloc(k.shared_ffn_dim && (int)P > kFusedMaxPairs ? sizeof(float) * (size_t)T * D : 16) &&
+              m->S.alloc(k.shared_ffn_dim && ((int)P > kFusedMaxPairs || k.ep_size > 1) ? sizeof(float) * (size_t)T * D
+                                                                                          : 16) &&
+              m->ujob.alloc(sizeof(int) * (size_t)E) && m->nu_job.alloc(sizeof(int) * 4) &&
               m->ticket.alloc(64) && m->err.alloc(64) && m->hbuf.alloc(sizeof(float) * (size_t)T * D) &&
               m->obuf.alloc(sizeof(float) * (size_t)T * D);
     ok = ok && cudaHostAlloc((void **)&m->hpin, sizeof(float) * (size_t)T * D, cudaHostAllocDefault) == cudaSuccess;
@@ -413,7 +432,7 @@ extern "C" HXB_API hxb_moe *hxb_moe_open(const hxb_moe_config *c, char *err, siz
         // HXB_PERSISTENT=0: per-phase kernels only
         const char *env = std::getenv("HXB_PERSISTENT");
         std::string why_not;
-        const bool off = env && env[0] == '0';
+        const bool off = (env && env[0] == '0') || k.ep_size > 1;
         m->use_decode = !off &&
                         decode_supported(D, k.expert_ffn_dim, E, K, k.expert_dtype, k.shared_ffn_dim > 0, &why_not);
         if (m->use_decode) {
@@ -501,6 +520,7 @@ extern "C" HXB_API int hxb_moe_set_expert(hxb_moe *m, int layer, int expert, con
     if (!m || layer < 0 || layer >= m->cfg.n_layers || expert < 0 || expert >= m->cfg.n_experts || !slab ||
         nbytes < (size_t)m->lay.end || nbytes > m->slab_bytes)
         return fail(HXB_E_ARG, "set_expert: bad arguments (slab must be %zu bytes)", m ? m->slab_bytes : (size_t)0);
+    if (!m->owns(expert)) return HXB_OK;   // expert parallelism: another rank's expert, not held here
     cudaSetDevice(m->device);
     std::string why;
     if (!m->store.set_source(layer, expert, slab, nbytes, why)) return fail(HXB_E_NOMEM, "set_expert: %s", why.c_str());
@@ -542,20 +562,30 @@ extern "C" HXB_API int hxb_moe_synthesize(hxb_moe *m, uint64_t seed, float sigma
         cudaMemcpy(b.norm.p, ones.data(), sizeof(float) * D, cudaMemcpyHostToDevice);
         b.set = true;
         for (int e = 0; e < E; e++) {
+            if (!m->owns(e)) continue;
             uint8_t *p = m->store.place_resident(l, e);
             if (!p) return fail(HXB_E_NOMEM, "synthesize: no slot");
             m->host_table[(size_t)l * E + e] = p;
         }
     }
-    // slots were handed out in order, so the L*E slabs are contiguous: one launch fills them all
-    const uint8_t *base = m->host_table[0];
-    for (int64_t i = 0; i < (int64_t)L * E; i++)
-        if (m->host_table[i] != base + (size_t)i * m->slab_bytes)
-            return fail(HXB_E_ARG, "synthesize: expert slots are not contiguous (experts were set before)");
-    if (!cuda_ok(launch_synth_q4(const_cast<uint8_t *>(base), (int64_t)L * E, (int64_t)m->slab_bytes, D,
-                                 k.expert_ffn_dim, seed, sigma_expert, m->stream),
-                 "synth experts"))
-        return HXB_E_DEVICE;
+    if (k.ep_size > 1) {   // this rank's slabs, each the bytes of its place in the whole sequence
+        for (int64_t i = 0; i < (int64_t)L * E; i++)
+            if (m->owns((int)(i % E)) &&
+                !cuda_ok(launch_synth_q4(const_cast<uint8_t *>(m->host_table[i]), 1, (int64_t)m->slab_bytes, D,
+                                         k.expert_ffn_dim, seed, sigma_expert, m->stream, i),
+                         "synth experts"))
+                return HXB_E_DEVICE;
+    } else {
+        // slots were handed out in order, so the L*E slabs are contiguous: one launch fills them all
+        const uint8_t *base = m->host_table[0];
+        for (int64_t i = 0; i < (int64_t)L * E; i++)
+            if (m->host_table[i] != base + (size_t)i * m->slab_bytes)
+                return fail(HXB_E_ARG, "synthesize: expert slots are not contiguous (experts were set before)");
+        if (!cuda_ok(launch_synth_q4(const_cast<uint8_t *>(base), (int64_t)L * E, (int64_t)m->slab_bytes, D,
+                                     k.expert_ffn_dim, seed, sigma_expert, m->stream),
+                     "synth experts"))
+            return HXB_E_DEVICE;
+    }
     if (!cuda_ok(cudaMemcpyAsync(m->table.p, m->host_table, sizeof(void *) * (size_t)L * E, cudaMemcpyHostToDevice,
                                  m->stream),
                  "table"))
@@ -705,6 +735,8 @@ static void reset_decode_state(hxb_moe *m) {
 
 static int run_range(hxb_moe *m, float *h, float *out, int T, int l0, int nl, bool with_norm, bool resid,
                      cudaStream_t user, bool host_io, const float *hin, float *hout) {
+    if (m->cfg.ep_size > 1)
+        return fail(HXB_E_UNSUPPORTED, "an expert-parallel handle evaluates layers through hxb_moe_ep_*");
     cudaStream_t s = user ? user : m->stream;
     const size_t bytes = sizeof(float) * (size_t)T * m->cfg.d_model;
     const double t0 = now_s();
@@ -956,6 +988,40 @@ extern "C" HXB_API int hxb_moe_profile(hxb_moe *m, int T, int iters, double *us)
     int word = 0;
     cudaMemcpy(&word, m->err.p, sizeof word, cudaMemcpyDeviceToHost);
     return take_device_error(m, word);
+}
+
+// Expert parallelism, step 1: routing of every token and this rank's pairs' outputs into y.
+extern "C" HXB_API int hxb_moe_ep_layer_dev(hxb_moe *m, int layer, const float *h, int T, float *y, void *stream) {
+    if (!m || layer < 0 || layer >= m->cfg.n_layers || T <= 0 || T > m->cfg.max_tokens || !h || !y)
+        return fail(HXB_E_ARG, "ep_layer: bad arguments");
+    if (!m->layers[(size_t)layer].set) return fail(HXB_E_ARG, "ep_layer: layer %d has no weights", layer);
+    cudaSetDevice(m->device);
+    const int E = m->cfg.n_experts;
+    for (int e = 0; e < E; e++)
+        if (m->owns(e) && !m->host_table[(size_t)layer * E + e])
+            return fail(HXB_E_IO, "ep_layer: expert %d of layer %d is not in HBM", e, layer);
+    MoeScratch sc = m->scratch();
+    sc.Y = y;
+    const MoeShape sh = m->shape(T);
+    const MoeLayerDev L = m->layer_dev(layer, true);
+    if (!cuda_ok(launch_moe_layer(sh, L, sc, const_cast<float *>(h), nullptr, false, (cudaStream_t)stream),
+                 "ep layer"))
+        return HXB_E_DEVICE;
+    m->st.expert_uses += (uint64_t)T * m->cfg.top_k;
+    return HXB_OK;
+}
+
+// Expert parallelism, step 2: rank-order sum over the gathered outputs, shared expert, residual.
+extern "C" HXB_API int hxb_moe_ep_combine_dev(hxb_moe *m, int layer, const float *y_all, int T, float *h,
+                                              void *stream) {
+    if (!m || layer < 0 || layer >= m->cfg.n_layers || T <= 0 || T > m->cfg.max_tokens || !h || !y_all)
+        return fail(HXB_E_ARG, "ep_combine: bad arguments");
+    cudaSetDevice(m->device);
+    if (!cuda_ok(launch_moe_ep_combine(m->shape(T), m->layer_dev(layer, true), m->scratch(), y_all, h,
+                                       (cudaStream_t)stream),
+                 "ep combine"))
+        return HXB_E_DEVICE;
+    return HXB_OK;
 }
 
 extern "C" HXB_API int hxb_moe_decode_path(const hxb_moe *m) {

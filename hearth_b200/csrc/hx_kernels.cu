@@ -282,6 +282,20 @@ __global__ void __launch_bounds__(512) k_route_union(MoeShape sh, MoeScratch sc)
     extern __shared__ int usm[];
     route_union_cta(sh.T, sh.route.K, sh.route.E, sc.ids, usm, usm + sh.route.E, sc.nu, sc.ulist, sc.u_p0,
                     sc.u_n, sc.pair_tok, sc.pair_of);
+    if (sh.ep_size > 1) {   // the buckets of this rank's experts, in bucket order
+        __syncthreads();
+        if (threadIdx.x == 0) {
+            int n = 0;
+            for (int u = 0; u < *sc.nu; u++)
+                if (sc.ulist[u] % sh.ep_size == sh.ep_rank) sc.ujob[n++] = u;
+            *sc.nu_job = n;
+        }
+    }
+}
+
+// Routed jobs of a launch: every bucket, or under expert parallelism this rank's buckets.
+__device__ __forceinline__ int routed_jobs(const MoeShape &sh, const MoeScratch &sc) {
+    return sh.ep_size > 1 ? *sc.nu_job : *sc.nu;
 }
 
 // =============================================================================================
@@ -299,6 +313,7 @@ struct Job {
 __device__ __forceinline__ bool get_job(const MoeShape &sh, const MoeLayerDev &L, const MoeScratch &sc, int u,
                                         int nu, Job &j) {
     if (u < nu) {
+        if (sh.ep_size > 1) u = sc.ujob[u];   // job -> bucket
         const int e = sc.ulist[u];
         const uint8_t *slab = L.slab[e];
         if (!slab) {
@@ -426,7 +441,7 @@ __device__ void gateup_body(const MoeShape &sh, const MoeScratch &sc, const Job 
 __global__ void __launch_bounds__(256) k_moe_gateup(MoeShape sh, MoeLayerDev L, MoeScratch sc, GateUpCfg c) {
     extern __shared__ __align__(128) uint8_t smem[];
     const int u = blockIdx.y, rb = blockIdx.x;
-    const int nu = *sc.nu;
+    const int nu = routed_jobs(sh, sc);
     const int njobs = nu + (L.Fs > 0 ? 1 : 0);
     if (u >= njobs) return;
     Job job;
@@ -497,7 +512,7 @@ __global__ void __launch_bounds__(256) k_moe_down(MoeShape sh, MoeLayerDev L, Mo
     extern __shared__ __align__(128) uint8_t smem[];
     const int tid = threadIdx.x, warp = tid >> 5;
     const int r0 = blockIdx.x * DN_ROWS;
-    const int nu = *sc.nu;
+    const int nu = routed_jobs(sh, sc);
     const int njobs = nu + (L.Fs > 0 ? 1 : 0);
     uint64_t *bars = reinterpret_cast<uint64_t *>(smem);
     uint8_t *ring = smem + 128;
@@ -572,6 +587,34 @@ __global__ void k_moe_sum(MoeShape sh, MoeLayerDev L, MoeScratch sc, float *h, f
                L.sh_gate_inp ? sc.sh_logit : nullptr, h, out, resid != 0);
 }
 
+// Expert-parallel combine: pair (t, j) of expert e comes from rank e % ep_size's slice of y_all.
+__global__ void k_moe_ep_combine(MoeShape sh, MoeLayerDev L, MoeScratch sc, const float *__restrict__ y_all,
+                                 float *h) {
+    const int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
+    if (i >= (int64_t)sh.T * sh.D) return;
+    const int t = (int)(i / sh.D), r = (int)(i - (int64_t)t * sh.D), K = sh.route.K;
+    const int64_t slice = (int64_t)sh.T * K * sh.D;
+    float o = 0.0f;   // rank-order sum (engine/src/model.c:904-923)
+    for (int j = 0; j < K; j++) {
+        const int owner = sc.ids[t * K + j] % sh.ep_size;
+        const float y = y_all[owner * slice + (int64_t)sc.pair_of[t * K + j] * sh.D + r];
+        o = __fadd_rn(o, __fmul_rn(sc.wts[t * K + j], y));
+    }
+    if (L.Fs > 0) {
+        float sv = sc.S[i];
+        if (L.sh_gate_inp) sv = __fmul_rn(sv, sigmoid_c(sc.sh_logit[t]));
+        o = __fadd_rn(o, sv);
+    }
+    h[i] = __fadd_rn(h[i], __fmul_rn(sh.residual_scale, o));
+}
+
+cudaError_t launch_moe_ep_combine(const MoeShape &sh, const MoeLayerDev &L, const MoeScratch &sc,
+                                  const float *y_all, float *h, cudaStream_t s) {
+    const int64_t n = (int64_t)sh.T * sh.D;
+    k_moe_ep_combine<<<(unsigned)((n + 255) / 256), 256, 0, s>>>(sh, L, sc, y_all, h);
+    return cudaGetLastError();
+}
+
 // =============================================================================================
 // Launch sequences.
 // =============================================================================================
@@ -582,7 +625,7 @@ static int fmax_nb_of(const MoeShape &sh, const MoeLayerDev &L) { return std::ma
 static void launch_route_stages(int which, const MoeShape &sh, const MoeLayerDev &L, const MoeScratch &sc,
                                 const float *h, cudaStream_t s) {
     const int T = sh.T, E = sh.route.E, K = sh.route.K;
-    const bool fused = T * K <= kFusedMaxPairs;
+    const bool fused = T * K <= kFusedMaxPairs && sh.ep_size == 1;
     if (which & 1) k_moe_norm_act<<<T, 256, 0, s>>>(h, L.ffn_norm, sh.eps, sh.D, sc.x, sc.xact);
     if (which & 2) {
         const int rows = E + (L.sh_gate_inp ? 1 : 0);
@@ -638,7 +681,7 @@ cudaError_t init_kernel_attributes() {
 static cudaError_t launch_expert_stages(int which, const MoeShape &sh, const MoeLayerDev &L, const MoeScratch &sc,
                                         float *h, float *out, bool resid, cudaStream_t s) {
     const int T = sh.T, K = sh.route.K, E = sh.route.E;
-    const bool fused = T * K <= kFusedMaxPairs;
+    const bool fused = T * K <= kFusedMaxPairs && sh.ep_size == 1;
     const size_t lim = smem_limit() - 1024;
     const int fmax_nb = fmax_nb_of(sh, L);
     // ---- gate/up + SwiGLU + mid activations
@@ -678,7 +721,7 @@ static cudaError_t launch_expert_stages(int which, const MoeShape &sh, const Moe
         if (c.nst < 1) return cudaErrorInvalidConfiguration;
         const size_t smem = fixed + (size_t)c.nst * c.stage;
         k_moe_down<<<(unsigned)(sh.D / DN_ROWS), 256, smem, s>>>(sh, L, sc, c, h, out, resid ? 1 : 0);
-        if (!fused) {
+        if (!fused && sh.ep_size == 1) {   // expert parallelism: the sum waits for the exchange
             const int64_t n = (int64_t)T * sh.D;
             k_moe_sum<<<(unsigned)((n + 255) / 256), 256, 0, s>>>(sh, L, sc, h, out, resid ? 1 : 0);
         }
@@ -722,7 +765,7 @@ __host__ __device__ inline uint64_t splitmix64(uint64_t z) {
 // nibbles follow a discretised Irwin-Hall(4) bell around 8, scales jitter around sigma/2.
 // One thread per 34-byte block; padding bytes of the slab stay zero.
 __global__ void k_synth_q4(uint8_t *dev, int64_t n_slabs, int64_t slab_bytes, int D, int F, uint64_t seed,
-                           uint32_t scale_bits) {
+                           uint32_t scale_bits, int64_t first_slab) {
     const slab_layout lay = make_slab_layout(Q4, D, F);
     const int64_t nb_gate = (int64_t)F * (D / QK);      // blocks in gate (and in up)
     const int64_t nb_down = (int64_t)D * (F / QK);
@@ -735,7 +778,7 @@ __global__ void k_synth_q4(uint8_t *dev, int64_t n_slabs, int64_t slab_bytes, in
     else if (b < 2 * nb_gate) off = lay.off_up + (b - nb_gate) * Q4_BLOCK;
     else off = lay.off_down + (b - 2 * nb_gate) * Q4_BLOCK;
     uint8_t *blk = dev + slab * slab_bytes + off;
-    uint64_t h = splitmix64(seed ^ splitmix64((uint64_t)i));
+    uint64_t h = splitmix64(seed ^ splitmix64((uint64_t)(i + first_slab * per_slab)));
     const uint32_t sc = scale_bits + (uint32_t)(h & 0x3f) - 32u;
     blk[0] = (uint8_t)(sc & 0xff);
     blk[1] = (uint8_t)(sc >> 8);
@@ -753,7 +796,7 @@ __global__ void k_synth_q4(uint8_t *dev, int64_t n_slabs, int64_t slab_bytes, in
 }
 
 cudaError_t launch_synth_q4(uint8_t *dev, int64_t n_slabs, int64_t slab_bytes, int D, int F, uint64_t seed,
-                            float sigma, cudaStream_t s) {
+                            float sigma, cudaStream_t s, int64_t first_slab) {
     // the f16 bits of sigma/2 (finite, normal for any sensible sigma)
     const float v = sigma * 0.5f;
     uint32_t fb;
@@ -763,7 +806,8 @@ cudaError_t launch_synth_q4(uint8_t *dev, int64_t n_slabs, int64_t slab_bytes, i
     const int64_t per_slab = 2 * (int64_t)F * (D / QK) + (int64_t)D * (F / QK);
     const int64_t n = n_slabs * per_slab;
     cudaMemsetAsync(dev, 0, (size_t)(n_slabs * slab_bytes), s);
-    k_synth_q4<<<(unsigned)((n + 255) / 256), 256, 0, s>>>(dev, n_slabs, slab_bytes, D, F, seed, scale_bits);
+    k_synth_q4<<<(unsigned)((n + 255) / 256), 256, 0, s>>>(dev, n_slabs, slab_bytes, D, F, seed, scale_bits,
+                                                          first_slab);
     return cudaGetLastError();
 }
 

@@ -45,6 +45,7 @@ struct MoeScratch {
     act_q8 *act_mid;     // [T*K + T, Fmax/64]
     float *Y;            // [T*K, D] per (token, rank) outputs (large batches)
     float *S;            // [T, D] shared expert output (large batches)
+    int *ujob, *nu_job;  // expert parallelism: buckets of this rank's experts [E], their count [1]
     unsigned *ticket;    // [1] last-CTA counter of moe_router (returns to 0 after every launch)
     int *err;            // [1] device error word
 };
@@ -67,6 +68,7 @@ struct MoeShape {
     int D, F, E, K, T;
     float eps, residual_scale;
     RouteCfg route;
+    int ep_size = 1, ep_rank = 0;   // expert parallelism: this rank computes experts e % ep_size == ep_rank
 };
 
 // Chooses the fused small-batch path (routing in moe_router's last CTA, sum in moe_down) when
@@ -83,6 +85,11 @@ cudaError_t launch_matmul(int dtype, const void *W, int64_t n_cols, const void *
                           int64_t ldy, int64_t r0, int64_t r1, cudaStream_t s);
 cudaError_t launch_dequantize(int dtype, const void *W, int64_t n_rows, int64_t n_cols, float *out,
                               cudaStream_t s);
+
+// Expert-parallel combine: h += rs * (rank-order sum over j of w_j * y_all[owner rank][pair(t, j)] +
+// shared output) with the routing and shared output of the preceding launch_moe_layer.
+cudaError_t launch_moe_ep_combine(const MoeShape &sh, const MoeLayerDev &L, const MoeScratch &sc,
+                                  const float *y_all, float *h, cudaStream_t s);
 
 // One MoE FFN. Input: h [T, D] (when L.ffn_norm is set, x = rmsnorm(h); otherwise x = h).
 // Output: if out != null, out [T, D] = rank-order expert sum (+ shared); if resid, h += rs * sum.
@@ -133,8 +140,10 @@ cudaError_t launch_moe_decode(const DecodeParams &p, cudaStream_t s);
 
 // Fills every expert slab of `n` slabs at dev with deterministic synthetic Q4 blocks (the
 // statistics of N(0, sigma) weights packed to Q4), for benchmarks without a container.
+// first_slab: index of dev's first slab in the generator's sequence (slab i's bytes depend only on
+// seed and i, so a subset of slabs can be generated anywhere).
 cudaError_t launch_synth_q4(uint8_t *dev, int64_t n_slabs, int64_t slab_bytes, int D, int F, uint64_t seed,
-                            float sigma, cudaStream_t s);
+                            float sigma, cudaStream_t s, int64_t first_slab = 0);
 cudaError_t launch_synth_f32(float *dev, int64_t n, uint64_t seed, float sigma, cudaStream_t s);
 
 // Device expf restatement over [x0, x0 + n) bit patterns (self-check support).

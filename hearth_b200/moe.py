@@ -44,7 +44,8 @@ class MoeBackend:
                  norm_topk_prob: int = 1, routed_scale: float = 1.0, residual_scale: float = 1.0,
                  norm_eps: float = 1e-6, expert_dtype: int = _lib.Q4, shared_ffn_dim: int = 0,
                  shared_dtype: int = _lib.Q8, shared_gate: int = 0, max_tokens: int = 1, cache_gb: float = 0.0,
-                 policy: int = _lib.POLICY_LFU, heat_decay: float = 0.995, device: int = 0):
+                 policy: int = _lib.POLICY_LFU, heat_decay: float = 0.995, device: int = 0, ep_size: int = 1,
+                 ep_rank: int = 0):
         L = lib()
         c = MoeConfig()
         L.hxb_moe_default_config(C.byref(c))
@@ -54,7 +55,7 @@ class MoeBackend:
                          residual_scale=residual_scale, norm_eps=norm_eps, expert_dtype=expert_dtype,
                          shared_ffn_dim=shared_ffn_dim, shared_dtype=shared_dtype, shared_gate=shared_gate,
                          max_tokens=max_tokens, cache_gb=cache_gb, policy=policy, heat_decay=heat_decay,
-                         device=device).items():
+                         device=device, ep_size=ep_size, ep_rank=ep_rank).items():
             setattr(c, k, v)
         err = C.create_string_buffer(512)
         h = L.hxb_moe_open(C.byref(c), err, 512)
@@ -64,6 +65,7 @@ class MoeBackend:
         self.cfg = c
         self.D, self.F, self.E, self.K = d_model, expert_ffn_dim, n_experts, top_k
         self.n_layers = n_layers
+        self.ep_size, self.ep_rank = ep_size, ep_rank
         self._hook = None
 
     # ------------------------------------------------------------------ weights
@@ -117,6 +119,21 @@ class MoeBackend:
     def sync(self, stream=None) -> None:
         """Waits for the stream of the *_dev calls and raises on a device-side error."""
         check(lib().hxb_moe_sync(self.h, _stream(stream)), "hxb_moe_sync")
+
+    # ------------------------------------------------------------------ expert parallelism
+    def owns(self, expert: int) -> bool:
+        """This handle holds and computes `expert` (expert e lives on rank e % ep_size)."""
+        return expert % self.ep_size == self.ep_rank
+
+    def ep_layer_dev(self, layer: int, h, T: int, y, stream=None) -> None:
+        """Expert parallelism, step 1: routing of the T tokens of h [T, D] and the outputs of this
+        rank's (token, rank) pairs into y [T*K, D] (device buffers); see hxb_moe_ep_layer_dev."""
+        check(lib().hxb_moe_ep_layer_dev(self.h, layer, _ptr(h), T, _ptr(y), _stream(stream)), "hxb_moe_ep_layer_dev")
+
+    def ep_combine_dev(self, layer: int, y_all, T: int, h, stream=None) -> None:
+        """Expert parallelism, step 2: h += rs * rank-order sum over y_all [ep_size, T*K, D]."""
+        check(lib().hxb_moe_ep_combine_dev(self.h, layer, _ptr(y_all), T, _ptr(h), _stream(stream)),
+              "hxb_moe_ep_combine_dev")
 
     def decode_path(self) -> str:
         """Kernel of a single-token forward over every layer: "layers" (per-phase kernels) or

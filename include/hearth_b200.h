@@ -104,6 +104,8 @@ typedef struct hxb_moe_config {
     int policy;            /* HEARTH_POLICY_LRU (0) / HEARTH_POLICY_LFU (1) */
     float heat_decay;      /* LFU per-token decay (default 0.995) */
     int device;            /* CUDA device ordinal */
+    int ep_size, ep_rank;  /* expert parallelism: this handle holds and computes the experts e with
+                              e % ep_size == ep_rank (default 1, 0: every expert) */
 } hxb_moe_config;
 
 typedef struct hxb_moe_stats {
@@ -159,6 +161,20 @@ HXB_API int hxb_moe_profile(hxb_moe *m, int T, int iters, double *us);
  * polled, mid blocks, down rows landed, down rows computed, y stored, y polled, h stored. Returns the
  * number of values (call with out = NULL to size the buffer), 0 when not tracing. */
 HXB_API int64_t hxb_moe_phase_trace(hxb_moe *m, uint64_t *out, int64_t max_values);
+/* Expert parallelism over ep_size handles (one per GPU, each holding its own experts), one MoE layer
+ * in two steps around an exchange the caller makes (an all-gather over NCCL, for example):
+ * 1. hxb_moe_ep_layer_dev: x = rmsnorm(h, ffn_norm), router, routing of the T tokens (identical on
+ *    every rank), and the outputs of the (token, rank) pairs whose expert this handle owns, written
+ *    to y [T*K, D] at the pair's index in the routing's expert-ascending bucket order (the same on
+ *    every rank); rows of other ranks' pairs are left as they are. The shared expert, if any, is
+ *    computed on every rank.
+ * 2. hxb_moe_ep_combine_dev: with y_all [ep_size][T*K][D] holding every rank's y, h += residual_scale
+ *    * (rank-order sum of w_j * y_all[owner of expert][pair] + shared output): the single-GPU result
+ *    bit for bit. It uses the routing of step 1, so no other call on the handle may come between.
+ * Device buffers, asynchronous on `stream`; every owned expert of the layer must be in HBM
+ * (HXB_E_IO otherwise). No counterpart in the reference (one process, one CPU). */
+HXB_API int hxb_moe_ep_layer_dev(hxb_moe *m, int layer, const float *h, int T, float *y, void *stream);
+HXB_API int hxb_moe_ep_combine_dev(hxb_moe *m, int layer, const float *y_all, int T, float *h, void *stream);
 /* Which kernel evaluates a single-token forward over every layer (every expert resident):
  * 0 per-phase kernels (one launch per phase and layer), 1 the persistent decode kernel (one launch
  * for all layers). Chosen at open from the shape; the environment variable HXB_PERSISTENT=0 forces

@@ -43,20 +43,11 @@ def make_slab(rng, D, F, dt=O.Q4):
     return s
 
 
-def build_pair(seed, *, L=1, D=256, F=128, E=16, K=4, score_fn=0, score_bias=0, n_group=1, topk_group=1,
-               norm=1, routed_scale=1.0, Fs=0, shared_gate=False, max_tokens=64, cache_gb=0.0, policy=1,
-               router_sigma=0.15, residual_scale=1.0, router_fn=None):
-    """An oracle model and a GPU backend holding the same random weights. router_fn(router) may
-    rewrite each layer's router matrix (e.g. duplicate rows to force tied scores)."""
+def make_weights(seed, *, L=1, D=256, F=128, E=16, Fs=0, shared_gate=False, score_bias=0, router_sigma=0.15,
+                 router_fn=None, **_):
+    """Random layer weights (reference-quantized experts) for L layers, reproducible from seed."""
     rng = np.random.default_rng(seed)
-    model = O.MoeModel(D, F, E, K, score_fn=score_fn, score_bias=score_bias, n_group=n_group,
-                       topk_group=topk_group, norm_topk_prob=norm, routed_scale=routed_scale,
-                       residual_scale=residual_scale)
-    be = hb.MoeBackend(n_layers=L, d_model=D, expert_ffn_dim=F, n_experts=E, top_k=K, score_fn=score_fn,
-                       score_bias=score_bias, n_group=n_group, topk_group=topk_group, norm_topk_prob=norm,
-                       routed_scale=routed_scale, residual_scale=residual_scale, shared_ffn_dim=Fs,
-                       shared_dtype=O.Q8, shared_gate=int(shared_gate), max_tokens=max_tokens, cache_gb=cache_gb,
-                       policy=policy)
+    layers = []
     for l in range(L):
         router = (rng.standard_normal((E, D)) * router_sigma).astype(np.float32)
         if router_fn is not None:
@@ -69,12 +60,55 @@ def build_pair(seed, *, L=1, D=256, F=128, E=16, K=4, score_fn=0, score_bias=0, 
             shared = dict(Fs=Fs, dtype=O.Q8, gate=q_matrix(rng, Fs, D, O.Q8), up=q_matrix(rng, Fs, D, O.Q8),
                           down=q_matrix(rng, D, Fs, O.Q8),
                           gate_inp=(rng.standard_normal(D) * 0.1).astype(np.float32) if shared_gate else None)
-        model.add_layer(router, slabs, [O.Q4] * E, ffn_norm=norm_w, bias=bias, shared=shared)
-        be.set_layer(l, router, bias, norm_w,
-                     shared["gate"] if shared else None, shared["up"] if shared else None,
-                     shared["down"] if shared else None, shared["gate_inp"] if shared else None)
-        for e in range(E):
-            be.set_expert(l, e, slabs[e])
+        layers.append(dict(router=router, bias=bias, norm=norm_w, slabs=slabs, shared=shared))
+    return layers
+
+
+def load_weights(b, layers):
+    """Loads make_weights' layers into a backend (an expert-parallel one keeps only its experts)."""
+    for l, w in enumerate(layers):
+        sh = w["shared"]
+        b.set_layer(l, w["router"], w["bias"], w["norm"], sh["gate"] if sh else None, sh["up"] if sh else None,
+                    sh["down"] if sh else None, sh["gate_inp"] if sh else None)
+        for e, slab in enumerate(w["slabs"]):
+            b.set_expert(l, e, slab)
+
+
+def backend_kwargs(*, L=1, D=256, F=128, E=16, K=4, score_fn=0, score_bias=0, n_group=1, topk_group=1, norm=1,
+                   routed_scale=1.0, Fs=0, shared_gate=False, max_tokens=64, cache_gb=0.0, policy=1,
+                   residual_scale=1.0, **_):
+    return dict(n_layers=L, d_model=D, expert_ffn_dim=F, n_experts=E, top_k=K, score_fn=score_fn,
+                score_bias=score_bias, n_group=n_group, topk_group=topk_group, norm_topk_prob=norm,
+                routed_scale=routed_scale, residual_scale=residual_scale, shared_ffn_dim=Fs,
+                shared_dtype=O.Q8, shared_gate=int(shared_gate), max_tokens=max_tokens, cache_gb=cache_gb,
+                policy=policy)
+
+
+def oracle_model(layers, *, D=256, F=128, E=16, K=4, score_fn=0, score_bias=0, n_group=1, topk_group=1, norm=1,
+                 routed_scale=1.0, residual_scale=1.0, **_):
+    model = O.MoeModel(D, F, E, K, score_fn=score_fn, score_bias=score_bias, n_group=n_group,
+                       topk_group=topk_group, norm_topk_prob=norm, routed_scale=routed_scale,
+                       residual_scale=residual_scale)
+    for w in layers:
+        model.add_layer(w["router"], w["slabs"], [O.Q4] * E, ffn_norm=w["norm"], bias=w["bias"], shared=w["shared"])
+    return model
+
+
+def build_pair(seed, *, ep_size=0, **kw):
+    """An oracle model and a GPU backend holding the same random weights (make_weights' arguments;
+    router_fn(router) may rewrite each layer's router matrix, e.g. duplicate rows to force tied
+    scores). ep_size > 0 also opens ep_size expert-parallel handles (ranks 0..ep_size-1, same
+    device) with the same weights and returns (model, backend, [handles])."""
+    layers = make_weights(seed, **kw)
+    model = oracle_model(layers, **kw)
+    be = hb.MoeBackend(**backend_kwargs(**kw))
+    load_weights(be, layers)
+    eps = []
+    for r in range(ep_size):
+        eps.append(hb.MoeBackend(ep_size=ep_size, ep_rank=r, **backend_kwargs(**kw)))
+        load_weights(eps[-1], layers)
+    if ep_size:
+        return model, be, eps
     return model, be
 
 
