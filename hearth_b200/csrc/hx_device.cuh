@@ -1,5 +1,5 @@
 // hx_device.cuh — sm_100a plumbing shared by the kernels: shared-memory addresses, mbarriers with
-// bounded waits, 1-D bulk copies (cp.async.bulk, no cluster multicast), the device error word,
+// bounded waits, 1-D bulk copies (cp.async.bulk into this CTA only), the device error word,
 // and the canonical row-chain machinery of the quantized GEMV tiles.
 #pragma once
 
