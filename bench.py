@@ -229,6 +229,81 @@ def run_trace(args, local_rank):
                       "layer_us_mean": round(float(layer.mean()), 3), "phases": phases}), flush=True)
 
 
+def run_ep(args, rank, world, local_rank):
+    """One token stream through the MoE stack with the experts spread over the ranks (expert e on rank
+    e % world): per layer every rank routes the batch, computes its experts' pairs, the ranks all-gather
+    the pairs' outputs (NCCL) and each forms the rank-order sum. Total work is fixed as N grows."""
+    import torch
+    import torch.distributed as dist
+    import hearth_b200 as hb
+    from hearth_b200.ep import ExpertParallelMoe
+    dev = torch.device("cuda", local_rank)
+    B = args.batch
+    be = hb.MoeBackend(n_layers=L_, d_model=D_, expert_ffn_dim=F_, n_experts=E_, top_k=K_, score_fn=0,
+                       norm_topk_prob=1, max_tokens=B, device=local_rank, ep_size=world, ep_rank=rank)
+    be.synthesize(SEED, SIGMA, SIGMA)
+    ep = ExpertParallelMoe(be)
+    P = 64
+    g = torch.Generator(device=dev).manual_seed(1000)   # the same tokens on every rank
+    pool = torch.randn((P, B, D_), generator=g, device=dev, dtype=torch.float32)
+    stream = torch.cuda.current_stream(dev)
+    for i in range(max(args.warmup, 3)):
+        ep.forward_dev(pool[i % P], B, stream=stream)
+    be.sync(stream)
+    torch.cuda.synchronize(dev)
+    dist.barrier()
+    clocks = Clocks(local_rank)
+    clocks.start()
+    time.sleep(0.3)
+    torch.cuda.synchronize(dev)
+    dist.barrier()
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e0.record(stream)
+    for i in range(args.steps):
+        ep.forward_dev(pool[i % P], B, stream=stream)
+    e1.record(stream)
+    torch.cuda.synchronize(dev)
+    be.sync(stream)
+    ms = max_over_ranks(e0.elapsed_time(e1), world, dev)
+    dist.barrier()
+    clk = clocks.stop()
+    value = args.steps * B / (ms / 1000.0)
+    # end to end: the token from pinned host memory and back each step
+    hin = torch.randn((B, D_), generator=torch.Generator().manual_seed(7)).pin_memory()
+    hout = torch.empty_like(hin).pin_memory()
+    hd = torch.empty((B, D_), device=dev)
+    n_e2e = min(args.steps, 500)
+    torch.cuda.synchronize(dev)
+    dist.barrier()
+    t0 = time.perf_counter()
+    for i in range(n_e2e):
+        hd.copy_(hin, non_blocking=True)
+        ep.forward_dev(hd, B, stream=stream)
+        hout.copy_(hd, non_blocking=True)
+        torch.cuda.current_stream(dev).synchronize()
+    t_e2e = max_over_ranks(time.perf_counter() - t0, world, dev)
+    ab = algorithmic_bytes()
+    hbm, peak_kind = peaks()
+    gbs = L_ * ab["layer"] / (ms / args.steps * 1e-3) / 1e9   # whole-stack bytes over all ranks
+    if rank == 0:
+        line = {"metric": METRIC, "value": round(value, 3), "unit": "tok/s", "n_gpus": world, "steps": args.steps,
+                "warmup": args.warmup, "ms_per_step": round(ms / args.steps, 5), "higher_is_better": True,
+                "scaling": "strong", "vs_baseline": None, "dtype": "q4xq8-int32+f32", "data": "synthetic",
+                "config": {"workload": f"qwen3-30b-a3b MoE stack decode, {L_} layers, batch {B}, expert-parallel",
+                           "layers": L_, "d_model": D_, "expert_ffn_dim": F_, "n_experts": E_, "top_k": K_,
+                           "batch": B, "parallelism": f"ep{world}",
+                           "l2": "no flush: each step reads ~1.01 GB of expert/router weights over the ranks"},
+                "roofline": {"bound": "hbm", "achieved": round(gbs, 1), "peak": round(hbm * world, 1), "unit": "GB/s",
+                             "frac": round(gbs / (hbm * world), 4), "traffic": None,
+                             "kernel": "per-phase kernels + NCCL all-gather per layer", "peak_kind": peak_kind},
+                "cpu_baseline": None,
+                "e2e": {"value": round(n_e2e * B / t_e2e, 3), "unit": "tok/s", "h2d_bytes_per_step": B * D_ * 4,
+                        "d2h_bytes_per_step": B * D_ * 4, "timing": "host clock, pinned copies in and out per step"},
+                "gpu_launches": args.steps * L_ * 7, "clocks": clk}
+        print(json.dumps(line), flush=True)
+    be.close()
+
+
 def run_ours(args, rank, world, local_rank):
     import torch
     import hearth_b200 as hb
@@ -375,6 +450,9 @@ def main():
     ap.add_argument("--layers", type=int, default=48, help="MoE layers (48 = the Qwen3-30B-A3B stack); fewer only "
                                                             "for small profiling captures")
     ap.add_argument("--no-cpu", action="store_true", help="skip the CPU baseline leg")
+    ap.add_argument("--ep", action="store_true",
+                    help="one token stream through the stack expert-parallel over the N ranks (expert e on rank "
+                         "e %% N, NCCL all-gather of the pairs' outputs per layer): strong scaling")
     ap.add_argument("--trace", action="store_true",
                     help="instead of the bench line: the persistent kernel's per-phase timeline (mean us per "
                          "layer over CTAs, thread 0's SM clock) as one JSON line")
@@ -394,6 +472,8 @@ def main():
                 run_trace(args, local_rank)
         elif args.impl == "reference":
             run_reference(args, rank, world)
+        elif args.ep and world > 1:
+            run_ep(args, rank, world, local_rank)
         else:
             run_ours(args, rank, world, local_rank)
     finally:

@@ -91,7 +91,7 @@ def _free_port():
 
 @pytest.mark.parametrize("T", [1, 5])
 def test_exchange_over_gloo_equals_single_rank(T):
-    mgr = mp.Manager()
+    mgr = mp.get_context("spawn").Manager()
     got = mgr.dict()
     mp.spawn(_rank_main, args=(2, _free_port(), T, got), nprocs=2, join=True)
     ref = mgr.dict()

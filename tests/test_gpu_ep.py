@@ -110,7 +110,7 @@ def test_ep_over_nccl_equals_oracle(gpu, T):
     s.bind(("127.0.0.1", 0))
     port = s.getsockname()[1]
     s.close()
-    got = mp.Manager().dict()
+    got = mp.get_context("spawn").Manager().dict()
     mp.spawn(_nccl_rank, args=(world, port, T, got), nprocs=world, join=True)
     kw = dict(L=3, D=256, F=128, E=16, K=4, Fs=128, shared_gate=True)
     want = oracle_model(make_weights(71, **kw), **kw).forward(
