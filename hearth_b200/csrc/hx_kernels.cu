@@ -6,8 +6,10 @@
 #include "hx_device.cuh"
 #include "hx_kernels.h"
 #include "hx_route.cuh"
+#include "hx_moe_job.cuh"
 
 #include <algorithm>
+#include <cstdlib>
 
 namespace hx {
 
@@ -293,10 +295,6 @@ __global__ void __launch_bounds__(512) k_route_union(MoeShape sh, MoeScratch sc)
     }
 }
 
-// Routed jobs of a launch: every bucket, or under expert parallelism this rank's buckets.
-__device__ __forceinline__ int routed_jobs(const MoeShape &sh, const MoeScratch &sc) {
-    return sh.ep_size > 1 ? *sc.nu_job : *sc.nu;
-}
 
 // =============================================================================================
 // MoE experts. A "job" is one routed expert bucket (jobs 0..nu-1, experts ascending) or the
@@ -304,51 +302,7 @@ __device__ __forceinline__ int routed_jobs(const MoeShape &sh, const MoeScratch 
 // shared token t -> T*K + t.
 // =============================================================================================
 
-struct Job {
-    const uint8_t *gate, *up, *down;
-    int dtype, F, nbF, n, p0;   // rows of gate/up, down's blocks per row, tokens, first pair
-    bool shared;
-};
 
-__device__ __forceinline__ bool get_job(const MoeShape &sh, const MoeLayerDev &L, const MoeScratch &sc, int u,
-                                        int nu, Job &j) {
-    if (u < nu) {
-        if (sh.ep_size > 1) u = sc.ujob[u];   // job -> bucket
-        const int e = sc.ulist[u];
-        const uint8_t *slab = L.slab[e];
-        if (!slab) {
-            set_error(sc.err, DEV_E_NOT_RESIDENT);
-            return false;
-        }
-        j.gate = slab;
-        j.up = slab + L.off_up;
-        j.down = slab + L.off_down;
-        j.dtype = L.expert_dtype;
-        j.F = sh.F;
-        j.n = sc.u_n[u];
-        j.p0 = sc.u_p0[u];
-        j.shared = false;
-    } else {
-        j.gate = L.sh_gate;
-        j.up = L.sh_up;
-        j.down = L.sh_down;
-        j.dtype = L.sh_dtype;
-        j.F = L.Fs;
-        j.n = sh.T;
-        j.p0 = sh.T * sh.route.K;
-        j.shared = true;
-    }
-    j.nbF = j.F / QK;
-    if (j.dtype != Q4 && j.dtype != Q8) {
-        set_error(sc.err, DEV_E_BAD_DTYPE);
-        return false;
-    }
-    return true;
-}
-
-__device__ __forceinline__ int job_token(const MoeScratch &sc, const Job &j, int i) {
-    return j.shared ? i : sc.pair_tok[j.p0 + i];
-}
 
 constexpr int GU_ROWS = 64;    // gate/up rows per CTA: one activation block of the mid vector
 constexpr int GU_CH = 8;       // rows of gate (and of up) per pipeline stage
@@ -684,6 +638,21 @@ static cudaError_t launch_expert_stages(int which, const MoeShape &sh, const Moe
     const bool fused = T * K <= kFusedMaxPairs && sh.ep_size == 1;
     const size_t lim = smem_limit() - 1024;
     const int fmax_nb = fmax_nb_of(sh, L);
+    // large batches: tensor-core expert stages (HXB_TC=0 keeps the SIMT stages)
+    static const bool tc_on = [] {
+        const char *e = std::getenv("HXB_TC");
+        return !(e && e[0] == '0');
+    }();
+    const bool tc = tc_on && !fused && T * K >= kTcMinPairs;
+    if (tc) {
+        cudaError_t e = launch_moe_experts_tc(sh, L, sc, which & 3, s);
+        if (e != cudaSuccess) return e;
+        if ((which & 2) && sh.ep_size == 1) {
+            const int64_t n = (int64_t)T * sh.D;
+            k_moe_sum<<<(unsigned)((n + 255) / 256), 256, 0, s>>>(sh, L, sc, h, out, resid ? 1 : 0);
+        }
+        return cudaGetLastError();
+    }
     // ---- gate/up + SwiGLU + mid activations
     if (which & 1) {
         GateUpCfg c;

@@ -86,6 +86,13 @@ cudaError_t launch_matmul(int dtype, const void *W, int64_t n_cols, const void *
 cudaError_t launch_dequantize(int dtype, const void *W, int64_t n_rows, int64_t n_cols, float *out,
                               cudaStream_t s);
 
+// Expert gate/up (which & 1) and down (which & 2) of the unfused path on the tensor cores (tcgen05,
+// hx_prefill_tc.cu): the same outputs as the SIMT stages, bit for bit.
+cudaError_t launch_moe_experts_tc(const MoeShape &sh, const MoeLayerDev &L, const MoeScratch &sc, int which,
+                                  cudaStream_t s);
+// Pairs (T * K) from which the unfused path runs its expert stages on the tensor cores.
+constexpr int kTcMinPairs = 256;
+
 // Expert-parallel combine: h += rs * (rank-order sum over j of w_j * y_all[owner rank][pair(t, j)] +
 // shared output) with the routing and shared output of the preceding launch_moe_layer.
 cudaError_t launch_moe_ep_combine(const MoeShape &sh, const MoeLayerDev &L, const MoeScratch &sc,

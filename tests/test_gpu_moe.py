@@ -250,3 +250,34 @@ def test_persistent_decode_device_api_repeats(gpu):
     for _ in range(25):
         want = model.forward(want)
     assert np.array_equal(bits(got), bits(want))
+
+
+@pytest.mark.parametrize("case", list(CASES))
+@pytest.mark.parametrize("T", [64, 100])
+def test_tensor_core_stages_equal_oracle(gpu, case, T):
+    """T * K >= 256 pairs: gate/up and down run on the tensor cores (tcgen05 .kind::i8, per-block int32
+    tiles drained into the canonical float chains); the layer equals the oracle bit for bit."""
+    kw = dict(CASES[case])
+    if T * kw.get("K", 4) < 256:
+        kw["K"] = 4
+        T = 64
+    model, be = build_pair(300 + T, max_tokens=T, **kw)
+    with be:
+        x = np.random.default_rng(T + 1).standard_normal((T, 256)).astype(np.float32)
+        y = be.layer(0, x)
+        ids, w = be.last_routing(T)
+    yo, ido, wo = model.layer_eval(0, x)
+    assert np.array_equal(ids, ido)
+    assert np.array_equal(bits(w), bits(wo))
+    assert np.array_equal(bits(y), bits(yo))
+
+
+def test_tensor_core_stages_qwen3_layer_shape(gpu):
+    """The BASELINE single-layer shape (D 2048, F 768, 128 experts, top-8) with 40 tokens (320 pairs,
+    six 128-row gate/up tiles, sixteen down tiles, partial token tiles) equals the oracle."""
+    model, be = build_pair(331, L=1, D=2048, F=768, E=128, K=8, max_tokens=40, router_sigma=0.02)
+    with be:
+        x = np.random.default_rng(12).standard_normal((40, 2048)).astype(np.float32)
+        y = be.layer(0, x)
+    yo, _, _ = model.layer_eval(0, x)
+    assert np.array_equal(bits(y), bits(yo))
