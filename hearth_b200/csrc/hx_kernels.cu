@@ -266,8 +266,63 @@ __global__ void __launch_bounds__(256) k_moe_router(MoeShape sh, const float *__
     __threadfence_block();
     int *cnt = reinterpret_cast<int *>(rsm), *start = cnt + E;
     route_union_cta(T, sh.route.K, E, sc.ids, cnt, start, sc.nu, sc.ulist, sc.u_p0, sc.u_n, sc.pair_tok,
-                    sc.pair_of);
+                    sc.pair_of, start + E);
     if (threadIdx.x == 0) *sc.ticket = 0u;   // ready for the next launch
+}
+
+// Router logits of a large batch as a tiled GEMM on the CUDA cores, in the canonical dot16 order
+// (NUMERICS §1): output (t, e) = tree16 over lanes j of L_j = ((0 + x_j w_j) + x_{j+16} w_{j+16}) + ...
+// A CTA computes 16 tokens x 16 rows (router rows, and the shared-expert gate row as row E): thread
+// (cell c, lane j) keeps lane j's chains of the 4 x 4 outputs of cell c, with K staged 64 columns at a
+// time in shared memory; the 16 lanes of a cell form one half-warp for the final tree.
+constexpr int RT_T = 16, RT_E = 16, RT_K = 64;
+
+__global__ void __launch_bounds__(256) k_moe_router_tiled(MoeShape sh, const float *__restrict__ router,
+                                                          const float *__restrict__ gate_inp, MoeScratch sc) {
+    __shared__ float xs[RT_T][RT_K + 1], ws[RT_E][RT_K + 1];
+    const int D = sh.D, E = sh.route.E, T = sh.T;
+    const int rows = E + (gate_inp ? 1 : 0);
+    const int t0 = blockIdx.x * RT_T, e0 = blockIdx.y * RT_E;
+    const int tid = threadIdx.x, j = tid & 15, cell = tid >> 4;   // 16 cells of 4 x 4 outputs
+    const int ct = (cell >> 2) * 4, ce = (cell & 3) * 4;           // the cell's first token / row in the tile
+    float L[4][4];
+#pragma unroll
+    for (int a = 0; a < 4; a++)
+#pragma unroll
+        for (int b = 0; b < 4; b++) L[a][b] = 0.0f;
+    for (int k0 = 0; k0 < D; k0 += RT_K) {
+        for (int i = tid; i < RT_T * RT_K; i += 256) {   // stage x and w (zeros outside the batch / rows)
+            const int r = i / RT_K, k = i - r * RT_K, t = t0 + r, e = e0 + r;
+            xs[r][k] = t < T ? sc.x[(int64_t)t * D + k0 + k] : 0.0f;
+            ws[r][k] = e < E ? __ldg(router + (int64_t)e * D + k0 + k) : (e < rows ? __ldg(gate_inp + k0 + k) : 0.0f);
+        }
+        __syncthreads();
+#pragma unroll
+        for (int s = 0; s < RT_K / 16; s++) {   // columns k0 + j + 16 s, in order
+            const int k = j + 16 * s;
+            float xv[4], wv[4];
+#pragma unroll
+            for (int a = 0; a < 4; a++) xv[a] = xs[ct + a][k];
+#pragma unroll
+            for (int b = 0; b < 4; b++) wv[b] = ws[ce + b][k];
+#pragma unroll
+            for (int a = 0; a < 4; a++)
+#pragma unroll
+                for (int b = 0; b < 4; b++) L[a][b] = __fadd_rn(L[a][b], __fmul_rn(wv[b], xv[a]));
+        }
+        __syncthreads();
+    }
+#pragma unroll
+    for (int a = 0; a < 4; a++)
+#pragma unroll
+        for (int b = 0; b < 4; b++) {
+            const float v = tree16(L[a][b], 0xffffffffu);
+            const int t = t0 + ct + a, e = e0 + ce + b;
+            if (j == 0 && t < T && e < rows) {
+                if (e < E) sc.logits[(int64_t)t * E + e] = canon(v);
+                else sc.sh_logit[t] = v;
+            }
+        }
 }
 
 __global__ void __launch_bounds__(256) k_route_select(MoeShape sh, const float *__restrict__ bias, MoeScratch sc) {
@@ -283,7 +338,7 @@ __global__ void __launch_bounds__(256) k_route_select(MoeShape sh, const float *
 __global__ void __launch_bounds__(512) k_route_union(MoeShape sh, MoeScratch sc) {
     extern __shared__ int usm[];
     route_union_cta(sh.T, sh.route.K, sh.route.E, sc.ids, usm, usm + sh.route.E, sc.nu, sc.ulist, sc.u_p0,
-                    sc.u_n, sc.pair_tok, sc.pair_of);
+                    sc.u_n, sc.pair_tok, sc.pair_of, usm + 2 * sh.route.E);
     if (sh.ep_size > 1) {   // the buckets of this rank's experts, in bucket order
         __syncthreads();
         if (threadIdx.x == 0) {
@@ -587,11 +642,15 @@ static void launch_route_stages(int which, const MoeShape &sh, const MoeLayerDev
         constexpr int RT = 64;   // 4 (row, token) items per CTA: E=128 rows -> 32 CTAs at T=1
         const unsigned grid = (unsigned)((items + RT / 16 - 1) / (RT / 16));
         const size_t route_smem = (size_t)8 * 2 * E * sizeof(float);
-        k_moe_router<<<grid, RT, fused ? route_smem : 0, s>>>(sh, L.router, L.sh_gate_inp, L.router_bias, sc,
-                                                               fused ? 1 : 0);
+        if (T >= RT_T && !fused)   // batches: tiled router GEMM
+            k_moe_router_tiled<<<dim3((unsigned)((T + RT_T - 1) / RT_T), (unsigned)((rows + RT_E - 1) / RT_E)), 256, 0,
+                                 s>>>(sh, L.router, L.sh_gate_inp, sc);
+        else
+            k_moe_router<<<grid, RT, fused ? route_smem : 0, s>>>(sh, L.router, L.sh_gate_inp, L.router_bias, sc,
+                                                                   fused ? 1 : 0);
         if (!fused) {
             k_route_select<<<(T + 7) / 8, 256, route_smem, s>>>(sh, L.router_bias, sc);
-            k_route_union<<<1, 512, (size_t)2 * E * sizeof(int), s>>>(sh, sc);
+            k_route_union<<<1, 512, (size_t)(2 + 512 / 32) * E * sizeof(int), s>>>(sh, sc);
         }
     }
 }

@@ -149,12 +149,19 @@ __device__ __forceinline__ void route_token_warp(const RouteCfg &R, const float 
 
 // Expert buckets of the batch (engine/src/model.c:1020-1037), by one CTA: experts ascending,
 // tokens ascending within an expert; pair_of[t*K + j] is the pair of token t's rank j.
+// The union of routed experts and the bucket order (engine/src/model.c:1020-1037): experts
+// ascending, and within an expert the pairs i = t*K + j ascending. One CTA: counts per expert
+// (shared atomics), an exclusive scan, then a stable counting sort over chunks of blockDim pairs in
+// order: within a warp, lanes holding the same expert rank themselves with __match_any_sync; the
+// warps' counts per expert give each warp its offset. Shared scratch: cnt [E], start [E] and
+// wcnt [blockDim/32][E].
 __device__ __forceinline__ void route_union_cta(int T, int K, int E, const int *ids, int *cnt, int *start, int *nu_out,
-                                int *ulist, int *u_p0, int *u_n, int *pair_tok, int *pair_of) {
-    const int tid = threadIdx.x, nt = blockDim.x;
+                                int *ulist, int *u_p0, int *u_n, int *pair_tok, int *pair_of, int *wcnt) {
+    const int tid = threadIdx.x, nt = blockDim.x, TK = T * K, lane = tid & 31, warp = tid >> 5;
+    const int nwarps = (nt + 31) >> 5;
     for (int e = tid; e < E; e += nt) cnt[e] = 0;
     __syncthreads();
-    for (int i = tid; i < T * K; i += nt) atomicAdd(&cnt[__ldcg(ids + i)], 1);
+    for (int i = tid; i < TK; i += nt) atomicAdd(&cnt[__ldcg(ids + i)], 1);
     __syncthreads();
     if (tid == 0) {
         int nu = 0, p = 0;
@@ -170,16 +177,29 @@ __device__ __forceinline__ void route_union_cta(int T, int K, int E, const int *
         *nu_out = nu;
     }
     __syncthreads();
-    for (int e = tid; e < E; e += nt) {
-        if (!cnt[e]) continue;
-        int p = start[e];
-        for (int t = 0; t < T; t++)
-            for (int j = 0; j < K; j++)
-                if (__ldcg(ids + t * K + j) == e) {
-                    pair_tok[p] = t;
-                    pair_of[t * K + j] = p;
-                    p++;
-                }
+    for (int c0 = 0; c0 < TK; c0 += nt) {
+        for (int k = tid; k < nwarps * E; k += nt) wcnt[k] = 0;
+        __syncthreads();
+        const int i = c0 + tid;
+        const bool live = i < TK;
+        const int e = live ? __ldcg(ids + i) : -1;
+        const unsigned peers = __match_any_sync(0xffffffffu, e);
+        const int rank = __popc(peers & ((1u << lane) - 1u));
+        if (live && rank == 0) wcnt[warp * E + e] = __popc(peers);
+        __syncthreads();
+        if (live) {
+            int p = start[e] + rank;
+            for (int w = 0; w < warp; w++) p += wcnt[w * E + e];
+            pair_tok[p] = i / K;
+            pair_of[i] = p;
+        }
+        __syncthreads();
+        for (int x = tid; x < E; x += nt) {
+            int add = 0;
+            for (int w = 0; w < nwarps; w++) add += wcnt[w * E + x];
+            start[x] += add;
+        }
+        __syncthreads();
     }
 }
 
