@@ -687,6 +687,7 @@ cudaError_t init_kernel_attributes() {
                              (const void *)k_route_union, (const void *)k_moe_sum};
     for (const void *k : kernels)
         if (e == cudaSuccess) e = cudaFuncGetAttributes(&fa, k);
+    if (e == cudaSuccess) e = init_tc_attributes();
     return e;
 }
 

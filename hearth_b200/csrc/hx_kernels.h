@@ -78,6 +78,7 @@ constexpr int kFusedMaxPairs = 64;
 // Raises the dynamic shared-memory limit of the staged kernels to the device maximum (once per
 // device, before any launch or stream capture).
 cudaError_t init_kernel_attributes();
+cudaError_t init_tc_attributes();   // the staged tensor-core kernels (hx_prefill_tc.cu)
 
 // Launchers return cudaGetLastError() of their launches.
 cudaError_t launch_act_quantize(const float *x, int64_t ldx, act_q8 *out, int64_t n, int T, cudaStream_t s);

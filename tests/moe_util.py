@@ -44,7 +44,7 @@ def make_slab(rng, D, F, dt=O.Q4):
 
 
 def make_weights(seed, *, L=1, D=256, F=128, E=16, Fs=0, shared_gate=False, score_bias=0, router_sigma=0.15,
-                 router_fn=None, **_):
+                 router_fn=None, shared_dtype=O.Q8, **_):
     """Random layer weights (reference-quantized experts) for L layers, reproducible from seed."""
     rng = np.random.default_rng(seed)
     layers = []
@@ -57,8 +57,9 @@ def make_weights(seed, *, L=1, D=256, F=128, E=16, Fs=0, shared_gate=False, scor
         slabs = [make_slab(rng, D, F) for _ in range(E)]
         shared = None
         if Fs:
-            shared = dict(Fs=Fs, dtype=O.Q8, gate=q_matrix(rng, Fs, D, O.Q8), up=q_matrix(rng, Fs, D, O.Q8),
-                          down=q_matrix(rng, D, Fs, O.Q8),
+            dt = shared_dtype
+            shared = dict(Fs=Fs, dtype=dt, gate=q_matrix(rng, Fs, D, dt), up=q_matrix(rng, Fs, D, dt),
+                          down=q_matrix(rng, D, Fs, dt),
                           gate_inp=(rng.standard_normal(D) * 0.1).astype(np.float32) if shared_gate else None)
         layers.append(dict(router=router, bias=bias, norm=norm_w, slabs=slabs, shared=shared))
     return layers
@@ -76,11 +77,11 @@ def load_weights(b, layers):
 
 def backend_kwargs(*, L=1, D=256, F=128, E=16, K=4, score_fn=0, score_bias=0, n_group=1, topk_group=1, norm=1,
                    routed_scale=1.0, Fs=0, shared_gate=False, max_tokens=64, cache_gb=0.0, policy=1,
-                   residual_scale=1.0, **_):
+                   residual_scale=1.0, shared_dtype=O.Q8, **_):
     return dict(n_layers=L, d_model=D, expert_ffn_dim=F, n_experts=E, top_k=K, score_fn=score_fn,
                 score_bias=score_bias, n_group=n_group, topk_group=topk_group, norm_topk_prob=norm,
                 routed_scale=routed_scale, residual_scale=residual_scale, shared_ffn_dim=Fs,
-                shared_dtype=O.Q8, shared_gate=int(shared_gate), max_tokens=max_tokens, cache_gb=cache_gb,
+                shared_dtype=shared_dtype, shared_gate=int(shared_gate), max_tokens=max_tokens, cache_gb=cache_gb,
                 policy=policy)
 
 

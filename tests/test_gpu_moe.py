@@ -272,6 +272,34 @@ def test_tensor_core_stages_equal_oracle(gpu, case, T):
     assert np.array_equal(bits(y), bits(yo))
 
 
+STAGED = {
+    # D a multiple of 512 and Q4 experts: the persistent bulk-copy-staged tensor-core kernels
+    "f256": dict(D=512, F=256, E=16, K=4, T=100),                    # down rows of 4 blocks, row pairs
+    "f512_shared_q4": dict(D=512, F=512, E=16, K=8, T=70, Fs=512, shared_dtype=O.Q4, shared_gate=True),
+    "f768_many_pair_tiles": dict(D=512, F=768, E=8, K=4, T=300),     # buckets of ~150 pairs: 5 pair tiles
+    "sigmoid_groups": dict(D=1024, F=256, E=32, K=8, T=48, score_fn=1, score_bias=1, n_group=4, topk_group=2,
+                           routed_scale=2.5, norm=0),
+    "shared_f_differs": dict(D=512, F=256, E=16, K=4, T=80, Fs=384, shared_dtype=O.Q4),   # down: register path
+}
+
+
+@pytest.mark.parametrize("case", list(STAGED))
+def test_staged_tensor_core_stages_equal_oracle(gpu, case):
+    """Staged persistent tensor-core kernels (weight and activation rows brought into shared memory
+    by bulk copies, a two-slot ring across tiles): routing, weights and outputs equal the oracle."""
+    kw = dict(STAGED[case])
+    T = kw.pop("T")
+    model, be = build_pair(500 + T, max_tokens=T, **kw)
+    with be:
+        x = np.random.default_rng(T + 3).standard_normal((T, kw["D"])).astype(np.float32)
+        y = be.layer(0, x)
+        ids, w = be.last_routing(T)
+    yo, ido, wo = model.layer_eval(0, x)
+    assert np.array_equal(ids, ido)
+    assert np.array_equal(bits(w), bits(wo))
+    assert np.array_equal(bits(y), bits(yo))
+
+
 def test_tensor_core_stages_qwen3_layer_shape(gpu):
     """The BASELINE single-layer shape (D 2048, F 768, 128 experts, top-8) with 40 tokens (320 pairs,
     six 128-row gate/up tiles, sixteen down tiles, partial token tiles) equals the oracle."""
