@@ -201,6 +201,7 @@ extern "C" HXB_API int hxb_dequantize(int dtype, const void *src, int64_t n_rows
 
 struct LayerBufs {
     DevBuf router, bias, norm, sh_gate, sh_up, sh_down, sh_gate_inp;
+    TcMaps maps;   // tensor maps of the staged tensor-core kernels (encoded when the layer is set)
     bool set = false;
 };
 
@@ -308,7 +309,34 @@ struct hxb_moe {
         d.sh_up = b.sh_up.as<uint8_t>();
         d.sh_down = b.sh_down.as<uint8_t>();
         d.sh_gate_inp = cfg.shared_gate ? b.sh_gate_inp.as<float>() : nullptr;
+        d.tc = &b.maps;
         return d;
+    }
+
+    // (Re)encodes layer l's tensor maps: the store views, its shared expert and the scratch rows.
+    void refresh_maps(int l) {
+        LayerBufs &b = layers[(size_t)l];
+        TcMapSrc a;
+        a.arena = store.n_slots() ? store.slot_ptr(0) : nullptr;
+        a.slot_bytes = (int64_t)slab_bytes;
+        a.n_slots = store.n_slots();
+        a.off_up = lay.off_up;
+        a.off_down = lay.off_down;
+        a.D = cfg.d_model;
+        a.F = cfg.expert_ffn_dim;
+        a.E = cfg.n_experts;
+        a.Fs = cfg.shared_ffn_dim;
+        a.expert_dtype = cfg.expert_dtype;
+        a.sh_dtype = cfg.shared_dtype;
+        a.sh_gate = b.sh_gate.as<uint8_t>();
+        a.sh_up = b.sh_up.as<uint8_t>();
+        a.sh_down = b.sh_down.as<uint8_t>();
+        a.xact = xact.p;
+        a.T = cfg.max_tokens;
+        a.mid = act_mid.p;
+        a.fmax_nb = std::max(cfg.expert_ffn_dim, cfg.shared_ffn_dim) / QK;
+        a.mid_rows = (int64_t)cfg.max_tokens * cfg.top_k + cfg.max_tokens;
+        encode_tc_maps(b.maps, a);
     }
 
     ~hxb_moe() {
@@ -511,6 +539,7 @@ extern "C" HXB_API int hxb_moe_set_layer(hxb_moe *m, int layer, const float *rou
         return fail(HXB_E_NOMEM, "set_layer: device allocation or copy failed");
     }
     b.set = true;
+    m->refresh_maps(layer);
     m->dec_dirty = true;
     drop_graphs(m);
     return HXB_OK;
@@ -561,6 +590,7 @@ extern "C" HXB_API int hxb_moe_synthesize(hxb_moe *m, uint64_t seed, float sigma
         std::vector<float> ones((size_t)D, 1.0f);
         cudaMemcpy(b.norm.p, ones.data(), sizeof(float) * D, cudaMemcpyHostToDevice);
         b.set = true;
+        m->refresh_maps(l);
         for (int e = 0; e < E; e++) {
             if (!m->owns(e)) continue;
             uint8_t *p = m->store.place_resident(l, e);

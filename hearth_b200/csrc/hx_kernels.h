@@ -50,6 +50,39 @@ struct MoeScratch {
     int *err;            // [1] device error word
 };
 
+// Tensor maps (CUtensorMap, 128 bytes each) of the staged tensor-core expert kernels, encoded on
+// the host per layer and passed to the kernels by value. Views: the expert store as
+// [slot][row][row bytes] for gate, up and down (down rows in groups of down_rg rows, so that a group
+// is a multiple of 16 bytes), this layer's shared expert, the batch's activation rows (token order)
+// and the mid activation rows (pair order).
+struct alignas(64) TcMaps {
+    uint64_t gate[16], up[16], down[16], sh_gate[16], sh_up[16], sh_down[16], xact[16], mid[16];
+    const uint8_t *arena = nullptr;   // slot 0 of the expert store
+    int64_t slot_bytes = 0;
+    int n_slots = 0, down_rg = 0;
+    int xact_rows = 0;                   // token rows the xact map covers
+    bool gu_ok = false, dn_ok = false;   // the staged gate/up and down kernels can take this layer
+};
+
+// What encode_tc_maps needs to know about a layer and the handle's buffers.
+struct TcMapSrc {
+    const uint8_t *arena;
+    int64_t slot_bytes;
+    int n_slots;
+    int64_t off_up, off_down;
+    int D, F, E, Fs, expert_dtype, sh_dtype;
+    const uint8_t *sh_gate, *sh_up, *sh_down;
+    const void *xact;
+    int T;                    // rows of xact
+    const void *mid;
+    int64_t mid_rows;         // rows of act_mid (pairs + shared tokens)
+    int fmax_nb;              // blocks per act_mid row
+};
+
+// Fills m (gu_ok / dn_ok false where a kernel's shape or alignment rules are not met or the driver
+// cannot encode a map; those stages then run the register-fed tensor-core kernels).
+void encode_tc_maps(TcMaps &m, const TcMapSrc &src);
+
 // One MoE layer's weights on the device.
 struct MoeLayerDev {
     const float *router;        // [E, D] f32
@@ -62,6 +95,7 @@ struct MoeLayerDev {
     int Fs, sh_dtype;
     const uint8_t *sh_gate, *sh_up, *sh_down;
     const float *sh_gate_inp;   // [D] or null
+    const TcMaps *tc = nullptr; // host copy of this layer's tensor maps (staged tensor-core kernels)
 };
 
 struct MoeShape {

@@ -24,6 +24,7 @@
 #include "hx_moe_job.cuh"
 
 #include <algorithm>
+#include <cuda.h>
 
 namespace hx {
 
@@ -367,7 +368,6 @@ __device__ void down_tc_body(const MoeShape &sh, const MoeScratch &sc, const Job
 // the same activations. Tile t goes to CTA t % gridDim.x.
 // =============================================================================================
 
-constexpr int SG_THREADS = 256;
 constexpr int SG_BLK = 8;                        // gate/up: blocks per stage
 constexpr int SG_SEG = SG_BLK * Q4_BLOCK;        // 272: one row's bytes per stage
 constexpr int SG_ASEG = SG_BLK * ACT_BLOCK;      // 576: one pair's activation bytes per stage
@@ -375,10 +375,10 @@ constexpr int SG_MAXJOBS = 1024 + 1;             // routed buckets (E <= 1024) +
 constexpr int SD_MAXNB = 12;                     // down: whole rows of at most 12 blocks (F <= 768)
 
 struct TileInfo {
-    const uint8_t *w0, *w1;   // gate and up rows (gate/up), down rows (down)
+    const uint8_t *w0, *w1;   // gate and up rows (gate/up), down rows (down); null: the job cannot run
     int rt, n0, nn, p0;       // row tile, first pair of the tile in the job, pairs, job's first pair
     int F, shared;            // job's expert width, shared-expert job
-    int tok[TC_N];            // token of each pair (gate/up)
+    int slot;                 // expert-store slot of a routed job
 };
 
 // Tiles per job and their exclusive prefix pre[0..njobs]; returns the number of tiles.
@@ -423,8 +423,8 @@ __device__ int tile_prefix(const MoeShape &sh, const MoeLayerDev &L, const MoeSc
 
 // Tile t -> its job and place (one thread). A job that cannot run (expert not resident) gives a
 // tile with no rows and no pairs: its stages copy nothing and its epilogue writes nothing.
-__device__ void decode_tile(const MoeShape &sh, const MoeLayerDev &L, const MoeScratch &sc, int nu, int njobs,
-                            const int *pre, int t, bool down, TileInfo &ti) {
+__device__ void decode_tile(const MoeShape &sh, const MoeLayerDev &L, const MoeScratch &sc, const TcMaps &mp, int nu,
+                            int njobs, const int *pre, int t, bool down, TileInfo &ti) {
     int lo = 0, hi = njobs;   // largest u with pre[u] <= t
     while (hi - lo > 1) {
         const int mid = (lo + hi) >> 1;
@@ -432,7 +432,14 @@ __device__ void decode_tile(const MoeShape &sh, const MoeLayerDev &L, const MoeS
         else hi = mid;
     }
     Job job;
-    const bool ok = get_job(sh, L, sc, lo, nu, job);
+    bool ok = get_job(sh, L, sc, lo, nu, job);
+    ti.slot = 0;
+    if (ok && !job.shared) {   // the tensor maps address routed experts by store slot
+        const int64_t off = job.gate - mp.arena;
+        ok = off >= 0 && off % mp.slot_bytes == 0 && off / mp.slot_bytes < mp.n_slots;
+        if (ok) ti.slot = (int)(off / mp.slot_bytes);
+        else set_error(sc.err, DEV_E_NOT_RESIDENT);
+    }
     const int F = ok ? job.F : 0;
     const int nrt = down ? (sh.D + TC_M - 1) / TC_M : (F + TC_M - 1) / TC_M;
     const int l = t - pre[lo];
@@ -497,154 +504,226 @@ __device__ __forceinline__ void tmem_ld16(uint32_t taddr, uint32_t v[16]) {
     asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory");
 }
 
-// Activation operand of block j for the 32 pairs of a stage (pair rows `pitch` bytes apart):
-// `nthr` threads (tid - t0 in [0, nthr), nthr = 128 or 256) move 16 or 8 bytes each; pairs past nn
-// get zeros. Thread t0 + n (n < 32) also stores the pair's d and -8 * sum (the Q4 offset term).
-__device__ __forceinline__ void unpack_act(const uint8_t *act, int pitch, int j, int nn, uint8_t *bop, float *dx,
-                                           int *c8, int t, int nthr) {
-    const int n = t & 31;
-    const bool live = n < nn;
-    const uint8_t *src = act + n * pitch + j * ACT_BLOCK + 8;
-    if (nthr == 256) {   // 8 bytes: chunk (t >> 5) & 3, half t >> 7
-        const int c = (t >> 5) & 3, h = t >> 7;
-        const uint2 v = live ? *reinterpret_cast<const uint2 *>(src + 16 * c + 8 * h) : make_uint2(0, 0);
-        *reinterpret_cast<uint2 *>(bop + op_off(n, c) + 8 * h) = v;
-    } else {             // 16 bytes: chunk t >> 5
-        const int c = t >> 5;
-        uint2 v0 = make_uint2(0, 0), v1 = make_uint2(0, 0);
-        if (live) {
-            v0 = *reinterpret_cast<const uint2 *>(src + 16 * c);
-            v1 = *reinterpret_cast<const uint2 *>(src + 16 * c + 8);
-        }
-        *reinterpret_cast<uint4 *>(bop + op_off(n, c)) = make_uint4(v0.x, v0.y, v1.x, v1.y);
-    }
-    if (t < 32) {
-        uint2 hd = make_uint2(0, 0);
-        if (live) hd = *reinterpret_cast<const uint2 *>(src - 8);
-        dx[n] = __uint_as_float(hd.x);
-        c8[n] = -8 * (int)hd.y;
+// Tensor-map loads into this CTA's shared memory (no multicast), completion counted on bar. The box
+// origin's x times the element size is a multiple of 16 bytes for every call below.
+__device__ __forceinline__ void tma_load_2d(void *dst, const void *map, int x, int y, uint64_t *bar) {
+    asm volatile(
+        "cp.async.bulk.tensor.2d.shared::cluster.global.tile.mbarrier::complete_tx::bytes [%0], [%1, {%2, %3}], [%4];" ::"r"(
+            smem_u32(dst)),
+        "l"(map), "r"(x), "r"(y), "r"(smem_u32(bar))
+        : "memory");
+}
+
+__device__ __forceinline__ void tma_load_3d(void *dst, const void *map, int x, int y, int z, uint64_t *bar) {
+    asm volatile(
+        "cp.async.bulk.tensor.3d.shared::cluster.global.tile.mbarrier::complete_tx::bytes [%0], [%1, {%2, %3, %4}], "
+        "[%5];" ::"r"(smem_u32(dst)),
+        "l"(map), "r"(x), "r"(y), "r"(z), "r"(smem_u32(bar))
+        : "memory");
+}
+
+// Four rows r0..r3 (box one row high) of a 2-D map, stored one after another.
+__device__ __forceinline__ void tma_gather4(void *dst, const void *map, int x, int r0, int r1, int r2, int r3,
+                                            uint64_t *bar) {
+    asm volatile(
+        "cp.async.bulk.tensor.2d.shared::cluster.global.tile::gather4.mbarrier::complete_tx::bytes [%0], [%1, {%2, %3, "
+        "%4, %5, %6}], [%7];" ::"r"(smem_u32(dst)),
+        "l"(map), "r"(x), "r"(r0), "r"(r1), "r"(r2), "r"(r3), "r"(smem_u32(bar))
+        : "memory");
+}
+
+// ---------------------------------------------------------------------------------------------
+// Warp roles of the staged kernels (448 threads, one CTA per SM):
+//   warps 0-7   drain: read a block's int32 tile from tensor memory and extend the float chains
+//   warps 8-11  unpack: stage rows -> operand A in tensor memory (tcgen05.st), activations ->
+//               operand B in shared memory, scales -> shared memory
+//   warp 12     copies: issues the bulk copies of the stage ring
+//   warp 13     MMA: one elected thread issues tcgen05.mma and commits
+// Operands and accumulators are double-buffered by block; mbarriers hand each buffer from role to
+// role, so unpacking, multiplication, draining and copying of different blocks overlap.
+//
+// Two exact identities keep the drain short:
+//   * Q4 offset: after the u8 (nibble) x s8 MMAs of a block, a second pair of MMAs with a constant
+//     A of -8 (s8) adds -8 * sum(q), so the accumulator holds the signed block dot isum.
+//   * int -> float: the accumulator starts at the bit pattern of 1.5 * 2^23 (0x4B400000). The block
+//     dot changes only the low 23 mantissa bits (|isum| <= 64 * 8 * 127 < 2^22), so the word read
+//     back, taken as a float, equals 12582912 + isum exactly and one subtraction gives (float)isum.
+// The chain's multiplies run as packed f32x2 pairs (two IEEE round-to-nearest products per
+// instruction); its adds stay scalar, in block order as before.
+// ---------------------------------------------------------------------------------------------
+
+constexpr int WS_THREADS = 448;
+constexpr int WS_DRAIN = 256;                    // warps 0-7
+constexpr int WS_UNPACK0 = 256;                  // warps 8-11
+constexpr int WS_COPY_WARP = 12, WS_MMA_WARP = 13;
+constexpr uint32_t kMagic = 0x4B400000u;         // 1.5 * 2^23
+constexpr float kMagicF = 12582912.0f;
+
+__device__ __forceinline__ void mbar_arrive(uint64_t *bar) {
+    asm volatile("mbarrier.arrive.shared::cta.b64 _, [%0];" ::"r"(smem_u32(bar)) : "memory");
+}
+
+__device__ __forceinline__ void tmem_wait_st() { asm volatile("tcgen05.wait::st.sync.aligned;" ::: "memory"); }
+
+__device__ __forceinline__ void tmem_st16(uint32_t taddr, const uint32_t v[16]) {
+    asm volatile(
+        "tcgen05.st.sync.aligned.32x32b.x16.b32 [%0], {%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,%14,%15,%16};" ::"r"(
+            taddr),
+        "r"(v[0]), "r"(v[1]), "r"(v[2]), "r"(v[3]), "r"(v[4]), "r"(v[5]), "r"(v[6]), "r"(v[7]), "r"(v[8]), "r"(v[9]),
+        "r"(v[10]), "r"(v[11]), "r"(v[12]), "r"(v[13]), "r"(v[14]), "r"(v[15])
+        : "memory");
+}
+
+// The same word into 16 consecutive columns of this warp's lanes.
+__device__ __forceinline__ void tmem_fill16(uint32_t taddr, uint32_t x) {
+    asm volatile(
+        "tcgen05.st.sync.aligned.32x32b.x16.b32 [%0], {%1,%1,%1,%1,%1,%1,%1,%1,%1,%1,%1,%1,%1,%1,%1,%1};" ::"r"(taddr),
+        "r"(x)
+        : "memory");
+}
+
+// D[tmem] (+)= A[tmem] x B[smem] (kind::i8, A from tensor memory).
+__device__ __forceinline__ void umma_i8_ts(uint32_t d, uint32_t a, uint64_t db, uint32_t idesc, bool accumulate) {
+    asm volatile(
+        "{\n\t.reg .pred p;\n\tsetp.ne.b32 p, %4, 0;\n\t"
+        "tcgen05.mma.cta_group::1.kind::i8 [%0], [%1], %2, %3, p;\n\t}" ::"r"(d),
+        "r"(a), "l"(db), "r"(idesc), "r"(accumulate ? 1u : 0u));
+}
+
+__device__ __forceinline__ uint64_t pack2(uint32_t lo, uint32_t hi) { return ((uint64_t)hi << 32) | lo; }
+
+__device__ __forceinline__ uint64_t f2_sub(uint64_t a, uint64_t b) {
+    uint64_t d;
+    asm("sub.rn.f32x2 %0, %1, %2;" : "=l"(d) : "l"(a), "l"(b));
+    return d;
+}
+__device__ __forceinline__ uint64_t f2_mul(uint64_t a, uint64_t b) {
+    uint64_t d;
+    asm("mul.rn.f32x2 %0, %1, %2;" : "=l"(d) : "l"(a), "l"(b));
+    return d;
+}
+
+// NC columns of block words v (magic-offset s32 dots) into the chains acc[NC]:
+// acc = acc + isum * (dw * dx[n]). The subtraction and both multiplies run as packed f32x2 pairs; the
+// chain adds stay scalar, because the assembler contracts a packed multiply feeding a packed add into
+// a fused multiply-add even when both carry .rn (measured: most chains then differ in the last bits).
+template <int NC>
+__device__ __forceinline__ void chain_f2(const uint32_t *v, float dw, const float *dx, float *acc) {
+    const uint64_t magic2 = pack2(__float_as_uint(kMagicF), __float_as_uint(kMagicF));
+    const uint64_t dw2 = pack2(__float_as_uint(dw), __float_as_uint(dw));
+#pragma unroll
+    for (int i = 0; i < NC / 2; i++) {
+        const uint64_t dx2 = *reinterpret_cast<const uint64_t *>(dx + 2 * i);
+        const uint64_t isum2 = f2_sub(pack2(v[2 * i], v[2 * i + 1]), magic2);
+        const uint64_t t2 = f2_mul(isum2, f2_mul(dw2, dx2));
+        acc[2 * i] = __fadd_rn(acc[2 * i], __uint_as_float((uint32_t)t2));
+        acc[2 * i + 1] = __fadd_rn(acc[2 * i + 1], __uint_as_float((uint32_t)(t2 >> 32)));
     }
 }
 
-// Q4 float chains of one drained accumulator: NC columns of v against pairs col0 + i.
-template <int NC>
-__device__ __forceinline__ void chain_q4(const uint32_t *v, float dw, const float *dx, const int *c8, int col0,
-                                         float *acc) {
+
+// Activation operand of block J for the 32 pairs of a stage (pair rows `pitch` bytes apart, 16-byte
+// aligned): the 128 unpack threads move one 16-byte chunk each; pairs past nn get zeros, and the
+// thread holding chunk 0 of a pair also stores the pair's d. Thread u = 8k + i takes pair
+// 8 (k & 3) + i and chunk ((i >> CSH) + (k >> 2)) & 3: the eight threads of a shared-memory phase
+// write eight different operand rows, and read eight different 16-byte bank groups when the pitch
+// in 16-byte units is 4 mod 8 (CSH = 1) or 2 or 6 mod 8 (CSH = 2).
+template <int JP, int CSH>   // JP = J & 1: block J's quantized bytes start 16-byte aligned when J is odd
+__device__ __forceinline__ void unpack_act_ws(const uint8_t *act, int pitch, int j, int nn, uint8_t *bop, float *dx,
+                                              int u) {
+    const int k = u >> 3, i = u & 7;
+    const int n = 8 * (k & 3) + i, c = ((i >> CSH) + (k >> 2)) & 3;
+    const bool live = n < nn;
+    const uint8_t *blk = act + n * pitch + j * ACT_BLOCK;
+    uint4 v = make_uint4(0, 0, 0, 0);
+    if (live) {
+        if constexpr (JP == 1) {
+            v = *reinterpret_cast<const uint4 *>(blk + 8 + 16 * c);
+        } else {
+            const uint2 a = *reinterpret_cast<const uint2 *>(blk + 8 + 16 * c);
+            const uint2 b = *reinterpret_cast<const uint2 *>(blk + 16 + 16 * c);
+            v = make_uint4(a.x, a.y, b.x, b.y);
+        }
+    }
+    *reinterpret_cast<uint4 *>(bop + op_off(n, c)) = v;
+    if (c == 0) dx[n] = live ? *reinterpret_cast<const float *>(blk) : 0.0f;
+}
+
+// NUMERICS §2 quantization of the mid values of a tile held in X[pair][128 rows] (shared): unit
+// (pair n, 64-row block b) is quantized by 8 consecutive lanes, 8 rows each (amax and the q sum by
+// 3-step shuffles; the same d, q and sum as act_quant_warp). Called by the 256 drain threads.
+__device__ __forceinline__ void quant_tile(const float *X, const TileInfo &ti, act_q8 *mid, int fmax_nb, int tid) {
+    const int lane = tid & 31;
 #pragma unroll
-    for (int i = 0; i < NC; i++) {
-        const int isum = (int)v[i] + c8[col0 + i];
-        acc[i] = __fadd_rn(acc[i], __fmul_rn(__int2float_rn(isum), __fmul_rn(dw, dx[col0 + i])));
+    for (int k = 0; k < 2; k++) {
+        const int item = tid + k * WS_DRAIN;            // 512 items: (pair, 8-row group)
+        const int n = item >> 4, grp = item & 15, b = grp >> 3, l8 = grp & 7;
+        const bool live = n < ti.nn && ti.rt * TC_M + b * 64 < ti.F;   // uniform over the 8 lanes
+        const float4 x0 = *reinterpret_cast<const float4 *>(X + n * TC_M + grp * 8);
+        const float4 x1 = *reinterpret_cast<const float4 *>(X + n * TC_M + grp * 8 + 4);
+        const float x[8] = {x0.x, x0.y, x0.z, x0.w, x1.x, x1.y, x1.z, x1.w};
+        float amax = fabsf(x[0]);
+#pragma unroll
+        for (int i = 1; i < 8; i++) amax = fmaxf(amax, fabsf(x[i]));   // fmaxf drops NaN
+#pragma unroll
+        for (int o = 4; o >= 1; o >>= 1) amax = fmaxf(amax, __shfl_xor_sync(0xffffffffu, amax, o));
+        amax = fmaxf(amax, 0.0f);
+        const float d = __fdiv_rn(amax, 127.0f);
+        const float id = d != 0.0f ? __fdiv_rn(1.0f, d) : 0.0f;
+        uint32_t qw[2] = {0, 0};
+        int sum = 0;
+#pragma unroll
+        for (int i = 0; i < 8; i++) {
+            float v = __fmul_rn(x[i], id);
+            if (v != v) v = 0.0f;
+            v = v > 127.0f ? 127.0f : (v < -127.0f ? -127.0f : v);
+            const int q = __float2int_rn(v);
+            sum += q;
+            qw[i >> 2] |= ((uint32_t)q & 0xffu) << (8 * (i & 3));
+        }
+#pragma unroll
+        for (int o = 4; o >= 1; o >>= 1) sum += __shfl_xor_sync(0xffffffffu, sum, o);
+        (void)lane;
+        if (live) {
+            act_q8 *o = mid + (int64_t)(ti.p0 + ti.n0 + n) * fmax_nb + ti.rt * 2 + b;
+            *reinterpret_cast<uint2 *>(o->q + 8 * l8) = make_uint2(qw[0], qw[1]);
+            if (l8 == 0) {
+                o->d = d;
+                o->sum = sum;
+            }
+        }
     }
 }
+
+__device__ __forceinline__ void drain_bar() { asm volatile("bar.sync 1, 256;" ::: "memory"); }
 
 // ------------------------------------------------------------------------------------ gate/up
 
 struct GuStage {
-    uint8_t w[2 * TC_M][SG_SEG];    // rows 0..127: gate, 128..255: up
-    uint8_t act[TC_N][SG_ASEG];
+    uint8_t w[2 * TC_M][SG_SEG];    // rows 0..127: gate, 128..255: up (one tensor-map box each)
+    uint8_t act[TC_N][SG_ASEG];     // pair rows (gather4 boxes of four rows)
 };
 
 struct GuSmem {
     GuStage st[2];
-    uint8_t a[2][2][TC_M * 64];     // [operand buffer][gate, up]; the epilogue reuses them as floats
-    uint8_t b[2][TC_N * 64];
+    uint8_t b[2][TC_N * 64];        // operand B (activations) per block buffer
     float dx[2][TC_N];
-    int c8[2][TC_N];
+    float dw[2][2 * TC_M];          // block scales of gate rows, then up rows
+    float X[TC_N * TC_M];           // epilogue: SwiGLU exchange and the mid values
     TileInfo ti[3];
     int pre[SG_MAXJOBS + 1];
-    uint64_t full[2], mma;
+    uint64_t full[2], empty[2], aready[2], accfull[2], accempty[2];
     uint32_t tmem;
 };
-static_assert(sizeof(GuStage) % 16 == 0, "stage slots stay 16-byte aligned");
+static_assert(sizeof(GuStage) % 128 == 0 && (TC_M * SG_SEG) % 128 == 0 && (4 * SG_ASEG) % 128 == 0,
+              "tensor-map destinations stay 128-byte aligned");
 
-// Issues stage q of this CTA (tile q / nS, blocks 8 (q % nS) ..) into slot q & 1.
-__device__ __forceinline__ void gu_issue(GuSmem &s, const MoeShape &sh, const MoeScratch &sc, int q, int nS,
-                                         int ntiles) {
-    const int i = q / nS, st = q % nS, t = blockIdx.x + i * gridDim.x;
-    if (t >= ntiles) return;
-    const TileInfo &ti = s.ti[i % 3];
-    const int tid = threadIdx.x, slot = q & 1;
-    uint64_t *bar = &s.full[slot];
-    const int64_t rbD = (int64_t)(sh.D / QK) * Q4_BLOCK;
-    const int m = tid >> 7, r = tid & (TC_M - 1), row = ti.rt * TC_M + r;
-    fence_proxy_async();   // this thread's earlier shared-memory reads of the slot come first
-    if (row < ti.F) bulk_g2s(s.st[slot].w[tid], (m ? ti.w1 : ti.w0) + row * rbD + st * SG_SEG, SG_SEG, bar);
-    if (tid < ti.nn)
-        bulk_g2s(s.st[slot].act[tid], reinterpret_cast<const uint8_t *>(sc.xact + (int64_t)ti.tok[tid] * (sh.D / QK)) +
-                                          st * SG_ASEG,
-                 SG_ASEG, bar);
-    if (tid == 0) {
-        const int rows = max(0, min(TC_M, ti.F - ti.rt * TC_M));
-        mbar_expect_tx(bar, (uint32_t)(2 * rows * SG_SEG + ti.nn * SG_ASEG));
-    }
-}
+// Tensor-memory columns (256 allocated): accumulators [b] at 64b (gate +0, up +32), operand A [b][m]
+// at 128 + 32b + 16m, the constant -8 operand at 192.
+constexpr uint32_t GU_ACC = 0, GU_A = 128, GU_CORR = 192;
 
-__device__ __forceinline__ void gu_fill_info(GuSmem &s, const MoeShape &sh, const MoeLayerDev &L,
-                                             const MoeScratch &sc, int nu, int njobs, int ntiles, int i) {
-    // warp 1 fills the description of this CTA's tile i (if it exists)
-    const int t = blockIdx.x + i * gridDim.x;
-    if (t >= ntiles) return;
-    TileInfo &ti = s.ti[i % 3];
-    const int lane = threadIdx.x & 31;
-    if (lane == 0) decode_tile(sh, L, sc, nu, njobs, s.pre, t, false, ti);
-    __syncwarp();
-    if (lane < ti.nn) {
-        Job j;
-        j.shared = ti.shared;
-        j.p0 = ti.p0;
-        ti.tok[lane] = job_token(sc, j, ti.n0 + lane);
-    }
-}
-
-template <int J>
-__device__ __forceinline__ uint32_t gu_unpack(GuSmem &s, const TileInfo &ti, int slot, int buf, int tid) {
-    const int m = tid >> 7, r = tid & (TC_M - 1);
-    uint32_t w[16];
-    uint32_t scb = 0;
-    if (ti.rt * TC_M + r < ti.F) {
-        scb = seg_q4_block<J>(s.st[slot].w[tid], w);
-    } else {
-#pragma unroll
-        for (int i = 0; i < 16; i++) w[i] = 0;
-    }
-    store_operand_row(s.a[buf][m], r, w);
-    unpack_act(&s.st[slot].act[0][0], SG_ASEG, J, ti.nn, s.b[buf], s.dx[buf], s.c8[buf], tid, SG_THREADS);
-    return scb;
-}
-
-// j in 0..7; inside the unrolled block loop j is a constant and the switch folds away.
-__device__ __forceinline__ uint32_t gu_unpack_j(GuSmem &s, const TileInfo &ti, int slot, int buf, int tid, int j) {
-    switch (j) {
-    case 0: return gu_unpack<0>(s, ti, slot, buf, tid);
-    case 1: return gu_unpack<1>(s, ti, slot, buf, tid);
-    case 2: return gu_unpack<2>(s, ti, slot, buf, tid);
-    case 3: return gu_unpack<3>(s, ti, slot, buf, tid);
-    case 4: return gu_unpack<4>(s, ti, slot, buf, tid);
-    case 5: return gu_unpack<5>(s, ti, slot, buf, tid);
-    case 6: return gu_unpack<6>(s, ti, slot, buf, tid);
-    default: return gu_unpack<7>(s, ti, slot, buf, tid);
-    }
-}
-
-__device__ __forceinline__ void gu_mma(GuSmem &s, uint32_t tmem, uint32_t idesc, int buf) {
-    const uint32_t sa0 = smem_u32(s.a[buf][0]), sa1 = smem_u32(s.a[buf][1]), sb = smem_u32(s.b[buf]);
-#pragma unroll
-    for (int k = 0; k < 2; k++) {
-        umma_i8(tmem, umma_desc(sa0 + 256 * k), umma_desc(sb + 256 * k), idesc, k > 0);
-        umma_i8(tmem + TC_N, umma_desc(sa1 + 256 * k), umma_desc(sb + 256 * k), idesc, k > 0);
-    }
-    umma_commit(&s.mma);
-}
-
-__device__ __forceinline__ void cta_sync_tc() {
-    fence_proxy_async();
-    tc_fence_before();
-    __syncthreads();
-    tc_fence_after();
-}
-
-__global__ void __launch_bounds__(SG_THREADS, 1) k_moe_gateup_tcs(MoeShape sh, MoeLayerDev L, MoeScratch sc,
-                                                                   int fmax_nb) {
+__global__ void __launch_bounds__(WS_THREADS, 1) k_moe_gateup_ws(MoeShape sh, MoeLayerDev L, MoeScratch sc,
+                                                                  int fmax_nb, const __grid_constant__ TcMaps mp) {
     extern __shared__ __align__(1024) uint8_t smem_raw[];
     GuSmem &s = *reinterpret_cast<GuSmem *>(smem_raw);
     const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
@@ -655,241 +734,420 @@ __global__ void __launch_bounds__(SG_THREADS, 1) k_moe_gateup_tcs(MoeShape sh, M
     const int mytiles = (ntiles - (int)blockIdx.x + (int)gridDim.x - 1) / (int)gridDim.x;
 
     if (tid == 0) {
-        mbar_init(&s.full[0], 1);
-        mbar_init(&s.full[1], 1);
-        mbar_init(&s.mma, 1);
+        for (int b = 0; b < 2; b++) {
+            mbar_init(&s.full[b], 1);
+            mbar_init(&s.empty[b], 128);
+            mbar_init(&s.aready[b], 128);
+            mbar_init(&s.accfull[b], 1);
+            mbar_init(&s.accempty[b], WS_DRAIN);
+        }
         fence_mbar_init();
     }
-    if (warp == 1) {
-        gu_fill_info(s, sh, L, sc, nu, njobs, ntiles, 0);
-        gu_fill_info(s, sh, L, sc, nu, njobs, ntiles, 1);
+    if (warp == 0) {
+        asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], 256;" ::"r"(smem_u32(&s.tmem)));
+        asm volatile("tcgen05.relinquish_alloc_permit.cta_group::1.sync.aligned;");
     }
-    const uint32_t tmem = tmem_alloc(&s.tmem, 2 * TC_N);   // includes a CTA barrier
-    gu_issue(s, sh, sc, 0, nS, ntiles);
-    gu_issue(s, sh, sc, 1, nS, ntiles);
-    const uint32_t idesc = umma_idesc_i8(false);
-    const int m = tid >> 7;
-    uint32_t mma_phase = 0;
+    tc_fence_before();
+    __syncthreads();
+    tc_fence_after();
+    const uint32_t tmem = s.tmem;
 
-    for (int i = 0; i < mytiles; i++) {
-        const TileInfo &ti = s.ti[i % 3];
-        if (warp == 1) gu_fill_info(s, sh, L, sc, nu, njobs, ntiles, i + 2);   // visible after the next barrier
-        float acc[TC_N];
+    if (warp < 8) {
+        // ------------------------------------------------------------------ drain warps
+        const int m = warp >> 2, q4 = warp & 3, r = q4 * 32 + lane;
+        const uint32_t lanes = (uint32_t)(q4 * 32) << 16;
+        for (int b = 0; b < 2; b++) {
+            tmem_fill16(tmem + lanes + GU_ACC + 64 * b + 32 * m, kMagic);
+            tmem_fill16(tmem + lanes + GU_ACC + 64 * b + 32 * m + 16, kMagic);
+        }
+        tmem_wait_st();
+        tc_fence_before();
+        mbar_arrive(&s.accempty[0]);
+        mbar_arrive(&s.accempty[1]);
+        uint32_t G = 0;
+        for (int i = 0; i < mytiles; i++) {
+            TileInfo ti;
+            if (lane == 0) decode_tile(sh, L, sc, mp, nu, njobs, s.pre, blockIdx.x + i * gridDim.x, false, ti);
+            ti.rt = __shfl_sync(0xffffffffu, ti.rt, 0);
+            ti.n0 = __shfl_sync(0xffffffffu, ti.n0, 0);
+            ti.nn = __shfl_sync(0xffffffffu, ti.nn, 0);
+            ti.p0 = __shfl_sync(0xffffffffu, ti.p0, 0);
+            ti.F = __shfl_sync(0xffffffffu, ti.F, 0);
+            float acc[TC_N];
 #pragma unroll
-        for (int n = 0; n < TC_N; n++) acc[n] = 0.0f;
-        float dw_next = 0.0f;
-        for (int s0 = 0; s0 < nS; s0++) {
-            const int q = i * nS + s0, slot = q & 1;
-            mbar_wait(&s.full[slot], (uint32_t)((q >> 1) & 1), sc.err);
-            if (s0 == 0) {   // prologue of the tile: block 0 unpacked and multiplied
-                dw_next = f16_to_f32(gu_unpack<0>(s, ti, slot, 0, tid));
-                cta_sync_tc();
-                if (tid == 0) gu_mma(s, tmem, idesc, 0);
-            }
-#pragma unroll
-            for (int jj = 0; jj < SG_BLK; jj++) {
-                const int g = s0 * SG_BLK + jj;
-                const float dw = dw_next;
-                if (jj + 1 < SG_BLK) {
-                    dw_next = f16_to_f32(gu_unpack_j(s, ti, slot, (g + 1) & 1, tid, jj + 1));
-                } else if (s0 + 1 < nS) {   // block 0 of the next stage
-                    const int q1 = q + 1;
-                    mbar_wait(&s.full[q1 & 1], (uint32_t)((q1 >> 1) & 1), sc.err);
-                    dw_next = f16_to_f32(gu_unpack<0>(s, ti, q1 & 1, (g + 1) & 1, tid));
-                }
-                mbar_wait(&s.mma, mma_phase, sc.err);
-                mma_phase ^= 1;
+            for (int k = 0; k < TC_N; k++) acc[k] = 0.0f;
+            for (int g = 0; g < nbD; g++, G++) {
+                const int b = G & 1;
+                mbar_wait(&s.accfull[b], (G >> 1) & 1, sc.err);
+                mbar_wait(&s.aready[b], (G >> 1) & 1, sc.err);   // acquires the unpackers' scales
                 tc_fence_after();
-                {
-                    uint32_t v[32];
-                    tmem_ld32(tmem + ((uint32_t)((warp & 3) * 32) << 16) + (uint32_t)(m * TC_N), v);
-                    chain_q4<TC_N>(v, dw, s.dx[g & 1], s.c8[g & 1], 0, acc);
+                uint32_t v[32];
+                const uint32_t ta = tmem + lanes + GU_ACC + 64 * b + 32 * m;
+                tmem_ld32(ta, v);
+                tmem_fill16(ta, kMagic);
+                tmem_fill16(ta + 16, kMagic);
+                chain_f2<TC_N>(v, s.dw[b][m * TC_M + r], s.dx[b], acc);
+                tmem_wait_st();
+                tc_fence_before();
+                mbar_arrive(&s.accempty[b]);
+            }
+            // epilogue: SwiGLU (gate warps take pairs 0-15, up warps 16-31; each hands the other half
+            // of its values over through X), then the mid activation blocks
+            float *X = s.X;
+#pragma unroll
+            for (int n = 0; n < TC_N; n++) {
+                const bool give = m == 0 ? n >= TC_N / 2 : n < TC_N / 2;
+                if (give) X[n * TC_M + r] = canon(acc[n]);
+            }
+            drain_bar();
+#pragma unroll
+            for (int n = 0; n < TC_N; n++) {
+                const bool keep = m == 0 ? n < TC_N / 2 : n >= TC_N / 2;
+                if (keep) {
+                    const float a = canon(acc[n]);
+                    float *x = X + n * TC_M + r;
+                    *x = m == 0 ? swiglu_c(a, *x) : swiglu_c(*x, a);
                 }
-                cta_sync_tc();
-                if (jj == SG_BLK - 2) gu_issue(s, sh, sc, q + 2, nS, ntiles);   // slot of stage q is read
-                if (g + 1 < nbD && tid == 0) gu_mma(s, tmem, idesc, (g + 1) & 1);
+            }
+            drain_bar();
+            quant_tile(X, ti, sc.act_mid, fmax_nb, tid);
+            drain_bar();   // X is rewritten by the next tile
+        }
+    } else if (warp < 12) {
+        // ------------------------------------------------------------------ unpack warps
+        const int u = tid - WS_UNPACK0, q4 = warp - 8;
+        const uint32_t lanes = (uint32_t)(q4 * 32) << 16;
+        {
+            uint32_t c[16];
+#pragma unroll
+            for (int k = 0; k < 16; k++) c[k] = 0xf8f8f8f8u;   // -8 as s8, K = 64
+            tmem_st16(tmem + lanes + GU_CORR, c);
+        }
+        uint32_t G = 0;
+        for (int i = 0; i < mytiles; i++) {
+            for (int s0 = 0; s0 < nS; s0++) {
+                const int qs = i * nS + s0, slot = qs & 1;
+                mbar_wait(&s.full[slot], (qs >> 1) & 1, sc.err);
+                const TileInfo &ti = s.ti[i % 3];
+                const bool rowok = ti.rt * TC_M + u < ti.F;
+                const int nn = ti.nn;
+#pragma unroll
+                for (int jj = 0; jj < SG_BLK; jj++, G++) {
+                    const int b = G & 1;
+                    mbar_wait(&s.accempty[b], (G >> 1) & 1, sc.err);
+                    tc_fence_after();
+#pragma unroll
+                    for (int m = 0; m < 2; m++) {
+                        uint32_t w[16];
+                        uint32_t scb = 0;
+                        if (rowok) {
+                            switch (jj) {
+                            case 0: scb = seg_q4_block<0>(s.st[slot].w[m * TC_M + u], w); break;
+                            case 1: scb = seg_q4_block<1>(s.st[slot].w[m * TC_M + u], w); break;
+                            case 2: scb = seg_q4_block<2>(s.st[slot].w[m * TC_M + u], w); break;
+                            case 3: scb = seg_q4_block<3>(s.st[slot].w[m * TC_M + u], w); break;
+                            case 4: scb = seg_q4_block<4>(s.st[slot].w[m * TC_M + u], w); break;
+                            case 5: scb = seg_q4_block<5>(s.st[slot].w[m * TC_M + u], w); break;
+                            case 6: scb = seg_q4_block<6>(s.st[slot].w[m * TC_M + u], w); break;
+                            default: scb = seg_q4_block<7>(s.st[slot].w[m * TC_M + u], w); break;
+                            }
+                        } else {
+#pragma unroll
+                            for (int k = 0; k < 16; k++) w[k] = 0;
+                        }
+                        tmem_st16(tmem + lanes + GU_A + 32 * b + 16 * m, w);
+                        s.dw[b][m * TC_M + u] = f16_to_f32(scb);
+                    }
+                    if (jj & 1) unpack_act_ws<1, 1>(&s.st[slot].act[0][0], SG_ASEG, jj, nn, s.b[b], s.dx[b], u);
+                    else unpack_act_ws<0, 1>(&s.st[slot].act[0][0], SG_ASEG, jj, nn, s.b[b], s.dx[b], u);
+                    if (jj == SG_BLK - 1) mbar_arrive(&s.empty[slot]);   // this thread is done with the slot
+                    tmem_wait_st();
+                    fence_proxy_async();
+                    tc_fence_before();
+                    mbar_arrive(&s.aready[b]);
+                }
             }
         }
-        // epilogue: SwiGLU through shared memory, then the mid activation blocks (NUMERICS §2)
-        float *U = reinterpret_cast<float *>(s.a[0]);   // [32][128]
-        float *M = reinterpret_cast<float *>(s.a[1]);   // [32][128]
-        const int r = tid & (TC_M - 1);
-        if (m == 1) {
+    } else if (warp == WS_COPY_WARP) {
+        // ------------------------------------------------------------------ copy warp
+        for (int i = 0; i < mytiles; i++) {
+            TileInfo &ti = s.ti[i % 3];
+            if (lane == 0) decode_tile(sh, L, sc, mp, nu, njobs, s.pre, blockIdx.x + i * gridDim.x, false, ti);
+            __syncwarp();
+            const int nn = ti.nn, ng = (nn + 3) / 4;
+            const bool wok = ti.w0 != nullptr;
+            int tok = 0;
+            if (lane < nn) {
+                Job j;
+                j.shared = ti.shared;
+                j.p0 = ti.p0;
+                tok = job_token(sc, j, ti.n0 + lane);
+            }
+            const int tok0 = __shfl_sync(0xffffffffu, tok, 0);
+            if (lane >= nn) tok = tok0;   // gather4 fills its four rows; rows past nn are not used
+            int t4[4];
 #pragma unroll
-            for (int n = 0; n < TC_N; n++) U[n * TC_M + r] = canon(acc[n]);
-        }
-        __syncthreads();
-        if (m == 0) {
-#pragma unroll
-            for (int n = 0; n < TC_N; n++) M[n * TC_M + r] = swiglu_c(canon(acc[n]), U[n * TC_M + r]);
-        }
-        __syncthreads();
-        for (int u = warp; u < 2 * TC_N; u += SG_THREADS / 32) {
-            const int n = u >> 1, b = u & 1;
-            if (n < ti.nn && ti.rt * TC_M + b * 64 < ti.F) {
-                act_q8 *o = sc.act_mid + (int64_t)(ti.p0 + ti.n0 + n) * fmax_nb + ti.rt * 2 + b;
-                act_quant_warp(M[n * TC_M + b * 64 + lane], M[n * TC_M + b * 64 + 32 + lane], o, lane);
+            for (int e = 0; e < 4; e++) t4[e] = __shfl_sync(0xffffffffu, tok, (4 * lane + e) & 31);
+            for (int s0 = 0; s0 < nS; s0++) {
+                const int qs = i * nS + s0, slot = qs & 1;
+                if (qs >= 2) mbar_wait(&s.empty[slot], ((qs >> 1) - 1) & 1, sc.err);
+                uint64_t *bar = &s.full[slot];
+                if (lane == 0) {
+                    mbar_expect_tx(bar, (uint32_t)((wok ? 2 * TC_M * SG_SEG : 0) + ng * 4 * SG_ASEG));
+                    if (wok) {
+                        const int x = s0 * (SG_SEG / 4), y = ti.rt * TC_M;
+                        if (ti.shared) {
+                            tma_load_2d(s.st[slot].w[0], mp.sh_gate, x, y, bar);
+                            tma_load_2d(s.st[slot].w[TC_M], mp.sh_up, x, y, bar);
+                        } else {
+                            tma_load_3d(s.st[slot].w[0], mp.gate, x, y, ti.slot, bar);
+                            tma_load_3d(s.st[slot].w[TC_M], mp.up, x, y, ti.slot, bar);
+                        }
+                    }
+                }
+                if (lane < ng)
+                    tma_gather4(s.st[slot].act[4 * lane], mp.xact, s0 * (SG_ASEG / 4), t4[0], t4[1], t4[2], t4[3], bar);
             }
         }
-        __syncthreads();   // U and M are operand buffers again
+    } else {
+        // ------------------------------------------------------------------ MMA warp
+        const uint32_t idesc_u = umma_idesc_i8(false), idesc_s = umma_idesc_i8(true);
+        uint32_t G = 0;
+        for (int i = 0; i < mytiles; i++) {
+            for (int g = 0; g < nbD; g++, G++) {
+                const int b = G & 1;
+                mbar_wait(&s.aready[b], (G >> 1) & 1, sc.err);
+                mbar_wait(&s.accempty[b], (G >> 1) & 1, sc.err);
+                tc_fence_after();
+                if (lane == 0) {
+                    const uint32_t sb = smem_u32(s.b[b]);
+#pragma unroll
+                    for (int m = 0; m < 2; m++) {
+                        const uint32_t d = tmem + GU_ACC + 64 * b + 32 * m, a = tmem + GU_A + 32 * b + 16 * m;
+#pragma unroll
+                        for (int k = 0; k < 2; k++) {
+                            umma_i8_ts(d, a + 8 * k, umma_desc(sb + 256 * k), idesc_u, true);
+                            umma_i8_ts(d, tmem + GU_CORR + 8 * k, umma_desc(sb + 256 * k), idesc_s, true);
+                        }
+                    }
+                    umma_commit(&s.accfull[b]);
+                }
+                __syncwarp();
+            }
+        }
     }
-    tmem_free(tmem, 2 * TC_N);
+    tc_fence_before();
+    __syncthreads();
+    if (warp == 0) asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, 256;" ::"r"(tmem));
 }
 
 // --------------------------------------------------------------------------------------- down
 
+constexpr int DN_SLOT = TC_M * SD_MAXNB * Q4_BLOCK + TC_N * SD_MAXNB * ACT_BLOCK;
+static_assert(DN_SLOT % 128 == 0, "tensor-map destinations stay 128-byte aligned");
+
 struct DnSmem {
-    uint8_t st[2][TC_M * SD_MAXNB * Q4_BLOCK + TC_N * SD_MAXNB * ACT_BLOCK];   // rows, then pairs
-    uint8_t a[2][TC_M * 64];
+    uint8_t st[2][DN_SLOT];         // one tile per slot: its 128 whole rows, then its 32 pair rows
     uint8_t b[2][TC_N * 64];
     float dx[2][TC_N];
-    int c8[2][TC_N];
     float dw[2][TC_M];
     TileInfo ti[3];
     int pre[SG_MAXJOBS + 1];
-    uint64_t full[2], mma;
+    uint64_t full[2], empty[2], aready[2], accfull[2], accempty[2];
     uint32_t tmem;
 };
-static_assert((TC_M * SD_MAXNB * Q4_BLOCK + TC_N * SD_MAXNB * ACT_BLOCK) % 16 == 0, "down slots 16-byte aligned");
 
-// Issues tile i of this CTA (all nbF blocks of its 128 rows and 32 pairs) into slot i & 1.
-// Rows go in groups of rg rows so that every copy is a multiple of 16 bytes.
-__device__ __forceinline__ void dn_issue(DnSmem &s, const MoeShape &sh, const MoeScratch &sc, int i, int ntiles,
-                                         int nbF, int rg, int fmax_nb) {
-    const int t = blockIdx.x + i * gridDim.x;
-    if (t >= ntiles) return;
-    const TileInfo &ti = s.ti[i % 3];
-    const int tid = threadIdx.x, slot = i & 1;
-    uint64_t *bar = &s.full[slot];
-    const int rb = nbF * Q4_BLOCK, pitch = nbF * ACT_BLOCK;
-    const int ngroups = TC_M / rg;
-    const int rows = ti.w0 ? max(0, min(TC_M, sh.D - ti.rt * TC_M)) : 0;
-    fence_proxy_async();
-    if (tid < ngroups && tid * rg < rows)
-        bulk_g2s(s.st[slot] + tid * rg * rb, ti.w0 + (int64_t)(ti.rt * TC_M + tid * rg) * rb, (uint32_t)(rg * rb), bar);
-    const int pn = tid - ngroups;
-    if (pn >= 0 && pn < ti.nn)
-        bulk_g2s(s.st[slot] + TC_M * rb + pn * pitch,
-                 reinterpret_cast<const uint8_t *>(sc.act_mid + (int64_t)(ti.p0 + ti.n0 + pn) * fmax_nb), (uint32_t)pitch,
-                 bar);
-    if (tid == 0) mbar_expect_tx(bar, (uint32_t)(rows * rb + ti.nn * pitch));
-}
+// Tensor-memory columns (128 allocated): accumulators [b] at 32b, operand A [b] at 64 + 16b, the
+// constant -8 operand at 96.
+constexpr uint32_t DN_ACC = 0, DN_A = 64, DN_CORR = 96;
 
-__device__ __forceinline__ void dn_fill_info(DnSmem &s, const MoeShape &sh, const MoeLayerDev &L,
-                                             const MoeScratch &sc, int nu, int njobs, int ntiles, int i) {
-    const int t = blockIdx.x + i * gridDim.x;
-    if (t >= ntiles) return;
-    if ((threadIdx.x & 31) == 0) decode_tile(sh, L, sc, nu, njobs, s.pre, t, true, s.ti[i % 3]);
-}
-
-template <int JM>
-__device__ __forceinline__ void dn_unpack(DnSmem &s, const TileInfo &ti, int slot, int buf, int j, int nbF, int D,
-                                          int tid) {
-    const int rb = nbF * Q4_BLOCK;
-    if (tid < TC_M) {
-        uint32_t w[16];
-        float dw = 0.0f;
-        if (ti.w0 && ti.rt * TC_M + tid < D) {
-            dw = f16_to_f32(row_q4_block<JM>(s.st[slot] + tid * rb, j, w));
-        } else {
-#pragma unroll
-            for (int i = 0; i < 16; i++) w[i] = 0;
-        }
-        store_operand_row(s.a[buf], tid, w);
-        s.dw[buf][tid] = dw;
+template <int JM, int CSH>
+__device__ __forceinline__ void dn_unpack_ws(DnSmem &s, int slot, int b, int j, int rb, int pitch, bool rowok, int nn,
+                                             uint32_t tm_a, int u) {
+    uint32_t w[16];
+    uint32_t scb = 0;
+    if (rowok) {
+        scb = row_q4_block<JM>(s.st[slot] + u * rb, j, w);
     } else {
-        unpack_act(s.st[slot] + TC_M * rb, nbF * ACT_BLOCK, j, ti.nn, s.b[buf], s.dx[buf], s.c8[buf], tid - TC_M, TC_M);
-    }
-}
-
-__device__ __forceinline__ void dn_unpack_j(DnSmem &s, const TileInfo &ti, int slot, int buf, int j, int nbF, int D,
-                                            int tid) {
-    switch (j & 3) {
-    case 0: dn_unpack<0>(s, ti, slot, buf, j, nbF, D, tid); break;
-    case 1: dn_unpack<1>(s, ti, slot, buf, j, nbF, D, tid); break;
-    case 2: dn_unpack<2>(s, ti, slot, buf, j, nbF, D, tid); break;
-    default: dn_unpack<3>(s, ti, slot, buf, j, nbF, D, tid); break;
-    }
-}
-
-__device__ __forceinline__ void dn_mma(DnSmem &s, uint32_t tmem, uint32_t idesc, int buf) {
-    const uint32_t sa = smem_u32(s.a[buf]), sb = smem_u32(s.b[buf]);
 #pragma unroll
-    for (int k = 0; k < 2; k++) umma_i8(tmem, umma_desc(sa + 256 * k), umma_desc(sb + 256 * k), idesc, k > 0);
-    umma_commit(&s.mma);
+        for (int k = 0; k < 16; k++) w[k] = 0;
+    }
+    tmem_st16(tm_a, w);
+    s.dw[b][u] = f16_to_f32(scb);
+    unpack_act_ws<JM & 1, CSH>(s.st[slot] + TC_M * rb, pitch, j, nn, s.b[b], s.dx[b], u);
 }
 
-__global__ void __launch_bounds__(SG_THREADS, 1) k_moe_down_tcs(MoeShape sh, MoeLayerDev L, MoeScratch sc,
-                                                                 int fmax_nb, int nbF, int rg) {
+__global__ void __launch_bounds__(WS_THREADS, 1) k_moe_down_ws(MoeShape sh, MoeLayerDev L, MoeScratch sc,
+                                                                int fmax_nb, int nbF, int rg,
+                                                                const __grid_constant__ TcMaps mp) {
     extern __shared__ __align__(1024) uint8_t smem_raw[];
     DnSmem &s = *reinterpret_cast<DnSmem *>(smem_raw);
-    const int tid = threadIdx.x, warp = tid >> 5;
+    const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
     const int nu = routed_jobs(sh, sc), njobs = nu + (L.Fs > 0 ? 1 : 0);
     const int ntiles = tile_prefix(sh, L, sc, nu, njobs, true, s.pre);
     if ((int)blockIdx.x >= ntiles) return;
     const int mytiles = (ntiles - (int)blockIdx.x + (int)gridDim.x - 1) / (int)gridDim.x;
+    const int rb = nbF * Q4_BLOCK, pitch = nbF * ACT_BLOCK;
+    const bool csh1 = ((pitch / 16) & 7) == 4;   // bank-group step of the pair rows
 
     if (tid == 0) {
-        mbar_init(&s.full[0], 1);
-        mbar_init(&s.full[1], 1);
-        mbar_init(&s.mma, 1);
+        for (int b = 0; b < 2; b++) {
+            mbar_init(&s.full[b], 1);
+            mbar_init(&s.empty[b], 128);
+            mbar_init(&s.aready[b], 128);
+            mbar_init(&s.accfull[b], 1);
+            mbar_init(&s.accempty[b], WS_DRAIN);
+        }
         fence_mbar_init();
     }
-    if (warp == 1) {
-        dn_fill_info(s, sh, L, sc, nu, njobs, ntiles, 0);
-        dn_fill_info(s, sh, L, sc, nu, njobs, ntiles, 1);
+    if (warp == 0) {
+        asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], 128;" ::"r"(smem_u32(&s.tmem)));
+        asm volatile("tcgen05.relinquish_alloc_permit.cta_group::1.sync.aligned;");
     }
-    const uint32_t tmem = tmem_alloc(&s.tmem, TC_N);
-    dn_issue(s, sh, sc, 0, ntiles, nbF, rg, fmax_nb);
-    dn_issue(s, sh, sc, 1, ntiles, nbF, rg, fmax_nb);
-    const uint32_t idesc = umma_idesc_i8(false);
-    const int h = warp >> 2, r = (warp & 3) * 32 + (tid & 31);
-    uint32_t mma_phase = 0;
+    tc_fence_before();
+    __syncthreads();
+    tc_fence_after();
+    const uint32_t tmem = s.tmem;
 
-    for (int i = 0; i < mytiles; i++) {
-        const TileInfo &ti = s.ti[i % 3];
-        const int slot = i & 1;
-        if (warp == 1) dn_fill_info(s, sh, L, sc, nu, njobs, ntiles, i + 2);
-        float acc[TC_N / 2];
+    if (warp < 8) {
+        // ------------------------------------------------------------------ drain warps
+        const int h = warp >> 2, q4 = warp & 3, r = q4 * 32 + lane;
+        const uint32_t lanes = (uint32_t)(q4 * 32) << 16;
+        for (int b = 0; b < 2; b++) tmem_fill16(tmem + lanes + DN_ACC + 32 * b + 16 * h, kMagic);
+        tmem_wait_st();
+        tc_fence_before();
+        mbar_arrive(&s.accempty[0]);
+        mbar_arrive(&s.accempty[1]);
+        uint32_t G = 0;
+        for (int i = 0; i < mytiles; i++) {
+            TileInfo ti;
+            if (lane == 0) decode_tile(sh, L, sc, mp, nu, njobs, s.pre, blockIdx.x + i * gridDim.x, true, ti);
+            const int rt = __shfl_sync(0xffffffffu, ti.rt, 0), n0 = __shfl_sync(0xffffffffu, ti.n0, 0);
+            const int nn = __shfl_sync(0xffffffffu, ti.nn, 0), p0 = __shfl_sync(0xffffffffu, ti.p0, 0);
+            const int shared = __shfl_sync(0xffffffffu, ti.shared, 0);
+            const int ok = __shfl_sync(0xffffffffu, ti.w0 != nullptr ? 1 : 0, 0);
+            float acc[16];
 #pragma unroll
-        for (int n = 0; n < TC_N / 2; n++) acc[n] = 0.0f;
-        mbar_wait(&s.full[slot], (uint32_t)((i >> 1) & 1), sc.err);
-        dn_unpack<0>(s, ti, slot, 0, 0, nbF, sh.D, tid);
-        cta_sync_tc();
-        if (tid == 0) dn_mma(s, tmem, idesc, 0);
-        for (int g0 = 0; g0 < nbF; g0 += 4) {
-#pragma unroll
-            for (int jm = 0; jm < 4; jm++) {
-                const int g = g0 + jm;
-                if (g + 1 < nbF) dn_unpack_j(s, ti, slot, (g + 1) & 1, g + 1, nbF, sh.D, tid);
-                mbar_wait(&s.mma, mma_phase, sc.err);
-                mma_phase ^= 1;
+            for (int k = 0; k < 16; k++) acc[k] = 0.0f;
+            for (int g = 0; g < nbF; g++, G++) {
+                const int b = G & 1;
+                mbar_wait(&s.accfull[b], (G >> 1) & 1, sc.err);
+                mbar_wait(&s.aready[b], (G >> 1) & 1, sc.err);   // acquires the unpackers' scales
                 tc_fence_after();
-                {
-                    uint32_t v[16];
-                    tmem_ld16(tmem + ((uint32_t)((warp & 3) * 32) << 16) + (uint32_t)(h * 16), v);
-                    chain_q4<TC_N / 2>(v, s.dw[g & 1][r], s.dx[g & 1], s.c8[g & 1], h * 16, acc);
-                }
-                cta_sync_tc();
-                if (g == nbF - 2) dn_issue(s, sh, sc, i + 2, ntiles, nbF, rg, fmax_nb);   // slot is read
-                if (g + 1 < nbF && tid == 0) dn_mma(s, tmem, idesc, (g + 1) & 1);
+                uint32_t v[16];
+                const uint32_t ta = tmem + lanes + DN_ACC + 32 * b + 16 * h;
+                tmem_ld16(ta, v);
+                tmem_fill16(ta, kMagic);
+                chain_f2<16>(v, s.dw[b][r], s.dx[b] + 16 * h, acc);
+                tmem_wait_st();
+                tc_fence_before();
+                mbar_arrive(&s.accempty[b]);
             }
-        }
-        const int row = ti.rt * TC_M + r;
-        if (ti.w0 && row < sh.D) {   // canonical outputs: Y [pair][D] (routed) or S [token][D] (shared)
+            const int row = rt * TC_M + r;
+            if (ok && row < sh.D) {   // canonical outputs: Y [pair][D] (routed) or S [token][D] (shared)
 #pragma unroll
-            for (int k = 0; k < TC_N / 2; k++) {
-                const int n = h * 16 + k;
-                if (n < ti.nn) {
-                    float *out = ti.shared ? sc.S + (int64_t)(ti.n0 + n) * sh.D
-                                           : sc.Y + (int64_t)(ti.p0 + ti.n0 + n) * sh.D;
-                    out[row] = canon(acc[k]);
+                for (int k = 0; k < 16; k++) {
+                    const int n = 16 * h + k;
+                    if (n < nn) {
+                        float *out = shared ? sc.S + (int64_t)(n0 + n) * sh.D : sc.Y + (int64_t)(p0 + n0 + n) * sh.D;
+                        out[row] = canon(acc[k]);
+                    }
                 }
             }
         }
-        __syncthreads();   // the next tile's warp 1 rewrites the info slot this epilogue read
+    } else if (warp < 12) {
+        // ------------------------------------------------------------------ unpack warps
+        const int u = tid - WS_UNPACK0, q4 = warp - 8;
+        const uint32_t lanes = (uint32_t)(q4 * 32) << 16;
+        {
+            uint32_t c[16];
+#pragma unroll
+            for (int k = 0; k < 16; k++) c[k] = 0xf8f8f8f8u;
+            tmem_st16(tmem + lanes + DN_CORR, c);
+        }
+        uint32_t G = 0;
+        for (int i = 0; i < mytiles; i++) {
+            const int slot = i & 1;
+            mbar_wait(&s.full[slot], (i >> 1) & 1, sc.err);
+            const TileInfo &ti = s.ti[i % 3];
+            const bool rowok = ti.w0 != nullptr && ti.rt * TC_M + u < sh.D;
+            const int nn = ti.nn;
+            for (int g0 = 0; g0 < nbF; g0 += 4) {
+#pragma unroll
+                for (int jm = 0; jm < 4; jm++, G++) {
+                    const int b = G & 1, j = g0 + jm;
+                    mbar_wait(&s.accempty[b], (G >> 1) & 1, sc.err);
+                    tc_fence_after();
+                    const uint32_t ta = tmem + lanes + DN_A + 16 * b;
+                    if (csh1) {
+                        switch (jm) {
+                        case 0: dn_unpack_ws<0, 1>(s, slot, b, j, rb, pitch, rowok, nn, ta, u); break;
+                        case 1: dn_unpack_ws<1, 1>(s, slot, b, j, rb, pitch, rowok, nn, ta, u); break;
+                        case 2: dn_unpack_ws<2, 1>(s, slot, b, j, rb, pitch, rowok, nn, ta, u); break;
+                        default: dn_unpack_ws<3, 1>(s, slot, b, j, rb, pitch, rowok, nn, ta, u); break;
+                        }
+                    } else {
+                        switch (jm) {
+                        case 0: dn_unpack_ws<0, 2>(s, slot, b, j, rb, pitch, rowok, nn, ta, u); break;
+                        case 1: dn_unpack_ws<1, 2>(s, slot, b, j, rb, pitch, rowok, nn, ta, u); break;
+                        case 2: dn_unpack_ws<2, 2>(s, slot, b, j, rb, pitch, rowok, nn, ta, u); break;
+                        default: dn_unpack_ws<3, 2>(s, slot, b, j, rb, pitch, rowok, nn, ta, u); break;
+                        }
+                    }
+                    if (j == nbF - 1) mbar_arrive(&s.empty[slot]);
+                    tmem_wait_st();
+                    fence_proxy_async();
+                    tc_fence_before();
+                    mbar_arrive(&s.aready[b]);
+                }
+            }
+        }
+    } else if (warp == WS_COPY_WARP) {
+        // ------------------------------------------------------------------ copy warp
+        for (int i = 0; i < mytiles; i++) {
+            const int slot = i & 1;
+            TileInfo &ti = s.ti[i % 3];
+            if (i >= 2) mbar_wait(&s.empty[slot], ((i >> 1) - 1) & 1, sc.err);
+            if (lane == 0) {
+                decode_tile(sh, L, sc, mp, nu, njobs, s.pre, blockIdx.x + i * gridDim.x, true, ti);
+                uint64_t *bar = &s.full[slot];
+                const bool wok = ti.w0 != nullptr;
+                mbar_expect_tx(bar, (uint32_t)(wok ? TC_M * rb + TC_N * pitch : 0));
+                if (wok) {
+                    const int y = ti.rt * TC_M / rg;
+                    if (ti.shared) tma_load_2d(s.st[slot], mp.sh_down, 0, y, bar);
+                    else tma_load_3d(s.st[slot], mp.down, 0, y, ti.slot, bar);
+                    tma_load_2d(s.st[slot] + TC_M * rb, mp.mid, 0, ti.p0 + ti.n0, bar);
+                }
+            }
+            __syncwarp();
+        }
+    } else {
+        // ------------------------------------------------------------------ MMA warp
+        const uint32_t idesc_u = umma_idesc_i8(false), idesc_s = umma_idesc_i8(true);
+        uint32_t G = 0;
+        for (int i = 0; i < mytiles; i++) {
+            for (int g = 0; g < nbF; g++, G++) {
+                const int b = G & 1;
+                mbar_wait(&s.aready[b], (G >> 1) & 1, sc.err);
+                mbar_wait(&s.accempty[b], (G >> 1) & 1, sc.err);
+                tc_fence_after();
+                if (lane == 0) {
+                    const uint32_t sb = smem_u32(s.b[b]), d = tmem + DN_ACC + 32 * b, a = tmem + DN_A + 16 * b;
+#pragma unroll
+                    for (int k = 0; k < 2; k++) {
+                        umma_i8_ts(d, a + 8 * k, umma_desc(sb + 256 * k), idesc_u, true);
+                        umma_i8_ts(d, tmem + DN_CORR + 8 * k, umma_desc(sb + 256 * k), idesc_s, true);
+                    }
+                    umma_commit(&s.accfull[b]);
+                }
+                __syncwarp();
+            }
+        }
     }
-    tmem_free(tmem, TC_N);
+    tc_fence_before();
+    __syncthreads();
+    if (warp == 0) asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, 128;" ::"r"(tmem));
 }
 
 __global__ void __launch_bounds__(TC_THREADS, 3) k_moe_gateup_tc(MoeShape sh, MoeLayerDev L, MoeScratch sc,
@@ -918,25 +1176,6 @@ __global__ void __launch_bounds__(TC_THREADS, 3) k_moe_down_tc(MoeShape sh, MoeL
     else down_tc_body<Q8>(sh, sc, job, rt, n0, fmax_nb, s);
 }
 
-// The staged kernels take Q4 experts (and a Q4 shared expert, if any) with D a multiple of 512 for
-// gate/up (8-block stages) and, for down, F (and Fs) of 4, 8 or 12 blocks (whole rows in a slot).
-static bool staged_gateup_ok(const MoeShape &sh, const MoeLayerDev &L) {
-    const int64_t rbD = (int64_t)(sh.D / QK) * Q4_BLOCK;
-    if (L.expert_dtype != Q4 || (L.Fs > 0 && L.sh_dtype != Q4)) return false;
-    if ((sh.D / QK) % SG_BLK || sh.E + 1 > SG_MAXJOBS || L.off_up % 16) return false;
-    if (L.Fs > 0 && ((reinterpret_cast<uintptr_t>(L.sh_gate) | reinterpret_cast<uintptr_t>(L.sh_up)) & 15)) return false;
-    return rbD % 16 == 0;
-}
-
-static bool staged_down_ok(const MoeShape &sh, const MoeLayerDev &L, int fmax_nb) {
-    if (L.expert_dtype != Q4 || (L.Fs > 0 && L.sh_dtype != Q4)) return false;
-    const int nbF = sh.F / QK;
-    if (L.Fs > 0 && L.Fs != sh.F) return false;   // one row width per launch (whole rows per slot)
-    if (nbF % 4 || nbF > SD_MAXNB || fmax_nb % 2 || sh.E + 1 > SG_MAXJOBS || L.off_down % 16) return false;
-    if (L.Fs > 0 && (reinterpret_cast<uintptr_t>(L.sh_down) & 15)) return false;
-    return true;
-}
-
 static int sm_count() {
     static int n = 0;
     if (!n) {
@@ -958,11 +1197,95 @@ static bool staged_on() {
 
 }  // namespace
 
+// ------------------------------------------------------------------------------ tensor maps
+
+using EncodeTiledFn = CUresult (*)(CUtensorMap *, CUtensorMapDataType, cuuint32_t, void *, const cuuint64_t *,
+                                   const cuuint64_t *, const cuuint32_t *, const cuuint32_t *, CUtensorMapInterleave,
+                                   CUtensorMapSwizzle, CUtensorMapL2promotion, CUtensorMapFloatOOBfill);
+
+static EncodeTiledFn encode_fn() {
+    static EncodeTiledFn fn = [] {
+        void *p = nullptr;
+        cudaDriverEntryPointQueryResult q;
+        if (cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &p, cudaEnableDefault, &q) != cudaSuccess ||
+            q != cudaDriverEntryPointSuccess)
+            p = nullptr;
+        return reinterpret_cast<EncodeTiledFn>(p);
+    }();
+    return fn;
+}
+
+// A map of 32-bit words: rank 2 or 3, dims innermost first, strides in bytes of dims 1.., box.
+static bool encode_u32(uint64_t out[16], const void *base, int rank, const uint64_t *dims, const uint64_t *strides,
+                       const uint32_t *box) {
+    const EncodeTiledFn fn = encode_fn();
+    if (!fn || !base || (reinterpret_cast<uintptr_t>(base) & 15)) return false;
+    cuuint64_t gd[3], gs[2];
+    cuuint32_t bx[3], es[3] = {1, 1, 1};
+    for (int i = 0; i < rank; i++) {
+        gd[i] = dims[i];
+        bx[i] = box[i];
+        if (i + 1 < rank) gs[i] = strides[i];
+    }
+    return fn(reinterpret_cast<CUtensorMap *>(out), CU_TENSOR_MAP_DATA_TYPE_UINT32, (cuuint32_t)rank,
+              const_cast<void *>(base), gd, gs, bx, es, CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_NONE,
+              CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS;
+}
+
+void encode_tc_maps(TcMaps &m, const TcMapSrc &a) {
+    m = TcMaps();
+    m.arena = a.arena;
+    m.slot_bytes = a.slot_bytes;
+    m.n_slots = a.n_slots;
+    m.xact_rows = a.T;
+    const bool q4 = a.expert_dtype == Q4 && (a.Fs == 0 || a.sh_dtype == Q4);
+    if (!q4 || !a.arena || a.slot_bytes % 16 || a.E + 1 > SG_MAXJOBS || a.D % QK || a.F % QK) return;
+    const int nbD = a.D / QK, nbF = a.F / QK;
+    const int64_t rbD = (int64_t)nbD * Q4_BLOCK;
+    const uint64_t S = (uint64_t)a.n_slots, SB = (uint64_t)a.slot_bytes;
+    // gate/up: 8-block stages of 128 rows; activations by gather4 rows of 8 blocks
+    if (nbD % SG_BLK == 0 && a.off_up % 16 == 0) {
+        const uint64_t d3[3] = {(uint64_t)rbD / 4, (uint64_t)a.F, S}, s3[2] = {(uint64_t)rbD, SB};
+        const uint32_t b3[3] = {SG_SEG / 4, TC_M, 1};
+        const uint64_t dx[2] = {(uint64_t)nbD * ACT_BLOCK / 4, (uint64_t)a.T}, sx[1] = {(uint64_t)nbD * ACT_BLOCK};
+        const uint32_t bxa[2] = {SG_ASEG / 4, 1};
+        bool ok = encode_u32(m.gate, a.arena, 3, d3, s3, b3) && encode_u32(m.up, a.arena + a.off_up, 3, d3, s3, b3) &&
+                  encode_u32(m.xact, a.xact, 2, dx, sx, bxa);
+        if (ok && a.Fs > 0) {
+            const uint64_t d2[2] = {(uint64_t)rbD / 4, (uint64_t)a.Fs}, s2[1] = {(uint64_t)rbD};
+            const uint32_t b2[2] = {SG_SEG / 4, TC_M};
+            ok = encode_u32(m.sh_gate, a.sh_gate, 2, d2, s2, b2) && encode_u32(m.sh_up, a.sh_up, 2, d2, s2, b2);
+        }
+        m.gu_ok = ok;
+    }
+    // down: whole rows (nbF of 4, 8 or 12 blocks) in groups of rg rows; mid rows of 32 pairs
+    if (nbF % 4 == 0 && nbF <= SD_MAXNB && (a.Fs == 0 || a.Fs == a.F) && a.fmax_nb == nbF && a.off_down % 16 == 0 &&
+        a.D % TC_M == 0) {
+        int rg = 1;
+        while ((rg * nbF * Q4_BLOCK) % 16) rg <<= 1;
+        const uint64_t gb = (uint64_t)rg * nbF * Q4_BLOCK;
+        const uint64_t d3[3] = {gb / 4, (uint64_t)a.D / rg, S}, s3[2] = {gb, SB};
+        const uint32_t b3[3] = {(uint32_t)(gb / 4), (uint32_t)(TC_M / rg), 1};
+        const uint64_t dm[2] = {(uint64_t)a.fmax_nb * ACT_BLOCK / 4, (uint64_t)a.mid_rows},
+                       sm[1] = {(uint64_t)a.fmax_nb * ACT_BLOCK};
+        const uint32_t bm[2] = {(uint32_t)(nbF * ACT_BLOCK / 4), TC_N};
+        bool ok = gb / 4 <= 256 && encode_u32(m.down, a.arena + a.off_down, 3, d3, s3, b3) &&
+                  encode_u32(m.mid, a.mid, 2, dm, sm, bm);
+        if (ok && a.Fs > 0) {
+            const uint64_t d2[2] = {gb / 4, (uint64_t)a.D / rg}, s2[1] = {gb};
+            const uint32_t b2[2] = {(uint32_t)(gb / 4), (uint32_t)(TC_M / rg)};
+            ok = encode_u32(m.sh_down, a.sh_down, 2, d2, s2, b2);
+        }
+        m.down_rg = rg;
+        m.dn_ok = ok;
+    }
+}
+
 cudaError_t init_tc_attributes() {
-    cudaError_t e = cudaFuncSetAttribute(k_moe_gateup_tcs, cudaFuncAttributeMaxDynamicSharedMemorySize,
+    cudaError_t e = cudaFuncSetAttribute(k_moe_gateup_ws, cudaFuncAttributeMaxDynamicSharedMemorySize,
                                          (int)sizeof(GuSmem));
     if (e == cudaSuccess)
-        e = cudaFuncSetAttribute(k_moe_down_tcs, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)sizeof(DnSmem));
+        e = cudaFuncSetAttribute(k_moe_down_ws, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)sizeof(DnSmem));
     cudaFuncAttributes fa;
     if (e == cudaSuccess) e = cudaFuncGetAttributes(&fa, (const void *)k_moe_gateup_tc);
     if (e == cudaSuccess) e = cudaFuncGetAttributes(&fa, (const void *)k_moe_down_tc);
@@ -976,8 +1299,8 @@ cudaError_t launch_moe_experts_tc(const MoeShape &sh, const MoeLayerDev &L, cons
     const int maxjobs = std::min(E, T * K) + (L.Fs > 0 ? 1 : 0);
     const int maxn = std::max(T, 1);   // a bucket holds at most T pairs (one per token)
     if (which & 1) {
-        if (staged_on() && staged_gateup_ok(sh, L)) {
-            k_moe_gateup_tcs<<<sm_count(), SG_THREADS, sizeof(GuSmem), s>>>(sh, L, sc, fmax_nb);
+        if (staged_on() && L.tc && L.tc->gu_ok && sh.T <= L.tc->xact_rows) {
+            k_moe_gateup_ws<<<sm_count(), WS_THREADS, sizeof(GuSmem), s>>>(sh, L, sc, fmax_nb, *L.tc);
         } else {
             const dim3 grid((unsigned)((std::max(sh.F, L.Fs) + TC_M - 1) / TC_M), (unsigned)maxjobs,
                             (unsigned)((maxn + TC_N - 1) / TC_N));
@@ -985,11 +1308,9 @@ cudaError_t launch_moe_experts_tc(const MoeShape &sh, const MoeLayerDev &L, cons
         }
     }
     if (which & 2) {
-        if (staged_on() && staged_down_ok(sh, L, fmax_nb)) {
-            const int nbF = sh.F / QK;
-            int rg = 1;
-            while ((rg * nbF * Q4_BLOCK) % 16) rg <<= 1;
-            k_moe_down_tcs<<<sm_count(), SG_THREADS, sizeof(DnSmem), s>>>(sh, L, sc, fmax_nb, nbF, rg);
+        if (staged_on() && L.tc && L.tc->dn_ok) {
+            k_moe_down_ws<<<sm_count(), WS_THREADS, sizeof(DnSmem), s>>>(sh, L, sc, fmax_nb, sh.F / QK, L.tc->down_rg,
+                                                                          *L.tc);
         } else {
             const dim3 grid((unsigned)((sh.D + TC_M - 1) / TC_M), (unsigned)maxjobs, (unsigned)((maxn + TC_N - 1) / TC_N));
             k_moe_down_tc<<<grid, TC_THREADS, 0, s>>>(sh, L, sc, fmax_nb);
