@@ -534,28 +534,28 @@ __device__ __forceinline__ void tma_gather4(void *dst, const void *map, int x, i
 
 // ---------------------------------------------------------------------------------------------
 // Warp roles of the staged kernels (448 threads, one CTA per SM):
-//   warps 0-7   drain: read a block's int32 tile from tensor memory and extend the float chains
-//   warps 8-11  unpack: stage rows -> operand A in tensor memory (tcgen05.st), activations ->
-//               operand B in shared memory, scales -> shared memory
-//   warp 12     copies: issues the bulk copies of the stage ring
-//   warp 13     MMA: one elected thread issues tcgen05.mma and commits
-// Operands and accumulators are double-buffered by block; mbarriers hand each buffer from role to
-// role, so unpacking, multiplication, draining and copying of different blocks overlap.
+//   warps 0-7    drain: read a block's int32 tile from tensor memory and extend the float chains
+//   warps 8-11   unpack: stage rows -> operand A in tensor memory (tcgen05.st), activations ->
+//                operand B in shared memory, scales -> shared memory
+//   warp 12      copies: decodes tiles and issues the tensor-map loads of the stage ring
+//   warp 13      MMA: one thread issues each block's tcgen05.mma and commits
+// Operands and accumulators rotate through WS_NBUF buffers by block; mbarriers hand each buffer from
+// role to role, so unpacking, multiplication and draining of different blocks overlap.
 //
-// Two exact identities keep the drain short:
-//   * Q4 offset: after the u8 (nibble) x s8 MMAs of a block, a second pair of MMAs with a constant
-//     A of -8 (s8) adds -8 * sum(q), so the accumulator holds the signed block dot isum.
-//   * int -> float: the accumulator starts at the bit pattern of 1.5 * 2^23 (0x4B400000). The block
-//     dot changes only the low 23 mantissa bits (|isum| <= 64 * 8 * 127 < 2^22), so the word read
-//     back, taken as a float, equals 12582912 + isum exactly and one subtraction gives (float)isum.
-// The chain's multiplies run as packed f32x2 pairs (two IEEE round-to-nearest products per
-// instruction); its adds stay scalar, in block order as before.
+// Two exact identities keep the tensor cores to the plain dots and the drain short. The accumulator
+// starts at the bit pattern of 1.5 * 2^23 (0x4B400000); the u8 (nibble) x s8 dot X of a block
+// changes only its low 23 mantissa bits (|X| <= 64 * 15 * 127 < 2^22), so the word read back, taken
+// as a float, is exactly 12582912 + X. The unpackers store cm = 12582912 + 8 * sum(q) per pair (an
+// integer below 2^24, exact in f32), and one subtraction gives the signed Q4 block dot
+// isum = X - 8 * sum(q) exactly. The chain's multiplies run as packed f32x2 pairs (two IEEE
+// round-to-nearest products per instruction); its adds stay scalar, in block order.
 // ---------------------------------------------------------------------------------------------
 
 constexpr int WS_THREADS = 448;
 constexpr int WS_DRAIN = 256;                    // warps 0-7
-constexpr int WS_UNPACK0 = 256;                  // warps 8-11
+constexpr int WS_UNPACK0 = 256, WS_UNPACK = 128; // warps 8-11
 constexpr int WS_COPY_WARP = 12, WS_MMA_WARP = 13;
+constexpr int WS_NBUF = 4;                       // blocks in flight between the roles
 constexpr uint32_t kMagic = 0x4B400000u;         // 1.5 * 2^23
 constexpr float kMagicF = 12582912.0f;
 
@@ -582,15 +582,16 @@ __device__ __forceinline__ void tmem_fill16(uint32_t taddr, uint32_t x) {
         : "memory");
 }
 
-// D[tmem] (+)= A[tmem] x B[smem] (kind::i8, A from tensor memory).
-__device__ __forceinline__ void umma_i8_ts(uint32_t d, uint32_t a, uint64_t db, uint32_t idesc, bool accumulate) {
+// D[tmem] += A[tmem] x B[smem] (kind::i8, A from tensor memory).
+__device__ __forceinline__ void umma_i8_ts(uint32_t d, uint32_t a, uint64_t db, uint32_t idesc) {
     asm volatile(
-        "{\n\t.reg .pred p;\n\tsetp.ne.b32 p, %4, 0;\n\t"
+        "{\n\t.reg .pred p;\n\tsetp.ne.b32 p, 1, 0;\n\t"
         "tcgen05.mma.cta_group::1.kind::i8 [%0], [%1], %2, %3, p;\n\t}" ::"r"(d),
-        "r"(a), "l"(db), "r"(idesc), "r"(accumulate ? 1u : 0u));
+        "r"(a), "l"(db), "r"(idesc));
 }
 
 __device__ __forceinline__ uint64_t pack2(uint32_t lo, uint32_t hi) { return ((uint64_t)hi << 32) | lo; }
+__device__ __forceinline__ uint64_t pack2f(float lo, float hi) { return pack2(__float_as_uint(lo), __float_as_uint(hi)); }
 
 __device__ __forceinline__ uint64_t f2_sub(uint64_t a, uint64_t b) {
     uint64_t d;
@@ -603,34 +604,38 @@ __device__ __forceinline__ uint64_t f2_mul(uint64_t a, uint64_t b) {
     return d;
 }
 
-// NC columns of block words v (magic-offset s32 dots) into the chains acc[NC]:
-// acc = acc + isum * (dw * dx[n]). The subtraction and both multiplies run as packed f32x2 pairs; the
-// chain adds stay scalar, because the assembler contracts a packed multiply feeding a packed add into
-// a fused multiply-add even when both carry .rn (measured: most chains then differ in the last bits).
+// Per-block pair constants in shared memory, interleaved for the drain: entry i holds
+// {cm[2i], cm[2i+1], dx[2i], dx[2i+1]}.
+struct PairConst {
+    float4 v[TC_N / 2];
+};
+
+// NC columns of block words v (magic-offset u8 x s8 dots) into the chains acc[NC]:
+// acc = acc + isum * (dw * dx[n]). The chain adds stay scalar because the assembler contracts a packed
+// multiply feeding a packed add into a fused multiply-add even when both carry .rn (measured: most
+// chains then differ in the last bits).
 template <int NC>
-__device__ __forceinline__ void chain_f2(const uint32_t *v, float dw, const float *dx, float *acc) {
-    const uint64_t magic2 = pack2(__float_as_uint(kMagicF), __float_as_uint(kMagicF));
-    const uint64_t dw2 = pack2(__float_as_uint(dw), __float_as_uint(dw));
+__device__ __forceinline__ void chain_f2(const uint32_t *v, float dw, const float4 *pc, float *acc) {
+    const uint64_t dw2 = pack2f(dw, dw);
 #pragma unroll
     for (int i = 0; i < NC / 2; i++) {
-        const uint64_t dx2 = *reinterpret_cast<const uint64_t *>(dx + 2 * i);
-        const uint64_t isum2 = f2_sub(pack2(v[2 * i], v[2 * i + 1]), magic2);
-        const uint64_t t2 = f2_mul(isum2, f2_mul(dw2, dx2));
+        const float4 q = pc[i];
+        const uint64_t isum2 = f2_sub(pack2(v[2 * i], v[2 * i + 1]), pack2f(q.x, q.y));
+        const uint64_t t2 = f2_mul(isum2, f2_mul(dw2, pack2f(q.z, q.w)));
         acc[2 * i] = __fadd_rn(acc[2 * i], __uint_as_float((uint32_t)t2));
         acc[2 * i + 1] = __fadd_rn(acc[2 * i + 1], __uint_as_float((uint32_t)(t2 >> 32)));
     }
 }
 
-
 // Activation operand of block J for the 32 pairs of a stage (pair rows `pitch` bytes apart, 16-byte
-// aligned): the 128 unpack threads move one 16-byte chunk each; pairs past nn get zeros, and the
-// thread holding chunk 0 of a pair also stores the pair's d. Thread u = 8k + i takes pair
+// aligned): 128 threads (u = 0..127) move one 16-byte chunk each; pairs past nn get zeros, and the
+// thread holding chunk 0 of a pair also stores the pair's dx and cm. Thread u = 8k + i takes pair
 // 8 (k & 3) + i and chunk ((i >> CSH) + (k >> 2)) & 3: the eight threads of a shared-memory phase
 // write eight different operand rows, and read eight different 16-byte bank groups when the pitch
 // in 16-byte units is 4 mod 8 (CSH = 1) or 2 or 6 mod 8 (CSH = 2).
 template <int JP, int CSH>   // JP = J & 1: block J's quantized bytes start 16-byte aligned when J is odd
-__device__ __forceinline__ void unpack_act_ws(const uint8_t *act, int pitch, int j, int nn, uint8_t *bop, float *dx,
-                                              int u) {
+__device__ __forceinline__ void unpack_act_ws(const uint8_t *act, int pitch, int j, int nn, uint8_t *bop,
+                                              PairConst &pc, int u) {
     const int k = u >> 3, i = u & 7;
     const int n = 8 * (k & 3) + i, c = ((i >> CSH) + (k >> 2)) & 3;
     const bool live = n < nn;
@@ -646,14 +651,18 @@ __device__ __forceinline__ void unpack_act_ws(const uint8_t *act, int pitch, int
         }
     }
     *reinterpret_cast<uint4 *>(bop + op_off(n, c)) = v;
-    if (c == 0) dx[n] = live ? *reinterpret_cast<const float *>(blk) : 0.0f;
+    if (c == 0) {
+        const uint2 hd = live ? *reinterpret_cast<const uint2 *>(blk) : make_uint2(0, 0);
+        float *e = reinterpret_cast<float *>(&pc.v[n >> 1]) + (n & 1);
+        e[0] = __int2float_rn(12582912 + 8 * (int)hd.y);   // cm: exact (below 2^24)
+        e[2] = __uint_as_float(hd.x);                        // dx
+    }
 }
 
 // NUMERICS §2 quantization of the mid values of a tile held in X[pair][128 rows] (shared): unit
 // (pair n, 64-row block b) is quantized by 8 consecutive lanes, 8 rows each (amax and the q sum by
 // 3-step shuffles; the same d, q and sum as act_quant_warp). Called by the 256 drain threads.
 __device__ __forceinline__ void quant_tile(const float *X, const TileInfo &ti, act_q8 *mid, int fmax_nb, int tid) {
-    const int lane = tid & 31;
 #pragma unroll
     for (int k = 0; k < 2; k++) {
         const int item = tid + k * WS_DRAIN;            // 512 items: (pair, 8-row group)
@@ -683,7 +692,6 @@ __device__ __forceinline__ void quant_tile(const float *X, const TileInfo &ti, a
         }
 #pragma unroll
         for (int o = 4; o >= 1; o >>= 1) sum += __shfl_xor_sync(0xffffffffu, sum, o);
-        (void)lane;
         if (live) {
             act_q8 *o = mid + (int64_t)(ti.p0 + ti.n0 + n) * fmax_nb + ti.rt * 2 + b;
             *reinterpret_cast<uint2 *>(o->q + 8 * l8) = make_uint2(qw[0], qw[1]);
@@ -697,6 +705,26 @@ __device__ __forceinline__ void quant_tile(const float *X, const TileInfo &ti, a
 
 __device__ __forceinline__ void drain_bar() { asm volatile("bar.sync 1, 256;" ::: "memory"); }
 
+// Barriers and scratch shared by both staged kernels.
+struct WsSync {
+    uint64_t full[2], empty[2];                       // stage ring: copies landed / unpackers done
+    uint64_t aready[WS_NBUF], accfull[WS_NBUF], accempty[WS_NBUF];
+    uint32_t tmem;
+};
+
+__device__ __forceinline__ void ws_init(WsSync &y) {
+    for (int b = 0; b < 2; b++) {
+        mbar_init(&y.full[b], 1);
+        mbar_init(&y.empty[b], WS_UNPACK);
+    }
+    for (int b = 0; b < WS_NBUF; b++) {
+        mbar_init(&y.aready[b], WS_UNPACK);
+        mbar_init(&y.accfull[b], 1);
+        mbar_init(&y.accempty[b], WS_DRAIN);
+    }
+    fence_mbar_init();
+}
+
 // ------------------------------------------------------------------------------------ gate/up
 
 struct GuStage {
@@ -706,26 +734,67 @@ struct GuStage {
 
 struct GuSmem {
     GuStage st[2];
-    uint8_t b[2][TC_N * 64];        // operand B (activations) per block buffer
-    float dx[2][TC_N];
-    float dw[2][2 * TC_M];          // block scales of gate rows, then up rows
+    uint8_t b[WS_NBUF][TC_N * 64];  // operand B (activations) per block buffer
+    PairConst pc[WS_NBUF];
+    float dw[WS_NBUF][2 * TC_M];    // block scales of gate rows, then up rows
     float X[TC_N * TC_M];           // epilogue: SwiGLU exchange and the mid values
     TileInfo ti[3];
     int pre[SG_MAXJOBS + 1];
-    uint64_t full[2], empty[2], aready[2], accfull[2], accempty[2];
-    uint32_t tmem;
+    WsSync y;
 };
 static_assert(sizeof(GuStage) % 128 == 0 && (TC_M * SG_SEG) % 128 == 0 && (4 * SG_ASEG) % 128 == 0,
               "tensor-map destinations stay 128-byte aligned");
 
-// Tensor-memory columns (256 allocated): accumulators [b] at 64b (gate +0, up +32), operand A [b][m]
-// at 128 + 32b + 16m, the constant -8 operand at 192.
-constexpr uint32_t GU_ACC = 0, GU_A = 128, GU_CORR = 192;
+// Tensor-memory columns (512 allocated): accumulators [b] at 64b (gate +0, up +32), operand A [b][m]
+// at 256 + 32b + 16m.
+constexpr uint32_t GU_ACC = 0, GU_A = 256, GU_TMEM_COLS = 512;
+
+// Tensor-map loads of gate/up stage qs (tile qs / nS, blocks 8 (qs % nS) ..) into slot qs & 1, by
+// the copy warp. The stage's tile description is decoded into the info ring at its first stage.
+__device__ __forceinline__ void gu_issue_stage(GuSmem &s, const MoeShape &sh, const MoeLayerDev &L,
+                                               const MoeScratch &sc, const TcMaps &mp, int nu, int njobs, int ntiles,
+                                               int nS, int qs) {
+    const int i = qs / nS, s0 = qs % nS, t = blockIdx.x + i * gridDim.x, lane = threadIdx.x & 31;
+    if (t >= ntiles) return;
+    TileInfo &ti = s.ti[i % 3];
+    if (s0 == 0 && lane == 0) decode_tile(sh, L, sc, mp, nu, njobs, s.pre, t, false, ti);
+    __syncwarp();
+    const int nn = ti.nn, ng = (nn + 3) / 4, slot = qs & 1;
+    const bool wok = ti.w0 != nullptr;
+    int tok = 0;
+    if (lane < nn) {
+        Job j;
+        j.shared = ti.shared;
+        j.p0 = ti.p0;
+        tok = job_token(sc, j, ti.n0 + lane);
+    }
+    const int tok0 = __shfl_sync(0xffffffffu, tok, 0);
+    if (lane >= nn) tok = tok0;   // gather4 fills its four rows; rows past nn are not used
+    int t4[4];
+#pragma unroll
+    for (int e = 0; e < 4; e++) t4[e] = __shfl_sync(0xffffffffu, tok, (4 * lane + e) & 31);
+    uint64_t *bar = &s.y.full[slot];
+    if (lane == 0) {
+        mbar_expect_tx(bar, (uint32_t)((wok ? 2 * TC_M * SG_SEG : 0) + ng * 4 * SG_ASEG));
+        if (wok) {
+            const int x = s0 * (SG_SEG / 4), yr = ti.rt * TC_M;
+            if (ti.shared) {
+                tma_load_2d(s.st[slot].w[0], mp.sh_gate, x, yr, bar);
+                tma_load_2d(s.st[slot].w[TC_M], mp.sh_up, x, yr, bar);
+            } else {
+                tma_load_3d(s.st[slot].w[0], mp.gate, x, yr, ti.slot, bar);
+                tma_load_3d(s.st[slot].w[TC_M], mp.up, x, yr, ti.slot, bar);
+            }
+        }
+    }
+    if (lane < ng) tma_gather4(s.st[slot].act[4 * lane], mp.xact, s0 * (SG_ASEG / 4), t4[0], t4[1], t4[2], t4[3], bar);
+}
 
 __global__ void __launch_bounds__(WS_THREADS, 1) k_moe_gateup_ws(MoeShape sh, MoeLayerDev L, MoeScratch sc,
                                                                   int fmax_nb, const __grid_constant__ TcMaps mp) {
     extern __shared__ __align__(1024) uint8_t smem_raw[];
     GuSmem &s = *reinterpret_cast<GuSmem *>(smem_raw);
+    WsSync &y = s.y;
     const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
     const int nu = routed_jobs(sh, sc), njobs = nu + (L.Fs > 0 ? 1 : 0);
     const int ntiles = tile_prefix(sh, L, sc, nu, njobs, false, s.pre);
@@ -733,37 +802,28 @@ __global__ void __launch_bounds__(WS_THREADS, 1) k_moe_gateup_ws(MoeShape sh, Mo
     const int nbD = sh.D / QK, nS = nbD / SG_BLK;
     const int mytiles = (ntiles - (int)blockIdx.x + (int)gridDim.x - 1) / (int)gridDim.x;
 
-    if (tid == 0) {
-        for (int b = 0; b < 2; b++) {
-            mbar_init(&s.full[b], 1);
-            mbar_init(&s.empty[b], 128);
-            mbar_init(&s.aready[b], 128);
-            mbar_init(&s.accfull[b], 1);
-            mbar_init(&s.accempty[b], WS_DRAIN);
-        }
-        fence_mbar_init();
-    }
+    if (tid == 0) ws_init(y);
     if (warp == 0) {
-        asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], 256;" ::"r"(smem_u32(&s.tmem)));
+        asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(smem_u32(&y.tmem)),
+                     "r"(GU_TMEM_COLS));
         asm volatile("tcgen05.relinquish_alloc_permit.cta_group::1.sync.aligned;");
     }
     tc_fence_before();
     __syncthreads();
     tc_fence_after();
-    const uint32_t tmem = s.tmem;
+    const uint32_t tmem = y.tmem;
 
     if (warp < 8) {
         // ------------------------------------------------------------------ drain warps
         const int m = warp >> 2, q4 = warp & 3, r = q4 * 32 + lane;
         const uint32_t lanes = (uint32_t)(q4 * 32) << 16;
-        for (int b = 0; b < 2; b++) {
+        for (int b = 0; b < WS_NBUF; b++) {
             tmem_fill16(tmem + lanes + GU_ACC + 64 * b + 32 * m, kMagic);
             tmem_fill16(tmem + lanes + GU_ACC + 64 * b + 32 * m + 16, kMagic);
         }
         tmem_wait_st();
         tc_fence_before();
-        mbar_arrive(&s.accempty[0]);
-        mbar_arrive(&s.accempty[1]);
+        for (int b = 0; b < WS_NBUF; b++) mbar_arrive(&y.accempty[b]);
         uint32_t G = 0;
         for (int i = 0; i < mytiles; i++) {
             TileInfo ti;
@@ -777,19 +837,20 @@ __global__ void __launch_bounds__(WS_THREADS, 1) k_moe_gateup_ws(MoeShape sh, Mo
 #pragma unroll
             for (int k = 0; k < TC_N; k++) acc[k] = 0.0f;
             for (int g = 0; g < nbD; g++, G++) {
-                const int b = G & 1;
-                mbar_wait(&s.accfull[b], (G >> 1) & 1, sc.err);
-                mbar_wait(&s.aready[b], (G >> 1) & 1, sc.err);   // acquires the unpackers' scales
+                const int b = G % WS_NBUF;
+                const uint32_t par = (G / WS_NBUF) & 1;
+                mbar_wait(&y.accfull[b], par, sc.err);
+                mbar_wait(&y.aready[b], par, sc.err);   // acquires the unpackers' scales
                 tc_fence_after();
                 uint32_t v[32];
                 const uint32_t ta = tmem + lanes + GU_ACC + 64 * b + 32 * m;
                 tmem_ld32(ta, v);
                 tmem_fill16(ta, kMagic);
                 tmem_fill16(ta + 16, kMagic);
-                chain_f2<TC_N>(v, s.dw[b][m * TC_M + r], s.dx[b], acc);
+                chain_f2<TC_N>(v, s.dw[b][m * TC_M + r], s.pc[b].v, acc);
                 tmem_wait_st();
                 tc_fence_before();
-                mbar_arrive(&s.accempty[b]);
+                mbar_arrive(&y.accempty[b]);
             }
             // epilogue: SwiGLU (gate warps take pairs 0-15, up warps 16-31; each hands the other half
             // of its values over through X), then the mid activation blocks
@@ -813,43 +874,38 @@ __global__ void __launch_bounds__(WS_THREADS, 1) k_moe_gateup_ws(MoeShape sh, Mo
             quant_tile(X, ti, sc.act_mid, fmax_nb, tid);
             drain_bar();   // X is rewritten by the next tile
         }
-    } else if (warp < 12) {
+    } else if (warp < WS_COPY_WARP) {
         // ------------------------------------------------------------------ unpack warps
-        const int u = tid - WS_UNPACK0, q4 = warp - 8;
+        const int u = tid - WS_UNPACK0, q4 = warp & 3;   // row u of gate and of up
         const uint32_t lanes = (uint32_t)(q4 * 32) << 16;
-        {
-            uint32_t c[16];
-#pragma unroll
-            for (int k = 0; k < 16; k++) c[k] = 0xf8f8f8f8u;   // -8 as s8, K = 64
-            tmem_st16(tmem + lanes + GU_CORR, c);
-        }
         uint32_t G = 0;
         for (int i = 0; i < mytiles; i++) {
             for (int s0 = 0; s0 < nS; s0++) {
                 const int qs = i * nS + s0, slot = qs & 1;
-                mbar_wait(&s.full[slot], (qs >> 1) & 1, sc.err);
+                mbar_wait(&y.full[slot], (qs >> 1) & 1, sc.err);
                 const TileInfo &ti = s.ti[i % 3];
                 const bool rowok = ti.rt * TC_M + u < ti.F;
                 const int nn = ti.nn;
 #pragma unroll
                 for (int jj = 0; jj < SG_BLK; jj++, G++) {
-                    const int b = G & 1;
-                    mbar_wait(&s.accempty[b], (G >> 1) & 1, sc.err);
+                    const int b = G % WS_NBUF;
+                    mbar_wait(&y.accempty[b], (G / WS_NBUF) & 1, sc.err);
                     tc_fence_after();
 #pragma unroll
                     for (int m = 0; m < 2; m++) {
+                        const uint8_t *row = s.st[slot].w[m * TC_M + u];
                         uint32_t w[16];
                         uint32_t scb = 0;
                         if (rowok) {
                             switch (jj) {
-                            case 0: scb = seg_q4_block<0>(s.st[slot].w[m * TC_M + u], w); break;
-                            case 1: scb = seg_q4_block<1>(s.st[slot].w[m * TC_M + u], w); break;
-                            case 2: scb = seg_q4_block<2>(s.st[slot].w[m * TC_M + u], w); break;
-                            case 3: scb = seg_q4_block<3>(s.st[slot].w[m * TC_M + u], w); break;
-                            case 4: scb = seg_q4_block<4>(s.st[slot].w[m * TC_M + u], w); break;
-                            case 5: scb = seg_q4_block<5>(s.st[slot].w[m * TC_M + u], w); break;
-                            case 6: scb = seg_q4_block<6>(s.st[slot].w[m * TC_M + u], w); break;
-                            default: scb = seg_q4_block<7>(s.st[slot].w[m * TC_M + u], w); break;
+                            case 0: scb = seg_q4_block<0>(row, w); break;
+                            case 1: scb = seg_q4_block<1>(row, w); break;
+                            case 2: scb = seg_q4_block<2>(row, w); break;
+                            case 3: scb = seg_q4_block<3>(row, w); break;
+                            case 4: scb = seg_q4_block<4>(row, w); break;
+                            case 5: scb = seg_q4_block<5>(row, w); break;
+                            case 6: scb = seg_q4_block<6>(row, w); break;
+                            default: scb = seg_q4_block<7>(row, w); break;
                             }
                         } else {
 #pragma unroll
@@ -858,87 +914,47 @@ __global__ void __launch_bounds__(WS_THREADS, 1) k_moe_gateup_ws(MoeShape sh, Mo
                         tmem_st16(tmem + lanes + GU_A + 32 * b + 16 * m, w);
                         s.dw[b][m * TC_M + u] = f16_to_f32(scb);
                     }
-                    if (jj & 1) unpack_act_ws<1, 1>(&s.st[slot].act[0][0], SG_ASEG, jj, nn, s.b[b], s.dx[b], u);
-                    else unpack_act_ws<0, 1>(&s.st[slot].act[0][0], SG_ASEG, jj, nn, s.b[b], s.dx[b], u);
-                    if (jj == SG_BLK - 1) mbar_arrive(&s.empty[slot]);   // this thread is done with the slot
+                    if (jj & 1) unpack_act_ws<1, 1>(&s.st[slot].act[0][0], SG_ASEG, jj, nn, s.b[b], s.pc[b], u);
+                    else unpack_act_ws<0, 1>(&s.st[slot].act[0][0], SG_ASEG, jj, nn, s.b[b], s.pc[b], u);
+                    if (jj == SG_BLK - 1) mbar_arrive(&y.empty[slot]);   // this thread is done with the slot
                     tmem_wait_st();
                     fence_proxy_async();
                     tc_fence_before();
-                    mbar_arrive(&s.aready[b]);
+                    mbar_arrive(&y.aready[b]);
                 }
             }
         }
     } else if (warp == WS_COPY_WARP) {
         // ------------------------------------------------------------------ copy warp
-        for (int i = 0; i < mytiles; i++) {
-            TileInfo &ti = s.ti[i % 3];
-            if (lane == 0) decode_tile(sh, L, sc, mp, nu, njobs, s.pre, blockIdx.x + i * gridDim.x, false, ti);
-            __syncwarp();
-            const int nn = ti.nn, ng = (nn + 3) / 4;
-            const bool wok = ti.w0 != nullptr;
-            int tok = 0;
-            if (lane < nn) {
-                Job j;
-                j.shared = ti.shared;
-                j.p0 = ti.p0;
-                tok = job_token(sc, j, ti.n0 + lane);
-            }
-            const int tok0 = __shfl_sync(0xffffffffu, tok, 0);
-            if (lane >= nn) tok = tok0;   // gather4 fills its four rows; rows past nn are not used
-            int t4[4];
-#pragma unroll
-            for (int e = 0; e < 4; e++) t4[e] = __shfl_sync(0xffffffffu, tok, (4 * lane + e) & 31);
-            for (int s0 = 0; s0 < nS; s0++) {
-                const int qs = i * nS + s0, slot = qs & 1;
-                if (qs >= 2) mbar_wait(&s.empty[slot], ((qs >> 1) - 1) & 1, sc.err);
-                uint64_t *bar = &s.full[slot];
-                if (lane == 0) {
-                    mbar_expect_tx(bar, (uint32_t)((wok ? 2 * TC_M * SG_SEG : 0) + ng * 4 * SG_ASEG));
-                    if (wok) {
-                        const int x = s0 * (SG_SEG / 4), y = ti.rt * TC_M;
-                        if (ti.shared) {
-                            tma_load_2d(s.st[slot].w[0], mp.sh_gate, x, y, bar);
-                            tma_load_2d(s.st[slot].w[TC_M], mp.sh_up, x, y, bar);
-                        } else {
-                            tma_load_3d(s.st[slot].w[0], mp.gate, x, y, ti.slot, bar);
-                            tma_load_3d(s.st[slot].w[TC_M], mp.up, x, y, ti.slot, bar);
-                        }
-                    }
-                }
-                if (lane < ng)
-                    tma_gather4(s.st[slot].act[4 * lane], mp.xact, s0 * (SG_ASEG / 4), t4[0], t4[1], t4[2], t4[3], bar);
-            }
+        for (int qs = 0; qs < mytiles * nS; qs++) {
+            if (qs >= 2) mbar_wait(&y.empty[qs & 1], ((qs >> 1) - 1) & 1, sc.err);
+            gu_issue_stage(s, sh, L, sc, mp, nu, njobs, ntiles, nS, qs);
         }
     } else {
         // ------------------------------------------------------------------ MMA warp
-        const uint32_t idesc_u = umma_idesc_i8(false), idesc_s = umma_idesc_i8(true);
-        uint32_t G = 0;
-        for (int i = 0; i < mytiles; i++) {
-            for (int g = 0; g < nbD; g++, G++) {
-                const int b = G & 1;
-                mbar_wait(&s.aready[b], (G >> 1) & 1, sc.err);
-                mbar_wait(&s.accempty[b], (G >> 1) & 1, sc.err);
-                tc_fence_after();
-                if (lane == 0) {
-                    const uint32_t sb = smem_u32(s.b[b]);
+        const uint32_t idesc = umma_idesc_i8(false);
+        for (uint32_t G = 0; G < (uint32_t)(mytiles * nbD); G++) {
+            const int b = G % WS_NBUF;
+            const uint32_t par = (G / WS_NBUF) & 1;
+            mbar_wait(&y.aready[b], par, sc.err);
+            mbar_wait(&y.accempty[b], par, sc.err);
+            tc_fence_after();
+            if (lane == 0) {
+                const uint32_t sb = smem_u32(s.b[b]);
 #pragma unroll
-                    for (int m = 0; m < 2; m++) {
-                        const uint32_t d = tmem + GU_ACC + 64 * b + 32 * m, a = tmem + GU_A + 32 * b + 16 * m;
+                for (int m = 0; m < 2; m++) {
+                    const uint32_t d = tmem + GU_ACC + 64 * b + 32 * m, a = tmem + GU_A + 32 * b + 16 * m;
 #pragma unroll
-                        for (int k = 0; k < 2; k++) {
-                            umma_i8_ts(d, a + 8 * k, umma_desc(sb + 256 * k), idesc_u, true);
-                            umma_i8_ts(d, tmem + GU_CORR + 8 * k, umma_desc(sb + 256 * k), idesc_s, true);
-                        }
-                    }
-                    umma_commit(&s.accfull[b]);
+                    for (int k = 0; k < 2; k++) umma_i8_ts(d, a + 8 * k, umma_desc(sb + 256 * k), idesc);
                 }
-                __syncwarp();
+                umma_commit(&y.accfull[b]);
             }
+            __syncwarp();
         }
     }
     tc_fence_before();
     __syncthreads();
-    if (warp == 0) asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, 256;" ::"r"(tmem));
+    if (warp == 0) asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(tmem), "r"(GU_TMEM_COLS));
 }
 
 // --------------------------------------------------------------------------------------- down
@@ -948,33 +964,54 @@ static_assert(DN_SLOT % 128 == 0, "tensor-map destinations stay 128-byte aligned
 
 struct DnSmem {
     uint8_t st[2][DN_SLOT];         // one tile per slot: its 128 whole rows, then its 32 pair rows
-    uint8_t b[2][TC_N * 64];
-    float dx[2][TC_N];
-    float dw[2][TC_M];
+    uint8_t b[WS_NBUF][TC_N * 64];
+    PairConst pc[WS_NBUF];
+    float dw[WS_NBUF][TC_M];
     TileInfo ti[3];
     int pre[SG_MAXJOBS + 1];
-    uint64_t full[2], empty[2], aready[2], accfull[2], accempty[2];
-    uint32_t tmem;
+    WsSync y;
 };
 
-// Tensor-memory columns (128 allocated): accumulators [b] at 32b, operand A [b] at 64 + 16b, the
-// constant -8 operand at 96.
-constexpr uint32_t DN_ACC = 0, DN_A = 64, DN_CORR = 96;
+// Tensor-memory columns (256 allocated): accumulators [b] at 32b, operand A [b] at 128 + 16b.
+constexpr uint32_t DN_ACC = 0, DN_A = 128, DN_TMEM_COLS = 256;
 
-template <int JM, int CSH>
-__device__ __forceinline__ void dn_unpack_ws(DnSmem &s, int slot, int b, int j, int rb, int pitch, bool rowok, int nn,
-                                             uint32_t tm_a, int u) {
+template <int JM>
+__device__ __forceinline__ void dn_unpack_row(DnSmem &s, int slot, int b, int j, int rb, bool rowok, uint32_t tm_a,
+                                              int r) {
     uint32_t w[16];
     uint32_t scb = 0;
     if (rowok) {
-        scb = row_q4_block<JM>(s.st[slot] + u * rb, j, w);
+        scb = row_q4_block<JM>(s.st[slot] + r * rb, j, w);
     } else {
 #pragma unroll
         for (int k = 0; k < 16; k++) w[k] = 0;
     }
     tmem_st16(tm_a, w);
-    s.dw[b][u] = f16_to_f32(scb);
-    unpack_act_ws<JM & 1, CSH>(s.st[slot] + TC_M * rb, pitch, j, nn, s.b[b], s.dx[b], u);
+    s.dw[b][r] = f16_to_f32(scb);
+}
+
+// Tensor-map loads of down tile i (its 128 whole rows and 32 pair rows) into slot i & 1, by lane 0
+// of the copy warp; the tile description goes into the info ring.
+__device__ __forceinline__ void dn_issue_tile(DnSmem &s, const MoeShape &sh, const MoeLayerDev &L,
+                                              const MoeScratch &sc, const TcMaps &mp, int nu, int njobs, int ntiles,
+                                              int i, int rb, int pitch, int rg) {
+    const int t = blockIdx.x + i * gridDim.x;
+    if (t >= ntiles) return;
+    if ((threadIdx.x & 31) == 0) {
+        TileInfo &ti = s.ti[i % 3];
+        decode_tile(sh, L, sc, mp, nu, njobs, s.pre, t, true, ti);
+        uint64_t *bar = &s.y.full[i & 1];
+        uint8_t *dst = s.st[i & 1];
+        const bool wok = ti.w0 != nullptr;
+        mbar_expect_tx(bar, (uint32_t)(wok ? TC_M * rb + TC_N * pitch : 0));
+        if (wok) {
+            const int yr = ti.rt * TC_M / rg;
+            if (ti.shared) tma_load_2d(dst, mp.sh_down, 0, yr, bar);
+            else tma_load_3d(dst, mp.down, 0, yr, ti.slot, bar);
+            tma_load_2d(dst + TC_M * rb, mp.mid, 0, ti.p0 + ti.n0, bar);
+        }
+    }
+    __syncwarp();
 }
 
 __global__ void __launch_bounds__(WS_THREADS, 1) k_moe_down_ws(MoeShape sh, MoeLayerDev L, MoeScratch sc,
@@ -982,6 +1019,7 @@ __global__ void __launch_bounds__(WS_THREADS, 1) k_moe_down_ws(MoeShape sh, MoeL
                                                                 const __grid_constant__ TcMaps mp) {
     extern __shared__ __align__(1024) uint8_t smem_raw[];
     DnSmem &s = *reinterpret_cast<DnSmem *>(smem_raw);
+    WsSync &y = s.y;
     const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
     const int nu = routed_jobs(sh, sc), njobs = nu + (L.Fs > 0 ? 1 : 0);
     const int ntiles = tile_prefix(sh, L, sc, nu, njobs, true, s.pre);
@@ -990,34 +1028,25 @@ __global__ void __launch_bounds__(WS_THREADS, 1) k_moe_down_ws(MoeShape sh, MoeL
     const int rb = nbF * Q4_BLOCK, pitch = nbF * ACT_BLOCK;
     const bool csh1 = ((pitch / 16) & 7) == 4;   // bank-group step of the pair rows
 
-    if (tid == 0) {
-        for (int b = 0; b < 2; b++) {
-            mbar_init(&s.full[b], 1);
-            mbar_init(&s.empty[b], 128);
-            mbar_init(&s.aready[b], 128);
-            mbar_init(&s.accfull[b], 1);
-            mbar_init(&s.accempty[b], WS_DRAIN);
-        }
-        fence_mbar_init();
-    }
+    if (tid == 0) ws_init(y);
     if (warp == 0) {
-        asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], 128;" ::"r"(smem_u32(&s.tmem)));
+        asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(smem_u32(&y.tmem)),
+                     "r"(DN_TMEM_COLS));
         asm volatile("tcgen05.relinquish_alloc_permit.cta_group::1.sync.aligned;");
     }
     tc_fence_before();
     __syncthreads();
     tc_fence_after();
-    const uint32_t tmem = s.tmem;
+    const uint32_t tmem = y.tmem;
 
     if (warp < 8) {
         // ------------------------------------------------------------------ drain warps
         const int h = warp >> 2, q4 = warp & 3, r = q4 * 32 + lane;
         const uint32_t lanes = (uint32_t)(q4 * 32) << 16;
-        for (int b = 0; b < 2; b++) tmem_fill16(tmem + lanes + DN_ACC + 32 * b + 16 * h, kMagic);
+        for (int b = 0; b < WS_NBUF; b++) tmem_fill16(tmem + lanes + DN_ACC + 32 * b + 16 * h, kMagic);
         tmem_wait_st();
         tc_fence_before();
-        mbar_arrive(&s.accempty[0]);
-        mbar_arrive(&s.accempty[1]);
+        for (int b = 0; b < WS_NBUF; b++) mbar_arrive(&y.accempty[b]);
         uint32_t G = 0;
         for (int i = 0; i < mytiles; i++) {
             TileInfo ti;
@@ -1030,18 +1059,19 @@ __global__ void __launch_bounds__(WS_THREADS, 1) k_moe_down_ws(MoeShape sh, MoeL
 #pragma unroll
             for (int k = 0; k < 16; k++) acc[k] = 0.0f;
             for (int g = 0; g < nbF; g++, G++) {
-                const int b = G & 1;
-                mbar_wait(&s.accfull[b], (G >> 1) & 1, sc.err);
-                mbar_wait(&s.aready[b], (G >> 1) & 1, sc.err);   // acquires the unpackers' scales
+                const int b = G % WS_NBUF;
+                const uint32_t par = (G / WS_NBUF) & 1;
+                mbar_wait(&y.accfull[b], par, sc.err);
+                mbar_wait(&y.aready[b], par, sc.err);   // acquires the unpackers' scales
                 tc_fence_after();
                 uint32_t v[16];
                 const uint32_t ta = tmem + lanes + DN_ACC + 32 * b + 16 * h;
                 tmem_ld16(ta, v);
                 tmem_fill16(ta, kMagic);
-                chain_f2<16>(v, s.dw[b][r], s.dx[b] + 16 * h, acc);
+                chain_f2<16>(v, s.dw[b][r], s.pc[b].v + 8 * h, acc);
                 tmem_wait_st();
                 tc_fence_before();
-                mbar_arrive(&s.accempty[b]);
+                mbar_arrive(&y.accempty[b]);
             }
             const int row = rt * TC_M + r;
             if (ok && row < sh.D) {   // canonical outputs: Y [pair][D] (routed) or S [token][D] (shared)
@@ -1055,99 +1085,73 @@ __global__ void __launch_bounds__(WS_THREADS, 1) k_moe_down_ws(MoeShape sh, MoeL
                 }
             }
         }
-    } else if (warp < 12) {
+    } else if (warp < WS_COPY_WARP) {
         // ------------------------------------------------------------------ unpack warps
-        const int u = tid - WS_UNPACK0, q4 = warp - 8;
+        const int u = tid - WS_UNPACK0, q4 = warp & 3;   // row u into operand A, chunk u of operand B
         const uint32_t lanes = (uint32_t)(q4 * 32) << 16;
-        {
-            uint32_t c[16];
-#pragma unroll
-            for (int k = 0; k < 16; k++) c[k] = 0xf8f8f8f8u;
-            tmem_st16(tmem + lanes + DN_CORR, c);
-        }
         uint32_t G = 0;
         for (int i = 0; i < mytiles; i++) {
             const int slot = i & 1;
-            mbar_wait(&s.full[slot], (i >> 1) & 1, sc.err);
+            mbar_wait(&y.full[slot], (i >> 1) & 1, sc.err);
             const TileInfo &ti = s.ti[i % 3];
             const bool rowok = ti.w0 != nullptr && ti.rt * TC_M + u < sh.D;
             const int nn = ti.nn;
+            const uint8_t *act = s.st[slot] + TC_M * rb;
             for (int g0 = 0; g0 < nbF; g0 += 4) {
 #pragma unroll
                 for (int jm = 0; jm < 4; jm++, G++) {
-                    const int b = G & 1, j = g0 + jm;
-                    mbar_wait(&s.accempty[b], (G >> 1) & 1, sc.err);
+                    const int b = G % WS_NBUF, j = g0 + jm;
+                    mbar_wait(&y.accempty[b], (G / WS_NBUF) & 1, sc.err);
                     tc_fence_after();
                     const uint32_t ta = tmem + lanes + DN_A + 16 * b;
-                    if (csh1) {
-                        switch (jm) {
-                        case 0: dn_unpack_ws<0, 1>(s, slot, b, j, rb, pitch, rowok, nn, ta, u); break;
-                        case 1: dn_unpack_ws<1, 1>(s, slot, b, j, rb, pitch, rowok, nn, ta, u); break;
-                        case 2: dn_unpack_ws<2, 1>(s, slot, b, j, rb, pitch, rowok, nn, ta, u); break;
-                        default: dn_unpack_ws<3, 1>(s, slot, b, j, rb, pitch, rowok, nn, ta, u); break;
-                        }
-                    } else {
-                        switch (jm) {
-                        case 0: dn_unpack_ws<0, 2>(s, slot, b, j, rb, pitch, rowok, nn, ta, u); break;
-                        case 1: dn_unpack_ws<1, 2>(s, slot, b, j, rb, pitch, rowok, nn, ta, u); break;
-                        case 2: dn_unpack_ws<2, 2>(s, slot, b, j, rb, pitch, rowok, nn, ta, u); break;
-                        default: dn_unpack_ws<3, 2>(s, slot, b, j, rb, pitch, rowok, nn, ta, u); break;
-                        }
+                    switch (jm) {
+                    case 0: dn_unpack_row<0>(s, slot, b, j, rb, rowok, ta, u); break;
+                    case 1: dn_unpack_row<1>(s, slot, b, j, rb, rowok, ta, u); break;
+                    case 2: dn_unpack_row<2>(s, slot, b, j, rb, rowok, ta, u); break;
+                    default: dn_unpack_row<3>(s, slot, b, j, rb, rowok, ta, u); break;
                     }
-                    if (j == nbF - 1) mbar_arrive(&s.empty[slot]);
+                    if (csh1) {
+                        if (jm & 1) unpack_act_ws<1, 1>(act, pitch, j, nn, s.b[b], s.pc[b], u);
+                        else unpack_act_ws<0, 1>(act, pitch, j, nn, s.b[b], s.pc[b], u);
+                    } else {
+                        if (jm & 1) unpack_act_ws<1, 2>(act, pitch, j, nn, s.b[b], s.pc[b], u);
+                        else unpack_act_ws<0, 2>(act, pitch, j, nn, s.b[b], s.pc[b], u);
+                    }
+                    if (j == nbF - 1) mbar_arrive(&y.empty[slot]);
                     tmem_wait_st();
                     fence_proxy_async();
                     tc_fence_before();
-                    mbar_arrive(&s.aready[b]);
+                    mbar_arrive(&y.aready[b]);
                 }
             }
         }
     } else if (warp == WS_COPY_WARP) {
         // ------------------------------------------------------------------ copy warp
         for (int i = 0; i < mytiles; i++) {
-            const int slot = i & 1;
-            TileInfo &ti = s.ti[i % 3];
-            if (i >= 2) mbar_wait(&s.empty[slot], ((i >> 1) - 1) & 1, sc.err);
-            if (lane == 0) {
-                decode_tile(sh, L, sc, mp, nu, njobs, s.pre, blockIdx.x + i * gridDim.x, true, ti);
-                uint64_t *bar = &s.full[slot];
-                const bool wok = ti.w0 != nullptr;
-                mbar_expect_tx(bar, (uint32_t)(wok ? TC_M * rb + TC_N * pitch : 0));
-                if (wok) {
-                    const int y = ti.rt * TC_M / rg;
-                    if (ti.shared) tma_load_2d(s.st[slot], mp.sh_down, 0, y, bar);
-                    else tma_load_3d(s.st[slot], mp.down, 0, y, ti.slot, bar);
-                    tma_load_2d(s.st[slot] + TC_M * rb, mp.mid, 0, ti.p0 + ti.n0, bar);
-                }
-            }
-            __syncwarp();
+            if (i >= 2) mbar_wait(&y.empty[i & 1], ((i >> 1) - 1) & 1, sc.err);
+            dn_issue_tile(s, sh, L, sc, mp, nu, njobs, ntiles, i, rb, pitch, rg);
         }
     } else {
         // ------------------------------------------------------------------ MMA warp
-        const uint32_t idesc_u = umma_idesc_i8(false), idesc_s = umma_idesc_i8(true);
-        uint32_t G = 0;
-        for (int i = 0; i < mytiles; i++) {
-            for (int g = 0; g < nbF; g++, G++) {
-                const int b = G & 1;
-                mbar_wait(&s.aready[b], (G >> 1) & 1, sc.err);
-                mbar_wait(&s.accempty[b], (G >> 1) & 1, sc.err);
-                tc_fence_after();
-                if (lane == 0) {
-                    const uint32_t sb = smem_u32(s.b[b]), d = tmem + DN_ACC + 32 * b, a = tmem + DN_A + 16 * b;
+        const uint32_t idesc = umma_idesc_i8(false);
+        for (uint32_t G = 0; G < (uint32_t)(mytiles * nbF); G++) {
+            const int b = G % WS_NBUF;
+            const uint32_t par = (G / WS_NBUF) & 1;
+            mbar_wait(&y.aready[b], par, sc.err);
+            mbar_wait(&y.accempty[b], par, sc.err);
+            tc_fence_after();
+            if (lane == 0) {
+                const uint32_t sb = smem_u32(s.b[b]), d = tmem + DN_ACC + 32 * b, a = tmem + DN_A + 16 * b;
 #pragma unroll
-                    for (int k = 0; k < 2; k++) {
-                        umma_i8_ts(d, a + 8 * k, umma_desc(sb + 256 * k), idesc_u, true);
-                        umma_i8_ts(d, tmem + DN_CORR + 8 * k, umma_desc(sb + 256 * k), idesc_s, true);
-                    }
-                    umma_commit(&s.accfull[b]);
-                }
-                __syncwarp();
+                for (int k = 0; k < 2; k++) umma_i8_ts(d, a + 8 * k, umma_desc(sb + 256 * k), idesc);
+                umma_commit(&y.accfull[b]);
             }
+            __syncwarp();
         }
     }
     tc_fence_before();
     __syncthreads();
-    if (warp == 0) asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, 128;" ::"r"(tmem));
+    if (warp == 0) asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(tmem), "r"(DN_TMEM_COLS));
 }
 
 __global__ void __launch_bounds__(TC_THREADS, 3) k_moe_gateup_tc(MoeShape sh, MoeLayerDev L, MoeScratch sc,
