@@ -533,12 +533,14 @@ __device__ __forceinline__ void tma_gather4(void *dst, const void *map, int x, i
 }
 
 // ---------------------------------------------------------------------------------------------
-// Warp roles of the staged kernels (448 threads, one CTA per SM):
-//   warps 0-7    drain: read a block's int32 tile from tensor memory and extend the float chains
-//   warps 8-11   unpack: stage rows -> operand A in tensor memory (tcgen05.st), activations ->
+// Warp roles of the staged kernels (832 threads, one CTA per SM; many light warps per role, so that
+// each scheduler always has a warp of every role ready while others wait on tensor memory or
+// shared memory):
+//   warps 0-15   drain: read a block's int32 tile from tensor memory and extend the float chains
+//   warps 16-23  unpack: stage rows -> operand A in tensor memory (tcgen05.st), activations ->
 //                operand B in shared memory, scales -> shared memory
-//   warp 12      copies: decodes tiles and issues the tensor-map loads of the stage ring
-//   warp 13      MMA: one thread issues each block's tcgen05.mma and commits
+//   warp 24      copies: decodes tiles and issues the tensor-map loads of the stage ring
+//   warp 25      MMA: one thread issues each block's tcgen05.mma and commits
 // Operands and accumulators rotate through WS_NBUF buffers by block; mbarriers hand each buffer from
 // role to role, so unpacking, multiplication and draining of different blocks overlap.
 //
@@ -551,16 +553,50 @@ __device__ __forceinline__ void tma_gather4(void *dst, const void *map, int x, i
 // round-to-nearest products per instruction); its adds stay scalar, in block order.
 // ---------------------------------------------------------------------------------------------
 
-constexpr int WS_THREADS = 448;
-constexpr int WS_DRAIN = 256;                    // warps 0-7
-constexpr int WS_UNPACK0 = 256, WS_UNPACK = 128; // warps 8-11
-constexpr int WS_COPY_WARP = 12, WS_MMA_WARP = 13;
+constexpr int WS_THREADS = 832;
+constexpr int WS_DRAIN = 512;                    // warps 0-15
+constexpr int WS_UNPACK0 = 512, WS_UNPACK = 256; // warps 16-23
+constexpr int WS_COPY_WARP = 24, WS_MMA_WARP = 25;
 constexpr int WS_NBUF = 4;                       // blocks in flight between the roles
 constexpr uint32_t kMagic = 0x4B400000u;         // 1.5 * 2^23
 constexpr float kMagicF = 12582912.0f;
 
 __device__ __forceinline__ void mbar_arrive(uint64_t *bar) {
     asm volatile("mbarrier.arrive.shared::cta.b64 _, [%0];" ::"r"(smem_u32(bar)) : "memory");
+}
+
+// One arrival for the whole warp, after every lane's preceding work (its fences included).
+__device__ __forceinline__ void warp_arrive(uint64_t *bar) {
+    __syncwarp();
+    if ((threadIdx.x & 31) == 0) mbar_arrive(bar);
+}
+
+// Loads without the wait: the registers are valid after tmem_wait_ld().
+__device__ __forceinline__ void tmem_ld16_async(uint32_t taddr, uint32_t v[16]) {
+    asm volatile(
+        "tcgen05.ld.sync.aligned.32x32b.x16.b32 {%0,%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,%14,%15}, [%16];"
+        : "=r"(v[0]), "=r"(v[1]), "=r"(v[2]), "=r"(v[3]), "=r"(v[4]), "=r"(v[5]), "=r"(v[6]), "=r"(v[7]), "=r"(v[8]),
+          "=r"(v[9]), "=r"(v[10]), "=r"(v[11]), "=r"(v[12]), "=r"(v[13]), "=r"(v[14]), "=r"(v[15])
+        : "r"(taddr)
+        : "memory");
+}
+__device__ __forceinline__ void tmem_ld8_async(uint32_t taddr, uint32_t v[8]) {
+    asm volatile("tcgen05.ld.sync.aligned.32x32b.x8.b32 {%0,%1,%2,%3,%4,%5,%6,%7}, [%8];"
+                 : "=r"(v[0]), "=r"(v[1]), "=r"(v[2]), "=r"(v[3]), "=r"(v[4]), "=r"(v[5]), "=r"(v[6]), "=r"(v[7])
+                 : "r"(taddr)
+                 : "memory");
+}
+__device__ __forceinline__ void tmem_wait_ld() { asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory"); }
+
+__device__ __forceinline__ void tmem_ld8(uint32_t taddr, uint32_t v[8]) {
+    asm volatile("tcgen05.ld.sync.aligned.32x32b.x8.b32 {%0,%1,%2,%3,%4,%5,%6,%7}, [%8];"
+                 : "=r"(v[0]), "=r"(v[1]), "=r"(v[2]), "=r"(v[3]), "=r"(v[4]), "=r"(v[5]), "=r"(v[6]), "=r"(v[7])
+                 : "r"(taddr));
+    asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory");
+}
+
+__device__ __forceinline__ void tmem_fill8(uint32_t taddr, uint32_t x) {
+    asm volatile("tcgen05.st.sync.aligned.32x32b.x8.b32 [%0], {%1,%1,%1,%1,%1,%1,%1,%1};" ::"r"(taddr), "r"(x) : "memory");
 }
 
 __device__ __forceinline__ void tmem_wait_st() { asm volatile("tcgen05.wait::st.sync.aligned;" ::: "memory"); }
@@ -659,13 +695,32 @@ __device__ __forceinline__ void unpack_act_ws(const uint8_t *act, int pitch, int
     }
 }
 
+// The same operand as unpack_act_ws with two threads per chunk: thread (u, hm) moves bytes
+// 8 hm .. 8 hm + 7 of chunk u's 16 (both reads and writes 8 bytes); hm == 0 also stores dx and cm.
+template <int CSH>
+__device__ __forceinline__ void unpack_act_half(const uint8_t *act, int pitch, int j, int nn, uint8_t *bop,
+                                                PairConst &pc, int u, int hm) {
+    const int k = u >> 3, i = u & 7;
+    const int n = 8 * (k & 3) + i, c = ((i >> CSH) + (k >> 2)) & 3;
+    const bool live = n < nn;
+    const uint8_t *blk = act + n * pitch + j * ACT_BLOCK;
+    const uint2 v = live ? *reinterpret_cast<const uint2 *>(blk + 8 + 16 * c + 8 * hm) : make_uint2(0, 0);
+    *reinterpret_cast<uint2 *>(bop + op_off(n, c) + 8 * hm) = v;
+    if (c == 0 && hm == 0) {
+        const uint2 hd = live ? *reinterpret_cast<const uint2 *>(blk) : make_uint2(0, 0);
+        float *e = reinterpret_cast<float *>(&pc.v[n >> 1]) + (n & 1);
+        e[0] = __int2float_rn(12582912 + 8 * (int)hd.y);   // cm: exact (below 2^24)
+        e[2] = __uint_as_float(hd.x);                        // dx
+    }
+}
+
 // NUMERICS §2 quantization of the mid values of a tile held in X[pair][128 rows] (shared): unit
 // (pair n, 64-row block b) is quantized by 8 consecutive lanes, 8 rows each (amax and the q sum by
-// 3-step shuffles; the same d, q and sum as act_quant_warp). Called by the 256 drain threads.
+// 3-step shuffles; the same d, q and sum as act_quant_warp). Called by the 512 drain threads.
 __device__ __forceinline__ void quant_tile(const float *X, const TileInfo &ti, act_q8 *mid, int fmax_nb, int tid) {
-#pragma unroll
-    for (int k = 0; k < 2; k++) {
-        const int item = tid + k * WS_DRAIN;            // 512 items: (pair, 8-row group)
+    static_assert(WS_DRAIN == TC_N * TC_M / 8, "one (pair, 8-row group) item per drain thread");
+    {
+        const int item = tid;                           // 512 items: (pair, 8-row group)
         const int n = item >> 4, grp = item & 15, b = grp >> 3, l8 = grp & 7;
         const bool live = n < ti.nn && ti.rt * TC_M + b * 64 < ti.F;   // uniform over the 8 lanes
         const float4 x0 = *reinterpret_cast<const float4 *>(X + n * TC_M + grp * 8);
@@ -703,7 +758,7 @@ __device__ __forceinline__ void quant_tile(const float *X, const TileInfo &ti, a
     }
 }
 
-__device__ __forceinline__ void drain_bar() { asm volatile("bar.sync 1, 256;" ::: "memory"); }
+__device__ __forceinline__ void drain_bar() { asm volatile("bar.sync 1, 512;" ::: "memory"); }
 
 // Barriers and scratch shared by both staged kernels.
 struct WsSync {
@@ -715,12 +770,12 @@ struct WsSync {
 __device__ __forceinline__ void ws_init(WsSync &y) {
     for (int b = 0; b < 2; b++) {
         mbar_init(&y.full[b], 1);
-        mbar_init(&y.empty[b], WS_UNPACK);
+        mbar_init(&y.empty[b], WS_UNPACK / 32);   // one arrival per warp
     }
     for (int b = 0; b < WS_NBUF; b++) {
-        mbar_init(&y.aready[b], WS_UNPACK);
+        mbar_init(&y.aready[b], WS_UNPACK / 32);
         mbar_init(&y.accfull[b], 1);
-        mbar_init(&y.accempty[b], WS_DRAIN);
+        mbar_init(&y.accempty[b], WS_DRAIN / 32);
     }
     fence_mbar_init();
 }
@@ -813,17 +868,15 @@ __global__ void __launch_bounds__(WS_THREADS, 1) k_moe_gateup_ws(MoeShape sh, Mo
     tc_fence_after();
     const uint32_t tmem = y.tmem;
 
-    if (warp < 8) {
+    if (warp < 16) {
         // ------------------------------------------------------------------ drain warps
-        const int m = warp >> 2, q4 = warp & 3, r = q4 * 32 + lane;
-        const uint32_t lanes = (uint32_t)(q4 * 32) << 16;
-        for (int b = 0; b < WS_NBUF; b++) {
-            tmem_fill16(tmem + lanes + GU_ACC + 64 * b + 32 * m, kMagic);
-            tmem_fill16(tmem + lanes + GU_ACC + 64 * b + 32 * m + 16, kMagic);
-        }
+        // warp w: rows 32 (w & 3) .. of matrix (w >> 2) & 1 (gate, up), pairs 16 (w >> 3) .. + 15
+        const int m = (warp >> 2) & 1, h = warp >> 3, q4 = warp & 3, r = q4 * 32 + lane;
+        const uint32_t lanes = (uint32_t)(q4 * 32) << 16, col = GU_ACC + 32 * m + 16 * h;
+        for (int b = 0; b < WS_NBUF; b++) tmem_fill16(tmem + lanes + col + 64 * b, kMagic);
         tmem_wait_st();
         tc_fence_before();
-        for (int b = 0; b < WS_NBUF; b++) mbar_arrive(&y.accempty[b]);
+        for (int b = 0; b < WS_NBUF; b++) warp_arrive(&y.accempty[b]);
         uint32_t G = 0;
         for (int i = 0; i < mytiles; i++) {
             TileInfo ti;
@@ -833,40 +886,39 @@ __global__ void __launch_bounds__(WS_THREADS, 1) k_moe_gateup_ws(MoeShape sh, Mo
             ti.nn = __shfl_sync(0xffffffffu, ti.nn, 0);
             ti.p0 = __shfl_sync(0xffffffffu, ti.p0, 0);
             ti.F = __shfl_sync(0xffffffffu, ti.F, 0);
-            float acc[TC_N];
+            float acc[16];
 #pragma unroll
-            for (int k = 0; k < TC_N; k++) acc[k] = 0.0f;
+            for (int k = 0; k < 16; k++) acc[k] = 0.0f;
             for (int g = 0; g < nbD; g++, G++) {
                 const int b = G % WS_NBUF;
                 const uint32_t par = (G / WS_NBUF) & 1;
                 mbar_wait(&y.accfull[b], par, sc.err);
                 mbar_wait(&y.aready[b], par, sc.err);   // acquires the unpackers' scales
                 tc_fence_after();
-                uint32_t v[32];
-                const uint32_t ta = tmem + lanes + GU_ACC + 64 * b + 32 * m;
-                tmem_ld32(ta, v);
+                uint32_t v[16];
+                const uint32_t ta = tmem + lanes + col + 64 * b;
+                tmem_ld16(ta, v);
                 tmem_fill16(ta, kMagic);
-                tmem_fill16(ta + 16, kMagic);
-                chain_f2<TC_N>(v, s.dw[b][m * TC_M + r], s.pc[b].v, acc);
+                chain_f2<16>(v, s.dw[b][m * TC_M + r], s.pc[b].v + 8 * h, acc);
                 tmem_wait_st();
                 tc_fence_before();
-                mbar_arrive(&y.accempty[b]);
+                warp_arrive(&y.accempty[b]);
             }
-            // epilogue: SwiGLU (gate warps take pairs 0-15, up warps 16-31; each hands the other half
-            // of its values over through X), then the mid activation blocks
+            // epilogue: SwiGLU (of its 16 pairs, a gate warp keeps the first 8 and an up warp the last
+            // 8; each hands the other half of its values over through X), then the mid blocks
             float *X = s.X;
 #pragma unroll
-            for (int n = 0; n < TC_N; n++) {
-                const bool give = m == 0 ? n >= TC_N / 2 : n < TC_N / 2;
-                if (give) X[n * TC_M + r] = canon(acc[n]);
+            for (int k = 0; k < 16; k++) {
+                const bool give = m == 0 ? k >= 8 : k < 8;
+                if (give) X[(16 * h + k) * TC_M + r] = canon(acc[k]);
             }
             drain_bar();
 #pragma unroll
-            for (int n = 0; n < TC_N; n++) {
-                const bool keep = m == 0 ? n < TC_N / 2 : n >= TC_N / 2;
+            for (int k = 0; k < 16; k++) {
+                const bool keep = m == 0 ? k < 8 : k >= 8;
                 if (keep) {
-                    const float a = canon(acc[n]);
-                    float *x = X + n * TC_M + r;
+                    const float a = canon(acc[k]);
+                    float *x = X + (16 * h + k) * TC_M + r;
                     *x = m == 0 ? swiglu_c(a, *x) : swiglu_c(*x, a);
                 }
             }
@@ -876,7 +928,8 @@ __global__ void __launch_bounds__(WS_THREADS, 1) k_moe_gateup_ws(MoeShape sh, Mo
         }
     } else if (warp < WS_COPY_WARP) {
         // ------------------------------------------------------------------ unpack warps
-        const int u = tid - WS_UNPACK0, q4 = warp & 3;   // row u of gate and of up
+        // warps 16-19: gate rows, warps 20-23: up rows; both halves of each activation chunk
+        const int u = tid - WS_UNPACK0, m = u >> 7, r = u & (TC_M - 1), q4 = warp & 3;
         const uint32_t lanes = (uint32_t)(q4 * 32) << 16;
         uint32_t G = 0;
         for (int i = 0; i < mytiles; i++) {
@@ -884,43 +937,39 @@ __global__ void __launch_bounds__(WS_THREADS, 1) k_moe_gateup_ws(MoeShape sh, Mo
                 const int qs = i * nS + s0, slot = qs & 1;
                 mbar_wait(&y.full[slot], (qs >> 1) & 1, sc.err);
                 const TileInfo &ti = s.ti[i % 3];
-                const bool rowok = ti.rt * TC_M + u < ti.F;
+                const bool rowok = ti.rt * TC_M + r < ti.F;
                 const int nn = ti.nn;
+                const uint8_t *row = s.st[slot].w[m * TC_M + r];
 #pragma unroll
                 for (int jj = 0; jj < SG_BLK; jj++, G++) {
                     const int b = G % WS_NBUF;
                     mbar_wait(&y.accempty[b], (G / WS_NBUF) & 1, sc.err);
                     tc_fence_after();
-#pragma unroll
-                    for (int m = 0; m < 2; m++) {
-                        const uint8_t *row = s.st[slot].w[m * TC_M + u];
-                        uint32_t w[16];
-                        uint32_t scb = 0;
-                        if (rowok) {
-                            switch (jj) {
-                            case 0: scb = seg_q4_block<0>(row, w); break;
-                            case 1: scb = seg_q4_block<1>(row, w); break;
-                            case 2: scb = seg_q4_block<2>(row, w); break;
-                            case 3: scb = seg_q4_block<3>(row, w); break;
-                            case 4: scb = seg_q4_block<4>(row, w); break;
-                            case 5: scb = seg_q4_block<5>(row, w); break;
-                            case 6: scb = seg_q4_block<6>(row, w); break;
-                            default: scb = seg_q4_block<7>(row, w); break;
-                            }
-                        } else {
-#pragma unroll
-                            for (int k = 0; k < 16; k++) w[k] = 0;
+                    uint32_t w[16];
+                    uint32_t scb = 0;
+                    if (rowok) {
+                        switch (jj) {
+                        case 0: scb = seg_q4_block<0>(row, w); break;
+                        case 1: scb = seg_q4_block<1>(row, w); break;
+                        case 2: scb = seg_q4_block<2>(row, w); break;
+                        case 3: scb = seg_q4_block<3>(row, w); break;
+                        case 4: scb = seg_q4_block<4>(row, w); break;
+                        case 5: scb = seg_q4_block<5>(row, w); break;
+                        case 6: scb = seg_q4_block<6>(row, w); break;
+                        default: scb = seg_q4_block<7>(row, w); break;
                         }
-                        tmem_st16(tmem + lanes + GU_A + 32 * b + 16 * m, w);
-                        s.dw[b][m * TC_M + u] = f16_to_f32(scb);
+                    } else {
+#pragma unroll
+                        for (int k = 0; k < 16; k++) w[k] = 0;
                     }
-                    if (jj & 1) unpack_act_ws<1, 1>(&s.st[slot].act[0][0], SG_ASEG, jj, nn, s.b[b], s.pc[b], u);
-                    else unpack_act_ws<0, 1>(&s.st[slot].act[0][0], SG_ASEG, jj, nn, s.b[b], s.pc[b], u);
-                    if (jj == SG_BLK - 1) mbar_arrive(&y.empty[slot]);   // this thread is done with the slot
+                    tmem_st16(tmem + lanes + GU_A + 32 * b + 16 * m, w);
+                    s.dw[b][m * TC_M + r] = f16_to_f32(scb);
+                    unpack_act_half<1>(&s.st[slot].act[0][0], SG_ASEG, jj, nn, s.b[b], s.pc[b], r, m);
+                    if (jj == SG_BLK - 1) warp_arrive(&y.empty[slot]);   // this warp is done with the slot
                     tmem_wait_st();
                     fence_proxy_async();
                     tc_fence_before();
-                    mbar_arrive(&y.aready[b]);
+                    warp_arrive(&y.aready[b]);
                 }
             }
         }
@@ -1039,14 +1088,15 @@ __global__ void __launch_bounds__(WS_THREADS, 1) k_moe_down_ws(MoeShape sh, MoeL
     tc_fence_after();
     const uint32_t tmem = y.tmem;
 
-    if (warp < 8) {
+    if (warp < 16) {
         // ------------------------------------------------------------------ drain warps
-        const int h = warp >> 2, q4 = warp & 3, r = q4 * 32 + lane;
-        const uint32_t lanes = (uint32_t)(q4 * 32) << 16;
-        for (int b = 0; b < WS_NBUF; b++) tmem_fill16(tmem + lanes + DN_ACC + 32 * b + 16 * h, kMagic);
+        // warp w: rows 32 (w & 3) .., pairs 8 (w >> 2) .. + 7
+        const int c4 = warp >> 2, q4 = warp & 3, r = q4 * 32 + lane;
+        const uint32_t lanes = (uint32_t)(q4 * 32) << 16, col = DN_ACC + 8 * c4;
+        for (int b = 0; b < WS_NBUF; b++) tmem_fill8(tmem + lanes + col + 32 * b, kMagic);
         tmem_wait_st();
         tc_fence_before();
-        for (int b = 0; b < WS_NBUF; b++) mbar_arrive(&y.accempty[b]);
+        for (int b = 0; b < WS_NBUF; b++) warp_arrive(&y.accempty[b]);
         uint32_t G = 0;
         for (int i = 0; i < mytiles; i++) {
             TileInfo ti;
@@ -1055,29 +1105,36 @@ __global__ void __launch_bounds__(WS_THREADS, 1) k_moe_down_ws(MoeShape sh, MoeL
             const int nn = __shfl_sync(0xffffffffu, ti.nn, 0), p0 = __shfl_sync(0xffffffffu, ti.p0, 0);
             const int shared = __shfl_sync(0xffffffffu, ti.shared, 0);
             const int ok = __shfl_sync(0xffffffffu, ti.w0 != nullptr ? 1 : 0, 0);
-            float acc[16];
+            float acc[8];
 #pragma unroll
-            for (int k = 0; k < 16; k++) acc[k] = 0.0f;
-            for (int g = 0; g < nbF; g++, G++) {
-                const int b = G % WS_NBUF;
-                const uint32_t par = (G / WS_NBUF) & 1;
-                mbar_wait(&y.accfull[b], par, sc.err);
-                mbar_wait(&y.aready[b], par, sc.err);   // acquires the unpackers' scales
+            for (int k = 0; k < 8; k++) acc[k] = 0.0f;
+            for (int g = 0; g < nbF; g += 2, G += 2) {   // two blocks per pass: one load latency
+                const int b0 = G % WS_NBUF, b1 = (G + 1) % WS_NBUF;
+                const uint32_t p0 = (G / WS_NBUF) & 1, p1 = ((G + 1) / WS_NBUF) & 1;
+                mbar_wait(&y.accfull[b0], p0, sc.err);
+                mbar_wait(&y.aready[b0], p0, sc.err);   // acquires the unpackers' scales
+                mbar_wait(&y.accfull[b1], p1, sc.err);
+                mbar_wait(&y.aready[b1], p1, sc.err);
                 tc_fence_after();
-                uint32_t v[16];
-                const uint32_t ta = tmem + lanes + DN_ACC + 32 * b + 16 * h;
-                tmem_ld16(ta, v);
-                tmem_fill16(ta, kMagic);
-                chain_f2<16>(v, s.dw[b][r], s.pc[b].v + 8 * h, acc);
+                uint32_t v0[8], v1[8];
+                const uint32_t t0 = tmem + lanes + col + 32 * b0, t1 = tmem + lanes + col + 32 * b1;
+                tmem_ld8_async(t0, v0);
+                tmem_ld8_async(t1, v1);
+                tmem_wait_ld();
+                tmem_fill8(t0, kMagic);
+                tmem_fill8(t1, kMagic);
+                chain_f2<8>(v0, s.dw[b0][r], s.pc[b0].v + 4 * c4, acc);
+                chain_f2<8>(v1, s.dw[b1][r], s.pc[b1].v + 4 * c4, acc);
                 tmem_wait_st();
                 tc_fence_before();
-                mbar_arrive(&y.accempty[b]);
+                warp_arrive(&y.accempty[b0]);
+                warp_arrive(&y.accempty[b1]);
             }
             const int row = rt * TC_M + r;
             if (ok && row < sh.D) {   // canonical outputs: Y [pair][D] (routed) or S [token][D] (shared)
 #pragma unroll
-                for (int k = 0; k < 16; k++) {
-                    const int n = 16 * h + k;
+                for (int k = 0; k < 8; k++) {
+                    const int n = 8 * c4 + k;
                     if (n < nn) {
                         float *out = shared ? sc.S + (int64_t)(n0 + n) * sh.D : sc.Y + (int64_t)(p0 + n0 + n) * sh.D;
                         out[row] = canon(acc[k]);
@@ -1087,14 +1144,16 @@ __global__ void __launch_bounds__(WS_THREADS, 1) k_moe_down_ws(MoeShape sh, MoeL
         }
     } else if (warp < WS_COPY_WARP) {
         // ------------------------------------------------------------------ unpack warps
-        const int u = tid - WS_UNPACK0, q4 = warp & 3;   // row u into operand A, chunk u of operand B
+        // warps 16-19: the 128 rows into operand A; warps 20-23: the 32 pair rows into operand B
+        const int u = tid - WS_UNPACK0, q4 = warp & 3, r = u & (TC_M - 1);
+        const bool rows_role = u < TC_M;
         const uint32_t lanes = (uint32_t)(q4 * 32) << 16;
         uint32_t G = 0;
         for (int i = 0; i < mytiles; i++) {
             const int slot = i & 1;
             mbar_wait(&y.full[slot], (i >> 1) & 1, sc.err);
             const TileInfo &ti = s.ti[i % 3];
-            const bool rowok = ti.w0 != nullptr && ti.rt * TC_M + u < sh.D;
+            const bool rowok = ti.w0 != nullptr && ti.rt * TC_M + r < sh.D;
             const int nn = ti.nn;
             const uint8_t *act = s.st[slot] + TC_M * rb;
             for (int g0 = 0; g0 < nbF; g0 += 4) {
@@ -1103,25 +1162,26 @@ __global__ void __launch_bounds__(WS_THREADS, 1) k_moe_down_ws(MoeShape sh, MoeL
                     const int b = G % WS_NBUF, j = g0 + jm;
                     mbar_wait(&y.accempty[b], (G / WS_NBUF) & 1, sc.err);
                     tc_fence_after();
-                    const uint32_t ta = tmem + lanes + DN_A + 16 * b;
-                    switch (jm) {
-                    case 0: dn_unpack_row<0>(s, slot, b, j, rb, rowok, ta, u); break;
-                    case 1: dn_unpack_row<1>(s, slot, b, j, rb, rowok, ta, u); break;
-                    case 2: dn_unpack_row<2>(s, slot, b, j, rb, rowok, ta, u); break;
-                    default: dn_unpack_row<3>(s, slot, b, j, rb, rowok, ta, u); break;
-                    }
-                    if (csh1) {
-                        if (jm & 1) unpack_act_ws<1, 1>(act, pitch, j, nn, s.b[b], s.pc[b], u);
-                        else unpack_act_ws<0, 1>(act, pitch, j, nn, s.b[b], s.pc[b], u);
+                    if (rows_role) {
+                        const uint32_t ta = tmem + lanes + DN_A + 16 * b;
+                        switch (jm) {
+                        case 0: dn_unpack_row<0>(s, slot, b, j, rb, rowok, ta, r); break;
+                        case 1: dn_unpack_row<1>(s, slot, b, j, rb, rowok, ta, r); break;
+                        case 2: dn_unpack_row<2>(s, slot, b, j, rb, rowok, ta, r); break;
+                        default: dn_unpack_row<3>(s, slot, b, j, rb, rowok, ta, r); break;
+                        }
+                    } else if (csh1) {
+                        if (jm & 1) unpack_act_ws<1, 1>(act, pitch, j, nn, s.b[b], s.pc[b], r);
+                        else unpack_act_ws<0, 1>(act, pitch, j, nn, s.b[b], s.pc[b], r);
                     } else {
-                        if (jm & 1) unpack_act_ws<1, 2>(act, pitch, j, nn, s.b[b], s.pc[b], u);
-                        else unpack_act_ws<0, 2>(act, pitch, j, nn, s.b[b], s.pc[b], u);
+                        if (jm & 1) unpack_act_ws<1, 2>(act, pitch, j, nn, s.b[b], s.pc[b], r);
+                        else unpack_act_ws<0, 2>(act, pitch, j, nn, s.b[b], s.pc[b], r);
                     }
-                    if (j == nbF - 1) mbar_arrive(&y.empty[slot]);
-                    tmem_wait_st();
+                    if (j == nbF - 1) warp_arrive(&y.empty[slot]);
+                    if (rows_role) tmem_wait_st();
                     fence_proxy_async();
                     tc_fence_before();
-                    mbar_arrive(&y.aready[b]);
+                    warp_arrive(&y.aready[b]);
                 }
             }
         }
