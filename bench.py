@@ -36,6 +36,15 @@ L_, D_, F_, E_, K_ = 48, 2048, 768, 128, 8
 SEED, SIGMA = 2, 0.02
 
 
+def batch_gateup_bytes(B):
+    """Algorithmic bytes of one launch of the staged tensor-core gate/up kernel at batch B: the gate and
+    up rows of every expert the batch routes to, read once (expected distinct experts of B tokens
+    drawing K of E), the B activation rows read once and the B * K mid rows written once."""
+    q4_row_d = 34 * D_ // 64
+    experts = E_ * (1.0 - (1.0 - K_ / E_) ** B)
+    return round(experts * 2 * F_ * q4_row_d + B * (D_ // 64) * 72 + B * K_ * (F_ // 64) * 72)
+
+
 def algorithmic_bytes():
     """Bytes the path must read per token and layer (B = 1), FORMAT §6 row sizes."""
     q4_row_d = 34 * D_ // 64            # gate/up row: 1088 B
@@ -380,6 +389,11 @@ def run_ours(args, rank, world, local_rank):
     if persistent:
         kernel = "k_moe_decode (persistent, one launch per token, all layers)"
         kbytes, kgbs = L_ * ab["layer"], step_gbs
+    elif B * K_ >= 256:
+        kernel = ("k_moe_gateup_ws (staged tcgen05 gate+up over expert buckets, SwiGLU, mid act-quant; "
+                  "time from hxb_moe_profile)")
+        kbytes = batch_gateup_bytes(B)
+        kgbs = kbytes / (us[2] * 1e-6) / 1e9
     else:
         kernel, kbytes = "k_moe_gateup (Q4 gate+up GEMV, SwiGLU, mid act-quant)", ab["gateup"]
         kgbs = ab["gateup"] / (us[2] * 1e-6) / 1e9
@@ -408,7 +422,9 @@ def run_ours(args, rank, world, local_rank):
             cpu = {"value": None, "unit": "tok/s", "cores": 0, "kind": "reference",
                    "sample": "oracle/_ref not built"}
 
-    launches_per_step = 1 if persistent else (L_ * 4 if B * K_ <= 64 else L_ * 6)
+    # per layer: norm+act, router (fused routing), gate/up, down for B * K <= 64; otherwise norm+act,
+    # router, select, union, gate/up, down, rank-order sum
+    launches_per_step = 1 if persistent else (L_ * 4 if B * K_ <= 64 else L_ * 7)
     line = {"metric": METRIC, "value": round(value, 3), "unit": "tok/s", "n_gpus": world, "steps": args.steps,
             "warmup": args.warmup, "ms_per_step": round(ms / args.steps, 5), "higher_is_better": True,
             "scaling": "weak", "vs_baseline": None, "dtype": "q4xq8-int32+f32", "data": "synthetic",

@@ -61,6 +61,7 @@ struct alignas(64) TcMaps {
     int64_t slot_bytes = 0;
     int n_slots = 0, down_rg = 0;
     int xact_rows = 0;                   // token rows the xact map covers
+    float zero = 0.0f;                   // a zero the device code cannot constant-fold
     bool gu_ok = false, dn_ok = false;   // the staged gate/up and down kernels can take this layer
 };
 

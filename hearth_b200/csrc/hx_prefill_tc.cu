@@ -639,6 +639,18 @@ __device__ __forceinline__ uint64_t f2_mul(uint64_t a, uint64_t b) {
     asm("mul.rn.f32x2 %0, %1, %2;" : "=l"(d) : "l"(a), "l"(b));
     return d;
 }
+__device__ __forceinline__ uint64_t f2_fma(uint64_t a, uint64_t b, uint64_t c) {
+    uint64_t d;
+    asm("fma.rn.f32x2 %0, %1, %2, %3;" : "=l"(d) : "l"(a), "l"(b), "l"(c));
+    return d;
+}
+__device__ __forceinline__ uint64_t f2_add(uint64_t a, uint64_t b) {
+    uint64_t d;
+    asm("add.rn.f32x2 %0, %1, %2;" : "=l"(d) : "l"(a), "l"(b));
+    return d;
+}
+__device__ __forceinline__ float lo_f(uint64_t x) { return __uint_as_float((uint32_t)x); }
+__device__ __forceinline__ float hi_f(uint64_t x) { return __uint_as_float((uint32_t)(x >> 32)); }
 
 // Per-block pair constants in shared memory, interleaved for the drain: entry i holds
 // {cm[2i], cm[2i+1], dx[2i], dx[2i+1]}.
@@ -646,20 +658,20 @@ struct PairConst {
     float4 v[TC_N / 2];
 };
 
-// NC columns of block words v (magic-offset u8 x s8 dots) into the chains acc[NC]:
-// acc = acc + isum * (dw * dx[n]). The chain adds stay scalar because the assembler contracts a packed
-// multiply feeding a packed add into a fused multiply-add even when both carry .rn (measured: most
-// chains then differ in the last bits).
+// NC columns of block words v (magic-offset u8 x s8 dots) into the packed chains acc2[NC / 2]:
+// acc = acc + isum * (dw * dx[n]), every operation a packed f32x2 pair rounded to nearest. The product
+// term comes from fma(isum, dw * dx, z) with z a zero the compiler cannot see (a kernel argument):
+// exactly the rounded product (the chains start at +0, so the sign of a zero product cannot
+// matter), and, unlike a multiply, it is never contracted into the following add (a packed multiply
+// feeding a packed add is contracted into a fused multiply-add even when both carry .rn).
 template <int NC>
-__device__ __forceinline__ void chain_f2(const uint32_t *v, float dw, const float4 *pc, float *acc) {
-    const uint64_t dw2 = pack2f(dw, dw);
+__device__ __forceinline__ void chain_f2(const uint32_t *v, float dw, const float4 *pc, uint64_t *acc2, float zero) {
+    const uint64_t dw2 = pack2f(dw, dw), z2 = pack2f(zero, zero);
 #pragma unroll
     for (int i = 0; i < NC / 2; i++) {
         const float4 q = pc[i];
         const uint64_t isum2 = f2_sub(pack2(v[2 * i], v[2 * i + 1]), pack2f(q.x, q.y));
-        const uint64_t t2 = f2_mul(isum2, f2_mul(dw2, pack2f(q.z, q.w)));
-        acc[2 * i] = __fadd_rn(acc[2 * i], __uint_as_float((uint32_t)t2));
-        acc[2 * i + 1] = __fadd_rn(acc[2 * i + 1], __uint_as_float((uint32_t)(t2 >> 32)));
+        acc2[i] = f2_add(acc2[i], f2_fma(isum2, f2_mul(dw2, pack2f(q.z, q.w)), z2));
     }
 }
 
@@ -886,9 +898,9 @@ __global__ void __launch_bounds__(WS_THREADS, 1) k_moe_gateup_ws(MoeShape sh, Mo
             ti.nn = __shfl_sync(0xffffffffu, ti.nn, 0);
             ti.p0 = __shfl_sync(0xffffffffu, ti.p0, 0);
             ti.F = __shfl_sync(0xffffffffu, ti.F, 0);
-            float acc[16];
+            uint64_t acc2[8];
 #pragma unroll
-            for (int k = 0; k < 16; k++) acc[k] = 0.0f;
+            for (int k = 0; k < 8; k++) acc2[k] = 0;
             for (int g = 0; g < nbD; g++, G++) {
                 const int b = G % WS_NBUF;
                 const uint32_t par = (G / WS_NBUF) & 1;
@@ -899,7 +911,7 @@ __global__ void __launch_bounds__(WS_THREADS, 1) k_moe_gateup_ws(MoeShape sh, Mo
                 const uint32_t ta = tmem + lanes + col + 64 * b;
                 tmem_ld16(ta, v);
                 tmem_fill16(ta, kMagic);
-                chain_f2<16>(v, s.dw[b][m * TC_M + r], s.pc[b].v + 8 * h, acc);
+                chain_f2<16>(v, s.dw[b][m * TC_M + r], s.pc[b].v + 8 * h, acc2, mp.zero);
                 tmem_wait_st();
                 tc_fence_before();
                 warp_arrive(&y.accempty[b]);
@@ -907,6 +919,12 @@ __global__ void __launch_bounds__(WS_THREADS, 1) k_moe_gateup_ws(MoeShape sh, Mo
             // epilogue: SwiGLU (of its 16 pairs, a gate warp keeps the first 8 and an up warp the last
             // 8; each hands the other half of its values over through X), then the mid blocks
             float *X = s.X;
+            float acc[16];
+#pragma unroll
+            for (int k = 0; k < 8; k++) {
+                acc[2 * k] = lo_f(acc2[k]);
+                acc[2 * k + 1] = hi_f(acc2[k]);
+            }
 #pragma unroll
             for (int k = 0; k < 16; k++) {
                 const bool give = m == 0 ? k >= 8 : k < 8;
@@ -963,7 +981,7 @@ __global__ void __launch_bounds__(WS_THREADS, 1) k_moe_gateup_ws(MoeShape sh, Mo
                         for (int k = 0; k < 16; k++) w[k] = 0;
                     }
                     tmem_st16(tmem + lanes + GU_A + 32 * b + 16 * m, w);
-                    s.dw[b][m * TC_M + r] = f16_to_f32(scb);
+                    s.dw[b][m * TC_M + r] = f16_to_f32_hw(scb);   // chains are canonicalised before use
                     unpack_act_half<1>(&s.st[slot].act[0][0], SG_ASEG, jj, nn, s.b[b], s.pc[b], r, m);
                     if (jj == SG_BLK - 1) warp_arrive(&y.empty[slot]);   // this warp is done with the slot
                     tmem_wait_st();
@@ -1036,7 +1054,7 @@ __device__ __forceinline__ void dn_unpack_row(DnSmem &s, int slot, int b, int j,
         for (int k = 0; k < 16; k++) w[k] = 0;
     }
     tmem_st16(tm_a, w);
-    s.dw[b][r] = f16_to_f32(scb);
+    s.dw[b][r] = f16_to_f32_hw(scb);   // chains are canonicalised before use
 }
 
 // Tensor-map loads of down tile i (its 128 whole rows and 32 pair rows) into slot i & 1, by lane 0
@@ -1105,9 +1123,9 @@ __global__ void __launch_bounds__(WS_THREADS, 1) k_moe_down_ws(MoeShape sh, MoeL
             const int nn = __shfl_sync(0xffffffffu, ti.nn, 0), p0 = __shfl_sync(0xffffffffu, ti.p0, 0);
             const int shared = __shfl_sync(0xffffffffu, ti.shared, 0);
             const int ok = __shfl_sync(0xffffffffu, ti.w0 != nullptr ? 1 : 0, 0);
-            float acc[8];
+            uint64_t acc2[4];
 #pragma unroll
-            for (int k = 0; k < 8; k++) acc[k] = 0.0f;
+            for (int k = 0; k < 4; k++) acc2[k] = 0;
             for (int g = 0; g < nbF; g += 2, G += 2) {   // two blocks per pass: one load latency
                 const int b0 = G % WS_NBUF, b1 = (G + 1) % WS_NBUF;
                 const uint32_t p0 = (G / WS_NBUF) & 1, p1 = ((G + 1) / WS_NBUF) & 1;
@@ -1123,8 +1141,8 @@ __global__ void __launch_bounds__(WS_THREADS, 1) k_moe_down_ws(MoeShape sh, MoeL
                 tmem_wait_ld();
                 tmem_fill8(t0, kMagic);
                 tmem_fill8(t1, kMagic);
-                chain_f2<8>(v0, s.dw[b0][r], s.pc[b0].v + 4 * c4, acc);
-                chain_f2<8>(v1, s.dw[b1][r], s.pc[b1].v + 4 * c4, acc);
+                chain_f2<8>(v0, s.dw[b0][r], s.pc[b0].v + 4 * c4, acc2, mp.zero);
+                chain_f2<8>(v1, s.dw[b1][r], s.pc[b1].v + 4 * c4, acc2, mp.zero);
                 tmem_wait_st();
                 tc_fence_before();
                 warp_arrive(&y.accempty[b0]);
@@ -1137,7 +1155,7 @@ __global__ void __launch_bounds__(WS_THREADS, 1) k_moe_down_ws(MoeShape sh, MoeL
                     const int n = 8 * c4 + k;
                     if (n < nn) {
                         float *out = shared ? sc.S + (int64_t)(n0 + n) * sh.D : sc.Y + (int64_t)(p0 + n0 + n) * sh.D;
-                        out[row] = canon(acc[k]);
+                        out[row] = canon(k & 1 ? hi_f(acc2[k >> 1]) : lo_f(acc2[k >> 1]));
                     }
                 }
             }
