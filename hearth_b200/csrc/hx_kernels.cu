@@ -276,6 +276,7 @@ __global__ void __launch_bounds__(256) k_moe_router(MoeShape sh, const float *__
 // (cell c, lane j) keeps lane j's chains of the 4 x 4 outputs of cell c, with K staged 64 columns at a
 // time in shared memory; the 16 lanes of a cell form one half-warp for the final tree.
 constexpr int RT_T = 16, RT_E = 16, RT_K = 64;
+constexpr int kTiledRouterMinT = 64;   // below, the per-(row, token) router keeps every SM busy
 
 __global__ void __launch_bounds__(256) k_moe_router_tiled(MoeShape sh, const float *__restrict__ router,
                                                           const float *__restrict__ gate_inp, MoeScratch sc) {
@@ -642,7 +643,7 @@ static void launch_route_stages(int which, const MoeShape &sh, const MoeLayerDev
         constexpr int RT = 64;   // 4 (row, token) items per CTA: E=128 rows -> 32 CTAs at T=1
         const unsigned grid = (unsigned)((items + RT / 16 - 1) / (RT / 16));
         const size_t route_smem = (size_t)8 * 2 * E * sizeof(float);
-        if (T >= RT_T && !fused)   // batches: tiled router GEMM
+        if (T >= kTiledRouterMinT && !fused)   // large batches: tiled router GEMM
             k_moe_router_tiled<<<dim3((unsigned)((T + RT_T - 1) / RT_T), (unsigned)((rows + RT_E - 1) / RT_E)), 256, 0,
                                  s>>>(sh, L.router, L.sh_gate_inp, sc);
         else

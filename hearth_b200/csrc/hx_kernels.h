@@ -127,7 +127,7 @@ cudaError_t launch_dequantize(int dtype, const void *W, int64_t n_rows, int64_t 
 cudaError_t launch_moe_experts_tc(const MoeShape &sh, const MoeLayerDev &L, const MoeScratch &sc, int which,
                                   cudaStream_t s);
 // Pairs (T * K) from which the unfused path runs its expert stages on the tensor cores.
-constexpr int kTcMinPairs = 256;
+constexpr int kTcMinPairs = kFusedMaxPairs + 1;
 
 // Expert-parallel combine: h += rs * (rank-order sum over j of w_j * y_all[owner rank][pair(t, j)] +
 // shared output) with the routing and shared output of the preceding launch_moe_layer.
