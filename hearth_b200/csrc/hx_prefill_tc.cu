@@ -907,12 +907,14 @@ __global__ void __launch_bounds__(WS_THREADS, 1) k_moe_gateup_ws(MoeShape sh, Mo
                 mbar_wait(&y.accfull[b], par, sc.err);
                 mbar_wait(&y.aready[b], par, sc.err);   // acquires the unpackers' scales
                 tc_fence_after();
-                uint32_t v[16];
-                const uint32_t ta = tmem + lanes + col + 64 * b;
-                tmem_ld16(ta, v);
-                tmem_fill16(ta, kMagic);
-                chain_f2<16>(v, s.dw[b][m * TC_M + r], s.pc[b].v + 8 * h, acc2, mp.zero);
-                tmem_wait_st();
+                if (16 * h < ti.nn) {   // columns of pairs past nn keep the magic start (zero operand rows)
+                    uint32_t v[16];
+                    const uint32_t ta = tmem + lanes + col + 64 * b;
+                    tmem_ld16(ta, v);
+                    tmem_fill16(ta, kMagic);
+                    chain_f2<16>(v, s.dw[b][m * TC_M + r], s.pc[b].v + 8 * h, acc2, mp.zero);
+                    tmem_wait_st();
+                }
                 tc_fence_before();
                 warp_arrive(&y.accempty[b]);
             }
