@@ -48,6 +48,40 @@ def test_ep_emulated_equals_single_handle(gpu, case, T, G):
 
 
 @pytest.mark.gpu
+@pytest.mark.parametrize("case", ["softmax", "sigmoid_group_bias"])
+def test_ep_emulated_staged_tensor_core(gpu, case):
+    """Expert parallelism on the staged tensor-core kernels (a batch of 40 tokens, D 512): each rank's
+    store holds only its experts, its jobs are its own buckets; every rank ends with the
+    single-handle h bit for bit."""
+    import torch
+    G, T, D = 2, 40, 512
+    model, be, eps = build_pair(63, L=2, D=D, F=256, E=16, K=4, max_tokens=T, ep_size=G, **CASES[case])
+    s = torch.cuda.current_stream()
+    h0 = np.random.default_rng(4).standard_normal((T, D)).astype(np.float32)
+    ref = torch.from_numpy(h0.copy()).cuda()
+    be.forward_dev(ref, T, stream=s)
+    hs = [torch.from_numpy(h0.copy()).cuda() for _ in range(G)]
+    for l in range(2):
+        ys = []
+        for r, b in enumerate(eps):
+            y = torch.full((T * 4, D), float("nan"), device="cuda")
+            b.ep_layer_dev(l, hs[r], T, y, stream=s)
+            ys.append(y)
+        y_all = torch.stack(ys).contiguous()
+        for r, b in enumerate(eps):
+            b.ep_combine_dev(l, y_all, T, hs[r], stream=s)
+    torch.cuda.synchronize()
+    for b in eps:
+        b.sync()
+    want = model.forward(h0)
+    assert np.array_equal(bits(ref.cpu().numpy()), bits(want))
+    for r in range(G):
+        assert np.array_equal(bits(hs[r].cpu().numpy()), bits(want)), f"rank {r}"
+    for b in eps + [be]:
+        b.close()
+
+
+@pytest.mark.gpu
 def test_ep_handle_rejects_whole_stack_calls(gpu):
     model, be, eps = build_pair(62, L=1, D=256, F=128, E=16, K=4, max_tokens=2, ep_size=2)
     h = np.zeros((1, 256), np.float32)

@@ -93,6 +93,32 @@ def test_streaming_store_equals_resident(gpu):
         assert st["hits"] + st["misses"] == st["expert_uses"] == 6 * 2 * 4 * L
 
 
+def slab_nbytes(D, F):
+    """FORMAT §5 slab size of a Q4 expert (gate, up at align64, down at align64, 4096-padded)."""
+    rbd, rbf = D // 64 * 34, F // 64 * 34
+    up = (F * rbd + 63) // 64 * 64
+    down = (up + F * rbd + 63) // 64 * 64
+    return (down + D * rbf + 4095) // 4096 * 4096
+
+
+def test_streaming_store_staged_tensor_core(gpu):
+    """Batches on the staged tensor-core kernels with a cache smaller than the model: each routed
+    expert sits in whatever slot the store gave it (the tensor maps address the slab arena by slot),
+    experts are evicted between layers, and the results equal the oracle."""
+    L, E, D, F, T = 3, 16, 512, 256, 40
+    model, be = build_pair(41, L=L, D=D, F=F, E=E, K=4, max_tokens=T,
+                           cache_gb=(E + 4) * slab_nbytes(D, F) / 2**30)
+    with be:
+        assert be.stats()["n_slots"] < L * E
+        rng = np.random.default_rng(9)
+        for step in range(3):
+            h = rng.standard_normal((T, D)).astype(np.float32)
+            hg = be.forward(h)
+            be.tick()
+            assert np.array_equal(bits(hg), bits(model.forward(h)))
+        assert be.stats()["evictions"] > 0
+
+
 def test_lru_policy_streaming(gpu):
     L, E = 3, 16
     model, be = build_pair(22, L=L, E=E, max_tokens=4, cache_gb=(E + 2) * 53248 / 2**30, policy=0)
