@@ -1,23 +1,26 @@
 // hx_prefill_tc.cu — expert gate/up and down on the 5th-generation tensor cores (tcgen05) for
-// prefill and verification batches (many tokens per expert).
+// prefill, speculative verification and batched decode (more than 64 token-expert pairs).
 //
 // NUMERICS §3 fixes each output as acc = ((0 + t_0) + t_1) + ... over the 64-weight blocks g of the
 // row, t_g = (float)isum_g * (dw_g * dx_g), where isum_g is the exact int32 dot of the block. The
-// tensor cores produce the isum_g of a whole tile: per block, two `tcgen05.mma .kind::i8` (K = 32
-// bytes each) write D[128 rows][32 tokens] (s32) into tensor memory, one fresh accumulation per block;
-// the CTA then reads the tile back (`tcgen05.ld`) and each thread runs its row's float chain in
-// registers, in block order. Q4 weights enter as unsigned nibbles (u8 x s8 MMA) and the identity
-// sum((nib-8)*xq) = sum(nib*xq) - 8*sum(xq) removes the offset exactly; Q8 weights enter as s8.
+// tensor cores produce the isum_g of a whole tile of 128 rows x 32 token pairs (`tcgen05.mma
+// .kind::i8`, K = 32 bytes per instruction, a fresh accumulation per block in tensor memory); the
+// CUDA cores read the tile back (`tcgen05.ld`) and run every row's float chain in block order. Q4
+// weights enter as unsigned nibbles (u8 x s8) and sum((nib-8)*xq) = sum(nib*xq) - 8*sum(xq) removes
+// the offset exactly; Q8 weights enter as s8. Operands in shared memory use the K-major, unswizzled
+// core-matrix layout of the UMMA descriptors (8 rows x 16 bytes per core matrix, K-chunks 128 bytes
+// apart, 8-row groups 512 bytes apart).
 //
-// Operands in shared memory use the K-major, unswizzled core-matrix layout of the UMMA descriptors:
-// a core matrix is 8 rows x 16 bytes (128 contiguous bytes), the four 16-byte K-chunks of a 64-byte
-// block row are 128 bytes apart (LBO) and 8-row groups 512 bytes apart (SBO). Every thread loads its
-// own row's block for the next iteration into registers while the current one is in flight.
-//
-// Gate/up CTA: 128 rows of gate and the same 128 rows of up x 32 token pairs of one job (routed expert
-// bucket or the shared expert); epilogue SwiGLU and the mid activation blocks (NUMERICS §2, one per
-// 64 rows). Down CTA: 128 rows of down x 32 pairs; epilogue the canonical outputs into Y (routed) or
-// S (shared) for the rank-order sum.
+// Two implementations:
+//   * staged (k_moe_gateup_ws / k_moe_down_ws, Q4 experts, D a multiple of 512, down rows of 4, 8 or
+//     12 blocks): persistent CTAs with warp roles, tensor-map loads into a stage ring, operand A in
+//     tensor memory, the offset and the int -> float conversion folded into the accumulator (see the
+//     section comment below);
+//   * register-fed (k_moe_gateup_tc / k_moe_down_tc, every other shape, Q8 experts included): one
+//     CTA per (row tile, job, pair tile), each thread loading its row's next block into registers
+//     while the current block is multiplied.
+// Gate/up tiles end with SwiGLU and the mid activation blocks (NUMERICS §2, one per 64 rows); down
+// tiles write the canonical outputs into Y (routed) or S (shared) for the rank-order sum.
 #include "hx_device.cuh"
 #include "hx_kernels.h"
 #include "hx_route.cuh"
@@ -571,15 +574,7 @@ __device__ __forceinline__ void warp_arrive(uint64_t *bar) {
     if ((threadIdx.x & 31) == 0) mbar_arrive(bar);
 }
 
-// Loads without the wait: the registers are valid after tmem_wait_ld().
-__device__ __forceinline__ void tmem_ld16_async(uint32_t taddr, uint32_t v[16]) {
-    asm volatile(
-        "tcgen05.ld.sync.aligned.32x32b.x16.b32 {%0,%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,%14,%15}, [%16];"
-        : "=r"(v[0]), "=r"(v[1]), "=r"(v[2]), "=r"(v[3]), "=r"(v[4]), "=r"(v[5]), "=r"(v[6]), "=r"(v[7]), "=r"(v[8]),
-          "=r"(v[9]), "=r"(v[10]), "=r"(v[11]), "=r"(v[12]), "=r"(v[13]), "=r"(v[14]), "=r"(v[15])
-        : "r"(taddr)
-        : "memory");
-}
+// Load without the wait: the registers are valid after tmem_wait_ld().
 __device__ __forceinline__ void tmem_ld8_async(uint32_t taddr, uint32_t v[8]) {
     asm volatile("tcgen05.ld.sync.aligned.32x32b.x8.b32 {%0,%1,%2,%3,%4,%5,%6,%7}, [%8];"
                  : "=r"(v[0]), "=r"(v[1]), "=r"(v[2]), "=r"(v[3]), "=r"(v[4]), "=r"(v[5]), "=r"(v[6]), "=r"(v[7])
@@ -587,13 +582,6 @@ __device__ __forceinline__ void tmem_ld8_async(uint32_t taddr, uint32_t v[8]) {
                  : "memory");
 }
 __device__ __forceinline__ void tmem_wait_ld() { asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory"); }
-
-__device__ __forceinline__ void tmem_ld8(uint32_t taddr, uint32_t v[8]) {
-    asm volatile("tcgen05.ld.sync.aligned.32x32b.x8.b32 {%0,%1,%2,%3,%4,%5,%6,%7}, [%8];"
-                 : "=r"(v[0]), "=r"(v[1]), "=r"(v[2]), "=r"(v[3]), "=r"(v[4]), "=r"(v[5]), "=r"(v[6]), "=r"(v[7])
-                 : "r"(taddr));
-    asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory");
-}
 
 __device__ __forceinline__ void tmem_fill8(uint32_t taddr, uint32_t x) {
     asm volatile("tcgen05.st.sync.aligned.32x32b.x8.b32 [%0], {%1,%1,%1,%1,%1,%1,%1,%1};" ::"r"(taddr), "r"(x) : "memory");
