@@ -561,8 +561,10 @@ constexpr int WS_DRAIN = 512;                    // warps 0-15
 constexpr int WS_UNPACK0 = 512, WS_UNPACK = 256; // warps 16-23
 constexpr int WS_COPY_WARP = 24, WS_MMA_WARP = 25;
 constexpr int WS_NBUF = 4;                       // blocks in flight between the roles
-constexpr uint32_t kMagic = 0x4B400000u;         // 1.5 * 2^23
-constexpr float kMagicF = 12582912.0f;
+constexpr uint32_t kMagic = 0x4B400000u;         // bit pattern of 1.5 * 2^23
+constexpr int kMagicI = 12582912;                // 1.5 * 2^23
+static_assert(WS_THREADS == (WS_MMA_WARP + 1) * 32 && WS_COPY_WARP * 32 == WS_UNPACK0 + WS_UNPACK,
+              "warp roles: drain, unpack, copy, MMA");
 
 __device__ __forceinline__ void mbar_arrive(uint64_t *bar) {
     asm volatile("mbarrier.arrive.shared::cta.b64 _, [%0];" ::"r"(smem_u32(bar)) : "memory");
@@ -690,7 +692,7 @@ __device__ __forceinline__ void unpack_act_ws(const uint8_t *act, int pitch, int
     if (c == 0) {
         const uint2 hd = live ? *reinterpret_cast<const uint2 *>(blk) : make_uint2(0, 0);
         float *e = reinterpret_cast<float *>(&pc.v[n >> 1]) + (n & 1);
-        e[0] = __int2float_rn(12582912 + 8 * (int)hd.y);   // cm: exact (below 2^24)
+        e[0] = __int2float_rn(kMagicI + 8 * (int)hd.y);   // cm: exact (below 2^24)
         e[2] = __uint_as_float(hd.x);                        // dx
     }
 }
@@ -709,7 +711,7 @@ __device__ __forceinline__ void unpack_act_half(const uint8_t *act, int pitch, i
     if (c == 0 && hm == 0) {
         const uint2 hd = live ? *reinterpret_cast<const uint2 *>(blk) : make_uint2(0, 0);
         float *e = reinterpret_cast<float *>(&pc.v[n >> 1]) + (n & 1);
-        e[0] = __int2float_rn(12582912 + 8 * (int)hd.y);   // cm: exact (below 2^24)
+        e[0] = __int2float_rn(kMagicI + 8 * (int)hd.y);   // cm: exact (below 2^24)
         e[2] = __uint_as_float(hd.x);                        // dx
     }
 }
