@@ -150,56 +150,91 @@ __device__ __forceinline__ void route_token_warp(const RouteCfg &R, const float 
 // Expert buckets of the batch (engine/src/model.c:1020-1037), by one CTA: experts ascending,
 // tokens ascending within an expert; pair_of[t*K + j] is the pair of token t's rank j.
 // The union of routed experts and the bucket order (engine/src/model.c:1020-1037): experts
-// ascending, and within an expert the pairs i = t*K + j ascending. One CTA: counts per expert
-// (shared atomics), an exclusive scan, then a stable counting sort over chunks of blockDim pairs in
-// order: within a warp, lanes holding the same expert rank themselves with __match_any_sync; the
-// warps' counts per expert give each warp its offset. Shared scratch: cnt [E], start [E] and
+// ascending, and within an expert the pairs i = t*K + j ascending. One CTA, a stable counting sort
+// in three barriers: warp w owns a contiguous range of pairs and counts its experts (lanes holding
+// the same expert find each other with __match_any_sync, one leader adds their number); warp 0 scans
+// the per-expert totals into bucket starts and the bucket list; each warp's first position in a
+// bucket follows the lower warps' pairs of that bucket; then every warp walks its range in order and
+// places its pairs. blockDim is a multiple of 32. Shared scratch: cnt [E], start [E] and
 // wcnt [blockDim/32][E].
 __device__ __forceinline__ void route_union_cta(int T, int K, int E, const int *ids, int *cnt, int *start, int *nu_out,
                                 int *ulist, int *u_p0, int *u_n, int *pair_tok, int *pair_of, int *wcnt) {
     const int tid = threadIdx.x, nt = blockDim.x, TK = T * K, lane = tid & 31, warp = tid >> 5;
-    const int nwarps = (nt + 31) >> 5;
-    for (int e = tid; e < E; e += nt) cnt[e] = 0;
+    const int nwarps = nt >> 5;   // blockDim is a multiple of 32
+    const int per = (TK + nwarps - 1) / nwarps, i0 = min(TK, warp * per), i1 = min(TK, i0 + per);
+    int *wh = wcnt + warp * E;    // this warp's counts per expert, then its next position per expert
+    for (int k = tid; k < nwarps * E; k += nt) wcnt[k] = 0;
     __syncthreads();
-    for (int i = tid; i < TK; i += nt) atomicAdd(&cnt[__ldcg(ids + i)], 1);
-    __syncthreads();
-    if (tid == 0) {
-        int nu = 0, p = 0;
-        for (int e = 0; e < E; e++) {
-            start[e] = p;
-            if (!cnt[e]) continue;
-            ulist[nu] = e;
-            u_p0[nu] = p;
-            u_n[nu] = cnt[e];
-            p += cnt[e];
-            nu++;
-        }
-        *nu_out = nu;
+    // 1. every warp counts the experts of its contiguous range of pairs (one leader per expert per round)
+    for (int b = i0; b < i1; b += 32) {
+        const int i = b + lane;
+        const bool live = i < i1;
+        const int e = live ? __ldcg(ids + i) : -1;
+        const unsigned peers = __match_any_sync(0xffffffffu, e);
+        if (live && (peers & ((1u << lane) - 1u)) == 0) wh[e] += __popc(peers);
+        __syncwarp();
     }
     __syncthreads();
-    for (int c0 = 0; c0 < TK; c0 += nt) {
-        for (int k = tid; k < nwarps * E; k += nt) wcnt[k] = 0;
-        __syncthreads();
-        const int i = c0 + tid;
-        const bool live = i < TK;
+    for (int e = tid; e < E; e += nt) {
+        int c = 0;
+        for (int w = 0; w < nwarps; w++) c += wcnt[w * E + e];
+        cnt[e] = c;
+    }
+    __syncthreads();
+    // 2. warp 0: bucket starts in expert order (exclusive scan of the counts) and the list of buckets
+    if (warp == 0) {
+        int run = 0, nrun = 0;
+        for (int e0 = 0; e0 < E; e0 += 32) {
+            const int e = e0 + lane;
+            const int c = e < E ? cnt[e] : 0, f = c > 0 ? 1 : 0;
+            int incl = c, fincl = f;
+#pragma unroll
+            for (int o = 1; o < 32; o <<= 1) {
+                const int v = __shfl_up_sync(0xffffffffu, incl, o), fv = __shfl_up_sync(0xffffffffu, fincl, o);
+                if (lane >= o) {
+                    incl += v;
+                    fincl += fv;
+                }
+            }
+            const int st = run + incl - c, u = nrun + fincl - f;
+            if (e < E) {
+                start[e] = st;
+                if (c) {
+                    ulist[u] = e;
+                    u_p0[u] = st;
+                    u_n[u] = c;
+                }
+            }
+            run += __shfl_sync(0xffffffffu, incl, 31);
+            nrun += __shfl_sync(0xffffffffu, fincl, 31);
+        }
+        if (lane == 0) *nu_out = nrun;
+    }
+    __syncthreads();
+    for (int e = tid; e < E; e += nt) {   // warp w's first position in bucket e: after the lower warps' pairs
+        int p = start[e];
+        for (int w = 0; w < nwarps; w++) {
+            const int c = wcnt[w * E + e];
+            wcnt[w * E + e] = p;
+            p += c;
+        }
+    }
+    __syncthreads();
+    // 3. every warp places its pairs, in pair order (so each bucket lists its tokens in ascending order)
+    for (int b = i0; b < i1; b += 32) {
+        const int i = b + lane;
+        const bool live = i < i1;
         const int e = live ? __ldcg(ids + i) : -1;
         const unsigned peers = __match_any_sync(0xffffffffu, e);
         const int rank = __popc(peers & ((1u << lane) - 1u));
-        if (live && rank == 0) wcnt[warp * E + e] = __popc(peers);
-        __syncthreads();
         if (live) {
-            int p = start[e] + rank;
-            for (int w = 0; w < warp; w++) p += wcnt[w * E + e];
+            const int p = wh[e] + rank;
             pair_tok[p] = i / K;
             pair_of[i] = p;
         }
-        __syncthreads();
-        for (int x = tid; x < E; x += nt) {
-            int add = 0;
-            for (int w = 0; w < nwarps; w++) add += wcnt[w * E + x];
-            start[x] += add;
-        }
-        __syncthreads();
+        __syncwarp();
+        if (live && rank == 0) wh[e] += __popc(peers);
+        __syncwarp();
     }
 }
 
