@@ -507,7 +507,7 @@ __device__ __forceinline__ void tmem_ld16(uint32_t taddr, uint32_t v[16]) {
     asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory");
 }
 
-// Tensor-map loads into this CTA's shared memory (no multicast), completion counted on bar. The box
+// Tensor-map loads into this CTA's own shared memory, completion counted on bar. The box
 // origin's x times the element size is a multiple of 16 bytes for every call below.
 __device__ __forceinline__ void tma_load_2d(void *dst, const void *map, int x, int y, uint64_t *bar) {
     asm volatile(
