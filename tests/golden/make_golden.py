@@ -2,7 +2,7 @@
 
 Run here (where the reference tree and its build exist), never on the GPU box:
 
-    python tests/golden/make_golden.py [--ref /root/reference]
+    python tests/golden/make_golden.py [--ref <checkout of the reference repository>]
 
 Sources of truth, all reference code:
 * pinned_matmul.npz  — the reference's pinned-hash inputs (engine/tests/test_quant.c:873-887 det_fill,
