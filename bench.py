@@ -428,7 +428,7 @@ def run_ours(args, rank, world, local_rank):
     line = {"metric": METRIC, "value": round(value, 3), "unit": "tok/s", "n_gpus": world, "steps": args.steps,
             "warmup": args.warmup, "ms_per_step": round(ms / args.steps, 5), "higher_is_better": True,
             "scaling": "weak", "vs_baseline": None, "dtype": "q4xq8-int32+f32", "data": "synthetic",
-            "config": {"workload": f"qwen3-30b-a3b MoE stack decode, {L_} layers, batch {B}",
+            "config": {"workload": f"qwen3-30b-a3b MoE stack {'decode' if B == 1 else 'batch step'}, {L_} layers, batch {B}",
                        "layers": L_, "d_model": D_, "expert_ffn_dim": F_, "n_experts": E_, "top_k": K_,
                        "batch": B, "parallelism": f"replica x{world}",
                        "l2": "no flush: each step reads ~1.01 GB of expert/router weights (> 126 MB L2)"},
