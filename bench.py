@@ -187,7 +187,7 @@ def run_reference(args, rank, world):
             "warmup": args.warmup, "ms_per_step": round(1000.0 * args.batch / tps, 3), "higher_is_better": True,
             "scaling": "weak", "vs_baseline": None, "dtype": "q4xq8-int32+f32", "data": "synthetic",
             "impl": "reference",
-            "config": {"workload": f"qwen3-30b-a3b MoE stack decode, {L_} layers, batch {args.batch}",
+            "config": {"workload": f"qwen3-30b-a3b MoE stack {'decode' if args.batch == 1 else 'batch step'}, {L_} layers, batch {args.batch}",
                        "layers": L_, "d_model": D_, "expert_ffn_dim": F_, "n_experts": E_, "top_k": K_,
                        "batch": args.batch},
             "cpu_baseline": {"value": round(tps, 3), "unit": "tok/s", "cores": ref.threads, "kind": "reference",
