@@ -358,13 +358,13 @@ __device__ void down_tc_body(const MoeShape &sh, const MoeScratch &sc, const Job
 }
 
 // =============================================================================================
-// Staged persistent path (Q4 experts). One CTA of 256 threads per SM walks a static list of
-// tiles; the weight rows and activation rows of each tile reach shared memory by 1-D bulk copies
-// (cp.async.bulk, one per row segment) into a two-slot ring that runs ahead across tiles, so that
-// up to two stages (~176 KB) per SM are in flight while the CTA unpacks, multiplies and drains.
-// Unpacking reads shared memory with 16- or 8-byte loads that are free of bank conflicts; the row
-// loads of the register path above touch one 32-byte sector per thread and instruction, which
-// keeps the load/store unit, not HBM, busy.
+// Staged persistent path (Q4 experts). One CTA per SM walks a static list of tiles; the weight rows
+// and activation rows of each tile reach shared memory through tensor-map loads (one box of 128 rows
+// per matrix and stage, gather4 boxes of four token rows, one box of 32 mid rows for down) into a
+// two-slot ring that runs ahead across tiles, so that up to two stages (~176 KB) per SM are in
+// flight while the CTA unpacks, multiplies and drains. Unpacking reads shared memory with 16- or
+// 8-byte loads laid out to avoid bank conflicts; the row loads of the register path above touch one
+// 32-byte sector per thread and instruction, which keeps the load/store unit, not HBM, busy.
 //
 // Tiles: job u (routed bucket or the shared expert) owns ceil(n_u / 32) x (row tiles) tiles, in
 // job order and, inside a job, pair tile major and row tile minor, so that consecutive tiles read
