@@ -11,6 +11,6 @@ CPU fallback.
 from ._lib import (BF16, F16, F32, POLICY_LFU, POLICY_LRU, Q4, Q8, SCORE_SIGMOID, SCORE_SOFTMAX,  # noqa: F401
                    lib, last_error)
 from . import native  # noqa: F401
-from .moe import MoeBackend  # noqa: F401
+from .moe import MoeBackend, container_probe  # noqa: F401
 
-__all__ = ["lib", "last_error", "native", "MoeBackend", "F32", "F16", "BF16", "Q8", "Q4"]
+__all__ = ["lib", "last_error", "native", "MoeBackend", "container_probe", "F32", "F16", "BF16", "Q8", "Q4"]

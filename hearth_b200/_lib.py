@@ -27,7 +27,7 @@ EXPORTS = [
     "hxb_moe_layer_dev", "hxb_moe_last_routing", "hxb_moe_get_stats", "hxb_moe_reset_stats",
     "hxb_moe_is_resident", "hxb_moe_tick", "hxb_moe_prefetch", "hxb_moe_seed_heat", "hxb_moe_set_copy_hook",
     "hxb_moe_sync", "hxb_moe_profile", "hxb_matmul_noalloc", "hxb_moe_phase_trace", "hxb_moe_decode_path",
-    "hxb_moe_ep_layer_dev", "hxb_moe_ep_combine_dev",
+    "hxb_moe_ep_layer_dev", "hxb_moe_ep_combine_dev", "hxb_container_probe", "hxb_moe_load_container",
 ]
 
 
@@ -39,6 +39,12 @@ class MoeConfig(C.Structure):
                 ("shared_ffn_dim", C.c_int), ("shared_dtype", C.c_int), ("shared_gate", C.c_int),
                 ("max_tokens", C.c_int), ("cache_gb", C.c_double), ("policy", C.c_int), ("heat_decay", C.c_float),
                 ("device", C.c_int), ("ep_size", C.c_int), ("ep_rank", C.c_int)]
+
+
+class ContainerInfo(C.Structure):
+    _fields_ = [("n_layers", C.c_int), ("n_moe_layers", C.c_int), ("n_expert_entries", C.c_int),
+                ("n_physical_slabs", C.c_int), ("n_aliased", C.c_int), ("expert_dtype", C.c_int),
+                ("slab_bytes", C.c_uint64)]
 
 
 class MoeStats(C.Structure):
@@ -100,6 +106,8 @@ def lib() -> C.CDLL:
         "hxb_moe_decode_path": (C.c_int, [vp]),
         "hxb_moe_ep_layer_dev": (i, [vp, i, vp, i, vp, vp]),
         "hxb_moe_ep_combine_dev": (i, [vp, i, vp, i, vp, vp]),
+        "hxb_container_probe": (i, [C.c_char_p, C.POINTER(MoeConfig), C.POINTER(ContainerInfo), C.c_char_p, sz]),
+        "hxb_moe_load_container": (i, [vp, C.c_char_p]),
     }
     for name, (res, args) in sig.items():
         fn = getattr(L, name)

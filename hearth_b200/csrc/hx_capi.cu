@@ -4,8 +4,11 @@
 #include "hx_common.cuh"
 #include "hx_kernels.h"
 #include "hx_store.h"
+#include "hx_container.h"
 
+#include <algorithm>
 #include <chrono>
+#include <sys/stat.h>
 #include <cstdlib>
 #include <cstdarg>
 #include <cstdio>
@@ -1068,4 +1071,155 @@ extern "C" HXB_API int64_t hxb_moe_phase_trace(hxb_moe *m, uint64_t *out, int64_
     cudaSetDevice(m->device);
     if (cudaMemcpy(out, m->dec_trace.p, sizeof(uint64_t) * (size_t)n, cudaMemcpyDeviceToHost) != cudaSuccess) return -1;
     return n;
+}
+
+// ------------------------------------------------------------------------------- .hearth containers
+
+extern "C" HXB_API int hxb_container_probe(const char *path, hxb_moe_config *cfg, hxb_container_info *info, char *err,
+                                           size_t errlen) {
+    if (!path) {
+        set_errbuf(err, errlen, "hxb_container_probe: null path");
+        return HXB_E_ARG;
+    }
+    ContainerFile f;
+    std::string why;
+    if (!f.open(path, why)) {
+        set_errbuf(err, errlen, "hxb_container_probe: " + why);
+        struct stat st;
+        return stat(path, &st) == 0 ? HXB_E_FORMAT : HXB_E_IO;
+    }
+    const Container &c = f.info();
+    if (cfg) {
+        hxb_moe_default_config(cfg);
+        cfg->n_layers = (int)c.n_layers;
+        cfg->d_model = (int)c.d_model;
+        cfg->expert_ffn_dim = (int)c.expert_ffn_dim;
+        cfg->n_experts = (int)c.n_experts;
+        cfg->top_k = (int)c.top_k;
+        cfg->score_fn = (int)c.score_fn;
+        cfg->score_bias = (int)c.score_bias;
+        cfg->n_group = (int)c.n_group;
+        cfg->topk_group = (int)c.topk_group;
+        cfg->norm_topk_prob = (int)c.norm_topk_prob;
+        cfg->routed_scale = c.routed_scale;
+        cfg->residual_scale = c.residual_scale;
+        cfg->norm_eps = c.norm_eps;
+        if (c.expert_dtype >= 0) cfg->expert_dtype = c.expert_dtype;
+        cfg->shared_ffn_dim = (int)c.shared_ffn_dim;
+        cfg->shared_gate = (int)c.shared_gate;
+        for (uint32_t l = 0; l < c.n_layers && c.shared_ffn_dim; l++) {   // the shared expert's dtype
+            const CtTensor *t = c.find("blk." + std::to_string(l) + ".shexp_gate");
+            if (c.layer_kind[l] && t) {
+                cfg->shared_dtype = (int)t->dtype;
+                break;
+            }
+        }
+    }
+    if (info) {
+        info->n_layers = (int)c.n_layers;
+        info->n_moe_layers = c.n_moe_layers;
+        info->n_expert_entries = (int)c.experts.size();
+        info->n_physical_slabs = c.n_physical;
+        info->n_aliased = c.n_aliased;
+        info->expert_dtype = c.expert_dtype;
+        info->slab_bytes = 0;
+        for (const CtExpert &x : c.experts)
+            if (x.nbytes) {
+                info->slab_bytes = x.nbytes;
+                break;
+            }
+    }
+    return HXB_OK;
+}
+
+extern "C" HXB_API int hxb_moe_load_container(hxb_moe *m, const char *path) {
+    if (!m || !path) return fail(HXB_E_ARG, "load_container: bad arguments");
+    ContainerFile f;
+    std::string why;
+    if (!f.open(path, why)) {
+        struct stat st;
+        return fail(stat(path, &st) == 0 ? HXB_E_FORMAT : HXB_E_IO, "load_container: %s", why.c_str());
+    }
+    const Container &c = f.info();
+    const hxb_moe_config &k = m->cfg;
+    const char *diff = nullptr;
+    if ((int)c.n_layers != k.n_layers) diff = "n_layers";
+    else if ((int)c.d_model != k.d_model) diff = "d_model";
+    else if ((int)c.n_experts != k.n_experts || (int)c.top_k != k.top_k) diff = "n_experts / top_k";
+    else if ((int)c.expert_ffn_dim != k.expert_ffn_dim) diff = "expert_ffn_dim";
+    else if ((int)c.score_fn != k.score_fn || (int)c.score_bias != k.score_bias || (int)c.n_group != k.n_group ||
+             (int)c.topk_group != k.topk_group || (int)c.norm_topk_prob != k.norm_topk_prob ||
+             c.routed_scale != k.routed_scale)
+        diff = "routing";
+    else if ((int)c.shared_ffn_dim != k.shared_ffn_dim || (int)c.shared_gate != k.shared_gate) diff = "shared expert";
+    if (diff) return fail(HXB_E_ARG, "load_container: the handle and the container disagree on %s", diff);
+    if (c.n_moe_layers && c.expert_dtype != k.expert_dtype)
+        return fail(HXB_E_UNSUPPORTED, "load_container: slabs must all have the handle's expert dtype");
+    const size_t D = (size_t)k.d_model, E = (size_t)k.n_experts;
+
+    // dense per-layer weights of every MoE layer
+    auto tensor = [&](uint32_t l, const char *name, uint32_t dtype, uint64_t nbytes, std::vector<uint8_t> &out,
+                      bool required) -> int {
+        const CtTensor *t = c.find("blk." + std::to_string(l) + "." + name);
+        if (!t) {
+            out.clear();
+            return required ? fail(HXB_E_FORMAT, "load_container: layer %u has no %s", l, name) : HXB_OK;
+        }
+        if ((dtype != ~0u && t->dtype != dtype) || t->nbytes != nbytes)
+            return fail(HXB_E_UNSUPPORTED, "load_container: layer %u %s has dtype %u and %llu bytes (expected %llu)", l,
+                        name, t->dtype, (unsigned long long)t->nbytes, (unsigned long long)nbytes);
+        out.resize(nbytes);
+        if (!f.read(t->off, out.data(), nbytes, why)) return fail(HXB_E_IO, "load_container: %s", why.c_str());
+        return HXB_OK;
+    };
+    std::vector<uint8_t> router, bias, norm, sg, su, sd, sgi;
+    const size_t Fs = (size_t)k.shared_ffn_dim;
+    const uint64_t shb = Fs ? (uint64_t)row_bytes(k.shared_dtype, (int64_t)D) * Fs : 0;
+    const uint64_t shd = Fs ? (uint64_t)row_bytes(k.shared_dtype, (int64_t)Fs) * D : 0;
+    for (uint32_t l = 0; l < c.n_layers; l++) {
+        if (!c.layer_kind[l]) continue;
+        int rc;
+        if ((rc = tensor(l, "moe_router", 0, 4 * E * D, router, true)) != HXB_OK ||
+            (rc = tensor(l, "moe_router_bias", 0, 4 * E, bias, k.score_bias != 0)) != HXB_OK ||
+            (rc = tensor(l, "ffn_norm", 0, 4 * D, norm, true)) != HXB_OK)
+            return rc;
+        if (Fs && ((rc = tensor(l, "shexp_gate", (uint32_t)k.shared_dtype, shb, sg, true)) != HXB_OK ||
+                   (rc = tensor(l, "shexp_up", (uint32_t)k.shared_dtype, shb, su, true)) != HXB_OK ||
+                   (rc = tensor(l, "shexp_down", (uint32_t)k.shared_dtype, shd, sd, true)) != HXB_OK ||
+                   (k.shared_gate && (rc = tensor(l, "shexp_gate_inp", 0, 4 * D, sgi, true)) != HXB_OK)))
+            return rc;
+        rc = hxb_moe_set_layer(m, (int)l, reinterpret_cast<const float *>(router.data()),
+                               k.score_bias ? reinterpret_cast<const float *>(bias.data()) : nullptr,
+                               reinterpret_cast<const float *>(norm.data()), Fs ? sg.data() : nullptr,
+                               Fs ? su.data() : nullptr, Fs ? sd.data() : nullptr,
+                               Fs && k.shared_gate ? reinterpret_cast<const float *>(sgi.data()) : nullptr);
+        if (rc != HXB_OK) return rc;
+    }
+
+    // expert slabs: each physical slab read once, in file order, for every entry naming it
+    std::vector<size_t> order;
+    for (size_t i = 0; i < c.experts.size(); i++)
+        if (c.experts[i].nbytes) order.push_back(i);
+    std::sort(order.begin(), order.end(),
+              [&](size_t a, size_t b) { return c.experts[a].off < c.experts[b].off || (c.experts[a].off == c.experts[b].off && a < b); });
+    std::vector<uint8_t> slab;
+    for (size_t q = 0; q < order.size();) {
+        size_t q1 = q;
+        bool wanted = false;
+        while (q1 < order.size() && c.experts[order[q1]].off == c.experts[order[q]].off) {
+            wanted = wanted || m->owns((int)(order[q1] % E));
+            q1++;
+        }
+        if (wanted) {
+            const CtExpert &x = c.experts[order[q]];
+            slab.resize(x.nbytes);
+            if (!f.read(x.off, slab.data(), x.nbytes, why)) return fail(HXB_E_IO, "load_container: %s", why.c_str());
+            for (size_t r = q; r < q1; r++) {
+                const int rc = hxb_moe_set_expert(m, (int)(order[r] / E), (int)(order[r] % E), slab.data(), x.nbytes);
+                if (rc != HXB_OK) return rc;
+            }
+        }
+        q = q1;
+    }
+    return HXB_OK;
 }

@@ -7,6 +7,7 @@ row-major [out, in] matrices), or are synthesised in HBM for benchmarks.
 from __future__ import annotations
 
 import ctypes as C
+import os
 
 import numpy as np
 
@@ -36,8 +37,47 @@ def _stream(s):
     return C.c_void_p(int(s))
 
 
+_CONFIG_KEYS = ("n_layers", "d_model", "expert_ffn_dim", "n_experts", "top_k", "score_fn", "score_bias", "n_group",
+                "topk_group", "norm_topk_prob", "routed_scale", "residual_scale", "norm_eps", "expert_dtype",
+                "shared_ffn_dim", "shared_dtype", "shared_gate")
+
+
+def container_probe(path) -> tuple[dict, dict]:
+    """Reads and validates a .hearth container (host only): (the MoeBackend configuration of its MoE
+    path, {n_layers, n_moe_layers, n_expert_entries, n_physical_slabs, n_aliased, expert_dtype,
+    slab_bytes}). Raises ValueError for a file that breaks the format, OSError for one that cannot be
+    read."""
+    from ._lib import ContainerInfo
+    c, info = MoeConfig(), ContainerInfo()
+    err = C.create_string_buffer(512)
+    rc = lib().hxb_container_probe(os.fsencode(path), C.byref(c), C.byref(info), err, 512)
+    if rc == _lib.HXB_E_IO:
+        raise OSError(err.value.decode())
+    if rc != 0:
+        raise ValueError(err.value.decode())
+    cfg = {k: getattr(c, k) for k in _CONFIG_KEYS}
+    return cfg, {k: getattr(info, k) for k, _ in info._fields_}
+
+
 class MoeBackend:
     """One MoE stack (n_layers layers of the same shape) on one CUDA device."""
+
+    @classmethod
+    def from_container(cls, path, **options) -> "MoeBackend":
+        """A handle for a .hearth container's MoE layers (one slot per model layer; dense layers stay
+        unset) with its weights loaded. options: max_tokens, cache_gb, policy, heat_decay, device,
+        ep_size, ep_rank."""
+        cfg, _ = container_probe(path)
+        b = cls(**cfg, **options)
+        try:
+            b.load_container(path)
+        except BaseException:
+            b.close()
+            raise
+        return b
+
+    def load_container(self, path) -> None:
+        check(lib().hxb_moe_load_container(self.h, os.fsencode(path)), "hxb_moe_load_container")
 
     def __init__(self, *, n_layers: int, d_model: int, expert_ffn_dim: int, n_experts: int, top_k: int,
                  score_fn: int = 0, score_bias: int = 0, n_group: int = 1, topk_group: int = 1,

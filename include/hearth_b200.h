@@ -137,6 +137,34 @@ HXB_API int hxb_moe_set_expert(hxb_moe *m, int layer, int expert, const void *sl
 HXB_API int hxb_moe_synthesize(hxb_moe *m, uint64_t seed, float sigma_router, float sigma_expert);
 HXB_API size_t hxb_moe_slab_bytes(const hxb_moe *m);
 
+/* ---- .hearth containers (docs/FORMAT.md of the reference; the reference reads them in
+ * engine/src/modelfile.c and builds its model from them in hx_model_open, engine/src/model.c:1651).
+ * hxb_container_probe reads and validates a container (preamble, metadata, tensor and expert
+ * directories, alignment, sizes, aliases, no overlaps; host only, no device work) and fills a
+ * configuration for it: hxb_moe_default_config values plus the container's MoE shape and routing
+ * (n_layers = the container's layers: one handle slot per layer, dense layers stay unset). The
+ * caller then sets max_tokens, cache_gb, policy, device, ep_size / ep_rank and opens the handle.
+ * Returns HXB_E_IO for a file that cannot be read, HXB_E_FORMAT (message in err) for one that breaks
+ * the format's rules. */
+typedef struct hxb_container_info {
+    int n_layers;            /* transformer blocks in the file */
+    int n_moe_layers;        /* of them MoE (layer_kind 1) */
+    int n_expert_entries;    /* n_layers * n_experts */
+    int n_physical_slabs;    /* distinct slabs among the MoE layers' entries */
+    int n_aliased;           /* entries that share another entry's slab (synthetic benchmark files) */
+    int expert_dtype;        /* dtype of every slab, -1 when the slabs mix dtypes */
+    uint64_t slab_bytes;     /* bytes of one slab */
+} hxb_container_info;
+HXB_API int hxb_container_probe(const char *path, hxb_moe_config *cfg, hxb_container_info *info, char *err,
+                                size_t errlen);
+/* Loads a container's MoE weights into a handle opened with a configuration from
+ * hxb_container_probe: per MoE layer hxb_moe_set_layer (moe_router, moe_router_bias, ffn_norm,
+ * shexp_gate/up/down, shexp_gate_inp), then hxb_moe_set_expert for every expert this handle holds.
+ * Each physical slab is read once and handed to every entry that names it. HXB_E_ARG if the handle
+ * and the container disagree on the shape or routing, HXB_E_UNSUPPORTED for slabs that are not all
+ * Q4 or all Q8 or a shexp_gate_inp that is not F32, HXB_E_FORMAT / HXB_E_IO as above. */
+HXB_API int hxb_moe_load_container(hxb_moe *m, const char *path);
+
 /* h[T, D] (host, in place): for l in [layer0, layer0 + n_layers): x = rmsnorm(h, ffn_norm_l);
  * h = h + residual_scale * moe_l(x)   (docs/NUMERICS.md §5, the FFN half of each layer). */
 HXB_API int hxb_moe_forward(hxb_moe *m, float *h, int T, int layer0, int n_layers);

@@ -1,0 +1,39 @@
+"""hxb_moe_load_container on the GPU: a handle opened from a .hearth file written by the reference's
+own container writer (tests/golden/make_container.py) evaluates its MoE layers bit for bit like the
+oracle on the same weights, with every expert resident and with a streaming store smaller than the
+file's physical slabs; aliased entries read their target's slab."""
+import numpy as np
+import pytest
+
+import hearth_b200 as hb
+from tests.container_util import FIXTURE, FIXTURE_KW, fixture_layers
+from tests.moe_util import bits, oracle_model
+
+pytestmark = pytest.mark.gpu
+
+
+@pytest.mark.parametrize("cache_slabs", [0, 10])
+@pytest.mark.parametrize("T", [1, 5])
+def test_container_layers_equal_oracle(gpu, T, cache_slabs):
+    model = oracle_model(fixture_layers(), **FIXTURE_KW)
+    opts = dict(max_tokens=8)
+    if cache_slabs:   # fewer slots than the 13 physical slabs (16 logical experts): streaming
+        opts["cache_gb"] = cache_slabs * 16384 / 2**30
+    be = hb.MoeBackend.from_container(FIXTURE, **opts)
+    with be:
+        if cache_slabs:
+            assert be.stats()["n_slots"] < 13
+        rng = np.random.default_rng(T)
+        for _ in range(3):
+            h = rng.standard_normal((T, 128)).astype(np.float32)
+            got = be.forward(h, layer0=1, n_layers=2)   # layer 0 of the file is dense: not in the handle
+            be.tick()
+            assert np.array_equal(bits(got), bits(model.forward(h)))
+
+
+def test_handle_that_disagrees_with_the_container_is_refused(gpu):
+    cfg, _ = hb.container_probe(FIXTURE)
+    cfg["top_k"] = 3
+    with hb.MoeBackend(**cfg, max_tokens=2) as be:
+        with pytest.raises(RuntimeError, match="disagree"):
+            be.load_container(FIXTURE)
