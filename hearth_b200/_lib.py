@@ -28,6 +28,7 @@ EXPORTS = [
     "hxb_moe_is_resident", "hxb_moe_tick", "hxb_moe_prefetch", "hxb_moe_seed_heat", "hxb_moe_set_copy_hook",
     "hxb_moe_sync", "hxb_moe_profile", "hxb_matmul_noalloc", "hxb_moe_phase_trace", "hxb_moe_decode_path",
     "hxb_moe_ep_layer_dev", "hxb_moe_ep_combine_dev", "hxb_container_probe", "hxb_moe_load_container",
+    "hxb_moe_share_expert",
 ]
 
 
@@ -53,7 +54,8 @@ class MoeStats(C.Structure):
                 ("evictions", C.c_uint64), ("prefetch_issued", C.c_uint64), ("prefetch_used", C.c_uint64),
                 ("prefetch_wasted", C.c_uint64), ("bytes_copied", C.c_uint64), ("copies", C.c_uint64),
                 ("copy_errors", C.c_uint64), ("n_slots", C.c_int), ("resident", C.c_int), ("pinned", C.c_int),
-                ("slot_bytes", C.c_uint64), ("wall_s", C.c_double), ("stall_s", C.c_double)]
+                ("slot_bytes", C.c_uint64), ("wall_s", C.c_double), ("stall_s", C.c_double),
+                ("host_bytes", C.c_uint64)]
 
 
 COPY_HOOK = C.CFUNCTYPE(C.c_int, C.c_void_p, C.c_int, C.c_int)
@@ -108,6 +110,7 @@ def lib() -> C.CDLL:
         "hxb_moe_ep_combine_dev": (i, [vp, i, vp, i, vp, vp]),
         "hxb_container_probe": (i, [C.c_char_p, C.POINTER(MoeConfig), C.POINTER(ContainerInfo), C.c_char_p, sz]),
         "hxb_moe_load_container": (i, [vp, C.c_char_p]),
+        "hxb_moe_share_expert": (i, [vp, i, i, i, i]),
     }
     for name, (res, args) in sig.items():
         fn = getattr(L, name)

@@ -548,6 +548,22 @@ extern "C" HXB_API int hxb_moe_set_layer(hxb_moe *m, int layer, const float *rou
     return HXB_OK;
 }
 
+// Resident mode: (re)places an expert's slab in its HBM slot from its host source and points both
+// pointer tables at it.
+static int place_resident_expert(hxb_moe *m, int layer, int expert) {
+    cudaEvent_t ev = nullptr;
+    const uint8_t *p = m->store.acquire_async(layer, expert, &ev);
+    if (!p) return fail(HXB_E_IO, "set_expert: could not place the expert in HBM");
+    m->store.release(layer, expert, m->store.copy_stream());
+    cudaStreamSynchronize(m->store.copy_stream());
+    m->host_table[(size_t)layer * m->cfg.n_experts + expert] = p;
+    if (!cuda_ok(cudaMemcpy(m->table.as<const uint8_t *>() + (size_t)layer * m->cfg.n_experts + expert, &p, sizeof p,
+                            cudaMemcpyHostToDevice),
+                 "set_expert table"))
+        return HXB_E_DEVICE;
+    return HXB_OK;
+}
+
 extern "C" HXB_API int hxb_moe_set_expert(hxb_moe *m, int layer, int expert, const void *slab, size_t nbytes) {
     if (!m || layer < 0 || layer >= m->cfg.n_layers || expert < 0 || expert >= m->cfg.n_experts || !slab ||
         nbytes < (size_t)m->lay.end || nbytes > m->slab_bytes)
@@ -556,17 +572,30 @@ extern "C" HXB_API int hxb_moe_set_expert(hxb_moe *m, int layer, int expert, con
     cudaSetDevice(m->device);
     std::string why;
     if (!m->store.set_source(layer, expert, slab, nbytes, why)) return fail(HXB_E_NOMEM, "set_expert: %s", why.c_str());
-    if (m->resident_mode) {   // every expert keeps a slot: copy it in now
-        cudaEvent_t ev = nullptr;
-        const uint8_t *p = m->store.acquire_async(layer, expert, &ev);
-        if (!p) return fail(HXB_E_IO, "set_expert: could not place the expert in HBM");
-        m->store.release(layer, expert, m->store.copy_stream());
-        cudaStreamSynchronize(m->store.copy_stream());
-        m->host_table[(size_t)layer * m->cfg.n_experts + expert] = p;
-        if (!cuda_ok(cudaMemcpy(m->table.as<const uint8_t *>() + (size_t)layer * m->cfg.n_experts + expert, &p,
-                                sizeof p, cudaMemcpyHostToDevice),
-                     "set_expert table"))
-            return HXB_E_DEVICE;
+    if (m->resident_mode) {   // every expert keeps a slot: copy it in now (and the experts sharing its bytes)
+        int rc = place_resident_expert(m, layer, expert);
+        for (int k : m->store.aliases_of(layer, expert))
+            if (rc == HXB_OK) rc = place_resident_expert(m, k / m->cfg.n_experts, k % m->cfg.n_experts);
+        if (rc != HXB_OK) return rc;
+        m->store.reset_stats();
+    }
+    drop_graphs(m);
+    return HXB_OK;
+}
+
+extern "C" HXB_API int hxb_moe_share_expert(hxb_moe *m, int layer, int expert, int src_layer, int src_expert) {
+    if (!m || layer < 0 || layer >= m->cfg.n_layers || expert < 0 || expert >= m->cfg.n_experts || src_layer < 0 ||
+        src_layer >= m->cfg.n_layers || src_expert < 0 || src_expert >= m->cfg.n_experts)
+        return fail(HXB_E_ARG, "share_expert: bad arguments");
+    if (!m->owns(expert)) return HXB_OK;
+    if (!m->owns(src_expert)) return fail(HXB_E_ARG, "share_expert: the source expert is not held by this handle");
+    cudaSetDevice(m->device);
+    std::string why;
+    if (!m->store.share_source(layer, expert, src_layer, src_expert, why))
+        return fail(HXB_E_ARG, "share_expert: %s", why.c_str());
+    if (m->resident_mode) {
+        const int rc = place_resident_expert(m, layer, expert);
+        if (rc != HXB_OK) return rc;
         m->store.reset_stats();
     }
     drop_graphs(m);
@@ -926,6 +955,7 @@ extern "C" HXB_API int hxb_moe_get_stats(hxb_moe *m, hxb_moe_stats *out) {
     out->resident = m->store.n_ready();
     out->pinned = m->store.n_pinned();
     out->slot_bytes = m->slab_bytes;
+    out->host_bytes = (uint64_t)m->store.host_bytes();
     return HXB_OK;
 }
 
@@ -1196,7 +1226,8 @@ extern "C" HXB_API int hxb_moe_load_container(hxb_moe *m, const char *path) {
         if (rc != HXB_OK) return rc;
     }
 
-    // expert slabs: each physical slab read once, in file order, for every entry naming it
+    // expert slabs: each physical slab read once, in file order; the entries naming it share one host
+    // copy (hxb_moe_share_expert)
     std::vector<size_t> order;
     for (size_t i = 0; i < c.experts.size(); i++)
         if (c.experts[i].nbytes) order.push_back(i);
@@ -1214,9 +1245,14 @@ extern "C" HXB_API int hxb_moe_load_container(hxb_moe *m, const char *path) {
             const CtExpert &x = c.experts[order[q]];
             slab.resize(x.nbytes);
             if (!f.read(x.off, slab.data(), x.nbytes, why)) return fail(HXB_E_IO, "load_container: %s", why.c_str());
+            int first = -1;   // the first entry this handle holds gets the bytes; the others share them
             for (size_t r = q; r < q1; r++) {
-                const int rc = hxb_moe_set_expert(m, (int)(order[r] / E), (int)(order[r] % E), slab.data(), x.nbytes);
+                const int l = (int)(order[r] / E), e = (int)(order[r] % E);
+                if (!m->owns(e)) continue;
+                const int rc = first < 0 ? hxb_moe_set_expert(m, l, e, slab.data(), x.nbytes)
+                                         : hxb_moe_share_expert(m, l, e, first / (int)E, first % (int)E);
                 if (rc != HXB_OK) return rc;
+                if (first < 0) first = (int)order[r];
             }
         }
         q = q1;

@@ -52,6 +52,7 @@ bool HbmStore::open(int L, int E, size_t slot_bytes, int n_slots, int policy, fl
     slot_of_.assign(nk, -1);
     host_.assign(nk, nullptr);
     host_n_.assign(nk, 0);
+    host_owner_.assign(nk, -1);
     heat_.assign(nk, 0.0);
     count_.assign(nk, 0.0);
     heat_tick_.assign(nk, 0);
@@ -69,9 +70,10 @@ void HbmStore::close() {
         if (s.done) cudaEventDestroy(s.done);
     }
     slots_.clear();
-    for (auto *p : host_)
-        if (p) cudaFreeHost(p);
+    for (size_t k = 0; k < host_.size(); k++)
+        if (host_[k] && host_owner_[k] == (int64_t)k) cudaFreeHost(host_[k]);
     host_.clear();
+    host_owner_.clear();
     if (copy_) cudaStreamDestroy(copy_);
     copy_ = nullptr;
     if (arena_) cudaFree(arena_);
@@ -84,19 +86,79 @@ bool HbmStore::set_source(int layer, int expert, const void *bytes, size_t n, st
         return false;
     }
     const size_t key = (size_t)layer * E_ + expert;
-    if (!host_[key] || host_n_[key] != n) {
-        if (host_[key]) cudaFreeHost(host_[key]);
+    if (host_owner_[key] >= 0 && host_owner_[key] != (int64_t)key) {   // an alias takes its own buffer now
         host_[key] = nullptr;
-        if (cudaHostAlloc((void **)&host_[key], n, cudaHostAllocDefault) != cudaSuccess) {
+        host_n_[key] = 0;
+        host_owner_[key] = -1;
+    }
+    if (!host_[key] || host_n_[key] != n) {
+        uint8_t *p = nullptr;
+        if (cudaHostAlloc((void **)&p, n, cudaHostAllocDefault) != cudaSuccess) {
             cudaGetLastError();
-            host_[key] = nullptr;
             err = "store: cannot pin host memory for an expert";
             return false;
         }
+        uint8_t *old = host_[key];
+        host_[key] = p;
         host_n_[key] = n;
+        host_owner_[key] = (int64_t)key;
+        for (size_t k = 0; k < host_.size(); k++)   // the aliases of this key follow its new buffer
+            if (k != key && host_owner_[k] == (int64_t)key) {
+                host_[k] = p;
+                host_n_[k] = n;
+            }
+        if (old) cudaFreeHost(old);
     }
     std::memcpy(host_[key], bytes, n);
-    // a resident copy of an older source is stale: drop it (unless in use)
+    drop_stale_slot(key);
+    for (size_t k = 0; k < host_.size(); k++)
+        if (k != key && host_owner_[k] == (int64_t)key) drop_stale_slot(k);
+    return true;
+}
+
+bool HbmStore::share_source(int layer, int expert, int src_layer, int src_expert, std::string &err) {
+    if (layer < 0 || layer >= L_ || expert < 0 || expert >= E_ || src_layer < 0 || src_layer >= L_ || src_expert < 0 ||
+        src_expert >= E_) {
+        err = "store: bad expert";
+        return false;
+    }
+    const size_t key = (size_t)layer * E_ + expert, src = (size_t)src_layer * E_ + src_expert;
+    if (key == src) return true;
+    if (!host_[src] || host_owner_[src] < 0) {
+        err = "store: the shared expert has no source yet";
+        return false;
+    }
+    if (host_owner_[key] == (int64_t)key) {   // its own buffer goes, unless other experts share it
+        for (size_t k = 0; k < host_.size(); k++)
+            if (k != key && host_owner_[k] == (int64_t)key) {
+                err = "store: the expert is the source of other experts";
+                return false;
+            }
+        cudaFreeHost(host_[key]);
+    }
+    host_[key] = host_[src];
+    host_n_[key] = host_n_[src];
+    host_owner_[key] = host_owner_[src];
+    drop_stale_slot(key);
+    return true;
+}
+
+size_t HbmStore::host_bytes() const {
+    size_t n = 0;
+    for (size_t k = 0; k < host_.size(); k++)
+        if (host_[k] && host_owner_[k] == (int64_t)k) n += host_n_[k];
+    return n;
+}
+
+std::vector<int> HbmStore::aliases_of(int layer, int expert) const {
+    std::vector<int> out;
+    const size_t key = (size_t)layer * E_ + expert;
+    for (size_t k = 0; k < host_.size(); k++)
+        if (k != key && host_owner_[k] == (int64_t)key) out.push_back((int)k);
+    return out;
+}
+
+void HbmStore::drop_stale_slot(size_t key) {
     const int si = slot_of_[key];
     if (si >= 0 && slots_[(size_t)si].refs == 0 && !slots_[(size_t)si].pinned) {
         Slot &s = slots_[(size_t)si];
@@ -107,7 +169,6 @@ bool HbmStore::set_source(int layer, int expert, const void *bytes, size_t n, st
         slot_of_[key] = -1;
         free_.push_back(si);
     }
-    return true;
 }
 
 uint8_t *HbmStore::place_resident(int layer, int expert) {

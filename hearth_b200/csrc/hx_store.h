@@ -50,6 +50,12 @@ public:
 
     // The host source of a key: the store copies the bytes into its own pinned host memory.
     bool set_source(int layer, int expert, const void *bytes, size_t n, std::string &err);
+    // An aliased expert (a container entry that names another entry's slab): its host source is the
+    // other expert's pinned copy, shared rather than copied. Its slot, counters and policy state stay
+    // its own. A later set_source of either side gives the aliases the new bytes too.
+    bool share_source(int layer, int expert, int src_layer, int src_expert, std::string &err);
+    size_t host_bytes() const;   // pinned host bytes held by the host tier
+    std::vector<int> aliases_of(int layer, int expert) const;   // experts sharing this one's source
     // Slab bytes generated directly in a slot (synthetic weights): makes the key resident.
     uint8_t *place_resident(int layer, int expert);
 
@@ -101,6 +107,7 @@ private:
     int slot_for(bool demand);
     bool issue_copy(int si, int key, bool demand);
     void settle(Slot &s);   // LOADING -> READY once its event completed
+    void drop_stale_slot(size_t key);   // a resident copy of an older source (unless in use)
     void count_use(int key, double n);
 
     int L_ = 0, E_ = 0, policy_ = POLICY_LFU;
@@ -111,6 +118,7 @@ private:
     std::vector<Slot> slots_;
     std::vector<int> slot_of_, free_;
     std::vector<uint8_t *> host_;       // pinned host copies (host tier)
+    std::vector<int64_t> host_owner_;   // key whose pinned buffer host_[key] is (-1: no source)
     std::vector<size_t> host_n_;
     std::vector<double> heat_, count_;
     std::vector<uint64_t> heat_tick_;

@@ -117,6 +117,7 @@ typedef struct hxb_moe_stats {
     int n_slots, resident, pinned;
     uint64_t slot_bytes;
     double wall_s, stall_s;
+    uint64_t host_bytes;   /* pinned host bytes of the store's host tier (shared sources counted once) */
 } hxb_moe_stats;
 
 HXB_API void hxb_moe_default_config(hxb_moe_config *c);
@@ -136,6 +137,11 @@ HXB_API int hxb_moe_set_expert(hxb_moe *m, int layer, int expert, const void *sl
  * norms and Q4/Q8 expert slabs for every layer, generated in HBM (every expert resident). */
 HXB_API int hxb_moe_synthesize(hxb_moe *m, uint64_t seed, float sigma_router, float sigma_expert);
 HXB_API size_t hxb_moe_slab_bytes(const hxb_moe *m);
+/* Expert (layer, expert) uses the slab of (src_layer, src_expert), which must already be set: the
+ * pinned host copy is shared, not duplicated (a .hearth entry with the aliased flag names another
+ * entry's slab, FORMAT §5); the expert keeps its own HBM slot and store counters. Setting either
+ * expert again later gives both the new bytes. */
+HXB_API int hxb_moe_share_expert(hxb_moe *m, int layer, int expert, int src_layer, int src_expert);
 
 /* ---- .hearth containers (docs/FORMAT.md of the reference; the reference reads them in
  * engine/src/modelfile.c and builds its model from them in hx_model_open, engine/src/model.c:1651).
@@ -160,7 +166,7 @@ HXB_API int hxb_container_probe(const char *path, hxb_moe_config *cfg, hxb_conta
 /* Loads a container's MoE weights into a handle opened with a configuration from
  * hxb_container_probe: per MoE layer hxb_moe_set_layer (moe_router, moe_router_bias, ffn_norm,
  * shexp_gate/up/down, shexp_gate_inp), then hxb_moe_set_expert for every expert this handle holds.
- * Each physical slab is read once and handed to every entry that names it. HXB_E_ARG if the handle
+ * Each physical slab is read once; the entries that name it share one pinned host copy. HXB_E_ARG if the handle
  * and the container disagree on the shape or routing, HXB_E_UNSUPPORTED for slabs that are not all
  * Q4 or all Q8 or a shexp_gate_inp that is not F32, HXB_E_FORMAT / HXB_E_IO as above. */
 HXB_API int hxb_moe_load_container(hxb_moe *m, const char *path);

@@ -23,6 +23,7 @@ def test_container_layers_equal_oracle(gpu, T, cache_slabs):
     with be:
         if cache_slabs:
             assert be.stats()["n_slots"] < 13
+        assert be.stats()["host_bytes"] == 13 * 16384   # 16 experts, 13 physical slabs: aliases share
         rng = np.random.default_rng(T)
         for _ in range(3):
             h = rng.standard_normal((T, 128)).astype(np.float32)
@@ -37,3 +38,23 @@ def test_handle_that_disagrees_with_the_container_is_refused(gpu):
     with hb.MoeBackend(**cfg, max_tokens=2) as be:
         with pytest.raises(RuntimeError, match="disagree"):
             be.load_container(FIXTURE)
+
+
+@pytest.mark.parametrize("cache_slabs", [0, 10])
+def test_setting_a_shared_slab_updates_its_aliases(gpu, cache_slabs):
+    """(2, 6) is an alias of (1, 0): new bytes for (1, 0) reach both experts (their HBM copies are
+    placed again in a resident handle, reloaded on demand in a streaming one)."""
+    layers = fixture_layers()
+    new = np.array(layers[1]["slabs"][3], copy=True)   # another expert's slab as the new bytes
+    opts = dict(max_tokens=8, cache_gb=cache_slabs * 16384 / 2**30)
+    with hb.MoeBackend.from_container(FIXTURE, **opts) as be:
+        be.set_expert(1, 0, new)
+        layers[0]["slabs"][0] = new
+        layers[1]["slabs"][6] = new
+        model = oracle_model(layers, **FIXTURE_KW)
+        rng = np.random.default_rng(11)
+        for _ in range(3):
+            h = rng.standard_normal((6, 128)).astype(np.float32)
+            got = be.forward(h, layer0=1, n_layers=2)
+            be.tick()
+            assert np.array_equal(bits(got), bits(model.forward(h)))
