@@ -1162,6 +1162,9 @@ extern "C" HXB_API int hxb_container_probe(const char *path, hxb_moe_config *cfg
     return HXB_OK;
 }
 
+// Float settings compared bit for bit: the kernels compute with exactly these values.
+static bool same_bits(float a, float b) { return std::memcmp(&a, &b, sizeof a) == 0; }
+
 extern "C" HXB_API int hxb_moe_load_container(hxb_moe *m, const char *path) {
     if (!m || !path) return fail(HXB_E_ARG, "load_container: bad arguments");
     ContainerFile f;
@@ -1179,9 +1182,11 @@ extern "C" HXB_API int hxb_moe_load_container(hxb_moe *m, const char *path) {
     else if ((int)c.expert_ffn_dim != k.expert_ffn_dim) diff = "expert_ffn_dim";
     else if ((int)c.score_fn != k.score_fn || (int)c.score_bias != k.score_bias || (int)c.n_group != k.n_group ||
              (int)c.topk_group != k.topk_group || (int)c.norm_topk_prob != k.norm_topk_prob ||
-             c.routed_scale != k.routed_scale)
+             !same_bits(c.routed_scale, k.routed_scale))
         diff = "routing";
     else if ((int)c.shared_ffn_dim != k.shared_ffn_dim || (int)c.shared_gate != k.shared_gate) diff = "shared expert";
+    else if (!same_bits(c.norm_eps, k.norm_eps)) diff = "norm_eps";
+    else if (!same_bits(c.residual_scale, k.residual_scale)) diff = "residual_scale";
     if (diff) return fail(HXB_E_ARG, "load_container: the handle and the container disagree on %s", diff);
     if (c.n_moe_layers && c.expert_dtype != k.expert_dtype)
         return fail(HXB_E_UNSUPPORTED, "load_container: slabs must all have the handle's expert dtype");

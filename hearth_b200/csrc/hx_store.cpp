@@ -86,33 +86,36 @@ bool HbmStore::set_source(int layer, int expert, const void *bytes, size_t n, st
         return false;
     }
     const size_t key = (size_t)layer * E_ + expert;
-    if (host_owner_[key] >= 0 && host_owner_[key] != (int64_t)key) {   // an alias takes its own buffer now
-        host_[key] = nullptr;
-        host_n_[key] = 0;
-        host_owner_[key] = -1;
-    }
-    if (!host_[key] || host_n_[key] != n) {
+    const bool alias = host_owner_[key] >= 0 && host_owner_[key] != (int64_t)key;
+    // every copy still reading the buffer this key reads (and, for an owner, its aliases' copies)
+    // lands before the buffer is written or freed: no slot can receive half-old, half-new bytes
+    wait_loading(key);
+    if (!alias)
+        for (size_t k = 0; k < host_.size(); k++)
+            if (k != key && host_owner_[k] == (int64_t)key) wait_loading(k);
+    if (alias || !host_[key] || host_n_[key] != n) {
         uint8_t *p = nullptr;
         if (cudaHostAlloc((void **)&p, n, cudaHostAllocDefault) != cudaSuccess) {
             cudaGetLastError();
-            err = "store: cannot pin host memory for an expert";
+            err = "store: cannot pin host memory for an expert";   // an alias keeps its shared source
             return false;
         }
-        uint8_t *old = host_[key];
+        uint8_t *old = alias ? nullptr : host_[key];   // an alias detaches; the owner keeps its buffer
         host_[key] = p;
         host_n_[key] = n;
         host_owner_[key] = (int64_t)key;
-        for (size_t k = 0; k < host_.size(); k++)   // the aliases of this key follow its new buffer
-            if (k != key && host_owner_[k] == (int64_t)key) {
-                host_[k] = p;
-                host_n_[k] = n;
-            }
+        if (!alias)
+            for (size_t k = 0; k < host_.size(); k++)   // the aliases of this key follow its new buffer
+                if (k != key && host_owner_[k] == (int64_t)key) {
+                    host_[k] = p;
+                    host_n_[k] = n;
+                }
         if (old) cudaFreeHost(old);
     }
     std::memcpy(host_[key], bytes, n);
-    drop_stale_slot(key);
+    refresh_slot(key);
     for (size_t k = 0; k < host_.size(); k++)
-        if (k != key && host_owner_[k] == (int64_t)key) drop_stale_slot(k);
+        if (k != key && host_owner_[k] == (int64_t)key) refresh_slot(k);
     return true;
 }
 
@@ -134,12 +137,13 @@ bool HbmStore::share_source(int layer, int expert, int src_layer, int src_expert
                 err = "store: the expert is the source of other experts";
                 return false;
             }
+        wait_loading(key);   // a copy from the buffer lands before the buffer is freed
         cudaFreeHost(host_[key]);
     }
     host_[key] = host_[src];
     host_n_[key] = host_n_[src];
     host_owner_[key] = host_owner_[src];
-    drop_stale_slot(key);
+    refresh_slot(key);
     return true;
 }
 
@@ -158,16 +162,32 @@ std::vector<int> HbmStore::aliases_of(int layer, int expert) const {
     return out;
 }
 
-void HbmStore::drop_stale_slot(size_t key) {
+void HbmStore::wait_loading(size_t key) {
     const int si = slot_of_[key];
-    if (si >= 0 && slots_[(size_t)si].refs == 0 && !slots_[(size_t)si].pinned) {
-        Slot &s = slots_[(size_t)si];
+    if (si >= 0 && slots_[(size_t)si].state == LOADING) cudaEventSynchronize(slots_[(size_t)si].ready);
+}
+
+void HbmStore::refresh_slot(size_t key) {
+    const int si = slot_of_[key];
+    if (si < 0) return;
+    Slot &s = slots_[(size_t)si];
+    if (s.state == LOADING) {
+        cudaEventSynchronize(s.ready);
+        settle(s);
+    }
+    if (s.refs == 0 && !s.pinned) {   // a resident copy of the older bytes is dropped
         if (s.state == READY) n_ready_--;
-        if (s.state == LOADING) cudaEventSynchronize(s.ready);
         s.key = -1;
         s.state = FREE;
         slot_of_[key] = -1;
         free_.push_back(si);
+        return;
+    }
+    // a pinned slot keeps its place and receives the new bytes (after the compute that last read it)
+    if (s.done) cudaEventSynchronize(s.done);
+    if (cudaMemcpy(slot_ptr(si), host_[key], host_n_[key], cudaMemcpyHostToDevice) != cudaSuccess) {
+        cudaGetLastError();
+        st_.copy_errors++;
     }
 }
 

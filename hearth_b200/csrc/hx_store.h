@@ -107,7 +107,8 @@ private:
     int slot_for(bool demand);
     bool issue_copy(int si, int key, bool demand);
     void settle(Slot &s);   // LOADING -> READY once its event completed
-    void drop_stale_slot(size_t key);   // a resident copy of an older source (unless in use)
+    void wait_loading(size_t key);      // the key's copy in flight (if any) has landed
+    void refresh_slot(size_t key);      // after new source bytes: drop the key's slot, or re-copy a pinned one
     void count_use(int key, double n);
 
     int L_ = 0, E_ = 0, policy_ = POLICY_LFU;

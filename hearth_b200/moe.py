@@ -133,6 +133,11 @@ class MoeBackend:
         slab = np.ascontiguousarray(slab, np.uint8)
         check(lib().hxb_moe_set_expert(self.h, layer, expert, _ptr(slab), slab.nbytes), "hxb_moe_set_expert")
 
+    def share_expert(self, layer: int, expert: int, src_layer: int, src_expert: int) -> None:
+        """(layer, expert) uses the pinned host copy of (src_layer, src_expert)'s slab (an aliased
+        container entry); it keeps its own HBM slot and counters."""
+        check(lib().hxb_moe_share_expert(self.h, layer, expert, src_layer, src_expert), "hxb_moe_share_expert")
+
     def synthesize(self, seed: int = 0, sigma_router: float = 0.02, sigma_expert: float = 0.02) -> None:
         check(lib().hxb_moe_synthesize(self.h, seed, sigma_router, sigma_expert), "hxb_moe_synthesize")
 

@@ -2,7 +2,10 @@
  * hearth_b200.h — C ABI of the B200 (sm_100a) backend for Hearth's quantized MoE expert path.
  *
  * Plain C types only (pointers, sizes, ints); no CUDA or torch types. Device pointers are
- * passed as void* / float*, CUDA streams as void* (NULL = the library's own stream).
+ * passed as void* / float*, CUDA streams as void* (cudaStream_t). A NULL stream means, for the
+ * hxb_moe_* calls on a handle, the handle's own non-blocking stream; for the handle-less
+ * device-pointer calls (hxb_act_quantize_dev, hxb_matmul_dev, hxb_dequantize_dev, hxb_expf_dev,
+ * hxb_matmul_noalloc), which have no stream of their own, CUDA's legacy default stream.
  *
  * The entry points replace these reference interfaces (pierce-lonergan/hearth):
  *   hxb_matmul          hearth_matmul       engine/include/hearth.h:157-158, engine/src/quant.c:574-600
@@ -76,7 +79,9 @@ HXB_API int hxb_expf_dev(uint32_t x0, int64_t n, float *out, void *stream);
  * (T * n_cols / 64 * 72 bytes at most, else HXB_E_CAPACITY with a message), held by every GPU
  * that loads the library until exit. The first call on a device looks up that array's address,
  * so make it before any stream capture. All calls share the array: calls that overlap on the
- * GPU race and must be serialised by the caller. Results equal hxb_matmul's bit for bit. */
+ * GPU race and must be serialised by the caller. Results equal hxb_matmul's bit for bit. The
+ * work is enqueued on `stream` (NULL: the legacy default stream) and the call returns without
+ * waiting for it. */
 #define HXB_NOALLOC_SCRATCH_BYTES ((size_t)4 << 20)
 HXB_API int hxb_matmul_noalloc(int dtype, const void *W, int64_t n_rows, int64_t n_cols, const float *X, int T,
                                float *Y, void *stream);

@@ -26,9 +26,23 @@ _ref = None
 _moe_ref = None
 
 
+def reference_tree():
+    """The reference checkout to compile _ref/ from: $HEARTH_REF, else a checkout named `reference`
+    beside this repository; None when neither holds the engine sources (e.g. on a GPU box, which only
+    uses the prebuilt _ref/)."""
+    for cand in (os.environ.get("HEARTH_REF"), os.path.join(os.path.dirname(os.path.dirname(HERE)), "reference")):
+        if cand and os.path.isdir(os.path.join(cand, "engine", "src")):
+            return cand
+    return None
+
+
 def build(quiet: bool = True) -> None:
-    """Build liboracle.so and, where the reference tree exists, _ref/ (make -C oracle)."""
-    out = subprocess.run(["make", "-C", HERE, "-j8"], capture_output=True, text=True)
+    """Build liboracle.so and, where the reference tree exists, _ref/ (make -C oracle REF=...)."""
+    cmd = ["make", "-C", HERE, "-j8"]
+    ref = reference_tree()
+    if ref:
+        cmd.append(f"REF={ref}")
+    out = subprocess.run(cmd, capture_output=True, text=True)
     if out.returncode != 0:
         raise RuntimeError("oracle build failed:\n" + out.stdout + out.stderr)
 
@@ -93,7 +107,7 @@ def ref_lib():
     if _ref is None:
         path = os.path.join(HERE, "_ref", "libhearth_ref.so")
         if not os.path.exists(path):
-            if os.path.isdir("/root/reference/engine/src"):
+            if reference_tree():
                 build()
             if not os.path.exists(path):
                 return None
@@ -116,7 +130,7 @@ def moe_ref_lib():
     if _moe_ref is None:
         path = os.path.join(HERE, "_ref", "libmoe_ref.so")
         if not os.path.exists(path):
-            if os.path.isdir("/root/reference/engine/src"):
+            if reference_tree():
                 build()
             if not os.path.exists(path):
                 return None
@@ -272,10 +286,11 @@ class MoeModel:
             raise ValueError(f"orc_moe_layer_eval returned {rc}")
         return out, ids, w
 
-    def forward(self, h: np.ndarray):
+    def forward(self, h: np.ndarray, layer0: int = 0, n_layers: int | None = None):
         h = np.array(h, np.float32, copy=True, order="C")
         arr = self.c_layers()
-        rc = lib().orc_moe_forward(arr, len(self.layers), _p(h), h.shape[0])
+        n = len(self.layers) - layer0 if n_layers is None else n_layers
+        rc = lib().orc_moe_forward(C.byref(arr[layer0]), n, _p(h), h.shape[0])
         if rc:
             raise ValueError(f"orc_moe_forward returned {rc}")
         return h

@@ -31,8 +31,11 @@ META = dict(arch="synthetic", n_layers=3, d_model=D, vocab_size=V, n_heads=H, n_
 
 def main():
     ap = argparse.ArgumentParser()
-    ap.add_argument("--ref", default=os.environ.get("HEARTH_REF", "/root/reference"))
+    ap.add_argument("--ref", default=os.environ.get("HEARTH_REF"),
+                    help="the reference checkout (default: $HEARTH_REF)")
     args = ap.parse_args()
+    if not args.ref:
+        ap.error("name the reference checkout with --ref or HEARTH_REF")
     sys.path.insert(0, os.path.join(args.ref, "python"))
     sys.path.insert(0, REPO)
     # the reference's Python quantizer runs its own C kernels: oracle/_ref holds them, compiled from the

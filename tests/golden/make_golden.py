@@ -183,8 +183,11 @@ def moe_layers(Reference, _Mat, quant):
 
 def main():
     ap = argparse.ArgumentParser()
-    ap.add_argument("--ref", default="/root/reference")
+    ap.add_argument("--ref", default=os.environ.get("HEARTH_REF"),
+                    help="the reference checkout (default: $HEARTH_REF)")
     a = ap.parse_args()
+    if not a.ref:
+        ap.error("name the reference checkout with --ref or HEARTH_REF")
     sys.path.insert(0, os.path.join(a.ref, "python"))
     from hearth.reference import Reference, _Mat  # noqa: E402
     from hearth import quant  # noqa: E402

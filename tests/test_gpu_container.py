@@ -32,9 +32,14 @@ def test_container_layers_equal_oracle(gpu, T, cache_slabs):
             assert np.array_equal(bits(got), bits(model.forward(h)))
 
 
-def test_handle_that_disagrees_with_the_container_is_refused(gpu):
+@pytest.mark.parametrize("field,value", [("top_k", 3), ("norm_eps", 1e-5), ("residual_scale", 1.0),
+                                         ("routed_scale", 2.5000002)])
+def test_handle_that_disagrees_with_the_container_is_refused(gpu, field, value):
+    """Every setting the kernels compute with must equal the container's (floats bit for bit): a
+    handle with another epsilon or residual scale would give results the reference does not."""
     cfg, _ = hb.container_probe(FIXTURE)
-    cfg["top_k"] = 3
+    assert np.float32(cfg[field]) != np.float32(value)
+    cfg[field] = value
     with hb.MoeBackend(**cfg, max_tokens=2) as be:
         with pytest.raises(RuntimeError, match="disagree"):
             be.load_container(FIXTURE)
@@ -58,3 +63,20 @@ def test_setting_a_shared_slab_updates_its_aliases(gpu, cache_slabs):
             got = be.forward(h, layer0=1, n_layers=2)
             be.tick()
             assert np.array_equal(bits(got), bits(model.forward(h)))
+
+
+def test_new_bytes_for_a_shared_slab_during_a_prefetch_of_an_alias(gpu):
+    """A prefetch copy of an alias (2, 6) reads the pinned buffer it shares with (1, 0); setting new
+    bytes for (1, 0) while that copy may still be in flight waits for it first, so neither expert's
+    HBM copy can mix old and new bytes: both then compute with the new slab."""
+    layers = fixture_layers()
+    new = np.array(layers[1]["slabs"][5], copy=True)
+    with hb.MoeBackend.from_container(FIXTURE, max_tokens=8, cache_gb=10 * 16384 / 2**30) as be:
+        for _ in range(4):
+            be.prefetch(2, [6, 0, 1])   # layer index 2 of the handle = MoE layer 1 of the oracle list
+            be.set_expert(1, 0, new)
+        layers[0]["slabs"][0] = new
+        layers[1]["slabs"][6] = new
+        model = oracle_model(layers, **FIXTURE_KW)
+        h = np.random.default_rng(12).standard_normal((4, 128)).astype(np.float32)
+        assert np.array_equal(bits(be.forward(h, layer0=1, n_layers=2)), bits(model.forward(h)))

@@ -3,8 +3,9 @@
 application that budgets device memory once at start). Its Q8/Q4 activation scratch is a static
 device array, so the test checks it against the allocating entry point hxb_matmul, bit for bit
 (the tolerance of every matmul parity test here), on two calls in a row — the second call finds
-the first call's leftovers in the shared array. This file is collected last on purpose: it loads
-no state from the other tests and passes alone in a fresh process as well as after them."""
+the first call's leftovers in the shared array — and against the oracle (the CPU restatement of the
+reference's matmul). This file is collected last on purpose: it loads no state from the other tests
+and passes alone in a fresh process as well as after them."""
 import ctypes as C
 
 import numpy as np
@@ -39,6 +40,7 @@ def test_noalloc_matmul_equals_hxb_matmul_on_two_calls(gpu):
             W = _weights(rng, dt, rows, cols)
             X = rng.standard_normal((T, cols)).astype(np.float32)
             want = native.matmul(dt, W, rows, cols, X)                 # allocating entry point
+            assert np.array_equal(want.view(np.uint32), O.matmul(dt, W, rows, cols, X).view(np.uint32))
             Wd = torch.from_numpy(np.ascontiguousarray(W)).cuda()
             Xd = torch.from_numpy(X).cuda()
             Yd = torch.full((T, rows), float("nan"), dtype=torch.float32, device="cuda")
