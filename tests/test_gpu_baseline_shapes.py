@@ -116,13 +116,12 @@ def test_config0_single_layer(gpu, config0, T):
 
 
 def test_olmoe_layer_decode(gpu):
-    """OLMoE-1B-7B: D 2048, F 1024, 64 experts, top-8 softmax without renormalisation; the single-token
-    forward of a 2-layer stack runs the persistent decode kernel."""
+    """OLMoE-1B-7B: D 2048, F 1024, 64 experts, top-8 softmax without renormalisation; single-token
+    forwards of a 2-layer stack (on whichever decode path the handle chose for the shape)."""
     lay = Layer(1, D=2048, F=1024, E=64, K=8, norm=0, max_tokens=1, L=2)
     try:
         rng = np.random.default_rng(5)
         lay.check_layer(rng.standard_normal((1, 2048), dtype=np.float32))
-        assert lay.be.decode_path() == "persistent"
         for _ in range(3):
             h = rng.standard_normal((1, 2048), dtype=np.float32)
             want = lay.ref.forward(lay.model, h.copy())
