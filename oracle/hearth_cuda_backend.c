@@ -1,0 +1,136 @@
+/*
+ * hearth_cuda_backend.c — the reference-side binding of the B200 MoE backend: what a maintainer of
+ * the reference engine adds so that its public C API (engine/include/hearth.h, hearth_open /
+ * hearth_eval) evaluates the MoE half of every layer on the GPU, and the Python toolkit that binds
+ * that API (python/hearth/_native.py, engine.py) drives the GPU unchanged.
+ *
+ * It is compiled as part of the reference's engine/src/model.c: oracle/Makefile makes a build copy
+ * of model.c with three anchored edits (the copy lives under oracle/_ref/, nothing is committed):
+ *   1. `#include "hearth_cuda_backend.c"` just before forward() (after moe_layer(), model.c:986);
+ *   2. forward()'s `rc = moe_layer(m, w, l, T, pos0);` (model.c:1204) becomes hxc_moe_layer(...);
+ *   3. hx_model_close() (model.c:1638) first calls hxc_close(m).
+ *
+ * Selection: the environment variable HEARTH_BACKEND=cuda, read when a model's first MoE layer is
+ * evaluated (the same place the reference reads its other environment overrides is api.c:118-128;
+ * reading it lazily keeps hearth_open and its options untouched). Then the MoE layer of forward() —
+ * x = rmsnorm(h, ffn_norm), router, routing, experts, rank-order sum, h += residual_scale * sum
+ * (model.c:1209-1214 with moe_layer) — runs as hxb_moe_forward on the handle's GPU, bit-identical to
+ * moe_layer (the backend's parity tests), while attention, the dense layers and the LM head stay on
+ * the CPU. There is no CPU fallback: when the backend was asked for and cannot be opened (no device,
+ * a container it cannot take) every evaluation fails with HX_E_IO, and the log says why.
+ *   HEARTH_CUDA_DEVICE   CUDA device ordinal (default 0)
+ *   HEARTH_CUDA_CACHE_GB HBM budget for expert slots in GiB (default 0: every expert resident)
+ * Routing trace rows (hearth_trace_start, docs/FORMAT.md §9) are filled from the GPU routing.
+ * Route replay (hearth_route_replay) is refused with the backend: the GPU routes for itself.
+ */
+#include "hearth_b200.h"
+
+#include <pthread.h>
+#include <stdlib.h>
+#include <string.h>
+
+#define HXC_MAX_MODELS 64
+enum { HXC_UNSET = 0, HXC_CUDA = 1, HXC_CPU = 2, HXC_FAILED = -1 };
+
+typedef struct hxc_slot {
+    hx_model *m;
+    hxb_moe *b;
+    int state;
+} hxc_slot;
+
+static hxc_slot hxc_slots[HXC_MAX_MODELS];
+static pthread_mutex_t hxc_mu = PTHREAD_MUTEX_INITIALIZER;
+
+static hxc_slot *hxc_slot_of(hx_model *m, int create) {
+    hxc_slot *s = NULL;
+    pthread_mutex_lock(&hxc_mu);
+    for (int i = 0; i < HXC_MAX_MODELS && !s; i++)
+        if (hxc_slots[i].m == m) s = &hxc_slots[i];
+    for (int i = 0; i < HXC_MAX_MODELS && !s && create; i++)
+        if (!hxc_slots[i].m) {
+            s = &hxc_slots[i];
+            s->m = m;
+            s->b = NULL;
+            s->state = HXC_UNSET;
+        }
+    pthread_mutex_unlock(&hxc_mu);
+    return s;
+}
+
+/* Opens the backend handle of model m from its own container: the container's MoE shape and
+ * routing, every MoE layer's router / bias / norm / shared expert and every expert slab. */
+static int hxc_open(hxc_slot *s, hx_model *m) {
+    hxb_moe_config cfg;
+    hxb_container_info info;
+    char err[512];
+    const char *dev = getenv("HEARTH_CUDA_DEVICE"), *gb = getenv("HEARTH_CUDA_CACHE_GB");
+    if (hxb_container_probe(m->mf->path, &cfg, &info, err, sizeof err) != HXB_OK) {
+        hx_log(HX_LOG_ERROR, "cuda backend: %s", err);
+        return HX_E_IO;
+    }
+    cfg.max_tokens = m->max_batch;
+    cfg.device = dev && *dev ? atoi(dev) : 0;
+    cfg.cache_gb = gb && *gb ? atof(gb) : 0.0;
+    s->b = hxb_moe_open(&cfg, err, sizeof err);
+    if (!s->b) {
+        hx_log(HX_LOG_ERROR, "cuda backend: %s", err);
+        return HX_E_IO;
+    }
+    if (hxb_moe_load_container(s->b, m->mf->path) != HXB_OK) {
+        hx_log(HX_LOG_ERROR, "cuda backend: %s", hxb_last_error());
+        hxb_moe_close(s->b);
+        s->b = NULL;
+        return HX_E_IO;
+    }
+    hx_log(HX_LOG_INFO, "cuda backend: MoE layers of %s on device %d (%s)", m->mf->path, cfg.device,
+           hxb_moe_decode_path(s->b) ? "persistent decode kernel" : "per-phase kernels");
+    return HX_OK;
+}
+
+/* forward()'s MoE layer: on the GPU when HEARTH_BACKEND=cuda, else the reference's moe_layer. */
+static int hxc_moe_layer(hx_model *m, const layer_w *w, int l, int T, int pos0) {
+    hxc_slot *s = hxc_slot_of(m, 1);
+    if (!s) {
+        hx_log(HX_LOG_ERROR, "cuda backend: more than %d open models", HXC_MAX_MODELS);
+        return HX_E_NOMEM;
+    }
+    if (s->state == HXC_UNSET) {
+        const char *b = getenv("HEARTH_BACKEND");
+        if (b && strcmp(b, "cuda") == 0) s->state = hxc_open(s, m) == HX_OK ? HXC_CUDA : HXC_FAILED;
+        else s->state = HXC_CPU;
+    }
+    if (s->state == HXC_CPU) return moe_layer(m, w, l, T, pos0);
+    if (s->state != HXC_CUDA) return HX_E_IO;
+    if (m->replay) {
+        hx_log(HX_LOG_ERROR, "cuda backend: route replay is not available (the GPU routes for itself)");
+        return HX_E_ARG;
+    }
+    const int rc = hxb_moe_forward(s->b, m->h, T, l, 1);   /* leaves m->h untouched on failure */
+    if (rc != HXB_OK) {
+        hx_log(HX_LOG_ERROR, "cuda backend: layer %d: %s", l, hxb_last_error());
+        return rc == HXB_E_CAPACITY ? HX_E_CAPACITY : rc == HXB_E_NOMEM ? HX_E_NOMEM : HX_E_IO;
+    }
+    /* routing of this layer into the per-token trace rows (model.c moe_layer, routes[]) */
+    const int K = m->K, mi = m->moe_index[l];
+    if (hxb_moe_last_routing(s->b, m->ids, m->wts, T) == HXB_OK)
+        for (int i = 0; i < T; i++)
+            for (int j = 0; j < K; j++)
+                m->routes[(size_t)i * (m->n_moe * K) + (size_t)mi * K + j] = (uint16_t)m->ids[(size_t)i * K + j];
+    m->st.expert_uses += (uint64_t)T * (uint64_t)K;
+    (void)w;
+    (void)pos0;
+    return HX_OK;
+}
+
+/* hx_model_close(): the backend handle goes with its model. */
+static void hxc_close(hx_model *m) {
+    if (!m) return;
+    hxc_slot *s = hxc_slot_of(m, 0);
+    if (!s) return;
+    if (s->b) hxb_moe_close(s->b);
+    pthread_mutex_lock(&hxc_mu);
+    s->b = NULL;
+    s->state = HXC_UNSET;
+    s->m = NULL;
+    pthread_mutex_unlock(&hxc_mu);
+}

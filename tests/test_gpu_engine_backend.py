@@ -1,0 +1,43 @@
+"""End to end through the reference engine's own public API with the B200 binding: the same container
+and tokens evaluated by the reference engine on the CPU and by the engine built with
+oracle/hearth_cuda_backend.c with HEARTH_BACKEND=cuda (MoE layers on the GPU; attention, the dense
+layer and the LM head on the CPU) give bit-identical logits for every prompt and decode position and
+byte-identical routing traces (docs/FORMAT.md §9 files written by hearth_trace_start): the MoE
+schedule on the GPU is the reference engine's own moe_layer, pinned by the engine itself rather
+than by a restatement. Also with an expert cache smaller than the container (HEARTH_CUDA_CACHE_GB),
+and with the prompt split into several forward calls (max_batch)."""
+import os
+
+import numpy as np
+import pytest
+
+from tests.engine_util import CUDA_LIB, REF_LIB, Engine, session
+
+pytestmark = pytest.mark.gpu
+
+PROMPT = [3, 1, 4, 1, 5, 9, 2, 6, 5, 3, 5, 8, 9, 7, 9, 3]
+
+
+@pytest.mark.parametrize("cache_gb,max_batch", [(None, 0), ("0.0001", 0), (None, 5)])
+def test_gpu_moe_layers_give_the_reference_engines_logits_and_trace(gpu, monkeypatch, tmp_path, cache_gb, max_batch):
+    monkeypatch.delenv("HEARTH_BACKEND", raising=False)
+    with Engine(REF_LIB, max_batch=max_batch) as cpu:
+        want = session(cpu, PROMPT, 8, str(tmp_path / "cpu.trace"))
+    monkeypatch.setenv("HEARTH_BACKEND", "cuda")
+    if cache_gb:
+        monkeypatch.setenv("HEARTH_CUDA_CACHE_GB", cache_gb)   # the store's minimum: E + 2 slots, streaming
+    with Engine(CUDA_LIB, max_batch=max_batch) as gpu_engine:
+        got = session(gpu_engine, PROMPT, 8, str(tmp_path / "gpu.trace"))
+    assert np.isfinite(want).all()
+    assert np.array_equal(got.view(np.uint32), want.view(np.uint32))
+    a = open(tmp_path / "cpu.trace", "rb").read()
+    b = open(tmp_path / "gpu.trace", "rb").read()
+    assert len(a) > 0 and a == b
+
+
+def test_gpu_backend_on_a_device_that_does_not_exist_fails(gpu, monkeypatch):
+    monkeypatch.setenv("HEARTH_BACKEND", "cuda")
+    monkeypatch.setenv("HEARTH_CUDA_DEVICE", "97")
+    with Engine(CUDA_LIB) as e:
+        rc, _ = e.eval(PROMPT)
+    assert rc == -4
