@@ -231,6 +231,10 @@ struct hxb_moe {
     // scratch
     DevBuf x, xact, logits, sh_logit, ids, wts, nu, ulist, u_p0, u_n, pair_tok, pair_of, act_mid, Y, S, ticket, err;
     DevBuf hbuf, obuf;                   // device copies of host inputs/outputs
+    DevBuf forced;                       // route replay: [n_layers][max_tokens][K] expert ids
+    // streaming store, next-layer prediction: the routing stages' own outputs for layer l+1
+    DevBuf px, pxact, plogits, psh_logit, pids, pwts, pnu, pulist, pu_p0, pu_n, ppair_tok, ppair_of, pticket;
+    cudaEvent_t pred_ready = nullptr;
     float *hpin = nullptr;               // pinned staging [max_tokens, D]
     int *epin = nullptr;                 // pinned: error word, nu, ulist
     std::map<GraphKey, cudaGraphExec_t> graphs;
@@ -264,6 +268,25 @@ struct hxb_moe {
         s.nu_job = nu_job.as<int>();
         s.ticket = ticket.as<unsigned>();
         s.err = err.as<int>();
+        return s;
+    }
+
+    // The scratch of a prediction: the routing stages write only into their own buffers.
+    MoeScratch pred_scratch() const {
+        MoeScratch s = scratch();
+        s.x = px.as<float>();
+        s.xact = pxact.as<act_q8>();
+        s.logits = plogits.as<float>();
+        s.sh_logit = psh_logit.as<float>();
+        s.ids = pids.as<int>();
+        s.wts = pwts.as<float>();
+        s.nu = pnu.as<int>();
+        s.ulist = pulist.as<int>();
+        s.u_p0 = pu_p0.as<int>();
+        s.u_n = pu_n.as<int>();
+        s.pair_tok = ppair_tok.as<int>();
+        s.pair_of = ppair_of.as<int>();
+        s.ticket = pticket.as<unsigned>();
         return s;
     }
 
@@ -349,6 +372,7 @@ struct hxb_moe {
         if (hpin) cudaFreeHost(hpin);
         if (epin) cudaFreeHost(epin);
         if (host_table) cudaFreeHost(host_table);
+        if (pred_ready) cudaEventDestroy(pred_ready);
         store.close();
         if (stream) cudaStreamDestroy(stream);
     }
@@ -363,6 +387,7 @@ extern "C" HXB_API void hxb_moe_default_config(hxb_moe_config *c) {
     c->topk_group = 1;
     c->norm_topk_prob = 1;
     c->routed_scale = 1.0f;
+    c->prefetch_next = 1;
     c->residual_scale = 1.0f;
     c->norm_eps = 1e-6f;
     c->expert_dtype = Q4;
@@ -448,9 +473,18 @@ extern "C" HXB_API hxb_moe *hxb_moe_open(const hxb_moe_config *c, char *err, siz
                                                                                           : 16) &&
               m->ujob.alloc(sizeof(int) * (size_t)E) && m->nu_job.alloc(sizeof(int) * 4) &&
               m->ticket.alloc(64) && m->err.alloc(64) && m->hbuf.alloc(sizeof(float) * (size_t)T * D) &&
+              m->forced.alloc(sizeof(int) * P * (size_t)L) &&
               m->obuf.alloc(sizeof(float) * (size_t)T * D);
+    if (ok && !m->resident_mode && k.prefetch_next)   // the prediction's own routing buffers
+        ok = m->px.alloc(sizeof(float) * (size_t)T * D) && m->pxact.alloc((size_t)T * (D / QK) * ACT_BLOCK) &&
+             m->plogits.alloc(sizeof(float) * (size_t)T * E) && m->psh_logit.alloc(sizeof(float) * (size_t)T) &&
+             m->pids.alloc(sizeof(int) * P) && m->pwts.alloc(sizeof(float) * P) && m->pnu.alloc(sizeof(int) * 4) &&
+             m->pulist.alloc(sizeof(int) * E) && m->pu_p0.alloc(sizeof(int) * E) && m->pu_n.alloc(sizeof(int) * E) &&
+             m->ppair_tok.alloc(sizeof(int) * P) && m->ppair_of.alloc(sizeof(int) * P) && m->pticket.alloc(64) &&
+             cudaMemset(m->pticket.p, 0, 64) == cudaSuccess &&
+             cudaEventCreateWithFlags(&m->pred_ready, cudaEventDisableTiming) == cudaSuccess;
     ok = ok && cudaHostAlloc((void **)&m->hpin, sizeof(float) * (size_t)T * D, cudaHostAllocDefault) == cudaSuccess;
-    ok = ok && cudaHostAlloc((void **)&m->epin, sizeof(int) * (size_t)(8 + 2 * E), cudaHostAllocDefault) == cudaSuccess;
+    ok = ok && cudaHostAlloc((void **)&m->epin, sizeof(int) * (size_t)(9 + 3 * E), cudaHostAllocDefault) == cudaSuccess;
     ok = ok && cudaHostAlloc((void **)&m->host_table, sizeof(void *) * (size_t)nkeys, cudaHostAllocDefault) ==
                    cudaSuccess;
     if (!ok) {
@@ -686,12 +720,13 @@ static int enqueue_resident(hxb_moe *m, float *h, float *out, int T, int l0, int
 // Experts may be missing from HBM: route on the device, read the bucket list back, acquire the
 // experts from the store (copies on its copy stream, waited for on the device), then run them.
 static int run_streaming(hxb_moe *m, float *h, float *out, int T, int l0, int nl, bool with_norm, bool resid,
-                         cudaStream_t s) {
-    const MoeScratch sc = m->scratch();
+                         cudaStream_t s, const int *forced = nullptr) {
+    MoeScratch sc = m->scratch();
     const MoeShape sh = m->shape(T);
     const int E = m->cfg.n_experts;
     for (int l = l0; l < l0 + nl; l++) {
         const MoeLayerDev L = m->layer_dev(l, with_norm);
+        sc.forced_ids = forced ? forced + (size_t)(l - l0) * T * m->cfg.top_k : nullptr;
         if (!cuda_ok(launch_moe_route(sh, L, sc, h, s), "route")) return HXB_E_DEVICE;
         int *nu_h = m->epin + 1, *ul_h = m->epin + 8, *un_h = m->epin + 8 + E;
         bool ok = cuda_ok(cudaMemcpyAsync(nu_h, sc.nu, sizeof(int), cudaMemcpyDeviceToHost, s), "nu") &&
@@ -728,7 +763,25 @@ static int run_streaming(hxb_moe *m, float *h, float *out, int T, int l0, int nl
                                      sizeof(void *) * (size_t)E, cudaMemcpyHostToDevice, s),
                      "table"))
             rc = HXB_E_DEVICE;
+        // next-layer prediction (engine/src/model.c:944-973, HEARTH_PREFETCH_NEXT): route layer l+1 with
+        // this layer's input h (before this layer's residual) and hand its experts to the store as
+        // prefetch hints; their copies follow this layer's demand copies on the copy stream
+        const bool predict = rc == HXB_OK && m->pred_ready && !forced && l + 1 < l0 + nl && m->layers[(size_t)l + 1].set;
+        int *pnu_h = m->epin + 8 + 2 * E + 0, *pul_h = m->epin + 8 + 2 * E + 1;
+        if (predict) {
+            const MoeScratch ps = m->pred_scratch();
+            if (!cuda_ok(launch_moe_route(sh, m->layer_dev(l + 1, with_norm), ps, h, s), "predict") ||
+                !cuda_ok(cudaMemcpyAsync(pnu_h, ps.nu, sizeof(int), cudaMemcpyDeviceToHost, s), "predicted nu") ||
+                !cuda_ok(cudaMemcpyAsync(pul_h, ps.ulist, sizeof(int) * (size_t)E, cudaMemcpyDeviceToHost, s),
+                         "predicted experts") ||
+                !cuda_ok(cudaEventRecord(m->pred_ready, s), "predict event"))
+                rc = HXB_E_DEVICE;
+        }
         if (rc == HXB_OK && !cuda_ok(launch_moe_experts(sh, L, sc, h, out, resid, s), "experts")) rc = HXB_E_DEVICE;
+        if (rc == HXB_OK && predict) {   // the experts run meanwhile; the hints go out as soon as they are known
+            if (!cuda_ok(cudaEventSynchronize(m->pred_ready), "predict wait")) rc = HXB_E_DEVICE;
+            else m->store.prefetch(l + 1, pul_h, std::min(*pnu_h, E));
+        }
         for (int e : got) m->store.release(l, e, s);
         if (rc != HXB_OK) {
             cudaStreamSynchronize(s);   // nothing of this call may still run when it returns
@@ -906,6 +959,53 @@ extern "C" HXB_API int hxb_moe_forward_dev(hxb_moe *m, float *h, int T, int laye
     if (rc) return rc;
     if (!h) return fail(HXB_E_ARG, "null h");
     return run_range(m, h, nullptr, T, layer0, n_layers, true, true, (cudaStream_t)stream, false, nullptr, nullptr);
+}
+
+// Route replay (hearth_route_replay, engine/src/model.c:1003-1009 and 1885-1959): the layers of
+// [layer0, layer0 + n_layers) with every token's K expert ids given (ids [n_layers][T][K], host), the
+// scores and weights computed as usual. Synchronous, host h in place; never the persistent kernel.
+extern "C" HXB_API int hxb_moe_forward_routed(hxb_moe *m, float *h, int T, int layer0, int n_layers, const int *ids) {
+    int rc = check_eval(m, T, layer0, n_layers);
+    if (rc) return rc;
+    if (!h || !ids) return fail(HXB_E_ARG, "forward_routed: null h or ids");
+    if (m->cfg.ep_size > 1) return fail(HXB_E_UNSUPPORTED, "forward_routed: not on an expert-parallel handle");
+    const int K = m->cfg.top_k, E = m->cfg.n_experts;
+    const size_t n = (size_t)n_layers * T * K;
+    for (size_t i = 0; i < n; i++)
+        if (ids[i] < 0 || ids[i] >= E) return fail(HXB_E_ARG, "forward_routed: expert id %d outside [0, %d)", ids[i], E);
+    cudaStream_t s = m->stream;
+    const size_t bytes = sizeof(float) * (size_t)T * m->cfg.d_model;
+    const double t0 = now_s();
+    float *dh = m->hbuf.as<float>();
+    std::memcpy(m->hpin, h, bytes);
+    if (!cuda_ok(cudaMemcpyAsync(dh, m->hpin, bytes, cudaMemcpyHostToDevice, s), "h in") ||
+        !cuda_ok(cudaMemcpyAsync(m->forced.p, ids, sizeof(int) * n, cudaMemcpyHostToDevice, s), "ids in"))
+        return HXB_E_DEVICE;
+    const int *fd = m->forced.as<int>();
+    if (m->resident_mode) {
+        MoeScratch sc = m->scratch();
+        for (int l = layer0; l < layer0 + n_layers; l++) {
+            sc.forced_ids = fd + (size_t)(l - layer0) * T * K;
+            if (!cuda_ok(launch_moe_layer(m->shape(T), m->layer_dev(l, true), sc, dh, nullptr, true, s), "layer"))
+                return HXB_E_DEVICE;
+        }
+    } else {
+        rc = run_streaming(m, dh, nullptr, T, layer0, n_layers, true, true, s, fd);
+        if (rc != HXB_OK) return rc;
+    }
+    if (!cuda_ok(cudaMemcpyAsync(m->hpin, dh, bytes, cudaMemcpyDeviceToHost, s), "h out") ||
+        !cuda_ok(cudaMemcpyAsync(m->epin, m->err.p, sizeof(int), cudaMemcpyDeviceToHost, s), "err") ||
+        !cuda_ok(cudaStreamSynchronize(s), "sync"))
+        return HXB_E_DEVICE;
+    rc = take_device_error(m, m->epin[0]);
+    if (rc != HXB_OK) return rc;
+    std::memcpy(h, m->hpin, bytes);
+    m->st.tokens += (uint64_t)T;
+    m->st.forward_calls++;
+    m->st.expert_uses += (uint64_t)T * (uint64_t)K * (uint64_t)n_layers;
+    m->st.wall_s += now_s() - t0;
+    m->last_T = T;
+    return HXB_OK;
 }
 
 extern "C" HXB_API int hxb_moe_layer(hxb_moe *m, int layer, const float *x, int T, float *out) {

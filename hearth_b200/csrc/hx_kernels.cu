@@ -261,7 +261,7 @@ __global__ void __launch_bounds__(256) k_moe_router(MoeShape sh, const float *__
     float *score = rsm + warp * 2 * E, *sel = score + E;
     for (int tt = warp; tt < T; tt += nwarps)
         route_token_warp(sh.route, sc.logits + (int64_t)tt * E, bias, score, sel, sc.ids + tt * sh.route.K,
-                         sc.wts + tt * sh.route.K);
+                         sc.wts + tt * sh.route.K, sc.forced_ids ? sc.forced_ids + tt * sh.route.K : nullptr);
     __syncthreads();
     __threadfence_block();
     int *cnt = reinterpret_cast<int *>(rsm), *start = cnt + E;
@@ -333,7 +333,7 @@ __global__ void __launch_bounds__(256) k_route_select(MoeShape sh, const float *
     if (t >= sh.T) return;
     float *score = rsm + warp * 2 * E, *sel = score + E;
     route_token_warp(sh.route, sc.logits + (int64_t)t * E, bias, score, sel, sc.ids + t * sh.route.K,
-                     sc.wts + t * sh.route.K);
+                     sc.wts + t * sh.route.K, sc.forced_ids ? sc.forced_ids + t * sh.route.K : nullptr);
 }
 
 __global__ void __launch_bounds__(512) k_route_union(MoeShape sh, MoeScratch sc) {

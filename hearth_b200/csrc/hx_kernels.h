@@ -48,6 +48,7 @@ struct MoeScratch {
     int *ujob, *nu_job;  // expert parallelism: buckets of this rank's experts [E], their count [1]
     unsigned *ticket;    // [1] last-CTA counter of moe_router (returns to 0 after every launch)
     int *err;            // [1] device error word
+    const int *forced_ids = nullptr;   // [T, K] route replay: the ids to use instead of the selection
 };
 
 // Tensor maps (CUtensorMap, 128 bytes each) of the staged tensor-core expert kernels, encoded on

@@ -36,8 +36,10 @@ __device__ __forceinline__ void act_quant_warp(float x0, float x1, act_q8 *o, in
 
 // Top-k routing of one token by one warp (engine/src/model.c:793-843, NUMERICS §5.3).
 // logit: [E] (global, written by other CTAs: read through L2), score/sel: [E] shared scratch.
+// forced: null, or the token's K expert ids to use instead of the selection (route replay,
+// engine/src/model.c:1003-1009: the scores are computed as usual, the ids come from a trace).
 __device__ __forceinline__ void route_token_warp(const RouteCfg &R, const float *logit, const float *bias, float *score,
-                                 float *sel, int *ids_out, float *w_out) {
+                                 float *sel, int *ids_out, float *w_out, const int *forced = nullptr) {
     const int lane = threadIdx.x & 31, E = R.E, K = R.K;
     if (R.score_fn == SCORE_SOFTMAX) {
         float m = -__uint_as_float(0x7f800000u);
@@ -99,7 +101,10 @@ __device__ __forceinline__ void route_token_warp(const RouteCfg &R, const float 
     // top-K by selection value, descending, ties to the lower index, NaN last
     unsigned taken[12] = {0};   // E <= 384: lane owns i = lane + 32 m
     int myid = -1;
-    for (int j = 0; j < K; j++) {
+    if (forced) {   // replayed ids: no selection
+        if (lane < K) myid = forced[lane];
+    }
+    for (int j = 0; j < K && !forced; j++) {
         float bv = 0.0f;
         int bi = -1;
         for (int m = 0, i = lane; i < E; m++, i += 32) {

@@ -85,7 +85,7 @@ class MoeBackend:
                  norm_eps: float = 1e-6, expert_dtype: int = _lib.Q4, shared_ffn_dim: int = 0,
                  shared_dtype: int = _lib.Q8, shared_gate: int = 0, max_tokens: int = 1, cache_gb: float = 0.0,
                  policy: int = _lib.POLICY_LFU, heat_decay: float = 0.995, device: int = 0, ep_size: int = 1,
-                 ep_rank: int = 0):
+                 ep_rank: int = 0, prefetch_next: int = 1):
         L = lib()
         c = MoeConfig()
         L.hxb_moe_default_config(C.byref(c))
@@ -95,7 +95,7 @@ class MoeBackend:
                          residual_scale=residual_scale, norm_eps=norm_eps, expert_dtype=expert_dtype,
                          shared_ffn_dim=shared_ffn_dim, shared_dtype=shared_dtype, shared_gate=shared_gate,
                          max_tokens=max_tokens, cache_gb=cache_gb, policy=policy, heat_decay=heat_decay,
-                         device=device, ep_size=ep_size, ep_rank=ep_rank).items():
+                         device=device, ep_size=ep_size, ep_rank=ep_rank, prefetch_next=prefetch_next).items():
             setattr(c, k, v)
         err = C.create_string_buffer(512)
         h = L.hxb_moe_open(C.byref(c), err, 512)
@@ -147,6 +147,16 @@ class MoeBackend:
         n_layers = self.n_layers - layer0 if n_layers is None else n_layers
         out = np.array(h, dtype=np.float32, copy=True, order="C")
         check(lib().hxb_moe_forward(self.h, _ptr(out), out.shape[0], layer0, n_layers), "hxb_moe_forward")
+        return out
+
+    def forward_routed(self, h: np.ndarray, ids: np.ndarray, layer0: int = 0) -> np.ndarray:
+        """Route replay: like forward, with every token's K expert ids of every layer given
+        (ids [n_layers, T, K]); scores and weights computed as usual. Returns a new array."""
+        out = np.array(h, dtype=np.float32, copy=True, order="C")
+        ids = np.ascontiguousarray(ids, np.int32)
+        assert ids.ndim == 3 and ids.shape[1:] == (out.shape[0], self.K)
+        check(lib().hxb_moe_forward_routed(self.h, _ptr(out), out.shape[0], layer0, ids.shape[0], _ptr(ids)),
+              "hxb_moe_forward_routed")
         return out
 
     def forward_into(self, h: np.ndarray, layer0: int = 0, n_layers: int | None = None) -> None:

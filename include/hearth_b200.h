@@ -111,6 +111,11 @@ typedef struct hxb_moe_config {
     int device;            /* CUDA device ordinal */
     int ep_size, ep_rank;  /* expert parallelism: this handle holds and computes the experts e with
                               e % ep_size == ep_rank (default 1, 0: every expert) */
+    int prefetch_next;     /* streaming store (cache_gb below the model): after routing layer l, route
+                              layer l+1 with layer l's input (its ffn_norm and router) and hand the
+                              predicted experts to the store as prefetch hints, so their copies run
+                              while layer l computes (HEARTH_PREFETCH_NEXT, engine/src/model.c:944-973).
+                              Default 1; 0 = demand copies only. */
 } hxb_moe_config;
 
 typedef struct hxb_moe_stats {
@@ -180,6 +185,11 @@ HXB_API int hxb_moe_load_container(hxb_moe *m, const char *path);
  * h = h + residual_scale * moe_l(x)   (docs/NUMERICS.md §5, the FFN half of each layer). */
 HXB_API int hxb_moe_forward(hxb_moe *m, float *h, int T, int layer0, int n_layers);
 HXB_API int hxb_moe_forward_dev(hxb_moe *m, float *h, int T, int layer0, int n_layers, void *stream);
+/* Route replay (hearth_route_replay, engine/include/hearth.h:144-147; engine/src/model.c:1003-1009):
+ * like hxb_moe_forward, but every token's K expert ids of every layer come from the caller (ids
+ * [n_layers][T][K], host, each in [0, n_experts)) instead of the selection; scores and weights are
+ * computed as usual. Synchronous; used to measure throughput under a recorded routing skew. */
+HXB_API int hxb_moe_forward_routed(hxb_moe *m, float *h, int T, int layer0, int n_layers, const int *ids);
 /* One MoE FFN on x[T, D] as given (no norm, no residual): out[T, D] = rank-order expert sum
  * (+ shared expert). Host and device variants. */
 HXB_API int hxb_moe_layer(hxb_moe *m, int layer, const float *x, int T, float *out);

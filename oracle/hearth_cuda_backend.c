@@ -20,8 +20,9 @@
  * a container it cannot take) every evaluation fails with HX_E_IO, and the log says why.
  *   HEARTH_CUDA_DEVICE   CUDA device ordinal (default 0)
  *   HEARTH_CUDA_CACHE_GB HBM budget for expert slots in GiB (default 0: every expert resident)
- * Routing trace rows (hearth_trace_start, docs/FORMAT.md §9) are filled from the GPU routing.
- * Route replay (hearth_route_replay) is refused with the backend: the GPU routes for itself.
+ * Routing trace rows (hearth_trace_start, docs/FORMAT.md §9) are filled from the GPU routing; with a
+ * route replay (hearth_route_replay) the replayed rows go to the GPU (hxb_moe_forward_routed), the
+ * way moe_layer takes them (model.c:1003-1009: row (pos + i) mod rows, the layer's K ids).
  */
 #include "hearth_b200.h"
 
@@ -101,24 +102,29 @@ static int hxc_moe_layer(hx_model *m, const layer_w *w, int l, int T, int pos0) 
     }
     if (s->state == HXC_CPU) return moe_layer(m, w, l, T, pos0);
     if (s->state != HXC_CUDA) return HX_E_IO;
-    if (m->replay) {
-        hx_log(HX_LOG_ERROR, "cuda backend: route replay is not available (the GPU routes for itself)");
-        return HX_E_ARG;
+    const int K = m->K, mi = m->moe_index[l];
+    int rc;
+    if (m->replay) {   /* the trace's ids for these tokens and this MoE layer */
+        for (int i = 0; i < T; i++) {
+            const uint16_t *row =
+                m->replay + (size_t)((pos0 + i) % m->replay_rows) * (size_t)(m->n_moe * K) + (size_t)mi * K;
+            for (int j = 0; j < K; j++) m->ids[(size_t)i * K + j] = row[j];
+        }
+        rc = hxb_moe_forward_routed(s->b, m->h, T, l, 1, m->ids);
+    } else {
+        rc = hxb_moe_forward(s->b, m->h, T, l, 1);   /* leaves m->h untouched on failure */
     }
-    const int rc = hxb_moe_forward(s->b, m->h, T, l, 1);   /* leaves m->h untouched on failure */
     if (rc != HXB_OK) {
         hx_log(HX_LOG_ERROR, "cuda backend: layer %d: %s", l, hxb_last_error());
         return rc == HXB_E_CAPACITY ? HX_E_CAPACITY : rc == HXB_E_NOMEM ? HX_E_NOMEM : HX_E_IO;
     }
     /* routing of this layer into the per-token trace rows (model.c moe_layer, routes[]) */
-    const int K = m->K, mi = m->moe_index[l];
-    if (hxb_moe_last_routing(s->b, m->ids, m->wts, T) == HXB_OK)
+    if (m->replay || hxb_moe_last_routing(s->b, m->ids, m->wts, T) == HXB_OK)
         for (int i = 0; i < T; i++)
             for (int j = 0; j < K; j++)
                 m->routes[(size_t)i * (m->n_moe * K) + (size_t)mi * K + j] = (uint16_t)m->ids[(size_t)i * K + j];
     m->st.expert_uses += (uint64_t)T * (uint64_t)K;
     (void)w;
-    (void)pos0;
     return HX_OK;
 }
 

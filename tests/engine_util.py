@@ -52,6 +52,7 @@ def load(path):
         L.hearth_info.argtypes = [C.c_void_p, C.POINTER(HearthModelInfo)]
         L.hearth_trace_start.argtypes = [C.c_void_p, C.c_char_p]
         L.hearth_trace_stop.argtypes = [C.c_void_p]
+        L.hearth_route_replay.argtypes = [C.c_void_p, C.c_char_p]
         _libs[path] = L
     return _libs[path]
 
@@ -89,6 +90,9 @@ class Engine:
 
     def trace_stop(self):
         return self.L.hearth_trace_stop(self.h)
+
+    def route_replay(self, path):
+        return self.L.hearth_route_replay(self.h, os.fsencode(path))
 
     def close(self):
         if self.h:

@@ -77,12 +77,12 @@ def load_weights(b, layers):
 
 def backend_kwargs(*, L=1, D=256, F=128, E=16, K=4, score_fn=0, score_bias=0, n_group=1, topk_group=1, norm=1,
                    routed_scale=1.0, Fs=0, shared_gate=False, max_tokens=64, cache_gb=0.0, policy=1,
-                   residual_scale=1.0, shared_dtype=O.Q8, **_):
+                   residual_scale=1.0, shared_dtype=O.Q8, prefetch_next=1, **_):
     return dict(n_layers=L, d_model=D, expert_ffn_dim=F, n_experts=E, top_k=K, score_fn=score_fn,
                 score_bias=score_bias, n_group=n_group, topk_group=topk_group, norm_topk_prob=norm,
                 routed_scale=routed_scale, residual_scale=residual_scale, shared_ffn_dim=Fs,
                 shared_dtype=shared_dtype, shared_gate=int(shared_gate), max_tokens=max_tokens, cache_gb=cache_gb,
-                policy=policy)
+                policy=policy, prefetch_next=prefetch_next)
 
 
 def oracle_model(layers, *, D=256, F=128, E=16, K=4, score_fn=0, score_bias=0, n_group=1, topk_group=1, norm=1,

@@ -41,3 +41,24 @@ def test_gpu_backend_on_a_device_that_does_not_exist_fails(gpu, monkeypatch):
     with Engine(CUDA_LIB) as e:
         rc, _ = e.eval(PROMPT)
     assert rc == -4
+
+
+def test_gpu_route_replay_gives_the_reference_engines_logits(gpu, monkeypatch, tmp_path):
+    """hearth_route_replay with the backend: the replayed ids (a trace recorded from another prompt)
+    drive the GPU's MoE layers (hxb_moe_forward_routed) exactly as they drive moe_layer on the CPU."""
+    monkeypatch.delenv("HEARTH_BACKEND", raising=False)
+    trace = str(tmp_path / "rec.trace")
+    with Engine(REF_LIB) as rec:
+        session(rec, PROMPT[::-1], 6, trace)
+    other = [7, 2, 7, 1, 8, 2, 8, 1, 8, 2]
+    with Engine(REF_LIB) as cpu:
+        plain = session(cpu, other, 4)
+    with Engine(REF_LIB) as cpu:
+        assert cpu.route_replay(trace) == 0
+        want = session(cpu, other, 4)
+    assert not np.array_equal(want, plain)   # the replay changed the routing
+    monkeypatch.setenv("HEARTH_BACKEND", "cuda")
+    with Engine(CUDA_LIB) as g:
+        assert g.route_replay(trace) == 0
+        got = session(g, other, 4)
+    assert np.array_equal(got.view(np.uint32), want.view(np.uint32))

@@ -335,3 +335,25 @@ def test_tensor_core_stages_qwen3_layer_shape(gpu):
         y = be.layer(0, x)
     yo, _, _ = model.layer_eval(0, x)
     assert np.array_equal(bits(y), bits(yo))
+
+
+@pytest.mark.parametrize("cache_gb", [0.0, 20 * 53248 / 2**30])
+def test_forward_routed_with_the_computed_ids_equals_forward(gpu, cache_gb):
+    """Route replay entry point: given exactly the ids the routing computes (layer by layer), the
+    result equals the plain forward bit for bit; given other ids it differs (resident and streaming)."""
+    L, T = 3, 4
+    model, be = build_pair(71, L=L, E=16, K=4, max_tokens=T, cache_gb=cache_gb)
+    with be:
+        h = np.random.default_rng(13).standard_normal((T, 256)).astype(np.float32)
+        ids, x = [], h.copy()
+        for l in range(L):
+            x = be.forward(x, layer0=l, n_layers=1)
+            ids.append(be.last_routing(T)[0])
+        ids = np.stack(ids)
+        want = be.forward(h)
+        assert np.array_equal(bits(be.forward_routed(h, ids)), bits(want))
+        assert np.array_equal(bits(want), bits(model.forward(h)))
+        other = (ids + 1) % 16
+        assert not np.array_equal(bits(be.forward_routed(h, other)), bits(want))
+        with pytest.raises(RuntimeError, match="-1"):
+            be.forward_routed(h, np.full_like(ids, 16))

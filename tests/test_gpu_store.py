@@ -47,7 +47,7 @@ def test_prefetch_hint_then_use_counts_as_used(gpu):
 
 
 def test_prefetch_hint_evicted_unused_counts_as_wasted(gpu):
-    kw = dict(L=2, E=32, K=2, max_tokens=1, cache_gb=34 * SLAB / 2**30, policy=1)
+    kw = dict(L=2, E=32, K=2, max_tokens=1, cache_gb=34 * SLAB / 2**30, policy=1, prefetch_next=0)
     rng = np.random.default_rng(32)
     hs = [rng.standard_normal((1, 256)).astype(np.float32) for _ in range(30)]
     routed = _routing(kw, 62, hs)
@@ -72,7 +72,7 @@ def test_prefetch_hint_evicted_unused_counts_as_wasted(gpu):
 def test_prefetch_dropped_without_a_cold_slot(gpu):
     """LRU store whose every slot was used by the current token: a hint has no victim and is dropped;
     after the token boundary the least recently used slot becomes a victim and the hint is issued."""
-    kw = dict(L=2, E=16, K=4, max_tokens=8, cache_gb=18 * SLAB / 2**30, policy=0)
+    kw = dict(L=2, E=16, K=4, max_tokens=8, cache_gb=18 * SLAB / 2**30, policy=0, prefetch_next=0)
     h = np.random.default_rng(33).standard_normal((8, 256)).astype(np.float32)
     model, be = build_pair(63, **kw)
     with be:
@@ -87,3 +87,26 @@ def test_prefetch_dropped_without_a_cold_slot(gpu):
         be.prefetch(1, absent[:1])
         assert be.stats()["prefetch_issued"] == 1
         assert np.array_equal(bits(be.forward(h)), bits(model.forward(h)))
+
+
+@pytest.mark.parametrize("policy", [0, 1])
+def test_next_layer_prediction_prefetches_while_a_layer_computes(gpu, policy):
+    """With prefetch_next (the default) a streaming forward routes layer l+1 with layer l's input and
+    hands the predicted experts to the store as hints (engine/src/model.c:944-973): hints are issued
+    and used, results stay bit-identical to the oracle; with prefetch_next=0 no hint is issued."""
+    L, E = 4, 16
+    rng = np.random.default_rng(34)
+    hs = [rng.standard_normal((1, 256)).astype(np.float32) for _ in range(6)]
+    stats = {}
+    for pn in (1, 0):
+        model, be = build_pair(64, L=L, E=E, K=4, max_tokens=1, cache_gb=(E + 4) * SLAB / 2**30, policy=policy,
+                               prefetch_next=pn)
+        with be:
+            assert be.stats()["n_slots"] < L * E
+            for h in hs:
+                assert np.array_equal(bits(be.forward(h)), bits(model.forward(h)))
+                be.tick()
+            stats[pn] = be.stats()
+    assert stats[1]["prefetch_issued"] > 0 and stats[1]["prefetch_used"] > 0
+    assert stats[1]["prefetch_used"] + stats[1]["prefetch_wasted"] <= stats[1]["prefetch_issued"]
+    assert stats[0]["prefetch_issued"] == 0
