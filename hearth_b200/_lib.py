@@ -23,7 +23,7 @@ EXPORTS = [
     "hxb_version", "hxb_last_error", "hxb_device_count", "hxb_row_bytes", "hxb_matmul", "hxb_dequantize",
     "hxb_act_quantize_dev", "hxb_matmul_dev", "hxb_dequantize_dev", "hxb_expf_dev",
     "hxb_moe_default_config", "hxb_moe_open", "hxb_moe_close", "hxb_moe_set_layer", "hxb_moe_set_expert",
-    "hxb_moe_synthesize", "hxb_moe_slab_bytes", "hxb_moe_forward", "hxb_moe_forward_dev", "hxb_moe_forward_routed", "hxb_moe_layer",
+    "hxb_moe_synthesize", "hxb_moe_slab_bytes", "hxb_moe_forward", "hxb_moe_forward_dev", "hxb_moe_forward_routed", "hxb_moe_ep_ipc_handle", "hxb_moe_ep_connect", "hxb_moe_layer",
     "hxb_moe_layer_dev", "hxb_moe_last_routing", "hxb_moe_get_stats", "hxb_moe_reset_stats",
     "hxb_moe_is_resident", "hxb_moe_tick", "hxb_moe_prefetch", "hxb_moe_seed_heat", "hxb_moe_set_copy_hook",
     "hxb_moe_sync", "hxb_moe_profile", "hxb_matmul_noalloc", "hxb_moe_phase_trace", "hxb_moe_decode_path",
@@ -92,6 +92,8 @@ def lib() -> C.CDLL:
         "hxb_moe_forward": (i, [vp, vp, i, i, i]),
         "hxb_moe_forward_dev": (i, [vp, vp, i, i, i, vp]),
         "hxb_moe_forward_routed": (i, [vp, vp, i, i, i, vp]),
+        "hxb_moe_ep_ipc_handle": (i, [vp, vp]),
+        "hxb_moe_ep_connect": (i, [vp, vp]),
         "hxb_moe_layer": (i, [vp, i, vp, i, vp]),
         "hxb_moe_layer_dev": (i, [vp, i, vp, i, vp, vp]),
         "hxb_moe_last_routing": (i, [vp, vp, vp, i]),

@@ -246,6 +246,11 @@ struct hxb_moe {
     DevBuf dec_router, dec_norm, dec_bias;
     DevBuf dec_xbuf, dec_epoch;          // exchange buffers (two sets) and the launch counter
     DevBuf dec_trace;                    // phase timeline of the last launch (HXB_TRACE=1)
+    // expert parallelism in the persistent kernel: this GPU's y words (written by every GPU) and the
+    // table of every GPU's y words, filled by hxb_moe_ep_connect from the other ranks' IPC handles
+    DevBuf ep_y, ep_peers;
+    std::vector<void *> ep_opened;       // peer mappings to close
+    bool ep_connected = false;
 
     MoeScratch scratch() const {
         MoeScratch s;
@@ -367,6 +372,7 @@ struct hxb_moe {
 
     ~hxb_moe() {
         if (stream) cudaStreamSynchronize(stream);
+        for (void *p : ep_opened) cudaIpcCloseMemHandle(p);
         for (auto &g : graphs) cudaGraphExecDestroy(g.second);
         graphs.clear();
         if (hpin) cudaFreeHost(hpin);
@@ -497,7 +503,7 @@ extern "C" HXB_API hxb_moe *hxb_moe_open(const hxb_moe_config *c, char *err, siz
         // HXB_PERSISTENT=0: per-phase kernels only
         const char *env = std::getenv("HXB_PERSISTENT");
         std::string why_not;
-        const bool off = (env && env[0] == '0') || k.ep_size > 1;
+        const bool off = env && env[0] == '0';
         m->use_decode = !off &&
                         decode_supported(D, k.expert_ffn_dim, E, K, k.expert_dtype, k.shared_ffn_dim > 0, &why_not);
         if (m->use_decode) {
@@ -508,6 +514,12 @@ extern "C" HXB_API hxb_moe *hxb_moe_open(const hxb_moe_config *c, char *err, siz
                 !cuda_ok(cudaMemset(m->dec_epoch.p, 0, 64), "decode buffers") ||
                 !cuda_ok(init_decode_attributes(), "decode attributes")) {
                 set_errbuf(err, errlen, "hxb_moe_open: persistent decode setup failed: " + g_err);
+                return nullptr;
+            }
+            if (k.ep_size > 1 &&
+                (!m->ep_y.alloc(sizeof(uint64_t) * (size_t)L * K * D) || !m->ep_peers.alloc(sizeof(void *) * 64) ||
+                 !cuda_ok(cudaMemset(m->ep_y.p, 0, m->ep_y.n), "ep words"))) {
+                set_errbuf(err, errlen, "hxb_moe_open: expert-parallel exchange words: " + g_err);
                 return nullptr;
             }
             const char *tr = std::getenv("HXB_TRACE");
@@ -837,6 +849,9 @@ static cudaError_t enqueue_decode(hxb_moe *m, float *h, int l0, int nl, cudaStre
     p.trace = m->dec_trace.as<unsigned long long>();
     p.prefetch = true;
     p.slab_used = (m->lay.end + 15) / 16 * 16;
+    p.ep_size = k.ep_size;
+    p.ep_rank = k.ep_rank;
+    p.ep_y = k.ep_size > 1 ? m->ep_peers.as<uint64_t *const>() : nullptr;
     return launch_moe_decode(p, s);
 }
 
@@ -850,8 +865,9 @@ static void reset_decode_state(hxb_moe *m) {
 
 static int run_range(hxb_moe *m, float *h, float *out, int T, int l0, int nl, bool with_norm, bool resid,
                      cudaStream_t user, bool host_io, const float *hin, float *hout) {
-    if (m->cfg.ep_size > 1)
-        return fail(HXB_E_UNSUPPORTED, "an expert-parallel handle evaluates layers through hxb_moe_ep_*");
+    if (m->cfg.ep_size > 1 && !(m->use_decode && m->ep_connected && T == 1 && with_norm && resid && !out))
+        return fail(HXB_E_UNSUPPORTED, "an expert-parallel handle evaluates batches through hxb_moe_ep_*, and "
+                                       "single tokens once hxb_moe_ep_connect has run");
     cudaStream_t s = user ? user : m->stream;
     const size_t bytes = sizeof(float) * (size_t)T * m->cfg.d_model;
     const double t0 = now_s();
@@ -1184,6 +1200,44 @@ extern "C" HXB_API int hxb_moe_ep_combine_dev(hxb_moe *m, int layer, const float
                                        (cudaStream_t)stream),
                  "ep combine"))
         return HXB_E_DEVICE;
+    return HXB_OK;
+}
+
+// Expert parallelism in the persistent decode kernel: this GPU's y-word buffer as a CUDA IPC handle
+// (64 bytes), for the other ranks' hxb_moe_ep_connect.
+extern "C" HXB_API int hxb_moe_ep_ipc_handle(hxb_moe *m, void *handle) {
+    if (!m || !handle) return fail(HXB_E_ARG, "ep_ipc_handle: bad arguments");
+    if (m->cfg.ep_size <= 1 || !m->ep_y.p) return fail(HXB_E_UNSUPPORTED, "ep_ipc_handle: not an expert-parallel decode handle");
+    cudaSetDevice(m->device);
+    cudaIpcMemHandle_t h;
+    if (!cuda_ok(cudaIpcGetMemHandle(&h, m->ep_y.p), "ipc handle")) return HXB_E_DEVICE;
+    std::memcpy(handle, &h, sizeof h);
+    return HXB_OK;
+}
+
+// handles [ep_size][64]: every rank's hxb_moe_ep_ipc_handle (this rank's own entry is ignored).
+extern "C" HXB_API int hxb_moe_ep_connect(hxb_moe *m, const void *handles) {
+    if (!m || !handles) return fail(HXB_E_ARG, "ep_connect: bad arguments");
+    const int N = m->cfg.ep_size;
+    if (N <= 1 || !m->ep_y.p || N > 64) return fail(HXB_E_UNSUPPORTED, "ep_connect: not an expert-parallel decode handle");
+    if (m->ep_connected) return HXB_OK;
+    cudaSetDevice(m->device);
+    std::vector<void *> ptrs((size_t)N, nullptr);
+    for (int r = 0; r < N; r++) {
+        if (r == m->cfg.ep_rank) {
+            ptrs[(size_t)r] = m->ep_y.p;
+            continue;
+        }
+        cudaIpcMemHandle_t h;
+        std::memcpy(&h, static_cast<const uint8_t *>(handles) + (size_t)r * sizeof h, sizeof h);
+        void *p = nullptr;
+        if (!cuda_ok(cudaIpcOpenMemHandle(&p, h, cudaIpcMemLazyEnablePeerAccess), "ipc open")) return HXB_E_DEVICE;
+        m->ep_opened.push_back(p);
+        ptrs[(size_t)r] = p;
+    }
+    if (!cuda_ok(cudaMemcpy(m->ep_peers.p, ptrs.data(), sizeof(void *) * (size_t)N, cudaMemcpyHostToDevice), "peers"))
+        return HXB_E_DEVICE;
+    m->ep_connected = true;
     return HXB_OK;
 }
 

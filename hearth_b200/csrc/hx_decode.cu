@@ -25,6 +25,14 @@
 // memory; each launch resets the set the previous launch used (spread over its layers), so the next
 // launch finds it empty — no end-of-launch barrier, and the launch can be captured in a CUDA graph.
 // Every poll and every mbarrier wait is bounded: on expiry it records an error word and moves on.
+//
+// Expert parallelism (ep_size > 1, one launch per token on every GPU): rank r holds the experts e with
+// e % ep_size == r. P1 and P2 run on every GPU (the same routing everywhere); P3 and P4 cover only the
+// ranks j whose expert this GPU owns (the CTAs split those instead of all K); P4 stores each y row as
+// a tagged 64-bit word (high half: the launch number + 1, the same on every GPU for the same token;
+// low half: the value) into every GPU's y-word buffer over NVLink (plain peer stores, system scope);
+// P5 polls its own GPU's y words. Nothing else crosses GPUs, so every GPU ends each layer with the
+// single-GPU h, bit for bit.
 #include "hx_device.cuh"
 #include "hx_kernels.h"
 #include "hx_route.cuh"
@@ -109,7 +117,8 @@ struct DecodeLayout {
     int64_t rbD, rbF;
     size_t off_hs, off_xs, off_xact, off_stab, off_rrow, off_norm, off_gu, off_dn, off_mid, off_amid, off_y, off_p,
         off_gout, off_lg, off_pr, off_score, off_sel, off_key, off_gsc, off_keep, off_ids, off_w, off_yv, off_ptrs,
-        total;
+        off_chain, total;
+    int cs;   // floats per lane row of the chain buffer
 };
 
 HX_HD inline size_t align16(size_t v) { return (v + 15) & ~size_t(15); }
@@ -149,6 +158,10 @@ HX_HD inline DecodeLayout decode_layout(int G, int D, int F, int E, int K, int d
     L.off_w = o; o = align16(o + 16 * 4);
     L.off_yv = o; o = align16(o + (size_t)K * P.hr_max * 4);
     L.off_ptrs = o; o = align16(o + (size_t)3 * DEC_MAXL * 8);
+    // the 16-lane chains of NUMERICS §1 read their terms from here, lane j's D/16 terms contiguous:
+    // the squares of h (rmsnorm), then the router row's products (one router row per CTA)
+    L.cs = D / 16 + 4;
+    L.off_chain = o; o = align16(o + (size_t)16 * L.cs * 4);
     L.total = o;
     return L;
 }
@@ -178,6 +191,8 @@ struct DecodeArgs {
     unsigned long long *trace;    // null, or [Lyr][G][DEC_STAMPS] SM clock stamps of thread 0
     bool predict;                 // next-layer prediction and prefetch
     int64_t slab_used;            // bytes of a slab the kernels read (prefetch extent)
+    int ep_size, ep_rank;         // expert parallelism (1, 0: every expert here)
+    uint64_t *const *ep_y;        // [ep_size] every GPU's y words [Lb][K][D] (this GPU's at ep_rank)
     DecodeLayout lay;
 };
 
@@ -211,6 +226,26 @@ __device__ __forceinline__ void st_x(float *p, float v) {
 }
 
 __device__ __forceinline__ bool empty_word(float v) { return __float_as_uint(v) == kEmpty; }
+
+// Tagged y words of expert parallelism (system scope: written by the GPU that owns the expert).
+__device__ __forceinline__ void st_ep(uint64_t *p, uint32_t tag, float v) {
+    const uint64_t w = ((uint64_t)tag << 32) | (uint64_t)__float_as_uint(v);
+    asm volatile("st.relaxed.sys.global.b64 [%0], %1;" ::"l"(p), "l"(w) : "memory");
+}
+
+constexpr uint32_t kEpPollLimit = 1u << 20;   // a peer GPU's word: longer, a rank may start later
+__device__ __forceinline__ float poll_ep(const uint64_t *p, uint32_t tag, int *err) {
+    for (uint32_t spins = 0;; spins++) {
+        uint64_t w;
+        asm volatile("ld.relaxed.sys.global.b64 %0, [%1];" : "=l"(w) : "l"(p) : "memory");
+        if ((uint32_t)(w >> 32) == tag) return __uint_as_float((uint32_t)w);
+        if (spins > kEpPollLimit || ((spins & 255u) == 255u && *(volatile int *)err)) {
+            set_error(err, DEV_E_POLL);
+            return 0.0f;
+        }
+        __nanosleep(64);
+    }
+}
 
 // Polls one exchange word until it is filled (bounded; on expiry records an error and returns 0).
 __device__ __forceinline__ float poll1(const float *p, int *err) {
@@ -275,6 +310,14 @@ __device__ __forceinline__ void warp_rows_1tok(const uint8_t *tile, int64_t rb, 
 #pragma unroll
             for (int k = 0; k < DEC_PROWS; k++)
                 if (k < nr) P[k * 33 + lane] = term(col + (int64_t)k * rb, ar);
+        } else if (gn <= 16) {   // lane = (row phase, block): each lane's activation block loaded once
+            const int rp = 32 / gn, g = lane % gn, r2 = lane / gn;
+            if (r2 < rp) {
+                act_regs ar;
+                load_act(act + g0 + g, ar);
+                const uint8_t *col = tile + (int64_t)(g0 + g) * BS;
+                for (int k = r2; k < nr; k += rp) P[k * 33 + g] = term(col + (int64_t)k * rb, ar);
+            }
         } else {
             for (int it = lane; it < nr * gn; it += 32) {
                 const int k = it / gn, g = it - k * gn;
@@ -293,6 +336,26 @@ __device__ __forceinline__ void warp_rows_1tok(const uint8_t *tile, int64_t rb, 
     }
     if (lane < nr) out[lane] = canon(acc);
     __syncwarp();
+}
+
+// The 16-lane chain of NUMERICS §1 over the chain buffer: lane j < 16 adds c[j*cs + k], k = 0..4*n4-1,
+// in order (its own terms are contiguous: 16-byte loads, several in flight ahead of the adds), then
+// the 8/4/2/1 tree; the result lands in lane 0.
+__device__ __forceinline__ float chain16_regs(const float *c, int cs, int n4) {
+    const int lane = threadIdx.x & 31;
+    float L = 0.0f;
+    if (lane < 16) {
+        const float4 *r = reinterpret_cast<const float4 *>(c + lane * cs);
+#pragma unroll 8
+        for (int k = 0; k < n4; k++) {
+            const float4 v = r[k];
+            L = __fadd_rn(L, v.x);
+            L = __fadd_rn(L, v.y);
+            L = __fadd_rn(L, v.z);
+            L = __fadd_rn(L, v.w);
+        }
+    }
+    return tree16(L, 0xffffffffu);
 }
 
 // The K largest of E <= 128 values (one warp; any order among equal values): ids[0..K) of the
@@ -364,6 +427,7 @@ __device__ void decode_body(const DecodeArgs &a, uint8_t *smem) {
     float *yv = reinterpret_cast<float *>(smem + ly.off_yv);
     const float **p_router = reinterpret_cast<const float **>(smem + ly.off_ptrs);
     const float **p_norm = p_router + DEC_MAXL, **p_bias = p_norm + DEC_MAXL;
+    float *chb = reinterpret_cast<float *>(smem + ly.off_chain);
     __shared__ float rms_r;
     __shared__ float pred_part[DEC_WARPS];
     __shared__ int pred_ids[16];
@@ -393,15 +457,20 @@ __device__ void decode_body(const DecodeArgs &a, uint8_t *smem) {
     auto xy = [&](int l, int j) { return X + o_y + ((int64_t)l * K + j) * D; };
     auto xh = [&](int l) { return X + o_h + (int64_t)l * D; };
 
-    // this CTA's work
+    // this CTA's work (with expert parallelism the chunks and down groups follow, per layer, the ranks
+    // whose expert this GPU owns: s_own[0..s_nown))
     int ch0, ch1;
     chunk_range(c, G, pl.nch, &ch0, &ch1);
-    const int nch_c = ch1 - ch0;
-    const int jd = down_group(c, G, K);
+    int nch_c = ch1 - ch0;
+    int jd = down_group(c, G, K);
     int dr0, dr1, hr0, hr1;
     down_rows(c, G, K, D, pl.ra, &dr0, &dr1);
     h_rows(c, G, D, &hr0, &hr1);
-    const int ndr = dr1 - dr0, nhr = hr1 - hr0;
+    int ndr = dr1 - dr0;
+    const int nhr = hr1 - hr0;
+    const bool ep = a.ep_size > 1;
+    __shared__ int s_own[16], s_nown;
+    const uint32_t ep_tag = s_epoch + 1u;   // y words of this launch (buffers start at 0)
     const int cpe = F / DEC_CH;   // chunks per expert
     const uint32_t chunk_bytes = (uint32_t)(DEC_CH * ly.rbD);
     const bool small_route = E <= 128 && a.route.n_group <= 1;
@@ -442,33 +511,43 @@ __device__ void decode_body(const DecodeArgs &a, uint8_t *smem) {
                 }
             }
         }
-        if (l == 0) {
-            for (int i = tid; i < D; i += DEC_THREADS) hs[i] = __ldcg(a.h + i);
-        } else {
-            poll_vec(xh(l), hs, D, a.err);
+        for (int i4 = tid; i4 * 4 < D; i4 += DEC_THREADS) {   // h, and its squares for lane (i & 15)'s chain
+            const float4 v = l == 0 ? __ldcg(reinterpret_cast<const float4 *>(a.h) + i4) : poll4(xh(l) + 4 * i4, a.err);
+            reinterpret_cast<float4 *>(hs)[i4] = v;
+            const float q[4] = {v.x, v.y, v.z, v.w};
+#pragma unroll
+            for (int k = 0; k < 4; k++) {
+                const int i = 4 * i4 + k;
+                chb[(i & 15) * ly.cs + (i >> 4)] = __fmul_rn(q[k], q[k]);
+            }
         }
         __syncthreads();
         HX_STAMP(ST_H);
         if (warp == 0) {
-            float L = 0.0f;
-            if (lane < 16) {
-#pragma unroll 8
-                for (int i = lane; i < D; i += 16) L = __fadd_rn(L, __fmul_rn(hs[i], hs[i]));
-            }
-            L = tree16(L, 0xffffffffu);
+            const float L = chain16_regs(chb, ly.cs, D / 64);
             if (lane == 0) rms_r = __fdiv_rn(1.0f, __fsqrt_rn(__fadd_rn(__fdiv_rn(L, (float)D), a.eps)));
             HX_STAMP(ST_RMS);
         }
         mbar_wait(&bars[BAR_ROUTER], par, a.err);
         __syncthreads();
         HX_STAMP(ST_NORM);
+        const bool one_row = pl.rpc == 1;   // the router row's products go through the chain buffer
         {
             const float r = rms_r;
-            for (int i = tid; i < D; i += DEC_THREADS) xs[i] = __fmul_rn(__fmul_rn(hs[i], r), normv[i]);
+            for (int i = tid; i < D; i += DEC_THREADS) {
+                const float x = __fmul_rn(__fmul_rn(hs[i], r), normv[i]);
+                xs[i] = x;
+                if (one_row && c < E) chb[(i & 15) * ly.cs + (i >> 4)] = __fmul_rn(rrow[i], x);
+            }
         }
         __syncthreads();
         HX_STAMP(ST_X);
-        {   // router rows first (the logits are on every CTA's path): one 16-lane group each
+        if (one_row) {   // router row c first (the logits are on every CTA's path)
+            if (warp == 0 && c < E) {
+                const float L = chain16_regs(chb, ly.cs, D / 64);
+                if (lane == 0) st_x(xlg(l) + c, canon(L));
+            }
+        } else {   // router rows: one 16-lane group each
             const int t = tid >> 4, j = tid & 15;
             const bool active = t < pl.rpc && c + t * G < E;
             float L = 0.0f;
@@ -518,11 +597,42 @@ __device__ void decode_body(const DecodeArgs &a, uint8_t *smem) {
             route_token_warp1<true>(a.route, lgs, p_bias[l], lgs, rkey, score, sel, gscr, gkeep, ids, wts);
         }
         HX_STAMP(ST_RT);
+        if (ep && tid == 0) {   // the ranks whose expert this GPU owns, in rank order
+            int n = 0;
+            for (int j = 0; j < K; j++)
+                if (ids[j] % a.ep_size == a.ep_rank) s_own[n++] = j;
+            s_nown = n;
+        }
         __syncthreads();
+        const int nown = ep ? s_nown : K;
+        if (ep) {
+            chunk_range(c, G, nown * cpe, &ch0, &ch1);
+            nch_c = ch1 - ch0;
+            if (nown > 0) {
+                const int gi = down_group(c, G, nown);
+                jd = s_own[gi];
+                down_rows(c, G, nown, D, pl.ra, &dr0, &dr1);
+                ndr = dr1 - dr0;
+            } else {
+                jd = 0;
+                ndr = 0;
+            }
+        }
+        // chunk index g -> (rank j, chunk p within the expert)
+        auto chunk_rank = [&](int g, int *p) {
+            const int o = g / cpe;
+            *p = g - o * cpe;
+            return ep ? s_own[o] : o;
+        };
         if (warp == kIssueWarp) {   // a warp without a chunk (when nch_c < 16): the others start at once
             fence_proxy_async();
-            for (int q = lane; q < nch_c; q += 32) {   // chunk q: rows 4p..4p+3 of gate and of up, expert rank j
-                const int g = ch0 + q, j = g / cpe, p = g - j * cpe;
+            for (int q = lane; q < pl.ch_max; q += 32) {   // chunk q: rows 4p..4p+3 of gate and up, rank j
+                if (q >= nch_c) {   // every chunk barrier completes one phase per layer
+                    mbar_expect_tx(&bars[q], 0);
+                    continue;
+                }
+                int p;
+                const int g = ch0 + q, j = chunk_rank(g, &p);
                 const uint8_t *slab = stab[ids[j]];
                 if (!slab) {
                     set_error(a.err, DEV_E_NOT_RESIDENT);
@@ -536,8 +646,10 @@ __device__ void decode_body(const DecodeArgs &a, uint8_t *smem) {
                 }
             }
             if (lane == 0) {   // this CTA's slice of the rank-jd expert's down rows
-                const uint8_t *slab = stab[ids[jd]];
-                if (!slab) {
+                const uint8_t *slab = ndr > 0 ? stab[ids[jd]] : nullptr;
+                if (ndr == 0) {
+                    mbar_expect_tx(&bars[BAR_DOWN], 0);
+                } else if (!slab) {
                     set_error(a.err, DEV_E_NOT_RESIDENT);
                     mbar_expect_tx(&bars[BAR_DOWN], 0);
                 } else {
@@ -555,7 +667,8 @@ __device__ void decode_body(const DecodeArgs &a, uint8_t *smem) {
 
         // ---------------- P3: gate/up chunks -> SwiGLU -> mid exchange; next-layer prefetch
         for (int q = warp; q < nch_c; q += DEC_WARPS) {
-            const int g = ch0 + q, j = g / cpe, p = g - j * cpe;
+            int p;
+            const int g = ch0 + q, j = chunk_rank(g, &p);
             if (mbar_wait(&bars[q], par, a.err)) {
                 if (q == 0) HX_STAMP(ST_CH0);
                 warp_rows_1tok<DT>(gu + (size_t)q * 2 * chunk_bytes, ly.rbD, ly.nbD, 2 * DEC_CH, xact, P, gout);
@@ -578,6 +691,7 @@ __device__ void decode_body(const DecodeArgs &a, uint8_t *smem) {
             }
         }
         {   // reset this CTA's share of the other set's slots of buffer layers [b0, b1) for the next launch
+            // (while this CTA waits for the other CTAs' mid values anyway)
             const int b0 = (int)((int64_t)a.Lb * l / a.Lyr), b1 = (int)((int64_t)a.Lb * (l + 1) / a.Lyr);
             const int64_t per_layer[5] = {E, E, (int64_t)K * F, (int64_t)K * D, D};
             const int64_t base[5] = {o_lg, o_pr, o_mid, o_y, o_h};
@@ -591,10 +705,11 @@ __device__ void decode_body(const DecodeArgs &a, uint8_t *smem) {
         HX_STAMP(ST_RESET);
 
         // ---------------- P4: expert jd's mid -> activation blocks -> this CTA's down rows -> y exchange
-        poll_vec(xmid(l, jd), mids, F, a.err);
+        if (ndr > 0) poll_vec(xmid(l, jd), mids, F, a.err);
         __syncthreads();
         HX_STAMP(ST_MIDP);
-        for (int b = warp; b < ly.nbF; b += DEC_WARPS) act_quant_warp(mids[b * QK + lane], mids[b * QK + lane + 32], amid + b, lane);
+        for (int b = warp; b < ly.nbF && ndr > 0; b += DEC_WARPS)
+            act_quant_warp(mids[b * QK + lane], mids[b * QK + lane + 32], amid + b, lane);
         __syncthreads();
         HX_STAMP(ST_MIDQ);
         {
@@ -605,13 +720,22 @@ __device__ void decode_body(const DecodeArgs &a, uint8_t *smem) {
         }
         __syncthreads();
         HX_STAMP(ST_DOWN);
-        for (int r = tid; r < ndr; r += DEC_THREADS) st_x(xy(l, jd) + dr0 + r, Ys[r]);
+        if (!ep) {
+            for (int r = tid; r < ndr; r += DEC_THREADS) st_x(xy(l, jd) + dr0 + r, Ys[r]);
+        } else {   // every GPU's y words (its own included)
+            const int64_t o = ((int64_t)l * K + jd) * D + dr0;
+            for (int i = tid; i < ndr * a.ep_size; i += DEC_THREADS) {
+                const int p = i / ndr, r = i - p * ndr;
+                st_ep(a.ep_y[p] + o + r, ep_tag, Ys[r]);
+            }
+        }
         HX_STAMP(ST_YST);
 
         // ---------------- P5: y of the K experts for this CTA's h rows -> rank-order sum -> residual
         for (int i = tid; i < K * nhr; i += DEC_THREADS) {
             const int j = i / nhr, r = i - j * nhr;
-            yv[i] = poll1(xy(l, j) + hr0 + r, a.err);
+            yv[i] = ep ? poll_ep(a.ep_y[a.ep_rank] + ((int64_t)l * K + j) * D + hr0 + r, ep_tag, a.err)
+                       : poll1(xy(l, j) + hr0 + r, a.err);
         }
         __syncthreads();
         HX_STAMP(ST_Y);
@@ -633,7 +757,7 @@ __device__ void decode_body(const DecodeArgs &a, uint8_t *smem) {
     // every bulk copy this CTA issued has landed before it exits (already true unless a wait gave up)
     if (tid == 0 && a.Lyr > 0) {
         const uint32_t last = (uint32_t)((a.Lyr - 1) & 1);
-        for (int q = 0; q < nch_c; q++) mbar_wait(&bars[q], last, nullptr);
+        for (int q = 0; q < pl.ch_max; q++) mbar_wait(&bars[q], last, nullptr);
         mbar_wait(&bars[BAR_DOWN], last, nullptr);
         mbar_wait(&bars[BAR_ROUTER], last, nullptr);
         // the last CTA to finish advances the launch counter (every CTA read it at its start)
@@ -732,6 +856,10 @@ cudaError_t launch_moe_decode(const DecodeParams &p, cudaStream_t s) {
     a.w_out = p.w_out;
     a.trace = p.trace;
     a.slab_used = p.slab_used;
+    a.ep_size = p.ep_size;
+    a.ep_rank = p.ep_rank;
+    a.ep_y = p.ep_y;
+    if (a.ep_size > 1 && !a.ep_y) return cudaErrorInvalidValue;
     const int G = decode_grid();
     a.lay = decode_layout(G, p.D, p.F, p.E, p.K, p.dtype);
     a.predict = p.prefetch && p.E <= G && p.E <= 128 && p.route.n_group <= 1 &&

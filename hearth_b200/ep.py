@@ -7,6 +7,11 @@ the ranks all-gather those outputs (NCCL over NVLink on B200), and every rank fo
 sum taking each pair from its owner. The result equals the single-GPU result bit for bit, for any
 number of ranks, and every rank ends the layer with the same h.
 
+Single tokens on handles the persistent decode kernel takes: one launch per token on every rank for
+every layer, the owners storing their (token, rank) outputs straight into every GPU's memory over
+NVLink (CUDA IPC mappings exchanged once at start); no collective per layer. Batches: per layer, the
+routing and the owned pairs, an NCCL all-gather, the combine.
+
 The reference evaluates the whole layer in one process (engine/src/model.c:986-1131 moe_layer,
 904-923 moe_sum_range); the exchange is this backend's addition.
 """
@@ -42,6 +47,27 @@ class ExpertParallelMoe:
         dev = torch.device(device) if device is not None else torch.device("cuda", backend.cfg.device)
         self._y = torch.zeros((T * backend.K, backend.D), dtype=torch.float32, device=dev)
         self._y_all = torch.zeros((self.world * T * backend.K * backend.D,), dtype=torch.float32, device=dev)
+        self.connected = False
+        decode_path = getattr(backend, "decode_path", None)
+        if dev.type == "cuda" and decode_path is not None and decode_path() == "persistent":
+            self._connect(dev)
+
+    def _connect(self, dev) -> None:
+        """Every rank maps the other ranks' y-word buffers (CUDA IPC handles, all-gathered)."""
+        import numpy as np
+        import torch
+        import torch.distributed as dist
+        from ._lib import check, lib
+        mine = np.zeros(64, np.uint8)
+        check(lib().hxb_moe_ep_ipc_handle(self.be.h, mine.ctypes.data), "hxb_moe_ep_ipc_handle")
+        t = torch.from_numpy(mine).to(dev)
+        every = torch.empty(self.world * 64, dtype=torch.uint8, device=dev)
+        dist.all_gather_into_tensor(every, t, group=self.group)
+        allh = np.ascontiguousarray(every.cpu().numpy())
+        check(lib().hxb_moe_ep_connect(self.be.h, allh.ctypes.data), "hxb_moe_ep_connect")
+        torch.cuda.synchronize(dev)
+        dist.barrier(group=self.group)   # no rank launches before every rank has mapped the others
+        self.connected = True
 
     @classmethod
     def open(cls, group=None, **cfg) -> "ExpertParallelMoe":
@@ -70,5 +96,8 @@ class ExpertParallelMoe:
     def forward_dev(self, h, T: int, layer0: int = 0, n_layers: int | None = None, stream=None) -> None:
         """Layers [layer0, layer0 + n_layers) in place on h [T, D]."""
         n_layers = self.be.n_layers - layer0 if n_layers is None else n_layers
+        if self.connected and T == 1:   # one persistent launch for every layer, exchange over NVLink
+            self.be.forward_dev(h, 1, layer0, n_layers, stream=stream)
+            return
         for l in range(layer0, layer0 + n_layers):
             self.layer_dev(l, h, T, stream=stream)

@@ -224,6 +224,16 @@ HXB_API int64_t hxb_moe_phase_trace(hxb_moe *m, uint64_t *out, int64_t max_value
  * (HXB_E_IO otherwise). No counterpart in the reference (one process, one CPU). */
 HXB_API int hxb_moe_ep_layer_dev(hxb_moe *m, int layer, const float *h, int T, float *y, void *stream);
 HXB_API int hxb_moe_ep_combine_dev(hxb_moe *m, int layer, const float *y_all, int T, float *h, void *stream);
+/* Expert parallelism in the persistent single-token kernel (every GPU launches one kernel per token,
+ * each computes the rank-order terms of the experts it owns and stores their y rows straight into
+ * every GPU's memory over NVLink): each rank exports its y-word buffer with hxb_moe_ep_ipc_handle
+ * (64 bytes), the ranks exchange the handles (an all-gather over any channel), and each passes all of
+ * them, in rank order, to hxb_moe_ep_connect. From then on hxb_moe_forward / hxb_moe_forward_dev with
+ * T = 1 on every rank, in the same order and with the same h, give every rank the single-GPU h bit
+ * for bit. All ranks must launch the same number of tokens (each launch waits for the other ranks'
+ * words of the same launch). No counterpart in the reference (one process, one CPU). */
+HXB_API int hxb_moe_ep_ipc_handle(hxb_moe *m, void *handle);
+HXB_API int hxb_moe_ep_connect(hxb_moe *m, const void *handles);
 /* Which kernel evaluates a single-token forward over every layer (every expert resident):
  * 0 per-phase kernels (one launch per phase and layer), 1 the persistent decode kernel (one launch
  * for all layers). Chosen at open from the shape; the environment variable HXB_PERSISTENT=0 forces

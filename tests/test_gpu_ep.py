@@ -151,3 +151,69 @@ def test_ep_over_nccl_equals_oracle(gpu, T):
         np.random.default_rng(4).standard_normal((T, 256)).astype(np.float32))
     for r in range(world):
         assert np.array_equal(bits(got[r]), bits(want)), f"rank {r}"
+
+
+def _persistent_rank(rank, world, port, steps, out):
+    import datetime
+    import os
+
+    import torch
+    import torch.distributed as dist
+
+    import hearth_b200 as hb
+    from hearth_b200.ep import ExpertParallelMoe
+    from moe_util import backend_kwargs, load_weights, make_weights
+
+    os.environ.update(MASTER_ADDR="127.0.0.1", MASTER_PORT=str(port), NCCL_NVLS_ENABLE="0")
+    torch.cuda.set_device(rank)
+    dist.init_process_group("nccl", rank=rank, world_size=world, timeout=datetime.timedelta(seconds=60),
+                            device_id=torch.device("cuda", rank))
+    try:
+        kw = dict(L=3, D=512, F=256, E=32, K=4, max_tokens=1, residual_scale=0.7)
+        be = hb.MoeBackend(ep_size=world, ep_rank=rank, device=rank, **backend_kwargs(**kw))
+        load_weights(be, make_weights(81, **kw))
+        ep = ExpertParallelMoe(be)
+        assert be.decode_path() == "persistent" and ep.connected
+        rng = np.random.default_rng(6)
+        res = []
+        for _ in range(steps):   # the same tokens on every rank; one launch per token and rank
+            h = torch.from_numpy(rng.standard_normal((1, 512)).astype(np.float32)).cuda()
+            ep.forward_dev(h, 1)
+            be.sync()
+            res.append(h.cpu().numpy())
+        out[rank] = np.concatenate(res)
+        torch.cuda.synchronize()
+        dist.barrier()
+        be.close()
+    finally:
+        dist.destroy_process_group()
+
+
+@pytest.mark.gpu
+def test_ep_persistent_decode_over_nvlink_equals_oracle(gpu):
+    """Expert parallelism inside the persistent decode kernel on two GPUs: each rank computes the
+    experts it owns and stores their y rows into both GPUs' memory (peer stores over NVLink, tagged
+    words); both ranks end every token with the oracle's h bit for bit."""
+    import socket
+
+    import torch
+    import torch.multiprocessing as mp
+
+    from moe_util import make_weights, oracle_model
+
+    world = 2
+    if torch.cuda.device_count() < world:
+        pytest.skip("needs two GPUs")
+    s = socket.socket()
+    s.bind(("127.0.0.1", 0))
+    port = s.getsockname()[1]
+    s.close()
+    steps = 6
+    got = mp.get_context("spawn").Manager().dict()
+    mp.spawn(_persistent_rank, args=(world, port, steps, got), nprocs=world, join=True)
+    kw = dict(L=3, D=512, F=256, E=32, K=4, residual_scale=0.7)
+    model = oracle_model(make_weights(81, **kw), **kw)
+    rng = np.random.default_rng(6)
+    want = np.concatenate([model.forward(rng.standard_normal((1, 512)).astype(np.float32)) for _ in range(steps)])
+    for r in range(world):
+        assert np.array_equal(bits(got[r]), bits(want)), f"rank {r}"
