@@ -1,6 +1,7 @@
 """Benchmark: Q4 MoE decode through the Qwen3-30B-A3B-shaped MoE stack on B200.
 
     python bench.py [--gpus N] [--steps K] [--warmup W] [--impl ours|reference] [--batch B]
+                    [--model qwen3|olmoe|mixtral|kimi] [--layers L]
 
 Workload (one "step" = one decode step of B tokens through the hot path of every layer):
 48 MoE layers of Qwen3-30B-A3B shape — per layer x = rmsnorm(h, ffn_norm), router [128 x 2048]
@@ -12,6 +13,8 @@ resident (14.7 GB). N > 1 (torchrun): the same token stream through the stack wi
 over the ranks (expert e on rank e % N), strong scaling: at batch 1 one persistent kernel per token
 and rank, the owners storing their experts' outputs into every GPU's memory over NVLink; --replicas
 instead runs N independent replicas (weak scaling, no exchange).
+--model selects another configuration's MoE stack (OLMoE-1B-7B, Mixtral-8x7B at batch 8, Kimi-K2
+with its grouped sigmoid router, selection bias and Q8 shared expert), same line format.
 
 value  : tokens/s with inputs resident in HBM (CUDA events on the launching stream, max over ranks)
 e2e    : tokens/s through the public C ABI with host buffers (hxb_moe_forward: pinned-host copies
@@ -35,8 +38,55 @@ REPO = os.path.dirname(os.path.abspath(__file__))
 sys.path.insert(0, REPO)
 
 METRIC = "Q4 MoE decode tok/s (Qwen3-30B-A3B shape); expert-GEMV HBM GB/s vs peak"
+SIGMA = 0.02
+
+# The MoE stacks of the benchmark configurations (routing as each architecture defines it; the
+# seed is the configuration's). qwen3 is the headline workload; the others are --model modes.
+MODELS = {
+    "qwen3": dict(name="qwen3-30b-a3b", layers=48, D=2048, F=768, E=128, K=8, seed=2, batch=1,
+                  route=dict(score_fn=0, norm_topk_prob=1)),
+    "olmoe": dict(name="olmoe-1b-7b", layers=16, D=2048, F=1024, E=64, K=8, seed=1, batch=1,
+                  route=dict(score_fn=0, norm_topk_prob=0)),
+    "mixtral": dict(name="mixtral-8x7b", layers=32, D=4096, F=14336, E=8, K=2, seed=3, batch=8,
+                    route=dict(score_fn=0, norm_topk_prob=1)),
+    # Kimi-K2 / DeepSeek-V3: 60 MoE layers (the first of 61 is dense), sigmoid scores + selection
+    # bias, 8 groups keep 4, routed_scale 2.827, one Q8 shared expert of width 2048
+    "kimi": dict(name="kimi-k2", layers=60, D=7168, F=2048, E=384, K=8, seed=4, batch=1, Fs=2048,
+                 route=dict(score_fn=1, score_bias=1, n_group=8, topk_group=4, norm_topk_prob=1,
+                            routed_scale=2.827)),
+}
+MODEL = "qwen3"
 L_, D_, F_, E_, K_ = 48, 2048, 768, 128, 8
-SEED, SIGMA = 2, 0.02
+FS_ = 0
+SEED = 2
+
+
+def set_model(key, layers=None, world=1):
+    """Selects the stack; layers default to the model's, or to as many as fit the GPUs' HBM (~150 GB
+    of expert slabs per GPU) when the whole stack does not."""
+    global MODEL, L_, D_, F_, E_, K_, FS_, SEED
+    m = MODELS[key]
+    MODEL, D_, F_, E_, K_, FS_, SEED = key, m["D"], m["F"], m["E"], m["K"], m.get("Fs", 0), m["seed"]
+    per_layer = E_ * slab_bytes()
+    fit = max(1, int(world * 150e9 // per_layer))
+    L_ = layers or min(m["layers"], fit)
+
+
+def slab_bytes():
+    """FORMAT §5 slab of one Q4 expert: gate/up [F, D] and down [D, F] at 64-byte aligned offsets,
+    padded to 4096."""
+    a = lambda n, k: (n + k - 1) // k * k
+    g = F_ * (34 * D_ // 64)
+    return a(a(a(g, 64) + g, 64) + D_ * (34 * F_ // 64), 4096)
+
+
+def backend_kw(**extra):
+    """MoeBackend arguments of the selected stack."""
+    m = MODELS[MODEL]
+    kw = dict(n_layers=L_, d_model=D_, expert_ffn_dim=F_, n_experts=E_, top_k=K_, shared_ffn_dim=FS_,
+              shared_dtype=3, **m["route"])
+    kw.update(extra)
+    return kw
 
 
 def batch_gateup_bytes(B):
@@ -49,13 +99,23 @@ def batch_gateup_bytes(B):
 
 
 def algorithmic_bytes():
-    """Bytes the path must read per token and layer (B = 1), FORMAT §6 row sizes."""
-    q4_row_d = 34 * D_ // 64            # gate/up row: 1088 B
-    q4_row_f = 34 * F_ // 64            # down row: 408 B
+    """Bytes the path must read per token and layer (B = 1), FORMAT §6 row sizes: K experts' gate,
+    up and down rows, the router (and selection bias), the norm, and a shared expert's Q8 rows."""
+    q4_row_d = 34 * D_ // 64            # gate/up row (Qwen3: 1088 B)
+    q4_row_f = 34 * F_ // 64            # down row (Qwen3: 408 B)
     expert = 2 * F_ * q4_row_d + D_ * q4_row_f
-    router = E_ * D_ * 4
+    router = E_ * D_ * 4 + (E_ * 4 if MODELS[MODEL]["route"].get("score_bias") else 0)
+    shared = 2 * FS_ * (66 * D_ // 64) + D_ * (66 * FS_ // 64) if FS_ else 0
     return dict(gateup=K_ * 2 * F_ * q4_row_d, down=K_ * D_ * q4_row_f, router=router, norm=D_ * 4,
-                layer=K_ * expert + router + D_ * 4, expert=expert)
+                shared=shared, layer=K_ * expert + router + D_ * 4 + shared, expert=expert)
+
+
+def step_bytes(B):
+    """Algorithmic bytes of one step of B tokens through the stack: per layer the expected distinct
+    experts of B tokens drawing K of E (all K at B = 1), the router, the norm and the shared expert."""
+    ab = algorithmic_bytes()
+    experts = K_ if B == 1 else E_ * (1.0 - (1.0 - K_ / E_) ** B)
+    return round(L_ * (experts * ab["expert"] + ab["router"] + ab["norm"] + ab["shared"]))
 
 
 # DRAM bytes (read + write) per layer of k_moe_decode from one ncu capture of a 4-layer launch of the
@@ -66,13 +126,22 @@ DECODE_DRAM_BYTES_PER_LAYER = (94_621_952 + 2_688_000) / 4
 
 def workload_config(B, world, parallelism=None):
     """The line's config (identical in both arms: the reference arm times the same workload)."""
-    return {"workload": f"qwen3-30b-a3b MoE stack {'decode' if B == 1 else 'batch step'}, {L_} layers, batch {B}",
-            "layers": L_, "d_model": D_, "expert_ffn_dim": F_, "n_experts": E_, "top_k": K_, "batch": B,
-            "parallelism": parallelism or f"replica x{world}",
-            "l2": "no flush: each step reads ~1.01 GB of expert/router weights (> 126 MB L2)",
-            "weights": "synthetic: seeded Q4 blocks with the statistics of N(0, 0.02) weights packed to Q4 and "
-                       "an N(0, 0.02) f32 router, generated by the library's device generator (the CPU arm "
-                       "generates the same bytes on the host)"}
+    m = MODELS[MODEL]
+    cfg = {"workload": f"{m['name']} MoE stack {'decode' if B == 1 else 'batch step'}, {L_} layers, batch {B}",
+           "layers": L_, "d_model": D_, "expert_ffn_dim": F_, "n_experts": E_, "top_k": K_, "batch": B,
+           "parallelism": parallelism or f"replica x{world}",
+           "l2": f"no flush: each step reads ~{L_ * algorithmic_bytes()['layer'] / 1e9:.2f} GB of expert/router "
+                 "weights (> 126 MB L2)",
+           "weights": "synthetic: seeded Q4 blocks with the statistics of N(0, 0.02) weights packed to Q4 and "
+                      "an N(0, 0.02) f32 router, generated by the library's device generator (the CPU arm "
+                      "generates the same bytes on the host)"}
+    if MODEL != "qwen3":
+        cfg["routing"] = dict(m["route"])
+        if FS_:
+            cfg["shared_expert"] = {"ffn_dim": FS_, "dtype": "q8"}
+        if L_ < m["layers"]:
+            cfg["layers_note"] = f"{L_} of the model's {m['layers']} MoE layers: as many as fit the GPUs' HBM"
+    return cfg
 
 
 def peaks():
@@ -151,14 +220,23 @@ def max_over_ranks(v: float, world: int, device=None) -> float:
 
 
 def cpu_model(ref, n_layers):
-    """The benchmark's model on the host, byte-identical to hxb_moe_synthesize(SEED)."""
+    """The benchmark's model on the host, byte-identical to hxb_moe_synthesize(SEED): the router, the
+    selection bias and the shared expert of layer l from seed SEED * 1000003 + l, the slabs from SEED."""
     from oracle import oracle as O
     up, down, nb = O.slab_layout(O.Q4, D_, F_)
     slabs = ref.synth_q4(n_layers * E_, nb, D_, F_, SEED, SIGMA)
-    model = O.MoeModel(D_, F_, E_, K_, score_fn=0, norm_topk_prob=1, eps=1e-6, residual_scale=1.0)
+    route = MODELS[MODEL]["route"]
+    model = O.MoeModel(D_, F_, E_, K_, eps=1e-6, residual_scale=1.0, **route)
     for l in range(n_layers):
-        router = ref.synth_f32(E_ * D_, SEED * 1000003 + l, SIGMA).reshape(E_, D_)
-        model.add_layer(router, [slabs[l * E_ + e] for e in range(E_)], [O.Q4] * E_)
+        ls = SEED * 1000003 + l
+        router = ref.synth_f32(E_ * D_, ls, SIGMA).reshape(E_, D_)
+        bias = ref.synth_f32(E_, ls ^ 0xb1a5b1a5, 0.5 * SIGMA) if route.get("score_bias") else None
+        shared = None
+        if FS_:
+            shared = dict(Fs=FS_, dtype=O.Q8, gate=ref.synth_blocks(O.Q8, FS_, D_, ls ^ 0x5a1, SIGMA),
+                          up=ref.synth_blocks(O.Q8, FS_, D_, ls ^ 0x5a2, SIGMA),
+                          down=ref.synth_blocks(O.Q8, D_, FS_, ls ^ 0x5a3, SIGMA), gate_inp=None)
+        model.add_layer(router, [slabs[l * E_ + e] for e in range(E_)], [O.Q4] * E_, bias=bias, shared=shared)
     return model, slabs
 
 
@@ -188,6 +266,10 @@ def run_reference(args, rank, world):
     from oracle import oracle as O
     if O.moe_ref_lib() is None:
         print(json.dumps({"impl": "reference", "unavailable": "oracle/_ref was not built (reference sources absent)"}))
+        return
+    if MODEL == "kimi":
+        print(json.dumps({"impl": "reference", "unavailable": "the Kimi-K2 stack's experts (539 GB) exceed the "
+                                                              "host memory the CPU arm would hold them in"}))
         return
     ref = O.MoeRef(n_threads=0)
     model, _ = cpu_model(ref, L_)
@@ -223,8 +305,7 @@ def run_trace(args, local_rank):
     import torch
     import hearth_b200 as hb
     torch.cuda.set_device(local_rank)
-    be = hb.MoeBackend(n_layers=L_, d_model=D_, expert_ffn_dim=F_, n_experts=E_, top_k=K_, score_fn=0,
-                       norm_topk_prob=1, max_tokens=1, device=local_rank)
+    be = hb.MoeBackend(**backend_kw(max_tokens=1, device=local_rank))
     be.synthesize(SEED, SIGMA, SIGMA)
     g = torch.Generator(device="cuda").manual_seed(1000)
     pool = torch.randn((64, 1, D_), generator=g, device="cuda")
@@ -265,8 +346,7 @@ def run_ep(args, rank, world, local_rank):
     from hearth_b200.ep import ExpertParallelMoe
     dev = torch.device("cuda", local_rank)
     B = args.batch
-    be = hb.MoeBackend(n_layers=L_, d_model=D_, expert_ffn_dim=F_, n_experts=E_, top_k=K_, score_fn=0,
-                       norm_topk_prob=1, max_tokens=B, device=local_rank, ep_size=world, ep_rank=rank)
+    be = hb.MoeBackend(**backend_kw(max_tokens=B, device=local_rank, ep_size=world, ep_rank=rank))
     be.synthesize(SEED, SIGMA, SIGMA)
     ep = ExpertParallelMoe(be)
     dist.barrier()
@@ -311,15 +391,12 @@ def run_ep(args, rank, world, local_rank):
     t_e2e = max_over_ranks(time.perf_counter() - t0, world, dev)
     ab = algorithmic_bytes()
     hbm, peak_kind = peaks()
-    gbs = L_ * ab["layer"] / (ms / args.steps * 1e-3) / 1e9   # whole-stack bytes over all ranks
+    gbs = step_bytes(B) / (ms / args.steps * 1e-3) / 1e9   # whole-stack bytes over all ranks
     if rank == 0:
         line = {"metric": METRIC, "value": round(value, 3), "unit": "tok/s", "n_gpus": world, "steps": args.steps,
                 "warmup": args.warmup, "ms_per_step": round(ms / args.steps, 5), "higher_is_better": True,
                 "scaling": "strong", "vs_baseline": None, "dtype": "q4xq8-int32+f32", "data": "synthetic",
-                "config": {"workload": f"qwen3-30b-a3b MoE stack decode, {L_} layers, batch {B}, expert-parallel",
-                           "layers": L_, "d_model": D_, "expert_ffn_dim": F_, "n_experts": E_, "top_k": K_,
-                           "batch": B, "parallelism": f"ep{world}",
-                           "l2": "no flush: each step reads ~1.01 GB of expert/router weights over the ranks"},
+                "config": workload_config(B, world, f"ep{world}"),
                 "roofline": {"bound": "hbm", "achieved": round(gbs, 1), "peak": round(hbm * world, 1), "unit": "GB/s",
                              "frac": round(gbs / (hbm * world), 4), "traffic": None,
                              "kernel": ("k_moe_decode expert-parallel (one launch per token and rank; y rows stored "
@@ -340,8 +417,7 @@ def run_ours(args, rank, world, local_rank):
     torch.cuda.set_device(local_rank)
     dev = torch.device("cuda", local_rank)
     B = args.batch
-    be = hb.MoeBackend(n_layers=L_, d_model=D_, expert_ffn_dim=F_, n_experts=E_, top_k=K_, score_fn=0,
-                       norm_topk_prob=1, max_tokens=B, device=local_rank)
+    be = hb.MoeBackend(**backend_kw(max_tokens=B, device=local_rank))
     be.synthesize(SEED, SIGMA, SIGMA)
     # token pool resident in HBM; each step evaluates a fresh slot in place
     P = 64
@@ -404,7 +480,7 @@ def run_ours(args, rank, world, local_rank):
     us = be.profile(B, 2)
     ab = algorithmic_bytes()
     hbm, peak_kind = peaks()
-    step_gbs = L_ * ab["layer"] / (ms / args.steps * 1e-3) / 1e9
+    step_gbs = step_bytes(B) / (ms / args.steps * 1e-3) / 1e9
     path = be.decode_path()
     persistent = B == 1 and path != "layers"
     if persistent:
@@ -423,7 +499,7 @@ def run_ours(args, rank, world, local_rank):
     # bit-exact spot check of the GPU against it on the sampled tokens
     cpu = None
     parity = None
-    if rank == 0 and world == 1 and not args.no_cpu:
+    if rank == 0 and world == 1 and not args.no_cpu and MODEL != "kimi":
         from oracle import oracle as O
         if O.moe_ref_lib() is not None:
             ref = O.MoeRef(n_threads=0)
@@ -431,7 +507,7 @@ def run_ours(args, rank, world, local_rank):
             arr = model.c_layers()
             tps, n, ins, outs = time_cpu(ref, model, arr, B, 20.0, 400, np.random.default_rng(99))
             cpu = {"value": round(tps, 3), "unit": "tok/s", "cores": ref.threads, "kind": "reference",
-                   "sample": f"{n} decode steps of batch {B} (~20 s) of the same 48-layer workload, reference "
+                   "sample": f"{n} decode steps of batch {B} (~20 s) of the same {L_}-layer workload, reference "
                              f"AVX-512 kernels + hx_pool on {ref.threads} threads"}
             bad = 0
             for hin, hout in zip(ins[:16], outs[:16]):
@@ -452,14 +528,15 @@ def run_ours(args, rank, world, local_rank):
             "config": workload_config(B, world),
             "roofline": {"bound": "hbm", "achieved": round(kgbs, 1), "peak": hbm, "unit": "GB/s",
                          "frac": round(kgbs / hbm, 4),
-                         "traffic": round(DECODE_DRAM_BYTES_PER_LAYER * L_) if persistent else None,
+                         "traffic": round(DECODE_DRAM_BYTES_PER_LAYER * L_) if persistent and MODEL == "qwen3"
+                         else None,
                          "traffic_note": ("ncu dram bytes of a 4-layer capture scaled to the launch's layers"
                                           if persistent else None),
                          "kernel": kernel, "peak_kind": peak_kind,
                          "multi_kernel_stage_us": {"norm_act": round(us[0], 3), "router": round(us[1], 3),
                                                    "gateup": round(us[2], 3), "down": round(us[3], 3)},
                          "bytes_per_launch": kbytes,
-                         "step_bytes": L_ * ab["layer"], "step_gbs": round(step_gbs, 1),
+                         "step_bytes": step_bytes(B), "step_gbs": round(step_gbs, 1),
                          "step_frac": round(step_gbs / hbm, 4)},
             "cpu_baseline": cpu,
             "e2e": {"value": round(e2e, 3), "unit": "tok/s", "h2d_bytes_per_step": B * D_ * 4,
@@ -474,15 +551,18 @@ def run_ours(args, rank, world, local_rank):
 
 
 def main():
-    global L_
     ap = argparse.ArgumentParser()
     ap.add_argument("--gpus", type=int, default=1)
     ap.add_argument("--steps", type=int, default=5000)
     ap.add_argument("--warmup", type=int, default=20)
     ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
-    ap.add_argument("--batch", type=int, default=1)
-    ap.add_argument("--layers", type=int, default=48, help="MoE layers (48 = the Qwen3-30B-A3B stack); fewer only "
-                                                            "for small profiling captures")
+    ap.add_argument("--model", default="qwen3", choices=sorted(MODELS),
+                    help="the MoE stack: qwen3 (Qwen3-30B-A3B, the headline), olmoe (OLMoE-1B-7B), mixtral "
+                         "(Mixtral-8x7B, batch 8 by default), kimi (Kimi-K2: sigmoid grouped router with bias, "
+                         "Q8 shared expert; expert-parallel over >= 4 GPUs for all 60 MoE layers)")
+    ap.add_argument("--batch", type=int, default=None, help="tokens per step (default: the model's configuration)")
+    ap.add_argument("--layers", type=int, default=None, help="MoE layers (default: the model's, or as many as fit "
+                                                              "the GPUs' HBM); fewer for small profiling captures")
     ap.add_argument("--no-cpu", action="store_true", help="skip the CPU baseline leg")
     ap.add_argument("--replicas", action="store_true",
                     help="N > 1: N independent replicas of the stack, one per GPU (weak scaling) instead of the "
@@ -491,8 +571,10 @@ def main():
                     help="instead of the bench line: the persistent kernel's per-phase timeline (mean us per "
                          "layer over CTAs, thread 0's SM clock) as one JSON line")
     args = ap.parse_args()
-    L_ = args.layers
     rank, world, local_rank = dist_env()
+    set_model(args.model, args.layers, 1 if args.replicas else world)
+    if args.batch is None:
+        args.batch = MODELS[args.model]["batch"]
     if world > 1:
         import datetime
         import torch

@@ -652,18 +652,43 @@ extern "C" HXB_API int hxb_moe_synthesize(hxb_moe *m, uint64_t seed, float sigma
     if (!m) return fail(HXB_E_ARG, "synthesize: null handle");
     if (!m->resident_mode) return fail(HXB_E_ARG, "synthesize: needs every expert resident (cache_gb = 0)");
     if (m->cfg.expert_dtype != Q4) return fail(HXB_E_UNSUPPORTED, "synthesize: Q4 experts only");
-    if (m->cfg.shared_ffn_dim) return fail(HXB_E_UNSUPPORTED, "synthesize: no shared expert");
+    if (m->cfg.shared_ffn_dim && m->cfg.shared_dtype != Q4 && m->cfg.shared_dtype != Q8)
+        return fail(HXB_E_UNSUPPORTED, "synthesize: Q4/Q8 shared experts only");
     cudaSetDevice(m->device);
     const hxb_moe_config &k = m->cfg;
-    const int L = k.n_layers, E = k.n_experts, D = k.d_model;
+    const int L = k.n_layers, E = k.n_experts, D = k.d_model, Fs = k.shared_ffn_dim;
     for (int l = 0; l < L; l++) {
         LayerBufs &b = m->layers[(size_t)l];
+        const uint64_t ls = seed * 1000003ull + (uint64_t)l;
+        const size_t shb = Fs ? (size_t)row_bytes(k.shared_dtype, (int64_t)D) * Fs : 0;
+        const size_t shd = Fs ? (size_t)row_bytes(k.shared_dtype, (int64_t)Fs) * D : 0;
         bool ok = b.router.alloc(sizeof(float) * (size_t)E * D) && b.norm.alloc(sizeof(float) * (size_t)D) &&
-                  (!k.score_bias || b.bias.alloc(sizeof(float) * (size_t)E));
+                  (!k.score_bias || b.bias.alloc(sizeof(float) * (size_t)E)) &&
+                  (!Fs || (b.sh_gate.alloc(shb) && b.sh_up.alloc(shb) && b.sh_down.alloc(shd))) &&
+                  (!k.shared_gate || b.sh_gate_inp.alloc(sizeof(float) * (size_t)D));
         if (!ok) return fail(HXB_E_NOMEM, "synthesize: out of device memory");
-        if (!cuda_ok(launch_synth_f32(b.router.as<float>(), (int64_t)E * D, seed * 1000003ull + (uint64_t)l,
-                                      sigma_router, m->stream),
+        if (!cuda_ok(launch_synth_f32(b.router.as<float>(), (int64_t)E * D, ls, sigma_router, m->stream),
                      "synth router"))
+            return HXB_E_DEVICE;
+        // the selection bias (sigmoid routers) at half the router's spread; the shared expert's
+        // matrices like the routed experts'; its gate input like the router
+        if (k.score_bias &&
+            !cuda_ok(launch_synth_f32(b.bias.as<float>(), E, ls ^ 0xb1a5b1a5ull, 0.5f * sigma_router, m->stream),
+                     "synth bias"))
+            return HXB_E_DEVICE;
+        if (Fs && !(cuda_ok(launch_synth_blocks(b.sh_gate.as<uint8_t>(), k.shared_dtype, Fs, D, ls ^ 0x5a1ull,
+                                                sigma_expert, m->stream),
+                            "synth shared gate") &&
+                    cuda_ok(launch_synth_blocks(b.sh_up.as<uint8_t>(), k.shared_dtype, Fs, D, ls ^ 0x5a2ull,
+                                                sigma_expert, m->stream),
+                            "synth shared up") &&
+                    cuda_ok(launch_synth_blocks(b.sh_down.as<uint8_t>(), k.shared_dtype, D, Fs, ls ^ 0x5a3ull,
+                                                sigma_expert, m->stream),
+                            "synth shared down")))
+            return HXB_E_DEVICE;
+        if (k.shared_gate && !cuda_ok(launch_synth_f32(b.sh_gate_inp.as<float>(), D, ls ^ 0x5a4ull, sigma_router,
+                                                       m->stream),
+                                      "synth shared gate input"))
             return HXB_E_DEVICE;
         std::vector<float> ones((size_t)D, 1.0f);
         cudaMemcpy(b.norm.p, ones.data(), sizeof(float) * D, cudaMemcpyHostToDevice);

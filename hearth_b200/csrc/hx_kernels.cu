@@ -841,6 +841,55 @@ cudaError_t launch_synth_q4(uint8_t *dev, int64_t n_slabs, int64_t slab_bytes, i
     return cudaGetLastError();
 }
 
+// A quantized matrix (Q4 or Q8 rows, `n_blocks` consecutive 64-weight blocks) with the statistics of
+// N(0, sigma) weights: Q4 as in k_synth_q4; Q8 values an Irwin-Hall(4) bell of sd ~53 under a scale
+// of sigma/53 (a 64-block of N(0, sigma) has amax ~2.4 sigma, so amax/127 ~ sigma/53). One thread
+// per block.
+__global__ void k_synth_blocks(uint8_t *dev, int64_t n_blocks, int dtype, uint64_t seed, uint32_t scale_bits) {
+    const int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
+    if (i >= n_blocks) return;
+    uint8_t *blk = dev + i * (dtype == Q8 ? Q8_BLOCK : Q4_BLOCK);
+    uint64_t h = splitmix64(seed ^ splitmix64((uint64_t)i));
+    const uint32_t sc = scale_bits + (uint32_t)(h & 0x3f) - 32u;
+    blk[0] = (uint8_t)(sc & 0xff);
+    blk[1] = (uint8_t)(sc >> 8);
+    for (int j = 0; j < (dtype == Q8 ? 64 : 32); j++) {
+        h = splitmix64(h);
+        const int s4 = (int)(h & 0xff) + (int)((h >> 8) & 0xff) + (int)((h >> 16) & 0xff) + (int)((h >> 24) & 0xff);
+        if (dtype == Q8) {
+            int q = ((s4 - 510) * 9 + (s4 >= 510 ? 12 : -12)) / 25;   // ~ round((s4-510)*0.36): sd ~53
+            q = q < -127 ? -127 : (q > 127 ? 127 : q);
+            blk[2 + j] = (uint8_t)(int8_t)q;
+        } else {
+            int lo = 8 + (s4 - 510 + 37 + 740) / 74 - 10;
+            const int s4b = (int)((h >> 32) & 0xff) + (int)((h >> 40) & 0xff) + (int)((h >> 48) & 0xff) +
+                            (int)((h >> 56) & 0xff);
+            int hi = 8 + (s4b - 510 + 37 + 740) / 74 - 10;
+            lo = lo < 0 ? 0 : (lo > 15 ? 15 : lo);
+            hi = hi < 0 ? 0 : (hi > 15 ? 15 : hi);
+            blk[2 + j] = (uint8_t)(lo | (hi << 4));
+        }
+    }
+}
+
+// f16 bits of a positive normal float (truncated mantissa).
+static uint32_t f16_bits_of(float v) {
+    uint32_t fb;
+    std::memcpy(&fb, &v, 4);
+    const int e = (int)((fb >> 23) & 0xff) - 127 + 15;
+    return (uint32_t)(e << 10) | ((fb >> 13) & 0x3ffu);
+}
+
+cudaError_t launch_synth_blocks(uint8_t *dev, int dtype, int64_t rows, int64_t cols, uint64_t seed, float sigma,
+                                cudaStream_t s) {
+    if (dtype != Q4 && dtype != Q8) return cudaErrorInvalidValue;
+    if (rows <= 0 || cols <= 0 || cols % QK) return cudaErrorInvalidValue;
+    const int64_t n = rows * (cols / QK);
+    const uint32_t scale_bits = f16_bits_of(dtype == Q8 ? sigma / 53.0f : sigma * 0.5f);
+    k_synth_blocks<<<(unsigned)((n + 255) / 256), 256, 0, s>>>(dev, n, dtype, seed, scale_bits);
+    return cudaGetLastError();
+}
+
 // f32 ~ N(0, sigma) approximated by Irwin-Hall(4) over bytes, one rounding: (s4 - 510) * (sigma/147.8).
 __global__ void k_synth_f32(float *dev, int64_t n, uint64_t seed, float k) {
     const int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;

@@ -191,6 +191,9 @@ cudaError_t launch_moe_decode(const DecodeParams &p, cudaStream_t s);
 cudaError_t launch_synth_q4(uint8_t *dev, int64_t n_slabs, int64_t slab_bytes, int D, int F, uint64_t seed,
                             float sigma, cudaStream_t s, int64_t first_slab = 0);
 cudaError_t launch_synth_f32(float *dev, int64_t n, uint64_t seed, float sigma, cudaStream_t s);
+// A [rows, cols] Q4 or Q8 matrix (rows of cols/64 blocks) with the statistics of N(0, sigma) weights.
+cudaError_t launch_synth_blocks(uint8_t *dev, int dtype, int64_t rows, int64_t cols, uint64_t seed, float sigma,
+                                cudaStream_t s);
 
 // Device expf restatement over [x0, x0 + n) bit patterns (self-check support).
 cudaError_t launch_expf_bits(uint32_t x0, int64_t n, float *out, cudaStream_t s);

@@ -143,8 +143,11 @@ HXB_API int hxb_moe_set_layer(hxb_moe *m, int layer, const float *router, const 
 /* One routed expert's slab (docs/FORMAT.md §5 layout, nbytes = the slab size) from host memory.
  * The store keeps a pinned host copy (the host tier) and moves it into HBM when needed. */
 HXB_API int hxb_moe_set_expert(hxb_moe *m, int layer, int expert, const void *slab, size_t nbytes);
-/* Benchmarks without a container: deterministic synthetic router (N(0, sigma_router)), unit
- * norms and Q4/Q8 expert slabs for every layer, generated in HBM (every expert resident). */
+/* Benchmarks without a container: deterministic synthetic router (N(0, sigma_router)), selection
+ * bias (N(0, sigma_router / 2), score_bias handles), unit norms, Q4 expert slabs and the Q4/Q8
+ * shared expert (with its gate input) for every layer, generated in HBM (every expert resident).
+ * With expert parallelism each rank generates only the slabs it owns, byte for byte the slabs of
+ * the same seed on one GPU. */
 HXB_API int hxb_moe_synthesize(hxb_moe *m, uint64_t seed, float sigma_router, float sigma_expert);
 HXB_API size_t hxb_moe_slab_bytes(const hxb_moe *m);
 /* Expert (layer, expert) uses the slab of (src_layer, src_expert), which must already be set: the

@@ -317,6 +317,40 @@ int moe_ref_synth_q4(moe_ref *m, uint8_t *dst, int64_t n_slabs, int64_t slab_byt
     return 0;
 }
 
+/* A [rows, cols] Q4 or Q8 matrix with the statistics of N(0, sigma) weights, byte-identical to the
+ * backend's device generator for shared experts (k_synth_blocks): per 64-weight block a jittered
+ * f16 scale (Q4 sigma/2, Q8 sigma/53) and Irwin-Hall(4) values over splitmix64 bytes. */
+int moe_ref_synth_blocks(uint8_t *dst, int dtype, int64_t rows, int64_t cols, uint64_t seed, float sigma) {
+    if ((dtype != ORC_Q4 && dtype != ORC_Q8) || rows <= 0 || cols <= 0 || cols % 64) return -1;
+    const int64_t n = rows * (cols / 64);
+    const int q8 = dtype == ORC_Q8;
+    const uint32_t scale_bits = half_scale_bits(q8 ? 2.0f * (sigma / 53.0f) : sigma);
+    for (int64_t i = 0; i < n; i++) {
+        uint8_t *blk = dst + i * (q8 ? 66 : 34);
+        uint64_t h = smix(seed ^ smix((uint64_t)i));
+        const uint32_t sc = scale_bits + (uint32_t)(h & 0x3f) - 32u;
+        blk[0] = (uint8_t)(sc & 0xff);
+        blk[1] = (uint8_t)(sc >> 8);
+        for (int j = 0; j < (q8 ? 64 : 32); j++) {
+            h = smix(h);
+            const int s4 = (int)(h & 0xff) + (int)((h >> 8) & 0xff) + (int)((h >> 16) & 0xff) + (int)((h >> 24) & 0xff);
+            if (q8) {
+                int q = ((s4 - 510) * 9 + (s4 >= 510 ? 12 : -12)) / 25;
+                q = q < -127 ? -127 : (q > 127 ? 127 : q);
+                blk[2 + j] = (uint8_t)(int8_t)q;
+            } else {
+                const int s4b = (int)((h >> 32) & 0xff) + (int)((h >> 40) & 0xff) + (int)((h >> 48) & 0xff) +
+                                (int)((h >> 56) & 0xff);
+                int lo = 8 + (s4 - 510 + 37 + 740) / 74 - 10, hi = 8 + (s4b - 510 + 37 + 740) / 74 - 10;
+                lo = lo < 0 ? 0 : (lo > 15 ? 15 : lo);
+                hi = hi < 0 ? 0 : (hi > 15 ? 15 : hi);
+                blk[2 + j] = (uint8_t)(lo | (hi << 4));
+            }
+        }
+    }
+    return 0;
+}
+
 /* f32 ~ N(0, sigma): (s4 - 510) * (sigma / 147.8f), one rounding. */
 void moe_ref_synth_f32(float *dst, int64_t n, uint64_t seed, float sigma) {
     const float k = sigma / 147.8f;

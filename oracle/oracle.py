@@ -150,6 +150,8 @@ def moe_ref_lib():
         L.moe_ref_synth_q4.argtypes = [C.c_void_p, C.c_void_p, C.c_int64, C.c_int64, C.c_int, C.c_int, C.c_uint64,
                                        C.c_float]
         L.moe_ref_synth_f32.argtypes = [C.c_void_p, C.c_int64, C.c_uint64, C.c_float]
+        L.moe_ref_synth_blocks.restype = C.c_int
+        L.moe_ref_synth_blocks.argtypes = [C.c_void_p, C.c_int, C.c_int64, C.c_int64, C.c_uint64, C.c_float]
         _moe_ref = L
     return _moe_ref
 
@@ -343,6 +345,14 @@ class MoeRef:
     def synth_f32(self, n: int, seed: int, sigma: float) -> np.ndarray:
         out = np.empty(n, np.float32)
         self.L.moe_ref_synth_f32(out.ctypes.data, n, seed, sigma)
+        return out
+
+    def synth_blocks(self, dtype: int, rows: int, cols: int, seed: int, sigma: float) -> np.ndarray:
+        """A [rows, row_bytes] Q4/Q8 matrix byte-identical to the backend's device generator of shared
+        experts (hxb_moe_synthesize)."""
+        out = np.empty((rows, row_bytes(dtype, cols)), np.uint8)
+        if self.L.moe_ref_synth_blocks(out.ctypes.data, dtype, rows, cols, seed, sigma):
+            raise ValueError("moe_ref_synth_blocks failed")
         return out
 
     def close(self):
