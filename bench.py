@@ -44,11 +44,14 @@ SIGMA = 0.02
 # seed is the configuration's). qwen3 is the headline workload; the others are --model modes.
 MODELS = {
     "qwen3": dict(name="qwen3-30b-a3b", layers=48, D=2048, F=768, E=128, K=8, seed=2, batch=1,
-                  route=dict(score_fn=0, norm_topk_prob=1)),
+                  route=dict(score_fn=0, norm_topk_prob=1),
+                  dense=dict(vocab_size=151936, n_heads=32, n_kv_heads=4, head_dim=128, qk_norm=1, rope_theta=1e6)),
     "olmoe": dict(name="olmoe-1b-7b", layers=16, D=2048, F=1024, E=64, K=8, seed=1, batch=1,
-                  route=dict(score_fn=0, norm_topk_prob=0)),
+                  route=dict(score_fn=0, norm_topk_prob=0),
+                  dense=dict(vocab_size=50304, n_heads=16, n_kv_heads=16, head_dim=128, qk_norm=2, rope_theta=1e4)),
     "mixtral": dict(name="mixtral-8x7b", layers=32, D=4096, F=14336, E=8, K=2, seed=3, batch=8,
-                    route=dict(score_fn=0, norm_topk_prob=1)),
+                    route=dict(score_fn=0, norm_topk_prob=1),
+                    dense=dict(vocab_size=32000, n_heads=32, n_kv_heads=8, head_dim=128, qk_norm=0, rope_theta=1e6)),
     # Kimi-K2 / DeepSeek-V3: 60 MoE layers (the first of 61 is dense), sigmoid scores + selection
     # bias, 8 groups keep 4, routed_scale 2.827, one Q8 shared expert of width 2048
     "kimi": dict(name="kimi-k2", layers=60, D=7168, F=2048, E=384, K=8, seed=4, batch=1, Fs=2048,
@@ -411,6 +414,107 @@ def run_ep(args, rank, world, local_rank):
     be.close()
 
 
+def full_bytes_per_token(pos):
+    """Algorithmic bytes of one decode token through the whole decoder at position pos: the MoE
+    stack's (step_bytes(1)), the attention projections and the LM head in Q8 (FORMAT §6 rows), the
+    embedding row, the norms, and the KV rows read (f32 k and v of positions 0..pos) and written."""
+    d = MODELS[MODEL]["dense"]
+    q8 = lambda n: 66 * n // 64
+    qd, kvd = d["n_heads"] * d["head_dim"], d["n_kv_heads"] * d["head_dim"]
+    attn = (qd + 2 * kvd) * q8(D_) + D_ * q8(qd) + 4 * D_
+    head = d["vocab_size"] * q8(D_) + 4 * D_
+    kv = 2 * kvd * 4 * (pos + 1)
+    return dict(moe=step_bytes(1), attn=L_ * attn, head=head + q8(D_), kv=L_ * kv,
+                total=step_bytes(1) + L_ * (attn + kv) + head + q8(D_))
+
+
+def run_full(args, rank, world, local_rank):
+    """The whole decoder (configuration 3 of the benchmark: a 512-token prompt, then decode steps at
+    batch 1): embedding, 48 layers of GQA attention with the KV cache and the MoE stack, LM head,
+    all on one GPU (hxb_model_synthesize weights). One step = one decode token at positions
+    512..1023 (cycling), its logits written to HBM; e2e = the same through hxb_model_forward with host
+    ids and logits."""
+    import torch
+    import hearth_b200 as hb
+    torch.cuda.set_device(local_rank)
+    dev = torch.device("cuda", local_rank)
+    d = MODELS[MODEL]["dense"]
+    P0, SEQ = 512, 1024
+    m = hb.Model.synthesize(seed=SEED, device=local_rank, max_batch=P0, max_seq=SEQ, **d, **backend_kw())
+    V = d["vocab_size"]
+    g = torch.Generator(device=dev).manual_seed(1000 + rank)
+    prompt = torch.randint(0, V, (P0,), generator=g, device=dev, dtype=torch.int32)
+    pool = torch.randint(0, V, (64, 1), generator=g, device=dev, dtype=torch.int32)
+    logits = torch.empty((1, V), device=dev, dtype=torch.float32)
+    stream = torch.cuda.current_stream(dev)
+    # prefill, timed once after a warm pass
+    m.forward_dev(prompt, 0, 0, stream=stream)
+    m.sync(stream)
+    p0, p1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    p0.record(stream)
+    m.forward_dev(prompt, 0, 0, stream=stream)
+    p1.record(stream)
+    m.sync(stream)
+    prefill_ms = p0.elapsed_time(p1)
+    for i in range(max(args.warmup, 3)):
+        m.forward_dev(pool[i % 64], P0 + i % (SEQ - P0), 1, logits, stream=stream)
+    m.sync(stream)
+    clocks = Clocks(local_rank)
+    clocks.start()
+    time.sleep(0.3)
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e0.record(stream)
+    for i in range(args.steps):
+        m.forward_dev(pool[i % 64], P0 + i % (SEQ - P0), 1, logits, stream=stream)
+    e1.record(stream)
+    m.sync(stream)
+    ms = e0.elapsed_time(e1)
+    clk = clocks.stop()
+    value = args.steps / (ms / 1000.0)
+    assert torch.isfinite(logits).all().item()
+    # end to end: host ids in, host logits out, every step
+    n_e2e = min(args.steps, 1000)
+    host_tok = np.random.default_rng(7).integers(0, V, size=64).astype(np.int32)
+    out = np.empty(V, np.float32)
+    t0 = time.perf_counter()
+    for i in range(n_e2e):
+        out = m.forward(host_tok[i % 64:i % 64 + 1], P0 + i % (SEQ - P0), 1)
+    t_e2e = time.perf_counter() - t0
+    hbm, peak_kind = peaks()
+    npos = min(args.steps, SEQ - P0)
+    mean_pos = P0 + (npos - 1) / 2.0
+    fb = full_bytes_per_token(int(mean_pos))
+    gbs = fb["total"] / (ms / args.steps * 1e-3) / 1e9
+    # embedding; per layer rmsnorm(+act), q, k, v, post, scores, softmax+values, act, o, residual and
+    # the MoE layer (one persistent launch, or four per-phase kernels); norm, LM head, scale, position
+    moe_launches = 1 if hb.lib().hxb_moe_decode_path(hb.lib().hxb_model_moe(m.h)) == 1 else 4
+    launches = 1 + L_ * (10 + moe_launches) + 4
+    line = {"metric": "Q4 MoE decode tok/s, whole decoder (Qwen3-30B-A3B shape); HBM GB/s of expert+dense+KV bytes",
+            "value": round(value, 3), "unit": "tok/s", "n_gpus": 1, "steps": args.steps, "warmup": args.warmup,
+            "ms_per_step": round(ms / args.steps, 5), "higher_is_better": True, "scaling": "weak",
+            "vs_baseline": None, "dtype": "q4/q8xq8-int32+f32", "data": "synthetic",
+            "config": {"workload": f"{MODELS[MODEL]['name']} whole decoder: {P0}-token prompt, then decode steps at "
+                                   f"positions {P0}..{SEQ - 1} (cycling), batch 1",
+                       "layers": L_, "d_model": D_, "n_heads": d["n_heads"], "n_kv_heads": d["n_kv_heads"],
+                       "head_dim": d["head_dim"], "vocab": V, "experts": E_, "top_k": K_, "expert_ffn_dim": F_,
+                       "parallelism": "single GPU",
+                       "l2": f"no flush: each step reads ~{fb['total'] / 1e9:.2f} GB (> 126 MB L2)",
+                       "weights": "synthetic: the library's device generator (Q8 dense, Q4 experts, f32 routers)"},
+            "roofline": {"bound": "hbm", "achieved": round(gbs, 1), "peak": hbm, "unit": "GB/s",
+                         "frac": round(gbs / hbm, 4), "traffic": None, "peak_kind": peak_kind,
+                         "kernel": "the whole decode step (one CUDA graph: embedding, attention, MoE, LM head)",
+                         "bytes_per_step": fb, "mean_position": mean_pos},
+            "prefill": {"tokens": P0, "ms": round(prefill_ms, 3), "tok_s": round(P0 / prefill_ms * 1000.0, 1)},
+            "cpu_baseline": None,
+            "cpu_baseline_note": "the reference engine needs a container of this model (17 GB) that is not written "
+                                 "on the GPU box; its CPU decode of the MoE stack is the headline line's baseline",
+            "e2e": {"value": round(n_e2e / t_e2e, 3), "unit": "tok/s", "h2d_bytes_per_step": 4,
+                    "d2h_bytes_per_step": 4 * V, "timing": "host clock around synchronous hxb_model_forward"},
+            "gpu_launches": launches * args.steps, "clocks": clk}
+    print(json.dumps(line), flush=True)
+    m.close()
+
+
 def run_ours(args, rank, world, local_rank):
     import torch
     import hearth_b200 as hb
@@ -567,6 +671,9 @@ def main():
     ap.add_argument("--replicas", action="store_true",
                     help="N > 1: N independent replicas of the stack, one per GPU (weak scaling) instead of the "
                          "default expert parallelism (one token stream, expert e on rank e %% N: strong scaling)")
+    ap.add_argument("--full", action="store_true",
+                    help="the whole decoder (embedding, GQA attention + KV cache, MoE, LM head) of qwen3 / olmoe / "
+                         "mixtral on one GPU, decode steps after a 512-token prompt")
     ap.add_argument("--trace", action="store_true",
                     help="instead of the bench line: the persistent kernel's per-phase timeline (mean us per "
                          "layer over CTAs, thread 0's SM clock) as one JSON line")
@@ -586,6 +693,13 @@ def main():
         if args.trace:
             if rank == 0:
                 run_trace(args, local_rank)
+        elif args.full:
+            if args.impl == "reference":
+                if rank == 0:
+                    print(json.dumps({"impl": "reference", "unavailable": "the reference engine needs a container of "
+                                                                          "the whole model, not written on the GPU box"}))
+            elif rank == 0:
+                run_full(args, rank, world, local_rank)
         elif args.impl == "reference":
             run_reference(args, rank, world)
         elif world > 1 and not args.replicas:

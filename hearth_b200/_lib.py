@@ -15,8 +15,8 @@ F32, F16, BF16, Q8, Q4 = 0, 1, 2, 3, 4
 POLICY_LRU, POLICY_LFU = 0, 1
 SCORE_SOFTMAX, SCORE_SIGMOID = 0, 1
 
-HXB_OK, HXB_E_ARG, HXB_E_CAPACITY, HXB_E_IO, HXB_E_NOMEM, HXB_E_FORMAT, HXB_E_DEVICE, HXB_E_UNSUPPORTED = \
-    0, -1, -3, -4, -5, -6, -7, -8
+HXB_OK, HXB_E_ARG, HXB_E_TOKEN, HXB_E_CAPACITY, HXB_E_IO, HXB_E_NOMEM, HXB_E_FORMAT, HXB_E_DEVICE, \
+    HXB_E_UNSUPPORTED = 0, -1, -2, -3, -4, -5, -6, -7, -8
 
 # every symbol the header declares (checked by the CPU tests)
 EXPORTS = [
@@ -28,7 +28,9 @@ EXPORTS = [
     "hxb_moe_is_resident", "hxb_moe_tick", "hxb_moe_prefetch", "hxb_moe_seed_heat", "hxb_moe_set_copy_hook",
     "hxb_moe_sync", "hxb_moe_profile", "hxb_matmul_noalloc", "hxb_moe_phase_trace", "hxb_moe_decode_path",
     "hxb_moe_ep_layer_dev", "hxb_moe_ep_combine_dev", "hxb_container_probe", "hxb_moe_load_container",
-    "hxb_moe_share_expert",
+    "hxb_moe_share_expert", "hxb_model_default_options", "hxb_model_open", "hxb_model_close", "hxb_model_info",
+    "hxb_model_forward", "hxb_model_last_routes", "hxb_model_set_replay", "hxb_model_moe", "hxb_model_synthesize",
+    "hxb_model_forward_dev", "hxb_model_sync",
 ]
 
 
@@ -40,6 +42,17 @@ class MoeConfig(C.Structure):
                 ("shared_ffn_dim", C.c_int), ("shared_dtype", C.c_int), ("shared_gate", C.c_int),
                 ("max_tokens", C.c_int), ("cache_gb", C.c_double), ("policy", C.c_int), ("heat_decay", C.c_float),
                 ("device", C.c_int), ("ep_size", C.c_int), ("ep_rank", C.c_int), ("prefetch_next", C.c_int)]
+
+
+class ModelOptions(C.Structure):
+    _fields_ = [("device", C.c_int), ("max_batch", C.c_int), ("max_seq", C.c_int), ("cache_gb", C.c_double),
+                ("policy", C.c_int)]
+
+
+class ModelArch(C.Structure):
+    _fields_ = [("vocab_size", C.c_int), ("n_heads", C.c_int), ("n_kv_heads", C.c_int), ("head_dim", C.c_int),
+                ("qk_norm", C.c_int), ("rope_theta", C.c_float), ("dense_dtype", C.c_int), ("sigma_dense", C.c_float),
+                ("moe", MoeConfig)]
 
 
 class ContainerInfo(C.Structure):
@@ -114,6 +127,17 @@ def lib() -> C.CDLL:
         "hxb_container_probe": (i, [C.c_char_p, C.POINTER(MoeConfig), C.POINTER(ContainerInfo), C.c_char_p, sz]),
         "hxb_moe_load_container": (i, [vp, C.c_char_p]),
         "hxb_moe_share_expert": (i, [vp, i, i, i, i]),
+        "hxb_model_default_options": (None, [C.POINTER(ModelOptions)]),
+        "hxb_model_open": (vp, [C.c_char_p, C.POINTER(ModelOptions), C.c_char_p, sz]),
+        "hxb_model_close": (None, [vp]),
+        "hxb_model_info": (i, [vp, vp, vp, vp, vp, vp, vp]),
+        "hxb_model_forward": (i, [vp, vp, i, i, vp, i]),
+        "hxb_model_last_routes": (i, [vp, vp, i]),
+        "hxb_model_set_replay": (i, [vp, vp, i]),
+        "hxb_model_moe": (vp, [vp]),
+        "hxb_model_forward_dev": (i, [vp, vp, i, i, vp, i, vp]),
+        "hxb_model_sync": (i, [vp, vp]),
+        "hxb_model_synthesize": (vp, [C.POINTER(ModelArch), C.POINTER(ModelOptions), C.c_uint64, C.c_char_p, sz]),
     }
     for name, (res, args) in sig.items():
         fn = getattr(L, name)

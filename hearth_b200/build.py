@@ -16,8 +16,9 @@ HERE = os.path.dirname(os.path.abspath(__file__))
 REPO = os.path.dirname(HERE)
 CSRC = os.path.join(HERE, "csrc")
 LIB = os.path.join(HERE, "libhearth_b200.so")
-SOURCES = ["hx_kernels.cu", "hx_decode.cu", "hx_prefill_tc.cu", "hx_capi.cu", "hx_store.cpp", "hx_noalloc.cu", "hx_container.cpp"]
-HEADERS = ["hx_common.cuh", "hx_device.cuh", "hx_kernels.h", "hx_store.h", "hx_route.cuh", "hx_moe_job.cuh", "hx_container.h"]
+SOURCES = ["hx_kernels.cu", "hx_decode.cu", "hx_prefill_tc.cu", "hx_capi.cu", "hx_store.cpp", "hx_noalloc.cu", "hx_container.cpp", "hx_model.cu"]
+HEADERS = ["hx_common.cuh", "hx_device.cuh", "hx_kernels.h", "hx_store.h", "hx_route.cuh", "hx_moe_job.cuh", "hx_container.h",
+           "hx_moe_internal.h"]
 NVCC_FLAGS = ["-gencode", "arch=compute_100a,code=sm_100a", "-O3", "-std=c++17", "-fmad=false", "-lineinfo",
               "-Xcompiler", "-fPIC", "-Xcompiler", "-fvisibility=hidden", "-Xcompiler", "-ffp-contract=off",
               "-shared"]

@@ -5,6 +5,7 @@
 #include "hx_kernels.h"
 #include "hx_store.h"
 #include "hx_container.h"
+#include "hx_moe_internal.h"
 
 #include <algorithm>
 #include <chrono>
@@ -1048,6 +1049,40 @@ extern "C" HXB_API int hxb_moe_forward_routed(hxb_moe *m, float *h, int T, int l
     m->last_T = T;
     return HXB_OK;
 }
+
+// ---- inside the library: the MoE layers of a whole-model handle (hx_model.cu)
+
+namespace hx {
+
+int moe_layer_for_model(hxb_moe *m, float *h, int T, int l, cudaStream_t s, const int *forced) {
+    int rc = check_eval(m, T, l, 1);
+    if (rc) return rc;
+    if (m->cfg.ep_size > 1) return fail(HXB_E_UNSUPPORTED, "whole-model evaluation on an expert-parallel handle");
+    if (m->resident_mode) {
+        if (m->use_decode && T == 1 && !forced) {
+            if (!refresh_decode_tables(m)) return HXB_E_DEVICE;
+            if (!cuda_ok(enqueue_decode(m, h, l, 1, s), "decode launch")) return HXB_E_DEVICE;
+        } else {
+            MoeScratch sc = m->scratch();
+            sc.forced_ids = forced;
+            if (!cuda_ok(launch_moe_layer(m->shape(T), m->layer_dev(l, true), sc, h, nullptr, true, s), "moe layer"))
+                return HXB_E_DEVICE;
+        }
+    } else {
+        rc = run_streaming(m, h, nullptr, T, l, 1, true, true, s, forced);
+        if (rc != HXB_OK) return rc;
+    }
+    m->st.expert_uses += (uint64_t)T * (uint64_t)m->cfg.top_k;
+    m->last_T = T;
+    return HXB_OK;
+}
+
+const int *moe_ids_dev(const hxb_moe *m) { return m->ids.as<int>(); }
+bool moe_resident(const hxb_moe *m) { return m->resident_mode; }
+const int *moe_err_dev(const hxb_moe *m) { return m->err.as<int>(); }
+int moe_take_error(hxb_moe *m, int word) { return take_device_error(m, word); }
+
+}  // namespace hx
 
 extern "C" HXB_API int hxb_moe_layer(hxb_moe *m, int layer, const float *x, int T, float *out) {
     int rc = check_eval(m, T, layer, 1);

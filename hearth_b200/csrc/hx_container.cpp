@@ -1,6 +1,8 @@
 // hx_container.cpp — `.hearth` container reader for the MoE path (see hx_container.h).
 #include "hx_container.h"
 
+#include <cmath>
+
 #include <algorithm>
 #include <cerrno>
 #include <cstdarg>
@@ -232,6 +234,34 @@ bool ContainerFile::parse(std::string &err) {
     if (!c.n_layers || !c.d_model || !c.vocab_size || !c.n_heads) {
         err = "n_layers, d_model, vocab_size and n_heads must be positive";
         return false;
+    }
+    // attention and dense keys (engine/src/modelfile.c:235-290): GQA / MHA only here; an MLA
+    // container keeps attn_kind 1 and is refused by the whole-model handle, not by the reader
+    {
+        uint32_t qk_rope = 0;
+        if (!get_u32("max_seq", 4096, false, c.max_seq) || !get_u32("attn_kind", 0, false, c.attn_kind) ||
+            !get_u32("n_kv_heads", c.n_heads, false, c.n_kv_heads) ||
+            !get_u32("head_dim", c.d_model / c.n_heads, false, c.head_dim) ||
+            !get_u32("qk_norm", 0, false, c.qk_norm) || !get_u32("qkv_bias", 0, false, c.qkv_bias) ||
+            !get_u32("qk_rope_dim", 0, false, qk_rope) || !get_u32("rope_style", 0, false, c.rope_style) ||
+            !get_u32("dense_ffn_dim", 0, false, c.dense_ffn_dim) ||
+            !get_u32("tie_embeddings", 0, false, c.tie_embeddings) ||
+            !get_f32("rope_attn_factor", 1.0f, c.rope_attn_factor) || !get_f32("emb_scale", 1.0f, c.emb_scale) ||
+            !get_f32("logit_scale", 1.0f, c.logit_scale))
+            return false;
+        const uint32_t rope_cap = c.attn_kind == 1 ? qk_rope : c.head_dim;
+        if (!get_u32("rope_dim", rope_cap, false, c.rope_dim)) return false;
+        if (c.attn_kind == 0) {
+            if (!c.head_dim || !c.n_kv_heads || c.n_heads % c.n_kv_heads || c.qk_norm > 2 || c.rope_dim > c.head_dim ||
+                c.rope_dim % 2 || c.rope_style > 1) {
+                err = "attention keys out of range (head_dim, n_kv_heads, qk_norm, rope_dim, rope_style)";
+                return false;
+            }
+            // float arithmetic, as hearth.format.apply_defaults and modelfile.c compute it
+            if (!get_f32("attn_scale", 1.0f / sqrtf((float)c.head_dim), c.attn_scale)) return false;
+        } else if (!get_f32("attn_scale", 1.0f, c.attn_scale)) {
+            return false;
+        }
     }
     {
         auto it = meta.find("layer_kind");

@@ -31,6 +31,10 @@ struct Container {
     uint32_t n_experts = 0, top_k = 0, expert_ffn_dim = 0, shared_ffn_dim = 0, shared_gate = 0;
     uint32_t score_fn = 0, score_bias = 0, n_group = 1, topk_group = 1, norm_topk_prob = 0;
     float norm_eps = 1e-6f, routed_scale = 1.0f, residual_scale = 1.0f;
+    // the rest of the decoder (FORMAT §3.1 keys, defaults applied as engine/src/modelfile.c does)
+    uint32_t max_seq = 4096, attn_kind = 0, n_kv_heads = 0, head_dim = 0, qk_norm = 0, qkv_bias = 0;
+    uint32_t rope_dim = 0, rope_style = 0, dense_ffn_dim = 0, tie_embeddings = 0;
+    float rope_attn_factor = 1.0f, attn_scale = 1.0f, emb_scale = 1.0f, logit_scale = 1.0f;
     std::vector<uint8_t> layer_kind;   // per layer: 0 dense FFN, 1 MoE
     std::vector<CtTensor> tensors;
     std::unordered_map<std::string, size_t> by_name;

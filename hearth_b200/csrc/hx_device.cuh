@@ -88,6 +88,34 @@ __device__ __forceinline__ bool mbar_wait(uint64_t *bar, uint32_t parity, int *e
 // activation rows (nb blocks each) start at act + tok_off[i]. Writes the canonical value of
 // (rlist[k], token i) to out[k * ok + i * oi]. Blocks are taken 32 at a time; the chain lane keeps
 // its running sum across those chunks, so P holds nr * nt * 33 floats whatever nb is. nr * nt <= 32.
+// d * (float)q with the NaN results of the host's SSE multiply, which the reference's dequantize
+// stores unmodified: a NaN scale comes back as itself (already quiet after the f16 decode) and
+// inf * 0 gives the x86 default NaN 0xffc00000. GPU arithmetic would return its own canonical NaN.
+__device__ __forceinline__ float x86_mul_scale(float d, int q) {
+    if (d != d) return d;
+    if (q == 0 && fabsf(d) == __uint_as_float(0x7f800000u)) return __uint_as_float(0xffc00000u);
+    return __fmul_rn(d, (float)q);
+}
+
+// Element c of a row of any dtype, as hx_dequantize_row (engine/src/quant.c:257-307) produces it.
+__device__ __forceinline__ float dequant_elem(int dtype, const uint8_t *row, int64_t c) {
+    switch (dtype) {
+    case F32: return reinterpret_cast<const float *>(row)[c];
+    case F16: return f16_to_f32(reinterpret_cast<const uint16_t *>(row)[c]);
+    case BF16: return bf16_to_f32(reinterpret_cast<const uint16_t *>(row)[c]);
+    case Q8: {
+        const uint8_t *blk = row + (c / QK) * Q8_BLOCK;
+        return x86_mul_scale(f16_to_f32((uint32_t)blk[0] | ((uint32_t)blk[1] << 8)), (int)(int8_t)blk[2 + c % QK]);
+    }
+    default: {
+        const uint8_t *blk = row + (c / QK) * Q4_BLOCK;
+        const int j = (int)(c % QK);
+        const int nib = j < 32 ? (blk[2 + j] & 15) : (blk[2 + j - 32] >> 4);
+        return x86_mul_scale(f16_to_f32((uint32_t)blk[0] | ((uint32_t)blk[1] << 8)), nib - 8);
+    }
+    }
+}
+
 template <int DT>
 __device__ __forceinline__ void warp_rows(const uint8_t *tile, int64_t rb, int nb, const int *rlist, int nr,
                                           const act_q8 *act, const int *tok_off, int nt, float *P, float *out,

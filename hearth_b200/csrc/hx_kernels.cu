@@ -137,41 +137,13 @@ cudaError_t launch_matmul(int dtype, const void *W, int64_t n_cols, const void *
     return cudaGetLastError();
 }
 
-// d * (float)q with the NaN results of the host's SSE multiply, which the reference's dequantize
-// stores unmodified: a NaN scale comes back as itself (already quiet after the f16 decode) and
-// inf * 0 gives the x86 default NaN 0xffc00000. GPU arithmetic would return its own canonical NaN.
-__device__ __forceinline__ float x86_mul_scale(float d, int q) {
-    if (d != d) return d;
-    if (q == 0 && fabsf(d) == __uint_as_float(0x7f800000u)) return __uint_as_float(0xffc00000u);
-    return __fmul_rn(d, (float)q);
-}
-
-// hearth_dequantize (engine/src/quant.c:257-307): w = f16(d) * q, one element per thread.
+// hearth_dequantize (engine/src/quant.c:257-307): one element per thread.
 __global__ void k_dequantize(int dtype, const uint8_t *__restrict__ W, int64_t n_rows, int64_t n_cols, int64_t rb,
                              float *__restrict__ out) {
     const int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
     if (i >= n_rows * n_cols) return;
     const int64_t r = i / n_cols, c = i - r * n_cols;
-    const uint8_t *row = W + r * rb;
-    float v;
-    switch (dtype) {
-    case F32: v = reinterpret_cast<const float *>(row)[c]; break;
-    case F16: v = f16_to_f32(reinterpret_cast<const uint16_t *>(row)[c]); break;
-    case BF16: v = bf16_to_f32(reinterpret_cast<const uint16_t *>(row)[c]); break;
-    case Q8: {
-        const uint8_t *blk = row + (c / QK) * Q8_BLOCK;
-        v = x86_mul_scale(f16_to_f32((uint32_t)blk[0] | ((uint32_t)blk[1] << 8)), (int)(int8_t)blk[2 + c % QK]);
-        break;
-    }
-    default: {
-        const uint8_t *blk = row + (c / QK) * Q4_BLOCK;
-        const int j = (int)(c % QK);
-        const int nib = j < 32 ? (blk[2 + j] & 15) : (blk[2 + j - 32] >> 4);
-        v = x86_mul_scale(f16_to_f32((uint32_t)blk[0] | ((uint32_t)blk[1] << 8)), nib - 8);
-        break;
-    }
-    }
-    out[i] = v;
+    out[i] = dequant_elem(dtype, W + r * rb, c);
 }
 
 cudaError_t launch_dequantize(int dtype, const void *W, int64_t n_rows, int64_t n_cols, float *out,

@@ -36,6 +36,7 @@ extern "C" {
 enum {
     HXB_OK = 0,
     HXB_E_ARG = -1,          /* HX_E_ARG */
+    HXB_E_TOKEN = -2,        /* HX_E_TOKEN: a token id outside [0, vocab_size) */
     HXB_E_CAPACITY = -3,     /* HX_E_CAPACITY: more tokens than the handle was opened for */
     HXB_E_IO = -4,           /* HX_E_IO: an expert could not be brought into HBM */
     HXB_E_NOMEM = -5,        /* HX_E_NOMEM */
@@ -261,6 +262,72 @@ HXB_API int hxb_moe_seed_heat(hxb_moe *m, const float *counts, int n_keys, float
  * before every host->HBM expert copy; a nonzero return fails that copy. NULL removes it. */
 typedef int (*hxb_copy_hook)(void *ctx, int layer, int expert);
 HXB_API void hxb_moe_set_copy_hook(hxb_moe *m, hxb_copy_hook fn, void *ctx);
+
+/* ---- the whole decoder on the GPU -----------------------------------------------------------
+ * forward() of engine/src/model.c:1171-1236 for GQA / MHA containers (attn_kind 0; MLA containers
+ * are refused with HXB_E_UNSUPPORTED): the embedding row times emb_scale; per layer
+ * x = rmsnorm(h, attn_norm), q/k/v projections (+ biases), qk-norm per head or full width, RoPE
+ * (cos/sin tables computed on the host with its libm, as rope_tables, model.c:386-397), the (k, v)
+ * rows appended to an f32 KV cache [layer][kv head][position][head_dim] in HBM, attention per head
+ * (dot16 scores times attn_scale, softmax, the value sum in position order; model.c:484-629),
+ * the o projection, h += residual_scale * out; then x = rmsnorm(h, ffn_norm) and the MoE layer (the
+ * hxb_moe path above: routing, experts, rank-order sum) or the dense SwiGLU FFN (model.c:444-460,
+ * 1133-1143), h += residual_scale * out; finally rmsnorm(h, out_norm), the LM head and logit_scale.
+ * Every value follows the canonical order of docs/NUMERICS.md, so the logits equal hearth_eval's bit
+ * for bit on the same host. Dense matrices may be F32, F16, BF16, Q8 or Q4; experts Q4 or Q8. */
+typedef struct hxb_model hxb_model;
+typedef struct hxb_model_options {
+    int device;        /* CUDA device ordinal */
+    int max_batch;     /* tokens per forward call (0: 512) */
+    int max_seq;       /* KV cache positions (0: the container's max_seq) */
+    double cache_gb;   /* HBM budget for expert slots in GiB (0: every expert resident) */
+    int policy;        /* expert store policy (HEARTH_POLICY_LRU / LFU) */
+} hxb_model_options;
+HXB_API void hxb_model_default_options(hxb_model_options *o);
+/* Opens the container at path: every dense tensor and expert slab goes to HBM (experts through the
+ * store, as hxb_moe_load_container). NULL with a message in err on failure. */
+HXB_API hxb_model *hxb_model_open(const char *path, const hxb_model_options *o, char *err, size_t errlen);
+HXB_API void hxb_model_close(hxb_model *m);
+/* n_layers, d_model, vocab_size, KV positions, MoE layers, top_k (any pointer may be NULL). */
+HXB_API int hxb_model_info(const hxb_model *m, int *n_layers, int *d_model, int *vocab, int *max_seq,
+                           int *n_moe_layers, int *top_k);
+/* forward(m, tok, T, pos0, logits, mode) (model.c:1171): T tokens (host ids) at positions
+ * pos0 .. pos0+T-1, their (k, v) rows written into the cache; mode 0 no logits, 1 the last token's
+ * logits[V], 2 every token's logits[T][V] (host). HXB_E_TOKEN for an id outside the vocabulary,
+ * HXB_E_CAPACITY beyond max_batch or max_seq. Synchronous. */
+HXB_API int hxb_model_forward(hxb_model *m, const int32_t *tokens, int T, int pos0, float *logits, int mode);
+/* forward() on device buffers, asynchronous on stream (NULL: the handle's own stream): tokens [T]
+ * (device ids; an id outside the vocabulary gives a NaN embedding row instead of HXB_E_TOKEN),
+ * logits [1 or T][V] (device, or NULL for mode 0). Every expert must be resident. A single-token
+ * forward replays a CUDA graph of the whole decoder after its first use. Errors of the device work
+ * (the MoE layers' error word) are reported by hxb_model_sync. */
+HXB_API int hxb_model_forward_dev(hxb_model *m, const int32_t *tokens, int T, int pos0, float *logits, int mode,
+                                  void *stream);
+HXB_API int hxb_model_sync(hxb_model *m, void *stream);
+/* The last forward's routing in the layout of model.c's routes[] (the FORMAT §9 trace rows): per
+ * token, MoE layer by MoE layer, the K expert ids in rank order: routes[T][n_moe_layers * K]. */
+HXB_API int hxb_model_last_routes(hxb_model *m, uint16_t *routes, int T);
+/* Route replay (hearth_route_replay, model.c:1003-1009): the MoE layers of later forwards take the
+ * ids of row (pos mod n_rows) of rows[n_rows][n_moe_layers * K] instead of their own selection (the
+ * scores and weights computed as usual). rows NULL stops the replay. */
+HXB_API int hxb_model_set_replay(hxb_model *m, const uint16_t *rows, int n_rows);
+/* The MoE backend handle inside (statistics, store control); owned by the model. */
+HXB_API hxb_moe *hxb_model_moe(hxb_model *m);
+/* Benchmarks without a container: a decoder whose every layer is MoE, generated in HBM from seed.
+ * Attention, embedding and LM head matrices in dense_dtype (Q8 or Q4) with the statistics of
+ * N(0, sigma_dense) weights (the embedding N(0, 1)), unit norms, RoPE over the whole head with
+ * inv_freq[j] = rope_theta^(-2j / head_dim); the MoE layers as hxb_moe_synthesize(seed). No
+ * counterpart in the reference (its synthetic models are containers written by synth.py). */
+typedef struct hxb_model_arch {
+    int vocab_size, n_heads, n_kv_heads, head_dim;
+    int qk_norm;            /* 0 none, 1 per head, 2 full width */
+    float rope_theta;
+    int dense_dtype;        /* HEARTH_Q8 or HEARTH_Q4 */
+    float sigma_dense;
+    hxb_moe_config moe;     /* the MoE layers: n_layers, d_model, routing, experts (every expert resident) */
+} hxb_model_arch;
+HXB_API hxb_model *hxb_model_synthesize(const hxb_model_arch *a, const hxb_model_options *o, uint64_t seed,
+                                        char *err, size_t errlen);
 
 #ifdef __cplusplus
 }

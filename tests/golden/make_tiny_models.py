@@ -12,6 +12,8 @@ Fixtures (3 layers, d_model 128, 8 experts of width 64, top-2, vocab 256, max_se
   tiny_olmoe.hearth      MHA, full-width qk-norm, softmax without renormalisation; Q4 / Q8
   tiny_mixtral.hearth    GQA 4/2, no qk-norm; Q4 / Q8
   tiny_qwen2_moe.hearth  GQA 4/2, q/k/v biases, gated shared expert; Q8 experts and dense
+  tiny_deepseek_v3.hearth  MLA attention (q-lora, kv-lora, GPT-J RoPE), a dense first layer, grouped
+                         sigmoid routing with bias, shared expert; Q4 / Q8
 """
 import argparse
 import os
@@ -20,7 +22,8 @@ import sys
 HERE = os.path.dirname(os.path.abspath(__file__))
 REPO = os.path.dirname(os.path.dirname(HERE))
 
-FIXTURES = [("qwen3_moe", "Q4", 11), ("olmoe", "Q4", 12), ("mixtral", "Q4", 13), ("qwen2_moe", "Q8", 14)]
+FIXTURES = [("qwen3_moe", "Q4", 11), ("olmoe", "Q4", 12), ("mixtral", "Q4", 13), ("qwen2_moe", "Q8", 14),
+            ("deepseek_v3", "Q4", 15)]
 
 
 def main():
