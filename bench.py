@@ -485,10 +485,10 @@ def run_full(args, rank, world, local_rank):
     mean_pos = P0 + (npos - 1) / 2.0
     fb = full_bytes_per_token(int(mean_pos))
     gbs = fb["total"] / (ms / args.steps * 1e-3) / 1e9
-    # embedding; per layer rmsnorm(+act), q, k, v, post, scores, softmax+values, act, o, residual and
+    # embedding; per layer rmsnorm(+act), q|k|v, post, scores, softmax+values(+act), o(+residual) and
     # the MoE layer (one persistent launch, or four per-phase kernels); norm, LM head, scale, position
     moe_launches = 1 if hb.lib().hxb_moe_decode_path(hb.lib().hxb_model_moe(m.h)) == 1 else 4
-    launches = 1 + L_ * (10 + moe_launches) + 4
+    launches = 1 + L_ * (6 + moe_launches) + 4
     line = {"metric": "Q4 MoE decode tok/s, whole decoder (Qwen3-30B-A3B shape); HBM GB/s of expert+dense+KV bytes",
             "value": round(value, 3), "unit": "tok/s", "n_gpus": 1, "steps": args.steps, "warmup": args.warmup,
             "ms_per_step": round(ms / args.steps, 5), "higher_is_better": True, "scaling": "weak",

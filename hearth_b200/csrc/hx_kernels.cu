@@ -41,10 +41,17 @@ cudaError_t launch_act_quantize(const float *x, int64_t ldx, act_q8 *out, int64_
 
 // Quantized weights: one warp per row, up to 16 tokens per pass, block terms chained per
 // (row, token) in block order.
+// Epilogue of the row-range matmuls: Y = y, or with a residual target h: h = h + rs * y (the
+// h_i + (rs * a_i) of engine/src/model.c:1194-1198 on the matmul's canonical output).
+__device__ __forceinline__ void mm_store(float *Y, float *resid, float rs, int64_t i, float y) {
+    if (resid) resid[i] = __fadd_rn(resid[i], __fmul_rn(rs, y));
+    else Y[i] = y;
+}
+
 template <int DT>
 __global__ void __launch_bounds__(256) k_matmul_q(const uint8_t *__restrict__ W, int nb, int64_t rb,
                                                   const act_q8 *__restrict__ act, int T, float *__restrict__ Y,
-                                                  int64_t ldy, int64_t r0, int64_t r1) {
+                                                  int64_t ldy, int64_t r0, int64_t r1, float *resid, float rs) {
     __shared__ float Pbuf[8][16 * 33];
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
     const int64_t r = r0 + (int64_t)blockIdx.x * 8 + warp;
@@ -78,7 +85,7 @@ __global__ void __launch_bounds__(256) k_matmul_q(const uint8_t *__restrict__ W,
                 for (int g = 0; g < gn; g++) acc = __fadd_rn(acc, P[lane * 33 + g]);
             __syncwarp();
         }
-        if (lane < nt) Y[(int64_t)(t0 + lane) * ldy + r] = canon(acc);
+        if (lane < nt) mm_store(Y, resid, rs, (int64_t)(t0 + lane) * ldy + r, canon(acc));
     }
 }
 
@@ -100,7 +107,7 @@ __device__ __forceinline__ float dot16_group(const uint8_t *row, const float *x,
 template <int DT>
 __global__ void __launch_bounds__(256) k_matmul_f(const uint8_t *__restrict__ W, int64_t n, int64_t rb,
                                                   const float *__restrict__ X, int T, float *__restrict__ Y,
-                                                  int64_t ldy, int64_t r0, int64_t r1) {
+                                                  int64_t ldy, int64_t r0, int64_t r1, float *resid, float rs) {
     const int grp = threadIdx.x >> 4, j = threadIdx.x & 15;
     const int64_t item = (int64_t)blockIdx.x * 16 + grp;   // (row, token) item
     const int64_t rows = r1 - r0;
@@ -110,11 +117,16 @@ __global__ void __launch_bounds__(256) k_matmul_f(const uint8_t *__restrict__ W,
     float L = valid ? dot16_group<DT>(W + r * rb, X + t * n, n, j) : 0.0f;
     const unsigned mask = 0xffffffffu;
     L = tree16(L, mask);
-    if (valid && j == 0) Y[t * ldy + r] = canon(L);
+    if (valid && j == 0) mm_store(Y, resid, rs, t * ldy + r, canon(L));
 }
 
 cudaError_t launch_matmul(int dtype, const void *W, int64_t n_cols, const void *act, int T, float *Y,
                           int64_t ldy, int64_t r0, int64_t r1, cudaStream_t s) {
+    return launch_matmul_resid(dtype, W, n_cols, act, T, Y, ldy, r0, r1, nullptr, 0.0f, s);
+}
+
+cudaError_t launch_matmul_resid(int dtype, const void *W, int64_t n_cols, const void *act, int T, float *Y,
+                                int64_t ldy, int64_t r0, int64_t r1, float *resid, float rs, cudaStream_t s) {
     const int64_t rows = r1 - r0;
     if (rows <= 0 || T <= 0) return cudaSuccess;
     const int64_t rb = row_bytes(dtype, n_cols);
@@ -123,16 +135,16 @@ cudaError_t launch_matmul(int dtype, const void *W, int64_t n_cols, const void *
         const int nb = (int)(n_cols / QK);
         dim3 grid((unsigned)((rows + 7) / 8), (unsigned)std::min<int64_t>((T + 15) / 16, 65535));
         if (dtype == Q4)
-            k_matmul_q<Q4><<<grid, 256, 0, s>>>(w, nb, rb, (const act_q8 *)act, T, Y, ldy, r0, r1);
+            k_matmul_q<Q4><<<grid, 256, 0, s>>>(w, nb, rb, (const act_q8 *)act, T, Y, ldy, r0, r1, resid, rs);
         else
-            k_matmul_q<Q8><<<grid, 256, 0, s>>>(w, nb, rb, (const act_q8 *)act, T, Y, ldy, r0, r1);
+            k_matmul_q<Q8><<<grid, 256, 0, s>>>(w, nb, rb, (const act_q8 *)act, T, Y, ldy, r0, r1, resid, rs);
     } else {
         const int64_t items = rows * T;
         const unsigned grid = (unsigned)((items + 15) / 16);
         const float *x = static_cast<const float *>(act);
-        if (dtype == F32) k_matmul_f<F32><<<grid, 256, 0, s>>>(w, n_cols, rb, x, T, Y, ldy, r0, r1);
-        else if (dtype == F16) k_matmul_f<F16><<<grid, 256, 0, s>>>(w, n_cols, rb, x, T, Y, ldy, r0, r1);
-        else k_matmul_f<BF16><<<grid, 256, 0, s>>>(w, n_cols, rb, x, T, Y, ldy, r0, r1);
+        if (dtype == F32) k_matmul_f<F32><<<grid, 256, 0, s>>>(w, n_cols, rb, x, T, Y, ldy, r0, r1, resid, rs);
+        else if (dtype == F16) k_matmul_f<F16><<<grid, 256, 0, s>>>(w, n_cols, rb, x, T, Y, ldy, r0, r1, resid, rs);
+        else k_matmul_f<BF16><<<grid, 256, 0, s>>>(w, n_cols, rb, x, T, Y, ldy, r0, r1, resid, rs);
     }
     return cudaGetLastError();
 }

@@ -78,6 +78,7 @@ struct DLayer {
     bool moe = false;
     Buf attn_norm, ffn_norm, bq, bk, bv, qn, kn;
     Mat q, k, v, o, gate, up, down;
+    Mat qkv;   // q, k and v rows in one matrix when they share a dtype (one launch for the three)
 };
 
 // The host libm's cosf / sinf as separate calls, as the reference makes them
@@ -102,7 +103,7 @@ struct hxb_model {
     std::vector<DLayer> layers;
     std::vector<int> moe_index;
     Buf kc, vc;                                      // [L][Hkv][max_seq][hd] f32
-    Buf tok, h, x, act, q, kk, vv, S, att, ao, f1, f2, logits, cs, routes, forced, dpos;
+    Buf tok, h, x, act, q, kk, S, att, f1, f2, logits, cs, routes, forced, dpos;   // q: [T][q|k|v]
     int32_t *tok_pin = nullptr;
     float *logit_pin = nullptr;
     int next_pos = -1;                               // the device position counter's value, if known
@@ -172,7 +173,9 @@ __global__ void __launch_bounds__(256) k_rmsnorm_rows(const float *__restrict__ 
 }
 
 struct PostArgs {
-    float *q, *k, *v;                        // [T][q_dim], [T][kv_dim] (q updated in place)
+    const float *qkv;                        // [T][ld]: q | k | v of each token
+    int64_t ld;
+    float *qout;                             // [T][q_dim]: q after bias, qk-norm and RoPE
     const float *bq, *bk, *bv, *qn, *kn;     // biases and qk-norm weights (null when absent)
     const float *cs;                         // [max_seq][rope_dim]: (cos, sin) pairs per position
     float *kc, *vc;                          // this layer's caches: [Hkv][max_seq][hd]
@@ -214,8 +217,9 @@ __global__ void __launch_bounds__(256) k_attn_post(PostArgs a) {
     const int t = blockIdx.x, tid = threadIdx.x, warp = tid >> 5, nw = blockDim.x >> 5;
     const int qd = a.H * a.hd, kd = a.Hkv * a.hd;
     float *q = sm, *k = sm + qd;
-    float *qg = a.q + (int64_t)t * qd;
-    const float *kg = a.k + (int64_t)t * kd, *vg = a.v + (int64_t)t * kd;
+    const float *qg = a.qkv + (int64_t)t * a.ld;
+    const float *kg = qg + qd, *vg = qg + qd + kd;
+    float *qo = a.qout + (int64_t)t * qd;
     for (int i = tid; i < qd; i += blockDim.x) q[i] = a.bq ? __fadd_rn(qg[i], a.bq[i]) : qg[i];
     for (int i = tid; i < kd; i += blockDim.x) k[i] = a.bk ? __fadd_rn(kg[i], a.bk[i]) : kg[i];
     __syncthreads();
@@ -236,7 +240,7 @@ __global__ void __launch_bounds__(256) k_attn_post(PostArgs a) {
             warp_rope(hh < a.H ? q + hh * a.hd : k + (hh - a.H) * a.hd, cs, a.rope_half, a.rope_style);
     }
     __syncthreads();
-    for (int i = tid; i < qd; i += blockDim.x) qg[i] = q[i];
+    for (int i = tid; i < qd; i += blockDim.x) qo[i] = q[i];
     for (int i = tid; i < kd; i += blockDim.x) {
         const int g = i / a.hd, d = i - g * a.hd;
         const int64_t o = ((int64_t)g * a.max_seq + pos) * a.hd + d;
@@ -278,8 +282,9 @@ __global__ void k_advance_pos(int *dpos, int T) { *dpos += T; }
 // and o[d] = sum_r p_r * v_r[d] in position order from 0.0f (value_sum, model.c:552-590).
 // Shared memory: p [pos + 1].
 __global__ void __launch_bounds__(128) k_attn_softmax_values(const float *__restrict__ S, const float *__restrict__ vc,
-                                                             float *__restrict__ att, int H, int Hkv, int hd,
-                                                             int max_seq, const int *__restrict__ dpos) {
+                                                             float *__restrict__ att, act_q8 *__restrict__ act,
+                                                             int H, int Hkv, int hd, int max_seq,
+                                                             const int *__restrict__ dpos) {
     extern __shared__ float p[];
     __shared__ float red[4];
     __shared__ float ssum;
@@ -326,12 +331,14 @@ __global__ void __launch_bounds__(128) k_attn_softmax_values(const float *__rest
         for (; r < n; r++) acc = __fadd_rn(acc, __fmul_rn(p[r], vg[(int64_t)r * hd + d]));
         o[d] = acc;
     }
-}
-
-// h = h + rs * a (model.c:1194-1198, 1138-1142).
-__global__ void k_residual(float *__restrict__ h, const float *__restrict__ a, int64_t n, float rs) {
-    const int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
-    if (i < n) h[i] = __fadd_rn(h[i], __fmul_rn(rs, a[i]));
+    if (act) {   // head_dim a multiple of 64: this head's activation blocks of the o projection's input
+        __syncthreads();   // every o[d] of the head written (read back through L1: same CTA)
+        const int nbh = hd / QK, nb = H * nbh;
+        for (int b = warp; b < nbh; b += blockDim.x >> 5) {
+            const float *ob = o + b * QK;
+            act_quant_warp(ob[lane], ob[lane + 32], act + (int64_t)t * nb + h * nbh + b, lane);
+        }
+    }
 }
 
 // g = silu(g) * u (hx_swiglu, NUMERICS §4).
@@ -355,7 +362,7 @@ unsigned blocks(int64_t n, int b) { return (unsigned)((n + b - 1) / b); }
 // (model.c:287-384): quantized weights take x's activation blocks (quantized once into act by the
 // caller, or here when act_ready is false), float weights take x itself.
 int matmul(hxb_model *m, const Mat &W, const float *x, int64_t ldx, act_q8 *act, bool &act_ready, int T, float *Y,
-           int64_t ldy, cudaStream_t s) {
+           int64_t ldy, cudaStream_t s, float *resid = nullptr, float rs = 0.0f) {
     (void)m;
     const void *in = x;
     if (is_quant(W.dtype)) {
@@ -367,7 +374,8 @@ int matmul(hxb_model *m, const Mat &W, const float *x, int64_t ldx, act_q8 *act,
     } else if (ldx != W.cols) {
         return mfail(HXB_E_ARG, "float matmul input stride");
     }
-    if (!mcuda(launch_matmul(W.dtype, W.w.p, W.cols, in, T, Y, ldy, 0, W.rows, s), "matmul")) return HXB_E_DEVICE;
+    if (!mcuda(launch_matmul_resid(W.dtype, W.w.p, W.cols, in, T, Y, ldy, 0, W.rows, resid, rs, s), "matmul"))
+        return HXB_E_DEVICE;
     return HXB_OK;
 }
 
@@ -447,10 +455,10 @@ extern "C" HXB_API void hxb_model_close(hxb_model *m) {
     if (m->moe) hxb_moe_close(m->moe);
     for (auto &l : m->layers)
         for (Buf *b : {&l.attn_norm, &l.ffn_norm, &l.bq, &l.bk, &l.bv, &l.qn, &l.kn, &l.q.w, &l.k.w, &l.v.w, &l.o.w,
-                       &l.gate.w, &l.up.w, &l.down.w})
+                       &l.gate.w, &l.up.w, &l.down.w, &l.qkv.w})
             b->release();
     for (Buf *b : {&m->tok_embd.w, &m->lm_head.w, &m->out_norm, &m->kc, &m->vc, &m->tok, &m->h, &m->x, &m->act, &m->q,
-                   &m->kk, &m->vv, &m->S, &m->att, &m->ao, &m->f1, &m->f2, &m->logits, &m->cs, &m->routes, &m->forced,
+                   &m->kk, &m->S, &m->att, &m->f1, &m->f2, &m->logits, &m->cs, &m->routes, &m->forced,
                    &m->dpos})
         b->release();
     for (void *p : {(void *)m->tok_pin, (void *)m->logit_pin, (void *)m->route_pin,
@@ -465,6 +473,27 @@ static hxb_model *open_fail(hxb_model *m, char *err, size_t errlen, const std::s
     set_last_error(msg.c_str());
     hxb_model_close(m);
     return nullptr;
+}
+
+// q, k and v of one dtype go into one matrix (rows q | k | v), so one launch computes the three.
+static bool fuse_qkv(DLayer &w) {
+    if (w.q.dtype != w.k.dtype || w.q.dtype != w.v.dtype) return true;
+    Mat &f = w.qkv;
+    f.dtype = w.q.dtype;
+    f.cols = w.q.cols;
+    f.rb = w.q.rb;
+    f.rows = w.q.rows + w.k.rows + w.v.rows;
+    if (!f.w.alloc((size_t)(f.rows * f.rb))) return false;
+    uint8_t *d = f.w.as<uint8_t>();
+    const size_t bq = (size_t)(w.q.rows * f.rb), bk = (size_t)(w.k.rows * f.rb), bv = (size_t)(w.v.rows * f.rb);
+    if (cudaMemcpy(d, w.q.w.p, bq, cudaMemcpyDeviceToDevice) != cudaSuccess ||
+        cudaMemcpy(d + bq, w.k.w.p, bk, cudaMemcpyDeviceToDevice) != cudaSuccess ||
+        cudaMemcpy(d + bq + bk, w.v.w.p, bv, cudaMemcpyDeviceToDevice) != cudaSuccess)
+        return false;
+    w.q.w.release();
+    w.k.w.release();
+    w.v.w.release();
+    return true;
 }
 
 // The KV cache, the scratch of a forward of max_batch tokens and the attention kernels' shared
@@ -486,9 +515,9 @@ static const char *alloc_runtime(hxb_model *m) {
     const size_t actb = T * ((size_t)m->max_in / QK + 1) * sizeof(act_q8);
     const size_t rows = std::max<size_t>(1, (size_t)m->n_moe * T * m->K);
     bool ok = m->kc.alloc(kvb) && m->vc.alloc(kvb) && m->tok.alloc(4 * T) && m->h.alloc(4 * T * m->D) &&
-              m->x.alloc(4 * T * m->max_in) && m->act.alloc(actb) && m->q.alloc(4 * T * m->q_dim) &&
-              m->kk.alloc(4 * T * m->kv_dim) && m->vv.alloc(4 * T * m->kv_dim) &&
-              m->S.alloc(4 * T * m->H * S) && m->att.alloc(4 * T * m->q_dim) && m->ao.alloc(4 * T * m->D) &&
+              m->x.alloc(4 * T * m->max_in) && m->act.alloc(actb) && m->q.alloc(4 * T * (m->q_dim + 2 * m->kv_dim)) &&
+              m->kk.alloc(4 * T * m->q_dim) &&
+              m->S.alloc(4 * T * m->H * S) && m->att.alloc(4 * T * m->q_dim) &&
               m->f1.alloc(4 * T * std::max(1, m->Fd)) && m->f2.alloc(4 * T * std::max(1, m->Fd)) &&
               m->logits.alloc(4 * T * m->V) && m->cs.alloc(4 * S * std::max(2, m->rope_dim)) &&
               m->routes.alloc(4 * rows) && m->forced.alloc(4 * rows) && m->dpos.alloc(4);
@@ -605,6 +634,7 @@ extern "C" HXB_API hxb_model *hxb_model_open(const char *path, const hxb_model_o
             ok = ld.mat(w.gate, l, "ffn_gate", m->Fd, m->D) && ld.mat(w.up, l, "ffn_up", m->Fd, m->D) &&
                  ld.mat(w.down, l, "ffn_down", m->D, m->Fd);
         if (!ok) return open_fail(m, err, errlen, ld.err);
+        if (!fuse_qkv(w)) return open_fail(m, err, errlen, "model_open: out of device memory");
     }
     // the MoE layers: the backend handle over the same container
     if (m->n_moe) {
@@ -699,6 +729,7 @@ extern "C" HXB_API hxb_model *hxb_model_synthesize(const hxb_model_arch *a, cons
              mat(w.k, m->kv_dim, m->D, sd) && mat(w.v, m->kv_dim, m->D, sd) && mat(w.o, m->D, m->q_dim, sd) &&
              (m->qk_norm != 1 || (unit(w.qn, m->hd) && unit(w.kn, m->hd))) &&
              (m->qk_norm != 2 || (unit(w.qn, m->q_dim) && unit(w.kn, m->kv_dim)));
+        ok = ok && cudaStreamSynchronize(s) == cudaSuccess && fuse_qkv(w);
     }
     if (!ok) return open_fail(m, err, errlen, "model_synthesize: out of device memory");
     hxb_moe_config mc = c;
@@ -758,15 +789,22 @@ static int attention(hxb_model *m, int l, int T, cudaStream_t s) {
                                                           x, m->D, quant_in ? act : nullptr);
     if (!mcuda(cudaGetLastError(), "rmsnorm")) return HXB_E_DEVICE;
     bool ready = quant_in;
-    int rc = matmul(m, w.q, x, m->D, act, ready, T, m->q.as<float>(), m->q_dim, s);
-    if (!rc) rc = matmul(m, w.k, x, m->D, act, ready, T, m->kk.as<float>(), m->kv_dim, s);
-    if (!rc) rc = matmul(m, w.v, x, m->D, act, ready, T, m->vv.as<float>(), m->kv_dim, s);
+    const int ld = m->q_dim + 2 * m->kv_dim;
+    float *qkv = m->q.as<float>();
+    int rc;
+    if (w.qkv.w.p) {
+        rc = matmul(m, w.qkv, x, m->D, act, ready, T, qkv, ld, s);
+    } else {
+        rc = matmul(m, w.q, x, m->D, act, ready, T, qkv, ld, s);
+        if (!rc) rc = matmul(m, w.k, x, m->D, act, ready, T, qkv + m->q_dim, ld, s);
+        if (!rc) rc = matmul(m, w.v, x, m->D, act, ready, T, qkv + m->q_dim + m->kv_dim, ld, s);
+    }
     if (rc) return rc;
     const size_t layer_kv = (size_t)m->Hkv * m->max_seq * m->hd;
     PostArgs a;
-    a.q = m->q.as<float>();
-    a.k = m->kk.as<float>();
-    a.v = m->vv.as<float>();
+    a.qkv = qkv;
+    a.ld = ld;
+    a.qout = m->kk.as<float>();
     a.bq = m->qkv_bias ? w.bq.as<float>() : nullptr;
     a.bk = m->qkv_bias ? w.bk.as<float>() : nullptr;
     a.bv = m->qkv_bias ? w.bv.as<float>() : nullptr;
@@ -787,18 +825,16 @@ static int attention(hxb_model *m, int l, int T, cudaStream_t s) {
     k_attn_post<<<T, 256, sizeof(float) * (m->q_dim + m->kv_dim), s>>>(a);
     // the score CTAs of a (token, head) stride over the positions: about 600 CTAs in all
     const int chunks = std::max(1, std::min((int)blocks(m->max_seq, 16), 600 / (m->H * T)));
-    k_attn_scores<<<dim3(chunks, m->H, T), 256, 0, s>>>(a.q, a.kc, m->S.as<float>(), m->H, m->Hkv, m->hd, m->max_seq,
-                                                         a.dpos, m->attn_scale);
-    k_attn_softmax_values<<<dim3(m->H, T), 128, sizeof(float) * m->max_seq, s>>>(m->S.as<float>(), a.vc,
-                                                                                m->att.as<float>(), m->H, m->Hkv,
-                                                                                m->hd, m->max_seq, a.dpos);
+    k_attn_scores<<<dim3(chunks, m->H, T), 256, 0, s>>>(a.qout, a.kc, m->S.as<float>(), m->H, m->Hkv, m->hd,
+                                                         m->max_seq, a.dpos, m->attn_scale);
+    // the o projection's activation blocks come out of the value kernel when a head holds whole blocks
+    const bool fuse_act = is_quant(w.o.dtype) && m->hd % QK == 0;
+    k_attn_softmax_values<<<dim3(m->H, T), 128, sizeof(float) * m->max_seq, s>>>(
+        m->S.as<float>(), a.vc, m->att.as<float>(), fuse_act ? act : nullptr, m->H, m->Hkv, m->hd, m->max_seq, a.dpos);
     if (!mcuda(cudaGetLastError(), "attention")) return HXB_E_DEVICE;
-    bool aready = false;
-    rc = matmul(m, w.o, m->att.as<float>(), m->q_dim, act, aready, T, m->ao.as<float>(), m->D, s);
-    if (rc) return rc;
-    k_residual<<<blocks((int64_t)T * m->D, 256), 256, 0, s>>>(m->h.as<float>(), m->ao.as<float>(), (int64_t)T * m->D,
-                                                              m->rs);
-    return mcuda(cudaGetLastError(), "residual") ? HXB_OK : HXB_E_DEVICE;
+    bool aready = fuse_act;
+    // h += rs * (Wo att): the residual in the matmul's epilogue
+    return matmul(m, w.o, m->att.as<float>(), m->q_dim, act, aready, T, nullptr, m->D, s, m->h.as<float>(), m->rs);
 }
 
 // A dense FFN sublayer (dense_layer + ffn, model.c:444-460, 1133-1143).
@@ -815,10 +851,8 @@ static int dense_ffn(hxb_model *m, int l, int T, cudaStream_t s) {
     if (rc) return rc;
     k_swiglu<<<blocks((int64_t)T * m->Fd, 256), 256, 0, s>>>(m->f1.as<float>(), m->f2.as<float>(), (int64_t)T * m->Fd);
     bool dready = false;
-    rc = matmul(m, w.down, m->f1.as<float>(), m->Fd, act, dready, T, m->ao.as<float>(), m->D, s);
+    rc = matmul(m, w.down, m->f1.as<float>(), m->Fd, act, dready, T, nullptr, m->D, s, m->h.as<float>(), m->rs);
     if (rc) return rc;
-    k_residual<<<blocks((int64_t)T * m->D, 256), 256, 0, s>>>(m->h.as<float>(), m->ao.as<float>(), (int64_t)T * m->D,
-                                                              m->rs);
     return mcuda(cudaGetLastError(), "dense ffn") ? HXB_OK : HXB_E_DEVICE;
 }
 
