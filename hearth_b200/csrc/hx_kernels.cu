@@ -89,6 +89,104 @@ __global__ void __launch_bounds__(256) k_matmul_q(const uint8_t *__restrict__ W,
     }
 }
 
+// Quantized weights at few tokens (decode): the rows stream through shared memory in tiles of R
+// consecutive rows, one 1-D bulk copy per tile into a 3-stage ring (up to ~180 KB in flight per
+// SM, what the HBM stream needs); one CTA per SM walks tiles blockIdx.x + k * gridDim.x. Each warp
+// takes rows of the tile: lane g forms block g's term for every token, then lane t adds token t's
+// terms in block order (the chain of NUMERICS §3). Rows must be a multiple of 16 bytes and the
+// matrix 16-byte aligned (every Q4/Q8 matrix with n_cols a multiple of 512, in cudaMalloc memory).
+constexpr int GV_NST = 3;
+constexpr int GV_TMAX = 4;
+
+template <int DT>
+__global__ void __launch_bounds__(256) k_gemv_staged(const uint8_t *__restrict__ W, int64_t rows, int nb, int64_t rb,
+                                                     int R, const act_q8 *__restrict__ act, int T,
+                                                     float *__restrict__ Y, int64_t ldy, float *resid, float rs) {
+    extern __shared__ __align__(128) uint8_t smem[];
+    uint64_t *bars = reinterpret_cast<uint64_t *>(smem);
+    uint8_t *ring = smem + 128;
+    const int64_t stage = (int64_t)R * rb;
+    act_q8 *acts = reinterpret_cast<act_q8 *>(ring + GV_NST * stage);
+    const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+    float *P = reinterpret_cast<float *>(acts + (int64_t)T * nb) + warp * (GV_TMAX * 33);
+    const int64_t ntiles = (rows + R - 1) / R;
+    const int64_t mine = (int64_t)blockIdx.x < ntiles ? (ntiles - 1 - blockIdx.x) / gridDim.x + 1 : 0;
+    if (tid == 0) {
+        for (int st = 0; st < GV_NST; st++) mbar_init(&bars[st], 1);
+        fence_mbar_init();
+    }
+    __syncthreads();
+    auto issue = [&](int64_t k) {
+        const int64_t r0 = ((int64_t)blockIdx.x + k * gridDim.x) * R;
+        const int64_t nr = min((int64_t)R, rows - r0);
+        const int st = (int)(k % GV_NST);
+        mbar_expect_tx(&bars[st], (uint32_t)(nr * rb));
+        bulk_g2s(ring + st * stage, W + r0 * rb, (uint32_t)(nr * rb), &bars[st]);
+    };
+    if (tid == 0)
+        for (int64_t k = 0; k < min((int64_t)GV_NST, mine); k++) issue(k);
+    {
+        const uint32_t *src = reinterpret_cast<const uint32_t *>(act);
+        uint32_t *dst = reinterpret_cast<uint32_t *>(acts);
+        for (int64_t i = tid; i < (int64_t)T * nb * (ACT_BLOCK / 4); i += blockDim.x) dst[i] = src[i];
+    }
+    __syncthreads();
+    constexpr int BS = DT == Q4 ? Q4_BLOCK : Q8_BLOCK;
+    for (int64_t k = 0; k < mine; k++) {
+        const int st = (int)(k % GV_NST);
+        const bool ok = mbar_wait(&bars[st], (uint32_t)((k / GV_NST) & 1), nullptr);
+        const int64_t r0 = ((int64_t)blockIdx.x + k * gridDim.x) * R;
+        const int nr = (int)min((int64_t)R, rows - r0);
+        const uint8_t *tile = ring + st * stage;
+        for (int rr = warp; ok && rr < nr; rr += 8) {
+            const uint8_t *row = tile + (int64_t)rr * rb;
+            float acc = 0.0f;
+            for (int g0 = 0; g0 < nb; g0 += 32) {
+                const int gn = min(32, nb - g0);
+                if (lane < gn) {
+                    const int g = g0 + lane;
+                    uint32_t wq[16];
+                    float dw;
+                    if constexpr (DT == Q4) dw = f16_to_f32(load_q4_block(row + (int64_t)g * BS, wq));
+                    else dw = f16_to_f32(load_q8_block(row + (int64_t)g * BS, wq));
+                    for (int i = 0; i < T; i++) {
+                        act_regs ar;
+                        load_act(acts + i * nb + g, ar);
+                        int isum;
+                        if constexpr (DT == Q4) isum = q4_isum(wq, ar.q, ar.sum);
+                        else isum = q8_isum(wq, ar.q);
+                        P[i * 33 + lane] = __fmul_rn(__int2float_rn(isum), __fmul_rn(dw, ar.d));
+                    }
+                }
+                __syncwarp();
+                if (lane < T)
+                    for (int g = 0; g < gn; g++) acc = __fadd_rn(acc, P[lane * 33 + g]);
+                __syncwarp();
+            }
+            if (lane < T) mm_store(Y, resid, rs, (int64_t)lane * ldy + r0 + rr, canon(acc));
+        }
+        __syncthreads();   // every warp is done with this stage
+        if (tid == 0 && k + GV_NST < mine) {
+            fence_proxy_async();
+            issue(k + GV_NST);
+        }
+    }
+}
+
+// The staged kernel's shape for a launch, or R = 0 when it does not apply.
+static int gemv_rows_per_stage(int dtype, const void *W, int64_t n_cols, int64_t rows, int T, size_t *smem) {
+    if (!is_quant(dtype) || T > GV_TMAX || rows < 1 || (reinterpret_cast<uintptr_t>(W) & 15)) return 0;
+    const int64_t rb = row_bytes(dtype, n_cols);
+    const int64_t nb = n_cols / QK;
+    if (rb % 16 || rb > 16384) return 0;
+    int R = (int)std::min<int64_t>(64, 56 * 1024 / rb);
+    R = R / 8 * 8;
+    if (R < 8) return 0;
+    *smem = 128 + (size_t)GV_NST * R * rb + (size_t)T * nb * ACT_BLOCK + 8 * GV_TMAX * 33 * sizeof(float);
+    if (*smem > 220 * 1024) return 0;
+    return R;
+}
+
 // Float weights: NUMERICS §1 dot16, one 16-lane group per (row, token).
 template <int DT>
 __device__ __forceinline__ float load_wf(const uint8_t *row, int64_t i) {
@@ -131,6 +229,36 @@ cudaError_t launch_matmul_resid(int dtype, const void *W, int64_t n_cols, const 
     if (rows <= 0 || T <= 0) return cudaSuccess;
     const int64_t rb = row_bytes(dtype, n_cols);
     const uint8_t *w = static_cast<const uint8_t *>(W);
+    size_t smem = 0;
+    const int R = gemv_rows_per_stage(dtype, w + r0 * rb, n_cols, rows, T, &smem);
+    if (R > 0) {   // few tokens: the rows stream through shared memory at the HBM rate
+        int dev = 0, sms = 148;
+        cudaGetDevice(&dev);
+        static bool attr_set[64][2] = {};   // per device: the attribute belongs to the device's context
+        const int di = dtype == Q4 ? 0 : 1;
+        if (dev < 0 || dev >= 64) return cudaErrorInvalidDevice;
+        if (!attr_set[dev][di]) {
+            cudaError_t e = dtype == Q4 ? cudaFuncSetAttribute(k_gemv_staged<Q4>,
+                                                               cudaFuncAttributeMaxDynamicSharedMemorySize, 220 * 1024)
+                                        : cudaFuncSetAttribute(k_gemv_staged<Q8>,
+                                                               cudaFuncAttributeMaxDynamicSharedMemorySize, 220 * 1024);
+            if (e != cudaSuccess) return e;
+            attr_set[dev][di] = true;
+        }
+        cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
+        const int64_t ntiles = (rows + R - 1) / R;
+        const unsigned grid = (unsigned)std::min<int64_t>(ntiles, sms);
+        const int nb = (int)(n_cols / QK);
+        float *Yr = resid ? nullptr : Y + r0;
+        float *hr = resid ? resid + r0 : nullptr;
+        if (dtype == Q4)
+            k_gemv_staged<Q4><<<grid, 256, smem, s>>>(w + r0 * rb, rows, nb, rb, R, (const act_q8 *)act, T, Yr, ldy,
+                                                      hr, rs);
+        else
+            k_gemv_staged<Q8><<<grid, 256, smem, s>>>(w + r0 * rb, rows, nb, rb, R, (const act_q8 *)act, T, Yr, ldy,
+                                                      hr, rs);
+        return cudaGetLastError();
+    }
     if (is_quant(dtype)) {
         const int nb = (int)(n_cols / QK);
         dim3 grid((unsigned)((rows + 7) / 8), (unsigned)std::min<int64_t>((T + 15) / 16, 65535));
