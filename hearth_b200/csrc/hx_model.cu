@@ -94,7 +94,7 @@ struct hxb_model {
     hxb_moe *moe = nullptr;
     // shape (engine/src/model.c:1394-1439 setup_dims, GQA)
     int L = 0, D = 0, V = 0, H = 0, Hkv = 0, hd = 0, q_dim = 0, kv_dim = 0, rope_dim = 0, rope_half = 0;
-    int rope_style = 0, qk_norm = 0, qkv_bias = 0, Fd = 0, n_moe = 0, K = 0, E = 0, max_in = 0;
+    int rope_style = 0, qk_norm = 0, qkv_bias = 0, Fd = 0, n_moe = 0, K = 0, E = 0, max_in = 0, dc = 64, vthreads = 0;
     float eps = 1e-6f, rs = 1.0f, es = 1.0f, ls = 1.0f, attn_scale = 1.0f, rope_factor = 1.0f;
     int max_batch = 0, max_seq = 0;
     std::vector<float> inv_freq;
@@ -210,35 +210,53 @@ __device__ __forceinline__ void warp_rope(float *x, const float *cs, int half, i
     __syncwarp();
 }
 
-// Per token (one CTA): biases, qk-norm, RoPE, the (k, v) rows into the cache (gqa_post_range,
-// model.c:484-517). Shared memory: q [q_dim], k [kv_dim].
+// Biases, qk-norm, RoPE, the (k, v) rows into the cache (gqa_post_range, model.c:484-517).
+// Per-head qk-norm or none: one warp per head (q heads, then kv heads), 8 heads per CTA, grid
+// (tokens, heads / 8). Full-width qk-norm: one CTA per token over the whole q and k rows.
+// Shared memory: q [q_dim], k [kv_dim] (full width) or 8 x head_dim (per head).
 __global__ void __launch_bounds__(256) k_attn_post(PostArgs a) {
     extern __shared__ float sm[];
-    const int t = blockIdx.x, tid = threadIdx.x, warp = tid >> 5, nw = blockDim.x >> 5;
+    const int t = blockIdx.x, tid = threadIdx.x, warp = tid >> 5, lane = tid & 31, nw = blockDim.x >> 5;
     const int qd = a.H * a.hd, kd = a.Hkv * a.hd;
-    float *q = sm, *k = sm + qd;
     const float *qg = a.qkv + (int64_t)t * a.ld;
     const float *kg = qg + qd, *vg = qg + qd + kd;
     float *qo = a.qout + (int64_t)t * qd;
+    const int pos = *a.dpos + t;
+    const float *cs = a.cs + (int64_t)pos * 2 * a.rope_half;
+    if (a.qk_norm != 2) {
+        const int hh = blockIdx.y * nw + warp;
+        if (hh >= a.H + a.Hkv) return;
+        const bool isq = hh < a.H;
+        const int off = isq ? hh * a.hd : (hh - a.H) * a.hd;
+        const float *src = isq ? qg + off : kg + off;
+        const float *bias = isq ? a.bq : a.bk;
+        float *x = sm + warp * a.hd;
+        for (int i = lane; i < a.hd; i += 32) x[i] = bias ? __fadd_rn(src[i], bias[off + i]) : src[i];
+        __syncwarp();
+        if (a.qk_norm == 1) warp_rmsnorm(x, isq ? a.qn : a.kn, a.hd, a.eps);
+        if (a.rope_half) warp_rope(x, cs, a.rope_half, a.rope_style);
+        if (isq) {
+            for (int i = lane; i < a.hd; i += 32) qo[off + i] = x[i];
+        } else {
+            const int g = hh - a.H;
+            const int64_t o = ((int64_t)g * a.max_seq + pos) * a.hd;
+            for (int i = lane; i < a.hd; i += 32) {
+                a.kc[o + i] = x[i];
+                a.vc[o + i] = a.bv ? __fadd_rn(vg[off + i], a.bv[off + i]) : vg[off + i];
+            }
+        }
+        return;
+    }
+    float *q = sm, *k = sm + qd;
     for (int i = tid; i < qd; i += blockDim.x) q[i] = a.bq ? __fadd_rn(qg[i], a.bq[i]) : qg[i];
     for (int i = tid; i < kd; i += blockDim.x) k[i] = a.bk ? __fadd_rn(kg[i], a.bk[i]) : kg[i];
     __syncthreads();
-    if (a.qk_norm == 1) {   // per head over head_dim
-        for (int hh = warp; hh < a.H + a.Hkv; hh += nw) {
-            float *x = hh < a.H ? q + hh * a.hd : k + (hh - a.H) * a.hd;
-            warp_rmsnorm(x, hh < a.H ? a.qn : a.kn, a.hd, a.eps);
-        }
-    } else if (a.qk_norm == 2) {   // full width
-        if (warp == 0) warp_rmsnorm(q, a.qn, qd, a.eps);
-        else if (warp == 1) warp_rmsnorm(k, a.kn, kd, a.eps);
-    }
+    if (warp == 0) warp_rmsnorm(q, a.qn, qd, a.eps);
+    else if (warp == 1) warp_rmsnorm(k, a.kn, kd, a.eps);
     __syncthreads();
-    const int pos = *a.dpos + t;
-    if (a.rope_half) {
-        const float *cs = a.cs + (int64_t)pos * 2 * a.rope_half;
+    if (a.rope_half)
         for (int hh = warp; hh < a.H + a.Hkv; hh += nw)
             warp_rope(hh < a.H ? q + hh * a.hd : k + (hh - a.H) * a.hd, cs, a.rope_half, a.rope_style);
-    }
     __syncthreads();
     for (int i = tid; i < qd; i += blockDim.x) qo[i] = q[i];
     for (int i = tid; i < kd; i += blockDim.x) {
@@ -278,19 +296,17 @@ __global__ void __launch_bounds__(256) k_attn_scores(const float *__restrict__ q
 __global__ void k_set_pos(int *dpos, int v) { *dpos = v; }
 __global__ void k_advance_pos(int *dpos, int T) { *dpos += T; }
 
-// Per (token, head), one CTA: p = softmax(S[0..pos]) (hx_softmax: max, expf(x - m), sum16, x / s)
-// and o[d] = sum_r p_r * v_r[d] in position order from 0.0f (value_sum, model.c:552-590).
-// Shared memory: p [pos + 1].
-__global__ void __launch_bounds__(128) k_attn_softmax_values(const float *__restrict__ S, const float *__restrict__ vc,
-                                                             float *__restrict__ att, act_q8 *__restrict__ act,
-                                                             int H, int Hkv, int hd, int max_seq,
-                                                             const int *__restrict__ dpos) {
+// Per (token, head), one CTA: p = softmax(S[0..pos]) in place (hx_softmax, model.c:534-550: max,
+// expf(x - m), sum16, x / s). The row is staged in shared memory, so the 16 sum16 chains read it
+// there. Shared memory: pos + 1 floats.
+__global__ void __launch_bounds__(256) k_attn_softmax(float *__restrict__ S, int H, int max_seq,
+                                                      const int *__restrict__ dpos) {
     extern __shared__ float p[];
-    __shared__ float red[4];
+    __shared__ float red[8];
     __shared__ float ssum;
     const int t = blockIdx.y, h = blockIdx.x, tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
-    const int n = *dpos + t + 1, g = h / (H / Hkv);
-    const float *s = S + ((int64_t)t * H + h) * max_seq;
+    const int n = *dpos + t + 1;
+    float *s = S + ((int64_t)t * H + h) * max_seq;
     // m = x[0] if it is NaN, else the largest non-NaN value (the comparison `x > m` skips NaNs)
     float m = -__uint_as_float(0x7f800000u);
     for (int i = tid; i < n; i += blockDim.x) {
@@ -301,7 +317,8 @@ __global__ void __launch_bounds__(128) k_attn_softmax_values(const float *__rest
     for (int o = 16; o >= 1; o >>= 1) m = fmaxf(m, __shfl_xor_sync(0xffffffffu, m, o));
     if (lane == 0) red[warp] = m;
     __syncthreads();
-    m = fmaxf(fmaxf(red[0], red[1]), fmaxf(red[2], red[3]));
+    m = red[0];
+    for (int w = 1; w < (int)(blockDim.x >> 5); w++) m = fmaxf(m, red[w]);
     if (p[0] != p[0]) m = p[0];
     for (int i = tid; i < n; i += blockDim.x) p[i] = host_expf(__fsub_rn(p[i], m));
     __syncthreads();
@@ -313,31 +330,83 @@ __global__ void __launch_bounds__(128) k_attn_softmax_values(const float *__rest
     }
     __syncthreads();
     const float sum = ssum;
-    for (int i = tid; i < n; i += blockDim.x) p[i] = __fdiv_rn(p[i], sum);
+    for (int i = tid; i < n; i += blockDim.x) s[i] = __fdiv_rn(p[i], sum);
+}
+
+// o_h[d] = sum_r p_h[r] * v_r[d] in position order from 0.0f (value_sum, model.c:552-590), one CTA
+// per (token, kv group, DC dims): thread (hh, d) runs the chain of head g*grp + hh, dim d. Each V row
+// slice is read once for the group's heads: tiles of VT positions (V and p) are staged in shared
+// memory, the next tile's loads issued into registers before the current tile's chains run. With
+// DC = 64 the CTA also forms the o projection's activation blocks of its heads (act not null).
+constexpr int VT = 32;
+__global__ void __launch_bounds__(1024) k_attn_values(const float *__restrict__ S, const float *__restrict__ vc,
+                                                      float *__restrict__ att, act_q8 *__restrict__ act, int H,
+                                                      int Hkv, int hd, int DC, int max_seq,
+                                                      const int *__restrict__ dpos) {
+    extern __shared__ float sm[];
+    const int grp = H / Hkv, nd = hd / DC;
+    const int t = blockIdx.y, g = blockIdx.x / nd, dc = blockIdx.x - g * nd;
+    const int tid = threadIdx.x, nthr = blockDim.x;   // >= grp * DC: the first grp * DC threads run chains
+    const int hh = tid / DC, d = tid - hh * DC;
+    const bool chain = tid < grp * DC;
+    const int n = *dpos + t + 1;
+    float *vbuf = sm;                       // [2][VT][DC]
+    float *pbuf = sm + 2 * VT * DC;         // [2][grp][VT]
+    float *ost = pbuf + 2 * grp * VT;       // [grp][DC]
+    const float *vg = vc + (int64_t)g * max_seq * hd + dc * DC;
+    const float *pg = S + ((int64_t)t * H + g * grp) * max_seq;
+    const int nv = VT * DC, np = grp * VT;
+    // per thread: elements i = tid + k * nthr of the tile's V part, then of its p part
+    constexpr int MAXL = 4;   // the launch gives at least (VT * DC + grp * VT) / 4 threads
+    float reg[MAXL];
+    auto load = [&](int r0) {
+#pragma unroll
+        for (int k = 0; k < MAXL; k++) {
+            const int i = tid + k * nthr;
+            float v = 0.0f;
+            if (i < nv) {
+                const int r = r0 + i / DC;
+                if (r < n) v = vg[(int64_t)r * hd + i % DC];
+            } else if (i < nv + np) {
+                const int j = i - nv, r = r0 + j % VT;
+                if (r < n) v = pg[(int64_t)(j / VT) * max_seq + r];
+            }
+            reg[k] = v;
+        }
+    };
+    auto store = [&](int b) {
+#pragma unroll
+        for (int k = 0; k < MAXL; k++) {
+            const int i = tid + k * nthr;
+            if (i < nv) vbuf[b * nv + i] = reg[k];
+            else if (i < nv + np) pbuf[b * np + (i - nv)] = reg[k];
+        }
+    };
+    load(0);
+    store(0);
     __syncthreads();
-    const float *vg = vc + (int64_t)g * max_seq * hd;
-    float *o = att + ((int64_t)t * H + h) * hd;
-    for (int d = tid; d < hd; d += blockDim.x) {
-        float acc = 0.0f;
-        int r = 0;
-        for (; r + 4 <= n; r += 4) {   // loads run ahead; the adds stay in position order
-            const float v0 = vg[(int64_t)r * hd + d], v1 = vg[(int64_t)(r + 1) * hd + d];
-            const float v2 = vg[(int64_t)(r + 2) * hd + d], v3 = vg[(int64_t)(r + 3) * hd + d];
-            acc = __fadd_rn(acc, __fmul_rn(p[r], v0));
-            acc = __fadd_rn(acc, __fmul_rn(p[r + 1], v1));
-            acc = __fadd_rn(acc, __fmul_rn(p[r + 2], v2));
-            acc = __fadd_rn(acc, __fmul_rn(p[r + 3], v3));
+    float acc = 0.0f;
+    const int ntile = (n + VT - 1) / VT;
+    for (int it = 0; it < ntile; it++) {
+        const int b = it & 1;
+        if (it + 1 < ntile) load((it + 1) * VT);   // in flight while this tile's chains run
+        if (chain) {
+            const float *vb = vbuf + b * nv + d;
+            const float *pb = pbuf + b * np + hh * VT;
+            const int m = min(VT, n - it * VT);
+            for (int r = 0; r < m; r++) acc = __fadd_rn(acc, __fmul_rn(pb[r], vb[r * DC]));
         }
-        for (; r < n; r++) acc = __fadd_rn(acc, __fmul_rn(p[r], vg[(int64_t)r * hd + d]));
-        o[d] = acc;
+        if (it + 1 < ntile) store(b ^ 1);
+        __syncthreads();
     }
-    if (act) {   // head_dim a multiple of 64: this head's activation blocks of the o projection's input
-        __syncthreads();   // every o[d] of the head written (read back through L1: same CTA)
-        const int nbh = hd / QK, nb = H * nbh;
-        for (int b = warp; b < nbh; b += blockDim.x >> 5) {
-            const float *ob = o + b * QK;
-            act_quant_warp(ob[lane], ob[lane + 32], act + (int64_t)t * nb + h * nbh + b, lane);
-        }
+    if (chain) att[((int64_t)t * H + g * grp + hh) * hd + dc * DC + d] = acc;
+    if (act) {   // DC == 64: one activation block per head of this CTA
+        if (chain) ost[tid] = acc;
+        __syncthreads();
+        const int warp = tid >> 5, lane = tid & 31, nb = H * hd / QK;
+        for (int w = warp; w < grp; w += nthr >> 5)
+            act_quant_warp(ost[w * DC + lane], ost[w * DC + lane + 32],
+                           act + (int64_t)t * nb + ((int64_t)(g * grp + w) * hd + dc * DC) / QK, lane);
     }
 }
 
@@ -500,14 +569,18 @@ static bool fuse_qkv(DLayer &w) {
 // memory; null, or why not.
 static const char *alloc_runtime(hxb_model *m) {
     // dynamic shared memory of the attention kernels: q and k rows of a token, a head's scores
-    const size_t post_smem = sizeof(float) * (size_t)(m->q_dim + m->kv_dim), sv_smem = sizeof(float) * (size_t)m->max_seq;
+    const size_t post_smem = sizeof(float) * (size_t)(m->q_dim + m->kv_dim), sm_smem = sizeof(float) * (size_t)m->max_seq;
+    const int grp = m->H / m->Hkv;
+    m->dc = m->hd % 64 == 0 ? 64 : m->hd;   // value-kernel dims per CTA (64: whole activation blocks)
+    m->vthreads = (std::max(grp * m->dc, (VT * m->dc + grp * VT + 3) / 4) + 31) / 32 * 32;
+    if (m->vthreads > 1024 || m->dc < 16)
+        return "model_open: attention heads per kv group times head_dim beyond the value kernel's CTA";
     int smem_max = 0;
     cudaDeviceGetAttribute(&smem_max, cudaDevAttrMaxSharedMemoryPerBlockOptin, m->device);
-    if (post_smem > (size_t)smem_max || sv_smem + 64 > (size_t)smem_max || sizeof(float) * (size_t)m->D > 48 * 1024)
+    if (post_smem > (size_t)smem_max || sm_smem + 64 > (size_t)smem_max || sizeof(float) * (size_t)m->D > 48 * 1024)
         return "model_open: max_seq or the attention width exceeds shared memory";
     if (cudaFuncSetAttribute(k_attn_post, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)post_smem) != cudaSuccess ||
-        cudaFuncSetAttribute(k_attn_softmax_values, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)sv_smem) !=
-            cudaSuccess)
+        cudaFuncSetAttribute(k_attn_softmax, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)sm_smem) != cudaSuccess)
         return "model_open: shared memory attributes refused";
     // KV cache and scratch
     const size_t T = (size_t)m->max_batch, S = (size_t)m->max_seq;
@@ -822,15 +895,22 @@ static int attention(hxb_model *m, int l, int T, cudaStream_t s) {
     a.rope_style = m->rope_style;
     a.max_seq = m->max_seq;
     a.eps = m->eps;
-    k_attn_post<<<T, 256, sizeof(float) * (m->q_dim + m->kv_dim), s>>>(a);
+    if (m->qk_norm == 2)
+        k_attn_post<<<dim3(T, 1), 256, sizeof(float) * (m->q_dim + m->kv_dim), s>>>(a);
+    else
+        k_attn_post<<<dim3(T, (m->H + m->Hkv + 7) / 8), 256, sizeof(float) * 8 * m->hd, s>>>(a);
     // the score CTAs of a (token, head) stride over the positions: about 600 CTAs in all
     const int chunks = std::max(1, std::min((int)blocks(m->max_seq, 16), 600 / (m->H * T)));
     k_attn_scores<<<dim3(chunks, m->H, T), 256, 0, s>>>(a.qout, a.kc, m->S.as<float>(), m->H, m->Hkv, m->hd,
                                                          m->max_seq, a.dpos, m->attn_scale);
-    // the o projection's activation blocks come out of the value kernel when a head holds whole blocks
-    const bool fuse_act = is_quant(w.o.dtype) && m->hd % QK == 0;
-    k_attn_softmax_values<<<dim3(m->H, T), 128, sizeof(float) * m->max_seq, s>>>(
-        m->S.as<float>(), a.vc, m->att.as<float>(), fuse_act ? act : nullptr, m->H, m->Hkv, m->hd, m->max_seq, a.dpos);
+    k_attn_softmax<<<dim3(m->H, T), 256, sizeof(float) * m->max_seq, s>>>(m->S.as<float>(), m->H, m->max_seq, a.dpos);
+    // the o projection's activation blocks come out of the value kernel when a CTA holds whole blocks
+    const bool fuse_act = is_quant(w.o.dtype) && m->dc == 64;
+    const int grp = m->H / m->Hkv;
+    const size_t vsm = sizeof(float) * (size_t)(2 * VT * m->dc + 2 * grp * VT + grp * m->dc);
+    k_attn_values<<<dim3(m->Hkv * (m->hd / m->dc), T), m->vthreads, vsm, s>>>(
+        m->S.as<float>(), a.vc, m->att.as<float>(), fuse_act ? act : nullptr, m->H, m->Hkv, m->hd, m->dc, m->max_seq,
+        a.dpos);
     if (!mcuda(cudaGetLastError(), "attention")) return HXB_E_DEVICE;
     bool aready = fuse_act;
     // h += rs * (Wo att): the residual in the matmul's epilogue

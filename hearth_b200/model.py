@@ -17,6 +17,7 @@ import numpy as np
 
 from . import _lib
 from ._lib import check, lib
+from .moe import _stream
 
 
 class _Synthetic:
@@ -74,14 +75,14 @@ class Model:
 
     def forward_dev(self, tokens, pos0: int, mode: int, logits=None, stream=None) -> None:
         """forward() on torch CUDA tensors (tokens int32 [T], logits float32 [1 or T, V]), asynchronous
-        on `stream` (a torch stream; None: the handle's own)."""
-        sp = None if stream is None else stream.cuda_stream
+        on `stream` (a torch stream, its default stream meaning the legacy default stream; None: the
+        handle's own)."""
         check(lib().hxb_model_forward_dev(self.h, tokens.data_ptr(), tokens.numel(), pos0,
-                                          logits.data_ptr() if logits is not None else None, mode, sp),
+                                          logits.data_ptr() if logits is not None else None, mode, _stream(stream)),
               "hxb_model_forward_dev")
 
     def sync(self, stream=None) -> None:
-        check(lib().hxb_model_sync(self.h, None if stream is None else stream.cuda_stream), "hxb_model_sync")
+        check(lib().hxb_model_sync(self.h, _stream(stream)), "hxb_model_sync")
 
     def eval(self, tokens, all_logits: bool = False) -> np.ndarray:
         """hearth_eval: the tokens in chunks of max_batch from the current position; the last token's

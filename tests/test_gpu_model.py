@@ -28,9 +28,9 @@ def _path(name):
 
 def _trace_rows(path):
     raw = open(path, "rb").read()
-    hdr = np.frombuffer(raw[:24], np.uint32)
+    hdr = np.frombuffer(raw[:24], np.uint32)   # magic, version, n_layers, n_experts, top_k, n_moe_layers
     assert hdr[0] == 0x52545248 and hdr[1] == 1
-    w = int(hdr[4]) * int(hdr[3])
+    w = int(hdr[5]) * int(hdr[4])
     return np.frombuffer(raw[24:], np.uint16).reshape(-1, w)
 
 
