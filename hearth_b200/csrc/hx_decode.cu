@@ -184,7 +184,8 @@ struct DecodeArgs {
     float *h;                     // [D] in / out
     float *xbuf;                  // two exchange sets of xset_floats(Lb, ...) floats, kEmpty at rest
     int Lb;
-    unsigned *epoch;              // [2]: launch counter (set = epoch & 1), CTAs done with this launch
+    unsigned *epoch;              // [4]: launch counter (set = epoch & 1), CTAs done with this launch,
+                                  // buffer layers last used in set 0 / set 1
     int *err;
     int *ids_out;                 // [K] routing of the last layer
     float *w_out;
@@ -431,7 +432,7 @@ __device__ void decode_body(const DecodeArgs &a, uint8_t *smem) {
     __shared__ float rms_r;
     __shared__ float pred_part[DEC_WARPS];
     __shared__ int pred_ids[16];
-    __shared__ unsigned s_epoch;
+    __shared__ unsigned s_epoch, s_prev;
 
     for (int i = tid; i < a.Lyr; i += DEC_THREADS) {
         p_router[i] = a.router[i];
@@ -440,6 +441,8 @@ __device__ void decode_body(const DecodeArgs &a, uint8_t *smem) {
     }
     if (tid == 0) {
         s_epoch = *(volatile unsigned *)a.epoch;
+        // buffer layers the previous launch used in the other set (launches may differ in layers)
+        s_prev = ((volatile unsigned *)a.epoch)[2 + ((s_epoch & 1u) ^ 1u)];
         for (int i = 0; i < 32; i++) mbar_init(&bars[i], 1);
         fence_mbar_init();
     }
@@ -692,7 +695,8 @@ __device__ void decode_body(const DecodeArgs &a, uint8_t *smem) {
         }
         {   // reset this CTA's share of the other set's slots of buffer layers [b0, b1) for the next launch
             // (while this CTA waits for the other CTAs' mid values anyway)
-            const int b0 = (int)((int64_t)a.Lb * l / a.Lyr), b1 = (int)((int64_t)a.Lb * (l + 1) / a.Lyr);
+            const int np = (int)min(s_prev, (unsigned)a.Lb);
+            const int b0 = (int)((int64_t)np * l / a.Lyr), b1 = (int)((int64_t)np * (l + 1) / a.Lyr);
             const int64_t per_layer[5] = {E, E, (int64_t)K * F, (int64_t)K * D, D};
             const int64_t base[5] = {o_lg, o_pr, o_mid, o_y, o_h};
             for (int k = 0; k < 5; k++)
@@ -763,6 +767,7 @@ __device__ void decode_body(const DecodeArgs &a, uint8_t *smem) {
         // the last CTA to finish advances the launch counter (every CTA read it at its start)
         if (atomicAdd(a.epoch + 1, 1u) == (unsigned)G - 1) {
             a.epoch[1] = 0u;
+            a.epoch[2 + (s_epoch & 1u)] = (unsigned)a.Lyr;   // what the next launch resets of this set
             a.epoch[0] = s_epoch + 1u;
         }
     }

@@ -169,7 +169,8 @@ struct DecodeParams {
     float *h;                     // [D]
     float *xbuf;                  // decode_xbuf_floats(buf_layers, ...) floats, 0xffffffff at allocation
     int buf_layers;               // layers the exchange buffers hold (>= n_layers)
-    unsigned *epoch;              // [2] launch counter and arrival count, zero at allocation
+    unsigned *epoch;              // [4] launch counter, arrival count, buffer layers last used by set 0 / 1;
+                                  // zero at allocation
     int *err;
     int *ids_out;
     float *w_out;

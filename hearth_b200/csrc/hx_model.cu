@@ -95,8 +95,9 @@ struct hxb_model {
     // shape (engine/src/model.c:1394-1439 setup_dims, GQA)
     int L = 0, D = 0, V = 0, H = 0, Hkv = 0, hd = 0, q_dim = 0, kv_dim = 0, rope_dim = 0, rope_half = 0;
     int rope_style = 0, qk_norm = 0, qkv_bias = 0, Fd = 0, n_moe = 0, K = 0, E = 0, max_in = 0, dc = 64, vthreads = 0;
+    size_t vsmem = 0;
     float eps = 1e-6f, rs = 1.0f, es = 1.0f, ls = 1.0f, attn_scale = 1.0f, rope_factor = 1.0f;
-    int max_batch = 0, max_seq = 0;
+    int max_batch = 0, max_seq = 0, kv_seq = 0;   // kv_seq: max_seq rounded up to 32, the cache's stride
     std::vector<float> inv_freq;
     Mat tok_embd, lm_head;
     Buf out_norm;
@@ -334,77 +335,67 @@ __global__ void __launch_bounds__(256) k_attn_softmax(float *__restrict__ S, int
 }
 
 // o_h[d] = sum_r p_h[r] * v_r[d] in position order from 0.0f (value_sum, model.c:552-590), one CTA
-// per (token, kv group, DC dims): thread (hh, d) runs the chain of head g*grp + hh, dim d. Each V row
-// slice is read once for the group's heads: tiles of VT positions (V and p) are staged in shared
-// memory, the next tile's loads issued into registers before the current tile's chains run. With
-// DC = 64 the CTA also forms the o projection's activation blocks of its heads (act not null).
-constexpr int VT = 32;
+// per (token, kv group, DC dims): thread (hh, d) runs the chain of head g*grp + hh, dim d. Tiles of VT
+// positions stream into a ring of shared-memory stages by 1-D bulk copies (the V rows of the tile,
+// contiguous in the cache, and the group's VT probabilities per head), so each V row is read once
+// for the group's heads while the chains run on the previous tiles. With DC = 64 the CTA also forms
+// the o projection's activation blocks of its heads (act not null). max_seq is a multiple of VT.
+constexpr int VT = 32, V_NST = 4;
 __global__ void __launch_bounds__(1024) k_attn_values(const float *__restrict__ S, const float *__restrict__ vc,
                                                       float *__restrict__ att, act_q8 *__restrict__ act, int H,
                                                       int Hkv, int hd, int DC, int max_seq,
                                                       const int *__restrict__ dpos) {
-    extern __shared__ float sm[];
+    extern __shared__ __align__(128) uint8_t smv[];
     const int grp = H / Hkv, nd = hd / DC;
     const int t = blockIdx.y, g = blockIdx.x / nd, dc = blockIdx.x - g * nd;
-    const int tid = threadIdx.x, nthr = blockDim.x;   // >= grp * DC: the first grp * DC threads run chains
+    const int tid = threadIdx.x;
     const int hh = tid / DC, d = tid - hh * DC;
     const bool chain = tid < grp * DC;
     const int n = *dpos + t + 1;
-    float *vbuf = sm;                       // [2][VT][DC]
-    float *pbuf = sm + 2 * VT * DC;         // [2][grp][VT]
-    float *ost = pbuf + 2 * grp * VT;       // [grp][DC]
-    const float *vg = vc + (int64_t)g * max_seq * hd + dc * DC;
+    uint64_t *bars = reinterpret_cast<uint64_t *>(smv);
+    float *vbuf = reinterpret_cast<float *>(smv + 128);          // [V_NST][VT][hd]
+    float *pbuf = vbuf + V_NST * VT * hd;                         // [V_NST][grp][VT]
+    float *ost = pbuf + V_NST * grp * VT;                         // [grp][DC]
+    const float *vg = vc + (int64_t)g * max_seq * hd;
     const float *pg = S + ((int64_t)t * H + g * grp) * max_seq;
-    const int nv = VT * DC, np = grp * VT;
-    // per thread: elements i = tid + k * nthr of the tile's V part, then of its p part
-    constexpr int MAXL = 4;   // the launch gives at least (VT * DC + grp * VT) / 4 threads
-    float reg[MAXL];
-    auto load = [&](int r0) {
-#pragma unroll
-        for (int k = 0; k < MAXL; k++) {
-            const int i = tid + k * nthr;
-            float v = 0.0f;
-            if (i < nv) {
-                const int r = r0 + i / DC;
-                if (r < n) v = vg[(int64_t)r * hd + i % DC];
-            } else if (i < nv + np) {
-                const int j = i - nv, r = r0 + j % VT;
-                if (r < n) v = pg[(int64_t)(j / VT) * max_seq + r];
-            }
-            reg[k] = v;
-        }
-    };
-    auto store = [&](int b) {
-#pragma unroll
-        for (int k = 0; k < MAXL; k++) {
-            const int i = tid + k * nthr;
-            if (i < nv) vbuf[b * nv + i] = reg[k];
-            else if (i < nv + np) pbuf[b * np + (i - nv)] = reg[k];
-        }
-    };
-    load(0);
-    store(0);
-    __syncthreads();
-    float acc = 0.0f;
     const int ntile = (n + VT - 1) / VT;
+    if (tid == 0) {
+        for (int st = 0; st < V_NST; st++) mbar_init(&bars[st], 1);
+        fence_mbar_init();
+    }
+    __syncthreads();
+    auto issue = [&](int it) {
+        const int st = it % V_NST, r0 = it * VT;
+        mbar_expect_tx(&bars[st], (uint32_t)(VT * hd * 4 + grp * VT * 4));
+        bulk_g2s(vbuf + st * VT * hd, vg + (int64_t)r0 * hd, (uint32_t)(VT * hd * 4), &bars[st]);
+        for (int j = 0; j < grp; j++)
+            bulk_g2s(pbuf + (st * grp + j) * VT, pg + (int64_t)j * max_seq + r0, (uint32_t)(VT * 4), &bars[st]);
+    };
+    if (tid == 0)
+        for (int it = 0; it < min(V_NST, ntile); it++) issue(it);
+    float acc = 0.0f;
+    bool ok = true;
     for (int it = 0; it < ntile; it++) {
-        const int b = it & 1;
-        if (it + 1 < ntile) load((it + 1) * VT);   // in flight while this tile's chains run
-        if (chain) {
-            const float *vb = vbuf + b * nv + d;
-            const float *pb = pbuf + b * np + hh * VT;
+        const int st = it % V_NST;
+        ok = ok && mbar_wait(&bars[st], (uint32_t)((it / V_NST) & 1), nullptr);
+        if (ok && chain) {
+            const float *vb = vbuf + st * VT * hd + dc * DC + d;
+            const float *pb = pbuf + (st * grp + hh) * VT;
             const int m = min(VT, n - it * VT);
-            for (int r = 0; r < m; r++) acc = __fadd_rn(acc, __fmul_rn(pb[r], vb[r * DC]));
+            for (int r = 0; r < m; r++) acc = __fadd_rn(acc, __fmul_rn(pb[r], vb[r * hd]));
         }
-        if (it + 1 < ntile) store(b ^ 1);
-        __syncthreads();
+        __syncthreads();   // every chain is done with this stage
+        if (tid == 0 && it + V_NST < ntile) {
+            fence_proxy_async();
+            issue(it + V_NST);
+        }
     }
     if (chain) att[((int64_t)t * H + g * grp + hh) * hd + dc * DC + d] = acc;
     if (act) {   // DC == 64: one activation block per head of this CTA
         if (chain) ost[tid] = acc;
         __syncthreads();
         const int warp = tid >> 5, lane = tid & 31, nb = H * hd / QK;
-        for (int w = warp; w < grp; w += nthr >> 5)
+        for (int w = warp; w < grp; w += (int)(blockDim.x >> 5))
             act_quant_warp(ost[w * DC + lane], ost[w * DC + lane + 32],
                            act + (int64_t)t * nb + ((int64_t)(g * grp + w) * hd + dc * DC) / QK, lane);
     }
@@ -572,18 +563,32 @@ static const char *alloc_runtime(hxb_model *m) {
     const size_t post_smem = sizeof(float) * (size_t)(m->q_dim + m->kv_dim), sm_smem = sizeof(float) * (size_t)m->max_seq;
     const int grp = m->H / m->Hkv;
     m->dc = m->hd % 64 == 0 ? 64 : m->hd;   // value-kernel dims per CTA (64: whole activation blocks)
-    m->vthreads = (std::max(grp * m->dc, (VT * m->dc + grp * VT + 3) / 4) + 31) / 32 * 32;
-    if (m->vthreads > 1024 || m->dc < 16)
+    m->vthreads = (grp * m->dc + 31) / 32 * 32;
+    m->vsmem = 128 + sizeof(float) * (size_t)(V_NST * VT * m->hd + V_NST * grp * VT + grp * m->dc);
+    if (m->vthreads > 1024 || m->hd % 4)
         return "model_open: attention heads per kv group times head_dim beyond the value kernel's CTA";
     int smem_max = 0;
     cudaDeviceGetAttribute(&smem_max, cudaDevAttrMaxSharedMemoryPerBlockOptin, m->device);
-    if (post_smem > (size_t)smem_max || sm_smem + 64 > (size_t)smem_max || sizeof(float) * (size_t)m->D > 48 * 1024)
+    if (post_smem + 1024 > (size_t)smem_max || sizeof(float) * 8 * (size_t)m->hd + 1024 > (size_t)smem_max ||
+        sm_smem + 1024 > (size_t)smem_max || m->vsmem + 1024 > (size_t)smem_max ||
+        sizeof(float) * (size_t)m->D > 48 * 1024)
         return "model_open: max_seq or the attention width exceeds shared memory";
-    if (cudaFuncSetAttribute(k_attn_post, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)post_smem) != cudaSuccess ||
-        cudaFuncSetAttribute(k_attn_softmax, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)sm_smem) != cudaSuccess)
+    // the attribute is the device's limit, not this model's need: it is per function, shared by every
+    // model of the process
+    cudaFuncAttributes fp{}, fs{}, fv{};
+    if (cudaFuncGetAttributes(&fp, (const void *)k_attn_post) != cudaSuccess ||
+        cudaFuncGetAttributes(&fs, (const void *)k_attn_softmax) != cudaSuccess ||
+        cudaFuncGetAttributes(&fv, (const void *)k_attn_values) != cudaSuccess ||
+        cudaFuncSetAttribute(k_attn_values, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                             smem_max - (int)fv.sharedSizeBytes) != cudaSuccess ||
+        cudaFuncSetAttribute(k_attn_post, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                             smem_max - (int)fp.sharedSizeBytes) != cudaSuccess ||
+        cudaFuncSetAttribute(k_attn_softmax, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                             smem_max - (int)fs.sharedSizeBytes) != cudaSuccess)
         return "model_open: shared memory attributes refused";
     // KV cache and scratch
-    const size_t T = (size_t)m->max_batch, S = (size_t)m->max_seq;
+    m->kv_seq = (m->max_seq + 31) / 32 * 32;
+    const size_t T = (size_t)m->max_batch, S = (size_t)m->kv_seq;
     const size_t kvb = sizeof(float) * (size_t)m->L * m->Hkv * S * m->hd;
     const size_t actb = T * ((size_t)m->max_in / QK + 1) * sizeof(act_q8);
     const size_t rows = std::max<size_t>(1, (size_t)m->n_moe * T * m->K);
@@ -873,7 +878,7 @@ static int attention(hxb_model *m, int l, int T, cudaStream_t s) {
         if (!rc) rc = matmul(m, w.v, x, m->D, act, ready, T, qkv + m->q_dim + m->kv_dim, ld, s);
     }
     if (rc) return rc;
-    const size_t layer_kv = (size_t)m->Hkv * m->max_seq * m->hd;
+    const size_t layer_kv = (size_t)m->Hkv * m->kv_seq * m->hd;
     PostArgs a;
     a.qkv = qkv;
     a.ld = ld;
@@ -893,7 +898,7 @@ static int attention(hxb_model *m, int l, int T, cudaStream_t s) {
     a.qk_norm = m->qk_norm;
     a.rope_half = m->rope_half;
     a.rope_style = m->rope_style;
-    a.max_seq = m->max_seq;
+    a.max_seq = m->kv_seq;
     a.eps = m->eps;
     if (m->qk_norm == 2)
         k_attn_post<<<dim3(T, 1), 256, sizeof(float) * (m->q_dim + m->kv_dim), s>>>(a);
@@ -902,14 +907,13 @@ static int attention(hxb_model *m, int l, int T, cudaStream_t s) {
     // the score CTAs of a (token, head) stride over the positions: about 600 CTAs in all
     const int chunks = std::max(1, std::min((int)blocks(m->max_seq, 16), 600 / (m->H * T)));
     k_attn_scores<<<dim3(chunks, m->H, T), 256, 0, s>>>(a.qout, a.kc, m->S.as<float>(), m->H, m->Hkv, m->hd,
-                                                         m->max_seq, a.dpos, m->attn_scale);
-    k_attn_softmax<<<dim3(m->H, T), 256, sizeof(float) * m->max_seq, s>>>(m->S.as<float>(), m->H, m->max_seq, a.dpos);
+                                                         m->kv_seq, a.dpos, m->attn_scale);
+    k_attn_softmax<<<dim3(m->H, T), 256, sizeof(float) * m->max_seq, s>>>(m->S.as<float>(), m->H, m->kv_seq, a.dpos);
     // the o projection's activation blocks come out of the value kernel when a CTA holds whole blocks
     const bool fuse_act = is_quant(w.o.dtype) && m->dc == 64;
     const int grp = m->H / m->Hkv;
-    const size_t vsm = sizeof(float) * (size_t)(2 * VT * m->dc + 2 * grp * VT + grp * m->dc);
-    k_attn_values<<<dim3(m->Hkv * (m->hd / m->dc), T), m->vthreads, vsm, s>>>(
-        m->S.as<float>(), a.vc, m->att.as<float>(), fuse_act ? act : nullptr, m->H, m->Hkv, m->hd, m->dc, m->max_seq,
+    k_attn_values<<<dim3(m->Hkv * (m->hd / m->dc), T), m->vthreads, m->vsmem, s>>>(
+        m->S.as<float>(), a.vc, m->att.as<float>(), fuse_act ? act : nullptr, m->H, m->Hkv, m->hd, m->dc, m->kv_seq,
         a.dpos);
     if (!mcuda(cudaGetLastError(), "attention")) return HXB_E_DEVICE;
     bool aready = fuse_act;
