@@ -101,7 +101,9 @@ constexpr int GV_TMAX = 4;
 template <int DT>
 __global__ void __launch_bounds__(256) k_gemv_staged(const uint8_t *__restrict__ W, int64_t rows, int nb, int64_t rb,
                                                      int R, const act_q8 *__restrict__ act, int T,
-                                                     float *__restrict__ Y, int64_t ldy, float *resid, float rs) {
+                                                     float *__restrict__ Y, int64_t ldy, float *resid, float rs,
+                                                     const float *__restrict__ nh, const float *__restrict__ nw,
+                                                     float eps) {
     extern __shared__ __align__(128) uint8_t smem[];
     uint64_t *bars = reinterpret_cast<uint64_t *>(smem);
     uint8_t *ring = smem + 128;
@@ -125,7 +127,24 @@ __global__ void __launch_bounds__(256) k_gemv_staged(const uint8_t *__restrict__
     };
     if (tid == 0)
         for (int64_t k = 0; k < min((int64_t)GV_NST, mine); k++) issue(k);
-    {
+    if (nh) {   // one token: x = rmsnorm(nh, nw) (NUMERICS §4) and its activation blocks, formed here
+        __shared__ float rsh;
+        float *xs = reinterpret_cast<float *>(acts + (int64_t)T * nb) + 8 * GV_TMAX * 33;
+        const int n = nb * QK;
+        for (int i = tid; i < n; i += blockDim.x) xs[i] = nh[i];
+        __syncthreads();
+        if (tid < 16) {
+            float L = 0.0f;
+            for (int i = tid; i < n; i += 16) L = __fadd_rn(L, __fmul_rn(xs[i], xs[i]));
+            L = tree16(L, 0xffffu);
+            if (tid == 0) rsh = __fdiv_rn(1.0f, __fsqrt_rn(__fadd_rn(__fdiv_rn(L, (float)n), eps)));
+        }
+        __syncthreads();
+        const float r = rsh;
+        for (int i = tid; i < n; i += blockDim.x) xs[i] = __fmul_rn(__fmul_rn(xs[i], r), nw[i]);
+        __syncthreads();
+        for (int b = warp; b < nb; b += 8) act_quant_warp(xs[b * QK + lane], xs[b * QK + lane + 32], acts + b, lane);
+    } else {
         const uint32_t *src = reinterpret_cast<const uint32_t *>(act);
         uint32_t *dst = reinterpret_cast<uint32_t *>(acts);
         for (int64_t i = tid; i < (int64_t)T * nb * (ACT_BLOCK / 4); i += blockDim.x) dst[i] = src[i];
@@ -218,6 +237,46 @@ __global__ void __launch_bounds__(256) k_matmul_f(const uint8_t *__restrict__ W,
     if (valid && j == 0) mm_store(Y, resid, rs, t * ldy + r, canon(L));
 }
 
+// The staged GEMV's shared-memory attribute on the current device (once per device) and its SM count.
+static cudaError_t gemv_prepare(int dtype, int *sms) {
+    int dev = 0;
+    cudaGetDevice(&dev);
+    static bool attr_set[64][2] = {};   // per device: the attribute belongs to the device's context
+    const int di = dtype == Q4 ? 0 : 1;
+    if (dev < 0 || dev >= 64) return cudaErrorInvalidDevice;
+    if (!attr_set[dev][di]) {
+        cudaError_t e = dtype == Q4 ? cudaFuncSetAttribute(k_gemv_staged<Q4>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                                           220 * 1024)
+                                    : cudaFuncSetAttribute(k_gemv_staged<Q8>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                                           220 * 1024);
+        if (e != cudaSuccess) return e;
+        attr_set[dev][di] = true;
+    }
+    return cudaDeviceGetAttribute(sms, cudaDevAttrMultiProcessorCount, dev);
+}
+
+cudaError_t launch_gemv_norm(int dtype, const void *W, int64_t n_cols, int64_t rows, const float *h, const float *nw,
+                             float eps, float *Y, float *resid, float rs, cudaStream_t s) {
+    size_t smem = 0;
+    const int R = gemv_rows_per_stage(dtype, W, n_cols, rows, 1, &smem);
+    smem += sizeof(float) * (size_t)n_cols;
+    if (R <= 0 || smem > 220 * 1024) return cudaErrorNotSupported;
+    int sms = 148;
+    cudaError_t e = gemv_prepare(dtype, &sms);
+    if (e != cudaSuccess) return e;
+    const int64_t rb = row_bytes(dtype, n_cols);
+    const unsigned grid = (unsigned)std::min<int64_t>((rows + R - 1) / R, sms);
+    const int nb = (int)(n_cols / QK);
+    const uint8_t *w = static_cast<const uint8_t *>(W);
+    if (dtype == Q4)
+        k_gemv_staged<Q4><<<grid, 256, smem, s>>>(w, rows, nb, rb, R, nullptr, 1, resid ? nullptr : Y, 0, resid, rs, h,
+                                                  nw, eps);
+    else
+        k_gemv_staged<Q8><<<grid, 256, smem, s>>>(w, rows, nb, rb, R, nullptr, 1, resid ? nullptr : Y, 0, resid, rs, h,
+                                                  nw, eps);
+    return cudaGetLastError();
+}
+
 cudaError_t launch_matmul(int dtype, const void *W, int64_t n_cols, const void *act, int T, float *Y,
                           int64_t ldy, int64_t r0, int64_t r1, cudaStream_t s) {
     return launch_matmul_resid(dtype, W, n_cols, act, T, Y, ldy, r0, r1, nullptr, 0.0f, s);
@@ -232,20 +291,9 @@ cudaError_t launch_matmul_resid(int dtype, const void *W, int64_t n_cols, const 
     size_t smem = 0;
     const int R = gemv_rows_per_stage(dtype, w + r0 * rb, n_cols, rows, T, &smem);
     if (R > 0) {   // few tokens: the rows stream through shared memory at the HBM rate
-        int dev = 0, sms = 148;
-        cudaGetDevice(&dev);
-        static bool attr_set[64][2] = {};   // per device: the attribute belongs to the device's context
-        const int di = dtype == Q4 ? 0 : 1;
-        if (dev < 0 || dev >= 64) return cudaErrorInvalidDevice;
-        if (!attr_set[dev][di]) {
-            cudaError_t e = dtype == Q4 ? cudaFuncSetAttribute(k_gemv_staged<Q4>,
-                                                               cudaFuncAttributeMaxDynamicSharedMemorySize, 220 * 1024)
-                                        : cudaFuncSetAttribute(k_gemv_staged<Q8>,
-                                                               cudaFuncAttributeMaxDynamicSharedMemorySize, 220 * 1024);
-            if (e != cudaSuccess) return e;
-            attr_set[dev][di] = true;
-        }
-        cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
+        int sms = 148;
+        cudaError_t e = gemv_prepare(dtype, &sms);
+        if (e != cudaSuccess) return e;
         const int64_t ntiles = (rows + R - 1) / R;
         const unsigned grid = (unsigned)std::min<int64_t>(ntiles, sms);
         const int nb = (int)(n_cols / QK);
@@ -253,10 +301,10 @@ cudaError_t launch_matmul_resid(int dtype, const void *W, int64_t n_cols, const 
         float *hr = resid ? resid + r0 : nullptr;
         if (dtype == Q4)
             k_gemv_staged<Q4><<<grid, 256, smem, s>>>(w + r0 * rb, rows, nb, rb, R, (const act_q8 *)act, T, Yr, ldy,
-                                                      hr, rs);
+                                                      hr, rs, nullptr, nullptr, 0.0f);
         else
             k_gemv_staged<Q8><<<grid, 256, smem, s>>>(w + r0 * rb, rows, nb, rb, R, (const act_q8 *)act, T, Yr, ldy,
-                                                      hr, rs);
+                                                      hr, rs, nullptr, nullptr, 0.0f);
         return cudaGetLastError();
     }
     if (is_quant(dtype)) {

@@ -120,6 +120,11 @@ cudaError_t init_tc_attributes();   // the staged tensor-core kernels (hx_prefil
 cudaError_t launch_act_quantize(const float *x, int64_t ldx, act_q8 *out, int64_t n, int T, cudaStream_t s);
 cudaError_t launch_matmul(int dtype, const void *W, int64_t n_cols, const void *act, int T, float *Y,
                           int64_t ldy, int64_t r0, int64_t r1, cudaStream_t s);
+// One token through the staged decode GEMV with x = rmsnorm(h, nw) formed in every CTA (the same
+// bits as a separate rmsnorm + activation quantization): Y[r] (or resid[r] += rs * y). Returns
+// cudaErrorNotSupported when the staged kernel does not take the shape (then norm and matmul separately).
+cudaError_t launch_gemv_norm(int dtype, const void *W, int64_t n_cols, int64_t rows, const float *h, const float *nw,
+                             float eps, float *Y, float *resid, float rs, cudaStream_t s);
 // The same with a residual epilogue: resid[t * ldy + r] += rs * y (Y unused) when resid is not null.
 cudaError_t launch_matmul_resid(int dtype, const void *W, int64_t n_cols, const void *act, int T, float *Y,
                                 int64_t ldy, int64_t r0, int64_t r1, float *resid, float rs, cudaStream_t s);

@@ -863,19 +863,28 @@ static int attention(hxb_model *m, int l, int T, cudaStream_t s) {
     float *x = m->x.as<float>();
     act_q8 *act = m->act.as<act_q8>();
     const bool quant_in = is_quant(w.q.dtype) && is_quant(w.k.dtype) && is_quant(w.v.dtype);
+    const int ld = m->q_dim + 2 * m->kv_dim;
+    float *qkv = m->q.as<float>();
+    int rc = HXB_OK;
+    // one token and one q|k|v matrix: the GEMV's CTAs form rmsnorm(h, attn_norm) themselves
+    cudaError_t fe = cudaErrorNotSupported;
+    if (T == 1 && w.qkv.w.p)
+        fe = launch_gemv_norm(w.qkv.dtype, w.qkv.w.p, m->D, w.qkv.rows, m->h.as<float>(), w.attn_norm.as<float>(),
+                              m->eps, qkv, nullptr, 0.0f, s);
+    if (fe != cudaErrorNotSupported) {
+        if (!mcuda(fe, "q|k|v")) return HXB_E_DEVICE;
+    } else {
     k_rmsnorm_rows<<<T, 256, sizeof(float) * m->D, s>>>(m->h.as<float>(), m->D, w.attn_norm.as<float>(), m->D, m->eps,
                                                           x, m->D, quant_in ? act : nullptr);
     if (!mcuda(cudaGetLastError(), "rmsnorm")) return HXB_E_DEVICE;
     bool ready = quant_in;
-    const int ld = m->q_dim + 2 * m->kv_dim;
-    float *qkv = m->q.as<float>();
-    int rc;
     if (w.qkv.w.p) {
         rc = matmul(m, w.qkv, x, m->D, act, ready, T, qkv, ld, s);
     } else {
         rc = matmul(m, w.q, x, m->D, act, ready, T, qkv, ld, s);
         if (!rc) rc = matmul(m, w.k, x, m->D, act, ready, T, qkv + m->q_dim, ld, s);
         if (!rc) rc = matmul(m, w.v, x, m->D, act, ready, T, qkv + m->q_dim + m->kv_dim, ld, s);
+    }
     }
     if (rc) return rc;
     const size_t layer_kv = (size_t)m->Hkv * m->kv_seq * m->hd;
@@ -970,13 +979,21 @@ static int enqueue_forward(hxb_model *m, int T, int mode, bool replay, cudaStrea
         float *x = m->x.as<float>();
         act_q8 *act = m->act.as<act_q8>();
         const bool q = is_quant(m->lm_head.dtype);
-        k_rmsnorm_rows<<<n, 256, sizeof(float) * m->D, s>>>(m->h.as<float>() + (size_t)first * m->D, m->D,
-                                                              m->out_norm.as<float>(), m->D, m->eps, x, m->D,
-                                                              q ? act : nullptr);
-        bool ready = q;
         Mat head = m->lm_head;
         head.w.p = m->lm_head.w.p ? m->lm_head.w.p : m->tok_embd.w.p;
-        rc = matmul(m, head, x, m->D, act, ready, n, m->logits.as<float>(), m->V, s);
+        cudaError_t fe = cudaErrorNotSupported;
+        if (n == 1)   // one row: the LM head's CTAs form rmsnorm(h, out_norm) themselves
+            fe = launch_gemv_norm(head.dtype, head.w.p, m->D, m->V, m->h.as<float>() + (size_t)first * m->D,
+                                  m->out_norm.as<float>(), m->eps, m->logits.as<float>(), nullptr, 0.0f, s);
+        if (fe != cudaErrorNotSupported) {
+            rc = mcuda(fe, "lm head") ? HXB_OK : HXB_E_DEVICE;
+        } else {
+            k_rmsnorm_rows<<<n, 256, sizeof(float) * m->D, s>>>(m->h.as<float>() + (size_t)first * m->D, m->D,
+                                                                  m->out_norm.as<float>(), m->D, m->eps, x, m->D,
+                                                                  q ? act : nullptr);
+            bool ready = q;
+            rc = matmul(m, head, x, m->D, act, ready, n, m->logits.as<float>(), m->V, s);
+        }
         if (rc == HXB_OK)
             k_scale<<<blocks((int64_t)n * m->V, 256), 256, 0, s>>>(m->logits.as<float>(), (int64_t)n * m->V, m->ls);
     }

@@ -14,6 +14,9 @@ Fixtures (3 layers, d_model 128, 8 experts of width 64, top-2, vocab 256, max_se
   tiny_qwen2_moe.hearth  GQA 4/2, q/k/v biases, gated shared expert; Q8 experts and dense
   tiny_deepseek_v3.hearth  MLA attention (q-lora, kv-lora, GPT-J RoPE), a dense first layer, grouped
                          sigmoid routing with bias, shared expert; Q4 / Q8
+  tiny_qwen3_moe_d512.hearth  the Qwen3 layout at d_model 512 (2 layers, 4 experts): rows of whole
+                         16-byte units, so the single-token path takes the staged GEMVs with the fused
+                         rmsnorm (q|k|v, LM head)
 """
 import argparse
 import os
@@ -22,8 +25,9 @@ import sys
 HERE = os.path.dirname(os.path.abspath(__file__))
 REPO = os.path.dirname(os.path.dirname(HERE))
 
-FIXTURES = [("qwen3_moe", "Q4", 11), ("olmoe", "Q4", 12), ("mixtral", "Q4", 13), ("qwen2_moe", "Q8", 14),
-            ("deepseek_v3", "Q4", 15)]
+FIXTURES = [("qwen3_moe", "Q4", 11, {}), ("olmoe", "Q4", 12, {}), ("mixtral", "Q4", 13, {}),
+            ("qwen2_moe", "Q8", 14, {}), ("deepseek_v3", "Q4", 15, {}),
+            ("qwen3_moe", "Q4", 16, dict(n_layers=2, d_model=512, n_experts=4, top_k=2, expert_ffn=64))]
 
 
 def main():
@@ -37,9 +41,10 @@ def main():
     os.environ.setdefault("HEARTH_LIB", os.path.join(REPO, "oracle", "_ref", "libhearth_ref.so"))
     from hearth import quant
     from hearth.synth import make_tiny
-    for arch, dt, seed in FIXTURES:
-        path = os.path.join(HERE, f"tiny_{arch}.hearth")
-        make_tiny(path, arch=arch, dtype=getattr(quant, dt), seed=seed)
+    for arch, dt, seed, shape in FIXTURES:
+        name = f"tiny_{arch}" + (f"_d{shape['d_model']}" if shape else "")
+        path = os.path.join(HERE, name + ".hearth")
+        make_tiny(path, arch=arch, dtype=getattr(quant, dt), seed=seed, **shape)
         print(path, os.path.getsize(path))
 
 

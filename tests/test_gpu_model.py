@@ -6,7 +6,8 @@ files written by hearth_trace_start). The containers are written by the referenc
 generator and container writer (tests/golden/make_tiny_models.py, make_container.py): GQA with
 per-head qk-norm (Qwen3), MHA with full-width qk-norm (OLMoE), GQA without qk-norm (Mixtral), q/k/v
 biases and a gated Q8 shared expert (Qwen2-MoE), a dense first layer with a grouped sigmoid router
-(tiny_moe)."""
+(tiny_moe), and the Qwen3 layout at d_model 512, whose single-token forwards take the staged GEMVs
+with the rmsnorm formed inside them."""
 import os
 
 import numpy as np
@@ -18,7 +19,7 @@ from tests.engine_util import REF_LIB, Engine, session
 pytestmark = pytest.mark.gpu
 
 GOLDEN = os.path.join(os.path.dirname(os.path.abspath(__file__)), "golden")
-MODELS = ["tiny_qwen3_moe", "tiny_olmoe", "tiny_mixtral", "tiny_qwen2_moe", "tiny_moe"]
+MODELS = ["tiny_qwen3_moe", "tiny_olmoe", "tiny_mixtral", "tiny_qwen2_moe", "tiny_moe", "tiny_qwen3_moe_d512"]
 PROMPT = [3, 1, 4, 1, 5, 9, 2, 6, 5, 3, 5, 8, 9, 7, 9, 3]
 
 
