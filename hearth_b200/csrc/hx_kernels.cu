@@ -379,14 +379,30 @@ __global__ void __launch_bounds__(256) k_moe_norm_act(const float *__restrict__ 
         act_quant_warp(xs[b * QK + lane], xs[b * QK + lane + 32], xact + (int64_t)t * nb + b, lane);
 }
 
+// The opt-in shared memory per block of the current device.
+static size_t smem_limit() {
+    static size_t lim = 0;
+    if (!lim) {
+        int dev = 0, v = 0;
+        cudaGetDevice(&dev);
+        cudaDeviceGetAttribute(&v, cudaDevAttrMaxSharedMemoryPerBlockOptin, dev);
+        lim = (size_t)v;
+    }
+    return lim;
+}
+
 // Router logits (F32 dot16 rows, canonical NaN) and the shared-expert gate logit, one 16-lane
 // group per (row, token). With fuse_route the last CTA to finish routes every token and builds
 // the buckets.
+// staged (one token): the CTA's rows and x arrive in shared memory by 1-D bulk copies first, so the
+// chains read shared memory and every CTA keeps its whole share of the router in flight at once.
 __global__ void __launch_bounds__(256) k_moe_router(MoeShape sh, const float *__restrict__ router,
                                                     const float *__restrict__ gate_inp,
-                                                    const float *__restrict__ bias, MoeScratch sc, int fuse_route) {
-    extern __shared__ float rsm[];
+                                                    const float *__restrict__ bias, MoeScratch sc, int fuse_route,
+                                                    int staged) {
+    extern __shared__ __align__(16) float rsm[];
     __shared__ int last;
+    __shared__ __align__(8) uint64_t rbar;
     const int D = sh.D, E = sh.route.E, T = sh.T;
     const int rows = E + (gate_inp ? 1 : 0);
     const int grp = threadIdx.x >> 4, j = threadIdx.x & 15;
@@ -394,10 +410,29 @@ __global__ void __launch_bounds__(256) k_moe_router(MoeShape sh, const float *__
     const bool valid = item < (int64_t)rows * T;
     const int r = valid ? (int)(item % rows) : 0;
     const int t = valid ? (int)(item / rows) : 0;
-    const float *x = sc.x + (int64_t)t * D;
-    const float *w = r < E ? router + (int64_t)r * D : gate_inp;
     float L = 0.0f;
-    if (valid) {
+    if (staged) {   // T == 1: item == row
+        const int r0 = blockIdx.x * (blockDim.x >> 4), nr = min((int)(blockDim.x >> 4), rows - r0);
+        float *xs = rsm, *ws = rsm + D;
+        if (threadIdx.x == 0) {
+            mbar_init(&rbar, 1);
+            fence_mbar_init();
+            mbar_expect_tx(&rbar, (uint32_t)((nr + 1) * D * 4));
+            bulk_g2s(xs, sc.x, (uint32_t)(D * 4), &rbar);
+            for (int k = 0; k < nr; k++)
+                bulk_g2s(ws + (int64_t)k * D, r0 + k < E ? router + (int64_t)(r0 + k) * D : gate_inp, (uint32_t)(D * 4),
+                         &rbar);
+        }
+        __syncthreads();
+        const bool ok = mbar_wait(&rbar, 0, sc.err);
+        if (valid && ok) {
+            const float *wr = ws + (int64_t)grp * D;
+#pragma unroll 8
+            for (int i = j; i < D; i += 16) L = __fadd_rn(L, __fmul_rn(wr[i], xs[i]));
+        }
+    } else if (valid) {
+        const float *x = sc.x + (int64_t)t * D;
+        const float *w = r < E ? router + (int64_t)r * D : gate_inp;
 #pragma unroll 8
         for (int i = j; i < D; i += 16) L = __fadd_rn(L, __fmul_rn(__ldg(w + i), x[i]));
     }
@@ -526,9 +561,8 @@ constexpr int GU_NCH = GU_ROWS / GU_CH;
 constexpr int DN_ROWS = 16;    // down rows per CTA
 
 struct GateUpCfg {
-    int nst;        // pipeline stages
     int ntok;       // tokens per pass
-    int64_t stage;  // bytes per stage (max over the jobs' dtypes)
+    int64_t ring;   // bytes of the copy ring; each job cuts it into stages of its own row size
     int nbD;
     int fmax_nb;    // activation blocks per mid row (max of F, Fs over 64)
 };
@@ -540,30 +574,33 @@ __device__ void gateup_body(const MoeShape &sh, const MoeScratch &sc, const Job 
     const int nbD = c.nbD;
     const int64_t rbD = row_bytes(DT, sh.D);
     const int64_t chunk = (int64_t)GU_CH * rbD;   // bytes of one matrix's stage rows
+    const int64_t stage = 2 * chunk;
+    const int nst = (int)min((int64_t)GU_NCH, c.ring / stage);   // >= 1: the host sized the ring for the widest rows
     uint64_t *bars = reinterpret_cast<uint64_t *>(smem);
     uint8_t *ring = smem + 128;
-    act_q8 *acts = reinterpret_cast<act_q8 *>(ring + (int64_t)c.nst * c.stage);
-    float *P = reinterpret_cast<float *>(acts + (int64_t)c.ntok * nbD) + warp * (32 * 33);
-    float *GU = reinterpret_cast<float *>(acts + (int64_t)c.ntok * nbD) + 8 * 32 * 33;   // [2][ntok][64]
+    act_q8 *acts = reinterpret_cast<act_q8 *>(ring + c.ring);
+    const int pw = 2 * c.ntok * 33;   // a warp's term buffer: 2 rows x ntok chains
+    float *P = reinterpret_cast<float *>(acts + (int64_t)c.ntok * nbD) + warp * pw;
+    float *GU = reinterpret_cast<float *>(acts + (int64_t)c.ntok * nbD) + 8 * pw;   // [2][ntok][64]
     int *tok_off = reinterpret_cast<int *>(GU + 2 * c.ntok * GU_ROWS);                  // [ntok]
 
     const int npass = (job.n + c.ntok - 1) / c.ntok;
     const int total = npass * GU_NCH;
     const uint8_t *g0 = job.gate + (int64_t)rb * GU_ROWS * rbD, *u0 = job.up + (int64_t)rb * GU_ROWS * rbD;
     if (tid == 0) {
-        for (int s = 0; s < c.nst; s++) mbar_init(&bars[s], 1);
+        for (int s = 0; s < nst; s++) mbar_init(&bars[s], 1);
         fence_mbar_init();
     }
     __syncthreads();
     auto issue = [&](int q) {   // thread 0: chunk q (pass q / GU_NCH, chunk q % GU_NCH)
-        const int s = q % c.nst, ch = q % GU_NCH;
-        uint8_t *dst = ring + (int64_t)s * c.stage;
+        const int s = q % nst, ch = q % GU_NCH;
+        uint8_t *dst = ring + (int64_t)s * stage;
         mbar_expect_tx(&bars[s], (uint32_t)(2 * chunk));
         bulk_g2s(dst, g0 + ch * chunk, (uint32_t)chunk, &bars[s]);
         bulk_g2s(dst + chunk, u0 + ch * chunk, (uint32_t)chunk, &bars[s]);
     };
     if (tid == 0)
-        for (int q = 0; q < min(c.nst, total); q++) issue(q);
+        for (int q = 0; q < min(nst, total); q++) issue(q);
     bool ok = true;
     for (int pass = 0; pass < npass; pass++) {
         const int i0 = pass * c.ntok, nt = min(c.ntok, job.n - i0);
@@ -577,10 +614,10 @@ __device__ void gateup_body(const MoeShape &sh, const MoeScratch &sc, const Job 
         if (tid < nt) tok_off[tid] = tid * nbD;
         __syncthreads();
         for (int ch = 0; ch < GU_NCH; ch++) {
-            const int q = pass * GU_NCH + ch, s = q % c.nst;
-            ok = ok && mbar_wait(&bars[s], (uint32_t)((q / c.nst) & 1), sc.err);
+            const int q = pass * GU_NCH + ch, s = q % nst;
+            ok = ok && mbar_wait(&bars[s], (uint32_t)((q / nst) & 1), sc.err);
             if (ok) {
-                const uint8_t *st = ring + (int64_t)s * c.stage;
+                const uint8_t *st = ring + (int64_t)s * stage;
                 // warp w: gate row w and up row w of this stage (rows 0..7 gate, 8..15 up)
                 const int rl[2] = {warp, GU_CH + warp};
                 const int row = ch * GU_CH + warp;   // row within the CTA's 64
@@ -591,9 +628,9 @@ __device__ void gateup_body(const MoeShape &sh, const MoeScratch &sc, const Job 
                 }
             }
             __syncthreads();
-            if (tid == 0 && q + c.nst < total) {
+            if (tid == 0 && q + nst < total) {
                 fence_proxy_async();
-                issue(q + c.nst);
+                issue(q + nst);
             }
         }
         if (!ok) break;
@@ -807,8 +844,15 @@ static void launch_route_stages(int which, const MoeShape &sh, const MoeLayerDev
             k_moe_router_tiled<<<dim3((unsigned)((T + RT_T - 1) / RT_T), (unsigned)((rows + RT_E - 1) / RT_E)), 256, 0,
                                  s>>>(sh, L.router, L.sh_gate_inp, sc);
         else
-            k_moe_router<<<grid, RT, fused ? route_smem : 0, s>>>(sh, L.router, L.sh_gate_inp, L.router_bias, sc,
-                                                                   fused ? 1 : 0);
+        {
+            // one token: stage the rows (RT / 16 per CTA) and x through shared memory when they fit
+            const size_t stage_smem = (size_t)(RT / 16 + 1) * sh.D * sizeof(float);
+            const bool staged = T == 1 && sh.D % 4 == 0 && stage_smem + 1024 <= smem_limit() &&
+                                (reinterpret_cast<uintptr_t>(sc.x) & 15) == 0;
+            const size_t smem = std::max(fused ? route_smem : (size_t)0, staged ? stage_smem : (size_t)0);
+            k_moe_router<<<grid, RT, smem, s>>>(sh, L.router, L.sh_gate_inp, L.router_bias, sc, fused ? 1 : 0,
+                                                staged ? 1 : 0);
+        }
         if (!fused) {
             k_route_select<<<(T + 7) / 8, 256, route_smem, s>>>(sh, L.router_bias, sc);
             k_route_union<<<1, 512, (size_t)(2 + 512 / 32) * E * sizeof(int), s>>>(sh, sc);
@@ -822,16 +866,6 @@ cudaError_t launch_moe_route(const MoeShape &sh, const MoeLayerDev &L, const Moe
     return cudaGetLastError();
 }
 
-static size_t smem_limit() {
-    static size_t lim = 0;
-    if (!lim) {
-        int dev = 0, v = 0;
-        cudaGetDevice(&dev);
-        cudaDeviceGetAttribute(&v, cudaDevAttrMaxSharedMemoryPerBlockOptin, dev);
-        lim = (size_t)v;
-    }
-    return lim;
-}
 
 cudaError_t init_kernel_attributes() {
     const int lim = (int)smem_limit();
@@ -840,6 +874,9 @@ cudaError_t init_kernel_attributes() {
     cudaError_t e = cudaFuncGetAttributes(&fa, (const void *)k_moe_gateup);
     if (e == cudaSuccess)
         e = cudaFuncSetAttribute(k_moe_gateup, cudaFuncAttributeMaxDynamicSharedMemorySize, lim - (int)fa.sharedSizeBytes);
+    if (e == cudaSuccess) e = cudaFuncGetAttributes(&fa, (const void *)k_moe_router);
+    if (e == cudaSuccess)
+        e = cudaFuncSetAttribute(k_moe_router, cudaFuncAttributeMaxDynamicSharedMemorySize, lim - (int)fa.sharedSizeBytes);
     if (e == cudaSuccess) e = cudaFuncGetAttributes(&fa, (const void *)k_moe_down);
     if (e == cudaSuccess)
         e = cudaFuncSetAttribute(k_moe_down, cudaFuncAttributeMaxDynamicSharedMemorySize, lim - (int)fa.sharedSizeBytes);
@@ -881,16 +918,20 @@ static cudaError_t launch_expert_stages(int which, const MoeShape &sh, const Moe
         c.fmax_nb = fmax_nb;
         int64_t rb = row_bytes(sh.F > 0 ? L.expert_dtype : Q4, sh.D);
         if (L.Fs > 0) rb = std::max<int64_t>(rb, row_bytes(L.sh_dtype, sh.D));
-        c.stage = 2 * GU_CH * rb;
+        const size_t stage_max = 2 * GU_CH * (size_t)rb;   // the widest job's stage
         c.ntok = std::min(8, std::max(1, T));
-        auto fixed = [&](int ntok) {
-            return (size_t)128 + (size_t)ntok * c.nbD * ACT_BLOCK + (size_t)8 * 32 * 33 * 4 +
+        auto fixed = [&](int ntok) {   // everything but the ring (P: 2 rows x ntok chains of 33 per warp)
+            return (size_t)128 + (size_t)ntok * c.nbD * ACT_BLOCK + (size_t)8 * 2 * ntok * 33 * 4 +
                    (size_t)2 * ntok * GU_ROWS * 4 + (size_t)ntok * 4 + 64;
         };
-        while (c.ntok > 1 && fixed(c.ntok) + (size_t)c.stage > lim) c.ntok /= 2;
-        c.nst = (int)std::min<int64_t>(GU_NCH, (int64_t)((lim - fixed(c.ntok)) / (size_t)c.stage));
-        if (c.nst < 1) return cudaErrorInvalidConfiguration;
-        const size_t smem = fixed(c.ntok) + (size_t)c.nst * c.stage;
+        while (c.ntok > 1 && fixed(c.ntok) + stage_max > lim) c.ntok /= 2;
+        if (fixed(c.ntok) + stage_max > lim) return cudaErrorInvalidConfiguration;
+        // the ring: 4 stages of the routed experts' rows where they fit (small rows leave room for a
+        // second CTA per SM), at least one stage of the widest rows
+        const size_t rb_min = (size_t)row_bytes(sh.F > 0 ? L.expert_dtype : L.sh_dtype, sh.D);
+        const size_t want = std::min(lim - fixed(c.ntok), (size_t)4 * 2 * GU_CH * rb_min) / 128 * 128;
+        c.ring = (int64_t)std::max(want, (stage_max + 127) / 128 * 128);
+        const size_t smem = fixed(c.ntok) + (size_t)c.ring;
         const int maxjobs = std::min(E, T * K) + (L.Fs > 0 ? 1 : 0);
         dim3 grid((unsigned)(std::max(sh.F, L.Fs) / GU_ROWS), (unsigned)maxjobs);
         k_moe_gateup<<<grid, 256, smem, s>>>(sh, L, sc, c);
