@@ -122,9 +122,9 @@ def step_bytes(B):
 
 
 # DRAM bytes (read + write) per layer of k_moe_decode from one ncu capture of a 4-layer launch of the
-# same shape (bench.py --layers 4: dram__bytes_read.sum 94.62 MB, dram__bytes_write.sum 2.69 MB); a
+# same shape (bench.py --layers 4: dram__bytes_read.sum 94.63 MB, dram__bytes_write.sum 2.89 MB); a
 # launch's traffic grows with its layers, so the full launch's figure is this times its layers.
-DECODE_DRAM_BYTES_PER_LAYER = (94_621_952 + 2_688_000) / 4
+DECODE_DRAM_BYTES_PER_LAYER = (94_631_424 + 2_893_312) / 4
 
 
 def workload_config(B, world, parallelism=None):

@@ -579,9 +579,10 @@ __device__ void gateup_body(const MoeShape &sh, const MoeScratch &sc, const Job 
     uint64_t *bars = reinterpret_cast<uint64_t *>(smem);
     uint8_t *ring = smem + 128;
     act_q8 *acts = reinterpret_cast<act_q8 *>(ring + c.ring);
-    const int pw = 2 * c.ntok * 33;   // a warp's term buffer: 2 rows x ntok chains
+    const int nw = blockDim.x >> 5;   // 16 warps: one row of each 16-row stage
+    const int pw = c.ntok * 33;         // a warp's term buffer: ntok chains
     float *P = reinterpret_cast<float *>(acts + (int64_t)c.ntok * nbD) + warp * pw;
-    float *GU = reinterpret_cast<float *>(acts + (int64_t)c.ntok * nbD) + 8 * pw;   // [2][ntok][64]
+    float *GU = reinterpret_cast<float *>(acts + (int64_t)c.ntok * nbD) + nw * pw;   // [2][ntok][64]
     int *tok_off = reinterpret_cast<int *>(GU + 2 * c.ntok * GU_ROWS);                  // [ntok]
 
     const int npass = (job.n + c.ntok - 1) / c.ntok;
@@ -618,13 +619,14 @@ __device__ void gateup_body(const MoeShape &sh, const MoeScratch &sc, const Job 
             ok = ok && mbar_wait(&bars[s], (uint32_t)((q / nst) & 1), sc.err);
             if (ok) {
                 const uint8_t *st = ring + (int64_t)s * stage;
-                // warp w: gate row w and up row w of this stage (rows 0..7 gate, 8..15 up)
-                const int rl[2] = {warp, GU_CH + warp};
-                const int row = ch * GU_CH + warp;   // row within the CTA's 64
+                // warp w: row w of this stage (rows 0..7 gate, 8..15 up)
+                const int rl[1] = {warp};
+                const int row = ch * GU_CH + (warp & (GU_CH - 1));   // row within the CTA's 64
+                float *out = GU + (warp >= GU_CH ? (int64_t)c.ntok * GU_ROWS : 0) + row;
                 for (int tg = 0; tg < nt; tg += 16) {
                     const int ntg = min(16, nt - tg);
-                    warp_rows<DT>(st, rbD, nbD, rl, 2, acts, tok_off + tg, ntg, P,
-                                  GU + (int64_t)tg * GU_ROWS + row, c.ntok * GU_ROWS, GU_ROWS);
+                    warp_rows<DT>(st, rbD, nbD, rl, 1, acts, tok_off + tg, ntg, P, out + (int64_t)tg * GU_ROWS, 0,
+                                  GU_ROWS);
                 }
             }
             __syncthreads();
@@ -635,7 +637,7 @@ __device__ void gateup_body(const MoeShape &sh, const MoeScratch &sc, const Job 
         }
         if (!ok) break;
         // SwiGLU and the mid activation block of each token (warp per token)
-        for (int i = warp; i < nt; i += 8) {
+        for (int i = warp; i < nt; i += nw) {
             const float *G = GU + i * GU_ROWS, *U = GU + c.ntok * GU_ROWS + i * GU_ROWS;
             const float m0 = swiglu_c(G[lane], U[lane]), m1 = swiglu_c(G[lane + 32], U[lane + 32]);
             act_q8 *dst = sc.act_mid + (int64_t)(job.p0 + i0 + i) * c.fmax_nb + rb;
@@ -645,7 +647,7 @@ __device__ void gateup_body(const MoeShape &sh, const MoeScratch &sc, const Job 
     }
 }
 
-__global__ void __launch_bounds__(256) k_moe_gateup(MoeShape sh, MoeLayerDev L, MoeScratch sc, GateUpCfg c) {
+__global__ void __launch_bounds__(512) k_moe_gateup(MoeShape sh, MoeLayerDev L, MoeScratch sc, GateUpCfg c) {
     extern __shared__ __align__(128) uint8_t smem[];
     const int u = blockIdx.y, rb = blockIdx.x;
     const int nu = routed_jobs(sh, sc);
@@ -672,7 +674,7 @@ __device__ void down_tile(const MoeShape &sh, const MoeScratch &sc, const Job &j
                           const uint8_t *tile, float *P, int *tok_off, float *Ys, float *Ss, int r0) {
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
     const int64_t rbF = row_bytes(DT, job.F);
-    const int rl[2] = {2 * warp, 2 * warp + 1};
+    const int rl[1] = {warp};   // 16 warps: one row of the 16-row tile each
     for (int i0 = 0; i0 < job.n; i0 += 16) {
         const int nt = min(16, job.n - i0);
         if (lane < nt) tok_off[lane] = (job.p0 + i0 + lane) * c.fmax_nb;
@@ -680,14 +682,14 @@ __device__ void down_tile(const MoeShape &sh, const MoeScratch &sc, const Job &j
         float *out;
         int oi;
         if (c.fused) {
-            out = job.shared ? Ss + (int64_t)i0 * DN_ROWS + 2 * warp : Ys + (int64_t)(job.p0 + i0) * DN_ROWS + 2 * warp;
+            out = job.shared ? Ss + (int64_t)i0 * DN_ROWS + warp : Ys + (int64_t)(job.p0 + i0) * DN_ROWS + warp;
             oi = DN_ROWS;
         } else {
-            out = job.shared ? sc.S + (int64_t)i0 * sh.D + r0 + 2 * warp
-                             : sc.Y + (int64_t)(job.p0 + i0) * sh.D + r0 + 2 * warp;
+            out = job.shared ? sc.S + (int64_t)i0 * sh.D + r0 + warp
+                             : sc.Y + (int64_t)(job.p0 + i0) * sh.D + r0 + warp;
             oi = sh.D;
         }
-        warp_rows<DT>(tile, rbF, job.nbF, rl, 2, sc.act_mid, tok_off, nt, P, out, 1, oi);
+        warp_rows<DT>(tile, rbF, job.nbF, rl, 1, sc.act_mid, tok_off, nt, P, out, 0, oi);
         __syncwarp();
     }
 }
@@ -714,7 +716,7 @@ __device__ __forceinline__ void finish_row(const MoeShape &sh, const MoeScratch 
     if (resid) h[idx] = __fadd_rn(h[idx], __fmul_rn(sh.residual_scale, o));
 }
 
-__global__ void __launch_bounds__(256) k_moe_down(MoeShape sh, MoeLayerDev L, MoeScratch sc, DownCfg c, float *h,
+__global__ void __launch_bounds__(512) k_moe_down(MoeShape sh, MoeLayerDev L, MoeScratch sc, DownCfg c, float *h,
                                                   float *out, int resid) {
     extern __shared__ __align__(128) uint8_t smem[];
     const int tid = threadIdx.x, warp = tid >> 5;
@@ -723,11 +725,12 @@ __global__ void __launch_bounds__(256) k_moe_down(MoeShape sh, MoeLayerDev L, Mo
     const int njobs = nu + (L.Fs > 0 ? 1 : 0);
     uint64_t *bars = reinterpret_cast<uint64_t *>(smem);
     uint8_t *ring = smem + 128;
-    float *P = reinterpret_cast<float *>(ring + (int64_t)c.nst * c.stage) + warp * (32 * 33);
-    int *tok_off = reinterpret_cast<int *>(reinterpret_cast<float *>(ring + (int64_t)c.nst * c.stage) + 8 * 32 * 33) +
+    // 16 warps: term buffers of 16 chains, token offsets, then the fused rows
+    float *P = reinterpret_cast<float *>(ring + (int64_t)c.nst * c.stage) + warp * (16 * 33);
+    int *tok_off = reinterpret_cast<int *>(reinterpret_cast<float *>(ring + (int64_t)c.nst * c.stage) + 16 * 16 * 33) +
                    warp * 16;
     float *Ys = reinterpret_cast<float *>(reinterpret_cast<int *>(reinterpret_cast<float *>(
-                                               ring + (int64_t)c.nst * c.stage) + 8 * 32 * 33) + 8 * 16);
+                                               ring + (int64_t)c.nst * c.stage) + 16 * 16 * 33) + 16 * 16);
     float *Ss = Ys + (int64_t)(c.fused ? c.max_pairs : 0) * DN_ROWS;
     if (tid == 0) {
         for (int s = 0; s < c.nst; s++) mbar_init(&bars[s], 1);
@@ -920,8 +923,8 @@ static cudaError_t launch_expert_stages(int which, const MoeShape &sh, const Moe
         if (L.Fs > 0) rb = std::max<int64_t>(rb, row_bytes(L.sh_dtype, sh.D));
         const size_t stage_max = 2 * GU_CH * (size_t)rb;   // the widest job's stage
         c.ntok = std::min(8, std::max(1, T));
-        auto fixed = [&](int ntok) {   // everything but the ring (P: 2 rows x ntok chains of 33 per warp)
-            return (size_t)128 + (size_t)ntok * c.nbD * ACT_BLOCK + (size_t)8 * 2 * ntok * 33 * 4 +
+        auto fixed = [&](int ntok) {   // everything but the ring (P: ntok chains of 33 per warp, 16 warps)
+            return (size_t)128 + (size_t)ntok * c.nbD * ACT_BLOCK + (size_t)16 * ntok * 33 * 4 +
                    (size_t)2 * ntok * GU_ROWS * 4 + (size_t)ntok * 4 + 64;
         };
         while (c.ntok > 1 && fixed(c.ntok) + stage_max > lim) c.ntok /= 2;
@@ -934,7 +937,7 @@ static cudaError_t launch_expert_stages(int which, const MoeShape &sh, const Moe
         const size_t smem = fixed(c.ntok) + (size_t)c.ring;
         const int maxjobs = std::min(E, T * K) + (L.Fs > 0 ? 1 : 0);
         dim3 grid((unsigned)(std::max(sh.F, L.Fs) / GU_ROWS), (unsigned)maxjobs);
-        k_moe_gateup<<<grid, 256, smem, s>>>(sh, L, sc, c);
+        k_moe_gateup<<<grid, 512, smem, s>>>(sh, L, sc, c);
     }
     // ---- down (+ rank-order sum for small batches)
     if (which & 2) {
@@ -945,13 +948,13 @@ static cudaError_t launch_expert_stages(int which, const MoeShape &sh, const Moe
         int64_t rbF = row_bytes(L.expert_dtype, sh.F);
         if (L.Fs > 0) rbF = std::max<int64_t>(rbF, row_bytes(L.sh_dtype, L.Fs));
         c.stage = ((int64_t)DN_ROWS * rbF + 127) / 128 * 128;
-        const size_t fixed = 128 + (size_t)8 * 32 * 33 * 4 + (size_t)8 * 16 * 4 +
+        const size_t fixed = 128 + (size_t)16 * 16 * 33 * 4 + (size_t)16 * 16 * 4 +
                              (fused ? (size_t)(T * K + T) * DN_ROWS * 4 : 0) + 64;
         const int maxjobs = std::min(E, T * K) + (L.Fs > 0 ? 1 : 0);
         c.nst = (int)std::min<int64_t>(std::min(maxjobs, 16), (int64_t)((lim - fixed) / (size_t)c.stage));
         if (c.nst < 1) return cudaErrorInvalidConfiguration;
         const size_t smem = fixed + (size_t)c.nst * c.stage;
-        k_moe_down<<<(unsigned)(sh.D / DN_ROWS), 256, smem, s>>>(sh, L, sc, c, h, out, resid ? 1 : 0);
+        k_moe_down<<<(unsigned)(sh.D / DN_ROWS), 512, smem, s>>>(sh, L, sc, c, h, out, resid ? 1 : 0);
         if (!fused && sh.ep_size == 1) {   // expert parallelism: the sum waits for the exchange
             const int64_t n = (int64_t)T * sh.D;
             k_moe_sum<<<(unsigned)((n + 255) / 256), 256, 0, s>>>(sh, L, sc, h, out, resid ? 1 : 0);
