@@ -660,6 +660,117 @@ __global__ void __launch_bounds__(512) k_moe_gateup(MoeShape sh, MoeLayerDev L, 
     else gateup_body<Q8>(sh, sc, job, c, smem, rb);
 }
 
+// ---- gate/up for single-token jobs (decode, T = 1): one CTA per (job, 64 mid rows), 8 warps; warp w
+// owns mid rows 8w..8w+7, i.e. gate rows and up rows 8w..8w+7 of its 64. It walks them in tiles of
+// 8 rows x 16 blocks that stream into its own 3 shared-memory slots by 1-D bulk copies (one per row),
+// lanes = (row phase, block) with each lane's activation block loaded once per tile, and lanes 0..7
+// carry the 8 rows' canonical chains across the tiles. SwiGLU and the mid activation block follow in
+// the CTA. Used when every row is a whole number of 16-byte units (D a multiple of 512).
+constexpr int G1_CW = 16, G1_NS = 3, G1_PS = 17;
+
+template <int DT>
+__device__ __forceinline__ void rows8_tile(const uint8_t *tile, int gn, const act_q8 *act, float *P, float &acc) {
+    constexpr int BS = DT == Q4 ? Q4_BLOCK : Q8_BLOCK;
+    const int lane = threadIdx.x & 31;
+    const int rp = 32 / gn, g = lane % gn, r2 = lane / gn;
+    if (r2 < rp) {
+        act_regs ar;
+        load_act(act + g, ar);
+        const uint8_t *col = tile + g * BS;
+        for (int k = r2; k < 8; k += rp) {
+            uint32_t wq[16];
+            int isum;
+            float dw;
+            if constexpr (DT == Q4) {
+                dw = f16_to_f32(load_q4_block(col + k * G1_CW * BS, wq));
+                isum = q4_isum(wq, ar.q, ar.sum);
+            } else {
+                dw = f16_to_f32(load_q8_block(col + k * G1_CW * BS, wq));
+                isum = q8_isum(wq, ar.q);
+            }
+            P[k * G1_PS + g] = __fmul_rn(__int2float_rn(isum), __fmul_rn(dw, ar.d));
+        }
+    }
+    __syncwarp();
+    if (lane < 8)
+        for (int gg = 0; gg < gn; gg++) acc = __fadd_rn(acc, P[lane * G1_PS + gg]);
+    __syncwarp();
+}
+
+template <int DT>
+__device__ void gateup1_body(const MoeShape &sh, const MoeScratch &sc, const Job &job, int fmax_nb, uint8_t *smem,
+                             int rb) {
+    constexpr int BS = DT == Q4 ? Q4_BLOCK : Q8_BLOCK;
+    constexpr int SLOT = 8 * G1_CW * BS;
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    const int nbD = sh.D / QK;
+    const int64_t rbD = row_bytes(DT, sh.D);
+    const int ntile = (nbD + G1_CW - 1) / G1_CW, total = 2 * ntile;   // gate tiles, then up tiles
+    uint64_t *bars = reinterpret_cast<uint64_t *>(smem) + warp * G1_NS;
+    uint8_t *slots = smem + 256 + (size_t)warp * G1_NS * SLOT;
+    act_q8 *acts = reinterpret_cast<act_q8 *>(smem + 256 + (size_t)8 * G1_NS * SLOT);
+    float *P = reinterpret_cast<float *>(acts + nbD) + warp * 8 * G1_PS;
+    float *mids = reinterpret_cast<float *>(acts + nbD) + 8 * 8 * G1_PS;   // [64]
+    const int row0 = rb * GU_ROWS + 8 * warp;
+    auto issue = [&](int q) {   // lane 0 of the warp: tile q into slot q % G1_NS
+        const int st = q % G1_NS, c0 = (q % ntile) * G1_CW, gn = min(G1_CW, nbD - c0);
+        const uint8_t *m = q < ntile ? job.gate : job.up;
+        mbar_expect_tx(&bars[st], (uint32_t)(8 * gn * BS));
+        for (int k = 0; k < 8; k++)
+            bulk_g2s(slots + st * SLOT + k * G1_CW * BS, m + (int64_t)(row0 + k) * rbD + (int64_t)c0 * BS,
+                     (uint32_t)(gn * BS), &bars[st]);
+    };
+    if (lane == 0) {
+        for (int st = 0; st < G1_NS; st++) mbar_init(&bars[st], 1);
+        fence_mbar_init();
+        for (int q = 0; q < min(G1_NS, total); q++) issue(q);
+    }
+    {   // the token's activation blocks
+        const int t = job_token(sc, job, 0);
+        const uint32_t *src = reinterpret_cast<const uint32_t *>(sc.xact + (int64_t)t * nbD);
+        uint32_t *dst = reinterpret_cast<uint32_t *>(acts);
+        for (int k = threadIdx.x; k < nbD * (ACT_BLOCK / 4); k += blockDim.x) dst[k] = src[k];
+    }
+    __syncthreads();
+    float accg = 0.0f, accu = 0.0f;
+    bool ok = true;
+    for (int q = 0; q < total; q++) {
+        const int st = q % G1_NS, c0 = (q % ntile) * G1_CW, gn = min(G1_CW, nbD - c0);
+        ok = ok && mbar_wait(&bars[st], (uint32_t)((q / G1_NS) & 1), sc.err);
+        if (ok) rows8_tile<DT>(slots + st * SLOT, gn, acts + c0, P, q < ntile ? accg : accu);
+        if (lane == 0 && q + G1_NS < total) {
+            fence_proxy_async();
+            issue(q + G1_NS);
+        }
+    }
+    if (!ok) {   // every copy this warp issued has landed before the CTA exits
+        if (lane == 0)
+            for (int q = max(0, total - G1_NS); q < total; q++) mbar_wait(&bars[q % G1_NS], (uint32_t)((q / G1_NS) & 1), nullptr);
+    }
+    if (lane < 8) mids[8 * warp + lane] = swiglu_c(canon(accg), canon(accu));
+    __syncthreads();
+    if (warp == 0 && ok)
+        act_quant_warp(mids[lane], mids[lane + 32], sc.act_mid + (int64_t)job.p0 * fmax_nb + rb, lane);
+}
+
+__global__ void __launch_bounds__(256) k_moe_gateup1(MoeShape sh, MoeLayerDev L, MoeScratch sc, int fmax_nb) {
+    extern __shared__ __align__(128) uint8_t smem[];
+    const int u = blockIdx.y, rb = blockIdx.x;
+    const int nu = routed_jobs(sh, sc);
+    const int njobs = nu + (L.Fs > 0 ? 1 : 0);
+    if (u >= njobs) return;
+    Job job;
+    if (!get_job(sh, L, sc, u, nu, job)) return;
+    if (rb * GU_ROWS >= job.F) return;
+    if (job.dtype == Q4) gateup1_body<Q4>(sh, sc, job, fmax_nb, smem, rb);
+    else gateup1_body<Q8>(sh, sc, job, fmax_nb, smem, rb);
+}
+
+static size_t gateup1_smem(int nbD, bool q8) {
+    const size_t slot = (size_t)8 * G1_CW * (q8 ? Q8_BLOCK : Q4_BLOCK);
+    return 256 + 8 * G1_NS * slot + (size_t)nbD * ACT_BLOCK + (size_t)8 * 8 * G1_PS * 4 + 64 * 4 + 64;
+}
+
 struct DownCfg {
     int nst;          // pipeline stages
     int64_t stage;    // bytes per stage (DN_ROWS rows of the widest down matrix)
@@ -877,6 +988,9 @@ cudaError_t init_kernel_attributes() {
     cudaError_t e = cudaFuncGetAttributes(&fa, (const void *)k_moe_gateup);
     if (e == cudaSuccess)
         e = cudaFuncSetAttribute(k_moe_gateup, cudaFuncAttributeMaxDynamicSharedMemorySize, lim - (int)fa.sharedSizeBytes);
+    if (e == cudaSuccess) e = cudaFuncGetAttributes(&fa, (const void *)k_moe_gateup1);
+    if (e == cudaSuccess)
+        e = cudaFuncSetAttribute(k_moe_gateup1, cudaFuncAttributeMaxDynamicSharedMemorySize, lim - (int)fa.sharedSizeBytes);
     if (e == cudaSuccess) e = cudaFuncGetAttributes(&fa, (const void *)k_moe_router);
     if (e == cudaSuccess)
         e = cudaFuncSetAttribute(k_moe_router, cudaFuncAttributeMaxDynamicSharedMemorySize, lim - (int)fa.sharedSizeBytes);
@@ -915,7 +1029,14 @@ static cudaError_t launch_expert_stages(int which, const MoeShape &sh, const Moe
         return cudaGetLastError();
     }
     // ---- gate/up + SwiGLU + mid activations
-    if (which & 1) {
+    const bool any_q8 = L.expert_dtype == Q8 || (L.Fs > 0 && L.sh_dtype == Q8);
+    const bool one_token = T == 1 && (sh.D / QK) % 8 == 0 && (sh.F % GU_ROWS) == 0 && (L.Fs % GU_ROWS) == 0 &&
+                           gateup1_smem(sh.D / QK, any_q8) + 1024 <= smem_limit();
+    if ((which & 1) && one_token) {
+        const int maxjobs = std::min(E, T * K) + (L.Fs > 0 ? 1 : 0);
+        dim3 grid((unsigned)(std::max(sh.F, L.Fs) / GU_ROWS), (unsigned)maxjobs);
+        k_moe_gateup1<<<grid, 256, gateup1_smem(sh.D / QK, any_q8), s>>>(sh, L, sc, fmax_nb);
+    } else if (which & 1) {
         GateUpCfg c;
         c.nbD = sh.D / QK;
         c.fmax_nb = fmax_nb;
