@@ -44,7 +44,7 @@ namespace hx {
 constexpr int DEC_THREADS = 512;
 constexpr int DEC_WARPS = DEC_THREADS / 32;
 constexpr int DEC_CH = 4;          // gate/up row pairs per chunk (one mbarrier, two bulk copies)
-constexpr int DEC_PROWS = 8;       // rows per warp_rows_1tok call (P buffer rows)
+constexpr int DEC_PROWS = ROWS_1TOK;   // rows per warp_rows_1tok call (P buffer rows)
 constexpr int DEC_MAXL = 128;      // layers per launch (router / norm / bias pointer tables in smem)
 constexpr int DEC_MAXCH = 26;      // gate/up chunks per CTA (mbarriers 0..25)
 constexpr int BAR_DOWN = 28, BAR_ROUTER = 29;
@@ -277,66 +277,6 @@ __device__ __forceinline__ float4 poll4(const float *p, int *err) {
 __device__ __forceinline__ void poll_vec(const float *src, float *dst, int n, int *err) {
     for (int i = threadIdx.x * 4; i < n; i += DEC_THREADS * 4)
         *reinterpret_cast<float4 *>(dst + i) = poll4(src + i, err);
-}
-
-// Rows [0, nr) of a tile whose rows are consecutive in shared memory, against one activation row
-// of nb blocks. out[k] = canonical NUMERICS §3 value of row k. nr <= DEC_PROWS. The row loop is
-// unrolled to DEC_PROWS (predicated on nr) so that the rows' loads and dot chains overlap.
-template <int DT>
-__device__ __forceinline__ void warp_rows_1tok(const uint8_t *tile, int64_t rb, int nb, int nr, const act_q8 *act,
-                                               float *P, float *out) {
-    const int lane = threadIdx.x & 31;
-    constexpr int BS = DT == Q4 ? Q4_BLOCK : Q8_BLOCK;
-    auto term = [&](const uint8_t *blk, const act_regs &ar) {
-        int isum;
-        uint32_t sc;
-        if constexpr (DT == Q4) {
-            uint32_t nib[8];
-            sc = load_q4_block_pad(blk, nib);
-            isum = q4_isum_hi(nib, ar.q, ar.sum);
-        } else {
-            uint32_t q[16];
-            sc = load_q8_block_pad(blk, q);
-            isum = q8_isum(q, ar.q);
-        }
-        return __fmul_rn(__int2float_rn(isum), __fmul_rn(f16_to_f32_hw(sc), ar.d));
-    };
-    float acc = 0.0f;
-    for (int g0 = 0; g0 < nb; g0 += 32) {
-        const int gn = min(32, nb - g0);
-        if (gn == 32) {   // lane = block: its activation block stays in registers for every row
-            act_regs ar;
-            load_act(act + g0 + lane, ar);
-            const uint8_t *col = tile + (int64_t)(g0 + lane) * BS;
-#pragma unroll
-            for (int k = 0; k < DEC_PROWS; k++)
-                if (k < nr) P[k * 33 + lane] = term(col + (int64_t)k * rb, ar);
-        } else if (gn <= 16) {   // lane = (row phase, block): each lane's activation block loaded once
-            const int rp = 32 / gn, g = lane % gn, r2 = lane / gn;
-            if (r2 < rp) {
-                act_regs ar;
-                load_act(act + g0 + g, ar);
-                const uint8_t *col = tile + (int64_t)(g0 + g) * BS;
-                for (int k = r2; k < nr; k += rp) P[k * 33 + g] = term(col + (int64_t)k * rb, ar);
-            }
-        } else {
-            for (int it = lane; it < nr * gn; it += 32) {
-                const int k = it / gn, g = it - k * gn;
-                act_regs ar;
-                load_act(act + g0 + g, ar);
-                P[k * 33 + g] = term(tile + (int64_t)k * rb + (int64_t)(g0 + g) * BS, ar);
-            }
-        }
-        __syncwarp();
-        if (lane < nr) {
-            const float *p = P + lane * 33;
-#pragma unroll 8
-            for (int g = 0; g < gn; g++) acc = __fadd_rn(acc, p[g]);
-        }
-        __syncwarp();
-    }
-    if (lane < nr) out[lane] = canon(acc);
-    __syncwarp();
 }
 
 // The 16-lane chain of NUMERICS §1 over the chain buffer: lane j < 16 adds c[j*cs + k], k = 0..4*n4-1,

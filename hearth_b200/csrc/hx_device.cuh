@@ -162,4 +162,68 @@ __device__ __forceinline__ void warp_rows(const uint8_t *tile, int64_t rb, int n
     }
 }
 
+// Single-token rows (the persistent decode kernel and the single-token expert kernels): P holds
+// ROWS_1TOK x 33 floats per warp; tiles in shared memory may be read up to 2 bytes past a block.
+constexpr int ROWS_1TOK = 8;
+
+// Rows [0, nr) of a tile whose rows are consecutive in shared memory, against one activation row
+// of nb blocks. out[k] = canonical NUMERICS §3 value of row k. nr <= ROWS_1TOK. The row loop is
+// unrolled to ROWS_1TOK (predicated on nr) so that the rows' loads and dot chains overlap.
+template <int DT>
+__device__ __forceinline__ void warp_rows_1tok(const uint8_t *tile, int64_t rb, int nb, int nr, const act_q8 *act,
+                                               float *P, float *out) {
+    const int lane = threadIdx.x & 31;
+    constexpr int BS = DT == Q4 ? Q4_BLOCK : Q8_BLOCK;
+    auto term = [&](const uint8_t *blk, const act_regs &ar) {
+        int isum;
+        uint32_t sc;
+        if constexpr (DT == Q4) {
+            uint32_t nib[8];
+            sc = load_q4_block_pad(blk, nib);
+            isum = q4_isum_hi(nib, ar.q, ar.sum);
+        } else {
+            uint32_t q[16];
+            sc = load_q8_block_pad(blk, q);
+            isum = q8_isum(q, ar.q);
+        }
+        return __fmul_rn(__int2float_rn(isum), __fmul_rn(f16_to_f32_hw(sc), ar.d));
+    };
+    float acc = 0.0f;
+    for (int g0 = 0; g0 < nb; g0 += 32) {
+        const int gn = min(32, nb - g0);
+        if (gn == 32) {   // lane = block: its activation block stays in registers for every row
+            act_regs ar;
+            load_act(act + g0 + lane, ar);
+            const uint8_t *col = tile + (int64_t)(g0 + lane) * BS;
+#pragma unroll
+            for (int k = 0; k < ROWS_1TOK; k++)
+                if (k < nr) P[k * 33 + lane] = term(col + (int64_t)k * rb, ar);
+        } else if (gn <= 16) {   // lane = (row phase, block): each lane's activation block loaded once
+            const int rp = 32 / gn, g = lane % gn, r2 = lane / gn;
+            if (r2 < rp) {
+                act_regs ar;
+                load_act(act + g0 + g, ar);
+                const uint8_t *col = tile + (int64_t)(g0 + g) * BS;
+                for (int k = r2; k < nr; k += rp) P[k * 33 + g] = term(col + (int64_t)k * rb, ar);
+            }
+        } else {
+            for (int it = lane; it < nr * gn; it += 32) {
+                const int k = it / gn, g = it - k * gn;
+                act_regs ar;
+                load_act(act + g0 + g, ar);
+                P[k * 33 + g] = term(tile + (int64_t)k * rb + (int64_t)(g0 + g) * BS, ar);
+            }
+        }
+        __syncwarp();
+        if (lane < nr) {
+            const float *p = P + lane * 33;
+#pragma unroll 8
+            for (int g = 0; g < gn; g++) acc = __fadd_rn(acc, p[g]);
+        }
+        __syncwarp();
+    }
+    if (lane < nr) out[lane] = canon(acc);
+    __syncwarp();
+}
+
 }  // namespace hx

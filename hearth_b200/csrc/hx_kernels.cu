@@ -660,70 +660,43 @@ __global__ void __launch_bounds__(512) k_moe_gateup(MoeShape sh, MoeLayerDev L, 
     else gateup_body<Q8>(sh, sc, job, c, smem, rb);
 }
 
-// ---- gate/up for single-token jobs (decode, T = 1): one CTA per (job, 64 mid rows), 8 warps; warp w
-// owns mid rows 8w..8w+7, i.e. gate rows and up rows 8w..8w+7 of its 64. It walks them in tiles of
-// 8 rows x 16 blocks that stream into its own 3 shared-memory slots by 1-D bulk copies (one per row),
-// lanes = (row phase, block) with each lane's activation block loaded once per tile, and lanes 0..7
-// carry the 8 rows' canonical chains across the tiles. SwiGLU and the mid activation block follow in
-// the CTA. Used when every row is a whole number of 16-byte units (D a multiple of 512).
-constexpr int G1_CW = 16, G1_NS = 3, G1_PS = 17;
+// ---- gate/up for single-token jobs (decode, T = 1): one CTA per (job, 64 mid rows), G1_WARPS warps.
+// The CTA's 128 rows (64 gate, then the 64 up rows of the same mid rows) go in tiles of TR
+// consecutive rows (TR rows of up to 32 KB: one 1-D bulk copy each), warp w taking tiles w,
+// w + G1_WARPS, ... into its own shared-memory slot; each tile runs through the single-token row loop
+// (lane = block, the activation block kept in registers across 8 rows, lanes 0..7 the rows' chains).
+// SwiGLU and the mid activation block follow in the CTA. Used when rows are whole 16-byte units.
+constexpr int G1_WARPS = 6;
+constexpr int G1_SLOT = 32 * 1024;
 
-template <int DT>
-__device__ __forceinline__ void rows8_tile(const uint8_t *tile, int gn, const act_q8 *act, float *P, float &acc) {
-    constexpr int BS = DT == Q4 ? Q4_BLOCK : Q8_BLOCK;
-    const int lane = threadIdx.x & 31;
-    const int rp = 32 / gn, g = lane % gn, r2 = lane / gn;
-    if (r2 < rp) {
-        act_regs ar;
-        load_act(act + g, ar);
-        const uint8_t *col = tile + g * BS;
-        for (int k = r2; k < 8; k += rp) {
-            uint32_t wq[16];
-            int isum;
-            float dw;
-            if constexpr (DT == Q4) {
-                dw = f16_to_f32(load_q4_block(col + k * G1_CW * BS, wq));
-                isum = q4_isum(wq, ar.q, ar.sum);
-            } else {
-                dw = f16_to_f32(load_q8_block(col + k * G1_CW * BS, wq));
-                isum = q8_isum(wq, ar.q);
-            }
-            P[k * G1_PS + g] = __fmul_rn(__int2float_rn(isum), __fmul_rn(dw, ar.d));
-        }
-    }
-    __syncwarp();
-    if (lane < 8)
-        for (int gg = 0; gg < gn; gg++) acc = __fadd_rn(acc, P[lane * G1_PS + gg]);
-    __syncwarp();
+__host__ __device__ inline int g1_tile_rows(int64_t rb) {   // largest power of two <= 32 with TR * rb <= G1_SLOT
+    int tr = 32;
+    while (tr > 1 && tr * rb > G1_SLOT) tr >>= 1;
+    return tr;
 }
 
 template <int DT>
 __device__ void gateup1_body(const MoeShape &sh, const MoeScratch &sc, const Job &job, int fmax_nb, uint8_t *smem,
                              int rb) {
-    constexpr int BS = DT == Q4 ? Q4_BLOCK : Q8_BLOCK;
-    constexpr int SLOT = 8 * G1_CW * BS;
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
     const int nbD = sh.D / QK;
     const int64_t rbD = row_bytes(DT, sh.D);
-    const int ntile = (nbD + G1_CW - 1) / G1_CW, total = 2 * ntile;   // gate tiles, then up tiles
-    uint64_t *bars = reinterpret_cast<uint64_t *>(smem) + warp * G1_NS;
-    uint8_t *slots = smem + 256 + (size_t)warp * G1_NS * SLOT;
-    act_q8 *acts = reinterpret_cast<act_q8 *>(smem + 256 + (size_t)8 * G1_NS * SLOT);
-    float *P = reinterpret_cast<float *>(acts + nbD) + warp * 8 * G1_PS;
-    float *mids = reinterpret_cast<float *>(acts + nbD) + 8 * 8 * G1_PS;   // [64]
-    const int row0 = rb * GU_ROWS + 8 * warp;
-    auto issue = [&](int q) {   // lane 0 of the warp: tile q into slot q % G1_NS
-        const int st = q % G1_NS, c0 = (q % ntile) * G1_CW, gn = min(G1_CW, nbD - c0);
-        const uint8_t *m = q < ntile ? job.gate : job.up;
-        mbar_expect_tx(&bars[st], (uint32_t)(8 * gn * BS));
-        for (int k = 0; k < 8; k++)
-            bulk_g2s(slots + st * SLOT + k * G1_CW * BS, m + (int64_t)(row0 + k) * rbD + (int64_t)c0 * BS,
-                     (uint32_t)(gn * BS), &bars[st]);
+    const int TR = g1_tile_rows(rbD), ntile = 2 * GU_ROWS / TR;   // gate tiles, then up tiles
+    uint64_t *bar = reinterpret_cast<uint64_t *>(smem) + warp;
+    uint8_t *slot = smem + 128 + (size_t)warp * G1_SLOT;
+    act_q8 *acts = reinterpret_cast<act_q8 *>(smem + 128 + (size_t)G1_WARPS * G1_SLOT);
+    float *P = reinterpret_cast<float *>(acts + nbD) + warp * ROWS_1TOK * 33;
+    float *GU = reinterpret_cast<float *>(acts + nbD) + G1_WARPS * ROWS_1TOK * 33;   // [2][64]
+    auto issue = [&](int tile) {
+        const int r = tile * TR;   // row in [0, 128): gate rows, then up rows
+        const uint8_t *src = (r < GU_ROWS ? job.gate : job.up) + ((int64_t)rb * GU_ROWS + (r % GU_ROWS)) * rbD;
+        mbar_expect_tx(bar, (uint32_t)(TR * rbD));
+        bulk_g2s(slot, src, (uint32_t)(TR * rbD), bar);
     };
     if (lane == 0) {
-        for (int st = 0; st < G1_NS; st++) mbar_init(&bars[st], 1);
+        mbar_init(bar, 1);
         fence_mbar_init();
-        for (int q = 0; q < min(G1_NS, total); q++) issue(q);
+        if (warp < ntile) issue(warp);
     }
     {   // the token's activation blocks
         const int t = job_token(sc, job, 0);
@@ -732,28 +705,28 @@ __device__ void gateup1_body(const MoeShape &sh, const MoeScratch &sc, const Job
         for (int k = threadIdx.x; k < nbD * (ACT_BLOCK / 4); k += blockDim.x) dst[k] = src[k];
     }
     __syncthreads();
-    float accg = 0.0f, accu = 0.0f;
     bool ok = true;
-    for (int q = 0; q < total; q++) {
-        const int st = q % G1_NS, c0 = (q % ntile) * G1_CW, gn = min(G1_CW, nbD - c0);
-        ok = ok && mbar_wait(&bars[st], (uint32_t)((q / G1_NS) & 1), sc.err);
-        if (ok) rows8_tile<DT>(slots + st * SLOT, gn, acts + c0, P, q < ntile ? accg : accu);
-        if (lane == 0 && q + G1_NS < total) {
+    int k = 0;
+    for (int tile = warp; tile < ntile; tile += G1_WARPS, k++) {
+        ok = ok && mbar_wait(bar, (uint32_t)(k & 1), sc.err);
+        if (ok)
+            for (int r8 = 0; r8 < TR; r8 += ROWS_1TOK)
+                warp_rows_1tok<DT>(slot + (int64_t)r8 * rbD, rbD, nbD, min(ROWS_1TOK, TR - r8), acts, P,
+                                   GU + tile * TR + r8);
+        if (lane == 0 && tile + G1_WARPS < ntile && ok) {
             fence_proxy_async();
-            issue(q + G1_NS);
+            issue(tile + G1_WARPS);
         }
+        __syncwarp();
     }
-    if (!ok) {   // every copy this warp issued has landed before the CTA exits
-        if (lane == 0)
-            for (int q = max(0, total - G1_NS); q < total; q++) mbar_wait(&bars[q % G1_NS], (uint32_t)((q / G1_NS) & 1), nullptr);
-    }
-    if (lane < 8) mids[8 * warp + lane] = swiglu_c(canon(accg), canon(accu));
     __syncthreads();
     if (warp == 0 && ok)
-        act_quant_warp(mids[lane], mids[lane + 32], sc.act_mid + (int64_t)job.p0 * fmax_nb + rb, lane);
+        act_quant_warp(swiglu_c(GU[lane], GU[GU_ROWS + lane]), swiglu_c(GU[lane + 32], GU[GU_ROWS + lane + 32]),
+                       sc.act_mid + (int64_t)job.p0 * fmax_nb + rb, lane);
 }
 
-__global__ void __launch_bounds__(256) k_moe_gateup1(MoeShape sh, MoeLayerDev L, MoeScratch sc, int fmax_nb) {
+__global__ void __launch_bounds__(G1_WARPS * 32) k_moe_gateup1(MoeShape sh, MoeLayerDev L, MoeScratch sc,
+                                                              int fmax_nb) {
     extern __shared__ __align__(128) uint8_t smem[];
     const int u = blockIdx.y, rb = blockIdx.x;
     const int nu = routed_jobs(sh, sc);
@@ -766,9 +739,9 @@ __global__ void __launch_bounds__(256) k_moe_gateup1(MoeShape sh, MoeLayerDev L,
     else gateup1_body<Q8>(sh, sc, job, fmax_nb, smem, rb);
 }
 
-static size_t gateup1_smem(int nbD, bool q8) {
-    const size_t slot = (size_t)8 * G1_CW * (q8 ? Q8_BLOCK : Q4_BLOCK);
-    return 256 + 8 * G1_NS * slot + (size_t)nbD * ACT_BLOCK + (size_t)8 * 8 * G1_PS * 4 + 64 * 4 + 64;
+static size_t gateup1_smem(int nbD) {
+    return 128 + (size_t)G1_WARPS * G1_SLOT + (size_t)nbD * ACT_BLOCK + (size_t)G1_WARPS * ROWS_1TOK * 33 * 4 +
+           2 * GU_ROWS * 4 + 64;
 }
 
 struct DownCfg {
@@ -908,6 +881,83 @@ __global__ void k_moe_sum(MoeShape sh, MoeLayerDev L, MoeScratch sc, float *h, f
                L.sh_gate_inp ? sc.sh_logit : nullptr, h, out, resid != 0);
 }
 
+// ---- down for single-token jobs (decode, T = 1): one CTA per DN_ROWS rows of D, 8 warps; its work
+// units are (job, 8 of its rows), warp w taking units w, w + 8, ...: each unit's 8 down rows are
+// consecutive (one 1-D bulk copy into the warp's slot) and run through the single-token row loop.
+// The pair outputs stay in shared memory and the CTA finishes its rows: rank-order sum, shared
+// expert, residual. Used when 8 down rows fit D1_SLOT bytes.
+constexpr int D1_SLOT = 20 * 1024;
+
+__global__ void __launch_bounds__(256) k_moe_down1(MoeShape sh, MoeLayerDev L, MoeScratch sc, int fmax_nb, float *h,
+                                                   float *out, int resid) {
+    extern __shared__ __align__(128) uint8_t smem[];
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    const int r0 = blockIdx.x * DN_ROWS;
+    const int nu = routed_jobs(sh, sc);
+    const int njobs = nu + (L.Fs > 0 ? 1 : 0);
+    uint64_t *bar = reinterpret_cast<uint64_t *>(smem) + warp;
+    uint8_t *slot = smem + 128 + (size_t)warp * D1_SLOT;
+    float *P = reinterpret_cast<float *>(smem + 128 + (size_t)8 * D1_SLOT) + warp * ROWS_1TOK * 33;
+    float *Ys = reinterpret_cast<float *>(smem + 128 + (size_t)8 * D1_SLOT) + 8 * ROWS_1TOK * 33;   // [K + 1][DN_ROWS]
+    const int units = njobs * (DN_ROWS / ROWS_1TOK);
+    auto issue = [&](int un) {
+        const int u = un / (DN_ROWS / ROWS_1TOK), gi = un - u * (DN_ROWS / ROWS_1TOK);
+        Job j;
+        if (!get_job(sh, L, sc, u, nu, j)) return false;
+        const int64_t rbF = row_bytes(j.dtype, j.F);
+        mbar_expect_tx(bar, (uint32_t)(ROWS_1TOK * rbF));
+        bulk_g2s(slot, j.down + (int64_t)(r0 + gi * ROWS_1TOK) * rbF, (uint32_t)(ROWS_1TOK * rbF), bar);
+        return true;
+    };
+    bool ok = true;
+    if (lane == 0) {
+        mbar_init(bar, 1);
+        fence_mbar_init();
+    }
+    __syncwarp();
+    if (warp < units) {
+        int issued = 1;
+        if (lane == 0) issued = issue(warp) ? 1 : 0;
+        ok = __shfl_sync(0xffffffffu, issued, 0) != 0;
+    }
+    int k = 0;
+    for (int un = warp; ok && un < units; un += 8, k++) {
+        const int u = un / (DN_ROWS / ROWS_1TOK), gi = un - u * (DN_ROWS / ROWS_1TOK);
+        Job job;
+        get_job(sh, L, sc, u, nu, job);
+        ok = mbar_wait(bar, (uint32_t)(k & 1), sc.err);
+        if (!ok) break;
+        // pair outputs by pair index (one pair per bucket at T = 1), the shared expert's after the K pairs
+        float *yout = Ys + (job.shared ? sh.route.K : job.p0) * DN_ROWS + gi * ROWS_1TOK;
+        const act_q8 *act = sc.act_mid + (int64_t)job.p0 * fmax_nb;
+        if (job.dtype == Q4) warp_rows_1tok<Q4>(slot, row_bytes(Q4, job.F), job.F / QK, ROWS_1TOK, act, P, yout);
+        else warp_rows_1tok<Q8>(slot, row_bytes(Q8, job.F), job.F / QK, ROWS_1TOK, act, P, yout);
+        if (un + 8 < units) {
+            int issued = 1;
+            if (lane == 0) {
+                fence_proxy_async();
+                issued = issue(un + 8) ? 1 : 0;
+            }
+            ok = __shfl_sync(0xffffffffu, issued, 0) != 0;
+        }
+    }
+    __shared__ int all_ok;
+    if (threadIdx.x == 0) all_ok = 1;
+    __syncthreads();
+    if (!ok) all_ok = 0;
+    __syncthreads();
+    if (!all_ok) return;
+    // finish this CTA's rows: rank-order sum, shared expert, residual (as the fused down kernel)
+    const bool has_shared = L.Fs > 0;
+    for (int rr = threadIdx.x; rr < DN_ROWS; rr += blockDim.x)
+        finish_row(sh, sc, 0, r0 + rr, Ys + rr, DN_ROWS, has_shared ? Ys[sh.route.K * DN_ROWS + rr] : 0.0f, has_shared,
+                   L.sh_gate_inp ? sc.sh_logit : nullptr, h, out, resid != 0);
+}
+
+static size_t down1_smem(int K) {
+    return 128 + (size_t)8 * D1_SLOT + (size_t)8 * ROWS_1TOK * 33 * 4 + (size_t)(K + 1) * DN_ROWS * 4 + 64;
+}
+
 // Expert-parallel combine: pair (t, j) of expert e comes from rank e % ep_size's slice of y_all.
 __global__ void k_moe_ep_combine(MoeShape sh, MoeLayerDev L, MoeScratch sc, const float *__restrict__ y_all,
                                  float *h) {
@@ -991,6 +1041,9 @@ cudaError_t init_kernel_attributes() {
     if (e == cudaSuccess) e = cudaFuncGetAttributes(&fa, (const void *)k_moe_gateup1);
     if (e == cudaSuccess)
         e = cudaFuncSetAttribute(k_moe_gateup1, cudaFuncAttributeMaxDynamicSharedMemorySize, lim - (int)fa.sharedSizeBytes);
+    if (e == cudaSuccess) e = cudaFuncGetAttributes(&fa, (const void *)k_moe_down1);
+    if (e == cudaSuccess)
+        e = cudaFuncSetAttribute(k_moe_down1, cudaFuncAttributeMaxDynamicSharedMemorySize, lim - (int)fa.sharedSizeBytes);
     if (e == cudaSuccess) e = cudaFuncGetAttributes(&fa, (const void *)k_moe_router);
     if (e == cudaSuccess)
         e = cudaFuncSetAttribute(k_moe_router, cudaFuncAttributeMaxDynamicSharedMemorySize, lim - (int)fa.sharedSizeBytes);
@@ -1029,13 +1082,15 @@ static cudaError_t launch_expert_stages(int which, const MoeShape &sh, const Moe
         return cudaGetLastError();
     }
     // ---- gate/up + SwiGLU + mid activations
-    const bool any_q8 = L.expert_dtype == Q8 || (L.Fs > 0 && L.sh_dtype == Q8);
+    // one token: the single-token kernels (rows of whole 16-byte units; 8 rows of the widest
+    // gate/up dtype within a slot: TR >= 8 keeps the row loop's 8 lanes busy)
+    const int64_t rbD_max = std::max<int64_t>(row_bytes(L.expert_dtype, sh.D), L.Fs > 0 ? row_bytes(L.sh_dtype, sh.D) : 0);
     const bool one_token = T == 1 && (sh.D / QK) % 8 == 0 && (sh.F % GU_ROWS) == 0 && (L.Fs % GU_ROWS) == 0 &&
-                           gateup1_smem(sh.D / QK, any_q8) + 1024 <= smem_limit();
+                           rbD_max * 4 <= G1_SLOT && gateup1_smem(sh.D / QK) + 1024 <= smem_limit();
     if ((which & 1) && one_token) {
         const int maxjobs = std::min(E, T * K) + (L.Fs > 0 ? 1 : 0);
         dim3 grid((unsigned)(std::max(sh.F, L.Fs) / GU_ROWS), (unsigned)maxjobs);
-        k_moe_gateup1<<<grid, 256, gateup1_smem(sh.D / QK, any_q8), s>>>(sh, L, sc, fmax_nb);
+        k_moe_gateup1<<<grid, G1_WARPS * 32, gateup1_smem(sh.D / QK), s>>>(sh, L, sc, fmax_nb);
     } else if (which & 1) {
         GateUpCfg c;
         c.nbD = sh.D / QK;
@@ -1061,7 +1116,12 @@ static cudaError_t launch_expert_stages(int which, const MoeShape &sh, const Moe
         k_moe_gateup<<<grid, 512, smem, s>>>(sh, L, sc, c);
     }
     // ---- down (+ rank-order sum for small batches)
-    if (which & 2) {
+    const int64_t rbF_max = std::max<int64_t>(row_bytes(L.expert_dtype, sh.F), L.Fs > 0 ? row_bytes(L.sh_dtype, L.Fs) : 0);
+    const bool down_one = one_token && fused && sh.D % DN_ROWS == 0 && (sh.F / QK) % 8 == 0 && (L.Fs / QK) % 8 == 0 &&
+                          ROWS_1TOK * rbF_max <= D1_SLOT && down1_smem(K) + 1024 <= smem_limit();
+    if ((which & 2) && down_one) {
+        k_moe_down1<<<(unsigned)(sh.D / DN_ROWS), 256, down1_smem(K), s>>>(sh, L, sc, fmax_nb, h, out, resid ? 1 : 0);
+    } else if (which & 2) {
         DownCfg c;
         c.fmax_nb = fmax_nb;
         c.fused = fused ? 1 : 0;
