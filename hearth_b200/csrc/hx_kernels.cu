@@ -351,11 +351,18 @@ cudaError_t launch_dequantize(int dtype, const void *W, int64_t n_rows, int64_t 
 __global__ void __launch_bounds__(256) k_moe_norm_act(const float *__restrict__ h, const float *__restrict__ w,
                                                       float eps, int D, float *__restrict__ x,
                                                       act_q8 *__restrict__ xact) {
-    __shared__ float xs[8192];
+    __shared__ __align__(16) float xs[8192];
     __shared__ float rsh;
     const int t = blockIdx.x, tid = threadIdx.x;
     const float *ht = h + (int64_t)t * D;
-    for (int i = tid; i < D; i += blockDim.x) xs[i] = ht[i];
+    if (D % 4 == 0) {   // 16-byte loads, several in flight per thread
+        const float4 *h4 = reinterpret_cast<const float4 *>(ht);
+        float4 *x4 = reinterpret_cast<float4 *>(xs);
+#pragma unroll 4
+        for (int i = tid; i < D / 4; i += blockDim.x) x4[i] = h4[i];
+    } else {
+        for (int i = tid; i < D; i += blockDim.x) xs[i] = ht[i];
+    }
     __syncthreads();
     if (w) {
         if (tid < 16) {   // ms = dot16(h, h) / n ; r = 1 / sqrtf(ms + eps)
@@ -369,6 +376,7 @@ __global__ void __launch_bounds__(256) k_moe_norm_act(const float *__restrict__ 
         }
         __syncthreads();
         const float r = rsh;
+#pragma unroll 4
         for (int i = tid; i < D; i += blockDim.x) xs[i] = __fmul_rn(__fmul_rn(xs[i], r), w[i]);
         __syncthreads();
     }
@@ -666,8 +674,8 @@ __global__ void __launch_bounds__(512) k_moe_gateup(MoeShape sh, MoeLayerDev L, 
 // w + G1_WARPS, ... into its own shared-memory slot; each tile runs through the single-token row loop
 // (lane = block, the activation block kept in registers across 8 rows, lanes 0..7 the rows' chains).
 // SwiGLU and the mid activation block follow in the CTA. Used when rows are whole 16-byte units.
-constexpr int G1_WARPS = 6;
-constexpr int G1_SLOT = 32 * 1024;
+constexpr int G1_WARPS = 12;
+constexpr int G1_SLOT = 16 * 1024;
 
 __host__ __device__ inline int g1_tile_rows(int64_t rb) {   // largest power of two <= 32 with TR * rb <= G1_SLOT
     int tr = 32;
@@ -1082,11 +1090,11 @@ static cudaError_t launch_expert_stages(int which, const MoeShape &sh, const Moe
         return cudaGetLastError();
     }
     // ---- gate/up + SwiGLU + mid activations
-    // one token: the single-token kernels (rows of whole 16-byte units; 8 rows of the widest
-    // gate/up dtype within a slot: TR >= 8 keeps the row loop's 8 lanes busy)
+    // one token: the single-token kernels (rows of whole 16-byte units; at least 2 rows of the widest
+    // gate/up dtype per slot)
     const int64_t rbD_max = std::max<int64_t>(row_bytes(L.expert_dtype, sh.D), L.Fs > 0 ? row_bytes(L.sh_dtype, sh.D) : 0);
     const bool one_token = T == 1 && (sh.D / QK) % 8 == 0 && (sh.F % GU_ROWS) == 0 && (L.Fs % GU_ROWS) == 0 &&
-                           rbD_max * 4 <= G1_SLOT && gateup1_smem(sh.D / QK) + 1024 <= smem_limit();
+                           rbD_max * 2 <= G1_SLOT && gateup1_smem(sh.D / QK) + 1024 <= smem_limit();
     if ((which & 1) && one_token) {
         const int maxjobs = std::min(E, T * K) + (L.Fs > 0 ? 1 : 0);
         dim3 grid((unsigned)(std::max(sh.F, L.Fs) / GU_ROWS), (unsigned)maxjobs);

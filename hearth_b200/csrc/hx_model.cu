@@ -146,11 +146,18 @@ __global__ void k_embed(const int32_t *__restrict__ tok, int T, const uint8_t *_
 __global__ void __launch_bounds__(256) k_rmsnorm_rows(const float *__restrict__ x, int64_t ldx,
                                                       const float *__restrict__ w, int n, float eps,
                                                       float *__restrict__ y, int64_t ldy, act_q8 *__restrict__ act) {
-    extern __shared__ float xs[];
+    extern __shared__ __align__(16) float xs[];
     __shared__ float rsh;
     const int t = blockIdx.x, tid = threadIdx.x;
     const float *xr = x + (int64_t)t * ldx;
-    for (int i = tid; i < n; i += blockDim.x) xs[i] = xr[i];
+    if (n % 4 == 0 && ldx % 4 == 0) {   // 16-byte loads, several in flight per thread
+        const float4 *x4 = reinterpret_cast<const float4 *>(xr);
+        float4 *s4 = reinterpret_cast<float4 *>(xs);
+#pragma unroll 4
+        for (int i = tid; i < n / 4; i += blockDim.x) s4[i] = x4[i];
+    } else {
+        for (int i = tid; i < n; i += blockDim.x) xs[i] = xr[i];
+    }
     __syncthreads();
     if (tid < 16) {
         float L = 0.0f;
@@ -160,6 +167,7 @@ __global__ void __launch_bounds__(256) k_rmsnorm_rows(const float *__restrict__ 
     }
     __syncthreads();
     const float r = rsh;
+#pragma unroll 4
     for (int i = tid; i < n; i += blockDim.x) xs[i] = __fmul_rn(__fmul_rn(xs[i], r), w[i]);
     __syncthreads();
     if (y) {
