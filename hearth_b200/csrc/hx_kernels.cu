@@ -404,12 +404,16 @@ static size_t smem_limit() {
 // the buckets.
 // staged (one token): the CTA's rows and x arrive in shared memory by 1-D bulk copies first, so the
 // chains read shared memory and every CTA keeps its whole share of the router in flight at once.
+// staged == 2 also forms x = rmsnorm(h, norm) (or x = h without a norm) in every CTA from h, and each
+// CTA writes its share of x's activation blocks (the separate norm kernel's work).
 __global__ void __launch_bounds__(256) k_moe_router(MoeShape sh, const float *__restrict__ router,
                                                     const float *__restrict__ gate_inp,
                                                     const float *__restrict__ bias, MoeScratch sc, int fuse_route,
-                                                    int staged) {
+                                                    int staged, const float *__restrict__ h,
+                                                    const float *__restrict__ norm) {
     extern __shared__ __align__(16) float rsm[];
     __shared__ int last;
+    __shared__ float rsh;
     __shared__ __align__(8) uint64_t rbar;
     const int D = sh.D, E = sh.route.E, T = sh.T;
     const int rows = E + (gate_inp ? 1 : 0);
@@ -421,18 +425,43 @@ __global__ void __launch_bounds__(256) k_moe_router(MoeShape sh, const float *__
     float L = 0.0f;
     if (staged) {   // T == 1: item == row
         const int r0 = blockIdx.x * (blockDim.x >> 4), nr = min((int)(blockDim.x >> 4), rows - r0);
-        float *xs = rsm, *ws = rsm + D;
+        const bool fnorm = staged == 2, wn = fnorm && norm;
+        float *xs = rsm, *nws = rsm + D, *ws = rsm + (fnorm ? 2 * D : D);
         if (threadIdx.x == 0) {
             mbar_init(&rbar, 1);
             fence_mbar_init();
-            mbar_expect_tx(&rbar, (uint32_t)((nr + 1) * D * 4));
-            bulk_g2s(xs, sc.x, (uint32_t)(D * 4), &rbar);
+            mbar_expect_tx(&rbar, (uint32_t)((nr + (wn ? 2 : 1)) * D * 4));
+            bulk_g2s(xs, fnorm ? h : sc.x, (uint32_t)(D * 4), &rbar);
+            if (wn) bulk_g2s(nws, norm, (uint32_t)(D * 4), &rbar);
             for (int k = 0; k < nr; k++)
                 bulk_g2s(ws + (int64_t)k * D, r0 + k < E ? router + (int64_t)(r0 + k) * D : gate_inp, (uint32_t)(D * 4),
                          &rbar);
         }
         __syncthreads();
         const bool ok = mbar_wait(&rbar, 0, sc.err);
+        if (fnorm && ok) {
+            if (wn) {   // x = rmsnorm(h, norm) (NUMERICS §4), as k_moe_norm_act forms it
+                const int tid = threadIdx.x;
+                if (tid < 16) {
+                    float Ls = 0.0f;
+                    for (int i = tid; i < D; i += 16) Ls = __fadd_rn(Ls, __fmul_rn(xs[i], xs[i]));
+                    Ls = tree16(Ls, 0xffffu);
+                    if (tid == 0) rsh = __fdiv_rn(1.0f, __fsqrt_rn(__fadd_rn(__fdiv_rn(Ls, (float)D), sh.eps)));
+                }
+                __syncthreads();
+                const float rr = rsh;
+                for (int i = tid; i < D; i += blockDim.x) xs[i] = __fmul_rn(__fmul_rn(xs[i], rr), nws[i]);
+                __syncthreads();
+            }
+            // this CTA's share of x and its activation blocks (blocks blockIdx.x + k * gridDim.x)
+            const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31, nwarps = blockDim.x >> 5;
+            for (int b = blockIdx.x + warp * gridDim.x; b < D / QK; b += gridDim.x * nwarps) {
+                const float x0 = xs[b * QK + lane], x1 = xs[b * QK + lane + 32];
+                sc.x[b * QK + lane] = x0;
+                sc.x[b * QK + lane + 32] = x1;
+                act_quant_warp(x0, x1, sc.xact + b, lane);
+            }
+        }
         if (valid && ok) {
             const float *wr = ws + (int64_t)grp * D;
 #pragma unroll 8
@@ -1005,7 +1034,15 @@ static void launch_route_stages(int which, const MoeShape &sh, const MoeLayerDev
                                 const float *h, cudaStream_t s) {
     const int T = sh.T, E = sh.route.E, K = sh.route.K;
     const bool fused = T * K <= kFusedMaxPairs && sh.ep_size == 1;
-    if (which & 1) k_moe_norm_act<<<T, 256, 0, s>>>(h, L.ffn_norm, sh.eps, sh.D, sc.x, sc.xact);
+    constexpr int RT0 = 64;
+    // one token: the router CTAs stage their rows (and h and the norm) through shared memory by bulk
+    // copies; with both stages asked for they also form x and its activation blocks (no norm launch)
+    const size_t stage_smem = (size_t)(RT0 / 16 + 2) * sh.D * sizeof(float);
+    const bool staged = T == 1 && sh.D % QK == 0 && stage_smem + 1024 <= smem_limit() &&
+                        (reinterpret_cast<uintptr_t>(sc.x) & 15) == 0 && (reinterpret_cast<uintptr_t>(h) & 15) == 0 &&
+                        (!L.ffn_norm || (reinterpret_cast<uintptr_t>(L.ffn_norm) & 15) == 0);
+    const bool fuse_norm = staged && which == 3;
+    if ((which & 1) && !fuse_norm) k_moe_norm_act<<<T, 256, 0, s>>>(h, L.ffn_norm, sh.eps, sh.D, sc.x, sc.xact);
     if (which & 2) {
         const int rows = E + (L.sh_gate_inp ? 1 : 0);
         const int64_t items = (int64_t)rows * T;
@@ -1017,13 +1054,10 @@ static void launch_route_stages(int which, const MoeShape &sh, const MoeLayerDev
                                  s>>>(sh, L.router, L.sh_gate_inp, sc);
         else
         {
-            // one token: stage the rows (RT / 16 per CTA) and x through shared memory when they fit
-            const size_t stage_smem = (size_t)(RT / 16 + 1) * sh.D * sizeof(float);
-            const bool staged = T == 1 && sh.D % 4 == 0 && stage_smem + 1024 <= smem_limit() &&
-                                (reinterpret_cast<uintptr_t>(sc.x) & 15) == 0;
+            static_assert(RT == RT0, "router CTA size");
             const size_t smem = std::max(fused ? route_smem : (size_t)0, staged ? stage_smem : (size_t)0);
             k_moe_router<<<grid, RT, smem, s>>>(sh, L.router, L.sh_gate_inp, L.router_bias, sc, fused ? 1 : 0,
-                                                staged ? 1 : 0);
+                                                fuse_norm ? 2 : (staged ? 1 : 0), h, L.ffn_norm);
         }
         if (!fused) {
             k_route_select<<<(T + 7) / 8, 256, route_smem, s>>>(sh, L.router_bias, sc);
