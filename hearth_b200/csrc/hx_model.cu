@@ -302,6 +302,52 @@ __global__ void __launch_bounds__(256) k_attn_scores(const float *__restrict__ q
     }
 }
 
+// One token with per-head or no qk-norm: the post-processing folded into the score kernel. Each CTA
+// forms its head's q and the token's own k row (bias, qk-norm, RoPE: the same arithmetic as
+// k_attn_post) in shared memory, scores the cache rows r < pos and that k row for r = pos; the first
+// CTA of each kv group's first head writes the token's (k, v) rows into the cache for later kernels.
+__global__ void __launch_bounds__(256) k_attn_scores1(PostArgs a, float *__restrict__ S, float scale) {
+    __shared__ float qh[1024], kp[1024];
+    const int h = blockIdx.y, grp16 = threadIdx.x >> 4, j = threadIdx.x & 15, warp = threadIdx.x >> 5;
+    const int grp = a.H / a.Hkv, g = h / grp;
+    const int pos = *a.dpos;
+    const int qd = a.H * a.hd, kd = a.Hkv * a.hd;
+    const float *qg = a.qkv + h * a.hd, *kg = a.qkv + qd + g * a.hd, *vg = a.qkv + qd + kd + g * a.hd;
+    const float *cs = a.cs + (int64_t)pos * 2 * a.rope_half;
+    if (warp < 2) {   // warp 0: this head's q; warp 1: the kv group's k row of this token
+        float *x = warp == 0 ? qh : kp;
+        const float *src = warp == 0 ? qg : kg;
+        const float *bias = warp == 0 ? (a.bq ? a.bq + h * a.hd : nullptr) : (a.bk ? a.bk + g * a.hd : nullptr);
+        const int lane = threadIdx.x & 31;
+        for (int i = lane; i < a.hd; i += 32) x[i] = bias ? __fadd_rn(src[i], bias[i]) : src[i];
+        __syncwarp();
+        if (a.qk_norm == 1) warp_rmsnorm(x, warp == 0 ? a.qn : a.kn, a.hd, a.eps);
+        if (a.rope_half) warp_rope(x, cs, a.rope_half, a.rope_style);
+    }
+    __syncthreads();
+    if (blockIdx.x == 0 && h % grp == 0) {   // the token's (k, v) rows into the cache
+        const int64_t o = ((int64_t)g * a.max_seq + pos) * a.hd;
+        for (int i = threadIdx.x; i < a.hd; i += blockDim.x) {
+            a.kc[o + i] = kp[i];
+            a.vc[o + i] = a.bv ? __fadd_rn(vg[i], a.bv[g * a.hd + i]) : vg[i];
+        }
+    }
+    for (int r0 = blockIdx.x * 16; r0 <= pos; r0 += gridDim.x * 16) {
+        const int r = r0 + grp16;
+        const bool valid = r <= pos;
+        float L = 0.0f;
+        if (valid) {
+            const float *kr = r == pos ? kp : a.kc + ((int64_t)g * a.max_seq + r) * a.hd;
+            for (int i = j; i < a.hd; i += 16) L = __fadd_rn(L, __fmul_rn(kr[i], qh[i]));
+        }
+        L = tree16(L, 0xffffffffu);
+        if (valid && j == 0) {
+            const float sv = canon(L);
+            S[(int64_t)h * a.max_seq + r] = sv != sv ? sv : __fmul_rn(scale, sv);
+        }
+    }
+}
+
 __global__ void k_set_pos(int *dpos, int v) { *dpos = v; }
 __global__ void k_advance_pos(int *dpos, int T) { *dpos += T; }
 
@@ -917,14 +963,18 @@ static int attention(hxb_model *m, int l, int T, cudaStream_t s) {
     a.rope_style = m->rope_style;
     a.max_seq = m->kv_seq;
     a.eps = m->eps;
-    if (m->qk_norm == 2)
-        k_attn_post<<<dim3(T, 1), 256, sizeof(float) * (m->q_dim + m->kv_dim), s>>>(a);
-    else
-        k_attn_post<<<dim3(T, (m->H + m->Hkv + 7) / 8), 256, sizeof(float) * 8 * m->hd, s>>>(a);
     // the score CTAs of a (token, head) stride over the positions: about 600 CTAs in all
     const int chunks = std::max(1, std::min((int)blocks(m->max_seq, 16), 600 / (m->H * T)));
-    k_attn_scores<<<dim3(chunks, m->H, T), 256, 0, s>>>(a.qout, a.kc, m->S.as<float>(), m->H, m->Hkv, m->hd,
-                                                         m->kv_seq, a.dpos, m->attn_scale);
+    if (T == 1 && m->qk_norm != 2 && m->hd <= 1024) {   // one token: post-processing inside the score kernel
+        k_attn_scores1<<<dim3(chunks, m->H, 1), 256, 0, s>>>(a, m->S.as<float>(), m->attn_scale);
+    } else {
+        if (m->qk_norm == 2)
+            k_attn_post<<<dim3(T, 1), 256, sizeof(float) * (m->q_dim + m->kv_dim), s>>>(a);
+        else
+            k_attn_post<<<dim3(T, (m->H + m->Hkv + 7) / 8), 256, sizeof(float) * 8 * m->hd, s>>>(a);
+        k_attn_scores<<<dim3(chunks, m->H, T), 256, 0, s>>>(a.qout, a.kc, m->S.as<float>(), m->H, m->Hkv, m->hd,
+                                                             m->kv_seq, a.dpos, m->attn_scale);
+    }
     k_attn_softmax<<<dim3(m->H, T), 256, sizeof(float) * m->max_seq, s>>>(m->S.as<float>(), m->H, m->kv_seq, a.dpos);
     // the o projection's activation blocks come out of the value kernel when a CTA holds whole blocks
     const bool fuse_act = is_quant(w.o.dtype) && m->dc == 64;
