@@ -30,7 +30,7 @@ EXPORTS = [
     "hxb_moe_ep_layer_dev", "hxb_moe_ep_combine_dev", "hxb_container_probe", "hxb_moe_load_container",
     "hxb_moe_share_expert", "hxb_model_default_options", "hxb_model_open", "hxb_model_close", "hxb_model_info",
     "hxb_model_forward", "hxb_model_last_routes", "hxb_model_set_replay", "hxb_model_moe", "hxb_model_synthesize",
-    "hxb_model_forward_dev", "hxb_model_sync",
+    "hxb_model_forward_dev", "hxb_model_sync", "hxb_moe_get_expert",
 ]
 
 
@@ -137,6 +137,7 @@ def lib() -> C.CDLL:
         "hxb_model_moe": (vp, [vp]),
         "hxb_model_forward_dev": (i, [vp, vp, i, i, vp, i, vp]),
         "hxb_model_sync": (i, [vp, vp]),
+        "hxb_moe_get_expert": (i, [vp, i, i, vp, sz]),
         "hxb_model_synthesize": (vp, [C.POINTER(ModelArch), C.POINTER(ModelOptions), C.c_uint64, C.c_char_p, sz]),
     }
     for name, (res, args) in sig.items():

@@ -630,6 +630,20 @@ extern "C" HXB_API int hxb_moe_set_expert(hxb_moe *m, int layer, int expert, con
     return HXB_OK;
 }
 
+extern "C" HXB_API int hxb_moe_get_expert(hxb_moe *m, int layer, int expert, void *dst, size_t nbytes) {
+    if (!m || layer < 0 || layer >= m->cfg.n_layers || expert < 0 || expert >= m->cfg.n_experts || !dst ||
+        nbytes < m->slab_bytes)
+        return fail(HXB_E_ARG, "get_expert: bad arguments (dst must hold %zu bytes)", m ? m->slab_bytes : (size_t)0);
+    if (!m->resident_mode) return fail(HXB_E_UNSUPPORTED, "get_expert: the handle does not hold every expert in HBM");
+    const uint8_t *p = m->host_table[(size_t)layer * m->cfg.n_experts + expert];
+    if (!p) return fail(HXB_E_ARG, "get_expert: expert (%d, %d) is not held by this handle", layer, expert);
+    cudaSetDevice(m->device);
+    if (!cuda_ok(cudaStreamSynchronize(m->stream), "get_expert") ||
+        !cuda_ok(cudaMemcpy(dst, p, m->slab_bytes, cudaMemcpyDeviceToHost), "get_expert"))
+        return HXB_E_DEVICE;
+    return HXB_OK;
+}
+
 extern "C" HXB_API int hxb_moe_share_expert(hxb_moe *m, int layer, int expert, int src_layer, int src_expert) {
     if (!m || layer < 0 || layer >= m->cfg.n_layers || expert < 0 || expert >= m->cfg.n_experts || src_layer < 0 ||
         src_layer >= m->cfg.n_layers || src_expert < 0 || src_expert >= m->cfg.n_experts)
@@ -651,7 +665,6 @@ extern "C" HXB_API int hxb_moe_share_expert(hxb_moe *m, int layer, int expert, i
 
 extern "C" HXB_API int hxb_moe_synthesize(hxb_moe *m, uint64_t seed, float sigma_router, float sigma_expert) {
     if (!m) return fail(HXB_E_ARG, "synthesize: null handle");
-    if (!m->resident_mode) return fail(HXB_E_ARG, "synthesize: needs every expert resident (cache_gb = 0)");
     if (m->cfg.expert_dtype != Q4) return fail(HXB_E_UNSUPPORTED, "synthesize: Q4 experts only");
     if (m->cfg.shared_ffn_dim && m->cfg.shared_dtype != Q4 && m->cfg.shared_dtype != Q8)
         return fail(HXB_E_UNSUPPORTED, "synthesize: Q4/Q8 shared experts only");
@@ -695,12 +708,34 @@ extern "C" HXB_API int hxb_moe_synthesize(hxb_moe *m, uint64_t seed, float sigma
         cudaMemcpy(b.norm.p, ones.data(), sizeof(float) * D, cudaMemcpyHostToDevice);
         b.set = true;
         m->refresh_maps(l);
+        if (!m->resident_mode) continue;
         for (int e = 0; e < E; e++) {
             if (!m->owns(e)) continue;
             uint8_t *p = m->store.place_resident(l, e);
             if (!p) return fail(HXB_E_NOMEM, "synthesize: no slot");
             m->host_table[(size_t)l * E + e] = p;
         }
+    }
+    if (!m->resident_mode) {   // the store's host tier: each slab generated on the device, then handed over
+        DevBuf tmp;
+        std::vector<uint8_t> host(m->slab_bytes);
+        if (!tmp.alloc(m->slab_bytes)) return fail(HXB_E_NOMEM, "synthesize: out of device memory");
+        for (int64_t i = 0; i < (int64_t)L * E; i++) {
+            if (!m->owns((int)(i % E))) continue;
+            if (!cuda_ok(launch_synth_q4(tmp.as<uint8_t>(), 1, (int64_t)m->slab_bytes, D, k.expert_ffn_dim, seed,
+                                         sigma_expert, m->stream, i),
+                         "synth experts") ||
+                !cuda_ok(cudaMemcpyAsync(host.data(), tmp.p, m->slab_bytes, cudaMemcpyDeviceToHost, m->stream),
+                         "synth copy") ||
+                !cuda_ok(cudaStreamSynchronize(m->stream), "synth copy"))
+                return HXB_E_DEVICE;
+            std::string why;
+            if (!m->store.set_source((int)(i / E), (int)(i % E), host.data(), m->slab_bytes, why))
+                return fail(HXB_E_NOMEM, "synthesize: %s", why.c_str());
+        }
+        m->dec_dirty = true;
+        drop_graphs(m);
+        return cuda_ok(cudaStreamSynchronize(m->stream), "synthesize") ? HXB_OK : HXB_E_DEVICE;
     }
     if (k.ep_size > 1) {   // this rank's slabs, each the bytes of its place in the whole sequence
         for (int64_t i = 0; i < (int64_t)L * E; i++)

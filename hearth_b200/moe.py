@@ -231,6 +231,14 @@ class MoeBackend:
         return ids, w
 
     # ------------------------------------------------------------------ store
+    def get_expert(self, layer: int, expert: int, out=None):
+        """The expert's slab bytes as this (resident) handle holds them in HBM."""
+        n = int(lib().hxb_moe_slab_bytes(self.h))
+        if out is None:
+            out = np.empty(n, np.uint8)
+        check(lib().hxb_moe_get_expert(self.h, layer, expert, out.ctypes.data, out.nbytes), "hxb_moe_get_expert")
+        return out
+
     def stats(self) -> dict:
         s = MoeStats()
         check(lib().hxb_moe_get_stats(self.h, C.byref(s)), "hxb_moe_get_stats")

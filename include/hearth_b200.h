@@ -144,9 +144,15 @@ HXB_API int hxb_moe_set_layer(hxb_moe *m, int layer, const float *router, const 
 /* One routed expert's slab (docs/FORMAT.md §5 layout, nbytes = the slab size) from host memory.
  * The store keeps a pinned host copy (the host tier) and moves it into HBM when needed. */
 HXB_API int hxb_moe_set_expert(hxb_moe *m, int layer, int expert, const void *slab, size_t nbytes);
+/* The bytes of one expert's slab as the handle holds them in HBM (every expert resident; nbytes >= the
+ * slab size), e.g. to hand a synthesized stack to a streaming handle. No counterpart in the
+ * reference (its slabs are read from the container file). */
+HXB_API int hxb_moe_get_expert(hxb_moe *m, int layer, int expert, void *dst, size_t nbytes);
 /* Benchmarks without a container: deterministic synthetic router (N(0, sigma_router)), selection
  * bias (N(0, sigma_router / 2), score_bias handles), unit norms, Q4 expert slabs and the Q4/Q8
- * shared expert (with its gate input) for every layer, generated in HBM (every expert resident).
+ * shared expert (with its gate input) for every layer, generated in HBM. A handle whose HBM budget
+ * holds every expert keeps them resident; a smaller budget gets the same bytes in the store's pinned
+ * host tier (each slab generated on the device and copied out), streamed like a container's.
  * With expert parallelism each rank generates only the slabs it owns, byte for byte the slabs of
  * the same seed on one GPU. */
 HXB_API int hxb_moe_synthesize(hxb_moe *m, uint64_t seed, float sigma_router, float sigma_expert);
