@@ -705,6 +705,7 @@ __global__ void __launch_bounds__(512) k_moe_gateup(MoeShape sh, MoeLayerDev L, 
 // SwiGLU and the mid activation block follow in the CTA. Used when rows are whole 16-byte units.
 constexpr int G1_WARPS = 12;
 constexpr int G1_SLOT = 16 * 1024;
+constexpr int G1_TMAX = 4;   // tokens per job (decode, speculative verification of a few tokens)
 
 __host__ __device__ inline int g1_tile_rows(int64_t rb) {   // largest power of two <= 32 with TR * rb <= G1_SLOT
     int tr = 32;
@@ -721,9 +722,10 @@ __device__ void gateup1_body(const MoeShape &sh, const MoeScratch &sc, const Job
     const int TR = g1_tile_rows(rbD), ntile = 2 * GU_ROWS / TR;   // gate tiles, then up tiles
     uint64_t *bar = reinterpret_cast<uint64_t *>(smem) + warp;
     uint8_t *slot = smem + 128 + (size_t)warp * G1_SLOT;
-    act_q8 *acts = reinterpret_cast<act_q8 *>(smem + 128 + (size_t)G1_WARPS * G1_SLOT);
-    float *P = reinterpret_cast<float *>(acts + nbD) + warp * ROWS_1TOK * 33;
-    float *GU = reinterpret_cast<float *>(acts + nbD) + G1_WARPS * ROWS_1TOK * 33;   // [2][64]
+    const int nt = job.n;   // <= G1_TMAX (host condition)
+    act_q8 *acts = reinterpret_cast<act_q8 *>(smem + 128 + (size_t)G1_WARPS * G1_SLOT);   // [nt][nbD]
+    float *P = reinterpret_cast<float *>(acts + sh.T * nbD) + warp * ROWS_1TOK * 33;
+    float *GU = reinterpret_cast<float *>(acts + sh.T * nbD) + G1_WARPS * ROWS_1TOK * 33;   // [nt][2][64]
     auto issue = [&](int tile) {
         const int r = tile * TR;   // row in [0, 128): gate rows, then up rows
         const uint8_t *src = (r < GU_ROWS ? job.gate : job.up) + ((int64_t)rb * GU_ROWS + (r % GU_ROWS)) * rbD;
@@ -735,10 +737,10 @@ __device__ void gateup1_body(const MoeShape &sh, const MoeScratch &sc, const Job
         fence_mbar_init();
         if (warp < ntile) issue(warp);
     }
-    {   // the token's activation blocks
-        const int t = job_token(sc, job, 0);
+    for (int i = 0; i < nt; i++) {   // the tokens' activation blocks
+        const int t = job_token(sc, job, i);
         const uint32_t *src = reinterpret_cast<const uint32_t *>(sc.xact + (int64_t)t * nbD);
-        uint32_t *dst = reinterpret_cast<uint32_t *>(acts);
+        uint32_t *dst = reinterpret_cast<uint32_t *>(acts + (int64_t)i * nbD);
         for (int k = threadIdx.x; k < nbD * (ACT_BLOCK / 4); k += blockDim.x) dst[k] = src[k];
     }
     __syncthreads();
@@ -747,9 +749,10 @@ __device__ void gateup1_body(const MoeShape &sh, const MoeScratch &sc, const Job
     for (int tile = warp; tile < ntile; tile += G1_WARPS, k++) {
         ok = ok && mbar_wait(bar, (uint32_t)(k & 1), sc.err);
         if (ok)
-            for (int r8 = 0; r8 < TR; r8 += ROWS_1TOK)
-                warp_rows_1tok<DT>(slot + (int64_t)r8 * rbD, rbD, nbD, min(ROWS_1TOK, TR - r8), acts, P,
-                                   GU + tile * TR + r8);
+            for (int i = 0; i < nt; i++)   // the tile stays in shared memory for every token
+                for (int r8 = 0; r8 < TR; r8 += ROWS_1TOK)
+                    warp_rows_1tok<DT>(slot + (int64_t)r8 * rbD, rbD, nbD, min(ROWS_1TOK, TR - r8), acts + (int64_t)i * nbD,
+                                       P, GU + i * 2 * GU_ROWS + tile * TR + r8);
         if (lane == 0 && tile + G1_WARPS < ntile && ok) {
             fence_proxy_async();
             issue(tile + G1_WARPS);
@@ -757,9 +760,11 @@ __device__ void gateup1_body(const MoeShape &sh, const MoeScratch &sc, const Job
         __syncwarp();
     }
     __syncthreads();
-    if (warp == 0 && ok)
-        act_quant_warp(swiglu_c(GU[lane], GU[GU_ROWS + lane]), swiglu_c(GU[lane + 32], GU[GU_ROWS + lane + 32]),
-                       sc.act_mid + (int64_t)job.p0 * fmax_nb + rb, lane);
+    if (warp < nt && ok) {   // warp i: token i's SwiGLU and mid activation block
+        const float *G = GU + warp * 2 * GU_ROWS, *U = G + GU_ROWS;
+        act_quant_warp(swiglu_c(G[lane], U[lane]), swiglu_c(G[lane + 32], U[lane + 32]),
+                       sc.act_mid + (int64_t)(job.p0 + warp) * fmax_nb + rb, lane);
+    }
 }
 
 __global__ void __launch_bounds__(G1_WARPS * 32) k_moe_gateup1(MoeShape sh, MoeLayerDev L, MoeScratch sc,
@@ -776,9 +781,9 @@ __global__ void __launch_bounds__(G1_WARPS * 32) k_moe_gateup1(MoeShape sh, MoeL
     else gateup1_body<Q8>(sh, sc, job, fmax_nb, smem, rb);
 }
 
-static size_t gateup1_smem(int nbD) {
-    return 128 + (size_t)G1_WARPS * G1_SLOT + (size_t)nbD * ACT_BLOCK + (size_t)G1_WARPS * ROWS_1TOK * 33 * 4 +
-           2 * GU_ROWS * 4 + 64;
+static size_t gateup1_smem(int nbD, int T) {
+    return 128 + (size_t)G1_WARPS * G1_SLOT + (size_t)T * nbD * ACT_BLOCK + (size_t)G1_WARPS * ROWS_1TOK * 33 * 4 +
+           (size_t)T * 2 * GU_ROWS * 4 + 64;
 }
 
 struct DownCfg {
@@ -935,7 +940,8 @@ __global__ void __launch_bounds__(256) k_moe_down1(MoeShape sh, MoeLayerDev L, M
     uint64_t *bar = reinterpret_cast<uint64_t *>(smem) + warp;
     uint8_t *slot = smem + 128 + (size_t)warp * D1_SLOT;
     float *P = reinterpret_cast<float *>(smem + 128 + (size_t)8 * D1_SLOT) + warp * ROWS_1TOK * 33;
-    float *Ys = reinterpret_cast<float *>(smem + 128 + (size_t)8 * D1_SLOT) + 8 * ROWS_1TOK * 33;   // [K + 1][DN_ROWS]
+    // [T * K pairs + T shared rows][DN_ROWS], the fused down kernel's layout
+    float *Ys = reinterpret_cast<float *>(smem + 128 + (size_t)8 * D1_SLOT) + 8 * ROWS_1TOK * 33;
     const int units = njobs * (DN_ROWS / ROWS_1TOK);
     auto issue = [&](int un) {
         const int u = un / (DN_ROWS / ROWS_1TOK), gi = un - u * (DN_ROWS / ROWS_1TOK);
@@ -964,11 +970,13 @@ __global__ void __launch_bounds__(256) k_moe_down1(MoeShape sh, MoeLayerDev L, M
         get_job(sh, L, sc, u, nu, job);
         ok = mbar_wait(bar, (uint32_t)(k & 1), sc.err);
         if (!ok) break;
-        // pair outputs by pair index (one pair per bucket at T = 1), the shared expert's after the K pairs
-        float *yout = Ys + (job.shared ? sh.route.K : job.p0) * DN_ROWS + gi * ROWS_1TOK;
-        const act_q8 *act = sc.act_mid + (int64_t)job.p0 * fmax_nb;
-        if (job.dtype == Q4) warp_rows_1tok<Q4>(slot, row_bytes(Q4, job.F), job.F / QK, ROWS_1TOK, act, P, yout);
-        else warp_rows_1tok<Q8>(slot, row_bytes(Q8, job.F), job.F / QK, ROWS_1TOK, act, P, yout);
+        // pair outputs by pair index, the shared expert's rows after the T * K pairs (one per token)
+        for (int i = 0; i < job.n; i++) {
+            float *yout = Ys + (job.shared ? sh.T * sh.route.K + i : job.p0 + i) * DN_ROWS + gi * ROWS_1TOK;
+            const act_q8 *act = sc.act_mid + (int64_t)(job.p0 + i) * fmax_nb;
+            if (job.dtype == Q4) warp_rows_1tok<Q4>(slot, row_bytes(Q4, job.F), job.F / QK, ROWS_1TOK, act, P, yout);
+            else warp_rows_1tok<Q8>(slot, row_bytes(Q8, job.F), job.F / QK, ROWS_1TOK, act, P, yout);
+        }
         if (un + 8 < units) {
             int issued = 1;
             if (lane == 0) {
@@ -986,13 +994,16 @@ __global__ void __launch_bounds__(256) k_moe_down1(MoeShape sh, MoeLayerDev L, M
     if (!all_ok) return;
     // finish this CTA's rows: rank-order sum, shared expert, residual (as the fused down kernel)
     const bool has_shared = L.Fs > 0;
-    for (int rr = threadIdx.x; rr < DN_ROWS; rr += blockDim.x)
-        finish_row(sh, sc, 0, r0 + rr, Ys + rr, DN_ROWS, has_shared ? Ys[sh.route.K * DN_ROWS + rr] : 0.0f, has_shared,
+    const int npairs = sh.T * sh.route.K;
+    for (int it = threadIdx.x; it < sh.T * DN_ROWS; it += blockDim.x) {
+        const int t = it / DN_ROWS, rr = it - t * DN_ROWS;
+        finish_row(sh, sc, t, r0 + rr, Ys + rr, DN_ROWS, has_shared ? Ys[(npairs + t) * DN_ROWS + rr] : 0.0f, has_shared,
                    L.sh_gate_inp ? sc.sh_logit : nullptr, h, out, resid != 0);
+    }
 }
 
-static size_t down1_smem(int K) {
-    return 128 + (size_t)8 * D1_SLOT + (size_t)8 * ROWS_1TOK * 33 * 4 + (size_t)(K + 1) * DN_ROWS * 4 + 64;
+static size_t down1_smem(int T, int K) {
+    return 128 + (size_t)8 * D1_SLOT + (size_t)8 * ROWS_1TOK * 33 * 4 + (size_t)(T * K + T) * DN_ROWS * 4 + 64;
 }
 
 // Expert-parallel combine: pair (t, j) of expert e comes from rank e % ep_size's slice of y_all.
@@ -1127,12 +1138,12 @@ static cudaError_t launch_expert_stages(int which, const MoeShape &sh, const Moe
     // one token: the single-token kernels (rows of whole 16-byte units; at least 2 rows of the widest
     // gate/up dtype per slot)
     const int64_t rbD_max = std::max<int64_t>(row_bytes(L.expert_dtype, sh.D), L.Fs > 0 ? row_bytes(L.sh_dtype, sh.D) : 0);
-    const bool one_token = T == 1 && (sh.D / QK) % 8 == 0 && (sh.F % GU_ROWS) == 0 && (L.Fs % GU_ROWS) == 0 &&
-                           rbD_max * 2 <= G1_SLOT && gateup1_smem(sh.D / QK) + 1024 <= smem_limit();
+    const bool one_token = T <= G1_TMAX && (sh.D / QK) % 8 == 0 && (sh.F % GU_ROWS) == 0 && (L.Fs % GU_ROWS) == 0 &&
+                           rbD_max * 2 <= G1_SLOT && gateup1_smem(sh.D / QK, T) + 1024 <= smem_limit();
     if ((which & 1) && one_token) {
         const int maxjobs = std::min(E, T * K) + (L.Fs > 0 ? 1 : 0);
         dim3 grid((unsigned)(std::max(sh.F, L.Fs) / GU_ROWS), (unsigned)maxjobs);
-        k_moe_gateup1<<<grid, G1_WARPS * 32, gateup1_smem(sh.D / QK), s>>>(sh, L, sc, fmax_nb);
+        k_moe_gateup1<<<grid, G1_WARPS * 32, gateup1_smem(sh.D / QK, T), s>>>(sh, L, sc, fmax_nb);
     } else if (which & 1) {
         GateUpCfg c;
         c.nbD = sh.D / QK;
@@ -1160,9 +1171,10 @@ static cudaError_t launch_expert_stages(int which, const MoeShape &sh, const Moe
     // ---- down (+ rank-order sum for small batches)
     const int64_t rbF_max = std::max<int64_t>(row_bytes(L.expert_dtype, sh.F), L.Fs > 0 ? row_bytes(L.sh_dtype, L.Fs) : 0);
     const bool down_one = one_token && fused && sh.D % DN_ROWS == 0 && (sh.F / QK) % 8 == 0 && (L.Fs / QK) % 8 == 0 &&
-                          ROWS_1TOK * rbF_max <= D1_SLOT && down1_smem(K) + 1024 <= smem_limit();
+                          ROWS_1TOK * rbF_max <= D1_SLOT && down1_smem(T, K) + 1024 <= smem_limit();
     if ((which & 2) && down_one) {
-        k_moe_down1<<<(unsigned)(sh.D / DN_ROWS), 256, down1_smem(K), s>>>(sh, L, sc, fmax_nb, h, out, resid ? 1 : 0);
+        k_moe_down1<<<(unsigned)(sh.D / DN_ROWS), 256, down1_smem(T, K), s>>>(sh, L, sc, fmax_nb, h, out,
+                                                                            resid ? 1 : 0);
     } else if (which & 2) {
         DownCfg c;
         c.fmax_nb = fmax_nb;
