@@ -122,9 +122,9 @@ def step_bytes(B):
 
 
 # DRAM bytes (read + write) per layer of k_moe_decode from one ncu capture of a 4-layer launch of the
-# same shape (bench.py --layers 4: dram__bytes_read.sum 94.63 MB, dram__bytes_write.sum 2.89 MB); a
+# same shape (bench.py --layers 4: dram__bytes_read.sum 84.73 MB, dram__bytes_write.sum 1.87 MB); a
 # launch's traffic grows with its layers, so the full launch's figure is this times its layers.
-DECODE_DRAM_BYTES_PER_LAYER = (94_631_424 + 2_893_312) / 4
+DECODE_DRAM_BYTES_PER_LAYER = (84_732_928 + 1_870_848) / 4
 
 
 def workload_config(B, world, parallelism=None):
@@ -296,9 +296,9 @@ def run_reference(args, rank, world):
 
 
 TRACE_STAMPS = ["start", "h polled", "rmsnorm chain", "router rows in", "x", "logit stored", "activation blocks",
-                "predicted-logit partial", "logits polled", "routed", "routing barrier", "first chunk landed",
-                "its SwiGLU stored", "exchange reset", "mid polled", "mid blocks", "down rows landed",
-                "down rows computed", "y stored", "y polled", "h stored"]
+                "logits polled", "routed",
+                "routing barrier", "first chunk landed", "its SwiGLU stored", "exchange reset", "mid polled", "mid blocks",
+                "down rows landed", "down rows computed", "y stored", "y polled", "h stored"]
 
 
 def run_trace(args, local_rank):

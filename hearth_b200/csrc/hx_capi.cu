@@ -908,8 +908,6 @@ static cudaError_t enqueue_decode(hxb_moe *m, float *h, int l0, int nl, cudaStre
     p.ids_out = m->ids.as<int>();
     p.w_out = m->wts.as<float>();
     p.trace = m->dec_trace.as<unsigned long long>();
-    p.prefetch = true;
-    p.slab_used = (m->lay.end + 15) / 16 * 16;
     p.ep_size = k.ep_size;
     p.ep_rank = k.ep_rank;
     p.ep_y = k.ep_size > 1 ? m->ep_peers.as<uint64_t *const>() : nullptr;

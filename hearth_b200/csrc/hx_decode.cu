@@ -9,14 +9,13 @@
 // own readiness flags: every slot holds kEmpty (0xffffffff, a NaN bit pattern no canonicalised value
 // has) until its producer stores the value, and a consumer polls exactly the words it needs. There
 // is no grid barrier, no atomic and no fence on the data path. Per layer l:
-//   P1  every CTA: h_l (layer 0: the input; later: polled from xh[l]), rmsnorm, x, activation
-//       blocks; CTA c computes router row c (dot16) -> xlg[l][c], and a predicted logit of the next
-//       layer's router -> xpr[l][c] (steers the L2 prefetch only);
-//   P2  every CTA: polls the E logits, routes the token (identical everywhere), issues the bulk
-//       copies of its gate/up chunks and of its down rows;
-//   P3  CTA c: gate/up chunks [c*NCH/G, (c+1)*NCH/G) of the K x F/4 four-row-pair chunks (warp q
-//       takes chunk q as soon as it lands), SwiGLU -> xmid[l][j][f]; the issuing warp then predicts
-//       the next layer's experts and issues L2 prefetches of this CTA's share of their slabs;
+//   P1  every CTA: h_l (layer 0: the input; later: polled from xh[l]), rmsnorm, x; CTA c computes
+//       router row c (dot16) -> xlg[l][c];
+//   P2  every CTA: every warp forms x's activation blocks, the CTA polls the E logits, warp 0 routes
+//       the token (identical everywhere); then the bulk copies of its gate/up chunks and of its down
+//       rows go out;
+//   P3  CTA c: gate/up chunks [c*NCH/G, (c+1)*NCH/G) of the K x F/ch chunks of ch row pairs (warp q
+//       takes chunk q as soon as it lands), SwiGLU -> xmid[l][j][f];
 //   P4  CTA c belongs to the down group of rank j = c*K/G: polls expert j's F mid values, forms its
 //       F/64 activation blocks (NUMERICS §2), computes its slice of expert j's down rows -> xy[l][j][d];
 //   P5  CTA c owns h rows [c*D/G, (c+1)*D/G): polls y of the K experts for them, rank-order sum,
@@ -43,36 +42,26 @@ namespace hx {
 
 constexpr int DEC_THREADS = 512;
 constexpr int DEC_WARPS = DEC_THREADS / 32;
-constexpr int DEC_CH = 4;          // gate/up row pairs per chunk (one mbarrier, two bulk copies)
 constexpr int DEC_PROWS = ROWS_1TOK;   // rows per warp_rows_1tok call (P buffer rows)
 constexpr int DEC_MAXL = 128;      // layers per launch (router / norm / bias pointer tables in smem)
 constexpr int DEC_MAXCH = 26;      // gate/up chunks per CTA (mbarriers 0..25)
 constexpr int BAR_DOWN = 28, BAR_ROUTER = 29;
-constexpr int kIssueWarp = DEC_WARPS - 1;   // issues the bulk copies and the prefetch of a layer
+constexpr int kIssueWarp = DEC_WARPS - 1;   // issues the bulk copies of a layer
 constexpr uint32_t kEmpty = 0xffffffffu;
 constexpr uint32_t kPollLimit = 1u << 18;   // polls of one word before giving up (~30 ms)
 enum : int { DEV_E_POLL = 4 };             // an exchange word never arrived
 
 // Phase stamps of the optional timeline (thread 0 of every CTA, per layer).
 // ST_H h polled; ST_RMS rmsnorm chain done; ST_NORM router rows in, barrier; ST_X x; ST_LOGIT logit
-// stored; ST_ACT activation blocks; ST_PRED predicted-logit partial; ST_LG logits polled; ST_RT
-// routed; ST_ROUTE barrier after routing; ST_CH0 thread 0's chunk landed; ST_CHD its SwiGLU values
-// stored; ST_RESET other set's slots reset; ST_MIDP mid polled; ST_MIDQ mid blocks; ST_DNW down rows
+// stored; ST_ACT activation blocks; ST_LG logits polled; ST_RT routed; ST_ROUTE barrier after
+// routing; ST_CH0 thread 0's chunk landed; ST_CHD its SwiGLU values stored; ST_RESET other set's slots reset; ST_MIDP mid polled; ST_MIDQ mid blocks; ST_DNW down rows
 // landed; ST_DOWN down rows computed; ST_YST y stored; ST_Y y polled; ST_SUM h stored.
-enum : int { ST_START, ST_H, ST_RMS, ST_NORM, ST_X, ST_LOGIT, ST_ACT, ST_PRED, ST_LG, ST_RT, ST_ROUTE, ST_CH0,
+enum : int { ST_START, ST_H, ST_RMS, ST_NORM, ST_X, ST_LOGIT, ST_ACT, ST_LG, ST_RT, ST_ROUTE, ST_CH0,
              ST_CHD, ST_RESET, ST_MIDP, ST_MIDQ, ST_DNW, ST_DOWN, ST_YST, ST_Y, ST_SUM, DEC_STAMPS };
-
-// Next-layer prefetch: each CTA c < E also computes router[l+1][c] . (h_l * rms(h_l) * ffn_norm[l+1])
-// in any summation order (it only steers the prefetch); an idle warp of every CTA takes the K
-// largest of these, and the CTAs issue cp.async.bulk.prefetch.L2 over those experts' slabs in
-// kPrefetchPiece pieces (piece i by CTA i mod G), early in the layer. A prefetch only moves data into
-// L2, so it cannot change any result.
-constexpr int kPredVec = 2;                 // float4 router / norm values per thread: D <= 4096
-constexpr uint32_t kPrefetchPiece = 32768;  // bytes per prefetch instruction
 
 // Work split of one launch (identical on host and device).
 struct DecodePlan {
-    int G, nch, ch_max;           // CTAs, gate/up chunks (K * F / 4), chunks per CTA at most
+    int G, ch, nch, ch_max;       // CTAs, row pairs per chunk, gate/up chunks (K * F / ch), chunks per CTA at most
     int ra, dr_max, hr_max;       // down-row alignment, down rows / CTA at most, h rows / CTA at most
     int rpc;                      // router rows per CTA
 };
@@ -98,7 +87,10 @@ HX_HD inline void h_rows(int c, int G, int D, int *r0, int *r1) {
 HX_HD inline DecodePlan decode_plan(int G, int D, int F, int E, int K, int dtype) {
     DecodePlan P{};
     P.G = G;
-    P.nch = K * F / DEC_CH;
+    // gate/up row pairs per chunk (one mbarrier, two bulk copies): 4 (3 measured no faster on the
+    // Qwen3 shape), 2 when F is not a multiple of 4
+    P.ch = F % 4 == 0 ? 4 : 2;
+    P.nch = K * F / P.ch;
     P.ch_max = (P.nch + G - 1) / G;
     const int64_t rbF = row_bytes(dtype, F);
     P.ra = 1;
@@ -116,7 +108,7 @@ struct DecodeLayout {
     int nbD, nbF;
     int64_t rbD, rbF;
     size_t off_hs, off_xs, off_xact, off_stab, off_rrow, off_norm, off_gu, off_dn, off_mid, off_amid, off_y, off_p,
-        off_gout, off_lg, off_pr, off_score, off_sel, off_key, off_gsc, off_keep, off_ids, off_w, off_yv, off_ptrs,
+        off_gout, off_lg, off_score, off_sel, off_key, off_gsc, off_keep, off_ids, off_w, off_yv, off_ptrs,
         off_chain, total;
     int cs;   // floats per lane row of the chain buffer
 };
@@ -140,7 +132,7 @@ HX_HD inline DecodeLayout decode_layout(int G, int D, int F, int E, int K, int d
     L.off_rrow = o; o = align16(o + (size_t)P.rpc * D * 4);
     L.off_norm = o; o = align16(o + (size_t)D * 4);
     // tiles keep 16 readable bytes after them (the padded block loaders read up to 2 past a block)
-    L.off_gu = o; o = align16(o + (size_t)P.ch_max * 2 * DEC_CH * L.rbD + 16);
+    L.off_gu = o; o = align16(o + (size_t)P.ch_max * 2 * P.ch * L.rbD + 16);
     L.off_dn = o; o = align16(o + (size_t)P.dr_max * L.rbF + 16);
     L.off_mid = o; o = align16(o + (size_t)F * 4);
     L.off_amid = o; o = align16(o + (size_t)L.nbF * ACT_BLOCK);
@@ -148,7 +140,6 @@ HX_HD inline DecodeLayout decode_layout(int G, int D, int F, int E, int K, int d
     L.off_p = o; o = align16(o + (size_t)DEC_WARPS * DEC_PROWS * 33 * 4);
     L.off_gout = o; o = align16(o + (size_t)DEC_WARPS * DEC_PROWS * 4);
     L.off_lg = o; o = align16(o + (size_t)Ek * 4);
-    L.off_pr = o; o = align16(o + (size_t)Ek * 4);
     L.off_score = o; o = align16(o + (size_t)E * 4);
     L.off_sel = o; o = align16(o + (size_t)E * 4);
     L.off_key = o; o = align16(o + (size_t)Ek * 8);
@@ -166,10 +157,10 @@ HX_HD inline DecodeLayout decode_layout(int G, int D, int F, int E, int K, int d
     return L;
 }
 
-// Exchange buffers of one set, in floats: xlg [Lb][E], xpr [Lb][E], xmid [Lb][K][F], xy [Lb][K][D],
+// Exchange buffers of one set, in floats: xlg [Lb][E], xmid [Lb][K][F], xy [Lb][K][D],
 // xh [Lb][D] (Lb = buffer layers, at least the layers of any launch).
 HX_HD inline int64_t xset_floats(int Lb, int D, int F, int E, int K) {
-    return (int64_t)Lb * (2 * (int64_t)E + (int64_t)K * F + (int64_t)K * D + D);
+    return (int64_t)Lb * ((int64_t)E + (int64_t)K * F + (int64_t)K * D + D);
 }
 
 struct DecodeArgs {
@@ -190,8 +181,6 @@ struct DecodeArgs {
     int *ids_out;                 // [K] routing of the last layer
     float *w_out;
     unsigned long long *trace;    // null, or [Lyr][G][DEC_STAMPS] SM clock stamps of thread 0
-    bool predict;                 // next-layer prediction and prefetch
-    int64_t slab_used;            // bytes of a slab the kernels read (prefetch extent)
     int ep_size, ep_rank;         // expert parallelism (1, 0: every expert here)
     uint64_t *const *ep_y;        // [ep_size] every GPU's y words [Lb][K][D] (this GPU's at ep_rank)
     DecodeLayout lay;
@@ -201,10 +190,6 @@ __device__ __forceinline__ unsigned long long sm_clock() {
     unsigned long long t;
     asm volatile("mov.u64 %0, %clock64;" : "=l"(t));
     return t;
-}
-
-__device__ __forceinline__ void prefetch_l2(const void *p, uint32_t bytes) {
-    asm volatile("cp.async.bulk.prefetch.L2.global [%0], %1;" ::"l"(p), "r"(bytes) : "memory");
 }
 
 __device__ __forceinline__ float ld_poll(const float *p) {
@@ -299,42 +284,6 @@ __device__ __forceinline__ float chain16_regs(const float *c, int cs, int n4) {
     return tree16(L, 0xffffffffu);
 }
 
-// The K largest of E <= 128 values (one warp; any order among equal values): ids[0..K) of the
-// predicted experts (-1 when fewer than K are numbers). Each round takes the warp maximum of an
-// order-preserving 32-bit key.
-__device__ __forceinline__ void warp_topk_pred(const float *v, int E, int K, int *ids) {
-    const int lane = threadIdx.x & 31;
-    uint32_t key[4];
-#pragma unroll
-    for (int t = 0; t < 4; t++) {
-        const int i = t * 32 + lane;
-        const uint32_t b = i < E ? __float_as_uint(v[i]) : 0u;
-        const bool nan = (b & 0x7fffffffu) > 0x7f800000u;
-        key[t] = i >= E || nan ? 0u : ((b & 0x80000000u) ? ~b : (b | 0x80000000u));
-    }
-    for (int r = 0; r < K; r++) {
-        uint32_t best = 0;
-        int bt = 0;
-#pragma unroll
-        for (int t = 0; t < 4; t++)
-            if (key[t] > best) {
-                best = key[t];
-                bt = t;
-            }
-        const uint32_t top = __reduce_max_sync(0xffffffffu, best);
-        const unsigned owners = __ballot_sync(0xffffffffu, best == top && top != 0u);
-        if (!owners) {
-            if (lane == 0) ids[r] = -1;
-            continue;
-        }
-        const int src = __ffs(owners) - 1;
-        const int id = __shfl_sync(0xffffffffu, bt * 32 + lane, src);
-        if (lane == src) key[bt] = 0u;
-        if (lane == 0) ids[r] = id;
-    }
-    __syncwarp();
-}
-
 template <int DT>
 __device__ void decode_body(const DecodeArgs &a, uint8_t *smem) {
     const DecodeLayout &ly = a.lay;
@@ -357,7 +306,6 @@ __device__ void decode_body(const DecodeArgs &a, uint8_t *smem) {
     float *P = reinterpret_cast<float *>(smem + ly.off_p) + warp * DEC_PROWS * 33;
     float *gout = reinterpret_cast<float *>(smem + ly.off_gout) + warp * DEC_PROWS;
     float *lgs = reinterpret_cast<float *>(smem + ly.off_lg);
-    float *prs = reinterpret_cast<float *>(smem + ly.off_pr);
     float *score = reinterpret_cast<float *>(smem + ly.off_score);
     float *sel = reinterpret_cast<float *>(smem + ly.off_sel);
     unsigned long long *rkey = reinterpret_cast<unsigned long long *>(smem + ly.off_key);
@@ -370,8 +318,6 @@ __device__ void decode_body(const DecodeArgs &a, uint8_t *smem) {
     const float **p_norm = p_router + DEC_MAXL, **p_bias = p_norm + DEC_MAXL;
     float *chb = reinterpret_cast<float *>(smem + ly.off_chain);
     __shared__ float rms_r;
-    __shared__ float pred_part[DEC_WARPS];
-    __shared__ int pred_ids[16];
     __shared__ unsigned s_epoch, s_prev;
 
     for (int i = tid; i < a.Lyr; i += DEC_THREADS) {
@@ -392,10 +338,9 @@ __device__ void decode_body(const DecodeArgs &a, uint8_t *smem) {
     const int64_t xset = xset_floats(a.Lb, D, F, E, K);
     float *X = a.xbuf + (int64_t)(s_epoch & 1u) * xset;
     float *Xo = a.xbuf + (int64_t)((s_epoch & 1u) ^ 1u) * xset;
-    const int64_t o_lg = 0, o_pr = (int64_t)a.Lb * E, o_mid = o_pr + (int64_t)a.Lb * E,
+    const int64_t o_lg = 0, o_mid = (int64_t)a.Lb * E,
                   o_y = o_mid + (int64_t)a.Lb * K * F, o_h = o_y + (int64_t)a.Lb * K * D;
     auto xlg = [&](int l) { return X + o_lg + (int64_t)l * E; };
-    auto xpr = [&](int l) { return X + o_pr + (int64_t)l * E; };
     auto xmid = [&](int l, int j) { return X + o_mid + ((int64_t)l * K + j) * F; };
     auto xy = [&](int l, int j) { return X + o_y + ((int64_t)l * K + j) * D; };
     auto xh = [&](int l) { return X + o_h + (int64_t)l * D; };
@@ -414,8 +359,9 @@ __device__ void decode_body(const DecodeArgs &a, uint8_t *smem) {
     const bool ep = a.ep_size > 1;
     __shared__ int s_own[16], s_nown;
     const uint32_t ep_tag = s_epoch + 1u;   // y words of this launch (buffers start at 0)
-    const int cpe = F / DEC_CH;   // chunks per expert
-    const uint32_t chunk_bytes = (uint32_t)(DEC_CH * ly.rbD);
+    const int CH = pl.ch;
+    const int cpe = F / CH;   // chunks per expert
+    const uint32_t chunk_bytes = (uint32_t)(CH * ly.rbD);
     const bool small_route = E <= 128 && a.route.n_group <= 1;
 
     auto issue_router = [&](int l) {   // router rows e = c + t*G, ffn_norm and the slab pointers of layer l
@@ -439,21 +385,7 @@ __device__ void decode_body(const DecodeArgs &a, uint8_t *smem) {
 #define HX_STAMP(i) \
     if (stamp && tid == 0) stamp[i] = sm_clock()
         HX_STAMP(ST_START);
-        // ---------------- P1: h, rmsnorm, activations, router rows, predicted logit
-        const bool predict = a.predict && l + 1 < a.Lyr;   // launch-uniform
-        float4 pr[kPredVec], pn[kPredVec];
-        if (predict && c < E) {   // operands of the predicted logit (independent of h)
-            const float4 *rw = reinterpret_cast<const float4 *>(p_router[l + 1] + (size_t)c * D);
-            const float4 *nw = reinterpret_cast<const float4 *>(p_norm[l + 1]);
-#pragma unroll
-            for (int v = 0; v < kPredVec; v++) {
-                const int i4 = tid + v * DEC_THREADS;
-                if (i4 * 4 < D) {
-                    pr[v] = __ldcg(rw + i4);
-                    pn[v] = __ldcg(nw + i4);
-                }
-            }
-        }
+        // ---------------- P1: h, rmsnorm, x, router rows
         for (int i4 = tid; i4 * 4 < D; i4 += DEC_THREADS) {   // h, and its squares for lane (i & 15)'s chain
             const float4 v = l == 0 ? __ldcg(reinterpret_cast<const float4 *>(a.h) + i4) : poll4(xh(l) + 4 * i4, a.err);
             reinterpret_cast<float4 *>(hs)[i4] = v;
@@ -507,39 +439,14 @@ __device__ void decode_body(const DecodeArgs &a, uint8_t *smem) {
         HX_STAMP(ST_LOGIT);
         for (int b = warp; b < ly.nbD; b += DEC_WARPS) act_quant_warp(xs[b * QK + lane], xs[b * QK + lane + 32], xact + b, lane);
         HX_STAMP(ST_ACT);
-        if (predict && c < E) {   // partial of the predicted logit (every thread, any order)
-            float sum = 0.0f;
-#pragma unroll
-            for (int v = 0; v < kPredVec; v++) {
-                const int i4 = tid + v * DEC_THREADS;
-                if (i4 * 4 < D) {
-                    const float4 hh = reinterpret_cast<const float4 *>(hs)[i4];
-                    sum += pr[v].x * pn[v].x * hh.x + pr[v].y * pn[v].y * hh.y + pr[v].z * pn[v].z * hh.z +
-                           pr[v].w * pn[v].w * hh.w;
-                }
-            }
-#pragma unroll
-            for (int o = 16; o >= 1; o >>= 1) sum += __shfl_xor_sync(0xffffffffu, sum, o);
-            if (lane == 0) pred_part[warp] = sum;
-        }
-        HX_STAMP(ST_PRED);
-
-        // ---------------- P2: logits, routing, copies in flight
         poll_vec(xlg(l), lgs, E, a.err);
         __syncthreads();
         HX_STAMP(ST_LG);
-        if (predict && c < E && warp == 1) {
-            float v = lane < DEC_WARPS ? pred_part[lane] : 0.0f;
-#pragma unroll
-            for (int o = 16; o >= 1; o >>= 1) v += __shfl_xor_sync(0xffffffffu, v, o);
-            if (lane == 0) st_x(xpr(l) + c, canon(v * rms_r));
+        if (warp == 0) {
+            if (small_route) route_token_warp128<true>(a.route, lgs, p_bias[l], ids, wts, gscr);
+            else route_token_warp1<true>(a.route, lgs, p_bias[l], lgs, rkey, score, sel, gscr, gkeep, ids, wts);
+            HX_STAMP(ST_RT);
         }
-        if (small_route) {
-            route_token_cta_small<true>(a.route, lgs, p_bias[l], score, rkey, ids, wts);
-        } else if (warp == 0) {
-            route_token_warp1<true>(a.route, lgs, p_bias[l], lgs, rkey, score, sel, gscr, gkeep, ids, wts);
-        }
-        HX_STAMP(ST_RT);
         if (ep && tid == 0) {   // the ranks whose expert this GPU owns, in rank order
             int n = 0;
             for (int j = 0; j < K; j++)
@@ -569,7 +476,7 @@ __device__ void decode_body(const DecodeArgs &a, uint8_t *smem) {
         };
         if (warp == kIssueWarp) {   // a warp without a chunk (when nch_c < 16): the others start at once
             fence_proxy_async();
-            for (int q = lane; q < pl.ch_max; q += 32) {   // chunk q: rows 4p..4p+3 of gate and up, rank j
+            for (int q = lane; q < pl.ch_max; q += 32) {   // chunk q: rows ch*p.. of gate and up, rank j
                 if (q >= nch_c) {   // every chunk barrier completes one phase per layer
                     mbar_expect_tx(&bars[q], 0);
                     continue;
@@ -581,7 +488,7 @@ __device__ void decode_body(const DecodeArgs &a, uint8_t *smem) {
                     set_error(a.err, DEV_E_NOT_RESIDENT);
                     mbar_expect_tx(&bars[q], 0);
                 } else {
-                    const int64_t r0 = (int64_t)p * DEC_CH;
+                    const int64_t r0 = (int64_t)p * CH;
                     uint8_t *dst = gu + (size_t)q * 2 * chunk_bytes;
                     mbar_expect_tx(&bars[q], 2 * chunk_bytes);
                     bulk_g2s(dst, slab + r0 * ly.rbD, chunk_bytes, &bars[q]);
@@ -608,38 +515,24 @@ __device__ void decode_body(const DecodeArgs &a, uint8_t *smem) {
         }
         HX_STAMP(ST_ROUTE);
 
-        // ---------------- P3: gate/up chunks -> SwiGLU -> mid exchange; next-layer prefetch
+        // ---------------- P3: gate/up chunks -> SwiGLU -> mid exchange
         for (int q = warp; q < nch_c; q += DEC_WARPS) {
             int p;
             const int g = ch0 + q, j = chunk_rank(g, &p);
             if (mbar_wait(&bars[q], par, a.err)) {
                 if (q == 0) HX_STAMP(ST_CH0);
-                warp_rows_1tok<DT>(gu + (size_t)q * 2 * chunk_bytes, ly.rbD, ly.nbD, 2 * DEC_CH, xact, P, gout);
-                if (lane < DEC_CH)
-                    st_x(xmid(l, j) + p * DEC_CH + lane, canon(swiglu_c(gout[lane], gout[DEC_CH + lane])));
+                warp_rows_1tok<DT>(gu + (size_t)q * 2 * chunk_bytes, ly.rbD, ly.nbD, 2 * CH, xact, P, gout);
+                if (lane < CH) st_x(xmid(l, j) + p * CH + lane, canon(swiglu_c(gout[lane], gout[CH + lane])));
                 if (q == 0) HX_STAMP(ST_CHD);
-            }
-        }
-        if (predict && warp == kIssueWarp && nch_c <= kIssueWarp) {
-            for (int i = lane; i < E; i += 32) prs[i] = poll1(xpr(l) + i, a.err);
-            __syncwarp();
-            warp_topk_pred(prs, E, K, pred_ids);
-            const int per = (int)((a.slab_used + kPrefetchPiece - 1) / kPrefetchPiece);
-            for (int pi = c + lane * G; pi < K * per; pi += 32 * G) {
-                const int j = pi / per, k = pi - j * per;
-                const int e = pred_ids[j];
-                const uint8_t *sl = e >= 0 ? a.slab[(size_t)(l + 1) * E + e] : nullptr;
-                const int64_t off = (int64_t)k * kPrefetchPiece, left = a.slab_used - off;
-                if (sl) prefetch_l2(sl + off, left < (int64_t)kPrefetchPiece ? (uint32_t)left : kPrefetchPiece);
             }
         }
         {   // reset this CTA's share of the other set's slots of buffer layers [b0, b1) for the next launch
             // (while this CTA waits for the other CTAs' mid values anyway)
             const int np = (int)min(s_prev, (unsigned)a.Lb);
             const int b0 = (int)((int64_t)np * l / a.Lyr), b1 = (int)((int64_t)np * (l + 1) / a.Lyr);
-            const int64_t per_layer[5] = {E, E, (int64_t)K * F, (int64_t)K * D, D};
-            const int64_t base[5] = {o_lg, o_pr, o_mid, o_y, o_h};
-            for (int k = 0; k < 5; k++)
+            const int64_t per_layer[4] = {E, (int64_t)K * F, (int64_t)K * D, D};
+            const int64_t base[4] = {o_lg, o_mid, o_y, o_h};
+            for (int k = 0; k < 4; k++)
                 for (int b = b0; b < b1; b++) {
                     float *s0 = Xo + base[k] + (int64_t)b * per_layer[k];
                     for (int64_t i = (int64_t)c * DEC_THREADS + tid; i < per_layer[k]; i += (int64_t)G * DEC_THREADS)
@@ -800,15 +693,12 @@ cudaError_t launch_moe_decode(const DecodeParams &p, cudaStream_t s) {
     a.ids_out = p.ids_out;
     a.w_out = p.w_out;
     a.trace = p.trace;
-    a.slab_used = p.slab_used;
     a.ep_size = p.ep_size;
     a.ep_rank = p.ep_rank;
     a.ep_y = p.ep_y;
     if (a.ep_size > 1 && !a.ep_y) return cudaErrorInvalidValue;
     const int G = decode_grid();
     a.lay = decode_layout(G, p.D, p.F, p.E, p.K, p.dtype);
-    a.predict = p.prefetch && p.E <= G && p.E <= 128 && p.route.n_group <= 1 &&
-                p.D <= 4 * kPredVec * DEC_THREADS && a.lay.plan.ch_max < DEC_WARPS && p.slab_used % 16 == 0;
     cudaLaunchConfig_t cfg = {};
     cfg.gridDim = dim3((unsigned)G);
     cfg.blockDim = dim3(DEC_THREADS);

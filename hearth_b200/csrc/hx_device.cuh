@@ -204,7 +204,11 @@ __device__ __forceinline__ void warp_rows_1tok(const uint8_t *tile, int64_t rb, 
                 act_regs ar;
                 load_act(act + g0 + g, ar);
                 const uint8_t *col = tile + (int64_t)(g0 + g) * BS;
-                for (int k = r2; k < nr; k += rp) P[k * 33 + g] = term(col + (int64_t)k * rb, ar);
+#pragma unroll
+                for (int i = 0; i < ROWS_1TOK / 2; i++) {   // rp >= 2: rows r2, r2 + rp, ... (loads overlap)
+                    const int k = r2 + i * rp;
+                    if (k < nr) P[k * 33 + g] = term(col + (int64_t)k * rb, ar);
+                }
             }
         } else {
             for (int it = lane; it < nr * gn; it += 32) {

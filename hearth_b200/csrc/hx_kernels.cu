@@ -89,47 +89,51 @@ __global__ void __launch_bounds__(256) k_matmul_q(const uint8_t *__restrict__ W,
     }
 }
 
-// Quantized weights at few tokens (decode): the rows stream through shared memory in tiles of R
-// consecutive rows, one 1-D bulk copy per tile into a 3-stage ring (up to ~180 KB in flight per
-// SM, what the HBM stream needs); one CTA per SM walks tiles blockIdx.x + k * gridDim.x. Each warp
-// takes rows of the tile: lane g forms block g's term for every token, then lane t adds token t's
-// terms in block order (the chain of NUMERICS §3). Rows must be a multiple of 16 bytes and the
-// matrix 16-byte aligned (every Q4/Q8 matrix with n_cols a multiple of 512, in cudaMalloc memory).
-constexpr int GV_NST = 3;
+// Quantized weights at few tokens (decode): every warp streams its own units of U consecutive rows
+// (one 1-D bulk copy each) through two shared-memory slots of its own, so all warps of every SM keep
+// copies in flight whatever the row width (16 slots of up to ~12 KB per SM, what the HBM stream
+// needs) and no warp waits for another. Warp w of CTA b takes units w + 8b, then every 8*gridDim
+// further. A unit runs through the single-token row loop (lane = block, the activation block in
+// registers across the unit's rows, lanes 0..U-1 the rows' chains in block order: NUMERICS §3) once
+// per token. Rows must be a multiple of 16 bytes and the matrix 16-byte aligned (every Q4/Q8 matrix
+// with n_cols a multiple of 512, in cudaMalloc memory).
+constexpr int GV_WARPS = 8;
+constexpr int GV_SLOTS = 2;
 constexpr int GV_TMAX = 4;
 
 template <int DT>
-__global__ void __launch_bounds__(256) k_gemv_staged(const uint8_t *__restrict__ W, int64_t rows, int nb, int64_t rb,
-                                                     int R, const act_q8 *__restrict__ act, int T,
-                                                     float *__restrict__ Y, int64_t ldy, float *resid, float rs,
-                                                     const float *__restrict__ nh, const float *__restrict__ nw,
-                                                     float eps) {
+__global__ void __launch_bounds__(GV_WARPS * 32) k_gemv_staged(const uint8_t *__restrict__ W, int64_t rows, int nb,
+                                                               int64_t rb, int U, const act_q8 *__restrict__ act,
+                                                               int T, float *__restrict__ Y, int64_t ldy, float *resid,
+                                                               float rs, const float *__restrict__ nh,
+                                                               const float *__restrict__ nw, float eps) {
     extern __shared__ __align__(128) uint8_t smem[];
-    uint64_t *bars = reinterpret_cast<uint64_t *>(smem);
-    uint8_t *ring = smem + 128;
-    const int64_t stage = (int64_t)R * rb;
-    act_q8 *acts = reinterpret_cast<act_q8 *>(ring + GV_NST * stage);
     const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
-    float *P = reinterpret_cast<float *>(acts + (int64_t)T * nb) + warp * (GV_TMAX * 33);
-    const int64_t ntiles = (rows + R - 1) / R;
-    const int64_t mine = (int64_t)blockIdx.x < ntiles ? (ntiles - 1 - blockIdx.x) / gridDim.x + 1 : 0;
-    if (tid == 0) {
-        for (int st = 0; st < GV_NST; st++) mbar_init(&bars[st], 1);
-        fence_mbar_init();
-    }
-    __syncthreads();
+    uint64_t *bars = reinterpret_cast<uint64_t *>(smem) + warp * GV_SLOTS;
+    const int64_t slot = (int64_t)U * rb + 16;   // the padded block loads read up to 2 bytes past a row
+    uint8_t *slots = smem + 128 + (size_t)warp * GV_SLOTS * slot;
+    act_q8 *acts = reinterpret_cast<act_q8 *>(smem + 128 + (size_t)GV_WARPS * GV_SLOTS * slot);
+    float *fbase = reinterpret_cast<float *>(acts + (int64_t)T * nb);
+    float *P = fbase + warp * ROWS_1TOK * 33;
+    float *outs = fbase + GV_WARPS * ROWS_1TOK * 33 + warp * GV_TMAX * ROWS_1TOK;
+    float *xs = fbase + GV_WARPS * ROWS_1TOK * 33 + GV_WARPS * GV_TMAX * ROWS_1TOK;   // nh: x = rmsnorm(nh)
+    const int64_t units = (rows + U - 1) / U;
+    const int64_t gw = (int64_t)blockIdx.x * GV_WARPS + warp, nwarps = (int64_t)gridDim.x * GV_WARPS;
+    const int64_t mine = gw < units ? (units - 1 - gw) / nwarps + 1 : 0;
     auto issue = [&](int64_t k) {
-        const int64_t r0 = ((int64_t)blockIdx.x + k * gridDim.x) * R;
-        const int64_t nr = min((int64_t)R, rows - r0);
-        const int st = (int)(k % GV_NST);
+        const int64_t r0 = (gw + k * nwarps) * U;
+        const int64_t nr = min((int64_t)U, rows - r0);
+        const int st = (int)(k % GV_SLOTS);
         mbar_expect_tx(&bars[st], (uint32_t)(nr * rb));
-        bulk_g2s(ring + st * stage, W + r0 * rb, (uint32_t)(nr * rb), &bars[st]);
+        bulk_g2s(slots + st * slot, W + r0 * rb, (uint32_t)(nr * rb), &bars[st]);
     };
-    if (tid == 0)
-        for (int64_t k = 0; k < min((int64_t)GV_NST, mine); k++) issue(k);
+    if (lane == 0) {
+        for (int st = 0; st < GV_SLOTS; st++) mbar_init(&bars[st], 1);
+        fence_mbar_init();
+        for (int64_t k = 0; k < min((int64_t)GV_SLOTS, mine); k++) issue(k);
+    }
     if (nh) {   // one token: x = rmsnorm(nh, nw) (NUMERICS §4) and its activation blocks, formed here
         __shared__ float rsh;
-        float *xs = reinterpret_cast<float *>(acts + (int64_t)T * nb) + 8 * GV_TMAX * 33;
         const int n = nb * QK;
         for (int i = tid; i < n; i += blockDim.x) xs[i] = nh[i];
         __syncthreads();
@@ -143,67 +147,47 @@ __global__ void __launch_bounds__(256) k_gemv_staged(const uint8_t *__restrict__
         const float r = rsh;
         for (int i = tid; i < n; i += blockDim.x) xs[i] = __fmul_rn(__fmul_rn(xs[i], r), nw[i]);
         __syncthreads();
-        for (int b = warp; b < nb; b += 8) act_quant_warp(xs[b * QK + lane], xs[b * QK + lane + 32], acts + b, lane);
+        for (int b = warp; b < nb; b += GV_WARPS) act_quant_warp(xs[b * QK + lane], xs[b * QK + lane + 32], acts + b, lane);
     } else {
         const uint32_t *src = reinterpret_cast<const uint32_t *>(act);
         uint32_t *dst = reinterpret_cast<uint32_t *>(acts);
         for (int64_t i = tid; i < (int64_t)T * nb * (ACT_BLOCK / 4); i += blockDim.x) dst[i] = src[i];
     }
     __syncthreads();
-    constexpr int BS = DT == Q4 ? Q4_BLOCK : Q8_BLOCK;
     for (int64_t k = 0; k < mine; k++) {
-        const int st = (int)(k % GV_NST);
-        const bool ok = mbar_wait(&bars[st], (uint32_t)((k / GV_NST) & 1), nullptr);
-        const int64_t r0 = ((int64_t)blockIdx.x + k * gridDim.x) * R;
-        const int nr = (int)min((int64_t)R, rows - r0);
-        const uint8_t *tile = ring + st * stage;
-        for (int rr = warp; ok && rr < nr; rr += 8) {
-            const uint8_t *row = tile + (int64_t)rr * rb;
-            float acc = 0.0f;
-            for (int g0 = 0; g0 < nb; g0 += 32) {
-                const int gn = min(32, nb - g0);
-                if (lane < gn) {
-                    const int g = g0 + lane;
-                    uint32_t wq[16];
-                    float dw;
-                    if constexpr (DT == Q4) dw = f16_to_f32(load_q4_block(row + (int64_t)g * BS, wq));
-                    else dw = f16_to_f32(load_q8_block(row + (int64_t)g * BS, wq));
-                    for (int i = 0; i < T; i++) {
-                        act_regs ar;
-                        load_act(acts + i * nb + g, ar);
-                        int isum;
-                        if constexpr (DT == Q4) isum = q4_isum(wq, ar.q, ar.sum);
-                        else isum = q8_isum(wq, ar.q);
-                        P[i * 33 + lane] = __fmul_rn(__int2float_rn(isum), __fmul_rn(dw, ar.d));
-                    }
-                }
-                __syncwarp();
-                if (lane < T)
-                    for (int g = 0; g < gn; g++) acc = __fadd_rn(acc, P[lane * 33 + g]);
-                __syncwarp();
-            }
-            if (lane < T) mm_store(Y, resid, rs, (int64_t)lane * ldy + r0 + rr, canon(acc));
-        }
-        __syncthreads();   // every warp is done with this stage
-        if (tid == 0 && k + GV_NST < mine) {
+        const int st = (int)(k % GV_SLOTS);
+        if (!mbar_wait(&bars[st], (uint32_t)((k / GV_SLOTS) & 1), nullptr)) break;
+        const int64_t r0 = (gw + k * nwarps) * U;
+        const int nr = (int)min((int64_t)U, rows - r0);
+        const uint8_t *tile = slots + st * slot;
+        for (int i = 0; i < T; i++)   // the unit stays in shared memory for every token
+            warp_rows_1tok<DT>(tile, rb, nb, nr, acts + (int64_t)i * nb, P, outs + i * ROWS_1TOK);
+        if (lane < nr)
+            for (int i = 0; i < T; i++) mm_store(Y, resid, rs, (int64_t)i * ldy + r0 + lane, outs[i * ROWS_1TOK + lane]);
+        __syncwarp();
+        if (lane == 0 && k + GV_SLOTS < mine) {
             fence_proxy_async();
-            issue(k + GV_NST);
+            issue(k + GV_SLOTS);
         }
     }
 }
 
-// The staged kernel's shape for a launch, or R = 0 when it does not apply.
-static int gemv_rows_per_stage(int dtype, const void *W, int64_t n_cols, int64_t rows, int T, size_t *smem) {
+// The staged kernel's rows per unit and shared memory for a launch (norm: the rmsnorm prologue's x),
+// or 0 when it does not apply.
+static int gemv_rows_per_stage(int dtype, const void *W, int64_t n_cols, int64_t rows, int T, bool norm,
+                               size_t *smem) {
     if (!is_quant(dtype) || T > GV_TMAX || rows < 1 || (reinterpret_cast<uintptr_t>(W) & 15)) return 0;
     const int64_t rb = row_bytes(dtype, n_cols);
     const int64_t nb = n_cols / QK;
-    if (rb % 16 || rb > 16384) return 0;
-    int R = (int)std::min<int64_t>(64, 56 * 1024 / rb);
-    R = R / 8 * 8;
-    if (R < 8) return 0;
-    *smem = 128 + (size_t)GV_NST * R * rb + (size_t)T * nb * ACT_BLOCK + 8 * GV_TMAX * 33 * sizeof(float);
-    if (*smem > 220 * 1024) return 0;
-    return R;
+    if (rb % 16) return 0;
+    const size_t fixed = 128 + (size_t)T * nb * ACT_BLOCK +
+                         sizeof(float) * ((size_t)GV_WARPS * ROWS_1TOK * 33 + (size_t)GV_WARPS * GV_TMAX * ROWS_1TOK) +
+                         (norm ? sizeof(float) * (size_t)n_cols : 0);
+    if (fixed + (size_t)GV_WARPS * GV_SLOTS * (rb + 16) > 220 * 1024) return 0;
+    const size_t per_slot = (220 * 1024 - fixed) / ((size_t)GV_WARPS * GV_SLOTS) - 16;
+    const int U = (int)std::min<int64_t>(ROWS_1TOK, (int64_t)(per_slot / (size_t)rb));
+    *smem = fixed + (size_t)GV_WARPS * GV_SLOTS * ((size_t)U * rb + 16);
+    return U;
 }
 
 // Float weights: NUMERICS §1 dot16, one 16-lane group per (row, token).
@@ -238,6 +222,7 @@ __global__ void __launch_bounds__(256) k_matmul_f(const uint8_t *__restrict__ W,
 }
 
 // The staged GEMV's shared-memory attribute on the current device (once per device) and its SM count.
+// Grid: enough CTAs for every unit's warp, at most one per SM.
 static cudaError_t gemv_prepare(int dtype, int *sms) {
     int dev = 0;
     cudaGetDevice(&dev);
@@ -258,22 +243,21 @@ static cudaError_t gemv_prepare(int dtype, int *sms) {
 cudaError_t launch_gemv_norm(int dtype, const void *W, int64_t n_cols, int64_t rows, const float *h, const float *nw,
                              float eps, float *Y, float *resid, float rs, cudaStream_t s) {
     size_t smem = 0;
-    const int R = gemv_rows_per_stage(dtype, W, n_cols, rows, 1, &smem);
-    smem += sizeof(float) * (size_t)n_cols;
-    if (R <= 0 || smem > 220 * 1024) return cudaErrorNotSupported;
+    const int U = gemv_rows_per_stage(dtype, W, n_cols, rows, 1, true, &smem);
+    if (U <= 0) return cudaErrorNotSupported;
     int sms = 148;
     cudaError_t e = gemv_prepare(dtype, &sms);
     if (e != cudaSuccess) return e;
     const int64_t rb = row_bytes(dtype, n_cols);
-    const unsigned grid = (unsigned)std::min<int64_t>((rows + R - 1) / R, sms);
+    const unsigned grid = (unsigned)std::min<int64_t>(((rows + U - 1) / U + GV_WARPS - 1) / GV_WARPS, sms);
     const int nb = (int)(n_cols / QK);
     const uint8_t *w = static_cast<const uint8_t *>(W);
     if (dtype == Q4)
-        k_gemv_staged<Q4><<<grid, 256, smem, s>>>(w, rows, nb, rb, R, nullptr, 1, resid ? nullptr : Y, 0, resid, rs, h,
-                                                  nw, eps);
+        k_gemv_staged<Q4><<<grid, GV_WARPS * 32, smem, s>>>(w, rows, nb, rb, U, nullptr, 1, resid ? nullptr : Y, 0,
+                                                            resid, rs, h, nw, eps);
     else
-        k_gemv_staged<Q8><<<grid, 256, smem, s>>>(w, rows, nb, rb, R, nullptr, 1, resid ? nullptr : Y, 0, resid, rs, h,
-                                                  nw, eps);
+        k_gemv_staged<Q8><<<grid, GV_WARPS * 32, smem, s>>>(w, rows, nb, rb, U, nullptr, 1, resid ? nullptr : Y, 0,
+                                                            resid, rs, h, nw, eps);
     return cudaGetLastError();
 }
 
@@ -289,22 +273,21 @@ cudaError_t launch_matmul_resid(int dtype, const void *W, int64_t n_cols, const 
     const int64_t rb = row_bytes(dtype, n_cols);
     const uint8_t *w = static_cast<const uint8_t *>(W);
     size_t smem = 0;
-    const int R = gemv_rows_per_stage(dtype, w + r0 * rb, n_cols, rows, T, &smem);
-    if (R > 0) {   // few tokens: the rows stream through shared memory at the HBM rate
+    const int U = gemv_rows_per_stage(dtype, w + r0 * rb, n_cols, rows, T, false, &smem);
+    if (U > 0) {   // few tokens: the rows stream through shared memory at the HBM rate
         int sms = 148;
         cudaError_t e = gemv_prepare(dtype, &sms);
         if (e != cudaSuccess) return e;
-        const int64_t ntiles = (rows + R - 1) / R;
-        const unsigned grid = (unsigned)std::min<int64_t>(ntiles, sms);
+        const unsigned grid = (unsigned)std::min<int64_t>(((rows + U - 1) / U + GV_WARPS - 1) / GV_WARPS, sms);
         const int nb = (int)(n_cols / QK);
         float *Yr = resid ? nullptr : Y + r0;
         float *hr = resid ? resid + r0 : nullptr;
         if (dtype == Q4)
-            k_gemv_staged<Q4><<<grid, 256, smem, s>>>(w + r0 * rb, rows, nb, rb, R, (const act_q8 *)act, T, Yr, ldy,
-                                                      hr, rs, nullptr, nullptr, 0.0f);
+            k_gemv_staged<Q4><<<grid, GV_WARPS * 32, smem, s>>>(w + r0 * rb, rows, nb, rb, U, (const act_q8 *)act, T,
+                                                                Yr, ldy, hr, rs, nullptr, nullptr, 0.0f);
         else
-            k_gemv_staged<Q8><<<grid, 256, smem, s>>>(w + r0 * rb, rows, nb, rb, R, (const act_q8 *)act, T, Yr, ldy,
-                                                      hr, rs, nullptr, nullptr, 0.0f);
+            k_gemv_staged<Q8><<<grid, GV_WARPS * 32, smem, s>>>(w + r0 * rb, rows, nb, rb, U, (const act_q8 *)act, T,
+                                                                Yr, ldy, hr, rs, nullptr, nullptr, 0.0f);
         return cudaGetLastError();
     }
     if (is_quant(dtype)) {
@@ -397,6 +380,19 @@ static size_t smem_limit() {
         lim = (size_t)v;
     }
     return lim;
+}
+
+// Routing of token t by one warp: the register-resident warp routing when E <= 128 without expert
+// groups or forced ids, else the general warp routing (groups, E > 128, route replay).
+// score / sel: 2 * E floats of this warp's shared scratch.
+__device__ __forceinline__ void route_one(const MoeShape &sh, const MoeScratch &sc, int t, const float *bias,
+                                          float *score, float *sel) {
+    const int E = sh.route.E, K = sh.route.K;
+    if (!sc.forced_ids && E <= 128 && sh.route.n_group <= 1 && K <= 16)
+        route_token_warp128(sh.route, sc.logits + (int64_t)t * E, bias, sc.ids + t * K, sc.wts + t * K, score);
+    else
+        route_token_warp(sh.route, sc.logits + (int64_t)t * E, bias, score, sel, sc.ids + t * K, sc.wts + t * K,
+                         sc.forced_ids ? sc.forced_ids + t * K : nullptr);
 }
 
 // Router logits (F32 dot16 rows, canonical NaN) and the shared-expert gate logit, one 16-lane
@@ -492,8 +488,7 @@ __global__ void __launch_bounds__(256) k_moe_router(MoeShape sh, const float *__
     const int warp = threadIdx.x >> 5, nwarps = blockDim.x >> 5;
     float *score = rsm + warp * 2 * E, *sel = score + E;
     for (int tt = warp; tt < T; tt += nwarps)
-        route_token_warp(sh.route, sc.logits + (int64_t)tt * E, bias, score, sel, sc.ids + tt * sh.route.K,
-                         sc.wts + tt * sh.route.K, sc.forced_ids ? sc.forced_ids + tt * sh.route.K : nullptr);
+        route_one(sh, sc, tt, bias, score, sel);
     __syncthreads();
     __threadfence_block();
     int *cnt = reinterpret_cast<int *>(rsm), *start = cnt + E;
@@ -564,8 +559,7 @@ __global__ void __launch_bounds__(256) k_route_select(MoeShape sh, const float *
     const int t = blockIdx.x * 8 + warp;
     if (t >= sh.T) return;
     float *score = rsm + warp * 2 * E, *sel = score + E;
-    route_token_warp(sh.route, sc.logits + (int64_t)t * E, bias, score, sel, sc.ids + t * sh.route.K,
-                     sc.wts + t * sh.route.K, sc.forced_ids ? sc.forced_ids + t * sh.route.K : nullptr);
+    route_one(sh, sc, t, bias, score, sel);
 }
 
 __global__ void __launch_bounds__(512) k_route_union(MoeShape sh, MoeScratch sc) {

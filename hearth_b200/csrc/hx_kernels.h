@@ -180,8 +180,6 @@ struct DecodeParams {
     int *ids_out;
     float *w_out;
     unsigned long long *trace;    // null, or [n_layers][grid][decode_stamps()] phase timestamps
-    bool prefetch;                // predict the next layer's experts and prefetch them into L2
-    int64_t slab_used;            // bytes of a slab the kernels read (gate, up, down)
     int ep_size = 1, ep_rank = 0; // expert parallelism: this GPU computes the experts e % ep_size == ep_rank
     uint64_t *const *ep_y = nullptr;   // [ep_size] device pointers: every GPU's y words [buf_layers][K][D]
 };

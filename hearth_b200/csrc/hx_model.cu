@@ -95,7 +95,9 @@ struct hxb_model {
     // shape (engine/src/model.c:1394-1439 setup_dims, GQA)
     int L = 0, D = 0, V = 0, H = 0, Hkv = 0, hd = 0, q_dim = 0, kv_dim = 0, rope_dim = 0, rope_half = 0;
     int rope_style = 0, qk_norm = 0, qkv_bias = 0, Fd = 0, n_moe = 0, K = 0, E = 0, max_in = 0, dc = 64, vthreads = 0;
-    size_t vsmem = 0;
+    size_t vsmem = 0, vsmem1 = 0;   // value kernel: batches, one decode token
+    int vnst1 = 0;                  // one decode token: ring stages, softmax fused
+    bool vfuse1 = false;
     float eps = 1e-6f, rs = 1.0f, es = 1.0f, ls = 1.0f, attn_scale = 1.0f, rope_factor = 1.0f;
     int max_batch = 0, max_seq = 0, kv_seq = 0;   // kv_seq: max_seq rounded up to 32, the cache's stride
     std::vector<float> inv_freq;
@@ -276,6 +278,23 @@ __global__ void __launch_bounds__(256) k_attn_post(PostArgs a) {
     }
 }
 
+// Lane j's chain of a 16-lane dot16 (NUMERICS §1) of a K row with q: k[j] q[j] + k[j+16] q[j+16] + ...
+// in order. Rows up to 256 floats load all their values before the chain, so the loads overlap.
+__device__ __forceinline__ float qk_chain(const float *kr, const float *q, int n, int j) {
+    float L = 0.0f;
+    if (n <= 256) {
+        float kv[16];
+#pragma unroll
+        for (int u = 0; u < 16; u++) kv[u] = j + 16 * u < n ? kr[j + 16 * u] : 0.0f;
+#pragma unroll
+        for (int u = 0; u < 16; u++)
+            if (j + 16 * u < n) L = __fadd_rn(L, __fmul_rn(kv[u], q[j + 16 * u]));
+    } else {
+        for (int i = j; i < n; i += 16) L = __fadd_rn(L, __fmul_rn(kr[i], q[i]));
+    }
+    return L;
+}
+
 // Scores S[t][h][r] = attn_scale * dot16(q_h, k_r) for r <= pos (gqa_scores through the F32
 // matmul kernel, then gqa_softmax's scaling; model.c:519-550). One 16-lane group per (h, r); the
 // CTAs of a (token, head) stride over the positions.
@@ -291,8 +310,7 @@ __global__ void __launch_bounds__(256) k_attn_scores(const float *__restrict__ q
         const bool valid = r <= pos;
         float L = 0.0f;
         if (valid) {
-            const float *kr = kc + ((int64_t)g * max_seq + r) * hd;
-            for (int i = j; i < hd; i += 16) L = __fadd_rn(L, __fmul_rn(kr[i], qh[i]));
+            L = qk_chain(kc + ((int64_t)g * max_seq + r) * hd, qh, hd, j);
         }
         L = tree16(L, 0xffffffffu);
         if (valid && j == 0) {
@@ -337,8 +355,7 @@ __global__ void __launch_bounds__(256) k_attn_scores1(PostArgs a, float *__restr
         const bool valid = r <= pos;
         float L = 0.0f;
         if (valid) {
-            const float *kr = r == pos ? kp : a.kc + ((int64_t)g * a.max_seq + r) * a.hd;
-            for (int i = j; i < a.hd; i += 16) L = __fadd_rn(L, __fmul_rn(kr[i], qh[i]));
+            L = qk_chain(r == pos ? kp : a.kc + ((int64_t)g * a.max_seq + r) * a.hd, qh, a.hd, j);
         }
         L = tree16(L, 0xffffffffu);
         if (valid && j == 0) {
@@ -389,69 +406,108 @@ __global__ void __launch_bounds__(256) k_attn_softmax(float *__restrict__ S, int
 }
 
 // o_h[d] = sum_r p_h[r] * v_r[d] in position order from 0.0f (value_sum, model.c:552-590), one CTA
-// per (token, kv group, DC dims): thread (hh, d) runs the chain of head g*grp + hh, dim d. Tiles of VT
-// positions stream into a ring of shared-memory stages by 1-D bulk copies (the V rows of the tile,
-// contiguous in the cache, and the group's VT probabilities per head), so each V row is read once
-// for the group's heads while the chains run on the previous tiles. With DC = 64 the CTA also forms
-// the o projection's activation blocks of its heads (act not null). max_seq is a multiple of VT.
-constexpr int VT = 32, V_NST = 4;
+// per (token, kv group g, hpc of the group's heads, DC dims): thread (hh, d) runs the chain of head
+// g*grp + hs*hpc + hh, dim dc*DC + d. Tiles of VT positions stream into a ring of nst shared-memory
+// stages by 1-D bulk copies (the V rows of the tile, contiguous in the cache, and the VT
+// probabilities of each of the CTA's heads), so each V row a CTA loads serves all its heads while the
+// chains run on the previous tiles. Batches take the whole group per CTA (hpc = grp, each V row read
+// once per group); a decode token takes one head per CTA (hpc = 1, DC = hd) and a deeper ring, so the
+// group's heads run on separate SMs; it also forms its head's probabilities itself (fuse_sm, the
+// softmax kernel's steps on the score row in shared memory) while the first V tiles stream in. With DC
+// a multiple of 64 the CTA also forms the o projection's activation blocks of its dims (act not
+// null). max_seq is a multiple of VT.
+constexpr int VT = 32, V_NST = 4, V_NST1 = 10;
 __global__ void __launch_bounds__(1024) k_attn_values(const float *__restrict__ S, const float *__restrict__ vc,
                                                       float *__restrict__ att, act_q8 *__restrict__ act, int H,
-                                                      int Hkv, int hd, int DC, int max_seq,
-                                                      const int *__restrict__ dpos) {
+                                                      int Hkv, int hd, int DC, int hpc, int nst, int max_seq,
+                                                      const int *__restrict__ dpos, int fuse_sm) {
     extern __shared__ __align__(128) uint8_t smv[];
-    const int grp = H / Hkv, nd = hd / DC;
-    const int t = blockIdx.y, g = blockIdx.x / nd, dc = blockIdx.x - g * nd;
+    const int grp = H / Hkv, nd = hd / DC, nh = grp / hpc;
+    const int t = blockIdx.y, g = blockIdx.x / (nh * nd), rem = blockIdx.x - g * nh * nd;
+    const int hs = rem / nd, dc = rem - hs * nd;
+    const int h0 = g * grp + hs * hpc;   // the CTA's first head
     const int tid = threadIdx.x;
     const int hh = tid / DC, d = tid - hh * DC;
-    const bool chain = tid < grp * DC;
+    const bool chain = tid < hpc * DC;
     const int n = *dpos + t + 1;
     uint64_t *bars = reinterpret_cast<uint64_t *>(smv);
-    float *vbuf = reinterpret_cast<float *>(smv + 128);          // [V_NST][VT][hd]
-    float *pbuf = vbuf + V_NST * VT * hd;                         // [V_NST][grp][VT]
-    float *ost = pbuf + V_NST * grp * VT;                         // [grp][DC]
+    float *vbuf = reinterpret_cast<float *>(smv + 128);          // [nst][VT][hd]
+    float *pbuf = vbuf + (size_t)nst * VT * hd;                  // [nst][hpc][VT]
+    float *ost = pbuf + (size_t)nst * hpc * VT;                  // [hpc][DC]
+    float *prow = ost + (size_t)hpc * DC;                        // fuse_sm: the head's probabilities [max_seq]
     const float *vg = vc + (int64_t)g * max_seq * hd;
-    const float *pg = S + ((int64_t)t * H + g * grp) * max_seq;
+    const float *pg = S + ((int64_t)t * H + h0) * max_seq;
     const int ntile = (n + VT - 1) / VT;
     if (tid == 0) {
-        for (int st = 0; st < V_NST; st++) mbar_init(&bars[st], 1);
+        for (int st = 0; st < nst; st++) mbar_init(&bars[st], 1);
         fence_mbar_init();
     }
     __syncthreads();
     auto issue = [&](int it) {
-        const int st = it % V_NST, r0 = it * VT;
-        mbar_expect_tx(&bars[st], (uint32_t)(VT * hd * 4 + grp * VT * 4));
-        bulk_g2s(vbuf + st * VT * hd, vg + (int64_t)r0 * hd, (uint32_t)(VT * hd * 4), &bars[st]);
-        for (int j = 0; j < grp; j++)
-            bulk_g2s(pbuf + (st * grp + j) * VT, pg + (int64_t)j * max_seq + r0, (uint32_t)(VT * 4), &bars[st]);
+        const int st = it % nst, r0 = it * VT;
+        mbar_expect_tx(&bars[st], (uint32_t)(VT * hd * 4 + (fuse_sm ? 0 : hpc * VT * 4)));
+        bulk_g2s(vbuf + (size_t)st * VT * hd, vg + (int64_t)r0 * hd, (uint32_t)(VT * hd * 4), &bars[st]);
+        for (int j = 0; j < hpc && !fuse_sm; j++)
+            bulk_g2s(pbuf + ((size_t)st * hpc + j) * VT, pg + (int64_t)j * max_seq + r0, (uint32_t)(VT * 4), &bars[st]);
     };
     if (tid == 0)
-        for (int it = 0; it < min(V_NST, ntile); it++) issue(it);
+        for (int it = 0; it < min(nst, ntile); it++) issue(it);
+    if (fuse_sm) {   // hpc == 1: k_attn_softmax's steps on the head's score row, in shared memory
+        __shared__ float red[32];
+        __shared__ float ssum;
+        const int lane = tid & 31, warp = tid >> 5, nw = (int)(blockDim.x >> 5);
+        float mx = -__uint_as_float(0x7f800000u);
+        for (int i = tid; i < n; i += blockDim.x) {
+            const float v = pg[i];
+            prow[i] = v;
+            mx = fmaxf(mx, v);
+        }
+        for (int o = 16; o >= 1; o >>= 1) mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, o));
+        if (lane == 0) red[warp] = mx;
+        __syncthreads();
+        mx = red[0];
+        for (int w = 1; w < nw; w++) mx = fmaxf(mx, red[w]);
+        if (prow[0] != prow[0]) mx = prow[0];
+        for (int i = tid; i < n; i += blockDim.x) prow[i] = host_expf(__fsub_rn(prow[i], mx));
+        __syncthreads();
+        if (tid < 16) {   // sum16 (NUMERICS §1)
+            float L = 0.0f;
+            for (int i = tid; i < n; i += 16) L = __fadd_rn(L, prow[i]);
+            L = tree16(L, 0xffffu);
+            if (tid == 0) ssum = L;
+        }
+        __syncthreads();
+        const float sum = ssum;
+        for (int i = tid; i < n; i += blockDim.x) prow[i] = __fdiv_rn(prow[i], sum);
+        __syncthreads();
+    }
     float acc = 0.0f;
     bool ok = true;
     for (int it = 0; it < ntile; it++) {
-        const int st = it % V_NST;
-        ok = ok && mbar_wait(&bars[st], (uint32_t)((it / V_NST) & 1), nullptr);
+        const int st = it % nst;
+        ok = ok && mbar_wait(&bars[st], (uint32_t)((it / nst) & 1), nullptr);
         if (ok && chain) {
-            const float *vb = vbuf + st * VT * hd + dc * DC + d;
-            const float *pb = pbuf + (st * grp + hh) * VT;
+            const float *vb = vbuf + (size_t)st * VT * hd + dc * DC + d;
+            const float *pb = fuse_sm ? prow + it * VT : pbuf + ((size_t)st * hpc + hh) * VT;
             const int m = min(VT, n - it * VT);
             for (int r = 0; r < m; r++) acc = __fadd_rn(acc, __fmul_rn(pb[r], vb[r * hd]));
         }
         __syncthreads();   // every chain is done with this stage
-        if (tid == 0 && it + V_NST < ntile) {
+        if (tid == 0 && it + nst < ntile) {
             fence_proxy_async();
-            issue(it + V_NST);
+            issue(it + nst);
         }
     }
-    if (chain) att[((int64_t)t * H + g * grp + hh) * hd + dc * DC + d] = acc;
-    if (act) {   // DC == 64: one activation block per head of this CTA
+    if (chain) att[((int64_t)t * H + h0 + hh) * hd + dc * DC + d] = acc;
+    if (act) {   // DC a multiple of 64: the activation blocks of the CTA's (head, 64 dims)
         if (chain) ost[tid] = acc;
         __syncthreads();
-        const int warp = tid >> 5, lane = tid & 31, nb = H * hd / QK;
-        for (int w = warp; w < grp; w += (int)(blockDim.x >> 5))
-            act_quant_warp(ost[w * DC + lane], ost[w * DC + lane + 32],
-                           act + (int64_t)t * nb + ((int64_t)(g * grp + w) * hd + dc * DC) / QK, lane);
+        const int warp = tid >> 5, lane = tid & 31, nb = H * hd / QK, bpc = DC / QK;
+        for (int w = warp; w < hpc * bpc; w += (int)(blockDim.x >> 5)) {
+            const int wh = w / bpc, sb = w - wh * bpc;
+            act_quant_warp(ost[wh * DC + sb * QK + lane], ost[wh * DC + sb * QK + lane + 32],
+                           act + (int64_t)t * nb + ((int64_t)(h0 + wh) * hd + dc * DC + sb * QK) / QK, lane);
+        }
     }
 }
 
@@ -613,6 +669,7 @@ static bool fuse_qkv(DLayer &w) {
 // The KV cache, the scratch of a forward of max_batch tokens and the attention kernels' shared
 // memory; null, or why not.
 static const char *alloc_runtime(hxb_model *m) {
+    m->kv_seq = (m->max_seq + 31) / 32 * 32;
     // dynamic shared memory of the attention kernels: q and k rows of a token, a head's scores
     const size_t post_smem = sizeof(float) * (size_t)(m->q_dim + m->kv_dim), sm_smem = sizeof(float) * (size_t)m->max_seq;
     const int grp = m->H / m->Hkv;
@@ -623,8 +680,18 @@ static const char *alloc_runtime(hxb_model *m) {
         return "model_open: attention heads per kv group times head_dim beyond the value kernel's CTA";
     int smem_max = 0;
     cudaDeviceGetAttribute(&smem_max, cudaDevAttrMaxSharedMemoryPerBlockOptin, m->device);
+    // one decode token: as many ring stages as fit beside the score row (the fused softmax), else the
+    // batch kernel's ring and the separate softmax
+    {
+        const size_t fixed = 128 + 1024 + sizeof(float) * (size_t)(m->hd + m->kv_seq), stage = sizeof(float) * (VT * m->hd + VT);
+        const size_t room = (size_t)smem_max > fixed ? (size_t)smem_max - fixed : 0;
+        m->vnst1 = (int)std::min<size_t>(V_NST1, room / stage);
+        m->vfuse1 = m->vnst1 >= 2 && m->hd <= 1024;
+        if (!m->vfuse1) m->vnst1 = V_NST;
+        m->vsmem1 = 128 + sizeof(float) * (size_t)(m->vnst1 * (VT * m->hd + VT) + m->hd + (m->vfuse1 ? m->kv_seq : 0));
+    }
     if (post_smem + 1024 > (size_t)smem_max || sizeof(float) * 8 * (size_t)m->hd + 1024 > (size_t)smem_max ||
-        sm_smem + 1024 > (size_t)smem_max || m->vsmem + 1024 > (size_t)smem_max ||
+        sm_smem + 1024 > (size_t)smem_max || m->vsmem + 1024 > (size_t)smem_max || m->vsmem1 + 1024 > (size_t)smem_max ||
         sizeof(float) * (size_t)m->D > 48 * 1024)
         return "model_open: max_seq or the attention width exceeds shared memory";
     // the attribute is the device's limit, not this model's need: it is per function, shared by every
@@ -641,7 +708,6 @@ static const char *alloc_runtime(hxb_model *m) {
                              smem_max - (int)fs.sharedSizeBytes) != cudaSuccess)
         return "model_open: shared memory attributes refused";
     // KV cache and scratch
-    m->kv_seq = (m->max_seq + 31) / 32 * 32;
     const size_t T = (size_t)m->max_batch, S = (size_t)m->kv_seq;
     const size_t kvb = sizeof(float) * (size_t)m->L * m->Hkv * S * m->hd;
     const size_t actb = T * ((size_t)m->max_in / QK + 1) * sizeof(act_q8);
@@ -963,8 +1029,8 @@ static int attention(hxb_model *m, int l, int T, cudaStream_t s) {
     a.rope_style = m->rope_style;
     a.max_seq = m->kv_seq;
     a.eps = m->eps;
-    // the score CTAs of a (token, head) stride over the positions: about 600 CTAs in all
-    const int chunks = std::max(1, std::min((int)blocks(m->max_seq, 16), 600 / (m->H * T)));
+    // the score CTAs of a (token, head) stride over the positions: about 1200 CTAs in all (8 per SM)
+    const int chunks = std::max(1, std::min((int)blocks(m->max_seq, 16), 1200 / (m->H * T)));
     if (T == 1 && m->qk_norm != 2 && m->hd <= 1024) {   // one token: post-processing inside the score kernel
         k_attn_scores1<<<dim3(chunks, m->H, 1), 256, 0, s>>>(a, m->S.as<float>(), m->attn_scale);
     } else {
@@ -975,13 +1041,26 @@ static int attention(hxb_model *m, int l, int T, cudaStream_t s) {
         k_attn_scores<<<dim3(chunks, m->H, T), 256, 0, s>>>(a.qout, a.kc, m->S.as<float>(), m->H, m->Hkv, m->hd,
                                                              m->kv_seq, a.dpos, m->attn_scale);
     }
+    // one decode token: a CTA per head (the group's heads on separate SMs); batches: a CTA per (group,
+    // dc dims). The o projection's activation blocks come out of the value kernel when a CTA holds
+    // whole blocks.
+    if (T == 1) {
+        if (!m->vfuse1)
+            k_attn_softmax<<<dim3(m->H, T), 256, sizeof(float) * m->max_seq, s>>>(m->S.as<float>(), m->H, m->kv_seq, a.dpos);
+        const bool fuse_act = is_quant(w.o.dtype) && m->hd % QK == 0;
+        k_attn_values<<<dim3(m->H, 1), (m->hd + 31) / 32 * 32, m->vsmem1, s>>>(
+            m->S.as<float>(), a.vc, m->att.as<float>(), fuse_act ? act : nullptr, m->H, m->Hkv, m->hd, m->hd, 1,
+            m->vnst1, m->kv_seq, a.dpos, m->vfuse1 ? 1 : 0);
+        if (!mcuda(cudaGetLastError(), "attention")) return HXB_E_DEVICE;
+        bool aready = fuse_act;
+        return matmul(m, w.o, m->att.as<float>(), m->q_dim, act, aready, T, nullptr, m->D, s, m->h.as<float>(), m->rs);
+    }
     k_attn_softmax<<<dim3(m->H, T), 256, sizeof(float) * m->max_seq, s>>>(m->S.as<float>(), m->H, m->kv_seq, a.dpos);
-    // the o projection's activation blocks come out of the value kernel when a CTA holds whole blocks
     const bool fuse_act = is_quant(w.o.dtype) && m->dc == 64;
     const int grp = m->H / m->Hkv;
     k_attn_values<<<dim3(m->Hkv * (m->hd / m->dc), T), m->vthreads, m->vsmem, s>>>(
-        m->S.as<float>(), a.vc, m->att.as<float>(), fuse_act ? act : nullptr, m->H, m->Hkv, m->hd, m->dc, m->kv_seq,
-        a.dpos);
+        m->S.as<float>(), a.vc, m->att.as<float>(), fuse_act ? act : nullptr, m->H, m->Hkv, m->hd, m->dc, grp, V_NST,
+        m->kv_seq, a.dpos, 0);
     if (!mcuda(cudaGetLastError(), "attention")) return HXB_E_DEVICE;
     bool aready = fuse_act;
     // h += rs * (Wo att): the residual in the matmul's epilogue

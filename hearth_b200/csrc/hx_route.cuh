@@ -357,6 +357,111 @@ __device__ __forceinline__ void route_token_warp1(const RouteCfg &R, const float
     __syncwarp();
 }
 
+// Top-k routing of one token by ONE warp, for E <= 128 and K <= 16 without expert groups, with no
+// CTA barrier: lane l holds experts l, l + 32, l + 64, l + 96 in registers. Softmax: the maximum by
+// shuffles (a NaN x[0] is kept, as `m = x[0]; m = x[i] > m ? x[i] : m`), exp per expert, the sum16
+// in NUMERICS §1 order (lane j < 16 adds e[j + 16k], k = 0..7: its own values and lane j + 16's),
+// then one division per expert; sigmoid scores need none of it. Selection (route_select,
+// engine/src/model.c:793-831): each lane sorts its 4 rank_keys, then K rounds take the warp maximum of
+// the lanes' heads (the high words by one reduction, then the low words of the lanes that hold that
+// high word; a low word encodes the expert, so one lane wins) and the winner records pick r and pops
+// its head. Weights as route_weights (model.c:833-843). ids / w / vs (K floats of scratch) are shared
+// memory; the warp's lanes see ids and w after the call, the CTA after its next barrier.
+template <bool kSharedLogits = false>
+__device__ __forceinline__ void route_token_warp128(const RouteCfg &R, const float *logit, const float *bias, int *ids,
+                                                    float *w, float *vs) {
+    const int lane = threadIdx.x & 31;
+    const int E = R.E, K = R.K;
+    float x[4], sc[4];
+#pragma unroll
+    for (int t = 0; t < 4; t++) {
+        const int i = t * 32 + lane;
+        x[t] = i < E ? (kSharedLogits ? logit[i] : __ldcg(logit + i)) : 0.0f;
+    }
+    if (R.score_fn == SCORE_SOFTMAX) {
+        float m = -__uint_as_float(0x7f800000u);
+#pragma unroll
+        for (int t = 0; t < 4; t++)
+            if (t * 32 + lane < E) m = fmaxf(m, x[t]);
+#pragma unroll
+        for (int s = 16; s >= 1; s >>= 1) m = fmaxf(m, __shfl_xor_sync(0xffffffffu, m, s));
+        const float x0 = __shfl_sync(0xffffffffu, x[0], 0);
+        if (x0 != x0) m = x0;
+        float e[4], o[4];
+#pragma unroll
+        for (int t = 0; t < 4; t++) e[t] = t * 32 + lane < E ? host_expf(__fsub_rn(x[t], m)) : 0.0f;
+#pragma unroll
+        for (int t = 0; t < 4; t++) o[t] = __shfl_down_sync(0xffffffffu, e[t], 16);   // lane j + 16's
+        float L = 0.0f;
+        if (lane < 16) {
+#pragma unroll
+            for (int k = 0; k < 8; k++)   // expert lane + 16k: k even in this lane (slot k/2), odd in lane + 16
+                if (lane + 16 * k < E) L = __fadd_rn(L, (k & 1) ? o[k >> 1] : e[k >> 1]);
+        }
+        L = tree16(L, 0xffffffffu);
+        const float den = __shfl_sync(0xffffffffu, L, 0);
+#pragma unroll
+        for (int t = 0; t < 4; t++) sc[t] = __fdiv_rn(e[t], den);
+    } else {
+#pragma unroll
+        for (int t = 0; t < 4; t++) sc[t] = sigmoid_c(x[t]);
+    }
+    uint32_t kh[4], kl[4];   // rank_key halves; (0, 0) below every expert's key
+#pragma unroll
+    for (int t = 0; t < 4; t++) {
+        const int i = t * 32 + lane;
+        kh[t] = kl[t] = 0u;
+        if (i < E) {
+            const float sv = (R.score_bias && bias) ? __fadd_rn(sc[t], __ldg(bias + i)) : sc[t];
+            const unsigned long long k = rank_key(sv, i);
+            kh[t] = (uint32_t)(k >> 32);
+            kl[t] = (uint32_t)k;
+        }
+    }
+    auto cswap = [&](int a, int b) {   // slot a keeps the larger key
+        const bool sw = kh[b] > kh[a] || (kh[b] == kh[a] && kl[b] > kl[a]);
+        if (sw) {
+            const uint32_t th = kh[a], tl = kl[a];
+            const float ts = sc[a];
+            kh[a] = kh[b]; kl[a] = kl[b]; sc[a] = sc[b];
+            kh[b] = th; kl[b] = tl; sc[b] = ts;
+        }
+    };
+    cswap(0, 1);
+    cswap(2, 3);
+    cswap(0, 2);
+    cswap(1, 3);
+    cswap(1, 2);
+    for (int r = 0; r < K; r++) {
+        const uint32_t mh = __reduce_max_sync(0xffffffffu, kh[0]);
+        const bool cand = kh[0] == mh;
+        const uint32_t ml = __reduce_max_sync(0xffffffffu, cand ? kl[0] : 0u);
+        if (cand && kl[0] == ml) {   // the winner: pick r, then its next key moves up
+            ids[r] = (int)(0xffffffffu - ml);
+            vs[r] = sc[0];
+            kh[0] = kh[1]; kl[0] = kl[1]; sc[0] = sc[1];
+            kh[1] = kh[2]; kl[1] = kl[2]; sc[1] = sc[2];
+            kh[2] = kh[3]; kl[2] = kl[3]; sc[2] = sc[3];
+            kh[3] = kl[3] = 0u;
+        }
+    }
+    __syncwarp();
+    float sacc = 0.0f, wj = 0.0f;   // route_weights: every lane forms the rank-order sum itself
+#pragma unroll
+    for (int j = 0; j < 16; j++)
+        if (j < K) {
+            const float vj = vs[j];
+            sacc = __fadd_rn(sacc, vj);
+            if (j == lane) wj = vj;
+        }
+    const float den = __fadd_rn(sacc, 1e-20f);
+    if (lane < K) {
+        if (R.norm_topk_prob) wj = __fdiv_rn(wj, den);
+        w[lane] = __fmul_rn(wj, R.routed_scale);
+    }
+    __syncwarp();
+}
+
 // Profiling hook of route_token_cta_small: HX_ROUTE_STAMP(i) marks the end of step i (empty here;
 // a timing harness defines it before including this header).
 #ifndef HX_ROUTE_STAMP
