@@ -490,7 +490,15 @@ __global__ void __launch_bounds__(1024) k_attn_values(const float *__restrict__ 
             const float *vb = vbuf + (size_t)st * VT * hd + dc * DC + d;
             const float *pb = fuse_sm ? prow + it * VT : pbuf + ((size_t)st * hpc + hh) * VT;
             const int m = min(VT, n - it * VT);
-            for (int r = 0; r < m; r++) acc = __fadd_rn(acc, __fmul_rn(pb[r], vb[r * hd]));
+            if (m == VT) {   // a whole tile: the loads go ahead of the dependent adds
+                float pv[VT];
+#pragma unroll
+                for (int r = 0; r < VT; r++) pv[r] = __fmul_rn(pb[r], vb[r * hd]);
+#pragma unroll
+                for (int r = 0; r < VT; r++) acc = __fadd_rn(acc, pv[r]);
+            } else {
+                for (int r = 0; r < m; r++) acc = __fadd_rn(acc, __fmul_rn(pb[r], vb[r * hd]));
+            }
         }
         __syncthreads();   // every chain is done with this stage
         if (tid == 0 && it + nst < ntile) {
