@@ -33,6 +33,32 @@ __device__ __forceinline__ void fence_mbar_init() {
     asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
 }
 
+// Programmatic dependent launch: a kernel launched with programmatic stream serialization may start
+// while its predecessor in the stream still runs; pdl_wait() returns once the predecessor has
+// completed and its memory is visible (at once for a kernel launched without the attribute), and
+// pdl_trigger() lets the next such kernel start launching. Before pdl_wait() a kernel reads only data
+// written before the stream work it follows (weights, older KV rows).
+__device__ __forceinline__ void pdl_wait() { asm volatile("griddepcontrol.wait;" ::: "memory"); }
+__device__ __forceinline__ void pdl_trigger() { asm volatile("griddepcontrol.launch_dependents;" ::: "memory"); }
+
+// Launches kernel k, with programmatic stream serialization when pdl is set (the kernel must
+// pdl_wait() before it reads anything earlier stream work wrote).
+template <typename... KArgs, typename... Args>
+static cudaError_t launch_pdl(bool pdl, void (*k)(KArgs...), dim3 grid, dim3 block, size_t smem, cudaStream_t s,
+                              Args... args) {
+    cudaLaunchConfig_t cfg = {};
+    cfg.gridDim = grid;
+    cfg.blockDim = block;
+    cfg.dynamicSmemBytes = smem;
+    cfg.stream = s;
+    cudaLaunchAttribute at[1];
+    at[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+    at[0].val.programmaticStreamSerializationAllowed = 1;
+    cfg.attrs = at;
+    cfg.numAttrs = pdl ? 1 : 0;
+    return cudaLaunchKernelEx(&cfg, k, static_cast<KArgs>(args)...);
+}
+
 __device__ __forceinline__ void fence_proxy_async() {
     asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
 }

@@ -127,11 +127,13 @@ __global__ void __launch_bounds__(GV_WARPS * 32) k_gemv_staged(const uint8_t *__
         mbar_expect_tx(&bars[st], (uint32_t)(nr * rb));
         bulk_g2s(slots + st * slot, W + r0 * rb, (uint32_t)(nr * rb), &bars[st]);
     };
-    if (lane == 0) {
+    pdl_trigger();
+    if (lane == 0) {   // the weights stream in while the previous kernel may still run
         for (int st = 0; st < GV_SLOTS; st++) mbar_init(&bars[st], 1);
         fence_mbar_init();
         for (int64_t k = 0; k < min((int64_t)GV_SLOTS, mine); k++) issue(k);
     }
+    pdl_wait();   // the activations, nh and the residual are the previous kernels' outputs
     if (nh) {   // one token: x = rmsnorm(nh, nw) (NUMERICS §4) and its activation blocks, formed here
         __shared__ float rsh;
         const int n = nb * QK;
@@ -241,7 +243,7 @@ static cudaError_t gemv_prepare(int dtype, int *sms) {
 }
 
 cudaError_t launch_gemv_norm(int dtype, const void *W, int64_t n_cols, int64_t rows, const float *h, const float *nw,
-                             float eps, float *Y, float *resid, float rs, cudaStream_t s) {
+                             float eps, float *Y, float *resid, float rs, cudaStream_t s, bool early_weights) {
     size_t smem = 0;
     const int U = gemv_rows_per_stage(dtype, W, n_cols, rows, 1, true, &smem);
     if (U <= 0) return cudaErrorNotSupported;
@@ -253,12 +255,10 @@ cudaError_t launch_gemv_norm(int dtype, const void *W, int64_t n_cols, int64_t r
     const int nb = (int)(n_cols / QK);
     const uint8_t *w = static_cast<const uint8_t *>(W);
     if (dtype == Q4)
-        k_gemv_staged<Q4><<<grid, GV_WARPS * 32, smem, s>>>(w, rows, nb, rb, U, nullptr, 1, resid ? nullptr : Y, 0,
-                                                            resid, rs, h, nw, eps);
-    else
-        k_gemv_staged<Q8><<<grid, GV_WARPS * 32, smem, s>>>(w, rows, nb, rb, U, nullptr, 1, resid ? nullptr : Y, 0,
-                                                            resid, rs, h, nw, eps);
-    return cudaGetLastError();
+        return launch_pdl(early_weights, k_gemv_staged<Q4>, grid, GV_WARPS * 32, smem, s, w, rows, nb, rb, U,
+                          nullptr, 1, resid ? nullptr : Y, 0, resid, rs, h, nw, eps);
+    return launch_pdl(early_weights, k_gemv_staged<Q8>, grid, GV_WARPS * 32, smem, s, w, rows, nb, rb, U, nullptr,
+                      1, resid ? nullptr : Y, 0, resid, rs, h, nw, eps);
 }
 
 cudaError_t launch_matmul(int dtype, const void *W, int64_t n_cols, const void *act, int T, float *Y,
@@ -267,7 +267,8 @@ cudaError_t launch_matmul(int dtype, const void *W, int64_t n_cols, const void *
 }
 
 cudaError_t launch_matmul_resid(int dtype, const void *W, int64_t n_cols, const void *act, int T, float *Y,
-                                int64_t ldy, int64_t r0, int64_t r1, float *resid, float rs, cudaStream_t s) {
+                                int64_t ldy, int64_t r0, int64_t r1, float *resid, float rs, cudaStream_t s,
+                                bool early_weights) {
     const int64_t rows = r1 - r0;
     if (rows <= 0 || T <= 0) return cudaSuccess;
     const int64_t rb = row_bytes(dtype, n_cols);
@@ -283,12 +284,10 @@ cudaError_t launch_matmul_resid(int dtype, const void *W, int64_t n_cols, const 
         float *Yr = resid ? nullptr : Y + r0;
         float *hr = resid ? resid + r0 : nullptr;
         if (dtype == Q4)
-            k_gemv_staged<Q4><<<grid, GV_WARPS * 32, smem, s>>>(w + r0 * rb, rows, nb, rb, U, (const act_q8 *)act, T,
-                                                                Yr, ldy, hr, rs, nullptr, nullptr, 0.0f);
-        else
-            k_gemv_staged<Q8><<<grid, GV_WARPS * 32, smem, s>>>(w + r0 * rb, rows, nb, rb, U, (const act_q8 *)act, T,
-                                                                Yr, ldy, hr, rs, nullptr, nullptr, 0.0f);
-        return cudaGetLastError();
+            return launch_pdl(early_weights, k_gemv_staged<Q4>, grid, GV_WARPS * 32, smem, s, w + r0 * rb, rows, nb,
+                              rb, U, (const act_q8 *)act, T, Yr, ldy, hr, rs, nullptr, nullptr, 0.0f);
+        return launch_pdl(early_weights, k_gemv_staged<Q8>, grid, GV_WARPS * 32, smem, s, w + r0 * rb, rows, nb, rb,
+                          U, (const act_q8 *)act, T, Yr, ldy, hr, rs, nullptr, nullptr, 0.0f);
     }
     if (is_quant(dtype)) {
         const int nb = (int)(n_cols / QK);

@@ -123,11 +123,14 @@ cudaError_t launch_matmul(int dtype, const void *W, int64_t n_cols, const void *
 // One token through the staged decode GEMV with x = rmsnorm(h, nw) formed in every CTA (the same
 // bits as a separate rmsnorm + activation quantization): Y[r] (or resid[r] += rs * y). Returns
 // cudaErrorNotSupported when the staged kernel does not take the shape (then norm and matmul separately).
+// early_weights: the staged kernel may start, and stream its weights, while the previous kernel in
+// the stream still runs (programmatic dependent launch); only for weights no kernel writes meanwhile.
 cudaError_t launch_gemv_norm(int dtype, const void *W, int64_t n_cols, int64_t rows, const float *h, const float *nw,
-                             float eps, float *Y, float *resid, float rs, cudaStream_t s);
+                             float eps, float *Y, float *resid, float rs, cudaStream_t s, bool early_weights = false);
 // The same with a residual epilogue: resid[t * ldy + r] += rs * y (Y unused) when resid is not null.
 cudaError_t launch_matmul_resid(int dtype, const void *W, int64_t n_cols, const void *act, int T, float *Y,
-                                int64_t ldy, int64_t r0, int64_t r1, float *resid, float rs, cudaStream_t s);
+                                int64_t ldy, int64_t r0, int64_t r1, float *resid, float rs, cudaStream_t s,
+                                bool early_weights = false);
 cudaError_t launch_dequantize(int dtype, const void *W, int64_t n_rows, int64_t n_cols, float *out,
                               cudaStream_t s);
 

@@ -332,6 +332,8 @@ __global__ void __launch_bounds__(256) k_attn_scores1(PostArgs a, float *__restr
     const int qd = a.H * a.hd, kd = a.Hkv * a.hd;
     const float *qg = a.qkv + h * a.hd, *kg = a.qkv + qd + g * a.hd, *vg = a.qkv + qd + kd + g * a.hd;
     const float *cs = a.cs + (int64_t)pos * 2 * a.rope_half;
+    pdl_trigger();
+    pdl_wait();   // q|k|v is the previous kernel's output
     if (warp < 2) {   // warp 0: this head's q; warp 1: the kv group's k row of this token
         float *x = warp == 0 ? qh : kp;
         const float *src = warp == 0 ? qg : kg;
@@ -450,8 +452,15 @@ __global__ void __launch_bounds__(1024) k_attn_values(const float *__restrict__ 
         for (int j = 0; j < hpc && !fuse_sm; j++)
             bulk_g2s(pbuf + ((size_t)st * hpc + j) * VT, pg + (int64_t)j * max_seq + r0, (uint32_t)(VT * 4), &bars[st]);
     };
+    // V tiles wholly before this token's position were written by earlier forwards: with the softmax
+    // fused (no probability rows to copy) they stream in before the previous kernel is done
+    pdl_trigger();
+    const int first = fuse_sm ? min(min(nst, ntile), (n - 1) / VT) : 0;
     if (tid == 0)
-        for (int it = 0; it < min(nst, ntile); it++) issue(it);
+        for (int it = 0; it < first; it++) issue(it);
+    pdl_wait();
+    if (tid == 0)
+        for (int it = first; it < min(nst, ntile); it++) issue(it);
     if (fuse_sm) {   // hpc == 1: k_attn_softmax's steps on the head's score row, in shared memory
         __shared__ float red[32];
         __shared__ float ssum;
@@ -552,7 +561,8 @@ int matmul(hxb_model *m, const Mat &W, const float *x, int64_t ldx, act_q8 *act,
     } else if (ldx != W.cols) {
         return mfail(HXB_E_ARG, "float matmul input stride");
     }
-    if (!mcuda(launch_matmul_resid(W.dtype, W.w.p, W.cols, in, T, Y, ldy, 0, W.rows, resid, rs, s), "matmul"))
+    // the model's weights are written once at open: the GEMV may stream them while the previous kernel runs
+    if (!mcuda(launch_matmul_resid(W.dtype, W.w.p, W.cols, in, T, Y, ldy, 0, W.rows, resid, rs, s, true), "matmul"))
         return HXB_E_DEVICE;
     return HXB_OK;
 }
@@ -998,7 +1008,7 @@ static int attention(hxb_model *m, int l, int T, cudaStream_t s) {
     cudaError_t fe = cudaErrorNotSupported;
     if (T == 1 && w.qkv.w.p)
         fe = launch_gemv_norm(w.qkv.dtype, w.qkv.w.p, m->D, w.qkv.rows, m->h.as<float>(), w.attn_norm.as<float>(),
-                              m->eps, qkv, nullptr, 0.0f, s);
+                              m->eps, qkv, nullptr, 0.0f, s, true);
     if (fe != cudaErrorNotSupported) {
         if (!mcuda(fe, "q|k|v")) return HXB_E_DEVICE;
     } else {
@@ -1040,7 +1050,10 @@ static int attention(hxb_model *m, int l, int T, cudaStream_t s) {
     // the score CTAs of a (token, head) stride over the positions: about 1200 CTAs in all (8 per SM)
     const int chunks = std::max(1, std::min((int)blocks(m->max_seq, 16), 1200 / (m->H * T)));
     if (T == 1 && m->qk_norm != 2 && m->hd <= 1024) {   // one token: post-processing inside the score kernel
-        k_attn_scores1<<<dim3(chunks, m->H, 1), 256, 0, s>>>(a, m->S.as<float>(), m->attn_scale);
+        if (!mcuda(launch_pdl(true, k_attn_scores1, dim3(chunks, m->H, 1), dim3(256), 0, s, a, m->S.as<float>(),
+                              m->attn_scale),
+                   "attention scores"))
+            return HXB_E_DEVICE;
     } else {
         if (m->qk_norm == 2)
             k_attn_post<<<dim3(T, 1), 256, sizeof(float) * (m->q_dim + m->kv_dim), s>>>(a);
@@ -1056,10 +1069,12 @@ static int attention(hxb_model *m, int l, int T, cudaStream_t s) {
         if (!m->vfuse1)
             k_attn_softmax<<<dim3(m->H, T), 256, sizeof(float) * m->max_seq, s>>>(m->S.as<float>(), m->H, m->kv_seq, a.dpos);
         const bool fuse_act = is_quant(w.o.dtype) && m->hd % QK == 0;
-        k_attn_values<<<dim3(m->H, 1), (m->hd + 31) / 32 * 32, m->vsmem1, s>>>(
-            m->S.as<float>(), a.vc, m->att.as<float>(), fuse_act ? act : nullptr, m->H, m->Hkv, m->hd, m->hd, 1,
-            m->vnst1, m->kv_seq, a.dpos, m->vfuse1 ? 1 : 0);
-        if (!mcuda(cudaGetLastError(), "attention")) return HXB_E_DEVICE;
+        // after the separate softmax kernel the launch is an ordinary one
+        if (!mcuda(launch_pdl(m->vfuse1, k_attn_values, dim3(m->H, 1), dim3((m->hd + 31) / 32 * 32), m->vsmem1, s,
+                              m->S.as<float>(), a.vc, m->att.as<float>(), fuse_act ? act : nullptr, m->H, m->Hkv,
+                              m->hd, m->hd, 1, m->vnst1, m->kv_seq, a.dpos, m->vfuse1 ? 1 : 0),
+                   "attention"))
+            return HXB_E_DEVICE;
         bool aready = fuse_act;
         return matmul(m, w.o, m->att.as<float>(), m->q_dim, act, aready, T, nullptr, m->D, s, m->h.as<float>(), m->rs);
     }
@@ -1129,7 +1144,7 @@ static int enqueue_forward(hxb_model *m, int T, int mode, bool replay, cudaStrea
         cudaError_t fe = cudaErrorNotSupported;
         if (n == 1)   // one row: the LM head's CTAs form rmsnorm(h, out_norm) themselves
             fe = launch_gemv_norm(head.dtype, head.w.p, m->D, m->V, m->h.as<float>() + (size_t)first * m->D,
-                                  m->out_norm.as<float>(), m->eps, m->logits.as<float>(), nullptr, 0.0f, s);
+                                  m->out_norm.as<float>(), m->eps, m->logits.as<float>(), nullptr, 0.0f, s, true);
         if (fe != cudaErrorNotSupported) {
             rc = mcuda(fe, "lm head") ? HXB_OK : HXB_E_DEVICE;
         } else {
