@@ -122,9 +122,9 @@ def step_bytes(B):
 
 
 # DRAM bytes (read + write) per layer of k_moe_decode from one ncu capture of a 4-layer launch of the
-# same shape (bench.py --layers 4: dram__bytes_read.sum 84.73 MB, dram__bytes_write.sum 1.87 MB); a
+# same shape (bench.py --layers 4: dram__bytes_read.sum 84.71 MB, dram__bytes_write.sum 2.30 MB); a
 # launch's traffic grows with its layers, so the full launch's figure is this times its layers.
-DECODE_DRAM_BYTES_PER_LAYER = (84_732_928 + 1_870_848) / 4
+DECODE_DRAM_BYTES_PER_LAYER = (84_705_536 + 2_298_624) / 4
 
 
 def workload_config(B, world, parallelism=None):
