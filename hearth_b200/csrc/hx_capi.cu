@@ -506,7 +506,8 @@ extern "C" HXB_API hxb_moe *hxb_moe_open(const hxb_moe_config *c, char *err, siz
         std::string why_not;
         const bool off = env && env[0] == '0';
         m->use_decode = !off &&
-                        decode_supported(D, k.expert_ffn_dim, E, K, k.expert_dtype, k.shared_ffn_dim > 0, &why_not);
+                        decode_supported(D, k.expert_ffn_dim, E, K, k.expert_dtype, k.shared_ffn_dim > 0, k.ep_size,
+                                         &why_not);
         if (m->use_decode) {
             const size_t xb = sizeof(float) * (size_t)decode_xbuf_floats(L, D, k.expert_ffn_dim, E, K);
             if (!m->dec_router.alloc(sizeof(void *) * (size_t)L) || !m->dec_norm.alloc(sizeof(void *) * (size_t)L) ||

@@ -62,6 +62,7 @@ enum : int { ST_START, ST_H, ST_RMS, ST_NORM, ST_X, ST_LOGIT, ST_ACT, ST_LG, ST_
 // Work split of one launch (identical on host and device).
 struct DecodePlan {
     int G, ch, nch, ch_max;       // CTAs, row pairs per chunk, gate/up chunks (K * F / ch), chunks per CTA at most
+    int prows;                    // down rows per single-token row loop call
     int ra, dr_max, hr_max;       // down-row alignment, down rows / CTA at most, h rows / CTA at most
     int rpc;                      // router rows per CTA
 };
@@ -84,12 +85,15 @@ HX_HD inline void h_rows(int c, int G, int D, int *r0, int *r1) {
     *r1 = (int)((int64_t)D * (c + 1) / G);
 }
 
-HX_HD inline DecodePlan decode_plan(int G, int D, int F, int E, int K, int dtype) {
+HX_HD inline DecodePlan decode_plan(int G, int D, int F, int E, int K, int dtype, int ep) {
     DecodePlan P{};
     P.G = G;
     // gate/up row pairs per chunk (one mbarrier, two bulk copies): 4 (3 measured no faster on the
-    // Qwen3 shape), 2 when F is not a multiple of 4
-    P.ch = F % 4 == 0 ? 4 : 2;
+    // Qwen3 shape), 2 when F is not a multiple of 4. With expert parallelism a GPU computes about K/ep
+    // of the ranks: chunks of 2 pairs keep every warp busy with half the dependent rows each, and the
+    // down rows go 4 to a warp call for the same reason.
+    P.ch = F % 4 == 0 && ep <= 1 ? 4 : 2;
+    P.prows = ep <= 1 ? 8 : 4;
     P.nch = K * F / P.ch;
     P.ch_max = (P.nch + G - 1) / G;
     const int64_t rbF = row_bytes(dtype, F);
@@ -115,9 +119,9 @@ struct DecodeLayout {
 
 HX_HD inline size_t align16(size_t v) { return (v + 15) & ~size_t(15); }
 
-HX_HD inline DecodeLayout decode_layout(int G, int D, int F, int E, int K, int dtype) {
+HX_HD inline DecodeLayout decode_layout(int G, int D, int F, int E, int K, int dtype, int ep) {
     DecodeLayout L{};
-    L.plan = decode_plan(G, D, F, E, K, dtype);
+    L.plan = decode_plan(G, D, F, E, K, dtype, ep);
     L.nbD = D / QK;
     L.nbF = F / QK;
     L.rbD = row_bytes(dtype, D);
@@ -552,8 +556,9 @@ __device__ void decode_body(const DecodeArgs &a, uint8_t *smem) {
         {
             const bool ok = mbar_wait(&bars[BAR_DOWN], par, a.err);
             HX_STAMP(ST_DNW);
-            for (int r0 = warp * DEC_PROWS; r0 < ndr && ok; r0 += DEC_WARPS * DEC_PROWS)
-                warp_rows_1tok<DT>(dn + (size_t)r0 * ly.rbF, ly.rbF, ly.nbF, min(DEC_PROWS, ndr - r0), amid, P, Ys + r0);
+            const int pr = pl.prows;
+            for (int r0 = warp * pr; r0 < ndr && ok; r0 += DEC_WARPS * pr)
+                warp_rows_1tok<DT>(dn + (size_t)r0 * ly.rbF, ly.rbF, ly.nbF, min(pr, ndr - r0), amid, P, Ys + r0);
         }
         __syncthreads();
         HX_STAMP(ST_DOWN);
@@ -630,7 +635,7 @@ int decode_grid() {
 
 int64_t decode_xbuf_floats(int Lb, int D, int F, int E, int K) { return 2 * xset_floats(Lb, D, F, E, K); }
 
-bool decode_supported(int D, int F, int E, int K, int dtype, bool shared, std::string *why) {
+bool decode_supported(int D, int F, int E, int K, int dtype, bool shared, int ep, std::string *why) {
     auto no = [&](const char *w) {
         if (why) *why = w;
         return false;
@@ -641,7 +646,7 @@ bool decode_supported(int D, int F, int E, int K, int dtype, bool shared, std::s
     if (K > 16) return no("top_k > 16");
     if (E % 4 || D % 4 || F % 4) return no("exchange vectors (D, F, E multiples of 4)");
     const int G = decode_grid();
-    const DecodeLayout ly = decode_layout(G, D, F, E, K, dtype);
+    const DecodeLayout ly = decode_layout(G, D, F, E, K, dtype, ep);
     const DecodePlan &pl = ly.plan;
     if (pl.rpc > 2 * DEC_WARPS) return no("router rows per CTA");
     if (pl.ch_max > DEC_MAXCH) return no("gate/up chunks per CTA");
@@ -698,7 +703,7 @@ cudaError_t launch_moe_decode(const DecodeParams &p, cudaStream_t s) {
     a.ep_y = p.ep_y;
     if (a.ep_size > 1 && !a.ep_y) return cudaErrorInvalidValue;
     const int G = decode_grid();
-    a.lay = decode_layout(G, p.D, p.F, p.E, p.K, p.dtype);
+    a.lay = decode_layout(G, p.D, p.F, p.E, p.K, p.dtype, p.ep_size);
     cudaLaunchConfig_t cfg = {};
     cfg.gridDim = dim3((unsigned)G);
     cfg.blockDim = dim3(DEC_THREADS);

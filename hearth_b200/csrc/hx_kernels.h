@@ -190,7 +190,7 @@ int decode_grid();
 int decode_stamps();
 int decode_max_layers();
 int64_t decode_xbuf_floats(int buf_layers, int D, int F, int E, int K);
-bool decode_supported(int D, int F, int E, int K, int dtype, bool shared, std::string *why);
+bool decode_supported(int D, int F, int E, int K, int dtype, bool shared, int ep, std::string *why);
 cudaError_t init_decode_attributes();
 cudaError_t launch_moe_decode(const DecodeParams &p, cudaStream_t s);
 
