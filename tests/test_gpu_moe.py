@@ -229,6 +229,36 @@ def test_persistent_decode_tied_scores(gpu, score_fn):
             assert tied == sorted(tied)
 
 
+@pytest.mark.parametrize("score_fn,nan_row", [(0, 0), (0, 9), (1, 7)])
+def test_persistent_decode_nan_router_rows(gpu, score_fn, nan_row):
+    """A NaN router row gives a NaN logit: with softmax every score turns NaN (the maximum keeps a
+    leading NaN, the sum takes any NaN) and the selection falls back to expert order, NaN ranking
+    last; with sigmoid only that expert's score is NaN and it is never selected. The warp routing's
+    results equal the oracle's (NaN outputs compared as NaN)."""
+    E, K = 32, 4
+
+    def poison(router):
+        r = router.copy()
+        r[nan_row] = np.nan
+        return r
+
+    model, be = build_pair(53, L=2, D=512, F=256, E=E, K=K, score_fn=score_fn, max_tokens=1, router_fn=poison)
+    rng = np.random.default_rng(9)
+    with be:
+        assert be.decode_path() == "persistent"
+        for _ in range(2):
+            h = rng.standard_normal((1, 512)).astype(np.float32)
+            hg, hr = be.forward(h), model.forward(h)
+            if score_fn == 0:
+                assert np.isnan(hg).all() and np.isnan(hr).all()
+                ids, _ = be.last_routing(1)
+                assert list(ids[0]) == list(range(K))
+            else:
+                assert np.array_equal(bits(hg), bits(hr))
+                ids, _ = be.last_routing(1)
+                assert nan_row not in list(ids[0])
+
+
 def test_persistent_decode_qwen3_shape_matches_multi_kernel_path(gpu, monkeypatch):
     """Qwen3-30B-A3B layer shape (D 2048, F 768, 128 experts, top-8), 2 layers: the persistent kernel,
     the multi-kernel path and the oracle agree bit for bit, and so does the last layer's routing."""
