@@ -698,6 +698,7 @@ __global__ void __launch_bounds__(512) k_moe_gateup(MoeShape sh, MoeLayerDev L, 
 // SwiGLU and the mid activation block follow in the CTA. Used when rows are whole 16-byte units.
 constexpr int G1_WARPS = 12;
 constexpr int G1_SLOT = 16 * 1024;
+constexpr int G1_HDR = (G1_WARPS * 8 + 127) / 128 * 128;   // the warps' mbarriers
 constexpr int G1_TMAX = 4;   // tokens per job (decode, speculative verification of a few tokens)
 
 __host__ __device__ inline int g1_tile_rows(int64_t rb) {   // largest power of two <= 32 with TR * rb <= G1_SLOT
@@ -714,9 +715,9 @@ __device__ void gateup1_body(const MoeShape &sh, const MoeScratch &sc, const Job
     const int64_t rbD = row_bytes(DT, sh.D);
     const int TR = g1_tile_rows(rbD), ntile = 2 * GU_ROWS / TR;   // gate tiles, then up tiles
     uint64_t *bar = reinterpret_cast<uint64_t *>(smem) + warp;
-    uint8_t *slot = smem + 128 + (size_t)warp * G1_SLOT;
+    uint8_t *slot = smem + G1_HDR + (size_t)warp * G1_SLOT;
     const int nt = job.n;   // <= G1_TMAX (host condition)
-    act_q8 *acts = reinterpret_cast<act_q8 *>(smem + 128 + (size_t)G1_WARPS * G1_SLOT);   // [nt][nbD]
+    act_q8 *acts = reinterpret_cast<act_q8 *>(smem + G1_HDR + (size_t)G1_WARPS * G1_SLOT);   // [nt][nbD]
     float *P = reinterpret_cast<float *>(acts + sh.T * nbD) + warp * ROWS_1TOK * 33;
     float *GU = reinterpret_cast<float *>(acts + sh.T * nbD) + G1_WARPS * ROWS_1TOK * 33;   // [nt][2][64]
     auto issue = [&](int tile) {
@@ -775,7 +776,7 @@ __global__ void __launch_bounds__(G1_WARPS * 32) k_moe_gateup1(MoeShape sh, MoeL
 }
 
 static size_t gateup1_smem(int nbD, int T) {
-    return 128 + (size_t)G1_WARPS * G1_SLOT + (size_t)T * nbD * ACT_BLOCK + (size_t)G1_WARPS * ROWS_1TOK * 33 * 4 +
+    return G1_HDR + (size_t)G1_WARPS * G1_SLOT + (size_t)T * nbD * ACT_BLOCK + (size_t)G1_WARPS * ROWS_1TOK * 33 * 4 +
            (size_t)T * 2 * GU_ROWS * 4 + 64;
 }
 
@@ -1128,11 +1129,11 @@ static cudaError_t launch_expert_stages(int which, const MoeShape &sh, const Moe
         return cudaGetLastError();
     }
     // ---- gate/up + SwiGLU + mid activations
-    // one token: the single-token kernels (rows of whole 16-byte units; at least 2 rows of the widest
-    // gate/up dtype per slot)
+    // up to G1_TMAX tokens: the single-token kernels (rows of whole 16-byte units; a row of the widest
+    // gate/up dtype fits a slot)
     const int64_t rbD_max = std::max<int64_t>(row_bytes(L.expert_dtype, sh.D), L.Fs > 0 ? row_bytes(L.sh_dtype, sh.D) : 0);
     const bool one_token = T <= G1_TMAX && (sh.D / QK) % 8 == 0 && (sh.F % GU_ROWS) == 0 && (L.Fs % GU_ROWS) == 0 &&
-                           rbD_max * 2 <= G1_SLOT && gateup1_smem(sh.D / QK, T) + 1024 <= smem_limit();
+                           rbD_max <= G1_SLOT && gateup1_smem(sh.D / QK, T) + 1024 <= smem_limit();
     if ((which & 1) && one_token) {
         const int maxjobs = std::min(E, T * K) + (L.Fs > 0 ? 1 : 0);
         dim3 grid((unsigned)(std::max(sh.F, L.Fs) / GU_ROWS), (unsigned)maxjobs);
