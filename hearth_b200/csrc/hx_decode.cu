@@ -614,6 +614,10 @@ __device__ void decode_body(const DecodeArgs &a, uint8_t *smem) {
 
 __global__ void __launch_bounds__(DEC_THREADS, 1) k_moe_decode(DecodeArgs a) {
     extern __shared__ __align__(128) uint8_t smem[];
+    // a kernel launched after this one with programmatic stream serialization (the whole decoder's
+    // next GEMV) may start as SMs free up and stream its weights; it waits for this grid before it
+    // reads h
+    pdl_trigger();
     if (a.dtype == Q4) decode_body<Q4>(a, smem);
     else decode_body<Q8>(a, smem);
 }
