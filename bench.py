@@ -745,6 +745,12 @@ def main():
         import datetime
         import torch
         import torch.distributed as dist
+        # the line is the only thing on stdout: native code (the communicator set-up prints its NCCL
+        # version there) writes to stderr from here on, Python's stdout keeps the original descriptor
+        sys.stdout.flush()
+        real_out = os.dup(1)
+        os.dup2(2, 1)
+        sys.stdout = os.fdopen(real_out, "w", buffering=1)
         torch.cuda.set_device(local_rank)
         dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=300),
                                 device_id=torch.device("cuda", local_rank))
