@@ -462,115 +462,4 @@ __device__ __forceinline__ void route_token_warp128(const RouteCfg &R, const flo
     __syncwarp();
 }
 
-// Profiling hook of route_token_cta_small: HX_ROUTE_STAMP(i) marks the end of step i (empty here;
-// a timing harness defines it before including this header).
-#ifndef HX_ROUTE_STAMP
-#define HX_ROUTE_STAMP(i)
-#endif
-
-// Top-k routing of one token by a whole CTA (at least 128 threads), for E <= 128 and K <= 16
-// without expert groups. Threads 0..E-1 own one expert each: softmax takes the maximum (warp 0), exp
-// per expert, the sum16 of the exps (warp 0, NUMERICS §1 order), then one division per expert;
-// sigmoid scores need none of the shared steps. Selection is exact without comparing all pairs:
-// each of warps 0..3 ranks its 32 keys among themselves (rank_key order; the slots past E get
-// distinct keys below every real key), the keys of within-warp rank < K are the warp's candidates,
-// and a candidate's rank is its within-warp rank plus, for each other warp, the number of that
-// warp's candidates above it. That count is exact whenever it is below K for every warp, and reaches
-// K otherwise, so the experts of rank < K come out exactly, in route_select's order. Warp 0 then
-// forms the weights. score_s [E] and key_s [128] are shared scratch. Results ids / w (shared);
-// every thread of the CTA must call it. kSharedLogits: the logits are in shared memory (plain
-// loads) rather than global (L2 loads).
-template <bool kSharedLogits = false>
-__device__ __forceinline__ void route_token_cta_small(const RouteCfg &R, const float *logit_g, const float *bias,
-                                                      float *score_s, unsigned long long *key_s, int *ids,
-                                                      float *w) {
-    __shared__ float s_red[2];                 // softmax maximum, sum of exps
-    __shared__ unsigned long long s_cand[4][16];   // each warp's K largest keys, by within-warp rank
-    const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
-    const int E = R.E, K = R.K;
-    auto logit = [&](int i) { return kSharedLogits ? logit_g[i] : __ldcg(logit_g + i); };
-    const bool mine = tid < E;   // this thread scores expert tid
-    const float x = mine ? logit(tid) : 0.0f;
-    float sc = 0.0f;
-    if (R.score_fn == SCORE_SOFTMAX) {
-        if (warp == 0) {   // m = x[0]; m = x[i] > m ? x[i] : m (NaN only through x[0])
-            float m = -__uint_as_float(0x7f800000u);
-#pragma unroll
-            for (int t = 0; t < 4; t++)
-                if (t * 32 + lane < E) m = fmaxf(m, logit(t * 32 + lane));
-#pragma unroll
-            for (int s = 16; s >= 1; s >>= 1) m = fmaxf(m, __shfl_xor_sync(0xffffffffu, m, s));
-            const float x0 = __shfl_sync(0xffffffffu, x, 0);
-            if (lane == 0) s_red[0] = x0 != x0 ? x0 : m;
-        }
-        HX_ROUTE_STAMP(0);
-        __syncthreads();
-        const float e = mine ? host_expf(__fsub_rn(x, s_red[0])) : 0.0f;
-        if (mine) score_s[tid] = e;
-        HX_ROUTE_STAMP(1);
-        __syncthreads();
-        if (warp == 0) {   // sum16: lane j < 16 adds e[j], e[j+16], ... in order, then the 8/4/2/1 tree
-            float L = 0.0f;
-            if (lane < 16)
-#pragma unroll
-                for (int i = lane; i < 128; i += 16)
-                    if (i < E) L = __fadd_rn(L, score_s[i]);
-            L = tree16(L, 0xffffffffu);
-            if (lane == 0) s_red[1] = L;
-        }
-        HX_ROUTE_STAMP(2);
-        __syncthreads();
-        sc = __fdiv_rn(e, s_red[1]);
-    } else {
-        sc = sigmoid_c(x);
-    }
-    unsigned long long ki = 0;
-    if (tid < 128) {   // slot s >= E: key 127 - s, below every real key (whose low word is >= 2^32 - 128)
-        const float sv = (R.score_bias && bias && mine) ? __fadd_rn(sc, __ldg(bias + tid)) : sc;
-        ki = mine ? rank_key(sv, tid) : (unsigned long long)(127 - tid);
-        key_s[tid] = ki;
-        if (mine) score_s[tid] = sc;
-    }
-    HX_ROUTE_STAMP(3);
-    __syncthreads();
-    int r = 0;
-    if (tid < 128) {   // within-warp rank: 32 broadcast loads
-        const unsigned long long *kw = key_s + (tid & ~31);
-#pragma unroll
-        for (int k = 0; k < 32; k++) r += kw[k] > ki ? 1 : 0;
-        if (r < K) s_cand[warp][r] = ki;
-    }
-    HX_ROUTE_STAMP(4);
-    __syncthreads();
-    if (mine && r < K) {   // own warp's candidates above ki number exactly r
-        int rank = 0;
-#pragma unroll
-        for (int w2 = 0; w2 < 4; w2++)
-#pragma unroll
-            for (int k = 0; k < 16; k++) rank += (k < K && s_cand[w2][k] > ki) ? 1 : 0;
-        if (rank < K) ids[rank] = tid;
-    }
-    HX_ROUTE_STAMP(5);
-    __syncthreads();
-    if (warp == 0) {   // route_weights (model.c:833-843): every lane forms the rank-order sum itself
-        float v[16];
-#pragma unroll
-        for (int j = 0; j < 16; j++) v[j] = j < K ? score_s[ids[j]] : 0.0f;
-        float sacc = 0.0f, wj = 0.0f;
-#pragma unroll
-        for (int j = 0; j < 16; j++)
-            if (j < K) {
-                sacc = __fadd_rn(sacc, v[j]);
-                if (j == lane) wj = v[j];
-            }
-        const float den = __fadd_rn(sacc, 1e-20f);
-        if (lane < K) {
-            if (R.norm_topk_prob) wj = __fdiv_rn(wj, den);
-            w[lane] = __fmul_rn(wj, R.routed_scale);
-        }
-        __syncwarp();
-    }
-    HX_ROUTE_STAMP(6);
-}
-
 }  // namespace hx
